@@ -1,0 +1,576 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+Configurations (BASELINE.json "configs", synthetic seeded data):
+  prefill  causal prefill SDPA, S 4096, Hq 16 / Hkv 4 / d 256, gated     TFLOP/s  (default)
+  decode   one decode step, n 2048, same heads, gated                    GB/s
+  gdn      GatedDeltaNet: prefill T 4096 then 256 decode steps           tok/s
+  batch    batched decode, 64 sequences, L ~ U{1024..32768}              GB/s
+A step is one pass of the path over one batch: one prefill / one decode step /
+one GDN prefill + 256 steps / one decode step of the whole batch.
+
+`value` is device-timed with CUDA events on the launching stream, inputs
+resident in HBM, L2 flushed (256 MB write) before every timed step; under
+torchrun the timed total is the max over ranks.  `e2e` is the same metric
+through the C ABI with inputs copied from pinned host memory and the result
+copied back inside the timed region.  `--impl reference` times the CPU
+restatement of the reference's x86 kernels (the oracle) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "herbert-jit-bf16_b200")]
+
+HQ, HKV, HD = 16, 4, 256
+NK, NV, HKD, HVD = 16, 32, 128, 128
+PREFILL_S = 4096
+DECODE_N = 2048
+GDN_T, GDN_STEPS = 4096, 256
+L2_FLUSH_BYTES = 256 << 20
+
+# dram bytes (read + write) of one launch of the dominant kernel, from the
+# committed ncu summaries under profiles/ (None until captured).
+NCU_TRAFFIC = {"prefill": None, "decode": None, "gdn": None, "batch": None}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm": float(j["hbm_gbs"]), "bf16": float(j["bf16_tflops"]),
+                "bf16_sustained": float(j.get("bf16_tflops_sustained", j["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def prefill_flops(S, past=0, heads=HQ, hd=HD):
+    n = sum(range(past + 1, past + S + 1))
+    return 4.0 * heads * hd * n
+
+
+def gdn_prefill_flops(T, nv=NV, dk=HKD, dv=HVD, C=64):
+    per = 6 * C * dk * dv + 6 * C * C * dk + 4 * C * C * dv + C ** 3 / 3
+    return per * (T // C) * nv
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons, every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits", "-i", str(self.idx)],
+                                     capture_output=True, text=True, timeout=5).stdout
+                for line in out.strip().splitlines():
+                    self.samples.append([x.strip() for x in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                mx = float(s[2])
+                for n, v in zip(names, s[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except Exception:
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def smi_index(dev):
+    """nvidia-smi index of torch device `dev` (matched by PCI bus id)."""
+    import torch
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id.lower()
+        out = subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id",
+                              "--format=csv,noheader"], capture_output=True, text=True,
+                             timeout=10).stdout
+        for line in out.strip().splitlines():
+            i, b = [x.strip().lower() for x in line.split(",")]
+            if b.endswith(bus[-12:]) or bus.endswith(b[-12:]):
+                return int(i)
+    except Exception:
+        pass
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [x for x in vis.split(",") if x.strip().isdigit()]
+    return int(ids[dev]) if dev < len(ids) else dev
+
+
+# --------------------------------------------------------------- workloads
+
+class Workload:
+    """One configuration on one GPU: device inputs, the step, the e2e step."""
+
+    launches_per_step = 1
+
+    def step(self):  # device-resident step
+        raise NotImplementedError
+
+    def e2e_step(self):  # host buffers -> device -> step -> result to host
+        raise NotImplementedError
+
+
+def _randn_bf16(shape, gen, device):
+    import torch
+    return torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(
+        torch.bfloat16)
+
+
+class PrefillWorkload(Workload):
+    def __init__(self, device, S=PREFILL_S, seed=0x5EED0002):
+        import torch
+        import herbert_b200 as hb
+        self.hb, self.S = hb, S
+        gen = torch.Generator(device=device).manual_seed(seed)
+        qd = HQ * HD
+        self.q = _randn_bf16((S, 2 * qd), gen, device)
+        self.k = _randn_bf16((HKV, S, HD), gen, device)
+        self.v = _randn_bf16((HKV, S, HD), gen, device)
+        self.out = torch.empty((S, qd), dtype=torch.bfloat16, device=device)
+        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
+        self.ws = None
+        self.work = prefill_flops(S)
+        self.units = "TFLOP/s"
+        self.h_in = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
+        self.d2h = self.h_out.numel() * self.h_out.element_size()
+
+    def step(self):
+        self.ws = self.hb.attention(self.spec, self.q, self.k, self.v, self.out, rows=self.S,
+                                    past=0, kv_stride=self.S * HD, capacity=self.S,
+                                    regime="prefill", workspace=self.ws)
+
+    def e2e_step(self):
+        for d, h in zip((self.q, self.k, self.v), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "causal prefill SDPA (BASELINE configs[1])", "seq_len": self.S,
+                "q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "gate": "sigmoid",
+                "past": 0}
+
+
+class DecodeWorkload(Workload):
+    def __init__(self, device, n=DECODE_N, seed=0x5EED0001):
+        import torch
+        import herbert_b200 as hb
+        self.hb, self.n = hb, n
+        gen = torch.Generator(device=device).manual_seed(seed)
+        qd = HQ * HD
+        self.q = _randn_bf16((1, 2 * qd), gen, device)
+        self.k = _randn_bf16((HKV, n, HD), gen, device)
+        self.v = _randn_bf16((HKV, n, HD), gen, device)
+        self.out = torch.empty((1, qd), dtype=torch.bfloat16, device=device)
+        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
+        self.ws = None
+        self.work = 2 * HKV * n * HD * 2 + 3 * qd * 2  # K+V + q + gate + out bytes
+        self.units = "GB/s"
+        self.h_in = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
+        self.d2h = self.h_out.numel() * self.h_out.element_size()
+
+    def step(self):
+        self.ws = self.hb.attention(self.spec, self.q, self.k, self.v, self.out, rows=1,
+                                    past=self.n - 1, kv_stride=self.n * HD, capacity=self.n,
+                                    regime="decode", workspace=self.ws)
+
+    def e2e_step(self):
+        for d, h in zip((self.q, self.k, self.v), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "single decode step gated SDPA (BASELINE configs[0])",
+                "kv_len": self.n, "q_heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                "gate": "sigmoid"}
+
+
+class GdnWorkload(Workload):
+    def __init__(self, device, T=GDN_T, steps=GDN_STEPS, seed=0x5EED0003):
+        import torch
+        import herbert_b200 as hb
+        self.hb, self.T, self.steps = hb, T, steps
+        gen = torch.Generator(device=device).manual_seed(seed)
+        conv = 2 * NK * HKD + NV * HVD
+        rows = T + steps
+        self.qkv = _randn_bf16((rows, conv), gen, device).float()
+        b = torch.randn((rows, NV), generator=gen, device=device)
+        g = torch.randn((rows, NV), generator=gen, device=device)
+        self.beta = torch.sigmoid(b)
+        self.decay = torch.exp(-torch.nn.functional.softplus(g))
+        self.state = torch.zeros((NV, HKD, HVD), dtype=torch.float32, device=device)
+        self.out = torch.empty((rows, NV * HVD), dtype=torch.float32, device=device)
+        self.shape = hb.DeltaShape(nk=NK, nv=NV, hkd=HKD, hvd=HVD)
+        self.ws = None
+        self.work = T + steps
+        self.units = "tok/s"
+        self.launches_per_step = 1 + steps
+        self.h_in = [t.cpu().pin_memory() for t in (self.qkv, self.beta, self.decay)]
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
+        self.d2h = self.h_out.numel() * self.h_out.element_size()
+
+    def step(self):
+        hb = self.hb
+        self.state.zero_()
+        self.ws = hb.delta_recurrence(self.shape, self.state, self.out, self.qkv, self.beta,
+                                      self.decay, rows=self.T, regime="prefill",
+                                      workspace=self.ws)
+        for t in range(self.T, self.T + self.steps):
+            hb.delta_recurrence(self.shape, self.state, self.out[t], self.qkv[t], self.beta[t],
+                                self.decay[t], rows=1, regime="decode")
+
+    def e2e_step(self):
+        for d, h in zip((self.qkv, self.beta, self.decay), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "GatedDeltaNet prefill then decode (BASELINE configs[2])",
+                "prefill_tokens": self.T, "decode_steps": self.steps, "key_heads": NK,
+                "value_heads": NV, "head_k_dim": HKD, "head_v_dim": HVD}
+
+
+class BatchWorkload(Workload):
+    def __init__(self, device, rank=0, world=1, seed=0x5EED0004):
+        import numpy as np
+        import torch
+        import herbert_b200 as hb
+        from herbert_b200.inputs import batch_lengths, lpt_assign
+        self.hb = hb
+        lens = batch_lengths(64, 1024, 32768, seed)
+        # the new token is position L-1: the cache holds L keys
+        mine = lpt_assign(lens * 1, world)[rank]
+        self.lens = [int(lens[i]) for i in mine]
+        gen = torch.Generator(device=device).manual_seed(seed + rank)
+        qd = HQ * HD
+        self.caches, seqs = [], []
+        self.q = _randn_bf16((len(mine), 2 * qd), gen, device)
+        self.out = torch.empty((len(mine), qd), dtype=torch.bfloat16, device=device)
+        for j, L in enumerate(self.lens):
+            kv = _randn_bf16((2, HKV, L, HD), gen, device)
+            self.caches.append(kv)
+            seqs.append(hb.DecodeSeq(q=self.q[j].data_ptr(), keys=kv[0].data_ptr(),
+                                     values=kv[1].data_ptr(), output=self.out[j].data_ptr(),
+                                     past=L - 1, kv_stride=L * HD))
+        self.table = hb.seq_table(seqs, device)
+        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
+        self.ws = None
+        self.work = sum(4 * HKV * L * HD for L in self.lens) + len(self.lens) * 3 * qd * 2
+        self.units = "GB/s"
+        self.h_in = [self.q.cpu().pin_memory()]
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = self.h_in[0].numel() * 2
+        self.d2h = self.h_out.numel() * 2
+        self.total_lens = lens
+
+    def step(self):
+        self.ws = self.hb.decode_batch(self.spec, self.table, len(self.lens),
+                                       max(self.lens) - 1, sum(self.lens) - len(self.lens),
+                                       workspace=self.ws)
+
+    def e2e_step(self):
+        # a decode step of a serving loop: the new query rows arrive from the
+        # host, the caches are already resident, the outputs go back
+        self.q.copy_(self.h_in[0], non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "batched decode SDPA, sequences sharded by LPT (BASELINE configs[3])",
+                "sequences": 64, "kv_len": "U{1024..32768} seed 0x5EED0004", "q_heads": HQ,
+                "kv_heads": HKV, "head_dim": HD, "gate": "sigmoid"}
+
+
+METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
+          "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s"}
+BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm"}
+
+
+def make_workload(cfg, device, rank, world):
+    if cfg == "prefill":
+        return PrefillWorkload(device)
+    if cfg == "decode":
+        return DecodeWorkload(device)
+    if cfg == "gdn":
+        return GdnWorkload(device)
+    if cfg == "batch":
+        return BatchWorkload(device, rank, world)
+    raise SystemExit(f"unknown config {cfg}")
+
+
+def value_of(work, seconds, units):
+    if units == "TFLOP/s":
+        return work / seconds / 1e12
+    if units == "GB/s":
+        return work / seconds / 1e9
+    return work / seconds
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=device)
+    cfg = args.config
+    wl = make_workload(cfg, device, rank, world)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        wl.step()
+    barrier()
+
+    def timed(fn, steps):
+        evs = []
+        for _ in range(steps):
+            flush.fill_(1)  # untimed: evict the inputs from L2
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / 1e3  # seconds
+
+    sampler = ClockSampler(smi_index(local)).start() if rank == 0 else None
+    barrier()
+    t_dev = timed(wl.step, args.steps)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    for _ in range(max(1, args.warmup // 2)):
+        wl.e2e_step()
+    barrier()
+    t_e2e = timed(wl.e2e_step, args.steps)
+    barrier()
+
+    t = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=device)
+    work = torch.tensor([float(wl.work)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(work, op=dist.ReduceOp.SUM)
+    t_dev, t_e2e = float(t[0]), float(t[1])
+    total_work = float(work[0])
+
+    if rank == 0:
+        pk = peaks()
+        per_launch = wl.work
+        kernel_s = t_dev / args.steps
+        if cfg == "gdn":
+            achieved = gdn_prefill_flops(wl.T) / kernel_s / 1e12
+            peak, unit = pk["bf16"], "TFLOP/s"
+        elif BOUND[cfg] == "tensor":
+            achieved = per_launch / kernel_s / 1e12
+            peak, unit = pk["bf16"], "TFLOP/s"
+        else:
+            achieved = per_launch / kernel_s / 1e9
+            peak, unit = pk["hbm"], "GB/s"
+        line = {
+            "metric": METRIC[cfg],
+            "value": round(value_of(total_work, t_dev / args.steps, wl.units), 4),
+            "unit": wl.units,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(t_dev / args.steps * 1e3, 5),
+            "higher_is_better": True,
+            "scaling": "strong" if cfg == "batch" else "weak",
+            "vs_baseline": None,
+            "dtype": "bf16" if cfg != "gdn" else "f32",
+            "data": "synthetic",
+            "config": dict(wl.describe(), parallelism=(
+                f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
+                else f"{world} independent replicas"), l2="flushed (256 MB write) before each step"),
+            "roofline": {"bound": BOUND[cfg], "achieved": round(achieved, 3), "peak": peak,
+                         "unit": unit, "frac": round(achieved / peak, 4),
+                         "peak_source": pk["source"] + (" burst" if unit == "TFLOP/s" else ""),
+                         "traffic": NCU_TRAFFIC.get(cfg)},
+            "e2e": {"value": round(value_of(total_work, t_e2e / args.steps, wl.units), 4),
+                    "unit": wl.units, "h2d_bytes_per_step": int(wl.h2d),
+                    "d2h_bytes_per_step": int(wl.d2h)},
+            "gpu_launches": int(wl.launches_per_step * args.steps),
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- CPU arm
+
+def _cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(cfg, budget_s=10.0, threads=0):
+    """Times the oracle (the C restatement of the reference's x86 kernels)
+    on this host's cores over a bounded sample of the configuration."""
+    sys.path[:0] = [os.path.join(ROOT, "oracle")]
+    import numpy as np
+    import oracle
+    from herbert_b200.inputs import AttentionInputs, DeltaInputs
+
+    oracle.build()
+    threads = threads or _cpu_threads()
+    impl = 1 if oracle.has_avx512bf16() else 0
+    if cfg in ("prefill",):
+        rows = 256 if impl else 32
+        past = PREFILL_S - rows
+        inp = AttentionInputs(rows, past)
+        work = prefill_flops(rows, past)
+        unit, scale = "TFLOP/s", 1e12
+        sample = f"last {rows} rows of the S={PREFILL_S} prefill (all 16 heads)"
+        fn = lambda: oracle.attention(  # noqa: E731
+            inp.q.ravel(), inp.keys.ravel(), inp.values.ravel(), rows=rows, past=past,
+            heads=HQ, gqa=HQ // HKV, head_dim=HD, q_row=inp.q_row, q_head=HD,
+            out_row=inp.out_row, gate_offset=inp.gate_offset, kv_stride=inp.kv_stride,
+            scale=inp.scale, impl=impl, use_block=0 if impl else 1, threads=threads)
+    elif cfg in ("decode", "batch"):
+        n = DECODE_N if cfg == "decode" else 16896
+        inp = AttentionInputs(1, n - 1)
+        work = 2 * HKV * n * HD * 2 + 3 * HQ * HD * 2
+        unit, scale = "GB/s", 1e9
+        sample = f"one decode step at n={n}" + (" (the mean batch length)" if cfg == "batch" else "")
+        fn = lambda: oracle.attention(  # noqa: E731
+            inp.q.ravel(), inp.keys.ravel(), inp.values.ravel(), rows=1, past=n - 1,
+            heads=HQ, gqa=HQ // HKV, head_dim=HD, q_row=inp.q_row, q_head=HD,
+            out_row=inp.out_row, gate_offset=inp.gate_offset, kv_stride=inp.kv_stride,
+            scale=inp.scale, impl=impl, use_block=0, threads=threads)
+    else:  # gdn
+        T = 64
+        d = DeltaInputs(T)
+        work = T
+        unit, scale = "tok/s", 1.0
+        sample = f"{T} positions of the recurrence at Qwen3.5 geometry (32 value heads)"
+        fn = lambda: oracle.gdn_layer(d.qkv, d.state, d.beta, d.decay, nk=NK, nv=NV,  # noqa
+                                      hkd=HKD, hvd=HVD, threads=threads)
+    fn()  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 100000:
+            break
+    val = work * reps / el / scale
+    return {"value": round(val, 6), "unit": unit, "cores": threads,
+            "kind": "port",
+            "sample": sample + f", repeated {reps}x in {el:.1f} s; "
+                      f"{'AVX512-BF16 transcription' if impl else 'portable emulation'}"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = args.config
+    budget = max(1.0, min(20.0, 60.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_baseline(cfg, budget_s=0.2)
+    vals = [cpu_baseline(cfg, budget_s=budget) for _ in range(args.steps)]
+    v = statistics.median(x["value"] for x in vals)
+    base = vals[0]
+    line = {
+        "impl": "reference",
+        "metric": METRIC[cfg], "value": v, "unit": base["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong" if cfg == "batch" else "weak", "vs_baseline": None,
+        "dtype": "bf16" if cfg != "gdn" else "f32", "data": "synthetic",
+        "config": {"workload": cfg, "note": "CPU restatement of the reference's x86 AVX-512 BF16 "
+                   "kernels (Rust reference not buildable here)"},
+        "cpu_baseline": dict(base, value=v),
+        "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="prefill", choices=sorted(METRIC))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,428 @@
+// attn_decode.cu -- split-KV flash-decoding SDPA for sm_100a, with the
+// Qwen3.5 sigmoid output gate fused into the final combine.
+//
+// Replaces, in the decode regime, the reference's attention node
+// (SdpaHeadFn per (row, head), src/jit/emit_sdpa.rs:131-140, driven by
+// src/jit/target/x86/execution/attention.rs:56-224) and the output-gate node
+// (ElemOp::SigmoidMul, src/jit/target/x86/emit_elem.rs:333-420).
+//
+// Work decomposition.  A "unit" is (sequence, query row, KV head): the G
+// query heads of one GQA group share every K/V row, so a CTA streams a range
+// of positions of one KV head once and scores it against all G heads.  The
+// positions of a unit are cut into splits of `chunk` positions; grid =
+// (splits, kv heads, sequences x rows).
+//
+// CTA = 1 producer warp + 8 consumer warps.  The producer streams 32-position
+// tiles of K and V with 1-D bulk copies (a tile of one head is contiguous in
+// the reference layout) into a 128 KB shared-memory ring (4 stages at
+// head_dim 256), completion tracked by mbarriers.  Consumer warp w owns positions 4w..4w+3 of every tile and
+// keeps its own online-softmax state (max, sum, G x head_dim accumulator, in
+// the log2 domain).  A lane holds head_dim/32 consecutive dimensions: each K
+// or V row is one 16-byte (head_dim 256) shared-memory load per lane.  The
+// 4G partial dot products of a lane are reduced across the warp by a
+// transposed butterfly (4G-1 shuffles for 4G sums instead of 5 per sum).
+//
+// The 8 warp states merge in shared memory; with one split the CTA
+// finalises, otherwise it writes an unnormalised partial (O, m, l) to the
+// workspace and the last CTA of the unit to arrive (atomic counter, reset
+// after use) merges the partials, rounds to bf16 and applies the gate with
+// the reference's own exp polynomial and rounding steps.
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "hb_common.cuh"
+#include "hb_internal.h"
+
+namespace hb {
+namespace {
+
+constexpr int kTile = 32;           // positions per pipeline tile
+constexpr int kRingBytes = 131072;  // K+V tiles in flight per CTA (one CTA per SM)
+constexpr int kConsumerWarps = 8;   // 4 positions per warp per tile
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+
+struct DecodeParams {
+  const hb_decode_seq* seqs;  // device table, or nullptr: use `one`
+  hb_decode_seq one;
+  int rows;                   // query rows per sequence (table mode: 1)
+  int hkv;                    // KV heads
+  int64_t q_row, q_head, out_row;
+  int64_t gate_offset;        // < 0: no gate
+  float scale_log2;           // scale * log2(e)
+  int chunk;                  // positions per split, multiple of kTile
+  int nsplit;                 // grid.x
+  int* status;
+  unsigned* counters;         // one per unit
+  float* partials;            // [unit][split][G*HD + 2G]
+};
+
+template <int HD>
+struct LaneVec;
+template <>
+struct LaneVec<256> {  // 8 bf16 per lane
+  static HB_DEV void load(const uint16_t* p, float (&x)[8]) {
+    uint4 w = *reinterpret_cast<const uint4*>(p);
+    x[0] = bf16lo(w.x); x[1] = bf16hi(w.x); x[2] = bf16lo(w.y); x[3] = bf16hi(w.y);
+    x[4] = bf16lo(w.z); x[5] = bf16hi(w.z); x[6] = bf16lo(w.w); x[7] = bf16hi(w.w);
+  }
+};
+template <>
+struct LaneVec<128> {  // 4 bf16 per lane
+  static HB_DEV void load(const uint16_t* p, float (&x)[4]) {
+    uint2 w = *reinterpret_cast<const uint2*>(p);
+    x[0] = bf16lo(w.x); x[1] = bf16hi(w.x); x[2] = bf16lo(w.y); x[3] = bf16hi(w.y);
+  }
+};
+
+template <int V>
+struct Log2 { static constexpr int value = 1 + Log2<V / 2>::value; };
+template <>
+struct Log2<1> { static constexpr int value = 0; };
+
+// Transposed butterfly: every lane enters with NV partial sums; on exit
+// lane l holds the warp-wide sum of value (l >> (5 - log2 NV)).
+template <int NV>
+HB_DEV float transpose_reduce(float (&v)[NV], int lane) {
+  constexpr int L = Log2<NV>::value;
+#pragma unroll
+  for (int lvl = 0; lvl < L; ++lvl) {
+    const int width = NV >> lvl, half = width >> 1, off = 16 >> lvl;
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < half; ++i) {
+      float send = upper ? v[i] : v[i + half];
+      float keep = upper ? v[i + half] : v[i];
+      v[i] = keep + __shfl_xor_sync(kFull, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = 16 >> L; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(kFull, v[0], off);
+  return v[0];
+}
+
+HB_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
+
+template <int HD>
+struct Ring { static constexpr int stages = kRingBytes / (2 * kTile * HD * 2); };
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodeParams p) {
+  constexpr int kStages = Ring<HD>::stages;
+  constexpr int DPL = HD / 32;             // dims per lane
+  constexpr int NV = 4 * G;                // partial sums per lane per tile
+  constexpr int SH = 5 - Log2<NV>::value;  // lane >> SH = value index
+  constexpr int TILE_ELEMS = kTile * HD;
+  constexpr int PSTRIDE = G * HD + 2 * G;  // floats per split partial
+
+  constexpr int RING_BYTES = 2 * kStages * TILE_ELEMS * 2;
+  constexpr int MERGE_BYTES = kConsumerWarps * PSTRIDE * 4;
+  constexpr int BODY = ((RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES) + 15) / 16 * 16;
+
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint16_t* ks = reinterpret_cast<uint16_t*>(smem_raw);
+  uint16_t* vs = ks + kStages * TILE_ELEMS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + BODY);
+  uint64_t* empty = full + kStages;
+  int* flags = reinterpret_cast<int*>(empty + kStages);  // [0] abort, [1] is-last
+
+  const int split = blockIdx.x, kh = blockIdx.y;
+  const int z = blockIdx.z, seq = z / p.rows, row = z % p.rows;
+  const hb_decode_seq d = p.seqs ? p.seqs[seq] : p.one;
+  const int64_t n = d.past + row + 1;  // keys visible to this row
+  const int64_t p0 = int64_t(split) * p.chunk;
+  if (p0 >= n) return;  // beyond this unit's last split: not counted
+  const int64_t p1 = min(n, p0 + p.chunk);
+  const int active = int((n + p.chunk - 1) / p.chunk);
+  const int ntiles = int((p1 - p0 + kTile - 1) / kTile);
+  const uint16_t* kbase = d.keys + int64_t(kh) * d.kv_stride;
+  const uint16_t* vbase = d.values + int64_t(kh) * d.kv_stride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(vbase) |
+        reinterpret_cast<uintptr_t>(d.q) | reinterpret_cast<uintptr_t>(d.output)) & 15) != 0) {
+    if (threadIdx.x == 0) record_status(p.status, kStatusArg);
+    return;
+  }
+
+  if (warp == kConsumerWarps) {  // ---------------------------- producer
+    if (lane == 0) {
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % kStages;
+        if (t >= kStages && !mbar_wait(&empty[s], ((t / kStages) - 1) & 1)) {
+          record_status(p.status, kStatusTimeout);
+          atomicExch(&flags[0], 1);
+          break;
+        }
+        const int64_t pos = p0 + int64_t(t) * kTile;
+        const uint32_t bytes = uint32_t(min(int64_t(kTile), p1 - pos)) * HD * 2u;
+        mbar_arrive_expect_tx(&full[s], 2u * bytes);
+        bulk_g2s(ks + s * TILE_ELEMS, kbase + pos * HD, bytes, &full[s]);
+        bulk_g2s(vs + s * TILE_ELEMS, vbase + pos * HD, bytes, &full[s]);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int h0 = kh * G;  // first query head of the group
+  const uint16_t* qrow = d.q + int64_t(row) * p.q_row;
+  float q[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float t[DPL];
+    LaneVec<HD>::load(qrow + int64_t(h0 + g) * p.q_head + lane * DPL, t);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) q[g][i] = t[i];
+  }
+  float o[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[g][i] = 0.f;
+  float m_own = -INFINITY, l_own = 0.f;  // state of value head (lane >> SH) >> 2
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % kStages;
+    if (*reinterpret_cast<volatile int*>(&flags[0])) break;
+    if (!mbar_wait(&full[s], (t / kStages) & 1)) {
+      record_status(p.status, kStatusTimeout);
+      atomicExch(&flags[0], 1);
+      break;
+    }
+    const int64_t tile_pos = p0 + int64_t(t) * kTile;
+    const int base = warp * 4;
+    const int vc = int(max(int64_t(0), min(int64_t(4), p1 - tile_pos - base)));
+    if (vc > 0) {
+      const uint16_t* kt = ks + s * TILE_ELEMS + base * HD + lane * DPL;
+      const uint16_t* vt = vs + s * TILE_ELEMS + base * HD + lane * DPL;
+      float part[NV];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float kx[DPL];
+        if (j < vc) LaneVec<HD>::load(kt + j * HD, kx);
+        else {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) kx[i] = 0.f;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc = fmaf(q[g][i], kx[i], acc);
+          part[g * 4 + j] = acc;
+        }
+      }
+      const float dot = transpose_reduce<NV>(part, lane);
+      const int vidx = lane >> SH, jown = vidx & 3;
+      float sc = jown < vc ? dot * p.scale_log2 : -INFINITY;
+      // max over the 4 positions of this lane's head
+      float tmax = fmaxf(sc, __shfl_xor_sync(kFull, sc, 1 << SH));
+      tmax = fmaxf(tmax, __shfl_xor_sync(kFull, tmax, 2 << SH));
+      const float m_new = fmaxf(m_own, tmax);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float corr = fast_exp2(m_own - m_use);
+      const float pr = fast_exp2(sc - m_use);
+      float psum = pr + __shfl_xor_sync(kFull, pr, 1 << SH);
+      psum += __shfl_xor_sync(kFull, psum, 2 << SH);
+      l_own = l_own * corr + psum;
+      m_own = m_new;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float cg = __shfl_sync(kFull, corr, (g * 4) << SH);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) o[g][i] *= cg;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j < vc) {
+          float vx[DPL];
+          LaneVec<HD>::load(vt + j * HD, vx);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float pg = __shfl_sync(kFull, pr, (g * 4 + j) << SH);
+#pragma unroll
+            for (int i = 0; i < DPL; ++i) o[g][i] = fmaf(pg, vx[i], o[g][i]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+
+  // ------------------------------------------ merge the 8 warp states (smem)
+  consumer_sync();  // every warp is done reading the ring
+  float* ws = reinterpret_cast<float*>(smem_raw);  // [warp][G*HD + 2G]
+  {
+    float* mine = ws + warp * PSTRIDE;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) mine[g * HD + lane * DPL + i] = o[g][i];
+    if ((lane & ((4 << SH) - 1)) == 0) {
+      const int g = (lane >> SH) >> 2;
+      mine[G * HD + g] = m_own;
+      mine[G * HD + G + g] = l_own;
+    }
+  }
+  consumer_sync();
+
+  constexpr int NOUT = G * HD;
+  constexpr int PER_T = (NOUT + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32);
+  const int tid = threadIdx.x;
+  float* part_out = p.partials;
+  const int unit = z * p.hkv + kh;
+  float om[PER_T], ol[PER_T], oo[PER_T];
+#pragma unroll
+  for (int k = 0; k < PER_T; ++k) {
+    const int e = min(tid + k * kConsumerWarps * 32, NOUT - 1), g = e / HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ws[w * PSTRIDE + G * HD + g]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float Ls = 0.f, Os = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float f = fast_exp2(ws[w * PSTRIDE + G * HD + g] - Mu);
+      Ls += ws[w * PSTRIDE + G * HD + G + g] * f;
+      Os += ws[w * PSTRIDE + e] * f;
+    }
+    om[k] = M; ol[k] = Ls; oo[k] = Os;
+  }
+
+  if (active > 1) {
+    float* mine = part_out + (int64_t(unit) * p.nsplit + split) * PSTRIDE;
+#pragma unroll
+    for (int k = 0; k < PER_T; ++k) {
+      const int e = tid + k * kConsumerWarps * 32, g = e / HD;
+      if (e >= NOUT) break;
+      __stcg(mine + e, oo[k]);
+      if ((e % HD) == 0) {
+        __stcg(mine + G * HD + g, om[k]);
+        __stcg(mine + G * HD + G + g, ol[k]);
+      }
+    }
+    __threadfence();
+    consumer_sync();
+    if (tid == 0) {
+      const unsigned prev = atomicAdd(&p.counters[unit], 1u);
+      flags[1] = (prev == unsigned(active - 1));
+    }
+    consumer_sync();
+    if (!flags[1]) return;
+    __threadfence();
+    const float* up = part_out + int64_t(unit) * p.nsplit * PSTRIDE;
+#pragma unroll
+    for (int k = 0; k < PER_T; ++k) {
+      const int e = min(tid + k * kConsumerWarps * 32, NOUT - 1), g = e / HD;
+      float M = -INFINITY;
+      for (int sp = 0; sp < active; ++sp) M = fmaxf(M, __ldcg(up + sp * PSTRIDE + G * HD + g));
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float Ls = 0.f, Os = 0.f;
+      for (int sp = 0; sp < active; ++sp) {
+        const float f = fast_exp2(__ldcg(up + sp * PSTRIDE + G * HD + g) - Mu);
+        Ls += __ldcg(up + sp * PSTRIDE + G * HD + G + g) * f;
+        Os += __ldcg(up + sp * PSTRIDE + e) * f;
+      }
+      ol[k] = Ls; oo[k] = Os;
+    }
+    if (tid == 0) p.counters[unit] = 0u;  // leave the workspace reusable
+  }
+
+  // ---------------------------------------------------- finalise + gate
+  uint16_t* orow = d.output + int64_t(row) * p.out_row;
+#pragma unroll
+  for (int k = 0; k < PER_T; ++k) {
+    const int e = tid + k * kConsumerWarps * 32, g = e / HD, dd = e % HD;
+    if (e >= NOUT) break;
+    const int h = h0 + g;
+    const float val = ol[k] > 0.f ? oo[k] / ol[k] : 0.f;
+    uint16_t a = f32_to_bf16_cvtne(val);
+    if (p.gate_offset >= 0) a = gate_bf16(a, qrow[p.gate_offset + int64_t(h) * HD + dd]);
+    orow[int64_t(h) * HD + dd] = a;
+  }
+}
+
+template <int HD, int G>
+size_t smem_bytes() {
+  constexpr int kStages = Ring<HD>::stages;
+  const size_t ring = size_t(2) * kStages * kTile * HD * sizeof(uint16_t);
+  const size_t merge = size_t(kConsumerWarps) * (G * HD + 2 * G) * sizeof(float);
+  const size_t body = ((ring > merge ? ring : merge) + 15) / 16 * 16;
+  return body + 2 * kStages * sizeof(uint64_t) + 16;
+}
+
+template <int HD, int G>
+cudaError_t launch(const DecodeParams& p, int units_z, cudaStream_t st) {
+  const size_t smem = smem_bytes<HD, G>();
+  static DeviceFlags configured;  // the attribute is set once per device
+  cudaError_t e = configured.once([&] {
+    return cudaFuncSetAttribute(attn_decode_kernel<HD, G>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  });
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.nsplit, p.hkv, units_z);
+  attn_decode_kernel<HD, G><<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Positions per split: enough CTAs to cover the SMs several times over
+// (load balance across units of unequal length), at least two tiles each.
+int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms) {
+  const int64_t target = int64_t(num_sms) * 8;
+  int64_t c = (total_positions + target - 1) / target;
+  c = (c + kTile - 1) / kTile * kTile;
+  if (c < 2 * kTile) c = 2 * kTile;
+  if (c > 8192) c = 8192;
+  if (c > max_n) c = (max_n + kTile - 1) / kTile * kTile;
+  return int(c);
+}
+
+size_t decode_partial_floats(int64_t gqa, int64_t head_dim) {
+  return size_t(gqa * head_dim + 2 * gqa);
+}
+
+cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st) {
+  DecodeParams p;
+  p.seqs = L.seqs;
+  p.one = L.one;
+  p.rows = int(L.rows);
+  p.hkv = int(L.hkv);
+  p.q_row = L.q_row;
+  p.q_head = L.q_head;
+  p.out_row = L.out_row;
+  p.gate_offset = L.gate_offset;
+  p.scale_log2 = L.scale * 1.4426950408889634f;
+  p.chunk = L.chunk;
+  p.nsplit = L.nsplit;
+  p.status = L.status;
+  p.counters = L.counters;
+  p.partials = L.partials;
+  const int z = int(L.nseq * L.rows);
+#define HB_DECODE_CASE(HD_, G_) \
+  if (L.head_dim == HD_ && L.gqa == G_) return launch<HD_, G_>(p, z, st);
+  HB_DECODE_CASE(256, 1) HB_DECODE_CASE(256, 2) HB_DECODE_CASE(256, 4) HB_DECODE_CASE(256, 8)
+  HB_DECODE_CASE(128, 1) HB_DECODE_CASE(128, 2) HB_DECODE_CASE(128, 4) HB_DECODE_CASE(128, 8)
+#undef HB_DECODE_CASE
+  return cudaErrorInvalidValue;
+}
+
+bool decode_serves(int64_t head_dim, int64_t gqa) {
+  return (head_dim == 128 || head_dim == 256) && (gqa == 1 || gqa == 2 || gqa == 4 || gqa == 8);
+}
+
+}  // namespace hb

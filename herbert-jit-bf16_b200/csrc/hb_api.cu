@@ -1,0 +1,339 @@
+// hb_api.cu -- the C ABI of libherbert_b200: argument validation that
+// mirrors the reference's own refusals, workspace layout, and dispatch to
+// the sm_100a kernels.  No allocation, no CPU compute path: a shape no
+// kernel serves is refused with a named status.
+//
+// Validation follows the reference:
+//  - attention geometry: tile_selector (src/jit/target/x86/execution/attention.rs:56-89)
+//  - SDPA shape:         SdpaShape::check (src/jit/ir.rs:140-160), Decline (:177-230)
+//  - KV geometry:        KvSpec::validate (src/jit/execution/abi.rs:75-103)
+//  - DeltaNet geometry:  Shape::check (src/jit/execution/abi.rs:283-306)
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "hb_internal.h"
+
+namespace hb {
+namespace {
+
+thread_local char g_err[512] = "";
+
+hb_status fail(hb_status s, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return s;
+}
+
+hb_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(HB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+constexpr int64_t kI32Half = 0x3FFFFFFF;  // i32::MAX / 2, the reference's bound
+
+// AttentionSpec checks of the tile selector, plus the head_dim domain.
+hb_status check_spec(const hb_attn_spec* s) {
+  if (!s) return fail(HB_ERR_ARG, "attention spec is null");
+  if (s->sink) return fail(HB_DECLINE_SINK, "attention sink is not served (Qwen3.5 has none)");
+  if (s->heads <= 0 || s->gqa <= 0 || s->head_dim <= 0)
+    return fail(HB_DECLINE_EMPTY, "empty shape (heads=%lld gqa=%lld head_dim=%lld)",
+                (long long)s->heads, (long long)s->gqa, (long long)s->head_dim);
+  if (s->heads % s->gqa || s->q_head < s->head_dim || s->heads * s->q_head > s->q_row ||
+      s->heads * s->head_dim > s->out_row || s->heads > kI32Half || s->gqa > kI32Half ||
+      s->head_dim > kI32Half || s->q_row > kI32Half || s->q_head > kI32Half ||
+      s->out_row > kI32Half)
+    return fail(HB_DECLINE_GEOMETRY, "invalid generated attention geometry");
+  if (s->gate_offset >= 0 && s->gate_offset + s->heads * s->head_dim > s->q_row)
+    return fail(HB_DECLINE_GEOMETRY, "gate_offset %lld + heads*head_dim exceeds q_row %lld",
+                (long long)s->gate_offset, (long long)s->q_row);
+  if (!decode_serves(s->head_dim, s->gqa))
+    return fail(HB_DECLINE_HEAD_DIM,
+                "head_dim out of domain (served: 128, 256 with gqa 1/2/4/8); got head_dim=%lld gqa=%lld",
+                (long long)s->head_dim, (long long)s->gqa);
+  if (s->q_row % 8 || s->q_head % 8 || s->out_row % 8)
+    return fail(HB_ERR_ARG, "q_row, q_head and out_row must be multiples of 8 elements (16 bytes)");
+  return HB_OK;
+}
+
+hb_status check_call(const hb_attn_spec* s, const hb_attn_call* c) {
+  if (!c) return fail(HB_ERR_ARG, "attention call is null");
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty shape (rows=%lld)", (long long)c->rows);
+  if (!c->q || !c->keys || !c->values || !c->output)
+    return fail(HB_ERR_ARG, "null q/keys/values/output pointer");
+  if (!aligned16(c->q) || !aligned16(c->keys) || !aligned16(c->values) || !aligned16(c->output))
+    return fail(HB_ERR_ARG, "q/keys/values/output must be 16-byte aligned");
+  if (c->past < 0) return fail(HB_ERR_ARG, "negative past");
+  const int64_t n_max = c->past + c->rows;
+  if (c->kv_stride % 8) return fail(HB_ERR_ARG, "kv_stride must be a multiple of 8 elements");
+  if (c->kv_stride < n_max * s->head_dim)
+    return fail(HB_ERR_ARG, "kv_stride %lld cannot hold past+rows=%lld positions",
+                (long long)c->kv_stride, (long long)n_max);
+  if (c->capacity > 0 && (n_max > c->capacity || c->kv_stride < c->capacity * s->head_dim))
+    return fail(HB_ERR_ARG, "past+rows=%lld exceeds the KV reserve (capacity %lld)",
+                (long long)n_max, (long long)c->capacity);
+  if (!(c->scale == c->scale)) return fail(HB_ERR_ARG, "scale is NaN");
+  return HB_OK;
+}
+
+struct DecodePlan {
+  int64_t units;
+  int chunk, nsplit;
+  size_t counters_off, partials_off, bytes;
+};
+
+DecodePlan plan_decode(const hb_attn_spec* s, int64_t nseq, int64_t rows, int64_t max_n,
+                       int64_t total_positions) {
+  DecodePlan p;
+  const int64_t hkv = s->heads / s->gqa;
+  p.units = nseq * rows * hkv;
+  p.chunk = decode_chunk(total_positions * hkv, max_n, device_sms());
+  p.nsplit = int((max_n + p.chunk - 1) / p.chunk);
+  p.counters_off = kWsHeader;
+  p.partials_off = p.counters_off + align256(size_t(p.units) * sizeof(unsigned));
+  p.bytes = p.partials_off + align256(size_t(p.units) * size_t(p.nsplit) *
+                                      decode_partial_floats(s->gqa, s->head_dim) * sizeof(float));
+  return p;
+}
+
+// Positions summed over the rows of one sequence: row r sees past + r + 1.
+int64_t row_positions(int64_t past, int64_t rows) { return rows * past + rows * (rows + 1) / 2; }
+
+hb_status check_ws(void* ws, size_t have, size_t need) {
+  if (!ws) return fail(HB_ERR_WORKSPACE, "workspace is null (need %zu bytes)", need);
+  if (reinterpret_cast<uintptr_t>(ws) & 255)
+    return fail(HB_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if (have < need) return fail(HB_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", have, need);
+  return HB_OK;
+}
+
+}  // namespace
+
+int device_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int& v = cache[dev & 63];
+  if (v == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    v = n;
+  }
+  return v;
+}
+
+}  // namespace hb
+
+using namespace hb;
+
+extern "C" {
+
+int hb_version(void) { return (0 << 16) | 1; }
+
+const char* hb_last_error(void) { return g_err; }
+
+const char* hb_status_name(int status) {
+  switch (status) {
+    case HB_OK: return "HB_OK";
+    case HB_DECLINE_EMPTY: return "HB_DECLINE_EMPTY";
+    case HB_DECLINE_HEAD_DIM: return "HB_DECLINE_HEAD_DIM";
+    case HB_DECLINE_GEOMETRY: return "HB_DECLINE_GEOMETRY";
+    case HB_DECLINE_SINK: return "HB_DECLINE_SINK";
+    case HB_ERR_ARG: return "HB_ERR_ARG";
+    case HB_ERR_WORKSPACE: return "HB_ERR_WORKSPACE";
+    case HB_ERR_CUDA: return "HB_ERR_CUDA";
+    case HB_ERR_TIMEOUT: return "HB_ERR_TIMEOUT";
+    case HB_ERR_NCCL: return "HB_ERR_NCCL";
+    default: return "HB_UNKNOWN";
+  }
+}
+
+hb_status hb_workspace_init(void* ws, size_t bytes, hb_stream_t stream) {
+  if (!ws || bytes < kWsHeader) return fail(HB_ERR_WORKSPACE, "workspace null or under 256 bytes");
+  cudaError_t e = cudaMemsetAsync(ws, 0, bytes, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "hb_workspace_init");
+  return HB_OK;
+}
+
+hb_status hb_workspace_status(void* ws, size_t bytes, hb_stream_t stream) {
+  if (!ws || bytes < kWsHeader) return fail(HB_ERR_WORKSPACE, "workspace null or under 256 bytes");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int code = 0;
+  cudaError_t e = cudaMemcpyAsync(&code, ws, sizeof code, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "hb_workspace_status");
+  if (code == 0) return HB_OK;
+  e = cudaMemsetAsync(ws, 0, sizeof code, st);
+  if (e != cudaSuccess) return cuda_fail(e, "hb_workspace_status");
+  if (code == kStatusTimeout) return fail(HB_ERR_TIMEOUT, "a bounded device wait ran out");
+  return fail(HB_ERR_ARG, "a kernel met a misaligned or invalid table entry (code %d)", code);
+}
+
+size_t hb_attn_decode_workspace_bytes(const hb_attn_spec* s, const hb_attn_call* c) {
+  if (check_spec(s) != HB_OK || !c || c->rows <= 0 || c->past < 0) return 0;
+  return plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows)).bytes;
+}
+
+static hb_status decode_common(const hb_attn_spec* s, const hb_attn_call* c, void* ws,
+                               size_t ws_bytes, hb_stream_t stream) {
+  hb_status r = check_spec(s);
+  if (r != HB_OK) return r;
+  if ((r = check_call(s, c)) != HB_OK) return r;
+  const DecodePlan pl = plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows));
+  if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
+  DecodeLaunch L;
+  L.seqs = nullptr;
+  L.one.q = c->q;
+  L.one.keys = c->keys;
+  L.one.values = c->values;
+  L.one.output = c->output;
+  L.one.past = c->past;
+  L.one.kv_stride = c->kv_stride;
+  L.nseq = 1;
+  L.rows = c->rows;
+  L.hkv = s->heads / s->gqa;
+  L.gqa = s->gqa;
+  L.head_dim = s->head_dim;
+  L.q_row = s->q_row;
+  L.q_head = s->q_head;
+  L.out_row = s->out_row;
+  L.gate_offset = s->gate_offset;
+  L.scale = c->scale;
+  L.chunk = pl.chunk;
+  L.nsplit = pl.nsplit;
+  char* base = static_cast<char*>(ws);
+  L.status = reinterpret_cast<int*>(base);
+  L.counters = reinterpret_cast<unsigned*>(base + pl.counters_off);
+  L.partials = reinterpret_cast<float*>(base + pl.partials_off);
+  cudaError_t e = launch_attn_decode(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attn_decode launch");
+  return HB_OK;
+}
+
+hb_status hb_attn_decode(const hb_attn_spec* s, const hb_attn_call* c, void* ws, size_t ws_bytes,
+                         hb_stream_t stream) {
+  return decode_common(s, c, ws, ws_bytes, stream);
+}
+
+size_t hb_attn_decode_batch_workspace_bytes(const hb_attn_spec* s, int64_t nseq, int64_t max_past,
+                                            int64_t sum_past) {
+  if (check_spec(s) != HB_OK || nseq <= 0 || max_past < 0) return 0;
+  const int64_t total = sum_past > 0 ? sum_past + nseq : nseq * (max_past + 1);
+  return plan_decode(s, nseq, 1, max_past + 1, total).bytes;
+}
+
+hb_status hb_attn_decode_batch(const hb_attn_spec* s, const hb_decode_seq* seqs, int64_t nseq,
+                               int64_t max_past, int64_t sum_past, void* ws, size_t ws_bytes,
+                               hb_stream_t stream) {
+  hb_status r = check_spec(s);
+  if (r != HB_OK) return r;
+  if (nseq <= 0) return fail(HB_DECLINE_EMPTY, "empty batch");
+  if (!seqs) return fail(HB_ERR_ARG, "sequence table is null");
+  if (max_past < 0) return fail(HB_ERR_ARG, "negative max_past");
+  if (nseq > 65535) return fail(HB_DECLINE_GEOMETRY, "at most 65535 sequences per call");
+  const int64_t total = sum_past > 0 ? sum_past + nseq : nseq * (max_past + 1);
+  const DecodePlan pl = plan_decode(s, nseq, 1, max_past + 1, total);
+  if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
+  DecodeLaunch L;
+  memset(&L.one, 0, sizeof L.one);
+  L.seqs = seqs;
+  L.nseq = nseq;
+  L.rows = 1;
+  L.hkv = s->heads / s->gqa;
+  L.gqa = s->gqa;
+  L.head_dim = s->head_dim;
+  L.q_row = s->q_row;
+  L.q_head = s->q_head;
+  L.out_row = s->out_row;
+  L.gate_offset = s->gate_offset;
+  // the scale of a batch: 1/sqrt(head_dim), as ModelShape::scale without attn_scale
+  L.scale = 1.0f / std::sqrt(float(s->head_dim));
+  L.chunk = pl.chunk;
+  L.nsplit = pl.nsplit;
+  char* base = static_cast<char*>(ws);
+  L.status = reinterpret_cast<int*>(base);
+  L.counters = reinterpret_cast<unsigned*>(base + pl.counters_off);
+  L.partials = reinterpret_cast<float*>(base + pl.partials_off);
+  cudaError_t e = launch_attn_decode(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attn_decode_batch launch");
+  return HB_OK;
+}
+
+size_t hb_attn_prefill_workspace_bytes(const hb_attn_spec* s, const hb_attn_call* c) {
+  return hb_attn_decode_workspace_bytes(s, c);
+}
+
+hb_status hb_attn_prefill(const hb_attn_spec* s, const hb_attn_call* c, void* ws, size_t ws_bytes,
+                          hb_stream_t stream) {
+  return decode_common(s, c, ws, ws_bytes, stream);
+}
+
+hb_status hb_kv_append(const hb_kv_spec* s, const hb_kv_call* c, hb_stream_t stream) {
+  if (!s || !c) return fail(HB_ERR_ARG, "kv spec or call is null");
+  const bool valid = s->heads > 0 && s->head_dim > 0 && s->max_batch > 0 &&
+                     s->capacity >= s->max_batch && s->capacity * s->head_dim <= s->stride &&
+                     s->heads * s->head_dim * 2 <= 0x7FFFFFFF && s->stride <= 0x3FFFFFFF;
+  if (!valid) return fail(HB_DECLINE_GEOMETRY, "invalid generated KV reserve geometry");
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty KV append");
+  if (!c->keys || !c->values || !c->input_keys || !c->input_values)
+    return fail(HB_ERR_ARG, "null KV append pointer");
+  if (c->rows > s->max_batch || c->past < 0 || c->past + c->rows > s->capacity)
+    return fail(HB_ERR_ARG, "append of %lld rows at %lld exceeds the reserve (capacity %lld, batch %lld)",
+                (long long)c->rows, (long long)c->past, (long long)s->capacity,
+                (long long)s->max_batch);
+  cudaError_t e = launch_kv_append(*s, *c, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "kv_append launch");
+  return HB_OK;
+}
+
+static hb_status check_gdn(const hb_gdn_shape* s, const hb_gdn_call* c) {
+  if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or call is null");
+  const int64_t lim = int64_t(1) << 16;
+  if (s->nk <= 0 || s->nv <= 0 || s->nv % s->nk || s->hkd <= 0 || s->hvd <= 0 || s->nk > lim ||
+      s->nv > lim || s->hkd > lim || s->hvd > lim ||
+      (2 * s->nk * s->hkd + s->nv * s->hvd) > 0x7FFFFFFF / 16 ||
+      s->nv * s->hkd * s->hvd > 0x7FFFFFFF / 4)
+    return fail(HB_DECLINE_GEOMETRY, "invalid generated DeltaNet geometry");
+  if (!gdn_decode_serves(*s))
+    return fail(HB_DECLINE_HEAD_DIM, "DeltaNet head dims not served (hkd 64/128, hvd multiple of 32)");
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
+  if (!c->state || !c->output || !c->qkv || !c->beta || !c->decay)
+    return fail(HB_ERR_ARG, "null DeltaNet pointer");
+  if (c->l2 && !(c->eps >= 0.f)) return fail(HB_ERR_ARG, "invalid L2 eps");
+  return HB_OK;
+}
+
+hb_status hb_gdn_decode(const hb_gdn_shape* s, const hb_gdn_call* c, hb_stream_t stream) {
+  hb_status r = check_gdn(s, c);
+  if (r != HB_OK) return r;
+  GdnLaunch L;
+  L.shape = *s;
+  L.call = *c;
+  L.scale = 1.0f / std::sqrt(float(s->hkd));
+  cudaError_t e = launch_gdn_decode(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_decode launch");
+  return HB_OK;
+}
+
+size_t hb_gdn_prefill_workspace_bytes(const hb_gdn_shape* s, int64_t rows) {
+  (void)s;
+  (void)rows;
+  return kWsHeader;
+}
+
+hb_status hb_gdn_prefill(const hb_gdn_shape* s, const hb_gdn_call* c, void* ws, size_t ws_bytes,
+                         hb_stream_t stream) {
+  (void)ws;
+  (void)ws_bytes;
+  return hb_gdn_decode(s, c, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+// hb_internal.h -- declarations shared between the host API layer
+// (hb_api.cu) and the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/herbert_b200.h"
+
+namespace hb {
+
+// Once-per-device initialisation flag (function attributes are per device).
+struct DeviceFlags {
+  std::atomic<uint64_t> done{0};
+  template <class F>
+  cudaError_t once(F&& f) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = uint64_t(1) << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    e = f();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+  }
+};
+
+// Codes of the device-side status word kept at the head of every workspace.
+enum : int { kStatusOk = 0, kStatusTimeout = 1, kStatusArg = 2 };
+
+// Layout of every workspace: a 256-byte header whose first int is the
+// device-side status word, then the kernel's own sections (256-aligned).
+constexpr size_t kWsHeader = 256;
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// ----------------------------------------------------------- attn decode
+struct DecodeLaunch {
+  const hb_decode_seq* seqs;  // device table or nullptr
+  hb_decode_seq one;          // the single sequence when seqs == nullptr
+  int64_t nseq, rows, hkv, gqa, head_dim;
+  int64_t q_row, q_head, out_row, gate_offset;
+  float scale;
+  int chunk, nsplit;
+  int* status;
+  unsigned* counters;
+  float* partials;
+};
+bool decode_serves(int64_t head_dim, int64_t gqa);
+int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms);
+size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
+cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
+
+// ------------------------------------------------------------ kv append
+cudaError_t launch_kv_append(const hb_kv_spec& s, const hb_kv_call& c, cudaStream_t st);
+
+// ------------------------------------------------------------ gdn decode
+struct GdnLaunch {
+  hb_gdn_shape shape;
+  hb_gdn_call call;
+  float scale;  // 1/sqrt(hkd), f32 as the reference computes it
+};
+bool gdn_decode_serves(const hb_gdn_shape& s);
+cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st);
+
+// Number of SMs of the current device (cached per device).
+int device_sms();
+
+}  // namespace hb

@@ -1,0 +1,283 @@
+"""Python binding of ``libherbert_b200.so`` -- the B200 attention hot path of
+the herbert-jit-bf16 Qwen3.5 engine behind the C ABI of
+``include/herbert_b200.h``.
+
+The records mirror the reference's call records field for field
+(src/jit/execution/abi.rs): ``AttentionSpec`` / ``AttentionCall`` (:136-180),
+``KvSpec`` / ``KvCall`` (:57-130), ``DeltaShape`` (``Shape``, :266-307) and
+``RecurrenceCall`` (:310-317).  The entry points mirror the node kernels of
+``trait KernelSet`` (src/jit/target/mod.rs:194-240): ``attention`` (the
+attention tile selector plus the output-gate node), ``kv_append`` and
+``delta_recurrence``.  A shape the kernels do not serve raises ``Decline``
+(the reference's named refusal, src/jit/ir.rs:177-230) so a caller can fall
+back; any other failure raises ``HBError``.
+
+There is no CPU path here: every call runs the CUDA library, and importing
+the binding without the built library fails loudly.  torch is used only for
+device memory and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_float, c_int32, c_int64, c_size_t, c_void_p
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libherbert_b200.so")
+HEADER_PATH = os.path.join(os.path.dirname(PKG_DIR), "include", "herbert_b200.h")
+
+HB_OK = 0
+HB_DECLINE_EMPTY = 1
+HB_DECLINE_HEAD_DIM = 2
+HB_DECLINE_GEOMETRY = 3
+HB_DECLINE_SINK = 4
+HB_ERR_ARG = 10
+HB_ERR_WORKSPACE = 11
+HB_ERR_CUDA = 12
+HB_ERR_TIMEOUT = 13
+HB_ERR_NCCL = 14
+
+
+class HBError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{status_name(status)}: {message}")
+
+
+class Decline(HBError):
+    """The kernels refuse this shape; the caller falls back."""
+
+
+class AttentionSpec(ctypes.Structure):
+    _fields_ = [("heads", c_int64), ("gqa", c_int64), ("head_dim", c_int64),
+                ("q_row", c_int64), ("q_head", c_int64), ("out_row", c_int64),
+                ("gate_offset", c_int64), ("grouped", c_int32), ("sink", c_int32)]
+
+
+class AttentionCall(ctypes.Structure):
+    _fields_ = [("q", c_void_p), ("keys", c_void_p), ("values", c_void_p),
+                ("output", c_void_p), ("rows", c_int64), ("past", c_int64),
+                ("kv_stride", c_int64), ("capacity", c_int64), ("scale", c_float),
+                ("sink", c_float)]
+
+
+class DecodeSeq(ctypes.Structure):
+    _fields_ = [("q", c_void_p), ("keys", c_void_p), ("values", c_void_p),
+                ("output", c_void_p), ("past", c_int64), ("kv_stride", c_int64)]
+
+
+class KvSpec(ctypes.Structure):
+    _fields_ = [("heads", c_int64), ("head_dim", c_int64), ("stride", c_int64),
+                ("capacity", c_int64), ("max_batch", c_int64)]
+
+
+class KvCall(ctypes.Structure):
+    _fields_ = [("keys", c_void_p), ("values", c_void_p), ("input_keys", c_void_p),
+                ("input_values", c_void_p), ("rows", c_int64), ("past", c_int64)]
+
+
+class DeltaShape(ctypes.Structure):
+    _fields_ = [("nk", c_int64), ("nv", c_int64), ("hkd", c_int64), ("hvd", c_int64)]
+
+
+class RecurrenceCall(ctypes.Structure):
+    _fields_ = [("state", c_void_p), ("output", c_void_p), ("qkv", c_void_p),
+                ("beta", c_void_p), ("decay", c_void_p), ("rows", c_int64),
+                ("l2", c_int32), ("eps", c_float)]
+
+
+_P = ctypes.POINTER
+_lib = None
+
+# name -> (restype, argtypes); every function the header declares.
+_SIGNATURES = {
+    "hb_version": (ctypes.c_int, []),
+    "hb_last_error": (ctypes.c_char_p, []),
+    "hb_status_name": (ctypes.c_char_p, [ctypes.c_int]),
+    "hb_workspace_init": (ctypes.c_int, [c_void_p, c_size_t, c_void_p]),
+    "hb_workspace_status": (ctypes.c_int, [c_void_p, c_size_t, c_void_p]),
+    "hb_attn_decode_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionCall)]),
+    "hb_attn_decode": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
+                                      c_void_p]),
+    "hb_attn_decode_batch_workspace_bytes": (c_size_t, [_P(AttentionSpec), c_int64, c_int64,
+                                                        c_int64]),
+    "hb_attn_decode_batch": (ctypes.c_int, [_P(AttentionSpec), c_void_p, c_int64, c_int64,
+                                            c_int64, c_void_p, c_size_t, c_void_p]),
+    "hb_attn_prefill_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionCall)]),
+    "hb_attn_prefill": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
+                                       c_void_p]),
+    "hb_kv_append": (ctypes.c_int, [_P(KvSpec), _P(KvCall), c_void_p]),
+    "hb_gdn_decode": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceCall), c_void_p]),
+    "hb_gdn_prefill_workspace_bytes": (c_size_t, [_P(DeltaShape), c_int64]),
+    "hb_gdn_prefill": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceCall), c_void_p, c_size_t,
+                                      c_void_p]),
+}
+
+
+def lib():
+    """Load the CUDA library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"libherbert_b200.so is missing at {LIB_PATH}: run __graft_entry__.build() "
+                "(there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def status_name(status: int) -> str:
+    return lib().hb_status_name(status).decode()
+
+
+def last_error() -> str:
+    return lib().hb_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status == HB_OK:
+        return
+    msg = last_error()
+    if status < HB_ERR_ARG:
+        raise Decline(status, msg)
+    raise HBError(status, msg)
+
+
+def version() -> tuple:
+    v = lib().hb_version()
+    return (v >> 16, v & 0xFFFF)
+
+
+# ----------------------------------------------------------- torch plumbing
+
+def _stream(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return c_void_p(stream.cuda_stream)
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+class Workspace:
+    """Caller-owned device scratch for one or more calls (zeroed once)."""
+
+    def __init__(self, nbytes: int, device=None, stream=None):
+        import torch
+        self.nbytes = max(256, int(nbytes))
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device or "cuda")
+        check(lib().hb_workspace_init(c_void_p(self.ptr), self.nbytes, _stream(stream)))
+
+    @property
+    def ptr(self) -> int:
+        return int(self.buf.data_ptr())
+
+    def ensure(self, nbytes: int, stream=None) -> "Workspace":
+        if nbytes > self.nbytes:
+            self.__init__(nbytes, self.buf.device, stream)
+        return self
+
+    def status(self, stream=None) -> None:
+        check(lib().hb_workspace_status(c_void_p(self.ptr), self.nbytes, _stream(stream)))
+
+
+def attention_spec(heads=16, gqa=4, head_dim=256, gated=True, q_row=None, out_row=None,
+                   q_head=None) -> AttentionSpec:
+    """The Qwen3.5 layer geometry: q rows [Q | gate] (src/jit/schedule.rs:172-186)."""
+    qd = heads * head_dim
+    return AttentionSpec(heads=heads, gqa=gqa, head_dim=head_dim,
+                         q_row=q_row if q_row is not None else (2 * qd if gated else qd),
+                         q_head=q_head if q_head is not None else head_dim,
+                         out_row=out_row if out_row is not None else qd,
+                         gate_offset=qd if gated else -1, grouped=0, sink=0)
+
+
+def attention(spec: AttentionSpec, q, keys, values, out, *, rows: int, past: int,
+              kv_stride: int, capacity: int = 0, scale: float | None = None,
+              regime: str = "decode", workspace: Workspace | None = None, stream=None):
+    """The attention node + output-gate node over device tensors (bf16 or int16/uint16 views).
+
+    regime "decode" runs the split-KV kernel, "prefill" the causal flash
+    attention kernel.  Returns the workspace used (reuse it across calls)."""
+    call = AttentionCall(q=_ptr(q), keys=_ptr(keys), values=_ptr(values), output=_ptr(out),
+                         rows=rows, past=past, kv_stride=kv_stride, capacity=capacity,
+                         scale=(1.0 / spec.head_dim ** 0.5) if scale is None else scale, sink=0.0)
+    L = lib()
+    if regime == "decode":
+        need, run = L.hb_attn_decode_workspace_bytes, L.hb_attn_decode
+    elif regime == "prefill":
+        need, run = L.hb_attn_prefill_workspace_bytes, L.hb_attn_prefill
+    else:
+        raise ValueError(regime)
+    nbytes = need(ctypes.byref(spec), ctypes.byref(call))
+    if nbytes == 0:
+        # the size query refuses what the call refuses: let the call name it
+        check(run(ctypes.byref(spec), ctypes.byref(call), None, 0, _stream(stream)))
+    if workspace is None:
+        workspace = Workspace(nbytes, q.device, stream)
+    else:
+        workspace.ensure(nbytes, stream)
+    check(run(ctypes.byref(spec), ctypes.byref(call), c_void_p(workspace.ptr), workspace.nbytes,
+              _stream(stream)))
+    return workspace
+
+
+def decode_batch(spec: AttentionSpec, seqs_table, nseq: int, max_past: int, sum_past: int = 0,
+                 workspace: Workspace | None = None, stream=None, device=None):
+    """Batched decode over a device table of DecodeSeq records (uint8 tensor)."""
+    L = lib()
+    nbytes = L.hb_attn_decode_batch_workspace_bytes(ctypes.byref(spec), nseq, max_past, sum_past)
+    if workspace is None:
+        workspace = Workspace(nbytes, device or seqs_table.device, stream)
+    else:
+        workspace.ensure(nbytes, stream)
+    check(L.hb_attn_decode_batch(ctypes.byref(spec), c_void_p(_ptr(seqs_table)), nseq, max_past,
+                                 sum_past, c_void_p(workspace.ptr), workspace.nbytes,
+                                 _stream(stream)))
+    return workspace
+
+
+def seq_table(entries, device="cuda"):
+    """Pack DecodeSeq records into a device uint8 tensor."""
+    import torch
+    arr = (DecodeSeq * len(entries))(*entries)
+    raw = bytes(arr)
+    host = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
+    return host.to(device)
+
+
+def kv_append(spec: KvSpec, keys, values, input_keys, input_values, *, rows: int, past: int,
+              stream=None) -> None:
+    call = KvCall(keys=_ptr(keys), values=_ptr(values), input_keys=_ptr(input_keys),
+                  input_values=_ptr(input_values), rows=rows, past=past)
+    check(lib().hb_kv_append(ctypes.byref(spec), ctypes.byref(call), _stream(stream)))
+
+
+def delta_recurrence(shape: DeltaShape, state, out, qkv, beta, decay, *, rows: int,
+                     l2: bool = True, eps: float = 1e-6, regime: str = "decode",
+                     workspace: Workspace | None = None, stream=None):
+    """The delta-l2-gates L2 step + delta-causal-recurrence node (f32 tensors).
+
+    regime "decode": positions in order with the reference's rounding;
+    "prefill": the chunked kernel."""
+    call = RecurrenceCall(state=_ptr(state), output=_ptr(out), qkv=_ptr(qkv), beta=_ptr(beta),
+                          decay=_ptr(decay), rows=rows, l2=int(l2), eps=eps)
+    L = lib()
+    if regime == "decode":
+        check(L.hb_gdn_decode(ctypes.byref(shape), ctypes.byref(call), _stream(stream)))
+        return workspace
+    nbytes = L.hb_gdn_prefill_workspace_bytes(ctypes.byref(shape), rows)
+    if workspace is None:
+        workspace = Workspace(nbytes, state.device, stream)
+    else:
+        workspace.ensure(nbytes, stream)
+    check(L.hb_gdn_prefill(ctypes.byref(shape), ctypes.byref(call), c_void_p(workspace.ptr),
+                           workspace.nbytes, _stream(stream)))
+    return workspace

@@ -1,0 +1,225 @@
+/*
+ * herbert_b200.h -- C ABI of the B200 (sm_100a) attention hot path of the
+ * herbert-jit-bf16 Qwen3.5 engine: full-attention SDPA (GQA over a bf16 KV
+ * cache, f32 softmax/accumulators, bf16 out, sigmoid output gate) in the
+ * prefill and decode regimes, and the GatedDeltaNet mixer core (recurrent
+ * decode over an f32 per-head state, chunked prefill).
+ *
+ * Conventions
+ *  - Every pointer in a *_call record is DEVICE memory; records themselves
+ *    are read on the host during the call (they may live on the stack).
+ *  - Strides are in ELEMENTS (bf16 for attention, f32 for DeltaNet), as in
+ *    the reference's call records.
+ *  - Layouts are the reference's:
+ *      KV cache  [kv_head][capacity][head_dim] bf16, head h at h*kv_stride
+ *                (src/jit/model.rs:545-559; src/jit/execution/abi.rs:57-130)
+ *      q row     [Q_0 .. Q_{H-1} | g_0 .. g_{H-1}] (src/jit/schedule.rs:109-133)
+ *      DeltaNet  qkv [rows][2*nk*hkd + nv*hvd] f32, beta/decay [rows][nv] f32,
+ *                state [nv][hkd][hvd] f32, out [rows][nv*hvd] f32
+ *                (src/jit/target/x86/execution/delta.rs:519-607)
+ *  - Calls are stream-ordered and never allocate.  Scratch ("workspace") is
+ *    owned by the caller and sized by the *_workspace_bytes queries; a
+ *    workspace must be zeroed once after allocation (hb_workspace_init) and
+ *    every completed call leaves it reusable without re-zeroing.  Calls that
+ *    share one workspace must be ordered on the GPU (same stream or events).
+ *  - A shape the kernels do not serve is refused with an HB_DECLINE_* status,
+ *    as the reference's emitters refuse with a named Decline
+ *    (src/jit/ir.rs:177-230); the caller falls back.  Failures return
+ *    HB_ERR_*; hb_last_error() gives a thread-local message.
+ */
+#ifndef HERBERT_B200_H
+#define HERBERT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HB_API __attribute__((visibility("default")))
+#else
+#define HB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without including the CUDA headers; 0 = the legacy stream. */
+typedef struct CUstream_st *hb_stream_t;
+
+typedef enum hb_status {
+    HB_OK = 0,
+    /* Refusals (src/jit/ir.rs:177-230 Decline, abi.rs validate/check). */
+    HB_DECLINE_EMPTY = 1,     /* Decline::Empty: zero rows / heads / length   */
+    HB_DECLINE_HEAD_DIM = 2,  /* Decline::HeadDim: head_dim not served        */
+    HB_DECLINE_GEOMETRY = 3,  /* "invalid generated ... geometry"             */
+    HB_DECLINE_SINK = 4,      /* attention sink (not used by Qwen3.5)         */
+    /* Errors. */
+    HB_ERR_ARG = 10,          /* null / misaligned pointer, capacity exceeded */
+    HB_ERR_WORKSPACE = 11,    /* workspace too small or misaligned            */
+    HB_ERR_CUDA = 12,         /* a CUDA runtime call failed                   */
+    HB_ERR_TIMEOUT = 13,      /* a bounded device wait ran out                */
+    HB_ERR_NCCL = 14          /* reserved for multi-GPU entry points          */
+} hb_status;
+
+/* Library version, (major << 16) | minor. */
+HB_API int hb_version(void);
+/* Message of the last non-OK status on this thread ("" if none). */
+HB_API const char *hb_last_error(void);
+/* Static name of a status code. */
+HB_API const char *hb_status_name(int status);
+/* Zero a freshly allocated workspace (one cudaMemsetAsync on `stream`). */
+HB_API hb_status hb_workspace_init(void *workspace, size_t bytes, hb_stream_t stream);
+/* Read (and clear) the device-side status word of a workspace: HB_OK,
+ * HB_ERR_TIMEOUT if a kernel's bounded wait ran out, HB_ERR_ARG if a kernel
+ * met a misaligned table entry.  Synchronises `stream`. */
+HB_API hb_status hb_workspace_status(void *workspace, size_t bytes, hb_stream_t stream);
+
+/* ------------------------------------------------------------------ SDPA */
+
+/* Per-layer attention geometry: AttentionSpec (src/jit/execution/abi.rs:136-151)
+ * plus the gate position of the output-gate node (src/jit/schedule/lowering.rs:642-666). */
+typedef struct hb_attn_spec {
+    int64_t heads;       /* query heads (Qwen3.5: 16)                          */
+    int64_t gqa;         /* query heads per KV head (4)                        */
+    int64_t head_dim;    /* elements per head (256)                            */
+    int64_t q_row;       /* elements between query rows (2*heads*head_dim)     */
+    int64_t q_head;      /* elements between query heads (head_dim)            */
+    int64_t out_row;     /* elements between output rows (heads*head_dim)      */
+    int64_t gate_offset; /* elements from a q row to its gate (heads*head_dim);
+                            < 0: no gate node, the output is the SDPA alone    */
+    int32_t grouped;     /* AttentionSpec::grouped task order (no effect on results) */
+    int32_t sink;        /* SdpaShape::sink: must be 0 (declined otherwise)    */
+} hb_attn_spec;
+
+/* One attention operation: AttentionCall (src/jit/execution/abi.rs:156-180).
+ * Row r (0 <= r < rows) is the query at absolute position past + r; it sees
+ * past + r + 1 keys, which must already be in the cache. */
+typedef struct hb_attn_call {
+    const uint16_t *q;       /* query rows (bf16), row stride spec.q_row       */
+    const uint16_t *keys;    /* head-major K cache (bf16)                      */
+    const uint16_t *values;  /* head-major V cache (bf16)                      */
+    uint16_t *output;        /* token-major output (bf16), row stride out_row  */
+    int64_t rows;            /* query rows in this block (>= 1)                */
+    int64_t past;            /* absolute position of row 0                     */
+    int64_t kv_stride;       /* elements between KV heads (capacity*head_dim)  */
+    int64_t capacity;        /* positions reserved per KV head; 0 = unchecked  */
+    float scale;             /* softmax scale (1/sqrt(head_dim))               */
+    float sink;              /* ignored unless spec.sink                       */
+} hb_attn_call;
+
+/* One sequence of a batched decode step (device memory, one row each). */
+typedef struct hb_decode_seq {
+    const uint16_t *q;       /* the sequence's query row                       */
+    const uint16_t *keys;    /* its K cache                                    */
+    const uint16_t *values;  /* its V cache                                    */
+    uint16_t *output;        /* its output row                                 */
+    int64_t past;            /* positions already cached (sees past + 1 keys)  */
+    int64_t kv_stride;       /* elements between its KV heads                  */
+} hb_decode_seq;
+
+/*
+ * Decode SDPA (split-KV flash decoding) for `rows` query rows of one
+ * sequence.  Replaces the attention node in the decode regime:
+ * SdpaHeadFn (src/jit/emit_sdpa.rs:131-140) driven by the tile selector
+ * (src/jit/target/x86/execution/attention.rs:56-224), followed by the
+ * output-gate node ElemOp::SigmoidMul (src/jit/target/x86/emit_elem.rs:333-420).
+ */
+HB_API size_t hb_attn_decode_workspace_bytes(const hb_attn_spec *spec, const hb_attn_call *call);
+HB_API hb_status hb_attn_decode(const hb_attn_spec *spec, const hb_attn_call *call,
+                         void *workspace, size_t workspace_bytes, hb_stream_t stream);
+
+/*
+ * Batched decode: `nseq` independent sequences (table in device memory),
+ * one query row each; max_past bounds every seqs[i].past and sum_past is
+ * their sum (0 = unknown), used only to size the splits.  No counterpart in
+ * the reference (one Runner = one sequence, src/jit/model.rs:329-396); it is
+ * the single-sequence node above applied per sequence.  Pointers in the
+ * table must be 16-byte aligned (a misaligned entry is skipped and reported
+ * through hb_workspace_status as HB_ERR_ARG).
+ */
+HB_API size_t hb_attn_decode_batch_workspace_bytes(const hb_attn_spec *spec, int64_t nseq,
+                                            int64_t max_past, int64_t sum_past);
+HB_API hb_status hb_attn_decode_batch(const hb_attn_spec *spec, const hb_decode_seq *seqs,
+                               int64_t nseq, int64_t max_past, int64_t sum_past,
+                               void *workspace, size_t workspace_bytes, hb_stream_t stream);
+
+/*
+ * Prefill SDPA: causal flash attention over `rows` query rows (tcgen05 MMA,
+ * TMEM accumulators).  Replaces the attention node in the prefill regime:
+ * SdpaPrefillFn blocks (src/jit/emit_sdpa.rs:173-304;
+ * src/jit/target/x86/emit_sdpa/x86/prefill.rs:733-912) plus the decode
+ * kernel for remainder rows, then the output-gate node.
+ */
+HB_API size_t hb_attn_prefill_workspace_bytes(const hb_attn_spec *spec, const hb_attn_call *call);
+HB_API hb_status hb_attn_prefill(const hb_attn_spec *spec, const hb_attn_call *call,
+                          void *workspace, size_t workspace_bytes, hb_stream_t stream);
+
+/* KV cache geometry: KvSpec (src/jit/execution/abi.rs:57-104). */
+typedef struct hb_kv_spec {
+    int64_t heads;      /* KV heads                        */
+    int64_t head_dim;   /* bf16 elements per head          */
+    int64_t stride;     /* bf16 elements reserved per head */
+    int64_t capacity;   /* positions reserved per head     */
+    int64_t max_batch;  /* maximum rows in one block       */
+} hb_kv_spec;
+
+/* KV append: KvCall (abi.rs:108-130) and append (src/jit/target/x86/execution/kv.rs:17-69):
+ * K[h][past + r][:] <- input_keys[r][h][:] (same for V), token-major inputs
+ * with row stride heads*head_dim. */
+typedef struct hb_kv_call {
+    uint16_t *keys;
+    uint16_t *values;
+    const uint16_t *input_keys;
+    const uint16_t *input_values;
+    int64_t rows;
+    int64_t past;
+} hb_kv_call;
+HB_API hb_status hb_kv_append(const hb_kv_spec *spec, const hb_kv_call *call, hb_stream_t stream);
+
+/* ------------------------------------------------------------- DeltaNet */
+
+/* DeltaNet geometry: Shape (src/jit/execution/abi.rs:266-307) without the conv width. */
+typedef struct hb_gdn_shape {
+    int64_t nk;   /* key heads (16)    */
+    int64_t nv;   /* value heads (32)  */
+    int64_t hkd;  /* key head dim (128)*/
+    int64_t hvd;  /* value head dim (128) */
+} hb_gdn_shape;
+
+/* RecurrenceCall (src/jit/execution/abi.rs:310-317) plus the L2 step of the
+ * delta-l2-gates node (src/jit/target/x86/execution/delta.rs:442-515). */
+typedef struct hb_gdn_call {
+    float *state;        /* [nv][hkd][hvd], read and updated in place      */
+    float *output;       /* [rows][nv*hvd]                                 */
+    const float *qkv;    /* [rows][2*nk*hkd + nv*hvd] (not modified)       */
+    const float *beta;   /* [rows][nv]                                     */
+    const float *decay;  /* [rows][nv]                                     */
+    int64_t rows;        /* positions in this block (>= 1)                 */
+    int32_t l2;          /* 1: L2-normalise q and k heads on load (eps)    */
+    float eps;           /* DN_L2_EPS = 1e-6 (src/jit/schedule/deltanet.rs:69) */
+} hb_gdn_call;
+
+/*
+ * Recurrent DeltaNet: the positions in order, one step each.  Replaces the
+ * delta-causal-recurrence node (RecurrenceFn, src/jit/emit_recurrence.rs:63-73;
+ * x86 src/jit/target/x86/emit_recurrence.rs:108-217; traversal
+ * src/jit/target/x86/execution/delta.rs:519-607) with the default non-FMA
+ * order, so the state and outputs are the reference's bits.
+ */
+HB_API hb_status hb_gdn_decode(const hb_gdn_shape *shape, const hb_gdn_call *call, hb_stream_t stream);
+
+/*
+ * Chunked DeltaNet prefill (chunk 64, WY/UT form, intra-chunk products on
+ * tcgen05).  Same inputs and outputs as hb_gdn_decode; sums are
+ * reassociated (the reference's own chunked form,
+ * src/jit/target/aarch64/deltanet_chunk.rs:6-15, is also not the bits of
+ * the sequential recurrence).
+ */
+HB_API size_t hb_gdn_prefill_workspace_bytes(const hb_gdn_shape *shape, int64_t rows);
+HB_API hb_status hb_gdn_prefill(const hb_gdn_shape *shape, const hb_gdn_call *call, void *workspace,
+                         size_t workspace_bytes, hb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HERBERT_B200_H */

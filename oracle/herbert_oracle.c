@@ -1,0 +1,627 @@
+/*
+ * herbert_oracle.c -- CPU restatement of the reference's attention-path
+ * kernels.  TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU
+ * baseline.  The product library never links it.
+ *
+ * Parity unpinned by reference outputs (the Rust reference cannot be built
+ * here and has no golden vectors); pinned instead against the x86 hardware
+ * semantics of the instructions the reference emits -- see the header.
+ *
+ * Build: -O2 -ffp-contract=off (no silent mul+add contraction: the
+ * reference's non-FMA forms round the product and the sum separately).
+ */
+#include "herbert_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#if defined(__x86_64__)
+#include <immintrin.h>
+#define ORC_X86 1
+#else
+#define ORC_X86 0
+#endif
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ---------------------------------------------------------------- bits */
+
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* The eight constants of the emitted exp polynomial
+ * (src/jit/exp_constants.rs:14-23), as f32 literals. */
+#define EXP_NEG87 (-87.33654f)
+#define EXP_LOG2E (1.442695f)
+#define EXP_C4 (0.00967248f)
+#define EXP_C3 (0.05550411f)
+#define EXP_C2 (0.2402265f)
+#define EXP_C1 (0.6931472f)
+#define EXP_C0 (1.0f)
+#define EXP_ONE_BITS 0x3F800000u
+/* Upper bound of the gate's exp argument (src/jit/target/x86/emit_elem.rs:61). */
+#define EXP_MAX88 (88.0f)
+
+float orc_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+/* vcvtneps2bf16: zero and denormal inputs give a signed zero, NaN a quiet
+ * NaN, infinities pass, everything else rounds to nearest even.  For finite
+ * normal values this is src/core/tensor.rs:14-24. */
+uint16_t orc_f32_to_bf16_cvtne(float x) {
+    uint32_t u = f2u(x);
+    uint32_t exp = (u >> 23) & 0xFF, man = u & 0x7FFFFF;
+    if (exp == 0) return (uint16_t)((u >> 16) & 0x8000);
+    if (exp == 0xFF) {
+        if (man == 0) return (uint16_t)(u >> 16);
+        return (uint16_t)((u >> 16) | 0x40);
+    }
+    uint32_t lsb = (u >> 16) & 1;
+    return (uint16_t)((u + 0x7FFF + lsb) >> 16);
+}
+
+void orc_f32_to_bf16_array(const float *x, uint16_t *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = orc_f32_to_bf16_cvtne(x[i]);
+}
+void orc_bf16_to_f32_array(const uint16_t *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = orc_bf16_to_f32(x[i]);
+}
+
+/* ------------------------------------------------------- x86 primitives */
+
+/* Denormals-are-zero on a bf16 operand, flush-to-zero on an f32 result:
+ * the two modes vdpbf16ps applies regardless of MXCSR. */
+static inline float daz_bf16(uint16_t h) {
+    if ((h & 0x7F80) == 0) return u2f((uint32_t)(h & 0x8000) << 16);
+    return orc_bf16_to_f32(h);
+}
+static inline float ftz(float x) {
+    uint32_t u = f2u(x);
+    if ((u & 0x7F800000u) == 0) return u2f(u & 0x80000000u);
+    return x;
+}
+
+/* One lane of vdpbf16ps: the odd pair is accumulated first, then the even
+ * pair, each as an FMA (the product of two bf16 is exact in f32). */
+static inline float dp_lane(float acc, uint16_t a0, uint16_t b0, uint16_t a1,
+                            uint16_t b1) {
+    acc = ftz(fmaf(daz_bf16(a1), daz_bf16(b1), acc));
+    acc = ftz(fmaf(daz_bf16(a0), daz_bf16(b0), acc));
+    return acc;
+}
+
+void orc_dpbf16_scalar(float *acc, const uint16_t *a, const uint16_t *b) {
+    for (int i = 0; i < 16; i++)
+        acc[i] = dp_lane(acc[i], a[2 * i], b[2 * i], a[2 * i + 1], b[2 * i + 1]);
+}
+
+/* vmaxps / vminps: the second operand wins on ties and on NaN. */
+static inline float x86_max(float a, float b) { return a > b ? a : b; }
+static inline float x86_min(float a, float b) { return a < b ? a : b; }
+
+/* exp_inline (src/jit/target/x86/emit_sdpa/x86/base.rs:189-212), one lane. */
+float orc_exp_poly(float x) {
+    x = x86_max(x, EXP_NEG87);
+    float t1 = x * EXP_LOG2E;
+    float t2 = nearbyintf(t1); /* vrndscaleps imm 0: nearest even */
+    t1 = t1 - t2;
+    float p = fmaf(EXP_C4, t1, EXP_C3);
+    p = fmaf(p, t1, EXP_C2);
+    p = fmaf(p, t1, EXP_C1);
+    p = fmaf(p, t1, EXP_C0);
+    int32_t r = (int32_t)t2; /* vcvtps2dq of an integral value */
+    uint32_t bits = ((uint32_t)r << 23) + EXP_ONE_BITS;
+    return p * u2f(bits);
+}
+
+/* hsum (base.rs:258-267): (l, l+8) -> (l, l+4) -> hadd -> hadd. */
+static inline float hsum16(const float *l) {
+    float d[8], e[4];
+    for (int i = 0; i < 8; i++) d[i] = l[i] + l[i + 8];
+    for (int i = 0; i < 4; i++) e[i] = d[i] + d[i + 4];
+    float a = e[1] + e[0], b = e[3] + e[2];
+    return b + a;
+}
+/* hmax (base.rs:271-282); max is exact, the tree only fixes tie signs. */
+static inline float hmax16(const float *l) {
+    float d[8], e[4];
+    for (int i = 0; i < 8; i++) d[i] = x86_max(l[i], l[i + 8]);
+    for (int i = 0; i < 4; i++) e[i] = x86_max(d[i], d[i + 4]);
+    float f0 = x86_max(e[0], e[2]), f1 = x86_max(e[1], e[3]);
+    return x86_max(f0, f1);
+}
+
+/* ----------------------------------------------------- SDPA, portable */
+
+/* One score: `chains` accumulation chains over head_dim/32 vdpbf16ps
+ * blocks, reduced (4 chains: (c0+c1)+(c2+c3), decode.rs:59-128; 1 chain:
+ * the qk_group kernel, prefill.rs:496-542 with qk_reduce :302-331, whose
+ * transposed tree is hsum's pairing), then hsum, then x scale. */
+static float qk_score(const uint16_t *q, const uint16_t *krow, size_t hd,
+                      float scale, int chains) {
+    size_t n32 = hd / 32;
+    int na = chains;
+    if ((size_t)na > n32) na = (int)n32;
+    if (na < 1) na = 1;
+    float acc[4][16];
+    memset(acc, 0, sizeof acc);
+    for (size_t c = 0; c < n32; c++) {
+        float *a = acc[c % (size_t)na];
+        for (int i = 0; i < 16; i++)
+            a[i] = dp_lane(a[i], krow[c * 32 + 2 * i], q[c * 32 + 2 * i],
+                           krow[c * 32 + 2 * i + 1], q[c * 32 + 2 * i + 1]);
+    }
+    float *a0 = acc[0];
+    if (na == 4) {
+        for (int i = 0; i < 16; i++) {
+            a0[i] = a0[i] + acc[1][i];
+            acc[2][i] = acc[2][i] + acc[3][i];
+            a0[i] = a0[i] + acc[2][i];
+        }
+    } else {
+        for (int c = 1; c < na; c++)
+            for (int i = 0; i < 16; i++) a0[i] = a0[i] + acc[c][i];
+    }
+    return hsum16(a0) * scale;
+}
+
+/* Softmax over nb blocks of 16 (decode.rs:212-293, no sink). */
+static void softmax_blocks(float *s, size_t nb) {
+    float maxv[16];
+    for (int i = 0; i < 16; i++) maxv[i] = -INFINITY;
+    for (size_t b = 0; b < nb; b++)
+        for (int i = 0; i < 16; i++) maxv[i] = x86_max(maxv[i], s[b * 16 + i]);
+    float m = hmax16(maxv);
+    float sumv[16] = {0};
+    for (size_t b = 0; b < nb; b++)
+        for (int i = 0; i < 16; i++) {
+            float w = orc_exp_poly(s[b * 16 + i] - m);
+            sumv[i] = sumv[i] + w;
+            s[b * 16 + i] = w;
+        }
+    float sum = hsum16(sumv);
+    for (size_t b = 0; b < nb; b++)
+        for (int i = 0; i < 16; i++) s[b * 16 + i] = s[b * 16 + i] / sum;
+}
+
+static int sdpa_head_scalar(const uint16_t *q, const uint16_t *k,
+                            const uint16_t *v, float *scores, uint16_t *out,
+                            size_t n, size_t hd, float scale, int chains) {
+    size_t nb = (n + 15) / 16;
+    for (size_t j = 0; j < n; j++) scores[j] = qk_score(q, k + j * hd, hd, scale, chains);
+    for (size_t j = n; j < nb * 16; j++) scores[j] = -INFINITY;
+    softmax_blocks(scores, nb);
+    float acc[512];
+    for (size_t d = 0; d < hd; d++) acc[d] = 0.0f;
+    for (size_t j = 0; j < n; j++) {
+        float p = scores[j];
+        const uint16_t *vr = v + j * hd;
+        for (size_t d = 0; d < hd; d++) acc[d] = fmaf(orc_bf16_to_f32(vr[d]), p, acc[d]);
+    }
+    for (size_t d = 0; d < hd; d++) out[d] = orc_f32_to_bf16_cvtne(acc[d]);
+    return 0;
+}
+
+/* -------------------------------------------- SDPA, AVX-512 transcription */
+
+#if ORC_X86
+#define AVX512_TARGET __attribute__((target("avx512f,avx512bw,avx512vl,avx512bf16,fma,sse3")))
+
+int orc_has_avx512bf16(void) {
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("avx512bf16") && __builtin_cpu_supports("avx512bw") &&
+           __builtin_cpu_supports("avx512vl");
+}
+
+AVX512_TARGET static inline __m512 bcast(float x) { return _mm512_set1_ps(x); }
+
+/* exp_inline, instruction by instruction. */
+AVX512_TARGET static inline __m512 exp16(__m512 io) {
+    io = _mm512_max_ps(io, bcast(EXP_NEG87));
+    __m512 t1 = _mm512_mul_ps(io, bcast(EXP_LOG2E));
+    __m512 t2 = _mm512_roundscale_ps(t1, 0);
+    t1 = _mm512_sub_ps(t1, t2);
+    __m512 t3 = bcast(EXP_C4);
+    t3 = _mm512_fmadd_ps(t3, t1, bcast(EXP_C3));
+    t3 = _mm512_fmadd_ps(t3, t1, bcast(EXP_C2));
+    t3 = _mm512_fmadd_ps(t3, t1, bcast(EXP_C1));
+    t3 = _mm512_fmadd_ps(t3, t1, bcast(EXP_C0));
+    __m512i e = _mm512_cvtps_epi32(t2);
+    e = _mm512_slli_epi32(e, 23);
+    e = _mm512_add_epi32(e, _mm512_set1_epi32((int)EXP_ONE_BITS));
+    return _mm512_mul_ps(t3, _mm512_castsi512_ps(e));
+}
+
+AVX512_TARGET static inline float hsum_hw(__m512 a) {
+    __m256 hi = _mm256_castpd_ps(_mm512_extractf64x4_pd(_mm512_castps_pd(a), 1));
+    __m256 s = _mm256_add_ps(_mm512_castps512_ps256(a), hi);
+    __m128 x = _mm_add_ps(_mm256_castps256_ps128(s), _mm256_extractf128_ps(s, 1));
+    x = _mm_hadd_ps(x, x);
+    x = _mm_hadd_ps(x, x);
+    return _mm_cvtss_f32(x);
+}
+
+AVX512_TARGET static inline float hmax_hw(__m512 a) {
+    __m256 hi = _mm256_castpd_ps(_mm512_extractf64x4_pd(_mm512_castps_pd(a), 1));
+    __m256 s = _mm256_max_ps(_mm512_castps512_ps256(a), hi);
+    __m128 x = _mm_max_ps(_mm256_castps256_ps128(s), _mm256_extractf128_ps(s, 1));
+    x = _mm_max_ps(x, _mm_shuffle_ps(x, x, 0x4E));
+    x = _mm_max_ps(x, _mm_shuffle_ps(x, x, 0xB1));
+    return _mm_cvtss_f32(x);
+}
+
+AVX512_TARGET int orc_dpbf16_hw(float *acc, const uint16_t *a, const uint16_t *b) {
+    if (!orc_has_avx512bf16()) return -1;
+    __m512 r = _mm512_loadu_ps(acc);
+    __m512bh va = (__m512bh)_mm512_loadu_si512(a);
+    __m512bh vb = (__m512bh)_mm512_loadu_si512(b);
+    r = _mm512_dpbf16_ps(r, va, vb);
+    _mm512_storeu_ps(acc, r);
+    return 0;
+}
+
+AVX512_TARGET int orc_exp_poly_hw16(const float *x, float *y) {
+    if (!orc_has_avx512bf16()) return -1;
+    _mm512_storeu_ps(y, exp16(_mm512_loadu_ps(x)));
+    return 0;
+}
+
+AVX512_TARGET static inline __m512 load_bf16_f32(const uint16_t *p) {
+    __m512i w = _mm512_cvtepu16_epi32(_mm256_loadu_si256((const __m256i *)p));
+    return _mm512_castsi512_ps(_mm512_slli_epi32(w, 16));
+}
+
+AVX512_TARGET static int sdpa_head_avx512(const uint16_t *q, const uint16_t *k,
+                                          const uint16_t *v, float *scores,
+                                          uint16_t *out, size_t n, size_t hd,
+                                          float scale, int chains) {
+    size_t n32 = hd / 32, nv = hd / 16, nb = (n + 15) / 16;
+    int na = chains;
+    if ((size_t)na > n32) na = (int)n32;
+    if (na < 1) na = 1;
+    /* QK: vdpbf16ps chains, chain tree, hsum, vmulss. */
+    for (size_t j = 0; j < n; j++) {
+        __m512 acc[4] = {_mm512_setzero_ps(), _mm512_setzero_ps(), _mm512_setzero_ps(),
+                         _mm512_setzero_ps()};
+        const uint16_t *kr = k + j * hd;
+        for (size_t c = 0; c < n32; c++) {
+            __m512bh kk = (__m512bh)_mm512_loadu_si512(kr + c * 32);
+            __m512bh qq = (__m512bh)_mm512_loadu_si512(q + c * 32);
+            acc[c % (size_t)na] = _mm512_dpbf16_ps(acc[c % (size_t)na], kk, qq);
+        }
+        if (na == 4) {
+            acc[0] = _mm512_add_ps(acc[0], acc[1]);
+            acc[2] = _mm512_add_ps(acc[2], acc[3]);
+            acc[0] = _mm512_add_ps(acc[0], acc[2]);
+        } else {
+            for (int c = 1; c < na; c++) acc[0] = _mm512_add_ps(acc[0], acc[c]);
+        }
+        __m128 s = _mm_mul_ss(_mm_set_ss(hsum_hw(acc[0])), _mm_set_ss(scale));
+        scores[j] = _mm_cvtss_f32(s);
+    }
+    for (size_t j = n; j < nb * 16; j++) scores[j] = -INFINITY;
+    /* softmax: max, exp + sum, divide. */
+    __m512 maxv = bcast(-INFINITY);
+    for (size_t b = 0; b < nb; b++) maxv = _mm512_max_ps(maxv, _mm512_loadu_ps(scores + b * 16));
+    __m512 m = bcast(hmax_hw(maxv));
+    __m512 sumv = _mm512_setzero_ps();
+    for (size_t b = 0; b < nb; b++) {
+        __m512 w = _mm512_sub_ps(_mm512_loadu_ps(scores + b * 16), m);
+        w = exp16(w);
+        sumv = _mm512_add_ps(sumv, w);
+        _mm512_storeu_ps(scores + b * 16, w);
+    }
+    __m512 sum = bcast(hsum_hw(sumv));
+    for (size_t b = 0; b < nb; b++)
+        _mm512_storeu_ps(scores + b * 16, _mm512_div_ps(_mm512_loadu_ps(scores + b * 16), sum));
+    /* SV: widen V, vfmadd231ps, vcvtneps2bf16. */
+    __m512 acc[32];
+    for (size_t c = 0; c < nv; c++) acc[c] = _mm512_setzero_ps();
+    for (size_t j = 0; j < n; j++) {
+        __m512 p = _mm512_set1_ps(scores[j]);
+        const uint16_t *vr = v + j * hd;
+        for (size_t c = 0; c < nv; c++) acc[c] = _mm512_fmadd_ps(load_bf16_f32(vr + c * 16), p, acc[c]);
+    }
+    for (size_t c = 0; c < nv; c++)
+        _mm256_storeu_si256((__m256i *)(out + c * 16), (__m256i)_mm512_cvtneps_pbh(acc[c]));
+    return 0;
+}
+
+AVX512_TARGET static void sigmoid_mul_avx512(const uint16_t *a, const uint16_t *b,
+                                             uint16_t *y, size_t n) {
+    for (size_t i = 0; i < n; i += 16) {
+        __m512 g = load_bf16_f32(a + i);
+        __m512 u = load_bf16_f32(b + i);
+        __m512 e = _mm512_sub_ps(_mm512_setzero_ps(), u);
+        e = _mm512_min_ps(e, bcast(EXP_MAX88));
+        e = exp16(e);
+        e = _mm512_add_ps(e, bcast(1.0f));
+        e = _mm512_div_ps(g, e);
+        _mm256_storeu_si256((__m256i *)(y + i), (__m256i)_mm512_cvtneps_pbh(e));
+    }
+}
+#else
+int orc_has_avx512bf16(void) { return 0; }
+int orc_dpbf16_hw(float *acc, const uint16_t *a, const uint16_t *b) {
+    (void)acc; (void)a; (void)b; return -1;
+}
+int orc_exp_poly_hw16(const float *x, float *y) { (void)x; (void)y; return -1; }
+#endif
+
+int orc_sdpa_head(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                  float *scores, uint16_t *out, size_t n, size_t head_dim,
+                  float scale, int impl, int qk_chains) {
+    if (n == 0 || head_dim == 0 || head_dim % 32 || head_dim > 512) return -2;
+    if (qk_chains != 1 && qk_chains != 4) return -2;
+    float *own = NULL;
+    if (!scores) {
+        own = (float *)malloc(((n + 15) / 16) * 16 * sizeof(float));
+        if (!own) return -3;
+        scores = own;
+    }
+    int rc;
+    if (impl == 1) {
+#if ORC_X86
+        rc = orc_has_avx512bf16()
+                 ? sdpa_head_avx512(q, k, v, scores, out, n, head_dim, scale, qk_chains)
+                 : -1;
+#else
+        rc = -1;
+#endif
+    } else {
+        rc = sdpa_head_scalar(q, k, v, scores, out, n, head_dim, scale, qk_chains);
+    }
+    free(own);
+    return rc;
+}
+
+/* The prefill block: the QK rectangle rows x N, the per-row -inf pad, the
+ * per-row softmax, the masked columns zeroed, the SV over the block
+ * (prefill.rs:733-912).  Each row sees past + i + 1 keys. */
+int orc_sdpa_prefill_block(const uint16_t *q, const uint16_t *k,
+                           const uint16_t *v, uint16_t *out, size_t past,
+                           size_t rows, size_t hd, size_t q_row_stride,
+                           size_t out_row_stride, float scale) {
+    if (rows == 0 || rows > 8 || hd == 0 || hd % 32 || hd > 512) return -2;
+    size_t N = past + rows, rowlen = (N + 15) / 16 * 16;
+    float *s = (float *)malloc(rows * rowlen * sizeof(float));
+    if (!s) return -3;
+    for (size_t i = 0; i < rows; i++)
+        for (size_t j = 0; j < N; j++)
+            s[i * rowlen + j] = qk_score(q + i * q_row_stride, k + j * hd, hd, scale, 1);
+    for (size_t i = 0; i < rows; i++) {
+        size_t ni = past + i + 1, end = (ni + 15) / 16 * 16;
+        for (size_t j = ni; j < end; j++) s[i * rowlen + j] = -INFINITY;
+        softmax_blocks(s + i * rowlen, end / 16);
+        for (size_t j = ni; j < N; j++) s[i * rowlen + j] = 0.0f;
+    }
+    float acc[8][512];
+    for (size_t i = 0; i < rows; i++)
+        for (size_t d = 0; d < hd; d++) acc[i][d] = 0.0f;
+    for (size_t j = 0; j < N; j++) {
+        const uint16_t *vr = v + j * hd;
+        for (size_t i = 0; i < rows; i++) {
+            float p = s[i * rowlen + j];
+            for (size_t d = 0; d < hd; d++) acc[i][d] = fmaf(orc_bf16_to_f32(vr[d]), p, acc[i][d]);
+        }
+    }
+    for (size_t i = 0; i < rows; i++)
+        for (size_t d = 0; d < hd; d++)
+            out[i * out_row_stride + d] = orc_f32_to_bf16_cvtne(acc[i][d]);
+    free(s);
+    return 0;
+}
+
+static void sigmoid_mul_scalar(const uint16_t *a, const uint16_t *b, uint16_t *y, size_t n) {
+    for (size_t i = 0; i < n; i++) {
+        float g = orc_bf16_to_f32(a[i]);
+        float u = orc_bf16_to_f32(b[i]);
+        float e = 0.0f - u;
+        e = x86_min(e, EXP_MAX88);
+        e = orc_exp_poly(e);
+        e = e + 1.0f;
+        e = g / e;
+        y[i] = orc_f32_to_bf16_cvtne(e);
+    }
+}
+
+int orc_sigmoid_mul(const uint16_t *a, const uint16_t *b, uint16_t *y, size_t n, int impl) {
+    if (impl == 1) {
+#if ORC_X86
+        if (!orc_has_avx512bf16() || n % 16) return -1;
+        sigmoid_mul_avx512(a, b, y, n);
+        return 0;
+#else
+        return -1;
+#endif
+    }
+    sigmoid_mul_scalar(a, b, y, n);
+    return 0;
+}
+
+int orc_attention(const uint16_t *q, const uint16_t *keys, const uint16_t *values,
+                  uint16_t *out, size_t rows, size_t past, size_t heads, size_t gqa,
+                  size_t hd, size_t q_row, size_t q_head, size_t out_row,
+                  ptrdiff_t gate_offset, size_t kv_stride, float scale, int impl,
+                  int use_block, int threads) {
+    if (rows == 0 || heads == 0 || gqa == 0 || heads % gqa || hd == 0 || hd % 32 || hd > 512)
+        return -2;
+    if (impl == 1 && !orc_has_avx512bf16()) return -1;
+    const size_t chunk = use_block ? 8 : 1;
+    const size_t chunks = (rows + chunk - 1) / chunk;
+    const long tasks = (long)(chunks * heads);
+    int err = 0;
+#ifdef _OPENMP
+    int nt = threads > 0 ? threads : omp_get_max_threads();
+#pragma omp parallel num_threads(nt) reduction(| : err)
+#else
+    (void)threads;
+#endif
+    {
+        float *scores = (float *)malloc((past + rows + 16) * 8 * sizeof(float));
+        if (!scores) err |= 1;
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 1)
+#endif
+        for (long t = 0; t < tasks; t++) {
+            if (!scores) continue;
+            /* task t -> chunk = t mod chunks, head = t / chunks
+             * (attention.rs:150-158, ungrouped order) */
+            size_t c = (size_t)t % chunks, h = (size_t)t / chunks;
+            size_t r0 = c * chunk, r1 = r0 + chunk < rows ? r0 + chunk : rows;
+            const uint16_t *kh = keys + (h / gqa) * kv_stride;
+            const uint16_t *vh = values + (h / gqa) * kv_stride;
+            if (use_block && r1 - r0 == chunk) {
+                err |= orc_sdpa_prefill_block(q + r0 * q_row + h * q_head, kh, vh,
+                                              out + r0 * out_row + h * hd, past + r0,
+                                              chunk, hd, q_row, out_row, scale) != 0;
+            } else {
+                for (size_t r = r0; r < r1; r++)
+                    err |= orc_sdpa_head(q + r * q_row + h * q_head, kh, vh, scores,
+                                         out + r * out_row + h * hd, past + r + 1, hd,
+                                         scale, impl, 1) != 0;
+            }
+        }
+        free(scores);
+    }
+    if (err) return -4;
+    if (gate_offset >= 0) {
+        /* The gate node: row by row, `heads*hd` elements (lowering.rs:645-666). */
+        for (size_t r = 0; r < rows; r++) {
+            const uint16_t *g = q + r * q_row + (size_t)gate_offset;
+            uint16_t *o = out + r * out_row;
+            if (orc_sigmoid_mul(o, g, o, heads * hd, impl) != 0) return -4;
+        }
+    }
+    return 0;
+}
+
+/* -------------------------------------------------------------- DeltaNet */
+
+/* l2norm (delta.rs:28-62): left-to-right sum of squares, separate multiply
+ * and add, then + eps, sqrt, 1/x, multiply. */
+void orc_l2norm(float *x, size_t dim, float eps) {
+    float sum = 0.0f;
+    for (size_t i = 0; i < dim; i++) {
+        float t = x[i] * x[i];
+        sum = sum + t;
+    }
+    sum = sum + eps;
+    float inv = 1.0f / sqrtf(sum);
+    for (size_t i = 0; i < dim; i++) x[i] = x[i] * inv;
+}
+
+/* The recurrence (emit_recurrence.rs:108-217; scalar delta_scalar.rs:9-82):
+ * pass 1 decays each state row and reads kv = S^T k, delta = (v - kv) beta,
+ * pass 2 writes S += k delta^T and reads out = S^T (q scale). */
+void orc_gdn_recurrence(float *s, float *out, const float *q, const float *k,
+                        const float *v, size_t hkd, size_t hvd, float beta,
+                        float decay, float scale, int fma) {
+    float kv[512], dl[512];
+    for (size_t j = 0; j < hvd; j++) kv[j] = 0.0f;
+    for (size_t kd = 0; kd < hkd; kd++) {
+        float kval = k[kd];
+        float *row = s + kd * hvd;
+        for (size_t j = 0; j < hvd; j++) {
+            float r = row[j] * decay;
+            row[j] = r;
+            if (fma) kv[j] = fmaf(r, kval, kv[j]);
+            else { float t = r * kval; kv[j] = kv[j] + t; }
+        }
+    }
+    for (size_t j = 0; j < hvd; j++) {
+        float t = v[j] - kv[j];
+        dl[j] = t * beta;
+    }
+    for (size_t j = 0; j < hvd; j++) out[j] = 0.0f;
+    for (size_t kd = 0; kd < hkd; kd++) {
+        float kval = k[kd];
+        float qval = q[kd] * scale;
+        float *row = s + kd * hvd;
+        for (size_t j = 0; j < hvd; j++) {
+            float r;
+            if (fma) {
+                r = fmaf(kval, dl[j], row[j]);
+                row[j] = r;
+                out[j] = fmaf(r, qval, out[j]);
+            } else {
+                float t = kval * dl[j];
+                r = row[j] + t;
+                row[j] = r;
+                float t2 = r * qval;
+                out[j] = out[j] + t2;
+            }
+        }
+    }
+}
+
+int orc_gdn_layer(float *qkv, float *state, float *out, const float *beta,
+                  const float *decay, size_t rows, size_t nk, size_t nv, size_t hkd,
+                  size_t hvd, int l2, float eps, int fma, int threads) {
+    if (nk == 0 || nv == 0 || nv % nk || hkd == 0 || hvd == 0 || hkd > 512 || hvd > 512)
+        return -2;
+    const size_t key = nk * hkd, value = nv * hvd, conv = 2 * key + value;
+    if (l2) {
+        /* Q then K of each key head, row by row (delta.rs:442-515). */
+        for (size_t t = 0; t < rows; t++)
+            for (size_t h = 0; h < nk; h++) {
+                orc_l2norm(qkv + t * conv + h * hkd, hkd, eps);
+                orc_l2norm(qkv + t * conv + key + h * hkd, hkd, eps);
+            }
+    }
+    /* 1/sqrt(hkd) in f32, as the traversal computes it (delta.rs:590). */
+    const float scale = 1.0f / sqrtf((float)hkd);
+    const size_t ratio = nv / nk;
+#ifdef _OPENMP
+    int nt = threads > 0 ? threads : omp_get_max_threads();
+#pragma omp parallel for num_threads(nt) schedule(dynamic, 1)
+#else
+    (void)threads;
+#endif
+    for (long hl = 0; hl < (long)nv; hl++) {
+        size_t h = (size_t)hl, kh = h / ratio;
+        float *s = state + h * hkd * hvd;
+        for (size_t t = 0; t < rows; t++) {
+            const float *row = qkv + t * conv;
+            orc_gdn_recurrence(s, out + t * value + h * hvd, row + kh * hkd,
+                               row + key + kh * hkd, row + 2 * key + h * hvd, hkd, hvd,
+                               beta[t * nv + h], decay[t * nv + h], scale, fma);
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------- inputs */
+
+static inline uint64_t splitmix64(uint64_t *s) {
+    uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+void orc_fill_normal_f64(double *x, size_t n, uint64_t seed) {
+    uint64_t st = seed;
+    const double two_pi = 6.283185307179586476925286766559;
+    for (size_t i = 0; i < n; i += 2) {
+        double u1 = ((double)(splitmix64(&st) >> 11) + 1.0) * 0x1.0p-53;
+        double u2 = (double)(splitmix64(&st) >> 11) * 0x1.0p-53;
+        double r = sqrt(-2.0 * log(u1));
+        x[i] = r * cos(two_pi * u2);
+        if (i + 1 < n) x[i + 1] = r * sin(two_pi * u2);
+    }
+}
+
+void orc_fill_normal_bf16(uint16_t *x, size_t n, uint64_t seed) {
+    const size_t blk = 4096;
+    double buf[4096];
+    uint64_t st = seed;
+    for (size_t i = 0; i < n; i += blk) {
+        size_t m = n - i < blk ? n - i : blk;
+        /* one independent stream per block keeps generation restartable */
+        orc_fill_normal_f64(buf, m, splitmix64(&st));
+        for (size_t j = 0; j < m; j++) x[i + j] = orc_f32_to_bf16_cvtne((float)buf[j]);
+    }
+}

@@ -1,0 +1,135 @@
+/*
+ * herbert_oracle.h -- CPU restatement of the reference's attention-path
+ * kernels (xigh/herbert-jit-bf16, x86 AVX-512 BF16 emitters).
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the product library links this
+ * file; only the tests, the smoke check and the CPU-baseline leg of
+ * bench.py load it, as the checker.
+ *
+ * Parity status: the reference is Rust and cannot be built here (no
+ * cargo/rustc, crates not vendored), and it ships no tests or golden
+ * vectors.  The restatement is therefore pinned in two ways instead:
+ *   (1) every primitive the reference emits (vdpbf16ps, vcvtneps2bf16,
+ *       the inline exp polynomial, the hsum/hmax trees) is emulated in
+ *       portable C and checked bit for bit against the same x86
+ *       instruction sequence transcribed with intrinsics, run on a CPU
+ *       with AVX512-BF16;
+ *   (2) the reference's own stated invariants (prefill block == repeated
+ *       decode, bit for bit; qk_group changes at most one bf16 step;
+ *       non-FMA recurrence == scalar order) are tests.
+ * There is no reference output to compare against: parity is "unpinned"
+ * by reference golden vectors.
+ *
+ * Layouts follow the reference:
+ *   K/V cache   : [kv_head][capacity][head_dim] bf16, head h at h*kv_stride
+ *                 (src/jit/model.rs:545-559, src/jit/execution/abi.rs:57-104)
+ *   q row       : [Q_0 .. Q_{H-1} | g_0 .. g_{H-1}], row stride q_row
+ *                 (src/jit/schedule.rs:109-133,172-186)
+ *   DeltaNet qkv: [rows][2*nk*hkd + nv*hvd] f32, state [nv][hkd][hvd] f32
+ *                 (src/jit/target/x86/execution/delta.rs:519-607)
+ */
+#ifndef HERBERT_ORACLE_H
+#define HERBERT_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* 1 when the AVX512-BF16 transcription can run on this CPU. */
+int orc_has_avx512bf16(void);
+
+/* Conversions (src/core/tensor.rs:8-24 and vcvtneps2bf16). */
+float orc_bf16_to_f32(uint16_t h);
+uint16_t orc_f32_to_bf16_cvtne(float x);
+void orc_f32_to_bf16_array(const float *x, uint16_t *y, size_t n);
+void orc_bf16_to_f32_array(const uint16_t *x, float *y, size_t n);
+
+/* Primitive checks: one vdpbf16ps over 16 lanes (acc[16] updated in place),
+ * scalar emulation and hardware instruction. */
+void orc_dpbf16_scalar(float *acc, const uint16_t *a, const uint16_t *b);
+int orc_dpbf16_hw(float *acc, const uint16_t *a, const uint16_t *b);
+/* The emitted exp polynomial (src/jit/target/x86/emit_sdpa/x86/base.rs:189-212). */
+float orc_exp_poly(float x);
+int orc_exp_poly_hw16(const float *x, float *y);
+
+/*
+ * Decode SDPA for one query head (SdpaHeadFn, src/jit/emit_sdpa.rs:131-140;
+ * Chained form, qk_group 8 = one accumulation chain per position).
+ * q[head_dim], k/v: [n][head_dim] rows of this KV head, out[head_dim].
+ * scores: caller scratch of align16(n) floats (may be NULL: internal).
+ * impl: 0 = portable emulation, 1 = AVX512-BF16 transcription (returns -1
+ * if unavailable).  qk_chains: 1 (qk_group 8/16, the default) or 4 (the
+ * historical row-by-row kernel, qk_group 0).
+ */
+int orc_sdpa_head(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                  float *scores, uint16_t *out, size_t n, size_t head_dim,
+                  float scale, int impl, int qk_chains);
+
+/*
+ * Prefill block of `rows` consecutive queries of one head against the same
+ * K/V (SdpaPrefillFn, src/jit/emit_sdpa.rs:173-304; assemble_prefill,
+ * src/jit/target/x86/emit_sdpa/x86/prefill.rs:733-912): the QK rectangle
+ * rows x (past+rows), -inf pad per row, softmax per row, masked columns set
+ * to +0, SV over the block.  q rows at q_row_stride, out rows at
+ * out_row_stride (elements).  Portable emulation only.
+ */
+int orc_sdpa_prefill_block(const uint16_t *q, const uint16_t *k,
+                           const uint16_t *v, uint16_t *out, size_t past,
+                           size_t rows, size_t head_dim, size_t q_row_stride,
+                           size_t out_row_stride, float scale);
+
+/* Output gate y = bf16(a / (1 + exp(-b))) over n elements
+ * (ElemOp::SigmoidMul, src/jit/target/x86/emit_elem.rs:333-420). */
+int orc_sigmoid_mul(const uint16_t *a, const uint16_t *b, uint16_t *y,
+                    size_t n, int impl);
+
+/*
+ * The attention node (src/jit/target/x86/execution/attention.rs:56-224)
+ * followed by the output-gate node (src/jit/schedule/lowering.rs:642-666):
+ * for every row r < rows and query head h < heads, n = past + r + 1 keys of
+ * KV head h / gqa.  q + r*q_row + h*q_head; out + r*out_row + h*head_dim;
+ * gate (if gate_offset >= 0) at q + r*q_row + gate_offset + h*head_dim.
+ * threads: OpenMP threads (0 = runtime default).  use_block: 1 = 8-row
+ * prefill blocks for full chunks (the reference's x86 path), 0 = decode
+ * kernel row by row (same bits).
+ */
+int orc_attention(const uint16_t *q, const uint16_t *keys,
+                  const uint16_t *values, uint16_t *out, size_t rows,
+                  size_t past, size_t heads, size_t gqa, size_t head_dim,
+                  size_t q_row, size_t q_head, size_t out_row,
+                  ptrdiff_t gate_offset, size_t kv_stride, float scale,
+                  int impl, int use_block, int threads);
+
+/* DeltaNet L2 norm of one head in place (src/jit/target/x86/execution/delta.rs:28-62). */
+void orc_l2norm(float *x, size_t dim, float eps);
+
+/* One recurrence step for one V head (RecurrenceFn,
+ * src/jit/target/x86/emit_recurrence.rs:108-217).  fma = 0 is the default
+ * (the bits of the scalar order), 1 the Knobs::deltanet_fma form. */
+void orc_gdn_recurrence(float *s, float *out, const float *q, const float *k,
+                        const float *v, size_t hkd, size_t hvd, float beta,
+                        float decay, float scale, int fma);
+
+/*
+ * The delta-l2-gates L2 part and the delta-causal-recurrence node over
+ * `rows` positions (src/jit/target/x86/execution/delta.rs:442-607):
+ * qkv [rows][2*nk*hkd + nv*hvd] f32 (L2-normalised in place when l2 != 0),
+ * beta/decay [rows][nv], state [nv][hkd][hvd] (updated), out [rows][nv*hvd].
+ */
+int orc_gdn_layer(float *qkv, float *state, float *out, const float *beta,
+                  const float *decay, size_t rows, size_t nk, size_t nv,
+                  size_t hkd, size_t hvd, int l2, float eps, int fma,
+                  int threads);
+
+/* Deterministic inputs: splitmix64 stream, Box-Muller N(0,1) in double,
+ * rounded to bf16 (RNE) -- the generator the fixtures use. */
+void orc_fill_normal_bf16(uint16_t *x, size_t n, uint64_t seed);
+void orc_fill_normal_f64(double *x, size_t n, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

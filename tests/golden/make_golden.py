@@ -1,0 +1,58 @@
+"""Writes the golden fixtures of this directory from the CPU oracle.
+
+The reference (xigh/herbert-jit-bf16) has no tests, no golden vectors and
+cannot be built in this image, so these fixtures are the oracle's own
+outputs on small seeded inputs, committed so that (a) any change to the
+oracle shows up as a fixture mismatch and (b) the GPU parity tests have
+inputs/outputs that do not depend on the host that runs them.
+
+Run from the repository root:  python tests/golden/make_golden.py
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "herbert-jit-bf16_b200"),
+                os.path.join(ROOT, "tests")]
+
+from herbert_b200.inputs import AttentionInputs, DeltaInputs  # noqa: E402
+from harness import oracle_attention, oracle_gdn  # noqa: E402
+
+ATTN_CASES = {
+    # name: (rows, past, heads, kv_heads, head_dim, gated)
+    "attn_decode_n38": (1, 37, 16, 4, 256, True),
+    "attn_decode_n1": (1, 0, 16, 4, 256, True),
+    "attn_rows11_past5": (11, 5, 16, 4, 256, True),
+    "attn_hd128_g2_nogate": (3, 20, 4, 2, 128, False),
+}
+GDN_CASES = {
+    # name: (rows, nk, nv, hkd, hvd, state_scale)
+    "gdn_rows5_zero_state": (5, 2, 4, 128, 128, 0.0),
+    "gdn_rows3_warm_state": (3, 2, 4, 128, 128, 0.1),
+}
+
+
+def main():
+    for name, (rows, past, heads, kvh, hd, gated) in ATTN_CASES.items():
+        inp = AttentionInputs(rows, past, heads=heads, kv_heads=kvh, head_dim=hd, gated=gated,
+                              seed=0x60D0 + len(name))
+        out = oracle_attention(inp)
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), q=inp.q, keys=inp.keys,
+                            values=inp.values, out=out,
+                            meta=np.array([rows, past, heads, kvh, hd, int(gated)], np.int64))
+    for name, (rows, nk, nv, hkd, hvd, ss) in GDN_CASES.items():
+        state = np.random.default_rng(7).standard_normal((nv, hkd, hvd)).astype(np.float32) * ss
+        inp = DeltaInputs(rows, nk=nk, nv=nv, hkd=hkd, hvd=hvd, seed=0x60D1 + len(name),
+                          state=state)
+        out, st = oracle_gdn(inp)
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), qkv=inp.qkv, beta=inp.beta,
+                            decay=inp.decay, state0=inp.state, out=out, state=st,
+                            meta=np.array([rows, nk, nv, hkd, hvd], np.int64))
+    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,127 @@
+"""The C ABI on CPU: the library loads, exports every function the header
+declares, its record layouts match the ctypes mirror, and the host-side
+refusals return the reference's named statuses (no kernel launches)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import herbert_b200 as hb
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    text = open(hb.HEADER_PATH).read()
+    return sorted(set(re.findall(r"HB_API\s+[\w\s\*]+?\b(hb_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function():
+    names = declared_functions()
+    assert len(names) >= 15
+    L = hb.lib()
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(hb._SIGNATURES), "binding and header disagree"
+    nm = subprocess.run(["nm", "-D", "--defined-only", hb.LIB_PATH], capture_output=True,
+                        text=True, check=True).stdout
+    exported = set(re.findall(r"\sT\s(hb_\w+)", nm))
+    assert exported == set(names)
+
+
+def test_record_layouts_match_the_header(tmp_path):
+    src = tmp_path / "layout.c"
+    recs = {"hb_attn_spec": hb.AttentionSpec, "hb_attn_call": hb.AttentionCall,
+            "hb_decode_seq": hb.DecodeSeq, "hb_kv_spec": hb.KvSpec, "hb_kv_call": hb.KvCall,
+            "hb_gdn_shape": hb.DeltaShape, "hb_gdn_call": hb.RecurrenceCall}
+    body = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{hb.HEADER_PATH}"',
+            "int main(void){"]
+    for c, py in recs.items():
+        body.append(f'printf("{c} %zu\\n", sizeof({c}));')
+        for f, _ in py._fields_:
+            body.append(f'printf("{c}.{f} %zu\\n", offsetof({c}, {f}));')
+    body.append("return 0;}")
+    src.write_text("\n".join(body))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for c, py in recs.items():
+        assert int(out[c]) == ctypes.sizeof(py), c
+        for f, _ in py._fields_:
+            assert int(out[f"{c}.{f}"]) == getattr(py, f).offset, f"{c}.{f}"
+
+
+def _call(spec, **kw):
+    base = dict(q=16, keys=16, values=16, output=16, rows=1, past=10, kv_stride=11 * 256,
+                capacity=0, scale=0.0625, sink=0.0)
+    base.update(kw)
+    return hb.AttentionCall(**base)
+
+
+@pytest.mark.parametrize("mutate,status", [
+    (dict(sink=1), hb.HB_DECLINE_SINK),
+    (dict(heads=0), hb.HB_DECLINE_EMPTY),
+    (dict(gqa=3), hb.HB_DECLINE_GEOMETRY),
+    (dict(q_head=128), hb.HB_DECLINE_GEOMETRY),
+    (dict(out_row=1024), hb.HB_DECLINE_GEOMETRY),
+    (dict(head_dim=96, q_head=96, q_row=2 * 16 * 96, out_row=16 * 96, gate_offset=16 * 96),
+     hb.HB_DECLINE_HEAD_DIM),
+    (dict(gate_offset=8000), hb.HB_DECLINE_GEOMETRY),
+])
+def test_spec_refusals(mutate, status):
+    spec = hb.attention_spec()
+    for k, v in mutate.items():
+        setattr(spec, k, v)
+    rc = hb.lib().hb_attn_decode(ctypes.byref(spec), ctypes.byref(_call(spec)), None, 0, None)
+    assert rc == status, hb.last_error()
+    assert hb.last_error()
+
+
+@pytest.mark.parametrize("mutate,status", [
+    (dict(rows=0), hb.HB_DECLINE_EMPTY),
+    (dict(q=0), hb.HB_ERR_ARG),
+    (dict(keys=24), hb.HB_ERR_ARG),
+    (dict(past=-1), hb.HB_ERR_ARG),
+    (dict(kv_stride=10 * 256), hb.HB_ERR_ARG),
+    (dict(capacity=5), hb.HB_ERR_ARG),
+])
+def test_call_refusals(mutate, status):
+    spec = hb.attention_spec()
+    rc = hb.lib().hb_attn_decode(ctypes.byref(spec), ctypes.byref(_call(spec, **mutate)), None, 0,
+                                 None)
+    assert rc == status, hb.last_error()
+
+
+def test_python_binding_raises_decline():
+    spec = hb.attention_spec()
+    spec.sink = 1
+    with pytest.raises(hb.Decline):
+        hb.check(hb.lib().hb_attn_decode(ctypes.byref(spec), ctypes.byref(_call(spec)), None, 0,
+                                         None))
+
+
+def test_kv_and_delta_refusals():
+    L = hb.lib()
+    ks = hb.KvSpec(heads=4, head_dim=256, stride=100, capacity=8, max_batch=4)
+    kc = hb.KvCall(keys=16, values=16, input_keys=16, input_values=16, rows=1, past=0)
+    assert L.hb_kv_append(ctypes.byref(ks), ctypes.byref(kc), None) == hb.HB_DECLINE_GEOMETRY
+    ks.stride = 8 * 256
+    kc.rows = 5
+    assert L.hb_kv_append(ctypes.byref(ks), ctypes.byref(kc), None) == hb.HB_ERR_ARG
+    sh = hb.DeltaShape(nk=16, nv=30, hkd=128, hvd=128)
+    rc = hb.RecurrenceCall(state=16, output=16, qkv=16, beta=16, decay=16, rows=1, l2=1, eps=1e-6)
+    assert L.hb_gdn_decode(ctypes.byref(sh), ctypes.byref(rc), None) == hb.HB_DECLINE_GEOMETRY
+    sh.nv, sh.hkd = 32, 96
+    assert L.hb_gdn_decode(ctypes.byref(sh), ctypes.byref(rc), None) == hb.HB_DECLINE_HEAD_DIM
+    sh.hkd = 128
+    rc.rows = 0
+    assert L.hb_gdn_decode(ctypes.byref(sh), ctypes.byref(rc), None) == hb.HB_DECLINE_EMPTY
+
+
+def test_status_names():
+    assert hb.status_name(0) == "HB_OK"
+    assert hb.status_name(hb.HB_ERR_TIMEOUT) == "HB_ERR_TIMEOUT"
+    assert hb.version() >= (0, 1)

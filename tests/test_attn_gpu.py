@@ -1,0 +1,121 @@
+"""GPU parity of the SDPA kernels against the CPU oracle, through the C ABI.
+
+Tolerance: max abs error <= 2 bf16 ulp of the output scale and relative
+Frobenius error <= 5e-3 (tests/harness.py).  The gate epilogue reproduces the
+reference's exp polynomial and rounding, so with the gate the outputs differ
+from the oracle only through the SDPA sum order.
+"""
+import numpy as np
+import pytest
+
+from herbert_b200.inputs import AttentionInputs, normal_bf16
+from harness import (ATTN_FIXTURES, assert_sdpa_close, gpu_attention, load_attn_fixture,
+                     oracle_attention, to_dev_bf16, bits_of)
+
+pytestmark = pytest.mark.gpu
+
+DECODE_CASES = [
+    # rows, past, heads, kv_heads, head_dim, gated
+    (1, 2047, 16, 4, 256, True),    # the single decode step of the Qwen3.5 layer, n = 2048
+    (1, 0, 16, 4, 256, True),       # n = 1
+    (1, 15, 16, 4, 256, True),
+    (1, 16, 16, 4, 256, True),
+    (1, 100, 16, 4, 256, False),
+    (1, 4999, 16, 4, 256, True),    # several splits, ragged last tile
+    (3, 50, 16, 4, 256, True),      # rows > 1 in the decode regime
+    (1, 700, 8, 8, 128, False),     # gqa 1, head_dim 128
+    (2, 300, 16, 2, 128, True),     # gqa 8
+    (1, 333, 8, 4, 256, True),      # gqa 2
+]
+
+
+@pytest.mark.parametrize("case", DECODE_CASES, ids=lambda c: "r{}p{}h{}k{}d{}{}".format(
+    c[0], c[1], c[2], c[3], c[4], "g" if c[5] else ""))
+def test_decode_matches_oracle(cuda_device, case):
+    rows, past, heads, kvh, hd, gated = case
+    inp = AttentionInputs(rows, past, heads=heads, kv_heads=kvh, head_dim=hd, gated=gated,
+                          capacity=past + rows + 7)
+    got, _ = gpu_attention(inp, "decode")
+    assert_sdpa_close(got, oracle_attention(inp), f"decode {case}")
+
+
+def test_decode_workspace_reuse_is_stable(cuda_device):
+    """The split counters reset themselves: the same workspace serves calls
+    back to back with identical results."""
+    inp = AttentionInputs(1, 3000)
+    a, ws = gpu_attention(inp, "decode")
+    b, _ = gpu_attention(inp, "decode", workspace=ws)
+    c, _ = gpu_attention(inp, "decode", workspace=ws)
+    assert np.array_equal(a, b) and np.array_equal(b, c)
+    assert_sdpa_close(a, oracle_attention(inp), "reuse")
+
+
+@pytest.mark.parametrize("rows,past", [(64, 0), (37, 11), (200, 300)])
+def test_prefill_matches_oracle(cuda_device, rows, past):
+    inp = AttentionInputs(rows, past, capacity=past + rows)
+    got, _ = gpu_attention(inp, "prefill")
+    assert_sdpa_close(got, oracle_attention(inp), f"prefill rows={rows} past={past}")
+
+
+@pytest.mark.parametrize("name", ATTN_FIXTURES)
+def test_golden_fixtures(cuda_device, name):
+    inp, ref = load_attn_fixture(name)
+    for regime in ("decode", "prefill"):
+        got, _ = gpu_attention(inp, regime)
+        assert_sdpa_close(got, ref, f"{name} {regime}")
+
+
+def test_batched_decode_ragged(cuda_device):
+    import torch
+    import herbert_b200 as hb
+    lens = [1, 2, 31, 32, 33, 1000, 4097]
+    spec = hb.attention_spec()
+    seqs, keep, refs = [], [], []
+    for i, n in enumerate(lens):
+        inp = AttentionInputs(1, n - 1, capacity=n + 3, seed=1000 + 10 * i)
+        q, k, v = to_dev_bf16(inp.q), to_dev_bf16(inp.keys), to_dev_bf16(inp.values)
+        out = torch.zeros((1, inp.out_row), dtype=torch.int16, device="cuda")
+        keep.append((q, k, v, out))
+        seqs.append(hb.DecodeSeq(q=q.data_ptr(), keys=k.data_ptr(), values=v.data_ptr(),
+                                 output=out.data_ptr(), past=n - 1, kv_stride=inp.kv_stride))
+        refs.append(oracle_attention(inp))
+    table = hb.seq_table(seqs)
+    ws = hb.decode_batch(spec, table, len(lens), max(lens) - 1, sum(lens) - len(lens))
+    torch.cuda.synchronize()
+    ws.status()
+    for (q, k, v, out), ref, n in zip(keep, refs, lens):
+        assert_sdpa_close(bits_of(out), ref, f"batch n={n}")
+
+
+def test_workspace_too_small_is_refused(cuda_device):
+    import ctypes
+    import torch
+    import herbert_b200 as hb
+    inp = AttentionInputs(1, 2047)
+    small = hb.Workspace(256)
+    q, k, v = to_dev_bf16(inp.q), to_dev_bf16(inp.keys), to_dev_bf16(inp.values)
+    out = torch.zeros((1, inp.out_row), dtype=torch.int16, device="cuda")
+    spec = hb.attention_spec()
+    call = hb.AttentionCall(q=q.data_ptr(), keys=k.data_ptr(), values=v.data_ptr(),
+                            output=out.data_ptr(), rows=1, past=2047, kv_stride=inp.kv_stride,
+                            capacity=0, scale=inp.scale, sink=0.0)
+    rc = hb.lib().hb_attn_decode(ctypes.byref(spec), ctypes.byref(call),
+                                 ctypes.c_void_p(small.ptr), small.nbytes, None)
+    assert rc == hb.HB_ERR_WORKSPACE, hb.last_error()
+
+
+def test_kv_append_copies_into_the_reference_layout(cuda_device):
+    import torch
+    import herbert_b200 as hb
+    heads, hd, cap, rows, past = 4, 256, 64, 9, 17
+    keys = torch.zeros((heads, cap, hd), dtype=torch.int16, device="cuda")
+    values = torch.zeros_like(keys)
+    ik = normal_bf16((rows, heads, hd), 5)
+    iv = normal_bf16((rows, heads, hd), 6)
+    spec = hb.KvSpec(heads=heads, head_dim=hd, stride=cap * hd, capacity=cap, max_batch=16)
+    hb.kv_append(spec, keys, values, to_dev_bf16(ik), to_dev_bf16(iv), rows=rows, past=past)
+    torch.cuda.synchronize()
+    K, V = bits_of(keys), bits_of(values)
+    assert np.array_equal(K[:, past:past + rows], ik.transpose(1, 0, 2))
+    assert np.array_equal(V[:, past:past + rows], iv.transpose(1, 0, 2))
+    assert not K[:, :past].any() and not K[:, past + rows:].any()
