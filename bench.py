@@ -10,9 +10,10 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
 A step is one pass of the path over one batch: one prefill / one decode step /
 one GDN prefill + 256 steps / one decode step of the whole batch.
 
-`value` is device-timed with CUDA events on the launching stream, inputs
-resident in HBM, L2 flushed (256 MB write) before every timed step; under
-torchrun the timed total is the max over ranks.  `e2e` is the same metric
+`value` is device-timed with CUDA events on the launching stream around one
+CUDA-graph replay of K steps, inputs resident in HBM and rotated over copies
+whose total exceeds twice the 126 MB L2 (so every step reads cold inputs);
+under torchrun the timed total is the max over ranks.  `e2e` is the same metric
 through the C ABI with inputs copied from pinned host memory and the result
 copied back inside the timed region.  `--impl reference` times the CPU
 restatement of the reference's x86 kernels (the oracle) on the host cores.
@@ -36,7 +37,7 @@ NK, NV, HKD, HVD = 16, 32, 128, 128
 PREFILL_S = 4096
 DECODE_N = 2048
 GDN_T, GDN_STEPS = 4096, 256
-L2_FLUSH_BYTES = 256 << 20
+L2_BYTES = 126 << 20
 
 # dram bytes (read + write) of one launch of the dominant kernel, from the
 # committed ncu summaries under profiles/ (None until captured).
@@ -138,15 +139,18 @@ def smi_index(dev):
 # --------------------------------------------------------------- workloads
 
 class Workload:
-    """One configuration on one GPU: device inputs, the step, the e2e step."""
+    """One configuration on one GPU.
+
+    `sets` holds R copies of the step's inputs (R chosen so that the copies
+    exceed twice the L2); step(i) runs the path on copy i % R with inputs
+    resident in HBM; e2e_step(i) copies the step's inputs from pinned host
+    memory, runs the path and copies the result back."""
 
     launches_per_step = 1
 
-    def step(self):  # device-resident step
-        raise NotImplementedError
-
-    def e2e_step(self):  # host buffers -> device -> step -> result to host
-        raise NotImplementedError
+    @staticmethod
+    def rotation(bytes_per_set):
+        return max(1, -(-2 * L2_BYTES // max(1, bytes_per_set)))
 
 
 def _randn_bf16(shape, gen, device):
@@ -155,36 +159,60 @@ def _randn_bf16(shape, gen, device):
         torch.bfloat16)
 
 
-class PrefillWorkload(Workload):
-    def __init__(self, device, S=PREFILL_S, seed=0x5EED0002):
+def _nbytes(*ts):
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
+class _AttnWorkload(Workload):
+    """Shared by the prefill and single-sequence decode configurations."""
+
+    def __init__(self, device, rows, past, seed):
         import torch
         import herbert_b200 as hb
-        self.hb, self.S = hb, S
+        self.hb, self.rows, self.past = hb, rows, past
+        n = past + rows
         gen = torch.Generator(device=device).manual_seed(seed)
         qd = HQ * HD
-        self.q = _randn_bf16((S, 2 * qd), gen, device)
-        self.k = _randn_bf16((HKV, S, HD), gen, device)
-        self.v = _randn_bf16((HKV, S, HD), gen, device)
-        self.out = torch.empty((S, qd), dtype=torch.bfloat16, device=device)
+        per_set = (rows * 2 * qd + 2 * HKV * n * HD + rows * qd) * 2
+        self.R = self.rotation(per_set)
+        self.sets = []
+        for _ in range(self.R):
+            self.sets.append((_randn_bf16((rows, 2 * qd), gen, device),
+                              _randn_bf16((HKV, n, HD), gen, device),
+                              _randn_bf16((HKV, n, HD), gen, device),
+                              torch.empty((rows, qd), dtype=torch.bfloat16, device=device)))
         self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
         self.ws = None
+        q, k, v, out = self.sets[0]
+        self.h_in = [t.cpu().pin_memory() for t in (q, k, v)]
+        self.h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
+        self.set_bytes = per_set
+
+    def step(self, i=0):
+        q, k, v, out = self.sets[i % self.R]
+        n = self.past + self.rows
+        self.ws = self.hb.attention(self.spec, q, k, v, out, rows=self.rows, past=self.past,
+                                    kv_stride=n * HD, capacity=n, regime=self.regime,
+                                    workspace=self.ws)
+
+    def e2e_step(self, i=0):
+        q, k, v, out = self.sets[0]
+        for d, h in zip((q, k, v), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step(0)
+        self.h_out.copy_(out, non_blocking=True)
+
+
+class PrefillWorkload(_AttnWorkload):
+    regime = "prefill"
+
+    def __init__(self, device, S=PREFILL_S, seed=0x5EED0002):
+        super().__init__(device, S, 0, seed)
+        self.S = S
         self.work = prefill_flops(S)
         self.units = "TFLOP/s"
-        self.h_in = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
-        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
-        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
-        self.d2h = self.h_out.numel() * self.h_out.element_size()
-
-    def step(self):
-        self.ws = self.hb.attention(self.spec, self.q, self.k, self.v, self.out, rows=self.S,
-                                    past=0, kv_stride=self.S * HD, capacity=self.S,
-                                    regime="prefill", workspace=self.ws)
-
-    def e2e_step(self):
-        for d, h in zip((self.q, self.k, self.v), self.h_in):
-            d.copy_(h, non_blocking=True)
-        self.step()
-        self.h_out.copy_(self.out, non_blocking=True)
 
     def describe(self):
         return {"workload": "causal prefill SDPA (BASELINE configs[1])", "seq_len": self.S,
@@ -192,36 +220,14 @@ class PrefillWorkload(Workload):
                 "past": 0}
 
 
-class DecodeWorkload(Workload):
+class DecodeWorkload(_AttnWorkload):
+    regime = "decode"
+
     def __init__(self, device, n=DECODE_N, seed=0x5EED0001):
-        import torch
-        import herbert_b200 as hb
-        self.hb, self.n = hb, n
-        gen = torch.Generator(device=device).manual_seed(seed)
-        qd = HQ * HD
-        self.q = _randn_bf16((1, 2 * qd), gen, device)
-        self.k = _randn_bf16((HKV, n, HD), gen, device)
-        self.v = _randn_bf16((HKV, n, HD), gen, device)
-        self.out = torch.empty((1, qd), dtype=torch.bfloat16, device=device)
-        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
-        self.ws = None
-        self.work = 2 * HKV * n * HD * 2 + 3 * qd * 2  # K+V + q + gate + out bytes
+        super().__init__(device, 1, n - 1, seed)
+        self.n = n
+        self.work = 2 * HKV * n * HD * 2 + 3 * HQ * HD * 2  # K+V + q + gate + out bytes
         self.units = "GB/s"
-        self.h_in = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
-        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
-        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
-        self.d2h = self.h_out.numel() * self.h_out.element_size()
-
-    def step(self):
-        self.ws = self.hb.attention(self.spec, self.q, self.k, self.v, self.out, rows=1,
-                                    past=self.n - 1, kv_stride=self.n * HD, capacity=self.n,
-                                    regime="decode", workspace=self.ws)
-
-    def e2e_step(self):
-        for d, h in zip((self.q, self.k, self.v), self.h_in):
-            d.copy_(h, non_blocking=True)
-        self.step()
-        self.h_out.copy_(self.out, non_blocking=True)
 
     def describe(self):
         return {"workload": "single decode step gated SDPA (BASELINE configs[0])",
@@ -237,38 +243,45 @@ class GdnWorkload(Workload):
         gen = torch.Generator(device=device).manual_seed(seed)
         conv = 2 * NK * HKD + NV * HVD
         rows = T + steps
-        self.qkv = _randn_bf16((rows, conv), gen, device).float()
-        b = torch.randn((rows, NV), generator=gen, device=device)
-        g = torch.randn((rows, NV), generator=gen, device=device)
-        self.beta = torch.sigmoid(b)
-        self.decay = torch.exp(-torch.nn.functional.softplus(g))
+        per_set = rows * (conv + 2 * NV + NV * HVD) * 4
+        self.R = self.rotation(per_set)
+        self.sets = []
+        for _ in range(self.R):
+            qkv = _randn_bf16((rows, conv), gen, device).float()
+            b = torch.randn((rows, NV), generator=gen, device=device)
+            g = torch.randn((rows, NV), generator=gen, device=device)
+            self.sets.append((qkv, torch.sigmoid(b),
+                              torch.exp(-torch.nn.functional.softplus(g)),
+                              torch.empty((rows, NV * HVD), dtype=torch.float32, device=device)))
         self.state = torch.zeros((NV, HKD, HVD), dtype=torch.float32, device=device)
-        self.out = torch.empty((rows, NV * HVD), dtype=torch.float32, device=device)
         self.shape = hb.DeltaShape(nk=NK, nv=NV, hkd=HKD, hvd=HVD)
         self.ws = None
         self.work = T + steps
         self.units = "tok/s"
         self.launches_per_step = 1 + steps
-        self.h_in = [t.cpu().pin_memory() for t in (self.qkv, self.beta, self.decay)]
-        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
-        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
-        self.d2h = self.h_out.numel() * self.h_out.element_size()
+        qkv, beta, decay, out = self.sets[0]
+        self.h_in = [t.cpu().pin_memory() for t in (qkv, beta, decay)]
+        self.h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
+        self.set_bytes = per_set
 
-    def step(self):
+    def step(self, i=0):
         hb = self.hb
+        qkv, beta, decay, out = self.sets[i % self.R]
         self.state.zero_()
-        self.ws = hb.delta_recurrence(self.shape, self.state, self.out, self.qkv, self.beta,
-                                      self.decay, rows=self.T, regime="prefill",
-                                      workspace=self.ws)
+        self.ws = hb.delta_recurrence(self.shape, self.state, out, qkv, beta, decay,
+                                      rows=self.T, regime="prefill", workspace=self.ws)
         for t in range(self.T, self.T + self.steps):
-            hb.delta_recurrence(self.shape, self.state, self.out[t], self.qkv[t], self.beta[t],
-                                self.decay[t], rows=1, regime="decode")
+            hb.delta_recurrence(self.shape, self.state, out[t], qkv[t], beta[t], decay[t],
+                                rows=1, regime="decode")
 
-    def e2e_step(self):
-        for d, h in zip((self.qkv, self.beta, self.decay), self.h_in):
+    def e2e_step(self, i=0):
+        qkv, beta, decay, out = self.sets[0]
+        for d, h in zip((qkv, beta, decay), self.h_in):
             d.copy_(h, non_blocking=True)
-        self.step()
-        self.h_out.copy_(self.out, non_blocking=True)
+        self.step(0)
+        self.h_out.copy_(out, non_blocking=True)
 
     def describe(self):
         return {"workload": "GatedDeltaNet prefill then decode (BASELINE configs[2])",
@@ -278,14 +291,13 @@ class GdnWorkload(Workload):
 
 class BatchWorkload(Workload):
     def __init__(self, device, rank=0, world=1, seed=0x5EED0004):
-        import numpy as np
         import torch
         import herbert_b200 as hb
         from herbert_b200.inputs import batch_lengths, lpt_assign
         self.hb = hb
         lens = batch_lengths(64, 1024, 32768, seed)
         # the new token is position L-1: the cache holds L keys
-        mine = lpt_assign(lens * 1, world)[rank]
+        mine = lpt_assign(lens, world)[rank]
         self.lens = [int(lens[i]) for i in mine]
         gen = torch.Generator(device=device).manual_seed(seed + rank)
         qd = HQ * HD
@@ -303,18 +315,19 @@ class BatchWorkload(Workload):
         self.ws = None
         self.work = sum(4 * HKV * L * HD for L in self.lens) + len(self.lens) * 3 * qd * 2
         self.units = "GB/s"
+        self.R = 1
+        self.set_bytes = self.work
         self.h_in = [self.q.cpu().pin_memory()]
         self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
-        self.h2d = self.h_in[0].numel() * 2
-        self.d2h = self.h_out.numel() * 2
-        self.total_lens = lens
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
 
-    def step(self):
+    def step(self, i=0):
         self.ws = self.hb.decode_batch(self.spec, self.table, len(self.lens),
                                        max(self.lens) - 1, sum(self.lens) - len(self.lens),
                                        workspace=self.ws)
 
-    def e2e_step(self):
+    def e2e_step(self, i=0):
         # a decode step of a serving loop: the new query rows arrive from the
         # host, the caches are already resident, the outputs go back
         self.q.copy_(self.h_in[0], non_blocking=True)
@@ -369,7 +382,6 @@ def run_ours(args):
                                 device_id=device)
     cfg = args.config
     wl = make_workload(cfg, device, rank, world)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -378,33 +390,39 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        wl.step()
+    for i in range(args.warmup):
+        wl.step(i)
+        wl.e2e_step(i)
     barrier()
 
-    def timed(fn, steps):
-        evs = []
-        for _ in range(steps):
-            flush.fill_(1)  # untimed: evict the inputs from L2
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            fn()
-            b.record(stream)
-            evs.append((a, b))
+    def capture(fn, steps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(steps):
+                fn(i)
+        return g
+
+    def timed(graph):
+        graph.replay()  # untimed replay: the graph's first launch uploads it
         torch.cuda.synchronize()
-        return sum(a.elapsed_time(b) for a, b in evs) / 1e3  # seconds
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 1e3  # seconds for all steps
 
-    sampler = ClockSampler(smi_index(local)).start() if rank == 0 else None
+    g_dev = capture(wl.step, args.steps)
+    g_e2e = capture(wl.e2e_step, args.steps)
     barrier()
-    t_dev = timed(wl.step, args.steps)
+    sampler = ClockSampler(smi_index(local)).start() if rank == 0 else None
+    t_dev = timed(g_dev)
     barrier()
     clocks = sampler.stop() if sampler else None
-    for _ in range(max(1, args.warmup // 2)):
-        wl.e2e_step()
+    t_e2e = timed(g_e2e)
     barrier()
-    t_e2e = timed(wl.e2e_step, args.steps)
-    barrier()
+    del g_dev, g_e2e
 
     t = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=device)
     work = torch.tensor([float(wl.work)], dtype=torch.float64, device=device)
@@ -442,7 +460,9 @@ def run_ours(args):
             "data": "synthetic",
             "config": dict(wl.describe(), parallelism=(
                 f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
-                else f"{world} independent replicas"), l2="flushed (256 MB write) before each step"),
+                else f"{world} independent replicas"),
+                l2=f"inputs rotate over {wl.R} copies ({wl.R * wl.set_bytes / 2**20:.0f} MiB) per GPU",
+                timing=f"one CUDA graph of {args.steps} steps between CUDA events"),
             "roofline": {"bound": BOUND[cfg], "achieved": round(achieved, 3), "peak": peak,
                          "unit": unit, "frac": round(achieved / peak, 4),
                          "peak_source": pk["source"] + (" burst" if unit == "TFLOP/s" else ""),

@@ -41,6 +41,7 @@ constexpr int kRingBytes = 131072;  // K+V tiles in flight per CTA (one CTA per 
 constexpr int kConsumerWarps = 8;   // 4 positions per warp per tile
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr uint32_t kFull = 0xFFFFFFFFu;
+constexpr int64_t kMaxSplits = 1024;  // 3 * 8 * 1024 floats fit the ring
 
 struct DecodeParams {
   const hb_decode_seq* seqs;  // device table, or nullptr: use `one`
@@ -323,20 +324,38 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
     consumer_sync();
     if (!flags[1]) return;
     __threadfence();
+    // The last CTA of the unit merges every split.  The split maxima and
+    // sums are staged in shared memory first (one load per thread), the
+    // per-split weights computed once per head, then each output element
+    // sums its splits with independent loads in flight.
     const float* up = part_out + int64_t(unit) * p.nsplit * PSTRIDE;
+    float* sml = ws;                       // [active][2G]: m then l
+    float* smw = ws + active * 2 * G;      // [active][G]: exp2(m_s - M)
+    float* smL = smw + active * G;         // [G]: merged sums
+    for (int i = tid; i < active * 2 * G; i += kConsumerWarps * 32)
+      sml[i] = __ldcg(up + (i / (2 * G)) * PSTRIDE + G * HD + (i % (2 * G)));
+    consumer_sync();
+    if (tid < G) {
+      float M = -INFINITY;
+      for (int sp = 0; sp < active; ++sp) M = fmaxf(M, sml[sp * 2 * G + tid]);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float Ls = 0.f;
+      for (int sp = 0; sp < active; ++sp) {
+        const float w = fast_exp2(sml[sp * 2 * G + tid] - Mu);
+        smw[sp * G + tid] = w;
+        Ls += sml[sp * 2 * G + G + tid] * w;
+      }
+      smL[tid] = Ls;
+    }
+    consumer_sync();
 #pragma unroll
     for (int k = 0; k < PER_T; ++k) {
       const int e = min(tid + k * kConsumerWarps * 32, NOUT - 1), g = e / HD;
-      float M = -INFINITY;
-      for (int sp = 0; sp < active; ++sp) M = fmaxf(M, __ldcg(up + sp * PSTRIDE + G * HD + g));
-      const float Mu = M == -INFINITY ? 0.f : M;
-      float Ls = 0.f, Os = 0.f;
-      for (int sp = 0; sp < active; ++sp) {
-        const float f = fast_exp2(__ldcg(up + sp * PSTRIDE + G * HD + g) - Mu);
-        Ls += __ldcg(up + sp * PSTRIDE + G * HD + G + g) * f;
-        Os += __ldcg(up + sp * PSTRIDE + e) * f;
-      }
-      ol[k] = Ls; oo[k] = Os;
+      float Os = 0.f;
+#pragma unroll 8
+      for (int sp = 0; sp < active; ++sp) Os += smw[sp * G + g] * __ldcg(up + sp * PSTRIDE + e);
+      ol[k] = smL[g];
+      oo[k] = Os;
     }
     if (tid == 0) p.counters[unit] = 0u;  // leave the workspace reusable
   }
@@ -388,6 +407,10 @@ int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms) {
   c = (c + kTile - 1) / kTile * kTile;
   if (c < 2 * kTile) c = 2 * kTile;
   if (c > 8192) c = 8192;
+  // the last CTA stages 3G floats per split in the 128 KB ring: at most
+  // 1024 splits per unit
+  const int64_t min_chunk = (max_n + kMaxSplits - 1) / kMaxSplits;
+  if (c < min_chunk) c = (min_chunk + kTile - 1) / kTile * kTile;
   if (c > max_n) c = (max_n + kTile - 1) / kTile * kTile;
   return int(c);
 }
