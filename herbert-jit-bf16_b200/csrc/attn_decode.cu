@@ -30,10 +30,38 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "hb_common.cuh"
 #include "hb_internal.h"
 
 namespace hb {
+
+// Scratch of hb_attn_decode_noalloc: a file-scope device array, so callers
+// that may not allocate device memory still get split-KV decoding.  Every
+// device that loads the library holds these bytes until the process exits.
+// In host code the name is only a host-side stand-in for the symbol; the
+// device address comes from cudaGetSymbolAddress (noalloc_scratch below).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[HB_NOALLOC_SCRATCH_BYTES];
+
+cudaError_t noalloc_scratch(void** ptr) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // with `dev` current
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *ptr = addr[dev];
+  return cudaSuccess;
+}
+
 namespace {
 
 constexpr int kTile = 32;           // positions per pipeline tile

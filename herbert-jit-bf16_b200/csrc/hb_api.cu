@@ -182,13 +182,10 @@ size_t hb_attn_decode_workspace_bytes(const hb_attn_spec* s, const hb_attn_call*
   return plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows)).bytes;
 }
 
-static hb_status decode_common(const hb_attn_spec* s, const hb_attn_call* c, void* ws,
-                               size_t ws_bytes, hb_stream_t stream) {
-  hb_status r = check_spec(s);
-  if (r != HB_OK) return r;
-  if ((r = check_call(s, c)) != HB_OK) return r;
-  const DecodePlan pl = plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows));
-  if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
+// Launches the decode kernel of one sequence on a validated call with the
+// workspace `ws` laid out by plan `pl`.
+static hb_status decode_launch(const hb_attn_spec* s, const hb_attn_call* c, const DecodePlan& pl,
+                               void* ws, hb_stream_t stream) {
   DecodeLaunch L;
   L.seqs = nullptr;
   L.one.q = c->q;
@@ -216,6 +213,40 @@ static hb_status decode_common(const hb_attn_spec* s, const hb_attn_call* c, voi
   cudaError_t e = launch_attn_decode(L, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode launch");
   return HB_OK;
+}
+
+static hb_status decode_common(const hb_attn_spec* s, const hb_attn_call* c, void* ws,
+                               size_t ws_bytes, hb_stream_t stream) {
+  hb_status r = check_spec(s);
+  if (r != HB_OK) return r;
+  if ((r = check_call(s, c)) != HB_OK) return r;
+  const DecodePlan pl = plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows));
+  if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
+  return decode_launch(s, c, pl, ws, stream);
+}
+
+// The allocation-free variant: the same kernel and plan, with the static
+// scratch of attn_decode.cu as its workspace.  Its status word and split
+// counters must start at zero, and the array keeps whatever the previous
+// call left, so they are cleared (one cudaMemsetAsync, no allocation) on
+// `stream` before the launch.
+hb_status hb_attn_decode_noalloc(const hb_attn_spec* s, const hb_attn_call* c,
+                                 hb_stream_t stream) {
+  hb_status r = check_spec(s);
+  if (r != HB_OK) return r;
+  if ((r = check_call(s, c)) != HB_OK) return r;
+  const DecodePlan pl = plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows));
+  if (pl.bytes > size_t(HB_NOALLOC_SCRATCH_BYTES))
+    return fail(HB_ERR_WORKSPACE,
+                "hb_attn_decode_noalloc: this call needs %zu bytes of scratch, above the static "
+                "maximum HB_NOALLOC_SCRATCH_BYTES = %zu; use hb_attn_decode with a workspace",
+                pl.bytes, size_t(HB_NOALLOC_SCRATCH_BYTES));
+  void* scratch = nullptr;
+  cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "hb_attn_decode_noalloc scratch set-up");
+  e = cudaMemsetAsync(scratch, 0, pl.partials_off, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "hb_attn_decode_noalloc scratch clear");
+  return decode_launch(s, c, pl, scratch, stream);
 }
 
 hb_status hb_attn_decode(const hb_attn_spec* s, const hb_attn_call* c, void* ws, size_t ws_bytes,

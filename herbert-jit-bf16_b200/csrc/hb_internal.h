@@ -49,6 +49,9 @@ struct DecodeLaunch {
   float* partials;
 };
 bool decode_serves(int64_t head_dim, int64_t gqa);
+// Device address of the static scratch of hb_attn_decode_noalloc on the
+// current device (looked up on the first call per device).
+cudaError_t noalloc_scratch(void** ptr);
 int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms);
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);

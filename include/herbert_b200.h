@@ -129,6 +129,29 @@ HB_API hb_status hb_attn_decode(const hb_attn_spec *spec, const hb_attn_call *ca
                          void *workspace, size_t workspace_bytes, hb_stream_t stream);
 
 /*
+ * Decode SDPA that allocates nothing and takes no workspace.  No counterpart
+ * in the reference: it exists for callers that cannot hand this library any
+ * device memory -- an engine whose device memory is planned once at start-up
+ * with nothing allocated during a pass, a host that exposes no workspace to
+ * its plugins, or code that must not trigger cudaMalloc's implicit device
+ * synchronisation in a latency-bound decode loop.
+ *
+ * Same arguments, kernel and results as hb_attn_decode.  Its scratch is one
+ * file-scope device array of HB_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until exit; a call needing more (see
+ * hb_attn_decode_workspace_bytes) is refused with HB_ERR_WORKSPACE before
+ * anything is launched.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) -- make that first call before any
+ * stream capture.  Each call clears the part of the array that must start at
+ * zero (one cudaMemsetAsync on `stream`) and then launches; the array is
+ * shared by all calls on a device, so calls whose executions overlap on the
+ * GPU (different streams without ordering) race and give wrong results.
+ */
+#define HB_NOALLOC_SCRATCH_BYTES (4u << 20)
+HB_API hb_status hb_attn_decode_noalloc(const hb_attn_spec *spec, const hb_attn_call *call,
+                                        hb_stream_t stream);
+
+/*
  * Batched decode: `nseq` independent sequences (table in device memory),
  * one query row each; max_past bounds every seqs[i].past and sum_past is
  * their sum (0 = unknown), used only to size the splits.  No counterpart in
