@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
   constexpr int NV = 4 * G;                // partial sums per lane per tile
   constexpr int SH = 5 - Log2<NV>::value;  // lane >> SH = value index
   constexpr int TILE_ELEMS = kTile * HD;
-  constexpr int PSTRIDE = G * HD + 2 * G;  // floats per split partial
+  constexpr int PSTRIDE = G * HD + ((2 * G + 3) & ~3);  // floats per split partial (16 B multiple)
 
   constexpr int RING_BYTES = 2 * kStages * TILE_ELEMS * 2;
   constexpr int MERGE_BYTES = kConsumerWarps * PSTRIDE * 4;
@@ -343,15 +343,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
         __stcg(mine + G * HD + G + g, ol[k]);
       }
     }
-    __threadfence();
-    consumer_sync();
+    consumer_sync();  // every partial store of this CTA precedes thread 0's release
     if (tid == 0) {
+      __threadfence();
       const unsigned prev = atomicAdd(&p.counters[unit], 1u);
+      __threadfence();
       flags[1] = (prev == unsigned(active - 1));
     }
     consumer_sync();
     if (!flags[1]) return;
-    __threadfence();
     // The last CTA of the unit merges every split.  The split maxima and
     // sums are staged in shared memory first (one load per thread), the
     // per-split weights computed once per head, then each output element
@@ -376,16 +376,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
       smL[tid] = Ls;
     }
     consumer_sync();
-#pragma unroll
-    for (int k = 0; k < PER_T; ++k) {
-      const int e = min(tid + k * kConsumerWarps * 32, NOUT - 1), g = e / HD;
-      float Os = 0.f;
-#pragma unroll 8
-      for (int sp = 0; sp < active; ++sp) Os += smw[sp * G + g] * __ldcg(up + sp * PSTRIDE + e);
-      ol[k] = smL[g];
-      oo[k] = Os;
+    // every thread owns 4 consecutive outputs (one head): one 16-byte load
+    // per split, all independent, then finalise them here
+    uint16_t* orow_l = d.output + int64_t(row) * p.out_row;
+    for (int qd = tid; qd < NOUT / 4; qd += kConsumerWarps * 32) {
+      const int e = qd * 4, g = e / HD, dd = e % HD, hq = h0 + g;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 16
+      for (int sp = 0; sp < active; ++sp) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(up + sp * PSTRIDE + e));
+        const float w = smw[sp * G + g];
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+      const float Ls = smL[g];
+      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+      uint16_t a[4] = {f32_to_bf16_cvtne(acc.x * inv), f32_to_bf16_cvtne(acc.y * inv),
+                       f32_to_bf16_cvtne(acc.z * inv), f32_to_bf16_cvtne(acc.w * inv)};
+      if (p.gate_offset >= 0) {
+        const uint2 gw = *reinterpret_cast<const uint2*>(qrow + p.gate_offset + int64_t(hq) * HD + dd);
+        a[0] = gate_bf16(a[0], uint16_t(gw.x & 0xFFFFu));
+        a[1] = gate_bf16(a[1], uint16_t(gw.x >> 16));
+        a[2] = gate_bf16(a[2], uint16_t(gw.y & 0xFFFFu));
+        a[3] = gate_bf16(a[3], uint16_t(gw.y >> 16));
+      }
+      *reinterpret_cast<uint2*>(orow_l + int64_t(hq) * HD + dd) =
+          make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
     }
     if (tid == 0) p.counters[unit] = 0u;  // leave the workspace reusable
+    return;
   }
 
   // ---------------------------------------------------- finalise + gate
@@ -444,7 +465,7 @@ int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms) {
 }
 
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim) {
-  return size_t(gqa * head_dim + 2 * gqa);
+  return size_t(gqa * head_dim + ((2 * gqa + 3) & ~int64_t(3)));
 }
 
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st) {

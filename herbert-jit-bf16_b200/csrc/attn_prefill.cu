@@ -1,0 +1,367 @@
+// attn_prefill.cu -- causal flash attention for sm_100a on the 5th-generation
+// tensor cores (tcgen05), with the Qwen3.5 output gate in the epilogue.
+//
+// Replaces, in the prefill regime, the reference's attention node
+// (SdpaPrefillFn blocks of 8 rows, src/jit/emit_sdpa.rs:173-304,
+// src/jit/target/x86/emit_sdpa/x86/prefill.rs:733-912, remainder rows on the
+// decode kernel) and the output-gate node (src/jit/target/x86/emit_elem.rs:333-420).
+// Row r of the call is the query at absolute position past + r and sees keys
+// [0, past + r] (src/jit/target/x86/execution/attention.rs:189-196).
+//
+// CTA = one tile of 128 query rows of one query head (head_dim 256):
+//   warp 4       TMA producer: Q tile once, then K and V tiles of 64 keys
+//                into two-stage rings (SWIZZLE_128B, no multicast);
+//   warp 5       MMA issuer: S_j = Q K_j^T (M128 N64 K256, 16 MMAs) into one
+//                of two TMEM S buffers, then O += P_{j-1} V_{j-1} (M128 N256
+//                K64, 4 MMAs, V read MN-major) into the TMEM O accumulator;
+//                each group is committed to an mbarrier;
+//   warps 0-3    softmax: one thread per query row reads its S row from TMEM,
+//                applies the causal mask, keeps the running max m and sum l in
+//                the log2 domain, writes P = 2^(s - m) as bf16 into shared
+//                memory in the UMMA K-major swizzled layout, and rescales the
+//                O row in TMEM only when the max grows by more than 2^8;
+//                the epilogue divides O by l, rounds to bf16 and applies the
+//                gate with the reference's exp polynomial.
+// TMEM: S buffers at columns [0,128), O at [256,512) of a 512-column
+// allocation.  Shared memory: Q 64 KB + K 2x32 KB + V 2x32 KB + P 2x16 KB.
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "hb_common.cuh"
+#include "hb_internal.h"
+#include "hb_sm100.cuh"
+
+namespace hb {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 64, HDIM = 256;
+constexpr int kThreads = 192;
+constexpr int Q_BYTES = BM * HDIM * 2;   // 4 column blocks of [128 rows x 128 B]
+constexpr int KV_BYTES = BN * HDIM * 2;  // 4 column blocks of [64 rows x 128 B]
+constexpr int P_BYTES = BM * BN * 2;     // 1 block of [128 rows x 128 B]
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;
+constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
+constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
+constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+constexpr int NBAR = 17;
+constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + 1 KB alignment slack
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t S_COL = 0, O_COL = 256;
+constexpr float kRescaleLog2 = 8.0f;  // keep a stale max while p stays below 2^8
+
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9,
+           S_EMPTY = 11, P_FULL = 13, PV_DONE = 15 };
+
+struct PrefillParams {
+  const uint16_t* q;  // gate reads
+  uint16_t* out;
+  int64_t q_row, out_row, gate_offset;
+  int rows, past, heads, gqa, n_qtiles;
+  float scale_log2;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = p.n_qtiles - 1 - int(blockIdx.x) / p.heads;  // heaviest tiles first
+  const int h = int(blockIdx.x) % p.heads;
+  const int kvh = h / p.gqa;
+  const int m0 = qt * BM;
+  const int n_kv = min(p.past + m0 + BM, p.past + p.rows);
+  const int ntiles = (n_kv + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[Q_FULL], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar[K_FULL + s], 1);
+      mbar_init(&bar[K_EMPTY + s], 1);
+      mbar_init(&bar[V_FULL + s], 1);
+      mbar_init(&bar[V_EMPTY + s], 1);
+      mbar_init(&bar[S_FULL + s], 1);
+      mbar_init(&bar[S_EMPTY + s], 128);
+      mbar_init(&bar[P_FULL + s], 128);
+      mbar_init(&bar[PV_DONE + s], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, TMEM_COLS);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](int b, uint32_t parity) -> bool {
+    if (*abort_flag) return false;
+    if (mbar_wait(&bar[b], parity)) return true;
+    record_status(p.status, kStatusTimeout);
+    *abort_flag = 1;
+    return false;
+  };
+
+  if (warp == 4) {  // ------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(&bar[Q_FULL], Q_BYTES);
+      for (int c = 0; c < 4; ++c)
+        tma_load_2d(smem + OFF_Q + c * (BM * 128), &tmQ, &bar[Q_FULL], h * HDIM + c * 64, m0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (j >= 2 && !wait(K_EMPTY + s, ph ^ 1)) break;
+        mbar_arrive_expect_tx(&bar[K_FULL + s], KV_BYTES);
+        for (int c = 0; c < 4; ++c)
+          tma_load_3d(smem + OFF_K + s * KV_BYTES + c * (BN * 128), &tmK, &bar[K_FULL + s], c * 64,
+                      j * BN, kvh);
+        if (j >= 2 && !wait(V_EMPTY + s, ph ^ 1)) break;
+        mbar_arrive_expect_tx(&bar[V_FULL + s], KV_BYTES);
+        for (int c = 0; c < 4; ++c)
+          tma_load_3d(smem + OFF_V + s * KV_BYTES + c * (BN * 128), &tmV, &bar[V_FULL + s], c * 64,
+                      j * BN, kvh);
+      }
+    }
+  } else if (warp == 5) {  // ------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idPV = idesc_bf16(BM, HDIM, false, true);
+      const uint32_t qb = smem_u32(smem + OFF_Q);
+      bool ok = wait(Q_FULL, 0);
+      for (int j = 0; ok && j <= ntiles; ++j) {
+        if (j < ntiles) {
+          const int s = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          if (!wait(K_FULL + s, ph)) break;
+          if (j >= 2 && !wait(S_EMPTY + s, ph ^ 1)) break;
+          fence_after_sync();
+          const uint32_t kb = smem_u32(smem + OFF_K + s * KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < HDIM / 16; ++kk) {
+            const uint64_t a = sw128_desc(qb + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t b = sw128_desc(kb + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+            mma_bf16_ss(tmem + S_COL + s * BN, a, b, idS, kk > 0);
+          }
+          mma_commit(&bar[S_FULL + s]);
+          mma_commit(&bar[K_EMPTY + s]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, s = jj & 1;
+          const uint32_t ph = (jj >> 1) & 1;
+          if (!wait(P_FULL + s, ph) || !wait(V_FULL + s, ph)) break;
+          fence_after_sync();
+          const uint32_t pb = smem_u32(smem + OFF_P + s * P_BYTES);
+          const uint32_t vb = smem_u32(smem + OFF_V + s * KV_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t a = sw128_desc(pb + kk * 32, 16, 1024);
+            const uint64_t b = sw128_desc(vb + kk * 16 * 128, BN * 128, 1024);
+            mma_bf16_ss(tmem + O_COL, a, b, idPV, jj > 0 || kk > 0);
+          }
+          mma_commit(&bar[PV_DONE + s]);
+          mma_commit(&bar[V_EMPTY + s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {  // ------------------------------------------ softmax + epilogue
+    const int row = threadIdx.x;  // 0..127 = TMEM lane
+    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    const int qpos = p.past + m0 + row;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      ok = __all_sync(0xFFFFFFFFu, wait(S_FULL + s, ph) && ok);
+      fence_after_sync();
+      uint32_t ra[32], rb[32];
+      tmem_ld32(tl + S_COL + s * BN, ra);
+      tmem_ld32(tl + S_COL + s * BN + 32, rb);
+      tmem_wait_ld();
+      fence_before_sync();
+      mbar_arrive(&bar[S_EMPTY + s]);
+      const int kb = j * BN;
+      float v[64];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        v[c] = (kb + c <= qpos) ? __uint_as_float(ra[c]) * p.scale_log2 : -INFINITY;
+        v[32 + c] = (kb + 32 + c <= qpos) ? __uint_as_float(rb[c]) * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, fmaxf(v[c], v[32 + c]));
+      }
+      const float m_new = fmaxf(m, mx);
+      float factor = 1.f;
+      bool resc = false;
+      if (m == -INFINITY) {
+        m = m_new;  // first keys of the row: O holds nothing yet
+      } else if (m_new > m + kRescaleLog2) {
+        factor = fast_exp2(m - m_new);
+        resc = true;
+      }
+      if (__any_sync(0xFFFFFFFFu, resc)) {
+        // O holds PV_0 .. PV_{j-1}; the last of them may still be running
+        const int jp = j - 1;
+        ok = __all_sync(0xFFFFFFFFu, wait(PV_DONE + (jp & 1), (jp >> 1) & 1) && ok);
+        fence_after_sync();
+#pragma unroll 1
+        for (int c = 0; c < HDIM / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tl + O_COL + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tmem_st32(tl + O_COL + c * 32, r);
+        }
+        tmem_wait_st();
+        fence_before_sync();
+        if (resc) {
+          l *= factor;
+          m = m_new;
+        }
+      }
+      // P_j goes to buffer s, which PV_{j-2} read
+      if (j >= 2) ok = __all_sync(0xFFFFFFFFu, wait(PV_DONE + s, ph ^ 1) && ok);
+      float rowsum = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = fast_exp2(v[2 * c] - m), p1 = fast_exp2(v[2 * c + 1] - m);
+        rowsum += p0 + p1;
+        pk[c] = pack_bf16x2(p0, p1);
+      }
+      l += rowsum;
+      uint8_t* prow = smem + OFF_P + s * P_BYTES + row * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch)
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
+            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      fence_proxy_async_smem();
+      mbar_arrive(&bar[P_FULL + s]);
+      if (!ok) break;
+    }
+    // epilogue: O / l -> bf16 -> gate -> global
+    const int jl = ntiles - 1;
+    ok = __all_sync(0xFFFFFFFFu, ok && wait(PV_DONE + (jl & 1), (jl >> 1) & 1));
+    fence_after_sync();
+    const int r = m0 + row;
+    const bool valid = ok && r < p.rows;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    uint16_t* orow = p.out + int64_t(r) * p.out_row + int64_t(h) * HDIM;
+    const uint16_t* grow = p.q + int64_t(r) * p.q_row + p.gate_offset + int64_t(h) * HDIM;
+#pragma unroll 1
+    for (int c = 0; c < HDIM / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32(tl + O_COL + c * 32, o);
+      tmem_wait_ld();
+      if (valid) {
+#pragma unroll
+        for (int g8 = 0; g8 < 4; ++g8) {
+          uint32_t w[4];
+          uint4 gv = make_uint4(0, 0, 0, 0);
+          if (p.gate_offset >= 0) gv = *reinterpret_cast<const uint4*>(grow + c * 32 + g8 * 8);
+          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint16_t a0 = f32_to_bf16_cvtne(__uint_as_float(o[g8 * 8 + 2 * i]) * inv);
+            uint16_t a1 = f32_to_bf16_cvtne(__uint_as_float(o[g8 * 8 + 2 * i + 1]) * inv);
+            if (p.gate_offset >= 0) {
+              a0 = gate_bf16(a0, uint16_t(gw[i] & 0xFFFFu));
+              a1 = gate_bf16(a1, uint16_t(gw[i] >> 16));
+            }
+            w[i] = uint32_t(a0) | (uint32_t(a1) << 16);
+          }
+          *reinterpret_cast<uint4*>(orow + c * 32 + g8 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    }
+  }
+
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 5) {
+    fence_after_sync();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+bool encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+                 const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint32_t es[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, cuuint32_t(rank), const_cast<void*>(base), dims,
+            strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool prefill_serves(int64_t head_dim) { return head_dim == HDIM; }
+
+cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
+  CUtensorMap tq, tk, tv;
+  const cuuint64_t qd[2] = {cuuint64_t(L.q_row), cuuint64_t(L.rows)};
+  const cuuint64_t qs[1] = {cuuint64_t(L.q_row) * 2};
+  const cuuint32_t qbox[2] = {64, BM};
+  const cuuint64_t kd[3] = {cuuint64_t(HDIM), cuuint64_t(L.past + L.rows), cuuint64_t(L.hkv)};
+  const cuuint64_t ks[2] = {cuuint64_t(HDIM) * 2, cuuint64_t(L.kv_stride) * 2};
+  const cuuint32_t kbox[3] = {64, BN, 1};
+  if (!encode_bf16(&tq, L.q, 2, qd, qs, qbox) || !encode_bf16(&tk, L.keys, 3, kd, ks, kbox) ||
+      !encode_bf16(&tv, L.values, 3, kd, ks, kbox))
+    return cudaErrorInvalidValue;
+  static DeviceFlags configured;
+  cudaError_t e = configured.once([] {
+    return cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                SMEM_BYTES);
+  });
+  if (e != cudaSuccess) return e;
+  PrefillParams p;
+  p.q = L.q;
+  p.out = L.out;
+  p.q_row = L.q_row;
+  p.out_row = L.out_row;
+  p.gate_offset = L.gate_offset;
+  p.rows = int(L.rows);
+  p.past = int(L.past);
+  p.heads = int(L.heads);
+  p.gqa = int(L.gqa);
+  p.n_qtiles = int((L.rows + BM - 1) / BM);
+  p.scale_log2 = L.scale * 1.4426950408889634f;
+  p.status = L.status;
+  attn_prefill_kernel<<<unsigned(p.n_qtiles * p.heads), kThreads, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace hb

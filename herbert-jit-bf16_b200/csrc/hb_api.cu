@@ -58,8 +58,9 @@ hb_status check_spec(const hb_attn_spec* s) {
     return fail(HB_DECLINE_HEAD_DIM,
                 "head_dim out of domain (served: 128, 256 with gqa 1/2/4/8); got head_dim=%lld gqa=%lld",
                 (long long)s->head_dim, (long long)s->gqa);
-  if (s->q_row % 8 || s->q_head % 8 || s->out_row % 8)
-    return fail(HB_ERR_ARG, "q_row, q_head and out_row must be multiples of 8 elements (16 bytes)");
+  if (s->q_row % 8 || s->q_head % 8 || s->out_row % 8 || (s->gate_offset > 0 && s->gate_offset % 8))
+    return fail(HB_ERR_ARG,
+                "q_row, q_head, out_row and gate_offset must be multiples of 8 elements (16 bytes)");
   return HB_OK;
 }
 
@@ -298,13 +299,49 @@ hb_status hb_attn_decode_batch(const hb_attn_spec* s, const hb_decode_seq* seqs,
   return HB_OK;
 }
 
+// Rows from which the tensor-core kernel takes a prefill block; shorter
+// blocks go to the decode kernel, as the reference serves the rows a block
+// kernel does not cover with its decode kernel.
+static constexpr int64_t kPrefillMinRows = 64;
+
+static bool prefill_on_tensor_cores(const hb_attn_spec* s, const hb_attn_call* c) {
+  return prefill_serves(s->head_dim) && c->rows >= kPrefillMinRows &&
+         c->past + c->rows < (int64_t(1) << 31) &&
+         (s->gate_offset < 0 || s->gate_offset % 8 == 0);
+}
+
 size_t hb_attn_prefill_workspace_bytes(const hb_attn_spec* s, const hb_attn_call* c) {
+  if (check_spec(s) != HB_OK || !c || c->rows <= 0 || c->past < 0) return 0;
+  if (prefill_on_tensor_cores(s, c)) return kWsHeader;
   return hb_attn_decode_workspace_bytes(s, c);
 }
 
 hb_status hb_attn_prefill(const hb_attn_spec* s, const hb_attn_call* c, void* ws, size_t ws_bytes,
                           hb_stream_t stream) {
-  return decode_common(s, c, ws, ws_bytes, stream);
+  hb_status r = check_spec(s);
+  if (r != HB_OK) return r;
+  if ((r = check_call(s, c)) != HB_OK) return r;
+  if (!prefill_on_tensor_cores(s, c)) return decode_common(s, c, ws, ws_bytes, stream);
+  if ((r = check_ws(ws, ws_bytes, kWsHeader)) != HB_OK) return r;
+  PrefillLaunch L;
+  L.q = c->q;
+  L.keys = c->keys;
+  L.values = c->values;
+  L.out = c->output;
+  L.q_row = s->q_row;
+  L.out_row = s->out_row;
+  L.gate_offset = s->gate_offset;
+  L.kv_stride = c->kv_stride;
+  L.rows = c->rows;
+  L.past = c->past;
+  L.heads = s->heads;
+  L.gqa = s->gqa;
+  L.hkv = s->heads / s->gqa;
+  L.scale = c->scale;
+  L.status = static_cast<int*>(ws);
+  cudaError_t e = launch_attn_prefill(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attn_prefill launch");
+  return HB_OK;
 }
 
 hb_status hb_kv_append(const hb_kv_spec* s, const hb_kv_call* c, hb_stream_t stream) {

@@ -56,6 +56,20 @@ int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms);
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
 
+// ---------------------------------------------------------- attn prefill
+struct PrefillLaunch {
+  const uint16_t* q;
+  const uint16_t* keys;
+  const uint16_t* values;
+  uint16_t* out;
+  int64_t q_row, out_row, gate_offset, kv_stride;
+  int64_t rows, past, heads, gqa, hkv;
+  float scale;
+  int* status;
+};
+bool prefill_serves(int64_t head_dim);
+cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st);
+
 // ------------------------------------------------------------ kv append
 cudaError_t launch_kv_append(const hb_kv_spec& s, const hb_kv_call& c, cudaStream_t st);
 

@@ -48,13 +48,18 @@ def rel_frob(got, ref) -> float:
 
 # ------------------------------------------------------------------ oracle
 
-def oracle_attention(inp: AttentionInputs, threads: int = 0, impl: int = 0) -> np.ndarray:
+def oracle_attention(inp: AttentionInputs, threads: int = 0, impl=None) -> np.ndarray:
+    # the AVX512-BF16 transcription (row by row) and the portable emulation
+    # (8-row blocks) give identical bits (tests/test_oracle.py); the first is
+    # ~40x faster where the CPU has it
+    if impl is None:
+        impl = 1 if oracle.has_avx512bf16() else 0
     out = oracle.attention(inp.q.ravel(), inp.keys.ravel(), inp.values.ravel(), rows=inp.rows,
                            past=inp.past, heads=inp.heads, gqa=inp.gqa, head_dim=inp.head_dim,
                            q_row=inp.q_row, q_head=inp.head_dim, out_row=inp.out_row,
                            gate_offset=inp.gate_offset if inp.gated else None,
-                           kv_stride=inp.kv_stride, scale=inp.scale, impl=impl, use_block=1,
-                           threads=threads)
+                           kv_stride=inp.kv_stride, scale=inp.scale, impl=impl,
+                           use_block=0 if impl == 1 else 1, threads=threads)
     return out.reshape(inp.rows, inp.out_row)
 
 

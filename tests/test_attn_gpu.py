@@ -50,11 +50,27 @@ def test_decode_workspace_reuse_is_stable(cuda_device):
     assert_sdpa_close(a, oracle_attention(inp), "reuse")
 
 
-@pytest.mark.parametrize("rows,past", [(64, 0), (37, 11), (200, 300)])
-def test_prefill_matches_oracle(cuda_device, rows, past):
-    inp = AttentionInputs(rows, past, capacity=past + rows)
+PREFILL_CASES = [
+    # rows, past, heads, kv_heads, gated
+    (64, 0, 16, 4, True),       # one partial 128-row tile on the tensor cores
+    (37, 11, 16, 4, True),      # below 64 rows: the decode kernel
+    (200, 300, 16, 4, True),
+    (256, 0, 16, 4, True),
+    (1000, 24, 16, 4, False),   # ragged last tile, no gate
+    (129, 5000, 8, 8, True),    # long past, gqa 1
+    (384, 0, 8, 1, True),       # gqa 8
+    (4096, 0, 16, 4, True),     # the prefill configuration of the benchmark
+]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES, ids=lambda c: "r{}p{}h{}k{}{}".format(
+    c[0], c[1], c[2], c[3], "g" if c[4] else ""))
+def test_prefill_matches_oracle(cuda_device, case):
+    rows, past, heads, kvh, gated = case
+    inp = AttentionInputs(rows, past, heads=heads, kv_heads=kvh, gated=gated,
+                          capacity=past + rows)
     got, _ = gpu_attention(inp, "prefill")
-    assert_sdpa_close(got, oracle_attention(inp), f"prefill rows={rows} past={past}")
+    assert_sdpa_close(got, oracle_attention(inp), f"prefill {case}")
 
 
 @pytest.mark.parametrize("name", ATTN_FIXTURES)
