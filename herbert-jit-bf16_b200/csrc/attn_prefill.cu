@@ -20,8 +20,10 @@
 //                the log2 domain, writes P = 2^(s - m) as bf16 into shared
 //                memory in the UMMA K-major swizzled layout, and rescales the
 //                O row in TMEM only when the max grows by more than 2^8;
-//                the epilogue divides O by l, rounds to bf16 and applies the
-//                gate with the reference's exp polynomial.
+//   warps 0-7    epilogue: O / l, bf16, gate with the reference's exp
+//                polynomial and rounding steps; the gate tile comes in by TMA
+//                (into the K ring, free once the last S is computed) and the
+//                output tile leaves by TMA store (staged in the V ring).
 // TMEM: S buffers at columns [0,128), O at [256,512) of a 512-column
 // allocation.  Shared memory: Q 64 KB + K 2x32 KB + V 2x32 KB + P 2x16 KB.
 #include <cstdint>
@@ -38,7 +40,8 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128, BN = 64, HDIM = 256;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warps 0-3 softmax, 0-7 epilogue, 8 TMA, 9 MMA
+constexpr int kTmaWarp = 8, kMmaWarp = 9;
 constexpr int Q_BYTES = BM * HDIM * 2;   // 4 column blocks of [128 rows x 128 B]
 constexpr int KV_BYTES = BN * HDIM * 2;  // 4 column blocks of [64 rows x 128 B]
 constexpr int P_BYTES = BM * BN * 2;     // 1 block of [128 rows x 128 B]
@@ -47,14 +50,17 @@ constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
 constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
 constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-constexpr int NBAR = 17;
-constexpr int SMEM_BYTES = OFF_BAR + NBAR * 8 + 16 + 1024;  // + 1 KB alignment slack
+constexpr int NBAR = 18;
+constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l of the 128 rows
+constexpr int SMEM_BYTES = OFF_INVL + BM * 4 + 1024;  // + 1 KB alignment slack
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL = 0, O_COL = 256;
 constexpr float kRescaleLog2 = 8.0f;  // keep a stale max while p stays below 2^8
 
 enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9,
-           S_EMPTY = 11, P_FULL = 13, PV_DONE = 15 };
+           S_EMPTY = 11, P_FULL = 13, PV_DONE = 15, GATE_FULL = 17 };
+
+HB_DEV void epilogue_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
 
 struct PrefillParams {
   const uint16_t* q;  // gate reads
@@ -68,12 +74,14 @@ struct PrefillParams {
 __global__ void __launch_bounds__(kThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmO, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* inv_l = reinterpret_cast<float*>(smem + OFF_INVL);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_qtiles - 1 - int(blockIdx.x) / p.heads;  // heaviest tiles first
@@ -95,10 +103,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar[P_FULL + s], 128);
       mbar_init(&bar[PV_DONE + s], 1);
     }
+    mbar_init(&bar[GATE_FULL], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == kMmaWarp) tmem_alloc(tmem_slot, TMEM_COLS);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
@@ -112,11 +121,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     return false;
   };
 
-  if (warp == 4) {  // ------------------------------------------ TMA producer
+  if (warp == kTmaWarp) {  // ----------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
+      prefetch_tmap(&tmO);
       mbar_arrive_expect_tx(&bar[Q_FULL], Q_BYTES);
       for (int c = 0; c < 4; ++c)
         tma_load_2d(smem + OFF_Q + c * (BM * 128), &tmQ, &bar[Q_FULL], h * HDIM + c * 64, m0);
@@ -134,8 +144,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(smem + OFF_V + s * KV_BYTES + c * (BN * 128), &tmV, &bar[V_FULL + s], c * 64,
                       j * BN, kvh);
       }
+      // the gate tile [128 rows x 256] goes into the K ring once the last one
+      // or two S products have read it
+      if (p.gate_offset >= 0) {
+        bool free_ring = true;
+        for (int j = ntiles > 2 ? ntiles - 2 : 0; j < ntiles; ++j)
+          free_ring = free_ring && wait(K_EMPTY + (j & 1), (j >> 1) & 1);
+        if (free_ring) {
+          mbar_arrive_expect_tx(&bar[GATE_FULL], Q_BYTES);
+          for (int c = 0; c < 4; ++c)
+            tma_load_2d(smem + OFF_K + c * (BM * 128), &tmQ, &bar[GATE_FULL],
+                        int(p.gate_offset) + h * HDIM + c * 64, m0);
+        }
+      }
     }
-  } else if (warp == 5) {  // ------------------------------------ MMA issuer
+  } else if (warp == kMmaWarp) {  // ------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(BM, BN, false, false);
       constexpr uint32_t idPV = idesc_bf16(BM, HDIM, false, true);
@@ -177,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else {  // ------------------------------------------ softmax + epilogue
+  } else if (warp < 4) {  // -------------------------------------- softmax
     const int row = threadIdx.x;  // 0..127 = TMEM lane
     const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
     const int qpos = p.past + m0 + row;
@@ -253,46 +276,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bar[P_FULL + s]);
       if (!ok) break;
     }
-    // epilogue: O / l -> bf16 -> gate -> global
+    inv_l[row] = l > 0.f ? 1.f / l : 0.f;
+    if (!ok) *abort_flag = 1;
+  }
+
+  if (warp < 8) {  // ------------------------------- epilogue (warps 0-7)
+    epilogue_sync();  // inv_l written
     const int jl = ntiles - 1;
-    ok = __all_sync(0xFFFFFFFFu, ok && wait(PV_DONE + (jl & 1), (jl >> 1) & 1));
+    bool ok = wait(PV_DONE + (jl & 1), (jl >> 1) & 1);
+    if (p.gate_offset >= 0) ok = wait(GATE_FULL, 0) && ok;
+    ok = __all_sync(0xFFFFFFFFu, ok);
     fence_after_sync();
-    const int r = m0 + row;
-    const bool valid = ok && r < p.rows;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint16_t* orow = p.out + int64_t(r) * p.out_row + int64_t(h) * HDIM;
-    const uint16_t* grow = p.q + int64_t(r) * p.q_row + p.gate_offset + int64_t(h) * HDIM;
+    const int qd = warp & 3, hc = warp >> 2;  // TMEM lane quadrant, column half
+    const int rl = qd * 32 + lane;            // row within the tile
+    const uint32_t tq = tmem + (uint32_t(qd * 32) << 16);
+    const float inv = inv_l[rl];
 #pragma unroll 1
-    for (int c = 0; c < HDIM / 32; ++c) {
+    for (int ch = 0; ch < 4; ++ch) {
+      const int col0 = hc * 128 + ch * 32;
       uint32_t o[32];
-      tmem_ld32(tl + O_COL + c * 32, o);
+      tmem_ld32(tq + O_COL + col0, o);
       tmem_wait_ld();
-      if (valid) {
+      const int cb = col0 >> 6, c16 = (col0 & 63) >> 3;
 #pragma unroll
-        for (int g8 = 0; g8 < 4; ++g8) {
-          uint32_t w[4];
-          uint4 gv = make_uint4(0, 0, 0, 0);
-          if (p.gate_offset >= 0) gv = *reinterpret_cast<const uint4*>(grow + c * 32 + g8 * 8);
-          const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      for (int k = 0; k < 4; ++k) {
+        const int phys = cb * (BM * 128) + rl * 128 + (((c16 + k) ^ (rl & 7)) << 4);
+        uint4 gv = make_uint4(0, 0, 0, 0);
+        if (p.gate_offset >= 0) gv = *reinterpret_cast<const uint4*>(smem + OFF_K + phys);
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
+        uint32_t w[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint16_t a0 = f32_to_bf16_cvtne(__uint_as_float(o[g8 * 8 + 2 * i]) * inv);
-            uint16_t a1 = f32_to_bf16_cvtne(__uint_as_float(o[g8 * 8 + 2 * i + 1]) * inv);
-            if (p.gate_offset >= 0) {
-              a0 = gate_bf16(a0, uint16_t(gw[i] & 0xFFFFu));
-              a1 = gate_bf16(a1, uint16_t(gw[i] >> 16));
-            }
-            w[i] = uint32_t(a0) | (uint32_t(a1) << 16);
+        for (int i = 0; i < 4; ++i) {
+          uint16_t a0 = f32_to_bf16_cvtne(__uint_as_float(o[k * 8 + 2 * i]) * inv);
+          uint16_t a1 = f32_to_bf16_cvtne(__uint_as_float(o[k * 8 + 2 * i + 1]) * inv);
+          if (p.gate_offset >= 0) {
+            a0 = gate_bf16(a0, uint16_t(gw[i] & 0xFFFFu));
+            a1 = gate_bf16(a1, uint16_t(gw[i] >> 16));
           }
-          *reinterpret_cast<uint4*>(orow + c * 32 + g8 * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+          w[i] = uint32_t(a0) | (uint32_t(a1) << 16);
         }
+        *reinterpret_cast<uint4*>(smem + OFF_V + phys) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+    }
+    fence_proxy_async_smem();
+    epilogue_sync();  // the output tile is staged
+    if (threadIdx.x == 0 && ok && !*abort_flag) {
+      for (int c = 0; c < 4; ++c)
+        tma_store_2d(&tmO, smem + OFF_V + c * (BM * 128), h * HDIM + c * 64, m0);
+      tma_store_commit();
+      tma_store_wait_read();
     }
   }
 
   fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     fence_after_sync();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -331,15 +369,17 @@ bool encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t*
 bool prefill_serves(int64_t head_dim) { return head_dim == HDIM; }
 
 cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   const cuuint64_t qd[2] = {cuuint64_t(L.q_row), cuuint64_t(L.rows)};
   const cuuint64_t qs[1] = {cuuint64_t(L.q_row) * 2};
   const cuuint32_t qbox[2] = {64, BM};
   const cuuint64_t kd[3] = {cuuint64_t(HDIM), cuuint64_t(L.past + L.rows), cuuint64_t(L.hkv)};
   const cuuint64_t ks[2] = {cuuint64_t(HDIM) * 2, cuuint64_t(L.kv_stride) * 2};
   const cuuint32_t kbox[3] = {64, BN, 1};
+  const cuuint64_t od[2] = {cuuint64_t(L.out_row), cuuint64_t(L.rows)};
+  const cuuint64_t os[1] = {cuuint64_t(L.out_row) * 2};
   if (!encode_bf16(&tq, L.q, 2, qd, qs, qbox) || !encode_bf16(&tk, L.keys, 3, kd, ks, kbox) ||
-      !encode_bf16(&tv, L.values, 3, kd, ks, kbox))
+      !encode_bf16(&tv, L.values, 3, kd, ks, kbox) || !encode_bf16(&to, L.out, 2, od, os, qbox))
     return cudaErrorInvalidValue;
   static DeviceFlags configured;
   cudaError_t e = configured.once([] {
@@ -360,7 +400,7 @@ cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   p.n_qtiles = int((L.rows + BM - 1) / BM);
   p.scale_log2 = L.scale * 1.4426950408889634f;
   p.status = L.status;
-  attn_prefill_kernel<<<unsigned(p.n_qtiles * p.heads), kThreads, SMEM_BYTES, st>>>(tq, tk, tv, p);
+  attn_prefill_kernel<<<unsigned(p.n_qtiles * p.heads), kThreads, SMEM_BYTES, st>>>(tq, tk, tv, to, p);
   return cudaGetLastError();
 }
 

@@ -44,6 +44,20 @@ HB_DEV void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, 
       : "memory");
 }
 
+// Tiled store shared -> global (bulk group); rows/columns outside the
+// tensor are not written.  Coordinates must be >= 0.
+HB_DEV void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+HB_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the committed stores have read their shared-memory source.
+HB_DEV void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until the committed stores are complete.
+HB_DEV void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ------------------------------------------------------------------ TMEM
 
 // One full warp allocates `cols` columns (power of two >= 32); the base
