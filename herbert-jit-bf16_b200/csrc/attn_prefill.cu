@@ -219,13 +219,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bar[S_EMPTY + s]);
       const int kb = j * BN;
       float v[64];
-      float mx = -INFINITY;
+      float m8[8];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        v[c] = (kb + c <= qpos) ? __uint_as_float(ra[c]) * p.scale_log2 : -INFINITY;
-        v[32 + c] = (kb + 32 + c <= qpos) ? __uint_as_float(rb[c]) * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, fmaxf(v[c], v[32 + c]));
+      for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+      if (kb + BN - 1 <= p.past + m0) {  // below the diagonal for every row of the tile
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          v[c] = __uint_as_float(ra[c]) * p.scale_log2;
+          v[32 + c] = __uint_as_float(rb[c]) * p.scale_log2;
+          m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          v[c] = (kb + c <= qpos) ? __uint_as_float(ra[c]) * p.scale_log2 : -INFINITY;
+          v[32 + c] = (kb + 32 + c <= qpos) ? __uint_as_float(rb[c]) * p.scale_log2 : -INFINITY;
+          m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
+        }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float m_new = fmaxf(m, mx);
       float factor = 1.f;
       bool resc = false;
@@ -258,15 +271,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // P_j goes to buffer s, which PV_{j-2} read
       if (j >= 2) ok = __all_sync(0xFFFFFFFFu, wait(PV_DONE + s, ph ^ 1) && ok);
-      float rowsum = 0.f;
+      float s8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
         const float p0 = fast_exp2(v[2 * c] - m), p1 = fast_exp2(v[2 * c + 1] - m);
-        rowsum += p0 + p1;
+        s8[c & 7] += p0 + p1;
         pk[c] = pack_bf16x2(p0, p1);
       }
-      l += rowsum;
+      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       uint8_t* prow = smem + OFF_P + s * P_BYTES + row * 128;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)

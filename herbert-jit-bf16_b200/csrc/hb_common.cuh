@@ -21,12 +21,15 @@ HB_DEV float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // Round to nearest even with the vcvtneps2bf16 special cases the reference's
 // epilogues use: zero and denormal inputs give a signed zero, NaN stays NaN.
+// Written with selects, no branches, so that many elements interleave.
 HB_DEV uint16_t f32_to_bf16_cvtne(float x) {
-  uint32_t u = __float_as_uint(x);
-  uint32_t e = (u >> 23) & 0xFFu;
-  if (e == 0) return uint16_t((u >> 16) & 0x8000u);
-  if (e == 0xFFu) return (u & 0x7FFFFFu) ? uint16_t((u >> 16) | 0x40u) : uint16_t(u >> 16);
-  return uint16_t((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+  const uint32_t u = __float_as_uint(x);
+  const uint32_t ex = u & 0x7F800000u;
+  const uint32_t rounded = (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+  const uint32_t special = (u & 0x7FFFFFu) ? ((u >> 16) | 0x40u) : (u >> 16);
+  uint32_t r = ex == 0x7F800000u ? special : rounded;
+  r = ex == 0u ? ((u >> 16) & 0x8000u) : r;
+  return uint16_t(r);
 }
 
 // The emitted exp polynomial of the reference (src/jit/exp_constants.rs:14-23,
@@ -35,24 +38,26 @@ HB_DEV uint16_t f32_to_bf16_cvtne(float x) {
 // fraction, scale by 2^r built in the exponent field.  Every step rounds as
 // the x86 sequence does.
 HB_DEV float exp_poly(float x) {
-  x = x > -87.33654f ? x : -87.33654f;
+  x = fmaxf(x, -87.33654f);  // vmaxps(x, c): c also when x is NaN, as fmaxf
   float t1 = __fmul_rn(x, 1.442695f);
-  float t2 = rintf(t1);
+  // round t1 to an integer, nearest even (vrndscaleps imm 0), by adding and
+  // removing 1.5 * 2^23; the low bits of the sum hold that integer
+  const float big = __fadd_rn(t1, 12582912.0f);
+  const float t2 = __fsub_rn(big, 12582912.0f);
   t1 = __fsub_rn(t1, t2);
   float p = __fmaf_rn(0.00967248f, t1, 0.05550411f);
   p = __fmaf_rn(p, t1, 0.2402265f);
   p = __fmaf_rn(p, t1, 0.6931472f);
   p = __fmaf_rn(p, t1, 1.0f);
-  int r = int(t2);
-  return __fmul_rn(p, __uint_as_float((uint32_t(r) << 23) + 0x3F800000u));
+  const uint32_t r = uint32_t(__float_as_int(big) - 0x4B400000);
+  return __fmul_rn(p, __uint_as_float((r << 23) + 0x3F800000u));
 }
 
 // The output gate of one element, y = bf16(a / (1 + exp(-b))), with the
 // SigmoidMul arm's steps (src/jit/target/x86/emit_elem.rs:333-420).
 HB_DEV uint16_t gate_bf16(uint16_t a_bits, uint16_t g_bits) {
   float a = bf16_to_f32(a_bits), u = bf16_to_f32(g_bits);
-  float e = __fsub_rn(0.0f, u);
-  e = e < 88.0f ? e : 88.0f;
+  float e = fminf(__fsub_rn(0.0f, u), 88.0f);  // vminps(e, 88): 88 also for NaN
   e = exp_poly(e);
   e = __fadd_rn(e, 1.0f);
   return f32_to_bf16_cvtne(__fdiv_rn(a, e));
