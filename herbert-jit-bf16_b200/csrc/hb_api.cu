@@ -391,17 +391,37 @@ hb_status hb_gdn_decode(const hb_gdn_shape* s, const hb_gdn_call* c, hb_stream_t
   return HB_OK;
 }
 
+// Positions from which the chunked tensor-core kernels take a block; shorter
+// blocks run the recurrence in order.
+static constexpr int64_t kGdnChunkMinRows = 128;
+
+static bool gdn_chunked(const hb_gdn_shape* s, const hb_gdn_call* c) {
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(c->qkv) | reinterpret_cast<uintptr_t>(c->state) |
+                        reinterpret_cast<uintptr_t>(c->output);
+  return gdn_prefill_serves(*s) && c->rows >= kGdnChunkMinRows && (mis & 15) == 0 &&
+         c->rows < (int64_t(1) << 31);
+}
+
 size_t hb_gdn_prefill_workspace_bytes(const hb_gdn_shape* s, int64_t rows) {
-  (void)s;
-  (void)rows;
-  return kWsHeader;
+  if (!s || rows <= 0) return kWsHeader;
+  if (!gdn_prefill_serves(*s)) return kWsHeader;
+  return gdn_prefill_plan(*s, rows).bytes;
 }
 
 hb_status hb_gdn_prefill(const hb_gdn_shape* s, const hb_gdn_call* c, void* ws, size_t ws_bytes,
                          hb_stream_t stream) {
-  (void)ws;
-  (void)ws_bytes;
-  return hb_gdn_decode(s, c, stream);
+  hb_status r = check_gdn(s, c);
+  if (r != HB_OK) return r;
+  if (!gdn_chunked(s, c)) return hb_gdn_decode(s, c, stream);
+  const GdnPrefillPlan pl = gdn_prefill_plan(*s, c->rows);
+  if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
+  GdnLaunch L;
+  L.shape = *s;
+  L.call = *c;
+  L.scale = 1.0f / std::sqrt(float(s->hkd));
+  cudaError_t e = launch_gdn_prefill(L, pl, ws, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill launch");
+  return HB_OK;
 }
 
 }  // extern "C"

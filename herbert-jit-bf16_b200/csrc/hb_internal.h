@@ -82,6 +82,16 @@ struct GdnLaunch {
 bool gdn_decode_serves(const hb_gdn_shape& s);
 cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st);
 
+// chunked prefill: workspace sections (bytes from the workspace start)
+struct GdnPrefillPlan {
+  int64_t nchunks;
+  size_t off_W, off_Qg, off_Kt, off_M, off_U, off_gl, bytes;
+};
+bool gdn_prefill_serves(const hb_gdn_shape& s);
+GdnPrefillPlan gdn_prefill_plan(const hb_gdn_shape& s, int64_t rows);
+cudaError_t launch_gdn_prefill(const GdnLaunch& L, const GdnPrefillPlan& pl, void* ws,
+                               cudaStream_t st);
+
 // Number of SMs of the current device (cached per device).
 int device_sms();
 

@@ -53,3 +53,41 @@ def test_decode_steps_chain(cuda_device):
         outs.append(o)
     assert np.array_equal(np.concatenate(outs).view(np.uint32), full_out.view(np.uint32))
     assert np.array_equal(state.view(np.uint32), full_state.view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,nk,nv,warm", [
+    (4096, 16, 32, False),   # the prefill of the benchmark configuration
+    (200, 2, 4, True),       # partial last chunk, warm state
+    (130, 4, 8, False),
+    (1000, 16, 32, True),
+])
+def test_chunked_prefill_within_tolerance(cuda_device, rows, nk, nv, warm):
+    """The chunk-64 tensor-core prefill reassociates the sums: relative
+    Frobenius error <= 1e-2 on the outputs and the final state."""
+    from harness import GDN_REL_FROB, rel_frob
+    state = (np.random.default_rng(11).standard_normal((nv, 128, 128)).astype(np.float32) * 0.1
+             if warm else None)
+    inp = DeltaInputs(rows, nk=nk, nv=nv, state=state, seed=0x5EED0003 + rows)
+    out, st, ws = gpu_gdn(inp, "prefill")
+    ws.status()
+    ref_out, ref_st = oracle_gdn(inp)
+    assert np.all(np.isfinite(out)) and np.all(np.isfinite(st))
+    eo, es = rel_frob(out, ref_out), rel_frob(st, ref_st)
+    assert eo <= GDN_REL_FROB and es <= GDN_REL_FROB, (eo, es)
+
+
+def test_chunked_prefill_then_decode(cuda_device):
+    """Prefill on the chunked kernels, then exact decode steps from its state."""
+    from harness import GDN_REL_FROB, rel_frob
+    inp = DeltaInputs(512 + 8, nk=2, nv=4)
+    ref_out, ref_st = oracle_gdn(inp)
+    pre = DeltaInputs.__new__(DeltaInputs)
+    pre.__dict__.update(inp.__dict__)
+    pre.rows, pre.qkv, pre.beta, pre.decay = 512, inp.qkv[:512], inp.beta[:512], inp.decay[:512]
+    o1, s1, _ = gpu_gdn(pre, "prefill")
+    dec = DeltaInputs.__new__(DeltaInputs)
+    dec.__dict__.update(inp.__dict__)
+    dec.rows, dec.qkv, dec.beta, dec.decay, dec.state = 8, inp.qkv[512:], inp.beta[512:], inp.decay[512:], s1
+    o2, s2, _ = gpu_gdn(dec, "decode")
+    assert rel_frob(np.concatenate([o1, o2]), ref_out) <= GDN_REL_FROB
+    assert rel_frob(s2, ref_st) <= GDN_REL_FROB
