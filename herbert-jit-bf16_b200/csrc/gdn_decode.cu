@@ -36,9 +36,11 @@ struct GdnParams {
 
 // Sequential L2 of one head held in shared memory: sum of squares left to
 // right, + eps, sqrt, 1/x (delta.rs:28-62).
-HB_DEV float l2_inverse(const float* x, int n, float eps) {
+template <int N>
+HB_DEV float l2_inverse(const float* x, float eps) {
   float sum = 0.f;
-  for (int i = 0; i < n; ++i) sum = __fadd_rn(sum, __fmul_rn(x[i], x[i]));
+#pragma unroll
+  for (int i = 0; i < N; ++i) sum = __fadd_rn(sum, __fmul_rn(x[i], x[i]));
   sum = __fadd_rn(sum, eps);
   return __fdiv_rn(1.0f, __fsqrt_rn(sum));
 }
@@ -68,7 +70,7 @@ __global__ void __launch_bounds__(32) gdn_decode_kernel(const GdnParams p) {
     }
     __syncwarp();
     if (p.l2) {
-      if (lane < 2) inv[lane] = l2_inverse(lane == 0 ? qn : kn, HKD, p.eps);
+      if (lane < 2) inv[lane] = l2_inverse<HKD>(lane == 0 ? qn : kn, p.eps);
       __syncwarp();
       const float iq = inv[0], ik = inv[1];
 #pragma unroll
