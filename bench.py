@@ -40,8 +40,11 @@ GDN_T, GDN_STEPS = 4096, 256
 L2_BYTES = 126 << 20
 
 # dram bytes (read + write) of one launch of the dominant kernel, from the
-# committed ncu summaries under profiles/ (None until captured).
-NCU_TRAFFIC = {"prefill": None, "decode": None, "gdn": None, "batch": None}
+# committed ncu summaries under profiles/: attn_prefill_s4096.md,
+# attn_decode_n2048.md, attn_decode_batch64.md (scaled from the n = 2048
+# capture by the bytes processed), gdn_prefill_decode_t4096.md (scan kernel).
+NCU_TRAFFIC = {"prefill": 93_318_912, "decode": 8_461_824, "gdn": 234_717_440,
+               "batch": 4_458_000_000}
 
 
 def peaks():
