@@ -7,8 +7,13 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
   decode   one decode step, n 2048, same heads, gated                    GB/s
   gdn      GatedDeltaNet: prefill T 4096 then 256 decode steps           tok/s
   batch    batched decode, 64 sequences, L ~ U{1024..32768}              GB/s
+  cp       causal prefill SDPA at S 131072, context parallel over the GPUs
+           (zig-zag shards, K/V ring by NCCL send/recv, LSE merge)      TFLOP/s
 A step is one pass of the path over one batch: one prefill / one decode step /
-one GDN prefill + 256 steps / one decode step of the whole batch.
+one GDN prefill + 256 steps / one decode step of the whole batch / one
+131072-token prefill.  The ring holds NCCL calls, so `cp` steps are issued
+eagerly between the CUDA events instead of from a CUDA graph (a step lasts
+tens of milliseconds; launch costs are microseconds).
 
 `value` is device-timed with CUDA events on the launching stream around one
 CUDA-graph replay of K steps, inputs resident in HBM and rotated over copies
@@ -37,6 +42,7 @@ NK, NV, HKD, HVD = 16, 32, 128, 128
 PREFILL_S = 4096
 DECODE_N = 2048
 GDN_T, GDN_STEPS = 4096, 256
+CP_S = 131072
 L2_BYTES = 126 << 20
 
 # dram bytes (read + write) of one launch of the dominant kernel, from the
@@ -44,7 +50,7 @@ L2_BYTES = 126 << 20
 # attn_decode_n2048.md, attn_decode_batch64.md (scaled from the n = 2048
 # capture by the bytes processed), gdn_prefill_decode_t4096.md (scan kernel).
 NCU_TRAFFIC = {"prefill": 93_318_912, "decode": 8_461_824, "gdn": 234_717_440,
-               "batch": 4_458_000_000}
+               "batch": 4_458_000_000, "cp": None}
 
 
 def peaks():
@@ -150,6 +156,7 @@ class Workload:
     memory, runs the path and copies the result back."""
 
     launches_per_step = 1
+    graphable = True
 
     @staticmethod
     def rotation(bytes_per_set):
@@ -343,9 +350,93 @@ class BatchWorkload(Workload):
                 "kv_heads": HKV, "head_dim": HD, "gate": "sigmoid"}
 
 
+class CpWorkload(Workload):
+    """Config 5: S = 131072 causal prefill, rank r holding the zig-zag shard of
+    chunks r and 2P-1-r (q rows, K and V); one GPU runs the whole sequence
+    through the single-GPU prefill kernel."""
+    graphable = False
+
+    def __init__(self, device, rank=0, world=1, seed=0x5EED0005):
+        import torch
+        import herbert_b200 as hb
+        if CP_S % (2 * world * 128):
+            raise SystemExit(f"cp: {CP_S} tokens do not split into 2x{world} chunks of 128-row tiles")
+        self.hb, self.rank, self.world = hb, rank, world
+        c = CP_S // (2 * world)
+        self.chunk = c
+        self.cp = hb.cp_spec(world, rank, c)
+        gen = torch.Generator(device=device).manual_seed(seed + rank)
+        qd = HQ * HD
+        self.q = _randn_bf16((2 * c, 2 * qd), gen, device)
+        self.kv = _randn_bf16((2, HKV, 2 * c, HD), gen, device)
+        self.out = torch.empty((2 * c, qd), dtype=torch.bfloat16, device=device)
+        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
+        self.comm = hb.CpComm() if world > 1 else None
+        self.side = torch.cuda.Stream(device=device, priority=-1) if world > 1 else None
+        self.ws = None
+        pos = hb.cp_positions(self.cp, rank)
+        self.work = 4 * HQ * HD * sum(p + 1 for p in pos)
+        self.units = "TFLOP/s"
+        self.launches_per_step = world + 1 if world > 1 else 1  # hops + finish
+        self.R = 1
+        self.set_bytes = _nbytes(self.q, self.kv, self.out)
+        self.h_in = [self.q.cpu().pin_memory(), self.kv.cpu().pin_memory()]
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
+
+    def step(self, i=0):
+        self.ws = self.hb.prefill_cp(self.spec, self.cp, self.q, self.kv[0], self.kv[1], self.out,
+                                     kv_stride=2 * self.chunk * HD, capacity=2 * self.chunk,
+                                     comm=self.comm, workspace=self.ws, comm_stream=self.side)
+
+    def e2e_step(self, i=0):
+        self.q.copy_(self.h_in[0], non_blocking=True)
+        self.kv.copy_(self.h_in[1], non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def kernel_probe(self, reps=3):
+        """(algorithmic FLOPs, seconds) of one launch of the dominant kernel, by
+        CUDA events on its stream: the whole-sequence prefill on one GPU, the
+        hop over the rank's own shard (hop 0) on a ring."""
+        import torch
+        st = torch.cuda.current_stream()
+        c = self.chunk
+        if self.world == 1:
+            fn, flops = self.step, self.work
+        else:
+            def fn():
+                self.hb.prefill_cp_hop(self.spec, self.cp, self.q, self.kv[0], self.kv[1],
+                                       self.out, 0, kv_stride=2 * c * HD, capacity=2 * c,
+                                       workspace=self.ws)
+            # chunk r vs r and 2P-1-r vs 2P-1-r (diagonals), 2P-1-r vs r (full)
+            flops = 4 * HQ * HD * (c * (c + 1) + c * c)
+        fn()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(st)
+        for _ in range(reps):
+            fn()
+        b.record(st)
+        torch.cuda.synchronize()
+        return flops, a.elapsed_time(b) / 1e3 / reps
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+
+    def describe(self):
+        return {"workload": "long-context causal prefill SDPA (BASELINE configs[4])",
+                "seq_len": CP_S, "q_heads": HQ, "kv_heads": HKV, "head_dim": HD,
+                "gate": "sigmoid", "chunk": self.chunk}
+
+
 METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
-          "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s"}
-BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm"}
+          "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s"}
+BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor"}
+STRONG = ("batch", "cp")  # total work fixed as the GPUs grow
 
 
 def make_workload(cfg, device, rank, world):
@@ -357,6 +448,8 @@ def make_workload(cfg, device, rank, world):
         return GdnWorkload(device)
     if cfg == "batch":
         return BatchWorkload(device, rank, world)
+    if cfg == "cp":
+        return CpWorkload(device, rank, world)
     raise SystemExit(f"unknown config {cfg}")
 
 
@@ -416,16 +509,33 @@ def run_ours(args):
         torch.cuda.synchronize()
         return a.elapsed_time(b) / 1e3  # seconds for all steps
 
-    g_dev = capture(wl.step, args.steps)
-    g_e2e = capture(wl.e2e_step, args.steps)
+    def timed_eager(fn):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for i in range(args.steps):
+            fn(i)
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / 1e3
+
+    if wl.graphable:
+        g_dev = capture(wl.step, args.steps)
+        g_e2e = capture(wl.e2e_step, args.steps)
+        run_dev, run_e2e = (lambda: timed(g_dev)), (lambda: timed(g_e2e))
+    else:
+        run_dev, run_e2e = (lambda: timed_eager(wl.step)), (lambda: timed_eager(wl.e2e_step))
     barrier()
     sampler = ClockSampler(smi_index(local)).start() if rank == 0 else None
-    t_dev = timed(g_dev)
+    t_dev = run_dev()
     barrier()
     clocks = sampler.stop() if sampler else None
-    t_e2e = timed(g_e2e)
+    t_e2e = run_e2e()
     barrier()
-    del g_dev, g_e2e
+    probe = wl.kernel_probe() if hasattr(wl, "kernel_probe") else None
+    barrier()
+    if wl.graphable:
+        del g_dev, g_e2e
 
     t = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=device)
     work = torch.tensor([float(wl.work)], dtype=torch.float64, device=device)
@@ -442,6 +552,9 @@ def run_ours(args):
         if cfg == "gdn":
             achieved = gdn_prefill_flops(wl.T) / kernel_s / 1e12
             peak, unit = pk["bf16"], "TFLOP/s"
+        elif probe is not None:
+            achieved = probe[0] / probe[1] / 1e12
+            peak, unit = pk["bf16"], "TFLOP/s"
         elif BOUND[cfg] == "tensor":
             achieved = per_launch / kernel_s / 1e12
             peak, unit = pk["bf16"], "TFLOP/s"
@@ -457,15 +570,19 @@ def run_ours(args):
             "warmup": args.warmup,
             "ms_per_step": round(t_dev / args.steps * 1e3, 5),
             "higher_is_better": True,
-            "scaling": "strong" if cfg == "batch" else "weak",
+            "scaling": "strong" if cfg in STRONG else "weak",
             "vs_baseline": None,
             "dtype": "bf16" if cfg != "gdn" else "f32",
             "data": "synthetic",
             "config": dict(wl.describe(), parallelism=(
                 f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
-                else f"{world} independent replicas"),
+                else (f"context parallel over {world} GPUs: zig-zag shards, K/V ring by NCCL "
+                      "send/recv, log-sum-exp merge" if world > 1 else "one GPU, whole sequence")
+                if cfg == "cp" else f"{world} independent replicas"),
                 l2=f"inputs rotate over {wl.R} copies ({wl.R * wl.set_bytes / 2**20:.0f} MiB) per GPU",
-                timing=f"one CUDA graph of {args.steps} steps between CUDA events"),
+                timing=(f"one CUDA graph of {args.steps} steps between CUDA events"
+                        if wl.graphable else
+                        f"{args.steps} steps issued eagerly between CUDA events")),
             "roofline": {"bound": BOUND[cfg], "achieved": round(achieved, 3), "peak": peak,
                          "unit": unit, "frac": round(achieved / peak, 4),
                          "peak_source": pk["source"] + (" burst" if unit == "TFLOP/s" else ""),
@@ -476,9 +593,16 @@ def run_ours(args):
             "gpu_launches": int(wl.launches_per_step * args.steps),
             "clocks": clocks,
         }
+        if probe is not None:
+            line["roofline"]["kernel"] = (
+                "attn_prefill_kernel over the whole sequence" if world == 1 else
+                "attn_prefill_kernel<CP> hop over the rank's own shard (hop 0)")
+            line["roofline"]["launch_ms"] = round(probe[1] * 1e3, 4)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
+    if hasattr(wl, "close"):
+        wl.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -504,13 +628,14 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
     oracle.build()
     threads = threads or _cpu_threads()
     impl = 1 if oracle.has_avx512bf16() else 0
-    if cfg in ("prefill",):
-        rows = 256 if impl else 32
-        past = PREFILL_S - rows
+    if cfg in ("prefill", "cp"):
+        S = PREFILL_S if cfg == "prefill" else CP_S
+        rows = (256 if impl else 32) if cfg == "prefill" else (16 if impl else 2)
+        past = S - rows
         inp = AttentionInputs(rows, past)
         work = prefill_flops(rows, past)
         unit, scale = "TFLOP/s", 1e12
-        sample = f"last {rows} rows of the S={PREFILL_S} prefill (all 16 heads)"
+        sample = f"last {rows} rows of the S={S} prefill (all 16 heads)"
         fn = lambda: oracle.attention(  # noqa: E731
             inp.q.ravel(), inp.keys.ravel(), inp.values.ravel(), rows=rows, past=past,
             heads=HQ, gqa=HQ // HKV, head_dim=HD, q_row=inp.q_row, q_head=HD,
@@ -566,7 +691,7 @@ def run_reference(args):
         "impl": "reference",
         "metric": METRIC[cfg], "value": v, "unit": base["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "scaling": "strong" if cfg == "batch" else "weak", "vs_baseline": None,
+        "scaling": "strong" if cfg in STRONG else "weak", "vs_baseline": None,
         "dtype": "bf16" if cfg != "gdn" else "f32", "data": "synthetic",
         "config": {"workload": cfg, "note": "CPU restatement of the reference's x86 AVX-512 BF16 "
                    "kernels (Rust reference not buildable here)"},

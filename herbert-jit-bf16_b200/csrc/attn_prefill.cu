@@ -26,6 +26,14 @@
 //                output tile leaves by TMA store (staged in the V ring).
 // TMEM: S buffers at columns [0,128), O at [256,512) of a 512-column
 // allocation.  Shared memory: Q 64 KB + K 2x32 KB + V 2x32 KB + P 2x16 KB.
+//
+// Context-parallel hops (template CP = true) run the same pipeline over the
+// K/V shard of one ring position: up to two key segments (a zig-zag shard
+// holds chunks j and 2P-1-j), query rows in up to two segments, the causal
+// mask taken on absolute positions.  Instead of the bf16 epilogue, the CTA
+// merges its unnormalised O and its (m, l) into an f32 accumulator in the
+// workspace (O_acc = O_acc 2^(m_acc - m) + O 2^(m_hop - m), the log-sum-exp
+// merge); a finishing kernel divides by l, rounds and gates.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -51,8 +59,9 @@ constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
 constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
 constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
 constexpr int NBAR = 18;
-constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l of the 128 rows
-constexpr int SMEM_BYTES = OFF_INVL + BM * 4 + 1024;  // + 1 KB alignment slack
+constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l (or the merge weight of O_acc)
+constexpr int OFF_FB = OFF_INVL + BM * 4;           // merge weight of this hop's O
+constexpr int SMEM_BYTES = OFF_FB + BM * 4 + 1024;  // + 1 KB alignment slack
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL = 0, O_COL = 256;
 constexpr float kRescaleLog2 = 8.0f;  // keep a stale max while p stays below 2^8
@@ -66,11 +75,28 @@ struct PrefillParams {
   const uint16_t* q;  // gate reads
   uint16_t* out;
   int64_t q_row, out_row, gate_offset;
-  int rows, past, heads, gqa, n_qtiles;
+  int rows, heads, gqa, n_qtiles;
+  // query rows [0, q_split) sit at positions q_pos0 + row, the others at
+  // q_pos1 + (row - q_split); key segment s holds positions
+  // [seg_pos[s], seg_pos[s] + seg_len[s]) at K/V rows seg_row[s]...
+  int q_split, q_pos0, q_pos1, nseg;
+  int seg_row[2], seg_pos[2], seg_len[2];
   float scale_log2;
   int* status;
+  // context-parallel hops: accumulators [head][q tile][8][32][128] f32 and
+  // [head][q tile][128] (m, l); merge = 0 on the first hop (write only)
+  float* acc_o;
+  float2* acc_ml;
+  int merge;
 };
 
+// Key tiles of segment s that the query rows with positions <= qmax see.
+HB_DEV int segment_tiles(const PrefillParams& p, int s, int qmax) {
+  if (s >= p.nseg || qmax < p.seg_pos[s]) return 0;
+  return (min(p.seg_len[s], qmax - p.seg_pos[s] + 1) + BN - 1) / BN;
+}
+
+template <bool CP>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -82,14 +108,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* inv_l = reinterpret_cast<float*>(smem + OFF_INVL);
+  float* w_hop = reinterpret_cast<float*>(smem + OFF_FB);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_qtiles - 1 - int(blockIdx.x) / p.heads;  // heaviest tiles first
   const int h = int(blockIdx.x) % p.heads;
   const int kvh = h / p.gqa;
   const int m0 = qt * BM;
-  const int n_kv = min(p.past + m0 + BM, p.past + p.rows);
-  const int ntiles = (n_kv + BN - 1) / BN;
+  const int qlo = m0 < p.q_split ? p.q_pos0 + m0 : p.q_pos1 + (m0 - p.q_split);
+  const int qmax = qlo + min(BM, p.rows - m0) - 1;
+  const int n0 = segment_tiles(p, 0, qmax);
+  const int ntiles = n0 + segment_tiles(p, 1, qmax);
+  if (CP && ntiles == 0) return;  // this shard holds no key the tile sees
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[Q_FULL], 1);
@@ -133,20 +163,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < ntiles; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
+        const int kr = j < n0 ? p.seg_row[0] + j * BN : p.seg_row[1] + (j - n0) * BN;
         if (j >= 2 && !wait(K_EMPTY + s, ph ^ 1)) break;
         mbar_arrive_expect_tx(&bar[K_FULL + s], KV_BYTES);
         for (int c = 0; c < 4; ++c)
           tma_load_3d(smem + OFF_K + s * KV_BYTES + c * (BN * 128), &tmK, &bar[K_FULL + s], c * 64,
-                      j * BN, kvh);
+                      kr, kvh);
         if (j >= 2 && !wait(V_EMPTY + s, ph ^ 1)) break;
         mbar_arrive_expect_tx(&bar[V_FULL + s], KV_BYTES);
         for (int c = 0; c < 4; ++c)
           tma_load_3d(smem + OFF_V + s * KV_BYTES + c * (BN * 128), &tmV, &bar[V_FULL + s], c * 64,
-                      j * BN, kvh);
+                      kr, kvh);
       }
       // the gate tile [128 rows x 256] goes into the K ring once the last one
       // or two S products have read it
-      if (p.gate_offset >= 0) {
+      if (!CP && p.gate_offset >= 0) {
         bool free_ring = true;
         for (int j = ntiles > 2 ? ntiles - 2 : 0; j < ntiles; ++j)
           free_ring = free_ring && wait(K_EMPTY + (j & 1), (j >> 1) & 1);
@@ -203,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {  // -------------------------------------- softmax
     const int row = threadIdx.x;  // 0..127 = TMEM lane
     const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
-    const int qpos = p.past + m0 + row;
+    const int qpos = qlo + row;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
@@ -217,12 +248,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       fence_before_sync();
       mbar_arrive(&bar[S_EMPTY + s]);
-      const int kb = j * BN;
+      // key positions kb.. of this tile; keys from klen on lie past the segment
+      const bool s1 = j >= n0;
+      const int t = s1 ? j - n0 : j;
+      const int kb = (s1 ? p.seg_pos[1] : p.seg_pos[0]) + t * BN;
+      const int klen = (s1 ? p.seg_len[1] : p.seg_len[0]) - t * BN;
       float v[64];
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-      if (kb + BN - 1 <= p.past + m0) {  // below the diagonal for every row of the tile
+      if (kb + BN - 1 <= qlo && klen >= BN) {  // below the diagonal for every row of the tile
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           v[c] = __uint_as_float(ra[c]) * p.scale_log2;
@@ -232,8 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          v[c] = (kb + c <= qpos) ? __uint_as_float(ra[c]) * p.scale_log2 : -INFINITY;
-          v[32 + c] = (kb + 32 + c <= qpos) ? __uint_as_float(rb[c]) * p.scale_log2 : -INFINITY;
+          v[c] = (kb + c <= qpos && c < klen) ? __uint_as_float(ra[c]) * p.scale_log2 : -INFINITY;
+          v[32 + c] = (kb + 32 + c <= qpos && 32 + c < klen) ? __uint_as_float(rb[c]) * p.scale_log2
+                                                             : -INFINITY;
           m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
         }
       }
@@ -291,7 +327,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&bar[P_FULL + s]);
       if (!ok) break;
     }
-    inv_l[row] = l > 0.f ? 1.f / l : 0.f;
+    if constexpr (CP) {
+      // log-sum-exp merge of (m, l) with what earlier hops left; O and l of
+      // this hop are relative to m (a max that may be stale by < 2^8)
+      float2* ml = p.acc_ml + (size_t(h) * p.n_qtiles + qt) * BM + row;
+      float wa = 0.f, wb = 1.f, mo = m, lo = l;
+      if (p.merge) {
+        const float2 a = *ml;
+        mo = fmaxf(a.x, m);
+        if (mo == -INFINITY) {
+          wb = 0.f;
+          lo = 0.f;
+        } else {
+          wa = fast_exp2(a.x - mo);
+          wb = fast_exp2(m - mo);
+          lo = a.y * wa + l * wb;
+        }
+      }
+      if (ok) *ml = make_float2(mo, lo);
+      inv_l[row] = wa;
+      w_hop[row] = wb;
+    } else {
+      inv_l[row] = l > 0.f ? 1.f / l : 0.f;
+    }
     if (!ok) *abort_flag = 1;
   }
 
@@ -299,13 +357,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     epilogue_sync();  // inv_l written
     const int jl = ntiles - 1;
     bool ok = wait(PV_DONE + (jl & 1), (jl >> 1) & 1);
-    if (p.gate_offset >= 0) ok = wait(GATE_FULL, 0) && ok;
+    if (!CP && p.gate_offset >= 0) ok = wait(GATE_FULL, 0) && ok;
     ok = __all_sync(0xFFFFFFFFu, ok);
     fence_after_sync();
     const int qd = warp & 3, hc = warp >> 2;  // TMEM lane quadrant, column half
     const int rl = qd * 32 + lane;            // row within the tile
     const uint32_t tq = tmem + (uint32_t(qd * 32) << 16);
     const float inv = inv_l[rl];
+    if constexpr (CP) {
+      // O_acc <- O_acc * wa + O * wb; [32 columns][128 rows] per block, so a
+      // warp's 32 rows are one 128-byte line per column
+      const float wa = inv, wb = w_hop[rl];
+      float* acc = p.acc_o + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM) + rl;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        const int col0 = hc * 128 + ch * 32;
+        uint32_t o[32];
+        tmem_ld32(tq + O_COL + col0, o);
+        tmem_wait_ld();
+        float* ap = acc + size_t(col0) * BM;
+        if (ok && !*abort_flag) {
+          if (p.merge) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              ap[i * BM] = fmaf(ap[i * BM], wa, __uint_as_float(o[i]) * wb);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ap[i * BM] = __uint_as_float(o[i]);
+          }
+        }
+      }
+    } else {
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch) {
       const int col0 = hc * 128 + ch * 32;
@@ -340,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_store_2d(&tmO, smem + OFF_V + c * (BM * 128), h * HDIM + c * 64, m0);
       tma_store_commit();
       tma_store_wait_read();
+    }
     }
   }
 
@@ -385,21 +468,31 @@ bool prefill_serves(int64_t head_dim) { return head_dim == HDIM; }
 
 cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   CUtensorMap tq, tk, tv, to;
+  const int64_t kv_rows = L.cp ? L.kv_rows : L.past + L.rows;
   const cuuint64_t qd[2] = {cuuint64_t(L.q_row), cuuint64_t(L.rows)};
   const cuuint64_t qs[1] = {cuuint64_t(L.q_row) * 2};
   const cuuint32_t qbox[2] = {64, BM};
-  const cuuint64_t kd[3] = {cuuint64_t(HDIM), cuuint64_t(L.past + L.rows), cuuint64_t(L.hkv)};
+  const cuuint64_t kd[3] = {cuuint64_t(HDIM), cuuint64_t(kv_rows), cuuint64_t(L.hkv)};
   const cuuint64_t ks[2] = {cuuint64_t(HDIM) * 2, cuuint64_t(L.kv_stride) * 2};
   const cuuint32_t kbox[3] = {64, BN, 1};
   const cuuint64_t od[2] = {cuuint64_t(L.out_row), cuuint64_t(L.rows)};
   const cuuint64_t os[1] = {cuuint64_t(L.out_row) * 2};
   if (!encode_bf16(&tq, L.q, 2, qd, qs, qbox) || !encode_bf16(&tk, L.keys, 3, kd, ks, kbox) ||
-      !encode_bf16(&tv, L.values, 3, kd, ks, kbox) || !encode_bf16(&to, L.out, 2, od, os, qbox))
+      !encode_bf16(&tv, L.values, 3, kd, ks, kbox))
     return cudaErrorInvalidValue;
+  if (L.cp) {
+    to = tq;  // no output store on a hop
+  } else if (!encode_bf16(&to, L.out, 2, od, os, qbox)) {
+    return cudaErrorInvalidValue;
+  }
   static DeviceFlags configured;
   cudaError_t e = configured.once([] {
-    return cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                SMEM_BYTES);
+    cudaError_t r = cudaFuncSetAttribute(attn_prefill_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(attn_prefill_kernel<true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    return r;
   });
   if (e != cudaSuccess) return e;
   PrefillParams p;
@@ -407,15 +500,114 @@ cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   p.out = L.out;
   p.q_row = L.q_row;
   p.out_row = L.out_row;
-  p.gate_offset = L.gate_offset;
+  p.gate_offset = L.cp ? -1 : L.gate_offset;
   p.rows = int(L.rows);
-  p.past = int(L.past);
   p.heads = int(L.heads);
   p.gqa = int(L.gqa);
   p.n_qtiles = int((L.rows + BM - 1) / BM);
+  if (L.cp) {
+    p.q_split = int(L.q_split);
+    p.q_pos0 = int(L.q_pos0);
+    p.q_pos1 = int(L.q_pos1);
+    p.nseg = L.nseg;
+    for (int s = 0; s < 2; ++s) {
+      p.seg_row[s] = int(L.seg_row[s]);
+      p.seg_pos[s] = int(L.seg_pos[s]);
+      p.seg_len[s] = int(L.seg_len[s]);
+    }
+  } else {  // one segment: keys [0, past + rows), row r at position past + r
+    p.q_split = int(L.rows);
+    p.q_pos0 = int(L.past);
+    p.q_pos1 = 0;
+    p.nseg = 1;
+    p.seg_row[0] = p.seg_pos[0] = 0;
+    p.seg_len[0] = int(L.past + L.rows);
+    p.seg_row[1] = p.seg_pos[1] = p.seg_len[1] = 0;
+  }
   p.scale_log2 = L.scale * 1.4426950408889634f;
   p.status = L.status;
-  attn_prefill_kernel<<<unsigned(p.n_qtiles * p.heads), kThreads, SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+  p.acc_o = L.acc_o;
+  p.acc_ml = reinterpret_cast<float2*>(L.acc_ml);
+  p.merge = L.merge ? 1 : 0;
+  const unsigned grid = unsigned(p.n_qtiles * p.heads);
+  if (L.cp)
+    attn_prefill_kernel<true><<<grid, kThreads, SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+  else
+    attn_prefill_kernel<false><<<grid, kThreads, SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+  return cudaGetLastError();
+}
+
+namespace {
+
+// The last step of a context-parallel prefill: O_acc / l, rounded to bf16
+// and gated exactly as the single-GPU epilogue does, written token-major.
+// CTA = one (q tile, head); 32-column blocks of the accumulator are turned
+// from [column][row] to row-major through shared memory.
+__global__ void __launch_bounds__(256)
+    attn_cp_finish_kernel(const float* __restrict__ acc_o, const float2* __restrict__ acc_ml,
+                          const uint16_t* __restrict__ q, uint16_t* __restrict__ out, int64_t q_row,
+                          int64_t out_row, int64_t gate_offset, int rows, int heads, int n_qtiles) {
+  __shared__ float tile[32][BM + 1];
+  __shared__ float inv_s[BM];
+  const int qt = int(blockIdx.x) / heads, h = int(blockIdx.x) % heads;
+  const size_t unit = size_t(h) * n_qtiles + qt;
+  const float* acc = acc_o + unit * (size_t(HDIM) * BM);
+  const int t = threadIdx.x;
+  if (t < BM) {
+    const float l = acc_ml[unit * BM + t].y;
+    inv_s[t] = l > 0.f ? 1.f / l : 0.f;
+  }
+  const int wr = t >> 1, part = t & 1;  // write phase: row, 16-column half
+  const int rr = t & (BM - 1), ih = t >> 7;  // read phase: row, 16-column half
+  const int64_t grow = int64_t(qt) * BM + wr;
+#pragma unroll 1
+  for (int cc = 0; cc < HDIM / 32; ++cc) {
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      tile[ih * 16 + i][rr] = acc[size_t(cc * 32 + ih * 16 + i) * BM + rr];
+    __syncthreads();
+    if (grow < rows) {
+      const float inv = inv_s[wr];
+      const int col = h * HDIM + cc * 32 + part * 16;
+      uint32_t g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (gate_offset >= 0) {
+        const uint4* gp = reinterpret_cast<const uint4*>(q + grow * q_row + gate_offset + col);
+        const uint4 g0 = gp[0], g1 = gp[1];
+        g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w;
+        g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+      }
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        uint16_t a0 = f32_to_bf16_cvtne(tile[part * 16 + 2 * k][wr] * inv);
+        uint16_t a1 = f32_to_bf16_cvtne(tile[part * 16 + 2 * k + 1][wr] * inv);
+        if (gate_offset >= 0) {
+          a0 = gate_bf16(a0, uint16_t(g[k] & 0xFFFFu));
+          a1 = gate_bf16(a1, uint16_t(g[k] >> 16));
+        }
+        w[k] = uint32_t(a0) | (uint32_t(a1) << 16);
+      }
+      uint4* op = reinterpret_cast<uint4*>(out + grow * out_row + col);
+      op[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      op[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+  }
+}
+
+}  // namespace
+
+size_t cp_acc_bytes(int64_t heads, int64_t rows) {
+  const int64_t nqt = (rows + BM - 1) / BM;
+  return align256(size_t(heads * nqt) * BM * 2 * sizeof(float)) +
+         align256(size_t(heads * nqt) * BM * HDIM * sizeof(float));
+}
+
+cudaError_t launch_attn_cp_finish(const PrefillLaunch& L, cudaStream_t st) {
+  const int nqt = int((L.rows + BM - 1) / BM);
+  attn_cp_finish_kernel<<<unsigned(nqt * L.heads), 256, 0, st>>>(
+      L.acc_o, reinterpret_cast<const float2*>(L.acc_ml), L.q, L.out, L.q_row, L.out_row,
+      L.gate_offset, int(L.rows), int(L.heads), nqt);
   return cudaGetLastError();
 }
 

@@ -23,6 +23,8 @@ namespace {
 
 thread_local char g_err[512] = "";
 
+}  // namespace
+
 hb_status fail(hb_status s, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -84,6 +86,8 @@ hb_status check_call(const hb_attn_spec* s, const hb_attn_call* c) {
   return HB_OK;
 }
 
+namespace {
+
 struct DecodePlan {
   int64_t units;
   int chunk, nsplit;
@@ -107,6 +111,8 @@ DecodePlan plan_decode(const hb_attn_spec* s, int64_t nseq, int64_t rows, int64_
 // Positions summed over the rows of one sequence: row r sees past + r + 1.
 int64_t row_positions(int64_t past, int64_t rows) { return rows * past + rows * (rows + 1) / 2; }
 
+}  // namespace
+
 hb_status check_ws(void* ws, size_t have, size_t need) {
   if (!ws) return fail(HB_ERR_WORKSPACE, "workspace is null (need %zu bytes)", need);
   if (reinterpret_cast<uintptr_t>(ws) & 255)
@@ -114,8 +120,6 @@ hb_status check_ws(void* ws, size_t have, size_t need) {
   if (have < need) return fail(HB_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", have, need);
   return HB_OK;
 }
-
-}  // namespace
 
 int device_sms() {
   static int cache[64] = {0};

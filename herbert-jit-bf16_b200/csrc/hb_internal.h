@@ -66,9 +66,25 @@ struct PrefillLaunch {
   int64_t rows, past, heads, gqa, hkv;
   float scale;
   int* status;
+  // context-parallel hop (cp): query rows [0, q_split) at positions q_pos0..,
+  // the others at q_pos1..; key segment s at K/V rows seg_row[s].. holds
+  // positions [seg_pos[s], seg_pos[s] + seg_len[s]); kv_rows = positions the
+  // K/V buffers hold.  The hop merges into acc_o / acc_ml (merge = false on
+  // the first hop, which writes them).
+  bool cp = false, merge = false;
+  int64_t q_split = 0, q_pos0 = 0, q_pos1 = 0;
+  int nseg = 1;
+  int64_t seg_row[2] = {0, 0}, seg_pos[2] = {0, 0}, seg_len[2] = {0, 0};
+  int64_t kv_rows = 0;
+  float* acc_o = nullptr;
+  float* acc_ml = nullptr;
 };
 bool prefill_serves(int64_t head_dim);
 cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st);
+// Bytes of the (m, l) and O accumulators of a context-parallel prefill over
+// `rows` local query rows (two 256-aligned sections, (m, l) first).
+size_t cp_acc_bytes(int64_t heads, int64_t rows);
+cudaError_t launch_attn_cp_finish(const PrefillLaunch& L, cudaStream_t st);
 
 // ------------------------------------------------------------ kv append
 cudaError_t launch_kv_append(const hb_kv_spec& s, const hb_kv_call& c, cudaStream_t st);
@@ -94,5 +110,14 @@ cudaError_t launch_gdn_prefill(const GdnLaunch& L, const GdnPrefillPlan& pl, voi
 
 // Number of SMs of the current device (cached per device).
 int device_sms();
+
+// Host-side checks and error reporting shared by the API translation units
+// (hb_api.cu): a failure sets the thread-local message of hb_last_error.
+hb_status fail(hb_status s, const char* fmt, ...);
+hb_status cuda_fail(cudaError_t e, const char* what);
+bool aligned16(const void* p);
+hb_status check_spec(const hb_attn_spec* s);
+hb_status check_call(const hb_attn_spec* s, const hb_attn_call* c);
+hb_status check_ws(void* ws, size_t have, size_t need);
 
 }  // namespace hb

@@ -86,6 +86,13 @@ class RecurrenceCall(ctypes.Structure):
                 ("l2", c_int32), ("eps", c_float)]
 
 
+class CpSpec(ctypes.Structure):
+    """hb_cp_spec: a zig-zag sharded sequence of 2*ranks*chunk positions."""
+    _fields_ = [("ranks", c_int32), ("rank", c_int32), ("chunk", c_int64)]
+
+
+HB_CP_ID_BYTES = 128
+
 _P = ctypes.POINTER
 _lib = None
 
@@ -112,6 +119,19 @@ _SIGNATURES = {
     "hb_gdn_prefill_workspace_bytes": (c_size_t, [_P(DeltaShape), c_int64]),
     "hb_gdn_prefill": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceCall), c_void_p, c_size_t,
                                       c_void_p]),
+    "hb_cp_hop_source": (c_int32, [_P(CpSpec), c_int32]),
+    "hb_cp_row_position": (c_int64, [_P(CpSpec), c_int32, c_int64]),
+    "hb_attn_prefill_cp_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(CpSpec)]),
+    "hb_attn_prefill_cp_hop": (ctypes.c_int, [_P(AttentionSpec), _P(CpSpec), _P(AttentionCall),
+                                              c_int32, c_void_p, c_size_t, c_void_p]),
+    "hb_attn_prefill_cp_finish": (ctypes.c_int, [_P(AttentionSpec), _P(CpSpec),
+                                                 _P(AttentionCall), c_void_p, c_size_t,
+                                                 c_void_p]),
+    "hb_cp_comm_unique_id": (ctypes.c_int, [c_void_p]),
+    "hb_cp_comm_init": (ctypes.c_int, [_P(c_void_p), c_int32, c_void_p, c_int32]),
+    "hb_cp_comm_destroy": (ctypes.c_int, [c_void_p]),
+    "hb_attn_prefill_cp": (ctypes.c_int, [_P(AttentionSpec), _P(CpSpec), _P(AttentionCall),
+                                          c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
 }
 
 
@@ -281,4 +301,107 @@ def delta_recurrence(shape: DeltaShape, state, out, qkv, beta, decay, *, rows: i
         workspace.ensure(nbytes, stream)
     check(L.hb_gdn_prefill(ctypes.byref(shape), ctypes.byref(call), c_void_p(workspace.ptr),
                            workspace.nbytes, _stream(stream)))
+    return workspace
+
+
+# ------------------------------------------------- context-parallel prefill
+
+def cp_spec(ranks: int, rank: int, chunk: int) -> CpSpec:
+    return CpSpec(ranks=ranks, rank=rank, chunk=chunk)
+
+
+def cp_hop_source(cp: CpSpec, hop: int) -> int:
+    """Rank whose K/V shard ``cp.rank`` computes at ``hop`` (0 = its own)."""
+    return lib().hb_cp_hop_source(ctypes.byref(cp), hop)
+
+
+def cp_row_position(cp: CpSpec, rank: int, row: int) -> int:
+    """Absolute position of local row ``row`` of ``rank`` (zig-zag shards)."""
+    return lib().hb_cp_row_position(ctypes.byref(cp), rank, row)
+
+
+def cp_positions(cp: CpSpec, rank: int):
+    """The 2*chunk absolute positions of ``rank``'s local rows, in order."""
+    c = cp.chunk
+    a = rank * c
+    b = (2 * cp.ranks - 1 - rank) * c
+    return list(range(a, a + c)) + list(range(b, b + c))
+
+
+def _cp_call(cp, q, keys, values, out, kv_stride, capacity, scale, spec):
+    return AttentionCall(q=_ptr(q), keys=_ptr(keys), values=_ptr(values), output=_ptr(out),
+                         rows=2 * cp.chunk, past=0, kv_stride=kv_stride, capacity=capacity,
+                         scale=(1.0 / spec.head_dim ** 0.5) if scale is None else scale, sink=0.0)
+
+
+def _cp_workspace(spec, cp, workspace, device, stream):
+    nbytes = lib().hb_attn_prefill_cp_workspace_bytes(ctypes.byref(spec), ctypes.byref(cp))
+    if nbytes == 0:
+        raise Decline(HB_DECLINE_GEOMETRY, "context-parallel prefill refuses this geometry")
+    if workspace is None:
+        return Workspace(nbytes, device, stream)
+    return workspace.ensure(nbytes, stream)
+
+
+def prefill_cp_hop(spec: AttentionSpec, cp: CpSpec, q, keys, values, out, hop: int, *,
+                   kv_stride: int, capacity: int = 0, scale: float | None = None,
+                   workspace: Workspace | None = None, stream=None) -> Workspace:
+    """One hop of the ring without transport: ``keys``/``values`` hold the shard of
+    ``cp_hop_source(cp, hop)``; hop 0 first."""
+    call = _cp_call(cp, q, keys, values, out, kv_stride, capacity, scale, spec)
+    workspace = _cp_workspace(spec, cp, workspace, q.device, stream)
+    check(lib().hb_attn_prefill_cp_hop(ctypes.byref(spec), ctypes.byref(cp), ctypes.byref(call),
+                                       hop, c_void_p(workspace.ptr), workspace.nbytes,
+                                       _stream(stream)))
+    return workspace
+
+
+def prefill_cp_finish(spec: AttentionSpec, cp: CpSpec, q, keys, values, out, *, kv_stride: int,
+                      capacity: int = 0, scale: float | None = None,
+                      workspace: Workspace, stream=None) -> None:
+    call = _cp_call(cp, q, keys, values, out, kv_stride, capacity, scale, spec)
+    check(lib().hb_attn_prefill_cp_finish(ctypes.byref(spec), ctypes.byref(cp),
+                                          ctypes.byref(call), c_void_p(workspace.ptr),
+                                          workspace.nbytes, _stream(stream)))
+
+
+class CpComm:
+    """The ring's NCCL communicator over the ranks of a torch.distributed group
+    (one GPU per rank, current before construction)."""
+
+    def __init__(self, group=None):
+        import torch
+        import torch.distributed as dist
+        self.ranks = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        uid = ctypes.create_string_buffer(HB_CP_ID_BYTES)
+        if self.rank == 0:
+            check(lib().hb_cp_comm_unique_id(uid))
+        obj = [bytes(uid.raw) if self.rank == 0 else None]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group else 0,
+                                   group=group)
+        uid = ctypes.create_string_buffer(obj[0], HB_CP_ID_BYTES)
+        handle = c_void_p()
+        torch.cuda.synchronize()
+        check(lib().hb_cp_comm_init(ctypes.byref(handle), self.ranks, uid, self.rank))
+        self.handle = handle
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            check(lib().hb_cp_comm_destroy(self.handle))
+        self.handle = None
+
+
+def prefill_cp(spec: AttentionSpec, cp: CpSpec, q, keys, values, out, *, kv_stride: int,
+               capacity: int = 0, scale: float | None = None, comm: CpComm | None = None,
+               workspace: Workspace | None = None, stream=None, comm_stream=None) -> Workspace:
+    """The whole ring (every rank calls it): P hops with the shards moving by NCCL
+    send/recv on ``comm_stream``, then the bf16 gated output of the local rows."""
+    call = _cp_call(cp, q, keys, values, out, kv_stride, capacity, scale, spec)
+    workspace = _cp_workspace(spec, cp, workspace, q.device, stream)
+    handle = comm.handle if comm is not None else None
+    cs = c_void_p(comm_stream.cuda_stream) if comm_stream is not None else None
+    check(lib().hb_attn_prefill_cp(ctypes.byref(spec), ctypes.byref(cp), ctypes.byref(call),
+                                   handle, c_void_p(workspace.ptr), workspace.nbytes,
+                                   _stream(stream), cs))
     return workspace

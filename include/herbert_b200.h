@@ -177,6 +177,67 @@ HB_API size_t hb_attn_prefill_workspace_bytes(const hb_attn_spec *spec, const hb
 HB_API hb_status hb_attn_prefill(const hb_attn_spec *spec, const hb_attn_call *call,
                           void *workspace, size_t workspace_bytes, hb_stream_t stream);
 
+/*
+ * Context-parallel causal prefill over a ring of P GPUs.  No counterpart in
+ * the reference (its prefill runs on one machine's cores through the same
+ * tile selector, src/jit/target/x86/execution/attention.rs:56-224); it
+ * extends hb_attn_prefill (past = 0) to a sequence of 2*P*chunk tokens
+ * sharded zig-zag: rank r holds the query rows, keys and values of chunks r
+ * and 2P-1-r (absolute positions r*chunk.. and (2P-1-r)*chunk..) as its
+ * local rows [0, chunk) and [chunk, 2*chunk), in the reference's layouts
+ * (call->rows = 2*chunk, call->past = 0, K/V [kv_head][kv_stride]).  K/V
+ * shards travel the ring (rank r sends to r+1 and receives from r-1) by
+ * NCCL send/recv on `comm_stream` while the previous shard is computed on
+ * `stream`; the partial results of each hop are merged by log-sum-exp into
+ * an f32 accumulator in the workspace, and the last step divides, rounds to
+ * bf16 and applies the output gate as hb_attn_prefill does.
+ */
+typedef struct hb_cp_spec {
+    int32_t ranks;  /* P >= 1                                     */
+    int32_t rank;   /* this GPU's place on the ring, 0 <= rank < P */
+    int64_t chunk;  /* positions per chunk, a multiple of 128     */
+} hb_cp_spec;
+
+/* Ring schedule (host only): the rank whose K/V shard `cp->rank` computes
+ * at hop `hop` (hop 0 = its own), or -1; the absolute position of local row
+ * `row` of rank `rank`, or -1. */
+HB_API int32_t hb_cp_hop_source(const hb_cp_spec *cp, int32_t hop);
+HB_API int64_t hb_cp_row_position(const hb_cp_spec *cp, int32_t rank, int64_t row);
+
+/* Workspace of hb_attn_prefill_cp and of the hop/finish pair below: header,
+ * (m, l) and O accumulators of the 2*chunk local rows, and for P > 1 two
+ * K/V receive buffers. */
+HB_API size_t hb_attn_prefill_cp_workspace_bytes(const hb_attn_spec *spec, const hb_cp_spec *cp);
+
+/* One hop without transport, for callers that move the shards themselves:
+ * call->keys/values hold the shard of rank hb_cp_hop_source(cp, hop) in the
+ * shard layout above; hop 0 must run first on a workspace (it writes the
+ * accumulators, later hops merge into them).  hb_attn_prefill_cp_finish
+ * then writes call->output. */
+HB_API hb_status hb_attn_prefill_cp_hop(const hb_attn_spec *spec, const hb_cp_spec *cp,
+                                 const hb_attn_call *call, int32_t hop, void *workspace,
+                                 size_t workspace_bytes, hb_stream_t stream);
+HB_API hb_status hb_attn_prefill_cp_finish(const hb_attn_spec *spec, const hb_cp_spec *cp,
+                                    const hb_attn_call *call, void *workspace,
+                                    size_t workspace_bytes, hb_stream_t stream);
+
+/* NCCL communicator of the ring.  NCCL is loaded on first use (the copy
+ * already in the process if there is one, else libnccl.so.2); the library
+ * itself does not depend on it.  `id` is HB_CP_ID_BYTES bytes made by one
+ * rank with hb_cp_comm_unique_id and given to every rank; hb_cp_comm_init is
+ * collective over the P ranks, each with its own GPU current. */
+#define HB_CP_ID_BYTES 128
+HB_API hb_status hb_cp_comm_unique_id(void *id);
+HB_API hb_status hb_cp_comm_init(void **comm, int32_t ranks, const void *id, int32_t rank);
+HB_API hb_status hb_cp_comm_destroy(void *comm);
+
+/* The whole ring: P hops and the finishing step.  Every rank calls it with
+ * the same chunk; `comm` comes from hb_cp_comm_init (unused when P = 1).
+ * On return all work, transfers included, is ordered on `stream`. */
+HB_API hb_status hb_attn_prefill_cp(const hb_attn_spec *spec, const hb_cp_spec *cp,
+                             const hb_attn_call *call, void *comm, void *workspace,
+                             size_t workspace_bytes, hb_stream_t stream, hb_stream_t comm_stream);
+
 /* KV cache geometry: KvSpec (src/jit/execution/abi.rs:57-104). */
 typedef struct hb_kv_spec {
     int64_t heads;      /* KV heads                        */
