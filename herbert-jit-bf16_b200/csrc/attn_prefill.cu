@@ -60,8 +60,10 @@ constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
 constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
 constexpr int NBAR = 18;
 constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l (or the merge weight of O_acc)
-constexpr int OFF_FB = OFF_INVL + BM * 4;           // merge weight of this hop's O
-constexpr int SMEM_BYTES = OFF_FB + BM * 4 + 1024;  // + 1 KB alignment slack
+constexpr int SMEM_BYTES = OFF_INVL + BM * 4 + 1024;  // + 1 KB alignment slack
+// merge weight of a CP hop's O: in the K ring, which no MMA reads once the
+// softmax has seen the last S (a hop loads no gate tile there)
+constexpr int OFF_FB = OFF_K;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t S_COL = 0, O_COL = 256;
 constexpr float kRescaleLog2 = 8.0f;  // keep a stale max while p stays below 2^8
@@ -71,29 +73,30 @@ enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL 
 
 HB_DEV void epilogue_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
 
+// Kept at 104 bytes: with the tensor maps, a larger parameter block made
+// the same kernel ~5% slower on B200 (measured).
 struct PrefillParams {
   const uint16_t* q;  // gate reads
   uint16_t* out;
   int64_t q_row, out_row, gate_offset;
   int rows, heads, gqa, n_qtiles;
-  // query rows [0, q_split) sit at positions q_pos0 + row, the others at
-  // q_pos1 + (row - q_split); key segment s holds positions
-  // [seg_pos[s], seg_pos[s] + seg_len[s]) at K/V rows seg_row[s]...
-  int q_split, q_pos0, q_pos1, nseg;
-  int seg_row[2], seg_pos[2], seg_len[2];
+  int q_pos0;  // position of row 0 (= past); on a CP hop, of the first chunk's row 0
   float scale_log2;
   int* status;
-  // context-parallel hops: accumulators [head][q tile][8][32][128] f32 and
-  // [head][q tile][128] (m, l); merge = 0 on the first hop (write only)
-  float* acc_o;
-  float2* acc_ml;
-  int merge;
+  // context-parallel hop: rows [0, chunk) sit at positions q_pos0.., rows
+  // [chunk, 2 chunk) at q_pos1..; the shard's K/V rows [0, chunk) hold
+  // positions kpos0.., rows [chunk, 2 chunk) positions kpos1..
+  int chunk, q_pos1, kpos0, kpos1;
+  int merge;  // 0 on the first hop (write the accumulators only)
+  // [head][q tile][256 columns][128 rows] f32 O, then [head][q tile][128] (m, l)
+  float* acc;
 };
 
-// Key tiles of segment s that the query rows with positions <= qmax see.
+// Key tiles of a CP hop's segment s that query rows at positions <= qmax see.
 HB_DEV int segment_tiles(const PrefillParams& p, int s, int qmax) {
-  if (s >= p.nseg || qmax < p.seg_pos[s]) return 0;
-  return (min(p.seg_len[s], qmax - p.seg_pos[s] + 1) + BN - 1) / BN;
+  const int pos = s ? p.kpos1 : p.kpos0;
+  if (qmax < pos) return 0;
+  return (min(p.chunk, qmax - pos + 1) + BN - 1) / BN;
 }
 
 template <bool CP>
@@ -115,10 +118,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h = int(blockIdx.x) % p.heads;
   const int kvh = h / p.gqa;
   const int m0 = qt * BM;
-  const int qlo = m0 < p.q_split ? p.q_pos0 + m0 : p.q_pos1 + (m0 - p.q_split);
-  const int qmax = qlo + min(BM, p.rows - m0) - 1;
-  const int n0 = segment_tiles(p, 0, qmax);
-  const int ntiles = n0 + segment_tiles(p, 1, qmax);
+  int qlo, n0, ntiles;  // position of row 0, key tiles of segment 0 and in all
+  if constexpr (CP) {
+    qlo = m0 < p.chunk ? p.q_pos0 + m0 : p.q_pos1 + (m0 - p.chunk);
+    const int qmax = qlo + min(BM, p.rows - m0) - 1;
+    n0 = segment_tiles(p, 0, qmax);
+    ntiles = n0 + segment_tiles(p, 1, qmax);
+  } else {  // row r at position past + r (= q_pos0 + r) sees keys [0, past + r]
+    qlo = p.q_pos0 + m0;
+    n0 = ntiles = (min(qlo + BM, p.q_pos0 + p.rows) + BN - 1) / BN;
+  }
   if (CP && ntiles == 0) return;  // this shard holds no key the tile sees
 
   if (threadIdx.x == 0) {
@@ -163,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < ntiles; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        const int kr = j < n0 ? p.seg_row[0] + j * BN : p.seg_row[1] + (j - n0) * BN;
+        const int kr = !CP ? j * BN : j < n0 ? j * BN : p.chunk + (j - n0) * BN;
         if (j >= 2 && !wait(K_EMPTY + s, ph ^ 1)) break;
         mbar_arrive_expect_tx(&bar[K_FULL + s], KV_BYTES);
         for (int c = 0; c < 4; ++c)
@@ -248,16 +257,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_ld();
       fence_before_sync();
       mbar_arrive(&bar[S_EMPTY + s]);
-      // key positions kb.. of this tile; keys from klen on lie past the segment
-      const bool s1 = j >= n0;
-      const int t = s1 ? j - n0 : j;
-      const int kb = (s1 ? p.seg_pos[1] : p.seg_pos[0]) + t * BN;
-      const int klen = (s1 ? p.seg_len[1] : p.seg_len[0]) - t * BN;
+      // key positions kb.. of this tile; keys from klen on lie past the
+      // segment (one segment starting at position 0 outside CP hops)
+      int kb = j * BN, klen = BN;
+      if constexpr (CP) {
+        const bool s1 = j >= n0;
+        const int t = s1 ? j - n0 : j;
+        kb = (s1 ? p.kpos1 : p.kpos0) + t * BN;
+        klen = p.chunk - t * BN;
+      }
       float v[64];
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-      if (kb + BN - 1 <= qlo && klen >= BN) {  // below the diagonal for every row of the tile
+      if (kb + BN - 1 <= qlo && (!CP || klen >= BN)) {  // below the diagonal for every row
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
           v[c] = __uint_as_float(ra[c]) * p.scale_log2;
@@ -267,9 +280,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          v[c] = (kb + c <= qpos && c < klen) ? __uint_as_float(ra[c]) * p.scale_log2 : -INFINITY;
-          v[32 + c] = (kb + 32 + c <= qpos && 32 + c < klen) ? __uint_as_float(rb[c]) * p.scale_log2
-                                                             : -INFINITY;
+          v[c] = (kb + c <= qpos && (!CP || c < klen)) ? __uint_as_float(ra[c]) * p.scale_log2
+                                                       : -INFINITY;
+          v[32 + c] = (kb + 32 + c <= qpos && (!CP || 32 + c < klen))
+                          ? __uint_as_float(rb[c]) * p.scale_log2
+                          : -INFINITY;
           m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
         }
       }
@@ -330,7 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (CP) {
       // log-sum-exp merge of (m, l) with what earlier hops left; O and l of
       // this hop are relative to m (a max that may be stale by < 2^8)
-      float2* ml = p.acc_ml + (size_t(h) * p.n_qtiles + qt) * BM + row;
+      const size_t units = size_t(p.heads) * p.n_qtiles;
+      float2* ml = reinterpret_cast<float2*>(p.acc + units * (size_t(HDIM) * BM)) +
+                   (size_t(h) * p.n_qtiles + qt) * BM + row;
       float wa = 0.f, wb = 1.f, mo = m, lo = l;
       if (p.merge) {
         const float2 a = *ml;
@@ -354,6 +371,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (warp < 8) {  // ------------------------------- epilogue (warps 0-7)
+    if (CP && p.merge && warp >= 4) {
+      // warps 4-7 idle through the main loop: bring this tile's accumulator
+      // (128 KB, 1024 lines) into L2 so the merge below reads it from there
+      const char* a = reinterpret_cast<const char*>(
+          p.acc + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM));
+      for (int ln = threadIdx.x - 128; ln < HDIM * BM * 4 / 128; ln += 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a + size_t(ln) * 128));
+    }
     epilogue_sync();  // inv_l written
     const int jl = ntiles - 1;
     bool ok = wait(PV_DONE + (jl & 1), (jl >> 1) & 1);
@@ -368,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O_acc <- O_acc * wa + O * wb; [32 columns][128 rows] per block, so a
       // warp's 32 rows are one 128-byte line per column
       const float wa = inv, wb = w_hop[rl];
-      float* acc = p.acc_o + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM) + rl;
+      float* acc = p.acc + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM) + rl;
 #pragma unroll 1
       for (int ch = 0; ch < 4; ++ch) {
         const int col0 = hc * 128 + ch * 32;
@@ -378,9 +403,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* ap = acc + size_t(col0) * BM;
         if (ok && !*abort_flag) {
           if (p.merge) {
+            float a[32];  // every load in flight before the first store
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              ap[i * BM] = fmaf(ap[i * BM], wa, __uint_as_float(o[i]) * wb);
+            for (int i = 0; i < 32; ++i) a[i] = ap[i * BM];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ap[i * BM] = fmaf(a[i], wa, __uint_as_float(o[i]) * wb);
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) ap[i * BM] = __uint_as_float(o[i]);
@@ -505,29 +532,14 @@ cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   p.heads = int(L.heads);
   p.gqa = int(L.gqa);
   p.n_qtiles = int((L.rows + BM - 1) / BM);
-  if (L.cp) {
-    p.q_split = int(L.q_split);
-    p.q_pos0 = int(L.q_pos0);
-    p.q_pos1 = int(L.q_pos1);
-    p.nseg = L.nseg;
-    for (int s = 0; s < 2; ++s) {
-      p.seg_row[s] = int(L.seg_row[s]);
-      p.seg_pos[s] = int(L.seg_pos[s]);
-      p.seg_len[s] = int(L.seg_len[s]);
-    }
-  } else {  // one segment: keys [0, past + rows), row r at position past + r
-    p.q_split = int(L.rows);
-    p.q_pos0 = int(L.past);
-    p.q_pos1 = 0;
-    p.nseg = 1;
-    p.seg_row[0] = p.seg_pos[0] = 0;
-    p.seg_len[0] = int(L.past + L.rows);
-    p.seg_row[1] = p.seg_pos[1] = p.seg_len[1] = 0;
-  }
+  p.q_pos0 = int(L.cp ? L.q_pos0 : L.past);
+  p.chunk = int(L.chunk);
+  p.q_pos1 = int(L.q_pos1);
+  p.kpos0 = int(L.kpos[0]);
+  p.kpos1 = int(L.kpos[1]);
   p.scale_log2 = L.scale * 1.4426950408889634f;
   p.status = L.status;
-  p.acc_o = L.acc_o;
-  p.acc_ml = reinterpret_cast<float2*>(L.acc_ml);
+  p.acc = L.acc;
   p.merge = L.merge ? 1 : 0;
   const unsigned grid = unsigned(p.n_qtiles * p.heads);
   if (L.cp)
@@ -544,14 +556,15 @@ namespace {
 // CTA = one (q tile, head); 32-column blocks of the accumulator are turned
 // from [column][row] to row-major through shared memory.
 __global__ void __launch_bounds__(256)
-    attn_cp_finish_kernel(const float* __restrict__ acc_o, const float2* __restrict__ acc_ml,
-                          const uint16_t* __restrict__ q, uint16_t* __restrict__ out, int64_t q_row,
+    attn_cp_finish_kernel(const float* __restrict__ acc_o, const uint16_t* __restrict__ q, uint16_t* __restrict__ out, int64_t q_row,
                           int64_t out_row, int64_t gate_offset, int rows, int heads, int n_qtiles) {
   __shared__ float tile[32][BM + 1];
   __shared__ float inv_s[BM];
   const int qt = int(blockIdx.x) / heads, h = int(blockIdx.x) % heads;
   const size_t unit = size_t(h) * n_qtiles + qt;
   const float* acc = acc_o + unit * (size_t(HDIM) * BM);
+  const float2* acc_ml =
+      reinterpret_cast<const float2*>(acc_o + size_t(heads) * n_qtiles * (size_t(HDIM) * BM));
   const int t = threadIdx.x;
   if (t < BM) {
     const float l = acc_ml[unit * BM + t].y;
@@ -599,14 +612,13 @@ __global__ void __launch_bounds__(256)
 
 size_t cp_acc_bytes(int64_t heads, int64_t rows) {
   const int64_t nqt = (rows + BM - 1) / BM;
-  return align256(size_t(heads * nqt) * BM * 2 * sizeof(float)) +
-         align256(size_t(heads * nqt) * BM * HDIM * sizeof(float));
+  return size_t(heads * nqt) * BM * (HDIM + 2) * sizeof(float);
 }
 
 cudaError_t launch_attn_cp_finish(const PrefillLaunch& L, cudaStream_t st) {
   const int nqt = int((L.rows + BM - 1) / BM);
   attn_cp_finish_kernel<<<unsigned(nqt * L.heads), 256, 0, st>>>(
-      L.acc_o, reinterpret_cast<const float2*>(L.acc_ml), L.q, L.out, L.q_row, L.out_row,
+      L.acc, L.q, L.out, L.q_row, L.out_row,
       L.gate_offset, int(L.rows), int(L.heads), nqt);
   return cudaGetLastError();
 }

@@ -150,20 +150,13 @@ PrefillLaunch hop_launch(const hb_attn_spec* s, const hb_cp_spec* cp, const hb_a
   L.status = reinterpret_cast<int*>(base);
   L.cp = true;
   L.merge = hop > 0;
-  L.q_split = cp->chunk;
+  L.chunk = cp->chunk;
   L.q_pos0 = chunk_position(cp, cp->rank, 0);
   L.q_pos1 = chunk_position(cp, cp->rank, 1);
-  L.nseg = 2;
-  for (int k = 0; k < 2; ++k) {
-    L.seg_row[k] = k * cp->chunk;
-    L.seg_pos[k] = chunk_position(cp, src, k);
-    L.seg_len[k] = cp->chunk;
-  }
+  L.kpos[0] = chunk_position(cp, src, 0);
+  L.kpos[1] = chunk_position(cp, src, 1);
   L.kv_rows = 2 * cp->chunk;
-  L.acc_ml = reinterpret_cast<float*>(base + pl.acc_off);
-  const size_t ml_bytes = align256(size_t(s->heads) * size_t((c->rows + kCpTile - 1) / kCpTile) *
-                                   kCpTile * 2 * sizeof(float));
-  L.acc_o = reinterpret_cast<float*>(base + pl.acc_off + ml_bytes);
+  L.acc = reinterpret_cast<float*>(base + pl.acc_off);
   return L;
 }
 

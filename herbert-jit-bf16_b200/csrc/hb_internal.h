@@ -66,23 +66,21 @@ struct PrefillLaunch {
   int64_t rows, past, heads, gqa, hkv;
   float scale;
   int* status;
-  // context-parallel hop (cp): query rows [0, q_split) at positions q_pos0..,
-  // the others at q_pos1..; key segment s at K/V rows seg_row[s].. holds
-  // positions [seg_pos[s], seg_pos[s] + seg_len[s]); kv_rows = positions the
-  // K/V buffers hold.  The hop merges into acc_o / acc_ml (merge = false on
-  // the first hop, which writes them).
+  // context-parallel hop (cp): query rows [0, chunk) at positions q_pos0..,
+  // rows [chunk, 2 chunk) at q_pos1..; the hop's K/V rows [0, chunk) hold
+  // positions kpos[0].., rows [chunk, 2 chunk) kpos[1]..; kv_rows =
+  // positions the K/V buffers hold.  The hop merges into the accumulators
+  // at acc (cp_acc_bytes; merge = false on the first hop, which writes them).
   bool cp = false, merge = false;
-  int64_t q_split = 0, q_pos0 = 0, q_pos1 = 0;
-  int nseg = 1;
-  int64_t seg_row[2] = {0, 0}, seg_pos[2] = {0, 0}, seg_len[2] = {0, 0};
+  int64_t chunk = 0, q_pos0 = 0, q_pos1 = 0;
+  int64_t kpos[2] = {0, 0};
   int64_t kv_rows = 0;
-  float* acc_o = nullptr;
-  float* acc_ml = nullptr;
+  float* acc = nullptr;
 };
 bool prefill_serves(int64_t head_dim);
 cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st);
-// Bytes of the (m, l) and O accumulators of a context-parallel prefill over
-// `rows` local query rows (two 256-aligned sections, (m, l) first).
+// Bytes of the O and (m, l) accumulators of a context-parallel prefill over
+// `rows` local query rows (O first, then (m, l)).
 size_t cp_acc_bytes(int64_t heads, int64_t rows);
 cudaError_t launch_attn_cp_finish(const PrefillLaunch& L, cudaStream_t st);
 
