@@ -13,11 +13,20 @@
 // __fadd_rn): the outputs and the state are the reference's bits.  Grid =
 // (value heads, hvd/32), one warp per CTA; the state crosses HBM once per
 // call however many positions the call carries.
+//
+// The CTA's state slice [hkd rows][32 columns] f32 moves as one TMA tile
+// each way (shared memory in between): with one warp per SM, per-thread
+// loads of 128 strided rows left the step latency-bound on memory
+// parallelism (a loads-and-stores-only kernel took 9 us per step, the TMA
+// tile takes one request).  The L2 norms of q and k run while the tile is
+// in flight.
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "hb_common.cuh"
 #include "hb_internal.h"
+#include "hb_sm100.cuh"
 
 namespace hb {
 namespace {
@@ -38,75 +47,139 @@ struct GdnParams {
 // right, + eps, sqrt, 1/x (delta.rs:28-62).
 template <int N>
 HB_DEV float l2_inverse(const float* x, float eps) {
+  const float4* x4 = reinterpret_cast<const float4*>(x);
   float sum = 0.f;
 #pragma unroll
-  for (int i = 0; i < N; ++i) sum = __fadd_rn(sum, __fmul_rn(x[i], x[i]));
+  for (int i = 0; i < N / 4; ++i) {
+    const float4 v = x4[i];
+    sum = __fadd_rn(sum, __fmul_rn(v.x, v.x));
+    sum = __fadd_rn(sum, __fmul_rn(v.y, v.y));
+    sum = __fadd_rn(sum, __fmul_rn(v.z, v.z));
+    sum = __fadd_rn(sum, __fmul_rn(v.w, v.w));
+  }
   sum = __fadd_rn(sum, eps);
   return __fdiv_rn(1.0f, __fsqrt_rn(sum));
 }
 
+// Set when a TMA wait of the decode kernel ran out (the call's outputs are
+// then not written); there is no workspace to carry a per-call status.
+__device__ int g_gdn_decode_timeout = 0;
+
 template <int HKD>
-__global__ void __launch_bounds__(32) gdn_decode_kernel(const GdnParams p) {
+__global__ void __launch_bounds__(32)
+    gdn_decode_kernel(const __grid_constant__ CUtensorMap tmS, const GdnParams p) {
+  __shared__ __align__(128) float st[HKD * 32];  // state rows kd, columns col0..col0+31
   __shared__ __align__(16) float qn[HKD];
   __shared__ __align__(16) float kn[HKD];
   __shared__ float inv[2];
+  __shared__ __align__(8) uint64_t bar;
   const int h = blockIdx.x, lane = threadIdx.x;
-  const int col = blockIdx.y * 32 + lane;
+  const int col0 = blockIdx.y * 32, col = col0 + lane;
   const int kh = h / (p.nv / p.nk);
   const int64_t key = int64_t(p.nk) * HKD, value = int64_t(p.nv) * p.hvd;
   const int64_t conv = 2 * key + value;
 
-  float* sp = p.state + int64_t(h) * HKD * p.hvd + col;
+  if (lane == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  // launched with programmatic stream serialization: everything above may
+  // overlap the previous kernel on the stream; nothing below reads memory
+  // before that kernel has completed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" :::);
+  if (lane == 0) {
+    mbar_arrive_expect_tx(&bar, HKD * 32 * 4);
+    sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
+  }
+  bool loaded = false;
   float s[HKD];
-#pragma unroll
-  for (int kd = 0; kd < HKD; ++kd) s[kd] = sp[int64_t(kd) * p.hvd];
 
   for (int64_t t = 0; t < p.rows; ++t) {
     const float* row = p.qkv + t * conv;
+    // every load of the position first, so their latencies overlap
+    const float beta = p.beta[t * p.nv + h];
+    const float decay = p.decay[t * p.nv + h];
+    const float v = row[2 * key + int64_t(h) * p.hvd + col];
 #pragma unroll
     for (int i = lane; i < HKD; i += 32) {
       qn[i] = row[int64_t(kh) * HKD + i];
       kn[i] = row[key + int64_t(kh) * HKD + i];
     }
     __syncwarp();
+    // qn <- q * inv_q * scale (the reference scales q inside pass 2, per
+    // element, after the L2 step: the same two roundings), kn <- k * inv_k
+    float iq = 1.f, ik = 1.f;
     if (p.l2) {
       if (lane < 2) inv[lane] = l2_inverse<HKD>(lane == 0 ? qn : kn, p.eps);
       __syncwarp();
-      const float iq = inv[0], ik = inv[1];
-#pragma unroll
-      for (int i = lane; i < HKD; i += 32) {
-        qn[i] = __fmul_rn(qn[i], iq);
-        kn[i] = __fmul_rn(kn[i], ik);
-      }
-      __syncwarp();
+      iq = inv[0];
+      ik = inv[1];
     }
-    const float beta = p.beta[t * p.nv + h];
-    const float decay = p.decay[t * p.nv + h];
-    const float v = row[2 * key + int64_t(h) * p.hvd + col];
+#pragma unroll
+    for (int i = lane; i < HKD; i += 32) {
+      const float qv = p.l2 ? __fmul_rn(qn[i], iq) : qn[i];
+      qn[i] = __fmul_rn(qv, p.scale);
+      if (p.l2) kn[i] = __fmul_rn(kn[i], ik);
+    }
+    __syncwarp();
+    if (!loaded) {  // the state tile (first position only)
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar, 0))) {
+        if (lane == 0) atomicExch(&g_gdn_decode_timeout, 1);
+        mbar_wait(&bar, 0);  // a second bounded wait for the copy in flight
+        return;
+      }
+#pragma unroll
+      for (int kd = 0; kd < HKD; ++kd) s[kd] = st[kd * 32 + lane];
+      loaded = true;
+    }
 
+    const float4* k4 = reinterpret_cast<const float4*>(kn);
+    const float4* q4 = reinterpret_cast<const float4*>(qn);
     // pass 1: decay, then read kv = S^T k
     float kv = 0.f;
 #pragma unroll
-    for (int kd = 0; kd < HKD; ++kd) {
-      const float r = __fmul_rn(s[kd], decay);
-      s[kd] = r;
-      kv = __fadd_rn(kv, __fmul_rn(r, kn[kd]));
+    for (int k = 0; k < HKD / 4; ++k) {
+      const float4 kk = k4[k];
+      const float kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float r = __fmul_rn(s[4 * k + e], decay);
+        s[4 * k + e] = r;
+        kv = __fadd_rn(kv, __fmul_rn(r, kw[e]));
+      }
     }
     const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
     // pass 2: write S += k delta, read out = S^T (q scale)
     float o = 0.f;
 #pragma unroll
-    for (int kd = 0; kd < HKD; ++kd) {
-      const float qs = __fmul_rn(qn[kd], p.scale);
-      const float r = __fadd_rn(s[kd], __fmul_rn(kn[kd], delta));
-      s[kd] = r;
-      o = __fadd_rn(o, __fmul_rn(r, qs));
+    for (int k = 0; k < HKD / 4; ++k) {
+      const float4 kk = k4[k], qq = q4[k];
+      const float kw[4] = {kk.x, kk.y, kk.z, kk.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float r = __fadd_rn(s[4 * k + e], __fmul_rn(kw[e], delta));
+        s[4 * k + e] = r;
+        o = __fadd_rn(o, __fmul_rn(r, qw[e]));
+      }
     }
     p.out[t * value + int64_t(h) * p.hvd + col] = o;
     __syncwarp();
   }
+  if (!loaded) {  // no position (the host refuses empty calls): leave the state as it is
+    mbar_wait(&bar, 0);
+    return;
+  }
 #pragma unroll
-  for (int kd = 0; kd < HKD; ++kd) sp[int64_t(kd) * p.hvd] = s[kd];
+  for (int kd = 0; kd < HKD; ++kd) st[kd * 32 + lane] = s[kd];
+  sm100::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    sm100::tma_store_2d(&tmS, st, col0, h * HKD);
+    sm100::tma_store_commit();
+    sm100::tma_store_wait_read();
+  }
+  __syncwarp();
 }
 
 }  // namespace
@@ -129,11 +202,28 @@ cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st) {
   p.l2 = L.call.l2;
   p.eps = L.call.eps;
   p.scale = L.scale;
-  dim3 grid(unsigned(L.shape.nv), unsigned(L.shape.hvd / 32));
-  if (L.shape.hkd == 128) gdn_decode_kernel<128><<<grid, 32, 0, st>>>(p);
-  else if (L.shape.hkd == 64) gdn_decode_kernel<64><<<grid, 32, 0, st>>>(p);
-  else return cudaErrorInvalidValue;
-  return cudaGetLastError();
+  // the state as [nv*hkd rows][hvd columns] f32, tiles [hkd rows][32 columns]
+  CUtensorMap tm;
+  if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.call.state,
+                 uint64_t(L.shape.nv) * L.shape.hkd, uint64_t(L.shape.hvd), uint64_t(L.shape.hvd),
+                 uint32_t(L.shape.hkd), 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  // programmatic dependent launch: the CTAs of consecutive steps are made
+  // resident while the previous step finishes (griddepcontrol.wait in the
+  // kernel orders every memory access after it)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(L.shape.nv), unsigned(L.shape.hvd / 32));
+  cfg.blockDim = dim3(32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (L.shape.hkd == 128) return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<128>, tm, p);
+  if (L.shape.hkd == 64) return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<64>, tm, p);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace hb

@@ -2,6 +2,7 @@
 // (hb_api.cu) and the kernel translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -108,6 +109,16 @@ cudaError_t launch_gdn_prefill(const GdnLaunch& L, const GdnPrefillPlan& pl, voi
 
 // Number of SMs of the current device (cached per device).
 int device_sms();
+
+// TMA tensor maps (hb_tma.cu): a rank-`rank` tiled map, element strides in
+// bytes for dimensions 1.., no interleave, zero fill out of bounds; and the
+// 2-D row-major case [rows][cols] with a row stride in elements.
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                  const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                  CUtensorMapSwizzle swizzle);
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base,
+               uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_rows,
+               uint32_t box_cols, CUtensorMapSwizzle swizzle);
 
 // Host-side checks and error reporting shared by the API translation units
 // (hb_api.cu): a failure sets the thread-local message of hb_last_error.
