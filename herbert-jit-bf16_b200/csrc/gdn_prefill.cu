@@ -18,15 +18,17 @@
 //  * gdn_prep, one CTA per (chunk, key head): both value heads of the key head
 //    at once so that every product is an M=128 tcgen05 MMA -- [K;Q] K^T gives
 //    K K^T and Q K^T; [T0'; T1'] K gives W for both heads; a block-diagonal
-//    [T0'' 0; 0 T1''] times [V0; V1] gives U for both.  T comes from forward
-//    substitution on the CUDA cores (one thread per column).  It writes W, U,
-//    M, Qg = diag(gamma scale) Q, Kt = diag(r_{C-1,.}) K and gamma_{C-1}.
+//    [T0'' 0; 0 T1''] times [V0; V1] gives U for both.  T comes from a blocked
+//    inverse on the CUDA cores (16 x 16 diagonal blocks by forward
+//    substitution, then the off-diagonal blocks block row by block row).  It
+//    writes W, U, M, Qg = diag(gamma scale) Q, Kt = diag(r_{C-1,.}) K as the
+//    scan's shared-memory tile images, and gamma_{C-1}.
 //  * gdn_scan, one CTA per (value head, half of dv), sequential over chunks:
 //    [W; Qg] S0 in one MMA (rows 0-63 W S0, rows 64-127 Q S0), D on the CUDA
 //    cores, then [0; M] D accumulated onto the Q S0 rows (= O) and Kt^T D
 //    accumulated onto the state, which lives in TMEM in f32 (scaled by
 //    gamma_{C-1} first); its bf16 copy in shared memory is the next chunk's
-//    operand.  Chunk inputs stream in by TMA two chunks ahead.
+//    operand.  Chunk tiles stream in by bulk copies two chunks ahead.
 // MMA operands are bf16, accumulators and the state f32; the result is not
 // the bits of the sequential recurrence (as for the reference's own chunked
 // kernel) and is held to a relative Frobenius tolerance.
@@ -49,14 +51,32 @@ constexpr int DV = 128;  // value head dim
 
 // ------------------------------------------------------------------ prep
 
-constexpr int P_SA = 0;             // [K; Q] bf16, 2 blocks of [128 rows x 128 B]
-constexpr int P_SV = 32768;         // [V0; V1] bf16, 2 blocks of [128 rows x 128 B]
-constexpr int P_S2 = 65536;         // [T0 bg0; T1 bg1] bf16, 1 block [128 x 128 B]
-constexpr int P_S3 = 81920;         // blockdiag(T0 b0, T1 b1) bf16, 2 blocks
-constexpr int P_AF = 114688;        // A f32 [2][64][65] (row stride 65: no bank conflicts)
-constexpr int P_VEC = 149504;       // beta[2][64], G[2][64]
+// Every per-(value head, chunk) output is written as the exact shared-memory
+// image the scan's MMAs read (bf16 K-major tiles and the f32 U tile in the
+// 128-byte swizzle, 1024-byte aligned), so both kernels move whole tiles
+// with one-dimensional bulk copies.  Tile images in the workspace:
+//   W, Qg, Kt  [2 column blocks][64 rows][128 B]       16 KB
+//   M          [64 rows][128 B]                         8 KB
+//   U          [4 column boxes of 32][64 rows][128 B]  32 KB (f32)
+constexpr int TILE_WQK = 16384, TILE_M = 8192, TILE_U = 32768;
+
+constexpr int P_SA = 0;          // [K; Q] bf16, 2 blocks of [128 rows x 128 B]
+constexpr int P_SV = 32768;      // [V0; V1] bf16, 2 blocks of [128 rows x 128 B]
+constexpr int P_S2 = 65536;      // [T0 bg0; T1 bg1] bf16, 1 block [128 x 128 B]
+constexpr int P_S3 = 81920;      // blockdiag(T0 b0, T1 b1) bf16, 2 blocks
+constexpr int P_AF = 114688;     // A f32 [2][64][65] (row stride 65: no bank conflicts)
+constexpr int P_TF = 148480;     // T f32 [2][64][65]
+constexpr int P_XS = 182272;     // X blocks f32 [2][3][16][16] of the blocked inverse
+constexpr int P_VEC = 188416;    // beta[2][64], G[2][64]
 constexpr int P_BAR = P_VEC + 1024;
 constexpr int P_SMEM = P_BAR + 64 + 1024;
+// staging of the output images (regions free at that point of the kernel)
+constexpr int P_STG_M = P_TF;    // M0, M1 (16 KB, before T is computed)
+// after the last MMA:
+constexpr int P_STG_QK = P_S2;   // Qg0, Kt0, Qg1, Kt1 (64 KB over S2, S3, AF), read from SA
+constexpr int P_STG_W = P_TF;    // W0, W1 (32 KB)
+constexpr int P_STG_U = P_SA;    // U0, U1 (64 KB over SA, SV), once SA is read
+constexpr int LDA = 65;          // row stride of A, T (floats)
 
 struct PrepParams {
   const float* qkv;
@@ -65,12 +85,12 @@ struct PrepParams {
   int64_t rows;
   int nk, nv, nchunks, l2;
   float eps, scale;
-  uint16_t* W;   // [nv][nchunks][64][128]
-  uint16_t* Qg;  // same
-  uint16_t* Kt;  // same
-  uint16_t* M;   // [nv][nchunks][64][64]
-  float* U;      // [nv][nchunks][64][128]
-  float* gl;     // [nv][nchunks]
+  uint8_t* W;   // [nv][nchunks] tile images
+  uint8_t* Qg;
+  uint8_t* Kt;
+  uint8_t* M;
+  uint8_t* U;
+  float* gl;    // [nv][nchunks]
   int* status;
 };
 
@@ -80,19 +100,26 @@ HB_DEV uint32_t sw_off(int row, int col, int block_bytes) {
   return uint32_t((col >> 6) * block_bytes + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) +
                   (col & 7) * 2);
 }
+// byte offset of 16-byte chunk `ch` (0..7) of row `row` in a 128B-swizzled block
+HB_DEV uint32_t sw_chunk(int row, int ch) { return uint32_t(row * 128 + ((ch ^ (row & 7)) << 4)); }
 
-__global__ void __launch_bounds__(128, 1) gdn_prep_kernel(const PrepParams p) {
+__global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const PrepParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + P_BAR);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 2);
   float* beta_s = reinterpret_cast<float*>(smem + P_VEC);  // [2][64]
   float* G_s = beta_s + 128;                               // [2][64]
+  float* Af = reinterpret_cast<float*>(smem + P_AF);
+  float* Tf = reinterpret_cast<float*>(smem + P_TF);
+  float* Xs = reinterpret_cast<float*>(smem + P_XS);
 
   const int c = blockIdx.x, kh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t key = int64_t(p.nk) * DK, conv = 2 * key + int64_t(p.nv) * DV;
   const int64_t t0 = int64_t(c) * C;
+  const int h0 = kh * 2;
+  const int64_t tile0 = int64_t(h0) * p.nchunks + c, tile1 = tile0 + p.nchunks;
 
   if (tid == 0) {
     mbar_init(&bar[0], 1);
@@ -100,74 +127,47 @@ __global__ void __launch_bounds__(128, 1) gdn_prep_kernel(const PrepParams p) {
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(tslot, 256);
-  // zero the block-diagonal operand (its off-diagonal halves stay zero)
-  for (int i = tid; i < 32768 / 16; i += 128)
-    reinterpret_cast<uint4*>(smem + P_S3)[i] = make_uint4(0, 0, 0, 0);
 
-  // ---- rows: k (tid < 64) or q (tid >= 64) of position t0 + (tid & 63), L2 normalised
+  // ---- rows, a warp per row, lane = 4 columns: warp w loads 32 rows of
+  // tensor w/2 (K, Q, V0, V1), K and Q L2-normalised, bf16 into SA / SV
   {
-    const int r = tid & 63, which = tid >> 6;
-    const int64_t t = t0 + r;
-    float x[DK];
-    if (t < p.rows) {
-      const float4* src = reinterpret_cast<const float4*>(
-          p.qkv + t * conv + (which ? int64_t(kh) * DK : key + int64_t(kh) * DK));
+    const int ten = warp >> 1;
+    const int64_t col_base = ten == 0 ? key + int64_t(kh) * DK
+                           : ten == 1 ? int64_t(kh) * DK
+                                      : 2 * key + int64_t(h0 + ten - 2) * DV;
+    uint8_t* dst = smem + (ten < 2 ? P_SA : P_SV);
+    const int row_off = (ten & 1) * 64;
+    {
+      float4 x[32];  // every row of the warp in flight at once
 #pragma unroll
-      for (int i = 0; i < DK / 4; ++i) {
-        const float4 v = src[i];
-        x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+      for (int i = 0; i < 32; ++i) {
+        const int r = (warp & 1) * 32 + i;
+        const int64_t t = t0 + r;
+        x[i] = t < p.rows ? reinterpret_cast<const float4*>(p.qkv + t * conv + col_base)[lane]
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    } else {
 #pragma unroll
-      for (int i = 0; i < DK; ++i) x[i] = 0.f;
-    }
-    float inv = 1.f;
-    if (p.l2) {
-      float ss = 0.f;
+      for (int i = 0; i < 32; ++i) {
+        const int r = (warp & 1) * 32 + i;
+        float inv = 1.f;
+        if (ten < 2 && p.l2) {
+          float ss = x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
 #pragma unroll
-      for (int i = 0; i < DK; ++i) ss = fmaf(x[i], x[i], ss);
-      inv = 1.f / sqrtf(ss + p.eps);
-    }
-    const int row = which * 64 + r;  // stacked [K; Q]
-#pragma unroll
-    for (int ch = 0; ch < DK / 8; ++ch) {
-      uint4 w;
-      w.x = pack_bf16x2(x[8 * ch] * inv, x[8 * ch + 1] * inv);
-      w.y = pack_bf16x2(x[8 * ch + 2] * inv, x[8 * ch + 3] * inv);
-      w.z = pack_bf16x2(x[8 * ch + 4] * inv, x[8 * ch + 5] * inv);
-      w.w = pack_bf16x2(x[8 * ch + 6] * inv, x[8 * ch + 7] * inv);
-      *reinterpret_cast<uint4*>(smem + P_SA + sw_off(row, ch * 8, 16384)) = w;
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+          inv = 1.f / sqrtf(ss + p.eps);
+        }
+        const uint2 w = make_uint2(pack_bf16x2(x[i].x * inv, x[i].y * inv),
+                                   pack_bf16x2(x[i].z * inv, x[i].w * inv));
+        *reinterpret_cast<uint2*>(dst + sw_off(row_off + r, lane * 4, 16384)) = w;
+      }
     }
   }
-  // ---- values of both heads (row = head * 64 + j), gates
-  {
-    const int r = tid & 63, hh = tid >> 6, h = kh * 2 + hh;
+  if (tid < 128) {  // gates of both value heads
+    const int hh = tid >> 6, r = tid & 63;
     const int64_t t = t0 + r;
-    float x[DV];
-    if (t < p.rows) {
-      const float4* src =
-          reinterpret_cast<const float4*>(p.qkv + t * conv + 2 * key + int64_t(h) * DV);
-#pragma unroll
-      for (int i = 0; i < DV / 4; ++i) {
-        const float4 v = src[i];
-        x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < DV; ++i) x[i] = 0.f;
-    }
-#pragma unroll
-    for (int ch = 0; ch < DV / 8; ++ch) {
-      uint4 w;
-      w.x = pack_bf16x2(x[8 * ch], x[8 * ch + 1]);
-      w.y = pack_bf16x2(x[8 * ch + 2], x[8 * ch + 3]);
-      w.z = pack_bf16x2(x[8 * ch + 4], x[8 * ch + 5]);
-      w.w = pack_bf16x2(x[8 * ch + 6], x[8 * ch + 7]);
-      *reinterpret_cast<uint4*>(smem + P_SV + sw_off(hh * 64 + r, ch * 8, 16384)) = w;
-    }
     const bool in = t < p.rows;
-    beta_s[hh * 64 + r] = in ? p.beta[t * p.nv + h] : 0.f;
-    G_s[hh * 64 + r] = in ? logf(p.decay[t * p.nv + h]) : 0.f;  // padded rows: decay 1
+    beta_s[hh * 64 + r] = in ? p.beta[t * p.nv + h0 + hh] : 0.f;
+    G_s[hh * 64 + r] = in ? logf(p.decay[t * p.nv + h0 + hh]) : 0.f;  // padded rows: decay 1
   }
   fence_proxy_async_smem();
   fence_before_sync();
@@ -200,99 +200,138 @@ __global__ void __launch_bounds__(128, 1) gdn_prep_kernel(const PrepParams p) {
     G_s[warp * 64 + 2 * lane + 1] = s;
   }
   __syncthreads();
+
+  if (tid < 2) p.gl[tid == 0 ? tile0 : tile1] = __expf(G_s[tid * 64 + 63]);
   if (!mbar_wait(&bar[0], 0)) record_status(p.status, kStatusTimeout);
+  __syncthreads();
   fence_after_sync();
 
-  // ---- read K K^T (rows 0-63) and Q K^T (rows 64-127)
-  float* Af = reinterpret_cast<float*>(smem + P_AF);
+  // ---- K K^T (rows 0-63) -> A, Q K^T (rows 64-127) -> M images; warp w
+  // reads TMEM lane quadrant w%4, columns 32 (w/4) .. + 32
   {
-    const uint32_t tq = tmem + (uint32_t(warp * 32) << 16);
-    uint32_t ra[32], rb[32];
-    tmem_ld32(tq, ra);
-    tmem_ld32(tq + 32, rb);
+    const int q = warp & 3, cb = (warp >> 2) * 32;
+    uint32_t ra[32];
+    tmem_ld32(tmem + (uint32_t(q * 32) << 16) + cb, ra);
     tmem_wait_ld();
-    const int t = tid & 63;
-    if (tid < 64) {  // A_h[t][j] = beta_t r_tj (k_t . k_j), j < t
+    const int t = (q & 1) * 32 + lane;
+    if (q < 2) {  // A_h[t][j] = beta_t r_tj (k_t . k_j), j < t
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const float bt = beta_s[hh * 64 + t], Gt = G_s[hh * 64 + t];
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float kk = __uint_as_float(j < 32 ? ra[j] : rb[j - 32]);
-          Af[(hh * 64 + t) * 65 + j] = j < t ? bt * __expf(Gt - G_s[hh * 64 + j]) * kk : 0.f;
+        for (int i = 0; i < 32; ++i) {
+          const int j = cb + i;
+          Af[(hh * 64 + t) * LDA + j] =
+              j < t ? bt * __expf(Gt - G_s[hh * 64 + j]) * __uint_as_float(ra[i]) : 0.f;
         }
       }
     } else {  // M_h[t][j] = scale r_tj (q_t . k_j), j <= t
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
-        const int h = kh * 2 + hh;
         const float Gt = G_s[hh * 64 + t];
-        uint16_t* mrow = p.M + ((int64_t(h) * p.nchunks + c) * C + t) * C;
+        uint8_t* img = smem + P_STG_M + hh * TILE_M;
 #pragma unroll
-        for (int j8 = 0; j8 < 8; ++j8) {
+        for (int c8 = 0; c8 < 4; ++c8) {
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int j0 = j8 * 8 + 2 * i, j1 = j0 + 1;
-            const float q0 = __uint_as_float(j0 < 32 ? ra[j0] : rb[j0 - 32]);
-            const float q1 = __uint_as_float(j1 < 32 ? ra[j1] : rb[j1 - 32]);
-            const float m0 = j0 <= t ? p.scale * __expf(Gt - G_s[hh * 64 + j0]) * q0 : 0.f;
-            const float m1 = j1 <= t ? p.scale * __expf(Gt - G_s[hh * 64 + j1]) * q1 : 0.f;
+            const int i0 = c8 * 8 + 2 * i, j0 = cb + i0, j1 = j0 + 1;
+            const float m0 = j0 <= t ? p.scale * __expf(Gt - G_s[hh * 64 + j0]) * __uint_as_float(ra[i0]) : 0.f;
+            const float m1 = j1 <= t ? p.scale * __expf(Gt - G_s[hh * 64 + j1]) * __uint_as_float(ra[i0 + 1]) : 0.f;
             w[i] = pack_bf16x2(m0, m1);
           }
-          reinterpret_cast<uint4*>(mrow)[j8] = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(img + sw_chunk(t, (cb >> 3) + c8)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
     }
   }
-  // ---- Qg = diag(gamma scale) Q and Kt = diag(r_{63,.}) K for both heads
-  {
-    const int hh = tid >> 6, t = tid & 63, h = kh * 2 + hh;
-    const float G = G_s[hh * 64 + t];
-    const float gq = __expf(G) * p.scale, gk = __expf(G_s[hh * 64 + 63] - G);
-    const int64_t base = ((int64_t(h) * p.nchunks + c) * C + t) * DK;
-#pragma unroll 4
-    for (int ch = 0; ch < DK / 8; ++ch) {
-      const uint4 kv = *reinterpret_cast<const uint4*>(smem + P_SA + sw_off(t, ch * 8, 16384));
-      const uint4 qv = *reinterpret_cast<const uint4*>(smem + P_SA + sw_off(64 + t, ch * 8, 16384));
-      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, qw[4] = {qv.x, qv.y, qv.z, qv.w};
-      uint32_t ko[4], qo[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ko[i] = pack_bf16x2(bf16lo(kw[i]) * gk, bf16hi(kw[i]) * gk);
-        qo[i] = pack_bf16x2(bf16lo(qw[i]) * gq, bf16hi(qw[i]) * gq);
-      }
-      reinterpret_cast<uint4*>(p.Kt + base)[ch] = make_uint4(ko[0], ko[1], ko[2], ko[3]);
-      reinterpret_cast<uint4*>(p.Qg + base)[ch] = make_uint4(qo[0], qo[1], qo[2], qo[3]);
-    }
-    if (t == 63) p.gl[int64_t(h) * p.nchunks + c] = __expf(G);
-  }
+  fence_proxy_async_smem();
   fence_before_sync();
   __syncthreads();
+  if (tid == 0) {
+    bulk_s2g(p.M + tile0 * TILE_M, smem + P_STG_M, TILE_M);
+    bulk_s2g(p.M + tile1 * TILE_M, smem + P_STG_M + TILE_M, TILE_M);
+    tma_store_commit();
+  }
 
-  // ---- T = (I + A)^-1 by forward substitution: thread (head hh, column j)
-  {
-    const int hh = tid >> 6, j = tid & 63;
-    const float* A = Af + hh * 64 * 65;
-    float tc[64];
+  // ---- T = (I + A)^-1 by 16 x 16 blocks (threads 128 per head):
+  //  diagonal blocks by forward substitution, then for block rows i = 1..3
+  //  X_ij = sum_{k=j}^{i-1} A_ik T_kj and T_ij = -T_ii X_ij
+  const int hh = tid >> 7, lt = tid & 127;
+  const float* A = Af + hh * 64 * LDA;
+  float* T = Tf + hh * 64 * LDA;
+  if (tid == 0) tma_store_wait_read();  // the M staging lies under T
+  __syncthreads();
+  if (lt < 64) {  // column jj of diagonal block ib
+    const int ib = lt >> 4, jj = lt & 15, o = ib * 16;
+    float x[16];
 #pragma unroll
-    for (int t = 0; t < 64; ++t) {
+    for (int t = 0; t < 16; ++t) {
       float acc = 0.f;
 #pragma unroll
-      for (int s = 0; s < t; ++s) acc = fmaf(A[t * 65 + s], tc[s], acc);
-      tc[t] = t == j ? 1.f : (t < j ? 0.f : -acc);
+      for (int s = 0; s < t; ++s) acc = fmaf(A[(o + t) * LDA + o + s], x[s], acc);
+      x[t] = t == jj ? 1.f : (t < jj ? 0.f : -acc);
     }
-    const float bj = beta_s[hh * 64 + j], gj = __expf(G_s[hh * 64 + j]);
-    const float wbg = bj * gj;
-    // S2 row (hh*64 + t), column j: T[t][j] beta_j gamma_j
-    // S3 row (hh*64 + t), column hh*64 + j: T[t][j] beta_j
 #pragma unroll
-    for (int t = 0; t < 64; ++t) {
-      const int row = hh * 64 + t;
-      *reinterpret_cast<uint16_t*>(smem + P_S2 + sw_off(row, j, 16384)) =
-          f32_to_bf16_cvtne(tc[t] * wbg);
-      *reinterpret_cast<uint16_t*>(smem + P_S3 + sw_off(row, hh * 64 + j, 16384)) =
-          f32_to_bf16_cvtne(tc[t] * bj);
+    for (int t = 0; t < 16; ++t) T[(o + t) * LDA + o + jj] = x[t];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int ib = 1; ib < 4; ++ib) {
+    // X_ij for j < ib: ib * 256 elements per head, ib * 2 per thread
+    float* X = Xs + hh * 768;
+    for (int e = lt; e < ib * 256; e += 128) {
+      const int jb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      float acc = 0.f;
+#pragma unroll
+      for (int kb = 0; kb < 3; ++kb) {
+        if (kb < jb || kb >= ib) continue;
+#pragma unroll
+        for (int s = 0; s < 16; ++s)
+          acc = fmaf(A[(ib * 16 + r) * LDA + kb * 16 + s], T[(kb * 16 + s) * LDA + jb * 16 + cc], acc);
+      }
+      X[e] = acc;
+    }
+    __syncthreads();
+    for (int e = lt; e < ib * 256; e += 128) {
+      const int jb = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+      float acc = 0.f;
+#pragma unroll
+      for (int s = 0; s < 16; ++s)
+        acc = fmaf(T[(ib * 16 + r) * LDA + ib * 16 + s], X[(jb * 16 + s) * 16 + cc], acc);
+      T[(ib * 16 + r) * LDA + jb * 16 + cc] = -acc;
+    }
+    __syncthreads();
+  }
+
+  // ---- S2 row (hh*64 + t) col j: T[t][j] beta_j gamma_j; S3 row (hh*64 + t)
+  // col (hh*64 + j): T[t][j] beta_j, other half of the row zero; j > t zero
+  {
+    const int t = lt >> 1, half = lt & 1;
+    const int row = hh * 64 + t;
+#pragma unroll
+    for (int c8 = 0; c8 < 4; ++c8) {
+      uint32_t w2[4], w3[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float a2[2], a3[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = half * 32 + c8 * 8 + 2 * i + e;
+          const float tv = j <= t ? T[t * LDA + j] : 0.f;
+          const float bj = beta_s[hh * 64 + j];
+          a3[e] = tv * bj;
+          a2[e] = a3[e] * __expf(G_s[hh * 64 + j]);
+        }
+        w2[i] = pack_bf16x2(a2[0], a2[1]);
+        w3[i] = pack_bf16x2(a3[0], a3[1]);
+      }
+      const int ch = half * 4 + c8;
+      *reinterpret_cast<uint4*>(smem + P_S2 + sw_chunk(row, ch)) = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+      *reinterpret_cast<uint4*>(smem + P_S3 + hh * 16384 + sw_chunk(row, ch)) =
+          make_uint4(w3[0], w3[1], w3[2], w3[3]);
+      *reinterpret_cast<uint4*>(smem + P_S3 + (hh ^ 1) * 16384 + sw_chunk(row, ch)) =
+          make_uint4(0, 0, 0, 0);
     }
   }
   fence_proxy_async_smem();
@@ -318,31 +357,75 @@ __global__ void __launch_bounds__(128, 1) gdn_prep_kernel(const PrepParams p) {
   __syncwarp();
   if (!mbar_wait(&bar[1], 0)) record_status(p.status, kStatusTimeout);
   fence_after_sync();
-  {
-    const int hh = tid >> 6, t = tid & 63, h = kh * 2 + hh;
-    const uint32_t tq = tmem + (uint32_t(warp * 32) << 16);
-    const int64_t base = ((int64_t(h) * p.nchunks + c) * C + t) * DK;
-#pragma unroll 1
-    for (int cb = 0; cb < 4; ++cb) {
-      uint32_t w[32], u[32];
-      tmem_ld32(tq + cb * 32, w);
-      tmem_ld32(tq + 128 + cb * 32, u);
-      tmem_wait_ld();
+
+  // ---- Qg = diag(gamma scale) Q, Kt = diag(r_{63,.}) K as tile images: a
+  // row scaling keeps each 16-byte chunk where the swizzle put it.  Unit =
+  // (head, tensor, row, column block), 128 bytes; 512 units, 2 per thread.
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        reinterpret_cast<uint4*>(p.W + base + cb * 32)[i] =
-            make_uint4(pack_bf16x2(__uint_as_float(w[8 * i]), __uint_as_float(w[8 * i + 1])),
-                       pack_bf16x2(__uint_as_float(w[8 * i + 2]), __uint_as_float(w[8 * i + 3])),
-                       pack_bf16x2(__uint_as_float(w[8 * i + 4]), __uint_as_float(w[8 * i + 5])),
-                       pack_bf16x2(__uint_as_float(w[8 * i + 6]), __uint_as_float(w[8 * i + 7])));
+  for (int k = 0; k < 2; ++k) {
+    const int u = tid + k * 256;
+    const int blk = u & 1, r = (u >> 1) & 63, ten = (u >> 7) & 1, hq = u >> 8;
+    const float G = G_s[hq * 64 + r];
+    const float f = ten == 0 ? __expf(G) * p.scale : __expf(G_s[hq * 64 + 63] - G);
+    const uint8_t* src = smem + P_SA + blk * 16384 + (ten == 0 ? 64 + r : r) * 128;
+    uint8_t* dst = smem + P_STG_QK + (hq * 2 + ten) * TILE_WQK + blk * 8192 + r * 128;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        reinterpret_cast<float4*>(p.U + base + cb * 32)[i] =
-            make_float4(__uint_as_float(u[4 * i]), __uint_as_float(u[4 * i + 1]),
-                        __uint_as_float(u[4 * i + 2]), __uint_as_float(u[4 * i + 3]));
+    for (int k8 = 0; k8 < 8; ++k8) {
+      const int ch = (k8 + r) & 7;  // rows of a warp start on different banks
+      const uint4 v = reinterpret_cast<const uint4*>(src)[ch];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = pack_bf16x2(bf16lo(w[i]) * f, bf16hi(w[i]) * f);
+      reinterpret_cast<uint4*>(dst)[ch] = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
+  __syncthreads();  // SA is read: the U images may overwrite it
+
+  // ---- W (bf16) and U (f32) images: warp w reads lane quadrant w%4 (row =
+  // head*64 + t), columns 64 (w/4) .. + 64 of W and of U
+  {
+    const int q = warp & 3, cb = (warp >> 2) * 64;
+    const int row = q * 32 + lane, wh = row >> 6, t = row & 63;
+    const uint32_t tq = tmem + (uint32_t(q * 32) << 16);
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      uint32_t w[32], u[32];
+      tmem_ld32(tq + cb + half * 32, w);
+      tmem_ld32(tq + 128 + cb + half * 32, u);
+      tmem_wait_ld();
+      const int col0 = cb + half * 32;  // 32 columns: 4 bf16 chunks of W, 8 f32 chunks of U
+      uint8_t* wimg = smem + P_STG_W + wh * TILE_WQK + (col0 >> 6) * 8192;
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8)
+        *reinterpret_cast<uint4*>(wimg + sw_chunk(t, ((col0 & 63) >> 3) + c8)) =
+            make_uint4(pack_bf16x2(__uint_as_float(w[8 * c8]), __uint_as_float(w[8 * c8 + 1])),
+                       pack_bf16x2(__uint_as_float(w[8 * c8 + 2]), __uint_as_float(w[8 * c8 + 3])),
+                       pack_bf16x2(__uint_as_float(w[8 * c8 + 4]), __uint_as_float(w[8 * c8 + 5])),
+                       pack_bf16x2(__uint_as_float(w[8 * c8 + 6]), __uint_as_float(w[8 * c8 + 7])));
+      uint8_t* uimg = smem + P_STG_U + wh * TILE_U + (col0 >> 5) * 8192;
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4)
+        *reinterpret_cast<float4*>(uimg + sw_chunk(t, c4)) =
+            make_float4(__uint_as_float(u[4 * c4]), __uint_as_float(u[4 * c4 + 1]),
+                        __uint_as_float(u[4 * c4 + 2]), __uint_as_float(u[4 * c4 + 3]));
+    }
+  }
+  fence_proxy_async_smem();
   fence_before_sync();
+  __syncthreads();
+  if (tid == 0) {
+    bulk_s2g(p.Qg + tile0 * TILE_WQK, smem + P_STG_QK + 0 * TILE_WQK, TILE_WQK);
+    bulk_s2g(p.Kt + tile0 * TILE_WQK, smem + P_STG_QK + 1 * TILE_WQK, TILE_WQK);
+    bulk_s2g(p.Qg + tile1 * TILE_WQK, smem + P_STG_QK + 2 * TILE_WQK, TILE_WQK);
+    bulk_s2g(p.Kt + tile1 * TILE_WQK, smem + P_STG_QK + 3 * TILE_WQK, TILE_WQK);
+    bulk_s2g(p.W + tile0 * TILE_WQK, smem + P_STG_W, TILE_WQK);
+    bulk_s2g(p.W + tile1 * TILE_WQK, smem + P_STG_W + TILE_WQK, TILE_WQK);
+    bulk_s2g(p.U + tile0 * TILE_U, smem + P_STG_U, TILE_U);
+    bulk_s2g(p.U + tile1 * TILE_U, smem + P_STG_U + TILE_U, TILE_U);
+    tma_store_commit();
+    tma_store_wait_read();
+  }
   __syncthreads();
   if (warp == 0) {
     fence_after_sync();
@@ -356,7 +439,7 @@ constexpr int BV = 64;                    // value columns per CTA
 constexpr int S_A1 = 0;                   // per stage: [W; Qg] 2 blocks x 16 KB
 constexpr int S_A2 = 32768;               //            [0; M] 1 block 16 KB
 constexpr int S_KT = 49152;               //            Kt 2 blocks of [64 x 128 B]
-constexpr int S_U = 65536;                //            U f32 [64][64]
+constexpr int S_U = 65536;                //            U f32, 2 blocks [64 rows x 128 B], 128B-swizzled
 constexpr int STAGE = 81920;
 constexpr int S_D = 2 * STAGE;            // D bf16 [64 rows x 128 B]
 constexpr int S_SB = S_D + 8192;          // S bf16 [128 rows x 128 B]
@@ -371,15 +454,17 @@ struct ScanParams {
   float* state;     // [nv][DK][DV]
   float* out;       // [rows][nv*DV]
   const float* gl;  // [nv][nchunks]
+  const uint8_t* W;  // tile images of the prep kernel, [nv][nchunks]
+  const uint8_t* Qg;
+  const uint8_t* Kt;
+  const uint8_t* M;
+  const uint8_t* U;
   int64_t rows;
   int nv, nchunks;
   int* status;
 };
 
-__global__ void __launch_bounds__(192, 1)
-    gdn_scan_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmQg,
-                    const __grid_constant__ CUtensorMap tmKt, const __grid_constant__ CUtensorMap tmM,
-                    const __grid_constant__ CUtensorMap tmU, const ScanParams p) {
+__global__ void __launch_bounds__(192, 1) gdn_scan_kernel(const ScanParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + S_BAR);
@@ -429,15 +514,16 @@ __global__ void __launch_bounds__(192, 1)
         const int s = c & 1;
         if (c >= 2 && !wait(EMPTY + s, ((c >> 1) - 1) & 1)) break;
         uint8_t* st = smem + s * STAGE;
-        const int row = (h * nc + c) * C;
-        mbar_arrive_expect_tx(&bar[FULL + s], 16384 * 2 + 8192 + 16384 + 16384);
-        for (int b = 0; b < 2; ++b) {
-          tma_load_2d(st + S_A1 + b * 16384, &tmW, &bar[FULL + s], b * 64, row);
-          tma_load_2d(st + S_A1 + b * 16384 + 8192, &tmQg, &bar[FULL + s], b * 64, row);
-          tma_load_2d(st + S_KT + b * 8192, &tmKt, &bar[FULL + s], b * 64, row);
+        const int64_t tile = int64_t(h) * nc + c;
+        uint64_t* fb = &bar[FULL + s];
+        mbar_arrive_expect_tx(fb, 4 * 8192 + TILE_WQK + TILE_M + TILE_U / 2);
+        for (int b = 0; b < 2; ++b) {  // [W; Qg] stacked per column block
+          bulk_g2s(st + S_A1 + b * 16384, p.W + tile * TILE_WQK + b * 8192, 8192, fb);
+          bulk_g2s(st + S_A1 + b * 16384 + 8192, p.Qg + tile * TILE_WQK + b * 8192, 8192, fb);
         }
-        tma_load_2d(st + S_A2 + 8192, &tmM, &bar[FULL + s], 0, row);
-        tma_load_2d(st + S_U, &tmU, &bar[FULL + s], vb * BV, row);
+        bulk_g2s(st + S_KT, p.Kt + tile * TILE_WQK, TILE_WQK, fb);
+        bulk_g2s(st + S_A2 + 8192, p.M + tile * TILE_M, TILE_M, fb);
+        bulk_g2s(st + S_U, p.U + tile * TILE_U + vb * (TILE_U / 2), TILE_U / 2, fb);
       }
     }
   } else if (warp == 5) {  // -------------------------------------------- MMA
@@ -505,8 +591,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_arrive(&bar[SBF_READY]);
     }
     bool ok = true;
+    float g_next = p.gl[int64_t(h) * nc];  // gamma_{C-1} of the chunk, one chunk ahead
     for (int c = 0; c < nc && ok; ++c) {
       const int s = c & 1;
+      const float g = g_next;
+      if (c + 1 < nc) g_next = p.gl[int64_t(h) * nc + c + 1];
       ok = __all_sync(0xFFFFFFFFu, wait(D0_FULL, c & 1));
       fence_after_sync();
       if (warp < 2) {  // D = U - W S0 for row t
@@ -514,13 +603,15 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld32(tq, a);
         tmem_ld32(tq + 32, b);
         tmem_wait_ld();
-        const float* u = reinterpret_cast<const float*>(smem + s * STAGE + S_U) + row * BV;
+        // U row `row`: columns c at block c/32, 16-byte chunk (c%32)/4 ^ (row%8)
+        const uint8_t* u = smem + s * STAGE + S_U + row * 128;
 #pragma unroll
         for (int ch = 0; ch < 8; ++ch) {
           const uint32_t* v = ch < 4 ? a : b;
           const int o = (ch & 3) * 8;
-          const float4 u0 = reinterpret_cast<const float4*>(u + ch * 8)[0];
-          const float4 u1 = reinterpret_cast<const float4*>(u + ch * 8)[1];
+          const int blk = (ch >> 2) * 8192, j = (ch & 3) * 2;
+          const float4 u0 = *reinterpret_cast<const float4*>(u + blk + ((j ^ (row & 7)) << 4));
+          const float4 u1 = *reinterpret_cast<const float4*>(u + blk + (((j + 1) ^ (row & 7)) << 4));
           *reinterpret_cast<uint4*>(smem + S_D + sw_off(row, ch * 8, 8192)) =
               make_uint4(pack_bf16x2(u0.x - __uint_as_float(v[o]), u0.y - __uint_as_float(v[o + 1])),
                          pack_bf16x2(u0.z - __uint_as_float(v[o + 2]), u0.w - __uint_as_float(v[o + 3])),
@@ -531,7 +622,6 @@ __global__ void __launch_bounds__(192, 1)
         mbar_arrive(&bar[DELTA_FULL]);
       }
       {  // S <- gamma_{C-1} S
-        const float g = p.gl[int64_t(h) * nc + c];
         uint32_t a[32], b[32];
         tmem_ld32(tq + 64, a);
         tmem_ld32(tq + 96, b);
@@ -610,12 +700,6 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// 2-D row-major tensor [rows][cols] of `elem` bytes, boxes [box_rows][box_cols].
-bool encode2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem, uint64_t rows,
-              uint64_t cols, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle sw) {
-  return encode_2d(m, dt, elem, base, rows, cols, cols, box_rows, box_cols, sw);
-}
-
 }  // namespace
 
 bool gdn_prefill_serves(const hb_gdn_shape& s) {
@@ -660,40 +744,31 @@ cudaError_t launch_gdn_prefill(const GdnLaunch& L, const GdnPrefillPlan& pl, voi
   pp.l2 = L.call.l2;
   pp.eps = L.call.eps;
   pp.scale = L.scale;
-  pp.W = reinterpret_cast<uint16_t*>(base + pl.off_W);
-  pp.Qg = reinterpret_cast<uint16_t*>(base + pl.off_Qg);
-  pp.Kt = reinterpret_cast<uint16_t*>(base + pl.off_Kt);
-  pp.M = reinterpret_cast<uint16_t*>(base + pl.off_M);
-  pp.U = reinterpret_cast<float*>(base + pl.off_U);
+  pp.W = reinterpret_cast<uint8_t*>(base + pl.off_W);
+  pp.Qg = reinterpret_cast<uint8_t*>(base + pl.off_Qg);
+  pp.Kt = reinterpret_cast<uint8_t*>(base + pl.off_Kt);
+  pp.M = reinterpret_cast<uint8_t*>(base + pl.off_M);
+  pp.U = reinterpret_cast<uint8_t*>(base + pl.off_U);
   pp.gl = reinterpret_cast<float*>(base + pl.off_gl);
   pp.status = reinterpret_cast<int*>(base);
-  gdn_prep_kernel<<<dim3(unsigned(pl.nchunks), unsigned(L.shape.nk)), 128, P_SMEM, st>>>(pp);
+  gdn_prep_kernel<<<dim3(unsigned(pl.nchunks), unsigned(L.shape.nk)), 256, P_SMEM, st>>>(pp);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  const uint64_t rows_all = uint64_t(L.shape.nv) * pl.nchunks * C;
-  CUtensorMap tW, tQ, tK, tM, tU;
-  if (!encode2d(&tW, pp.W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_all, DK, 64, 64,
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode2d(&tQ, pp.Qg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_all, DK, 64, 64,
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode2d(&tK, pp.Kt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_all, DK, 64, 64,
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode2d(&tM, pp.M, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows_all, C, 64, 64,
-                CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode2d(&tU, pp.U, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows_all, DV, 64, BV,
-                CU_TENSOR_MAP_SWIZZLE_NONE))
-    return cudaErrorInvalidValue;
   ScanParams sp;
   sp.state = L.call.state;
   sp.out = L.call.output;
   sp.gl = pp.gl;
+  sp.W = pp.W;
+  sp.Qg = pp.Qg;
+  sp.Kt = pp.Kt;
+  sp.M = pp.M;
+  sp.U = pp.U;
   sp.rows = L.call.rows;
   sp.nv = int(L.shape.nv);
   sp.nchunks = int(pl.nchunks);
   sp.status = pp.status;
-  gdn_scan_kernel<<<dim3(unsigned(L.shape.nv), DV / BV), 192, S_SMEM, st>>>(tW, tQ, tK, tM, tU,
-                                                                             sp);
+  gdn_scan_kernel<<<dim3(unsigned(L.shape.nv), DV / BV), 192, S_SMEM, st>>>(sp);
   return cudaGetLastError();
 }
 

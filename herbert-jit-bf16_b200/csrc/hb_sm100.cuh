@@ -53,6 +53,14 @@ HB_DEV void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) 
                : "memory");
 }
 HB_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// One-dimensional bulk store shared -> global (bulk group): both addresses
+// 16-byte aligned, bytes a multiple of 16.
+HB_DEV void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
 // Waits until the committed stores have read their shared-memory source.
 HB_DEV void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // Waits until the committed stores are complete.
