@@ -9,22 +9,25 @@
 // [0, past + r] (src/jit/target/x86/execution/attention.rs:189-196).
 //
 // CTA = one tile of 128 query rows of one query head (head_dim 256):
-//   warp 4       TMA producer: Q tile once, then K and V tiles of 64 keys
+//   warp 8       TMA producer: Q tile once, then K and V tiles of 64 keys
 //                into two-stage rings (SWIZZLE_128B, no multicast);
-//   warp 5       MMA issuer: S_j = Q K_j^T (M128 N64 K256, 16 MMAs) into one
-//                of two TMEM S buffers, then O += P_{j-1} V_{j-1} (M128 N256
-//                K64, 4 MMAs, V read MN-major) into the TMEM O accumulator;
+//   warp 9       MMA issuer: S_j = Q K_j^T (M128 N64 K256, 16 MMAs) into one
+//                of three TMEM S buffers, O += P_j V_j (M128 N256 K64, 4 MMAs,
+//                V read MN-major) into the TMEM O accumulator, issued in the
+//                order PV_j, S_{j+2} so S runs two tiles ahead of the softmax;
 //                each group is committed to an mbarrier;
-//   warps 0-3    softmax: one thread per query row reads its S row from TMEM,
-//                applies the causal mask, keeps the running max m and sum l in
-//                the log2 domain, writes P = 2^(s - m) as bf16 into shared
-//                memory in the UMMA K-major swizzled layout, and rescales the
-//                O row in TMEM only when the max grows by more than 2^8;
+//   warps 0-7    softmax: two threads per query row (warps q and q+4 share
+//                TMEM lanes 32q.., each takes 32 of a tile's 64 keys) read S
+//                from TMEM, apply the causal mask, exchange their partial row
+//                maxima through TMEM, keep the running max m and sum l in the
+//                log2 domain, write P = 2^(s - m) as bf16 into shared memory
+//                in the UMMA K-major swizzled layout, and rescale the O row in
+//                TMEM only when the max grows by more than 2^8;
 //   warps 0-7    epilogue: O / l, bf16, gate with the reference's exp
 //                polynomial and rounding steps; the gate tile comes in by TMA
 //                (into the K ring, free once the last S is computed) and the
 //                output tile leaves by TMA store (staged in the V ring).
-// TMEM: S buffers at columns [0,128), O at [256,512) of a 512-column
+// TMEM: S buffers at columns [0,192), O at [256,512) of a 512-column
 // allocation.  Shared memory: Q 64 KB + K 2x32 KB + V 2x32 KB + P 2x16 KB.
 //
 // Context-parallel hops (template CP = true) run the same pipeline over the
@@ -47,31 +50,49 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 64, HDIM = 256;
-constexpr int kThreads = 320;  // warps 0-3 softmax, 0-7 epilogue, 8 TMA, 9 MMA
+constexpr int BM = 128, BN = 128, HDIM = 256;  // query rows, keys per tile, head dim
+constexpr int kThreads = 320;  // warps 0-7 softmax and epilogue, 8 TMA, 9 MMA
 constexpr int kTmaWarp = 8, kMmaWarp = 9;
-constexpr int Q_BYTES = BM * HDIM * 2;   // 4 column blocks of [128 rows x 128 B]
-constexpr int KV_BYTES = BN * HDIM * 2;  // 4 column blocks of [64 rows x 128 B]
-constexpr int P_BYTES = BM * BN * 2;     // 1 block of [128 rows x 128 B]
+constexpr int Q_BYTES = BM * HDIM * 2;  // 4 column blocks of [128 rows x 128 B]
+constexpr int SLOT = 16384;             // one ring slot
+constexpr int NSLOT = 4;
 constexpr int OFF_Q = 0;
+// K ring: slot b holds column block b (dims 64b..64b+63) of a key tile,
+// [128 keys x 128 B]; V ring: slot c holds keys 32c..32c+31 of a tile,
+// [4 column blocks][32 keys][128 B].  A slot is refilled for the next tile
+// as soon as the MMAs that read it have completed.
 constexpr int OFF_K = OFF_Q + Q_BYTES;
-constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-constexpr int NBAR = 18;
+constexpr int OFF_V = OFF_K + NSLOT * SLOT;
+constexpr int OFF_BAR = OFF_V + NSLOT * SLOT;
+constexpr int NBAR = 24;
 constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l (or the merge weight of O_acc)
-constexpr int SMEM_BYTES = OFF_INVL + BM * 4 + 1024;  // + 1 KB alignment slack
-// merge weight of a CP hop's O: in the K ring, which no MMA reads once the
-// softmax has seen the last S (a hop loads no gate tile there)
-constexpr int OFF_FB = OFF_K;
+constexpr int OFF_FB = OFF_INVL + BM * 4;          // merge weight of a CP hop's O
+constexpr int OFF_XM = OFF_FB + BM * 4;            // row maxima [2 parity][2 halves][128]
+constexpr int OFF_XL = OFF_XM + 4 * BM * 4;        // row sums [2 halves][128]
+constexpr int SMEM_BYTES = OFF_XL + 2 * BM * 4 + 1024;  // + 1 KB alignment slack
 constexpr uint32_t TMEM_COLS = 512;
+// S_j in columns [128 (j%2), +128); P_j (bf16, two per column) overwrites
+// its first 64 columns; O in [256, 512)
 constexpr uint32_t S_COL = 0, O_COL = 256;
 constexpr float kRescaleLog2 = 8.0f;  // keep a stale max while p stays below 2^8
 
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 3, V_FULL = 5, V_EMPTY = 7, S_FULL = 9,
-           S_EMPTY = 11, P_FULL = 13, PV_DONE = 15, GATE_FULL = 17 };
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 5, V_FULL = 9, V_EMPTY = 13, S_FULL = 17,
+           P_FULL = 19, PV_DONE = 21, GATE_FULL = 23 };
 
 HB_DEV void epilogue_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+
+// Barrier of the two softmax warps of lane quadrant q (warps q and q + 4,
+// named barrier 3 + q); returns the AND of `v` over their 64 threads, so
+// both warps take the same early exit.
+HB_DEV bool pair_sync_and(int q, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, 64, p; selp.u32 %0, 1, 0, q; }"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(3 + q)
+      : "memory");
+  return r != 0;
+}
 
 // Kept at 104 bytes: with the tensor maps, a larger parameter block made
 // the same kernel ~5% slower on B200 (measured).
@@ -112,6 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* inv_l = reinterpret_cast<float*>(smem + OFF_INVL);
   float* w_hop = reinterpret_cast<float*>(smem + OFF_FB);
+  float* xmax = reinterpret_cast<float*>(smem + OFF_XM);
+  float* xsum = reinterpret_cast<float*>(smem + OFF_XL);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = p.n_qtiles - 1 - int(blockIdx.x) / p.heads;  // heaviest tiles first
@@ -132,14 +155,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[Q_FULL], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&bar[K_FULL + s], 1);
       mbar_init(&bar[K_EMPTY + s], 1);
       mbar_init(&bar[V_FULL + s], 1);
       mbar_init(&bar[V_EMPTY + s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bar[S_FULL + s], 1);
-      mbar_init(&bar[S_EMPTY + s], 128);
-      mbar_init(&bar[P_FULL + s], 128);
+      mbar_init(&bar[P_FULL + s], 256);
       mbar_init(&bar[PV_DONE + s], 1);
     }
     mbar_init(&bar[GATE_FULL], 1);
@@ -159,104 +183,141 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 1;
     return false;
   };
+  // K/V row of the first key of tile j in the K/V buffers
+  auto key_row = [&](int j) -> int {
+    return !CP ? j * BN : j < n0 ? j * BN : p.chunk + (j - n0) * BN;
+  };
 
-  if (warp == kTmaWarp) {  // ----------------------------------- TMA producer
-    if (lane == 0) {
+  if (warp == kTmaWarp) {  // ---------------------- TMA producers (lanes 0, 1)
+    if (lane == 0) {  // Q, then the K slots, then the gate tile
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
       prefetch_tmap(&tmO);
       mbar_arrive_expect_tx(&bar[Q_FULL], Q_BYTES);
       for (int c = 0; c < 4; ++c)
-        tma_load_2d(smem + OFF_Q + c * (BM * 128), &tmQ, &bar[Q_FULL], h * HDIM + c * 64, m0);
-      for (int j = 0; j < ntiles; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int kr = !CP ? j * BN : j < n0 ? j * BN : p.chunk + (j - n0) * BN;
-        if (j >= 2 && !wait(K_EMPTY + s, ph ^ 1)) break;
-        mbar_arrive_expect_tx(&bar[K_FULL + s], KV_BYTES);
-        for (int c = 0; c < 4; ++c)
-          tma_load_3d(smem + OFF_K + s * KV_BYTES + c * (BN * 128), &tmK, &bar[K_FULL + s], c * 64,
-                      kr, kvh);
-        if (j >= 2 && !wait(V_EMPTY + s, ph ^ 1)) break;
-        mbar_arrive_expect_tx(&bar[V_FULL + s], KV_BYTES);
-        for (int c = 0; c < 4; ++c)
-          tma_load_3d(smem + OFF_V + s * KV_BYTES + c * (BN * 128), &tmV, &bar[V_FULL + s], c * 64,
-                      kr, kvh);
+        tma_load_2d(smem + OFF_Q + c * SLOT, &tmQ, &bar[Q_FULL], h * HDIM + c * 64, m0);
+      bool ok = true;
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int kr = key_row(j);
+        for (int b = 0; b < NSLOT; ++b) {
+          if (j >= 1 && !wait(K_EMPTY + b, (j - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bar[K_FULL + b], SLOT);
+          tma_load_3d(smem + OFF_K + b * SLOT, &tmK, &bar[K_FULL + b], b * 64, kr, kvh);
+        }
       }
-      // the gate tile [128 rows x 256] goes into the K ring once the last one
-      // or two S products have read it
-      if (!CP && p.gate_offset >= 0) {
+      // the gate tile [128 rows x 256] goes into the K ring once the last S
+      // product has read it
+      if (ok && !CP && p.gate_offset >= 0) {
         bool free_ring = true;
-        for (int j = ntiles > 2 ? ntiles - 2 : 0; j < ntiles; ++j)
-          free_ring = free_ring && wait(K_EMPTY + (j & 1), (j >> 1) & 1);
+        for (int b = 0; b < NSLOT; ++b) free_ring = free_ring && wait(K_EMPTY + b, (ntiles - 1) & 1);
         if (free_ring) {
           mbar_arrive_expect_tx(&bar[GATE_FULL], Q_BYTES);
           for (int c = 0; c < 4; ++c)
-            tma_load_2d(smem + OFF_K + c * (BM * 128), &tmQ, &bar[GATE_FULL],
+            tma_load_2d(smem + OFF_K + c * SLOT, &tmQ, &bar[GATE_FULL],
                         int(p.gate_offset) + h * HDIM + c * 64, m0);
         }
       }
-    }
-  } else if (warp == kMmaWarp) {  // ------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16(BM, BN, false, false);
-      constexpr uint32_t idPV = idesc_bf16(BM, HDIM, false, true);
-      const uint32_t qb = smem_u32(smem + OFF_Q);
-      bool ok = wait(Q_FULL, 0);
-      for (int j = 0; ok && j <= ntiles; ++j) {
-        if (j < ntiles) {
-          const int s = j & 1;
-          const uint32_t ph = (j >> 1) & 1;
-          if (!wait(K_FULL + s, ph)) break;
-          if (j >= 2 && !wait(S_EMPTY + s, ph ^ 1)) break;
-          fence_after_sync();
-          const uint32_t kb = smem_u32(smem + OFF_K + s * KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < HDIM / 16; ++kk) {
-            const uint64_t a = sw128_desc(qb + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t b = sw128_desc(kb + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-            mma_bf16_ss(tmem + S_COL + s * BN, a, b, idS, kk > 0);
+    } else if (lane == 1) {  // the V slots
+      prefetch_tmap(&tmV);
+      bool ok = true;
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int kr = key_row(j);
+        for (int c = 0; c < NSLOT; ++c) {
+          if (j >= 1 && !wait(V_EMPTY + c, (j - 1) & 1)) {
+            ok = false;
+            break;
           }
-          mma_commit(&bar[S_FULL + s]);
-          mma_commit(&bar[K_EMPTY + s]);
-        }
-        if (j >= 1) {
-          const int jj = j - 1, s = jj & 1;
-          const uint32_t ph = (jj >> 1) & 1;
-          if (!wait(P_FULL + s, ph) || !wait(V_FULL + s, ph)) break;
-          fence_after_sync();
-          const uint32_t pb = smem_u32(smem + OFF_P + s * P_BYTES);
-          const uint32_t vb = smem_u32(smem + OFF_V + s * KV_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t a = sw128_desc(pb + kk * 32, 16, 1024);
-            const uint64_t b = sw128_desc(vb + kk * 16 * 128, BN * 128, 1024);
-            mma_bf16_ss(tmem + O_COL, a, b, idPV, jj > 0 || kk > 0);
-          }
-          mma_commit(&bar[PV_DONE + s]);
-          mma_commit(&bar[V_EMPTY + s]);
+          mbar_arrive_expect_tx(&bar[V_FULL + c], SLOT);
+          for (int db = 0; db < 4; ++db)
+            tma_load_3d(smem + OFF_V + c * SLOT + db * 4096, &tmV, &bar[V_FULL + c], db * 64,
+                        kr + c * 32, kvh);
         }
       }
     }
     __syncwarp();
-  } else if (warp < 4) {  // -------------------------------------- softmax
-    const int row = threadIdx.x;  // 0..127 = TMEM lane
-    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+  } else if (warp == kMmaWarp) {  // ------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idPV = idesc_bf16(BM, HDIM, false, true);
+      const uint32_t qb = smem_u32(smem + OFF_Q), kb = smem_u32(smem + OFF_K),
+                     vb = smem_u32(smem + OFF_V);
+      // S_j = Q K_j^T (M128 N128 K256) into TMEM buffer j % 2; that buffer
+      // held P_{j-2}, so PV_{j-2} must have completed
+      auto issue_s = [&](int j) -> bool {
+        const int sb = j & 1;
+        if (j >= 2 && !wait(PV_DONE + sb, ((j - 2) >> 1) & 1)) return false;
+        for (int b = 0; b < NSLOT; ++b) {
+          if (!wait(K_FULL + b, j & 1)) return false;
+          fence_after_sync();
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const uint64_t a = sw128_desc(qb + b * SLOT + k4 * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(kb + b * SLOT + k4 * 32, 16, 1024);
+            mma_bf16_ss(tmem + S_COL + sb * BN, a, bd, idS, b > 0 || k4 > 0);
+          }
+          mma_commit(&bar[K_EMPTY + b]);
+        }
+        mma_commit(&bar[S_FULL + sb]);
+        return true;
+      };
+      // order S_0, S_1, then PV_j followed by S_{j+2}
+      bool ok = wait(Q_FULL, 0);
+      for (int j = 0; ok && j < ntiles && j < 2; ++j) ok = issue_s(j);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int sb = j & 1;
+        if (!wait(P_FULL + sb, (j >> 1) & 1)) break;
+        fence_after_sync();
+        // O += P_j V_j: P from TMEM (8 columns per 16 keys), V slot c holds
+        // keys 32c.. (column blocks 4096 B apart)
+        for (int c = 0; c < NSLOT; ++c) {
+          if (!wait(V_FULL + c, j & 1)) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+#pragma unroll
+          for (int k2 = 0; k2 < 2; ++k2) {
+            const int kk = c * 2 + k2;
+            const uint64_t bd = sw128_desc(vb + c * SLOT + k2 * 2048, 4096, 1024);
+            mma_bf16_ts(tmem + O_COL, tmem + S_COL + sb * BN + kk * 8, bd, idPV, j > 0 || kk > 0);
+          }
+          mma_commit(&bar[V_EMPTY + c]);
+        }
+        if (!ok) break;
+        mma_commit(&bar[PV_DONE + sb]);
+        if (j + 2 < ntiles) ok = issue_s(j + 2);
+      }
+    }
+    __syncwarp();
+  } else {  // ------------------------------------------ softmax (warps 0-7)
+    // warps q and q + 4 own rows 32q .. 32q + 31 (TMEM lanes), warp q the
+    // keys 0-63 of each tile, warp q + 4 the keys 64-127; the row max is
+    // exchanged through shared memory each tile, the row sum at the end
+    const int q4 = warp & 3, hc = warp >> 2;
+    const int row = q4 * 32 + lane;
+    const uint32_t tl = tmem + (uint32_t(q4 * 32) << 16);
     const int qpos = qlo + row;
+    if (CP && p.merge && hc == 1) {
+      // bring this tile's accumulator (128 KB, 1024 lines) into L2 for the merge
+      const char* a = reinterpret_cast<const char*>(
+          p.acc + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM));
+      for (int ln = threadIdx.x - 128; ln < HDIM * BM * 4 / 128; ln += 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a + size_t(ln) * 128));
+    }
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      const int s = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      ok = __all_sync(0xFFFFFFFFu, wait(S_FULL + s, ph) && ok);
+      const int sb = j & 1;
+      ok = __all_sync(0xFFFFFFFFu, wait(S_FULL + sb, (j >> 1) & 1) && ok);
       fence_after_sync();
       uint32_t ra[32], rb[32];
-      tmem_ld32(tl + S_COL + s * BN, ra);
-      tmem_ld32(tl + S_COL + s * BN + 32, rb);
+      tmem_ld32(tl + S_COL + sb * BN + hc * 64, ra);
+      tmem_ld32(tl + S_COL + sb * BN + hc * 64 + 32, rb);
       tmem_wait_ld();
       fence_before_sync();
-      mbar_arrive(&bar[S_EMPTY + s]);
       // key positions kb.. of this tile; keys from klen on lie past the
       // segment (one segment starting at position 0 outside CP hops)
       int kb = j * BN, klen = BN;
@@ -266,6 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         kb = (s1 ? p.kpos1 : p.kpos0) + t * BN;
         klen = p.chunk - t * BN;
       }
+      const int kh0 = kb + hc * 64, klh = klen - hc * 64;  // this thread's 64 keys
       float v[64];
       float m8[8];
 #pragma unroll
@@ -280,16 +342,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          v[c] = (kb + c <= qpos && (!CP || c < klen)) ? __uint_as_float(ra[c]) * p.scale_log2
+          v[c] = (kh0 + c <= qpos && (!CP || c < klh)) ? __uint_as_float(ra[c]) * p.scale_log2
                                                        : -INFINITY;
-          v[32 + c] = (kb + 32 + c <= qpos && (!CP || 32 + c < klen))
+          v[32 + c] = (kh0 + 32 + c <= qpos && (!CP || 32 + c < klh))
                           ? __uint_as_float(rb[c]) * p.scale_log2
                           : -INFINITY;
           m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
         }
       }
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      // the other half's maximum (and one shared decision to stop); the
+      // barrier also orders both threads' S reads before either writes P
+      // over them
+      xmax[((j & 1) * 2 + hc) * BM + row] = mx;
+      ok = pair_sync_and(q4, ok);
+      fence_after_sync();
+      if (!ok) break;
+      mx = fmaxf(mx, xmax[((j & 1) * 2 + (hc ^ 1)) * BM + row]);
       const float m_new = fmaxf(m, mx);
       float factor = 1.f;
       bool resc = false;
@@ -300,28 +370,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         resc = true;
       }
       if (__any_sync(0xFFFFFFFFu, resc)) {
-        // O holds PV_0 .. PV_{j-1}; the last of them may still be running
+        // O holds PV_0 .. PV_{j-1}; the last of them may still be running.
+        // Each thread rescales its half of the row's 256 columns.
         const int jp = j - 1;
         ok = __all_sync(0xFFFFFFFFu, wait(PV_DONE + (jp & 1), (jp >> 1) & 1) && ok);
         fence_after_sync();
 #pragma unroll 1
-        for (int c = 0; c < HDIM / 32; ++c) {
+        for (int c = 0; c < HDIM / 64; ++c) {
           uint32_t r[32];
-          tmem_ld32(tl + O_COL + c * 32, r);
+          tmem_ld32(tl + O_COL + hc * 128 + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          tmem_st32(tl + O_COL + c * 32, r);
+          tmem_st32(tl + O_COL + hc * 128 + c * 32, r);
         }
         tmem_wait_st();
-        fence_before_sync();
         if (resc) {
           l *= factor;
           m = m_new;
         }
       }
-      // P_j goes to buffer s, which PV_{j-2} read
-      if (j >= 2) ok = __all_sync(0xFFFFFFFFu, wait(PV_DONE + s, ph ^ 1) && ok);
+      // P_j = 2^(s - m) in bf16 over the first 64 columns of S_j: keys
+      // 64 hc .. + 63 go to columns 32 hc .. + 31, two keys per column
       float s8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) s8[i] = 0.f;
@@ -333,52 +403,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[c] = pack_bf16x2(p0, p1);
       }
       l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
-      uint8_t* prow = smem + OFF_P + s * P_BYTES + row * 128;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-      fence_proxy_async_smem();
-      mbar_arrive(&bar[P_FULL + s]);
-      if (!ok) break;
+      tmem_st32(tl + S_COL + sb * BN + hc * 32, pk);
+      tmem_wait_st();
+      fence_before_sync();
+      mbar_arrive(&bar[P_FULL + sb]);
     }
-    if constexpr (CP) {
-      // log-sum-exp merge of (m, l) with what earlier hops left; O and l of
-      // this hop are relative to m (a max that may be stale by < 2^8)
-      const size_t units = size_t(p.heads) * p.n_qtiles;
-      float2* ml = reinterpret_cast<float2*>(p.acc + units * (size_t(HDIM) * BM)) +
-                   (size_t(h) * p.n_qtiles + qt) * BM + row;
-      float wa = 0.f, wb = 1.f, mo = m, lo = l;
-      if (p.merge) {
-        const float2 a = *ml;
-        mo = fmaxf(a.x, m);
-        if (mo == -INFINITY) {
-          wb = 0.f;
-          lo = 0.f;
-        } else {
-          wa = fast_exp2(a.x - mo);
-          wb = fast_exp2(m - mo);
-          lo = a.y * wa + l * wb;
-        }
-      }
-      if (ok) *ml = make_float2(mo, lo);
-      inv_l[row] = wa;
-      w_hop[row] = wb;
-    } else {
-      inv_l[row] = l > 0.f ? 1.f / l : 0.f;
-    }
+    // the row sum of the two halves
+    xsum[hc * BM + row] = l;
     if (!ok) *abort_flag = 1;
+    epilogue_sync();
+    if (hc == 0) {
+      l += xsum[BM + row];
+      if constexpr (CP) {
+        // log-sum-exp merge of (m, l) with what earlier hops left; O and l of
+        // this hop are relative to m (a max that may be stale by < 2^8)
+        const size_t units = size_t(p.heads) * p.n_qtiles;
+        float2* ml = reinterpret_cast<float2*>(p.acc + units * (size_t(HDIM) * BM)) +
+                     (size_t(h) * p.n_qtiles + qt) * BM + row;
+        float wa = 0.f, wb = 1.f, mo = m, lo = l;
+        if (p.merge) {
+          const float2 a = *ml;
+          mo = fmaxf(a.x, m);
+          if (mo == -INFINITY) {
+            wb = 0.f;
+            lo = 0.f;
+          } else {
+            wa = fast_exp2(a.x - mo);
+            wb = fast_exp2(m - mo);
+            lo = a.y * wa + l * wb;
+          }
+        }
+        if (ok && !*abort_flag) *ml = make_float2(mo, lo);
+        inv_l[row] = wa;
+        w_hop[row] = wb;
+      } else {
+        inv_l[row] = l > 0.f ? 1.f / l : 0.f;
+      }
+    }
   }
 
   if (warp < 8) {  // ------------------------------- epilogue (warps 0-7)
-    if (CP && p.merge && warp >= 4) {
-      // warps 4-7 idle through the main loop: bring this tile's accumulator
-      // (128 KB, 1024 lines) into L2 so the merge below reads it from there
-      const char* a = reinterpret_cast<const char*>(
-          p.acc + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM));
-      for (int ln = threadIdx.x - 128; ln < HDIM * BM * 4 / 128; ln += 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(a + size_t(ln) * 128));
-    }
     epilogue_sync();  // inv_l written
     const int jl = ntiles - 1;
     bool ok = wait(PV_DONE + (jl & 1), (jl >> 1) & 1);
@@ -479,11 +543,12 @@ cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   const cuuint32_t qbox[2] = {64, BM};
   const cuuint64_t kd[3] = {cuuint64_t(HDIM), cuuint64_t(kv_rows), cuuint64_t(L.hkv)};
   const cuuint64_t ks[2] = {cuuint64_t(HDIM) * 2, cuuint64_t(L.kv_stride) * 2};
-  const cuuint32_t kbox[3] = {64, BN, 1};
+  const cuuint32_t kbox[3] = {64, BN, 1};  // one K slot: 128 keys of one column block
+  const cuuint32_t vbox[3] = {64, 32, 1};  // a quarter of a V slot: 32 keys of one column block
   const cuuint64_t od[2] = {cuuint64_t(L.out_row), cuuint64_t(L.rows)};
   const cuuint64_t os[1] = {cuuint64_t(L.out_row) * 2};
   if (!encode_bf16(&tq, L.q, 2, qd, qs, qbox) || !encode_bf16(&tk, L.keys, 3, kd, ks, kbox) ||
-      !encode_bf16(&tv, L.values, 3, kd, ks, kbox))
+      !encode_bf16(&tv, L.values, 3, kd, ks, vbox))
     return cudaErrorInvalidValue;
   if (L.cp) {
     to = tq;  // no output store on a hop

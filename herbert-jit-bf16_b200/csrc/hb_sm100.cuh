@@ -117,6 +117,19 @@ HB_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 
+// One column, 32 lanes x 32 bits: thread t of the warp reads / writes lane
+// (base lane + t) of column `taddr`.
+HB_DEV void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v)
+               : "memory");
+}
+HB_DEV uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t v;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v) : "r"(taddr)
+               : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------------- MMA
 
 // K-major or MN-major operand, 128-byte swizzle, as TMA SWIZZLE_128B writes
@@ -144,6 +157,18 @@ HB_DEV void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint3
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(uint32_t(accumulate))
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]: A (M rows = lanes, K 16-bit elements
+// packed two per 32-bit column, the lower half the even element) is read
+// from Tensor Memory; issued by one thread.
+HB_DEV void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                        bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(uint32_t(accumulate))
       : "memory");
 }
 
