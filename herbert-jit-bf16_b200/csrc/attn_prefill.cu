@@ -486,25 +486,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(tq + O_COL + col0, o);
       tmem_wait_ld();
       const int cb = col0 >> 6, c16 = (col0 & 63) >> 3;
+      int phys[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int phys = cb * (BM * 128) + rl * 128 + (((c16 + k) ^ (rl & 7)) << 4);
-        uint4 gv = make_uint4(0, 0, 0, 0);
-        if (p.gate_offset >= 0) gv = *reinterpret_cast<const uint4*>(smem + OFF_K + phys);
-        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w};
-        uint32_t w[4];
+      for (int k = 0; k < 4; ++k)
+        phys[k] = cb * (BM * 128) + rl * 128 + (((c16 + k) ^ (rl & 7)) << 4);
+      // a = bf16(O / l), then the gate y = bf16(a / (1 + exp(-g))) for 32
+      // columns at once: SFU quotients, the rare ones that may round
+      // differently recomputed with the correctly rounded division
+      uint32_t aw[16];  // a, two bf16 per word
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint16_t a0 = f32_to_bf16_cvtne(__uint_as_float(o[k * 8 + 2 * i]) * inv);
-          uint16_t a1 = f32_to_bf16_cvtne(__uint_as_float(o[k * 8 + 2 * i + 1]) * inv);
-          if (p.gate_offset >= 0) {
-            a0 = gate_bf16(a0, uint16_t(gw[i] & 0xFFFFu));
-            a1 = gate_bf16(a1, uint16_t(gw[i] >> 16));
-          }
-          w[i] = uint32_t(a0) | (uint32_t(a1) << 16);
-        }
-        *reinterpret_cast<uint4*>(smem + OFF_V + phys) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int i = 0; i < 16; ++i) {
+        const uint64_t ov =
+            f2mul(f2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), f2(inv, inv));
+        aw[i] = bf16x2_cvtne(f2lo(ov), f2hi(ov));
       }
+      uint32_t w[16];
+      if (p.gate_offset >= 0) {
+        uint32_t gw[16];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 gv = *reinterpret_cast<const uint4*>(smem + OFF_K + phys[k]);
+          gw[4 * k] = gv.x; gw[4 * k + 1] = gv.y; gw[4 * k + 2] = gv.z; gw[4 * k + 3] = gv.w;
+        }
+        float qv[32];
+        uint32_t risky = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint64_t d2 = gate_divisor2(gw[i]);
+          bool r0, r1;
+          qv[2 * i] = gate_quotient_fast(bf16lo(aw[i]), f2lo(d2), r0);
+          qv[2 * i + 1] = gate_quotient_fast(bf16hi(aw[i]), f2hi(d2), r1);
+          risky |= (uint32_t(r0) << (2 * i)) | (uint32_t(r1) << (2 * i + 1));
+        }
+        if (risky) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if ((risky >> i) & 1u) {
+              const uint32_t a_bits = i & 1 ? aw[i >> 1] >> 16 : aw[i >> 1] & 0xFFFFu;
+              const uint16_t g = uint16_t(i & 1 ? gw[i >> 1] >> 16 : gw[i >> 1] & 0xFFFFu);
+              qv[i] = __fdiv_rn(bf16_to_f32(uint16_t(a_bits)), gate_divisor(g));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = bf16x2_cvtne(qv[2 * i], qv[2 * i + 1]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = aw[i];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        *reinterpret_cast<uint4*>(smem + OFF_V + phys[k]) =
+            make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
     }
     fence_proxy_async_smem();
     epilogue_sync();  // the output tile is staged

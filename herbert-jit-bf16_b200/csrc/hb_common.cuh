@@ -63,6 +63,101 @@ HB_DEV uint16_t gate_bf16(uint16_t a_bits, uint16_t g_bits) {
   return f32_to_bf16_cvtne(__fdiv_rn(a, e));
 }
 
+// ------------------------------------------------ paired f32 arithmetic
+// sm_100 add/sub/mul/fma on two f32 lanes at once, each lane rounded to
+// nearest as the scalar instruction is: same bits, half the instructions.
+// A paired multiply whose result feeds a paired add or subtract may be
+// fused into one rounding by the assembler (measured: it was), so products
+// that must round on their own stay on the scalar __fmul_rn.
+HB_DEV uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+HB_DEV float f2lo(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+HB_DEV float f2hi(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
+HB_DEV uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+HB_DEV uint64_t f2sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+HB_DEV uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+HB_DEV uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+// f32_to_bf16_cvtne on two values, packed (lo in the low half): the
+// hardware round-to-nearest-even conversion, then the reference's special
+// cases (zero/denormal inputs give a signed zero, NaN keeps its payload).
+HB_DEV uint32_t bf16x2_cvtne(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  const uint32_t ul = __float_as_uint(lo), uh = __float_as_uint(hi);
+  const uint32_t el = ul & 0x7F800000u, eh = uh & 0x7F800000u;
+  uint32_t rl = r & 0xFFFFu, rh = r >> 16;
+  rl = el == 0u ? (ul >> 16) & 0x8000u : rl;
+  rh = eh == 0u ? (uh >> 16) & 0x8000u : rh;
+  rl = (el == 0x7F800000u && (ul & 0x7FFFFFu)) ? (ul >> 16) | 0x40u : rl;
+  rh = (eh == 0x7F800000u && (uh & 0x7FFFFFu)) ? (uh >> 16) | 0x40u : rh;
+  return rl | (rh << 16);
+}
+
+// gate_divisor of the two bf16 gate values in `gw` (lo, hi), with the
+// polynomial steps on paired lanes.
+HB_DEV uint64_t gate_divisor2(uint32_t gw) {
+  const uint64_t u = f2(__uint_as_float(gw << 16), __uint_as_float(gw & 0xFFFF0000u));
+  const uint64_t neg = f2sub(f2(0.0f, 0.0f), u);
+  float x0 = fminf(f2lo(neg), 88.0f), x1 = fminf(f2hi(neg), 88.0f);
+  x0 = fmaxf(x0, -87.33654f);
+  x1 = fmaxf(x1, -87.33654f);
+  uint64_t t1 = f2(__fmul_rn(x0, 1.442695f), __fmul_rn(x1, 1.442695f));
+  const uint64_t big = f2add(t1, f2(12582912.0f, 12582912.0f));
+  const uint64_t t2 = f2sub(big, f2(12582912.0f, 12582912.0f));
+  t1 = f2sub(t1, t2);
+  uint64_t p = f2fma(f2(0.00967248f, 0.00967248f), t1, f2(0.05550411f, 0.05550411f));
+  p = f2fma(p, t1, f2(0.2402265f, 0.2402265f));
+  p = f2fma(p, t1, f2(0.6931472f, 0.6931472f));
+  p = f2fma(p, t1, f2(1.0f, 1.0f));
+  const uint32_t r0 = uint32_t(int32_t(uint32_t(big)) - 0x4B400000);
+  const uint32_t r1 = uint32_t(int32_t(uint32_t(big >> 32)) - 0x4B400000);
+  const float e0 = __fmul_rn(f2lo(p), __uint_as_float((r0 << 23) + 0x3F800000u));
+  const float e1 = __fmul_rn(f2hi(p), __uint_as_float((r1 << 23) + 0x3F800000u));
+  return f2(__fadd_rn(e0, 1.0f), __fadd_rn(e1, 1.0f));
+}
+
+// The gate's divisor 1 + exp(-b) with the SigmoidMul arm's steps.
+HB_DEV float gate_divisor(uint16_t g_bits) {
+  const float e = fminf(__fsub_rn(0.0f, bf16_to_f32(g_bits)), 88.0f);  // 88 also for NaN
+  return __fadd_rn(exp_poly(e), 1.0f);
+}
+
+// a / d for d >= 1 through the SFU reciprocal, and whether that quotient
+// may round to a different bf16 than the correctly rounded one: the
+// reciprocal is off by a few f32 ulps at most, so the bf16 rounding can
+// only differ when the quotient's low 16 bits lie within 32 ulps of the
+// half-way point 0x8000, or when the quotient is near the smallest normal
+// (denormals flush to zero in the conversion).  Callers recompute those
+// rare quotients with the correctly rounded division.
+HB_DEV float gate_quotient_fast(float a, float d, bool& risky) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  const float q = __fmul_rn(a, r);
+  const uint32_t qb = __float_as_uint(q);
+  risky = ((qb & 0xFFFFu) - 0x7FE0u) <= 0x40u || (qb & 0x7F000000u) == 0u;
+  return q;
+}
+
 // 2^x with the SFU (ex2.approx.ftz): -inf -> +0.
 HB_DEV float fast_exp2(float x) {
   float y;
