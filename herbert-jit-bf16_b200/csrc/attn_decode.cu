@@ -27,6 +27,13 @@
 // workspace and the last CTA of the unit to arrive (atomic counter, reset
 // after use) merges the partials, rounds to bf16 and applies the gate with
 // the reference's own exp polynomial and rounding steps.
+//
+// Short sequences (one call, at most 16 splits of <= 256 positions) take
+// the cluster form instead: the splits of a unit are one thread-block
+// cluster, each CTA leaves its partial in its own shared memory, and after
+// a cluster barrier CTA r merges output slice r from all the partials
+// through distributed shared memory -- no global partials, no atomics, and
+// the merge is spread over the cluster instead of one last CTA.
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -86,6 +93,33 @@ struct DecodeParams {
   float* partials;            // [unit][split][G*HD + 2G]
 };
 
+// ------------------------------------------------ cluster shared memory
+HB_DEV uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+HB_DEV float dsmem_ld(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+// (not volatile: the reads of one merge are independent and overlap; the
+// cluster barrier before them orders them after the peers' writes)
+HB_DEV float4 dsmem_ld4(uint32_t addr) {
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"(addr));
+  return v;
+}
+// Every thread of every CTA of the cluster (hardware barrier: each path
+// through the kernel reaches it exactly as often).
+HB_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+
 template <int HD>
 struct LaneVec;
 template <>
@@ -135,7 +169,7 @@ HB_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarp
 template <int HD>
 struct Ring { static constexpr int stages = kRingBytes / (2 * kTile * HD * 2); };
 
-template <int HD, int G>
+template <int HD, int G, bool CL>
 __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodeParams p) {
   constexpr int kStages = Ring<HD>::stages;
   constexpr int DPL = HD / 32;             // dims per lane
@@ -160,8 +194,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
   const hb_decode_seq d = p.seqs ? p.seqs[seq] : p.one;
   const int64_t n = d.past + row + 1;  // keys visible to this row
   const int64_t p0 = int64_t(split) * p.chunk;
-  if (p0 >= n) return;  // beyond this unit's last split: not counted
-  const int64_t p1 = min(n, p0 + p.chunk);
+  // beyond this unit's last split: not counted (a cluster CTA still merges
+  // its output slice, with an empty partial)
+  if (!CL && p0 >= n) return;
+  const int64_t p1 = max(p0, min(n, p0 + p.chunk));
   const int active = int((n + p.chunk - 1) / p.chunk);
   const int ntiles = int((p1 - p0 + kTile - 1) / kTile);
   const uint16_t* kbase = d.keys + int64_t(kh) * d.kv_stride;
@@ -179,8 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
   }
   __syncthreads();
 
-  if (((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(vbase) |
-        reinterpret_cast<uintptr_t>(d.q) | reinterpret_cast<uintptr_t>(d.output)) & 15) != 0) {
+  if (!CL && ((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(vbase) |
+               reinterpret_cast<uintptr_t>(d.q) | reinterpret_cast<uintptr_t>(d.output)) & 15) != 0) {
     if (threadIdx.x == 0) record_status(p.status, kStatusArg);
     return;
   }
@@ -201,26 +237,46 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
         bulk_g2s(vs + s * TILE_ELEMS, vbase + pos * HD, bytes, &full[s]);
       }
     }
+    if constexpr (CL) {  // the producer warp takes part in both cluster barriers
+      __syncwarp();
+      cluster_sync_all();
+      cluster_sync_all();
+    }
     return;
   }
 
   // ------------------------------------------------------------ consumers
   const int h0 = kh * G;  // first query head of the group
   const uint16_t* qrow = d.q + int64_t(row) * p.q_row;
-  float q[G][DPL];
+  // q and the accumulators as paired f32 lanes (dims 2k, 2k+1): one
+  // paired FMA per two products
+  constexpr int DP2 = DPL / 2;
+  uint64_t q2[G][DP2];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     float t[DPL];
     LaneVec<HD>::load(qrow + int64_t(h0 + g) * p.q_head + lane * DPL, t);
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) q[g][i] = t[i];
+    for (int k = 0; k < DP2; ++k) q2[g][k] = f2(t[2 * k], t[2 * k + 1]);
   }
-  float o[G][DPL];
+  uint64_t o2[G][DP2];
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) o[g][i] = 0.f;
+    for (int k = 0; k < DP2; ++k) o2[g][k] = f2(0.f, 0.f);
   float m_own = -INFINITY, l_own = 0.f;  // state of value head (lane >> SH) >> 2
+  // cluster form: the gate values of this thread's output quad, fetched now
+  // so that the final merge does not wait on them
+  uint2 gate_pre = make_uint2(0u, 0u);
+  if (CL && p.gate_offset >= 0) {
+    constexpr int Q4 = G * HD / 4;
+    const int ns = p.nsplit, qb = split * Q4 / ns, qe = (split + 1) * Q4 / ns;
+    const int tid0 = threadIdx.x;
+    if (tid0 < qe - qb) {
+      const int e = (qb + tid0) * 4, g = e / HD, dd = e % HD;
+      gate_pre = *reinterpret_cast<const uint2*>(qrow + p.gate_offset + int64_t(h0 + g) * HD + dd);
+    }
+  }
 
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % kStages;
@@ -237,20 +293,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
       const uint16_t* kt = ks + s * TILE_ELEMS + base * HD + lane * DPL;
       const uint16_t* vt = vs + s * TILE_ELEMS + base * HD + lane * DPL;
       float part[NV];
+      // all four rows are read whatever vc is (the reads stay inside the
+      // ring), so the loads issue together; a dot of a row past vc only
+      // reaches its own slot, which the mask below sets to -inf
+      float kxa[4][DPL];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) LaneVec<HD>::load(kt + j * HD, kxa[j]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float kx[DPL];
-        if (j < vc) LaneVec<HD>::load(kt + j * HD, kx);
-        else {
+        const float (&kx)[DPL] = kxa[j];
+        uint64_t k2[DP2];
 #pragma unroll
-          for (int i = 0; i < DPL; ++i) kx[i] = 0.f;
-        }
+        for (int k = 0; k < DP2; ++k) k2[k] = f2(kx[2 * k], kx[2 * k + 1]);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          float acc = 0.f;
+          uint64_t acc = f2mul(q2[g][0], k2[0]);
 #pragma unroll
-          for (int i = 0; i < DPL; ++i) acc = fmaf(q[g][i], kx[i], acc);
-          part[g * 4 + j] = acc;
+          for (int k = 1; k < DP2; ++k) acc = f2fma(q2[g][k], k2[k], acc);
+          part[g * 4 + j] = f2lo(acc) + f2hi(acc);
         }
       }
       const float dot = transpose_reduce<NV>(part, lane);
@@ -270,26 +330,41 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float cg = __shfl_sync(kFull, corr, (g * 4) << SH);
+        const uint64_t cg2 = f2(cg, cg);
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) o[g][i] *= cg;
+        for (int k = 0; k < DP2; ++k) o2[g][k] = f2mul(o2[g][k], cg2);
       }
+      float vxa[4][DPL];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) LaneVec<HD>::load(vt + j * HD, vxa[j]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (j < vc) {
-          float vx[DPL];
-          LaneVec<HD>::load(vt + j * HD, vx);
+        // rows past vc may hold any bits (even NaN): zero them, p is 0 there
+        uint64_t v2[DP2];
 #pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float pg = __shfl_sync(kFull, pr, (g * 4 + j) << SH);
+        for (int k = 0; k < DP2; ++k)
+          v2[k] = j < vc ? f2(vxa[j][2 * k], vxa[j][2 * k + 1]) : f2(0.f, 0.f);
 #pragma unroll
-            for (int i = 0; i < DPL; ++i) o[g][i] = fmaf(pg, vx[i], o[g][i]);
-          }
+        for (int g = 0; g < G; ++g) {
+          const float pg = __shfl_sync(kFull, pr, (g * 4 + j) << SH);
+          const uint64_t pg2 = f2(pg, pg);
+#pragma unroll
+          for (int k = 0; k < DP2; ++k) o2[g][k] = f2fma(pg2, v2[k], o2[g][k]);
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
+
+  float o[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int k = 0; k < DP2; ++k) {
+      o[g][2 * k] = f2lo(o2[g][k]);
+      o[g][2 * k + 1] = f2hi(o2[g][k]);
+    }
 
   // ------------------------------------------ merge the 8 warp states (smem)
   consumer_sync();  // every warp is done reading the ring
@@ -329,6 +404,86 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
       Os += ws[w * PSTRIDE + e] * f;
     }
     om[k] = M; ol[k] = Ls; oo[k] = Os;
+  }
+
+  if constexpr (CL) {
+    // this CTA's partial stays in its shared memory for the cluster merge
+    float* cpart = reinterpret_cast<float*>(smem_raw + (MERGE_BYTES + 15) / 16 * 16);
+#pragma unroll
+    for (int k = 0; k < PER_T; ++k) {
+      const int e = tid + k * kConsumerWarps * 32, g = e / HD;
+      if (e >= NOUT) break;
+      cpart[e] = oo[k];
+      if ((e % HD) == 0) {
+        cpart[G * HD + g] = om[k];
+        cpart[G * HD + G + g] = ol[k];
+      }
+    }
+    cluster_sync_all();
+    // output slice of this CTA: quads [split * Q / ns, (split + 1) * Q / ns)
+    const int ns = p.nsplit;
+    float* sml = ws;                 // [ns][2G]: m then l of every split
+    float* smw = ws + ns * 2 * G;    // [ns][G]: exp2(m_s - M)
+    float* smL = smw + ns * G;       // [G]
+    for (int i = tid; i < ns * 2 * G; i += kConsumerWarps * 32)
+      sml[i] = dsmem_ld(dsmem_addr(cpart + G * HD + (i % (2 * G)), uint32_t(i / (2 * G))));
+    consumer_sync();
+    if (tid < G) {
+      float M = -INFINITY;
+      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, sml[sp * 2 * G + tid]);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float Ls = 0.f;
+      for (int sp = 0; sp < ns; ++sp) {
+        const float w = fast_exp2(sml[sp * 2 * G + tid] - Mu);
+        smw[sp * G + tid] = w;
+        Ls += sml[sp * 2 * G + G + tid] * w;
+      }
+      smL[tid] = Ls;
+    }
+    consumer_sync();
+    constexpr int Q4 = NOUT / 4;
+    const int qb = split * Q4 / ns, qe = (split + 1) * Q4 / ns, nq = qe - qb;
+    // one 16-byte read per (output quad, split), all in flight at once, then
+    // the splits of each quad summed through shared memory
+    float4* red = reinterpret_cast<float4*>(smL + G + 3) ;  // [ns][nq], 16-byte aligned below
+    red = reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(red) + 15) & ~uintptr_t(15));
+    for (int idx = tid; idx < nq * ns; idx += kConsumerWarps * 32) {
+      const int sp = idx / nq, qi = idx % nq, e = (qb + qi) * 4, g = e / HD;
+      const float4 v = dsmem_ld4(dsmem_addr(cpart + e, uint32_t(sp)));
+      const float w = smw[sp * G + g];
+      red[idx] = make_float4(w * v.x, w * v.y, w * v.z, w * v.w);
+    }
+    consumer_sync();
+    uint16_t* orow_c = d.output + int64_t(row) * p.out_row;
+    for (int qi = tid; qi < nq; qi += kConsumerWarps * 32) {
+      const int e = (qb + qi) * 4, g = e / HD, dd = e % HD, hq = h0 + g;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < ns; ++sp) {
+        const float4 v = red[sp * nq + qi];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const float Ls = smL[g];
+      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+      uint16_t a[4] = {f32_to_bf16_cvtne(acc.x * inv), f32_to_bf16_cvtne(acc.y * inv),
+                       f32_to_bf16_cvtne(acc.z * inv), f32_to_bf16_cvtne(acc.w * inv)};
+      if (p.gate_offset >= 0) {
+        // fetched at the start when this thread owns the quad (nq <= 256)
+        const uint2 gw = qi == tid ? gate_pre
+                                   : *reinterpret_cast<const uint2*>(qrow + p.gate_offset +
+                                                                     int64_t(hq) * HD + dd);
+        a[0] = gate_bf16(a[0], uint16_t(gw.x & 0xFFFFu));
+        a[1] = gate_bf16(a[1], uint16_t(gw.x >> 16));
+        a[2] = gate_bf16(a[2], uint16_t(gw.y & 0xFFFFu));
+        a[3] = gate_bf16(a[3], uint16_t(gw.y >> 16));
+      }
+      *reinterpret_cast<uint2*>(orow_c + int64_t(hq) * HD + dd) =
+          make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
+    }
+    cluster_sync_all();  // the peers are done reading this CTA's partial
+    return;
   }
 
   if (active > 1) {
@@ -432,17 +587,85 @@ size_t smem_bytes() {
   return body + 2 * kStages * sizeof(uint64_t) + 16;
 }
 
+// Largest cluster (16 with non-portable sizes, else 8) that the device can
+// co-schedule for this kernel, or 0; probed once per device.
 template <int HD, int G>
-cudaError_t launch(const DecodeParams& p, int units_z, cudaStream_t st) {
+int cluster_limit(size_t smem) {
+  static int cache[64];
+  static DeviceFlags probed;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  cudaError_t e = probed.once([&] {
+    int best = 0;
+    for (int c : {16, 8}) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(c, 1, 1);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = c;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel<HD, G, true>, &cfg) == cudaSuccess &&
+          n >= 1) {
+        best = c;
+        break;
+      }
+      cudaGetLastError();  // a refused size is not an error of this call
+    }
+    cache[dev] = best;
+    return cudaSuccess;
+  });
+  return e == cudaSuccess ? cache[dev] : 0;
+}
+
+template <int HD, int G>
+cudaError_t launch(DecodeParams p, int units_z, bool single, int64_t max_n, cudaStream_t st) {
   const size_t smem = smem_bytes<HD, G>();
-  static DeviceFlags configured;  // the attribute is set once per device
+  static DeviceFlags configured;  // the attributes are set once per device
   cudaError_t e = configured.once([&] {
-    return cudaFuncSetAttribute(attn_decode_kernel<HD, G>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaError_t r = cudaFuncSetAttribute(attn_decode_kernel<HD, G, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(attn_decode_kernel<HD, G, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(attn_decode_kernel<HD, G, true>,
+                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return r;
   });
   if (e != cudaSuccess) return e;
+  // one short sequence: splits of <= 256 positions merged inside a cluster
+  const int cmax = single ? cluster_limit<HD, G>(smem) : 0;
+  if (cmax > 1) {
+    int64_t c = (max_n + cmax - 1) / cmax;
+    c = (c + kTile - 1) / kTile * kTile;
+    if (c <= 256) {
+      p.chunk = int(c);
+      p.nsplit = int((max_n + c - 1) / c);
+      if (p.nsplit >= 2) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(p.nsplit, p.hkv, units_z);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = p.nsplit;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, G, true>, p);
+      }
+    }
+  }
   dim3 grid(p.nsplit, p.hkv, units_z);
-  attn_decode_kernel<HD, G><<<grid, kThreads, smem, st>>>(p);
+  attn_decode_kernel<HD, G, false><<<grid, kThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -485,8 +708,10 @@ cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st) {
   p.counters = L.counters;
   p.partials = L.partials;
   const int z = int(L.nseq * L.rows);
+  const bool single = L.seqs == nullptr && L.nseq == 1;
+  const int64_t max_n = L.one.past + L.rows;
 #define HB_DECODE_CASE(HD_, G_) \
-  if (L.head_dim == HD_ && L.gqa == G_) return launch<HD_, G_>(p, z, st);
+  if (L.head_dim == HD_ && L.gqa == G_) return launch<HD_, G_>(p, z, single, max_n, st);
   HB_DECODE_CASE(256, 1) HB_DECODE_CASE(256, 2) HB_DECODE_CASE(256, 4) HB_DECODE_CASE(256, 8)
   HB_DECODE_CASE(128, 1) HB_DECODE_CASE(128, 2) HB_DECODE_CASE(128, 4) HB_DECODE_CASE(128, 8)
 #undef HB_DECODE_CASE
