@@ -83,15 +83,13 @@ __global__ void __launch_bounds__(32)
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
-  // launched with programmatic stream serialization: everything above may
-  // overlap the previous kernel on the stream; nothing below reads memory
-  // before that kernel has completed
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" :::);
-  if (lane == 0) {
-    mbar_arrive_expect_tx(&bar, HKD * 32 * 4);
-    sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
-  }
+  // Launched with programmatic stream serialization.  This kernel is the
+  // only one that lets a successor start early, and it never writes qkv,
+  // beta or decay, so the first position's inputs are read (and
+  // L2-normalised) at once -- overlapping the previous step's tail when
+  // that step is this kernel; the state is touched only after
+  // griddepcontrol.wait, i.e. after the previous kernel completed, and the
+  // next step is released only then (one step in flight ahead, not a chain).
   bool loaded = false;
   float s[HKD];
 
@@ -124,6 +122,12 @@ __global__ void __launch_bounds__(32)
     }
     __syncwarp();
     if (!loaded) {  // the state tile (first position only)
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      asm volatile("griddepcontrol.launch_dependents;" :::);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bar, HKD * 32 * 4);
+        sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
+      }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar, 0))) {
         if (lane == 0) atomicExch(&g_gdn_decode_timeout, 1);
         mbar_wait(&bar, 0);  // a second bounded wait for the copy in flight
@@ -166,10 +170,7 @@ __global__ void __launch_bounds__(32)
     p.out[t * value + int64_t(h) * p.hvd + col] = o;
     __syncwarp();
   }
-  if (!loaded) {  // no position (the host refuses empty calls): leave the state as it is
-    mbar_wait(&bar, 0);
-    return;
-  }
+  if (!loaded) return;  // no position (the host refuses empty calls): state untouched
 #pragma unroll
   for (int kd = 0; kd < HKD; ++kd) st[kd * 32 + lane] = s[kd];
   sm100::fence_proxy_async_smem();
