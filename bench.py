@@ -48,9 +48,10 @@ L2_BYTES = 126 << 20
 # dram bytes (read + write) of one launch of the dominant kernel, from the
 # committed ncu summaries under profiles/: attn_prefill_s4096.md,
 # attn_decode_n2048.md, attn_decode_batch64.md (scaled from the n = 2048
-# capture by the bytes processed), gdn_prefill_decode_t4096.md (scan kernel).
-NCU_TRAFFIC = {"prefill": 93_318_912, "decode": 8_461_824, "gdn": 234_717_440,
-               "batch": 4_458_000_000, "cp": None}
+# capture by the bytes processed), gdn_prefill_decode_t4096.md (prep + scan,
+# one chunked prefill); cp: the 131072-token launch is too large to capture.
+NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_455_424, "gdn": 500_502_272,
+               "batch": 4_452_000_000, "cp": None}
 
 
 def peaks():
@@ -268,7 +269,7 @@ class GdnWorkload(Workload):
         self.ws = None
         self.work = T + steps
         self.units = "tok/s"
-        self.launches_per_step = 1 + steps
+        self.launches_per_step = 2 + steps  # prep + scan, then one kernel per decode step
         qkv, beta, decay, out = self.sets[0]
         self.h_in = [t.cpu().pin_memory() for t in (qkv, beta, decay)]
         self.h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
@@ -292,6 +293,27 @@ class GdnWorkload(Workload):
             d.copy_(h, non_blocking=True)
         self.step(0)
         self.h_out.copy_(out, non_blocking=True)
+
+    def kernel_probe(self, reps=5):
+        """(FLOPs, seconds) of one chunked prefill (prep + scan kernels), by
+        CUDA events on the launching stream."""
+        import torch
+        qkv, beta, decay, out = self.sets[0]
+        st = torch.cuda.current_stream()
+
+        def fn():
+            self.ws = self.hb.delta_recurrence(self.shape, self.state, out, qkv, beta, decay,
+                                               rows=self.T, regime="prefill", workspace=self.ws)
+        fn()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(st)
+        for _ in range(reps):
+            fn()
+        b.record(st)
+        torch.cuda.synchronize()
+        return gdn_prefill_flops(self.T), a.elapsed_time(b) / 1e3 / reps
 
     def describe(self):
         return {"workload": "GatedDeltaNet prefill then decode (BASELINE configs[2])",
@@ -549,15 +571,16 @@ def run_ours(args):
         pk = peaks()
         per_launch = wl.work
         kernel_s = t_dev / args.steps
-        if cfg == "gdn":
-            achieved = gdn_prefill_flops(wl.T) / kernel_s / 1e12
-            peak, unit = pk["bf16"], "TFLOP/s"
-        elif probe is not None:
+        # a dense kernel kept busy for half a second or more runs at the power
+        # cap: its denominator is the sustained GEMM figure, else the burst one
+        sustained = t_dev >= 0.5
+        bf16_peak = pk["bf16_sustained"] if sustained else pk["bf16"]
+        if probe is not None:
             achieved = probe[0] / probe[1] / 1e12
-            peak, unit = pk["bf16"], "TFLOP/s"
+            peak, unit = bf16_peak, "TFLOP/s"
         elif BOUND[cfg] == "tensor":
             achieved = per_launch / kernel_s / 1e12
-            peak, unit = pk["bf16"], "TFLOP/s"
+            peak, unit = bf16_peak, "TFLOP/s"
         else:
             achieved = per_launch / kernel_s / 1e9
             peak, unit = pk["hbm"], "GB/s"
@@ -585,7 +608,9 @@ def run_ours(args):
                         f"{args.steps} steps issued eagerly between CUDA events")),
             "roofline": {"bound": BOUND[cfg], "achieved": round(achieved, 3), "peak": peak,
                          "unit": unit, "frac": round(achieved / peak, 4),
-                         "peak_source": pk["source"] + (" burst" if unit == "TFLOP/s" else ""),
+                         "peak_source": pk["source"] + (
+                             ("" if unit != "TFLOP/s" else
+                              " sustained (timed region >= 0.5 s)" if sustained else " burst")),
                          "traffic": NCU_TRAFFIC.get(cfg)},
             "e2e": {"value": round(value_of(total_work, t_e2e / args.steps, wl.units), 4),
                     "unit": wl.units, "h2d_bytes_per_step": int(wl.h2d),
@@ -595,6 +620,8 @@ def run_ours(args):
         }
         if probe is not None:
             line["roofline"]["kernel"] = (
+                "gdn_prep_kernel + gdn_scan_kernel (one chunked prefill of T tokens)"
+                if cfg == "gdn" else
                 "attn_prefill_kernel over the whole sequence" if world == 1 else
                 "attn_prefill_kernel<CP> hop over the rank's own shard (hop 0)")
             line["roofline"]["launch_ms"] = round(probe[1] * 1e3, 4)
