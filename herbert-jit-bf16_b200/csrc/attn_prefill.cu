@@ -8,27 +8,31 @@
 // Row r of the call is the query at absolute position past + r and sees keys
 // [0, past + r] (src/jit/target/x86/execution/attention.rs:189-196).
 //
-// CTA = one tile of 128 query rows of one query head (head_dim 256):
-//   warp 8       TMA producer: Q tile once, then K and V tiles of 64 keys
-//                into two-stage rings (SWIZZLE_128B, no multicast);
-//   warp 9       MMA issuer: S_j = Q K_j^T (M128 N64 K256, 16 MMAs) into one
-//                of three TMEM S buffers, O += P_j V_j (M128 N256 K64, 4 MMAs,
-//                V read MN-major) into the TMEM O accumulator, issued in the
-//                order PV_j, S_{j+2} so S runs two tiles ahead of the softmax;
-//                each group is committed to an mbarrier;
-//   warps 0-7    softmax: two threads per query row (warps q and q+4 share
-//                TMEM lanes 32q.., each takes 32 of a tile's 64 keys) read S
-//                from TMEM, apply the causal mask, exchange their partial row
-//                maxima through TMEM, keep the running max m and sum l in the
-//                log2 domain, write P = 2^(s - m) as bf16 into shared memory
-//                in the UMMA K-major swizzled layout, and rescale the O row in
-//                TMEM only when the max grows by more than 2^8;
-//   warps 0-7    epilogue: O / l, bf16, gate with the reference's exp
-//                polynomial and rounding steps; the gate tile comes in by TMA
-//                (into the K ring, free once the last S is computed) and the
-//                output tile leaves by TMA store (staged in the V ring).
-// TMEM: S buffers at columns [0,192), O at [256,512) of a 512-column
-// allocation.  Shared memory: Q 64 KB + K 2x32 KB + V 2x32 KB + P 2x16 KB.
+// CTA = one tile of 128 query rows of one query head (head_dim 256), 320
+// threads:
+//   warp 8       TMA producers (no multicast, SWIZZLE_128B): lane 0 loads
+//                the Q tile, then the K slots (a ring of four 16 KB slots,
+//                slot b = column block b of a 128-key tile) and finally the
+//                gate tile into the K ring; lane 1 loads the V slots (four
+//                16 KB slots of 32 keys x 256 dims);
+//   warp 9       MMA issuer: S_j = Q K_j^T (M128 N128 K256) into TMEM S
+//                buffer j % 2; O += P_j V_j (M128 N256 K128) with P_j taken
+//                from TMEM (the TS form) and V MN-major from shared memory;
+//                issue order S_0, S_1, then PV_j, S_{j+2}, S_{j+2} waiting
+//                for PV_j to free its buffer; every group committed to an
+//                mbarrier that also frees the ring slots it read;
+//   warps 0-7    softmax: warps q and q+4 own TMEM lanes 32q.. (one query
+//                row per thread), each half of a tile's 128 keys; the row
+//                maxima meet through shared memory and a 64-thread named
+//                barrier; running max and sum in the log2 domain; P = 2^(s-m)
+//                written as bf16 pairs over the first 64 columns of its S
+//                buffer (tcgen05.st); O rescaled in TMEM only when the max
+//                grows by more than 2^8;
+//   warps 0-7    epilogue: O / l, bf16, the output gate with the
+//                reference's polynomial and rounding steps (hb_epilogue.cuh),
+//                each thread storing its row's 16-byte pieces.
+// TMEM: S buffers at columns [0, 256), O at [256, 512) of a 512-column
+// allocation.  Shared memory: Q 64 KB + K ring 64 KB + V ring 80 KB.
 //
 // Context-parallel hops (template CP = true) run the same pipeline over the
 // K/V shard of one ring position: up to two key segments (a zig-zag shard
@@ -42,6 +46,7 @@
 #include <cuda_runtime.h>
 
 #include "hb_common.cuh"
+#include "hb_epilogue.cuh"
 #include "hb_internal.h"
 #include "hb_sm100.cuh"
 
@@ -55,16 +60,19 @@ constexpr int kThreads = 320;  // warps 0-7 softmax and epilogue, 8 TMA, 9 MMA
 constexpr int kTmaWarp = 8, kMmaWarp = 9;
 constexpr int Q_BYTES = BM * HDIM * 2;  // 4 column blocks of [128 rows x 128 B]
 constexpr int SLOT = 16384;             // one ring slot
-constexpr int NSLOT = 4;
+constexpr int NSLOT = 4;                // K slots: one 128-key tile
+constexpr int NVSLOT = 5;               // V slots: a tile and a quarter
 constexpr int OFF_Q = 0;
 // K ring: slot b holds column block b (dims 64b..64b+63) of a key tile,
-// [128 keys x 128 B]; V ring: slot c holds keys 32c..32c+31 of a tile,
-// [4 column blocks][32 keys][128 B].  A slot is refilled for the next tile
-// as soon as the MMAs that read it have completed.
+// [128 keys x 128 B]; V ring: quarter g = 4 j + c of the key stream (keys
+// 32c..32c+31 of tile j, [4 column blocks][32 keys][128 B]) sits in slot
+// g % 5, so the first quarter of a tile loads while the previous tile's
+// products still read the other four.  A slot is refilled as soon as the
+// MMAs that read it have completed.
 constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int OFF_V = OFF_K + NSLOT * SLOT;
-constexpr int OFF_BAR = OFF_V + NSLOT * SLOT;
-constexpr int NBAR = 24;
+constexpr int OFF_BAR = OFF_V + NVSLOT * SLOT;
+constexpr int NBAR = 26;
 constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l (or the merge weight of O_acc)
 constexpr int OFF_FB = OFF_INVL + BM * 4;          // merge weight of a CP hop's O
 constexpr int OFF_XM = OFF_FB + BM * 4;            // row maxima [2 parity][2 halves][128]
@@ -75,9 +83,32 @@ constexpr uint32_t TMEM_COLS = 512;
 // its first 64 columns; O in [256, 512)
 constexpr uint32_t S_COL = 0, O_COL = 256;
 constexpr float kRescaleLog2 = 8.0f;  // keep a stale max while p stays below 2^8
+// pairs c % 8 of a thread's 32 probability pairs whose 2^x comes from the
+// polynomial (bit c set), the rest from the SFU
+constexpr uint32_t kPolyPairs = 0xA4u;  // pairs 2, 5, 7
 
-enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 5, V_FULL = 9, V_EMPTY = 13, S_FULL = 17,
-           P_FULL = 19, PV_DONE = 21, GATE_FULL = 23 };
+// 2^x on two lanes for x <= 8 (the max may be stale by up to 2^8) without
+// the SFU: Cody-Waite range reduction x = j + f with j = round(x) (adding
+// and removing 1.5 * 2^23 leaves j in the low bits of the sum) and f in
+// [-1/2, 1/2], 2^f by a cubic fitted here for least relative error on that
+// interval (max relative error 7.5e-5, far below the bf16 rounding of P),
+// and j added to the exponent field.  x is clamped at -126 so that the
+// exponent stays in range; such p are below 2^-125 and vanish in the sums.
+HB_DEV uint64_t exp2_poly2(uint64_t x2) {
+  const uint64_t x = f2(fmaxf(f2lo(x2), -126.0f), fmaxf(f2hi(x2), -126.0f));
+  const uint64_t shift = f2(12582912.0f, 12582912.0f);
+  const uint64_t t = f2add(x, shift);
+  const uint64_t f = f2sub(x, f2sub(t, shift));
+  uint64_t q = f2fma(f2(0.055171650f, 0.055171650f), f, f2(0.24261114f, 0.24261114f));
+  q = f2fma(q, f, f2(0.69326097f, 0.69326097f));
+  q = f2fma(q, f, f2(0.99992806f, 0.99992806f));
+  const uint32_t lo = uint32_t(q) + (uint32_t(t) << 23);
+  const uint32_t hi = uint32_t(q >> 32) + (uint32_t(t >> 32) << 23);
+  return (uint64_t(hi) << 32) | lo;
+}
+
+enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 5, V_FULL = 9, V_EMPTY = 14, S_FULL = 19,
+           P_FULL = 21, PV_DONE = 23, GATE_FULL = 25 };
 
 HB_DEV void epilogue_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
 
@@ -124,8 +155,7 @@ template <bool CP>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmV,
-                        const __grid_constant__ CUtensorMap tmO, const PrefillParams p) {
+                        const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -158,6 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&bar[K_FULL + s], 1);
       mbar_init(&bar[K_EMPTY + s], 1);
+    }
+    for (int s = 0; s < NVSLOT; ++s) {
       mbar_init(&bar[V_FULL + s], 1);
       mbar_init(&bar[V_EMPTY + s], 1);
     }
@@ -192,10 +224,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {  // Q, then the K slots, then the gate tile
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
-      prefetch_tmap(&tmO);
       mbar_arrive_expect_tx(&bar[Q_FULL], Q_BYTES);
       for (int c = 0; c < 4; ++c)
         tma_load_2d(smem + OFF_Q + c * SLOT, &tmQ, &bar[Q_FULL], h * HDIM + c * 64, m0);
+      {  // the Q tile of the CTA one SM-count later, which starts about when
+         // this one ends, into L2
+        uint32_t nsm;
+        asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+        const int nb = int(blockIdx.x + nsm);
+        if (nb < int(gridDim.x)) {
+          const int nqt = p.n_qtiles - 1 - nb / p.heads, nh = nb % p.heads;
+          for (int c = 0; c < 4; ++c) tma_prefetch_l2_2d(&tmQ, nh * HDIM + c * 64, nqt * BM);
+        }
+      }
       bool ok = true;
       for (int j = 0; ok && j < ntiles; ++j) {
         const int kr = key_row(j);
@@ -220,21 +261,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         int(p.gate_offset) + h * HDIM + c * 64, m0);
         }
       }
-    } else if (lane == 1) {  // the V slots
+    } else if (lane == 1) {  // the V quarters, through five slots
       prefetch_tmap(&tmV);
-      bool ok = true;
-      for (int j = 0; ok && j < ntiles; ++j) {
-        const int kr = key_row(j);
-        for (int c = 0; c < NSLOT; ++c) {
-          if (j >= 1 && !wait(V_EMPTY + c, (j - 1) & 1)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&bar[V_FULL + c], SLOT);
-          for (int db = 0; db < 4; ++db)
-            tma_load_3d(smem + OFF_V + c * SLOT + db * 4096, &tmV, &bar[V_FULL + c], db * 64,
-                        kr + c * 32, kvh);
-        }
+      for (int g = 0; g < 4 * ntiles; ++g) {
+        const int sl = g % NVSLOT, fill = g / NVSLOT;
+        if (fill >= 1 && !wait(V_EMPTY + sl, (fill - 1) & 1)) break;
+        mbar_arrive_expect_tx(&bar[V_FULL + sl], SLOT);
+        const int kr = key_row(g >> 2) + (g & 3) * 32;
+        for (int db = 0; db < 4; ++db)
+          tma_load_3d(smem + OFF_V + sl * SLOT + db * 4096, &tmV, &bar[V_FULL + sl], db * 64, kr,
+                      kvh);
       }
     }
     __syncwarp();
@@ -272,8 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after_sync();
         // O += P_j V_j: P from TMEM (8 columns per 16 keys), V slot c holds
         // keys 32c.. (column blocks 4096 B apart)
-        for (int c = 0; c < NSLOT; ++c) {
-          if (!wait(V_FULL + c, j & 1)) {
+        for (int c = 0; c < 4; ++c) {
+          const int g = 4 * j + c, sl = g % NVSLOT;
+          if (!wait(V_FULL + sl, (g / NVSLOT) & 1)) {
             ok = false;
             break;
           }
@@ -281,10 +318,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k2 = 0; k2 < 2; ++k2) {
             const int kk = c * 2 + k2;
-            const uint64_t bd = sw128_desc(vb + c * SLOT + k2 * 2048, 4096, 1024);
+            const uint64_t bd = sw128_desc(vb + sl * SLOT + k2 * 2048, 4096, 1024);
             mma_bf16_ts(tmem + O_COL, tmem + S_COL + sb * BN + kk * 8, bd, idPV, j > 0 || kk > 0);
           }
-          mma_commit(&bar[V_EMPTY + c]);
+          mma_commit(&bar[V_EMPTY + sl]);
         }
         if (!ok) break;
         mma_commit(&bar[PV_DONE + sb]);
@@ -328,28 +365,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         klen = p.chunk - t * BN;
       }
       const int kh0 = kb + hc * 64, klh = klen - hc * 64;  // this thread's 64 keys
-      float v[64];
+      const bool full = kb + BN - 1 <= qlo && (!CP || klen >= BN);  // no key masked
+      if (!full) {  // masked scores become -inf (raw, before scaling)
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (!(kh0 + c <= qpos && (!CP || c < klh))) ra[c] = 0xFF800000u;
+          if (!(kh0 + 32 + c <= qpos && (!CP || 32 + c < klh))) rb[c] = 0xFF800000u;
+        }
+      }
+      // the max of the raw scores, scaled once (scale > 0)
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
-      if (kb + BN - 1 <= qlo && (!CP || klen >= BN)) {  // below the diagonal for every row
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          v[c] = __uint_as_float(ra[c]) * p.scale_log2;
-          v[32 + c] = __uint_as_float(rb[c]) * p.scale_log2;
-          m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
-        }
-      } else {
+      for (int c = 0; c < 32; ++c)
+        m8[c & 7] = fmaxf(m8[c & 7], fmaxf(__uint_as_float(ra[c]), __uint_as_float(rb[c])));
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          v[c] = (kh0 + c <= qpos && (!CP || c < klh)) ? __uint_as_float(ra[c]) * p.scale_log2
-                                                       : -INFINITY;
-          v[32 + c] = (kh0 + 32 + c <= qpos && (!CP || 32 + c < klh))
-                          ? __uint_as_float(rb[c]) * p.scale_log2
-                          : -INFINITY;
-          m8[c & 7] = fmaxf(m8[c & 7], fmaxf(v[c], v[32 + c]));
-        }
-      }
+      for (int i = 0; i < 8; ++i) m8[i] *= p.scale_log2;
       float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                        fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       // the other half's maximum (and one shared decision to stop); the
@@ -392,17 +424,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // P_j = 2^(s - m) in bf16 over the first 64 columns of S_j: keys
       // 64 hc .. + 63 go to columns 32 hc .. + 31, two keys per column
-      float s8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
+      // x = s scale - m by one paired FMA; 2^x by the SFU, except, on tiles
+      // with no masked key, for three pairs in eight, which go to
+      // exp2_poly2 on the FMA pipe so that neither unit alone paces the
+      // softmax (a masked x = -inf must give exactly 0: SFU)
       uint32_t pk[32];
+      const uint64_t sc2 = f2(p.scale_log2, p.scale_log2), nm2 = f2(-m, -m);
+      uint64_t s4[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float p0 = fast_exp2(v[2 * c] - m), p1 = fast_exp2(v[2 * c + 1] - m);
-        s8[c & 7] += p0 + p1;
-        pk[c] = pack_bf16x2(p0, p1);
+        const uint32_t* src = c < 16 ? ra : rb;
+        const int e = (c & 15) * 2;
+        const uint64_t x2 =
+            f2fma(f2(__uint_as_float(src[e]), __uint_as_float(src[e + 1])), sc2, nm2);
+        const uint64_t p2 = full && ((kPolyPairs >> (c & 7)) & 1u)
+                                ? exp2_poly2(x2)
+                                : f2(fast_exp2(f2lo(x2)), fast_exp2(f2hi(x2)));
+        s4[c & 3] = f2add(s4[c & 3], p2);
+        pk[c] = pack_bf16x2(f2lo(p2), f2hi(p2));
       }
-      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      const uint64_t s2 = f2add(f2add(s4[0], s4[1]), f2add(s4[2], s4[3]));
+      l += f2lo(s2) + f2hi(s2);
       tmem_st32(tl + S_COL + sb * BN + hc * 32, pk);
       tmem_wait_st();
       fence_before_sync();
@@ -479,6 +521,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else {
+    // each thread writes its row's 64-byte pieces straight to global memory
+    const bool store = ok && !*abort_flag && m0 + rl < p.rows;
+    uint16_t* orow = p.out + size_t(m0 + rl) * size_t(p.out_row) + h * HDIM;
 #pragma unroll 1
     for (int ch = 0; ch < 4; ++ch) {
       const int col0 = hc * 128 + ch * 32;
@@ -491,60 +536,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k)
         phys[k] = cb * (BM * 128) + rl * 128 + (((c16 + k) ^ (rl & 7)) << 4);
       // a = bf16(O / l), then the gate y = bf16(a / (1 + exp(-g))) for 32
-      // columns at once: SFU quotients, the rare ones that may round
-      // differently recomputed with the correctly rounded division
-      uint32_t aw[16];  // a, two bf16 per word
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint64_t ov =
-            f2mul(f2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), f2(inv, inv));
-        aw[i] = bf16x2_cvtne(f2lo(ov), f2hi(ov));
-      }
-      uint32_t w[16];
+      // columns at once (hb_epilogue.cuh)
+      uint32_t gw[16], w[16];
       if (p.gate_offset >= 0) {
-        uint32_t gw[16];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint4 gv = *reinterpret_cast<const uint4*>(smem + OFF_K + phys[k]);
           gw[4 * k] = gv.x; gw[4 * k + 1] = gv.y; gw[4 * k + 2] = gv.z; gw[4 * k + 3] = gv.w;
         }
-        float qv[32];
-        uint32_t risky = 0;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint64_t d2 = gate_divisor2(gw[i]);
-          bool r0, r1;
-          qv[2 * i] = gate_quotient_fast(bf16lo(aw[i]), f2lo(d2), r0);
-          qv[2 * i + 1] = gate_quotient_fast(bf16hi(aw[i]), f2hi(d2), r1);
-          risky |= (uint32_t(r0) << (2 * i)) | (uint32_t(r1) << (2 * i + 1));
-        }
-        if (risky) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if ((risky >> i) & 1u) {
-              const uint32_t a_bits = i & 1 ? aw[i >> 1] >> 16 : aw[i >> 1] & 0xFFFFu;
-              const uint16_t g = uint16_t(i & 1 ? gw[i >> 1] >> 16 : gw[i >> 1] & 0xFFFFu);
-              qv[i] = __fdiv_rn(bf16_to_f32(uint16_t(a_bits)), gate_divisor(g));
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = bf16x2_cvtne(qv[2 * i], qv[2 * i + 1]);
+        epilogue_block32<true>(o, inv, gw, w);
       } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = aw[i];
+        epilogue_block32<false>(o, inv, gw, w);
       }
+      if (store) {
+        uint4* dst = reinterpret_cast<uint4*>(orow + col0);
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        *reinterpret_cast<uint4*>(smem + OFF_V + phys[k]) =
-            make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
-    }
-    fence_proxy_async_smem();
-    epilogue_sync();  // the output tile is staged
-    if (threadIdx.x == 0 && ok && !*abort_flag) {
-      for (int c = 0; c < 4; ++c)
-        tma_store_2d(&tmO, smem + OFF_V + c * (BM * 128), h * HDIM + c * 64, m0);
-      tma_store_commit();
-      tma_store_wait_read();
+        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+      }
     }
     }
   }
@@ -568,7 +576,7 @@ bool encode_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t*
 bool prefill_serves(int64_t head_dim) { return head_dim == HDIM; }
 
 cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
-  CUtensorMap tq, tk, tv, to;
+  CUtensorMap tq, tk, tv;
   const int64_t kv_rows = L.cp ? L.kv_rows : L.past + L.rows;
   const cuuint64_t qd[2] = {cuuint64_t(L.q_row), cuuint64_t(L.rows)};
   const cuuint64_t qs[1] = {cuuint64_t(L.q_row) * 2};
@@ -577,16 +585,12 @@ cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   const cuuint64_t ks[2] = {cuuint64_t(HDIM) * 2, cuuint64_t(L.kv_stride) * 2};
   const cuuint32_t kbox[3] = {64, BN, 1};  // one K slot: 128 keys of one column block
   const cuuint32_t vbox[3] = {64, 32, 1};  // a quarter of a V slot: 32 keys of one column block
-  const cuuint64_t od[2] = {cuuint64_t(L.out_row), cuuint64_t(L.rows)};
-  const cuuint64_t os[1] = {cuuint64_t(L.out_row) * 2};
   if (!encode_bf16(&tq, L.q, 2, qd, qs, qbox) || !encode_bf16(&tk, L.keys, 3, kd, ks, kbox) ||
       !encode_bf16(&tv, L.values, 3, kd, ks, vbox))
     return cudaErrorInvalidValue;
-  if (L.cp) {
-    to = tq;  // no output store on a hop
-  } else if (!encode_bf16(&to, L.out, 2, od, os, qbox)) {
+  // the epilogue writes 16-byte pieces of output rows
+  if (!L.cp && ((reinterpret_cast<uintptr_t>(L.out) & 15) || (L.out_row & 7)))
     return cudaErrorInvalidValue;
-  }
   static DeviceFlags configured;
   cudaError_t e = configured.once([] {
     cudaError_t r = cudaFuncSetAttribute(attn_prefill_kernel<false>,
@@ -618,9 +622,9 @@ cudaError_t launch_attn_prefill(const PrefillLaunch& L, cudaStream_t st) {
   p.merge = L.merge ? 1 : 0;
   const unsigned grid = unsigned(p.n_qtiles * p.heads);
   if (L.cp)
-    attn_prefill_kernel<true><<<grid, kThreads, SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+    attn_prefill_kernel<true><<<grid, kThreads, SMEM_BYTES, st>>>(tq, tk, tv, p);
   else
-    attn_prefill_kernel<false><<<grid, kThreads, SMEM_BYTES, st>>>(tq, tk, tv, to, p);
+    attn_prefill_kernel<false><<<grid, kThreads, SMEM_BYTES, st>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 

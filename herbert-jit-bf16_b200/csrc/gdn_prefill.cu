@@ -128,6 +128,16 @@ __global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const PrepParams p) {
   }
   if (warp == 0) tmem_alloc(tslot, 256);
 
+  // gates of both value heads, loaded first so that their latency hides
+  // under the row loads
+  float beta_v = 0.f, decay_v = 1.f;  // padded rows: decay 1
+  if (tid < 128) {
+    const int64_t t = t0 + (tid & 63);
+    if (t < p.rows) {
+      beta_v = p.beta[t * p.nv + h0 + (tid >> 6)];
+      decay_v = p.decay[t * p.nv + h0 + (tid >> 6)];
+    }
+  }
   // ---- rows, a warp per row, lane = 4 columns: warp w loads 32 rows of
   // tensor w/2 (K, Q, V0, V1), K and Q L2-normalised, bf16 into SA / SV
   {
@@ -162,12 +172,9 @@ __global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const PrepParams p) {
       }
     }
   }
-  if (tid < 128) {  // gates of both value heads
-    const int hh = tid >> 6, r = tid & 63;
-    const int64_t t = t0 + r;
-    const bool in = t < p.rows;
-    beta_s[hh * 64 + r] = in ? p.beta[t * p.nv + h0 + hh] : 0.f;
-    G_s[hh * 64 + r] = in ? logf(p.decay[t * p.nv + h0 + hh]) : 0.f;  // padded rows: decay 1
+  if (tid < 128) {
+    beta_s[tid] = beta_v;  // [head][row]: tid = hh * 64 + r
+    G_s[tid] = logf(decay_v);
   }
   fence_proxy_async_smem();
   fence_before_sync();

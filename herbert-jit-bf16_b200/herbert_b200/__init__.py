@@ -107,6 +107,7 @@ _SIGNATURES = {
     "hb_attn_decode": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
                                       c_void_p]),
     "hb_attn_decode_noalloc": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p]),
+    "hb_selftest_prefill_epilogue": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), c_void_p]),
     "hb_attn_decode_batch_workspace_bytes": (c_size_t, [_P(AttentionSpec), c_int64, c_int64,
                                                         c_int64]),
     "hb_attn_decode_batch": (ctypes.c_int, [_P(AttentionSpec), c_void_p, c_int64, c_int64,

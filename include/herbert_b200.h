@@ -303,6 +303,19 @@ HB_API size_t hb_gdn_prefill_workspace_bytes(const hb_gdn_shape *shape, int64_t 
 HB_API hb_status hb_gdn_prefill(const hb_gdn_shape *shape, const hb_gdn_call *call, void *workspace,
                          size_t workspace_bytes, hb_stream_t stream);
 
+/*
+ * Self-test, no counterpart in the reference: runs the arithmetic of
+ * hb_attn_prefill's epilogue (O / l rounded to bf16, then the output gate)
+ * over every pair of bf16 values (a, g) and over every f32 value of O / l,
+ * and compares each result with the exact per-element steps.  Synchronous
+ * on `stream`; tens of milliseconds on a B200.  out[8]: [0] gate
+ * mismatches, [1] column pairs the fast path sent to the exact steps,
+ * [2] first mismatching element + 1 (a | g << 16; 0 = none), [3] its result
+ * | expected << 16; [4..7] the same for the O / l rounding (element = the
+ * f32 bits).
+ */
+HB_API hb_status hb_selftest_prefill_epilogue(uint64_t *out, hb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
