@@ -8,29 +8,29 @@
 // Row r of the call is the query at absolute position past + r and sees keys
 // [0, past + r] (src/jit/target/x86/execution/attention.rs:189-196).
 //
-// CTA = one tile of 128 query rows of one query head (head_dim 256), 320
+// CTA = one tile of 128 query rows of one query head (head_dim 256), 576
 // threads:
-//   warp 8       TMA producers (no multicast, SWIZZLE_128B): lane 0 loads
+//   warp 16      TMA producers (no multicast, SWIZZLE_128B): lane 0 loads
 //                the Q tile, then the K slots (a ring of four 16 KB slots,
 //                slot b = column block b of a 128-key tile) and finally the
-//                gate tile into the K ring; lane 1 loads the V slots (four
+//                gate tile into the K ring; lane 1 loads the V slots (five
 //                16 KB slots of 32 keys x 256 dims);
-//   warp 9       MMA issuer: S_j = Q K_j^T (M128 N128 K256) into TMEM S
+//   warp 17      MMA issuer: S_j = Q K_j^T (M128 N128 K256) into TMEM S
 //                buffer j % 2; O += P_j V_j (M128 N256 K128) with P_j taken
 //                from TMEM (the TS form) and V MN-major from shared memory;
 //                issue order S_0, S_1, then PV_j, S_{j+2}, S_{j+2} waiting
 //                for PV_j to free its buffer; every group committed to an
 //                mbarrier that also frees the ring slots it read;
-//   warps 0-7    softmax: warps q and q+4 own TMEM lanes 32q.. (one query
-//                row per thread), each half of a tile's 128 keys; the row
-//                maxima meet through shared memory and a 64-thread named
-//                barrier; running max and sum in the log2 domain; P = 2^(s-m)
-//                written as bf16 pairs over the first 64 columns of its S
-//                buffer (tcgen05.st); O rescaled in TMEM only when the max
-//                grows by more than 2^8;
-//   warps 0-7    epilogue: O / l, bf16, the output gate with the
+//   warps 0-15   softmax: warps q, q+4, q+8, q+12 own TMEM lanes 32q.. (one
+//                query row per thread), each a quarter of a tile's 128 keys;
+//                the row maxima meet through shared memory and a 128-thread
+//                named barrier; running max and sum in the log2 domain;
+//                P = 2^(s-m) written as bf16 pairs over the first 64 columns
+//                of its S buffer (tcgen05.st); O rescaled in TMEM only when
+//                the max grows by more than 2^8;
+//   warps 0-15   epilogue: O / l, bf16, the output gate with the
 //                reference's polynomial and rounding steps (hb_epilogue.cuh),
-//                each thread storing its row's 16-byte pieces.
+//                each thread storing 64 columns of its row.
 // TMEM: S buffers at columns [0, 256), O at [256, 512) of a 512-column
 // allocation.  Shared memory: Q 64 KB + K ring 64 KB + V ring 80 KB.
 //
@@ -56,8 +56,10 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128, BN = 128, HDIM = 256;  // query rows, keys per tile, head dim
-constexpr int kThreads = 320;  // warps 0-7 softmax and epilogue, 8 TMA, 9 MMA
-constexpr int kTmaWarp = 8, kMmaWarp = 9;
+// warps 0-15 softmax and epilogue, 16 TMA, 17 MMA
+constexpr int kSoftmaxWarps = 16, kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kTmaWarp = 16, kMmaWarp = 17;
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
 constexpr int Q_BYTES = BM * HDIM * 2;  // 4 column blocks of [128 rows x 128 B]
 constexpr int SLOT = 16384;             // one ring slot
 constexpr int NSLOT = 4;                // K slots: one 128-key tile
@@ -75,9 +77,9 @@ constexpr int OFF_BAR = OFF_V + NVSLOT * SLOT;
 constexpr int NBAR = 26;
 constexpr int OFF_INVL = OFF_BAR + NBAR * 8 + 16;  // 1/l (or the merge weight of O_acc)
 constexpr int OFF_FB = OFF_INVL + BM * 4;          // merge weight of a CP hop's O
-constexpr int OFF_XM = OFF_FB + BM * 4;            // row maxima [2 parity][2 halves][128]
-constexpr int OFF_XL = OFF_XM + 4 * BM * 4;        // row sums [2 halves][128]
-constexpr int SMEM_BYTES = OFF_XL + 2 * BM * 4 + 1024;  // + 1 KB alignment slack
+constexpr int OFF_XM = OFF_FB + BM * 4;            // row maxima [2 parity][4 quarters][128]
+constexpr int OFF_XL = OFF_XM + 8 * BM * 4;        // row sums [4 quarters][128]
+constexpr int SMEM_BYTES = OFF_XL + 4 * BM * 4 + 1024;  // + 1 KB alignment slack
 constexpr uint32_t TMEM_COLS = 512;
 // S_j in columns [128 (j%2), +128); P_j (bf16, two per column) overwrites
 // its first 64 columns; O in [256, 512)
@@ -110,15 +112,15 @@ HB_DEV uint64_t exp2_poly2(uint64_t x2) {
 enum Bar { Q_FULL = 0, K_FULL = 1, K_EMPTY = 5, V_FULL = 9, V_EMPTY = 14, S_FULL = 19,
            P_FULL = 21, PV_DONE = 23, GATE_FULL = 25 };
 
-HB_DEV void epilogue_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
+HB_DEV void epilogue_sync() { asm volatile("bar.sync 2, 512;" ::: "memory"); }
 
-// Barrier of the two softmax warps of lane quadrant q (warps q and q + 4,
-// named barrier 3 + q); returns the AND of `v` over their 64 threads, so
-// both warps take the same early exit.
-HB_DEV bool pair_sync_and(int q, bool v) {
+// Barrier of the four softmax warps of lane quadrant q (warps q, q + 4,
+// q + 8, q + 12, named barrier 3 + q); returns the AND of `v` over their 128
+// threads, so all four take the same early exit.
+HB_DEV bool quad_sync_and(int q, bool v) {
   uint32_t r;
   asm volatile(
-      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, 64, p; selp.u32 %0, 1, 0, q; }"
+      "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, 128, p; selp.u32 %0, 1, 0, q; }"
       : "=r"(r)
       : "r"(uint32_t(v)), "r"(3 + q)
       : "memory");
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar[S_FULL + s], 1);
-      mbar_init(&bar[P_FULL + s], 256);
+      mbar_init(&bar[P_FULL + s], kSoftmaxThreads);
       mbar_init(&bar[PV_DONE + s], 1);
     }
     mbar_init(&bar[GATE_FULL], 1);
@@ -329,19 +331,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else {  // ------------------------------------------ softmax (warps 0-7)
-    // warps q and q + 4 own rows 32q .. 32q + 31 (TMEM lanes), warp q the
-    // keys 0-63 of each tile, warp q + 4 the keys 64-127; the row max is
-    // exchanged through shared memory each tile, the row sum at the end
-    const int q4 = warp & 3, hc = warp >> 2;
+  } else {  // ----------------------------------------- softmax (warps 0-15)
+    // warps q, q + 4, q + 8, q + 12 own rows 32q .. 32q + 31 (TMEM lanes);
+    // warp q + 4k takes keys 32k .. 32k + 31 of each tile.  The row max is
+    // exchanged through shared memory each tile, the row sum at the end.
+    const int q4 = warp & 3, hq = warp >> 2;
     const int row = q4 * 32 + lane;
     const uint32_t tl = tmem + (uint32_t(q4 * 32) << 16);
     const int qpos = qlo + row;
-    if (CP && p.merge && hc == 1) {
+    if (CP && p.merge && hq == 3) {
       // bring this tile's accumulator (128 KB, 1024 lines) into L2 for the merge
       const char* a = reinterpret_cast<const char*>(
           p.acc + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM));
-      for (int ln = threadIdx.x - 128; ln < HDIM * BM * 4 / 128; ln += 128)
+      for (int ln = threadIdx.x - 384; ln < HDIM * BM * 4 / 128; ln += 128)
         asm volatile("prefetch.global.L2 [%0];" ::"l"(a + size_t(ln) * 128));
     }
     float m = -INFINITY, l = 0.f;
@@ -350,9 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int sb = j & 1;
       ok = __all_sync(0xFFFFFFFFu, wait(S_FULL + sb, (j >> 1) & 1) && ok);
       fence_after_sync();
-      uint32_t ra[32], rb[32];
-      tmem_ld32(tl + S_COL + sb * BN + hc * 64, ra);
-      tmem_ld32(tl + S_COL + sb * BN + hc * 64 + 32, rb);
+      uint32_t ra[32];
+      tmem_ld32(tl + S_COL + sb * BN + hq * 32, ra);
       tmem_wait_ld();
       fence_before_sync();
       // key positions kb.. of this tile; keys from klen on lie past the
@@ -364,34 +365,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         kb = (s1 ? p.kpos1 : p.kpos0) + t * BN;
         klen = p.chunk - t * BN;
       }
-      const int kh0 = kb + hc * 64, klh = klen - hc * 64;  // this thread's 64 keys
+      const int kh0 = kb + hq * 32, klh = klen - hq * 32;  // this thread's 32 keys
       const bool full = kb + BN - 1 <= qlo && (!CP || klen >= BN);  // no key masked
       if (!full) {  // masked scores become -inf (raw, before scaling)
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
+        for (int c = 0; c < 32; ++c)
           if (!(kh0 + c <= qpos && (!CP || c < klh))) ra[c] = 0xFF800000u;
-          if (!(kh0 + 32 + c <= qpos && (!CP || 32 + c < klh))) rb[c] = 0xFF800000u;
-        }
       }
       // the max of the raw scores, scaled once (scale > 0)
       float m8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        m8[c & 7] = fmaxf(m8[c & 7], fmaxf(__uint_as_float(ra[c]), __uint_as_float(rb[c])));
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] *= p.scale_log2;
+      for (int c = 0; c < 32; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(ra[c]));
       float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      // the other half's maximum (and one shared decision to stop); the
-      // barrier also orders both threads' S reads before either writes P
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.scale_log2;
+      // the other quarters' maxima (and one shared decision to stop); the
+      // barrier also orders all four threads' S reads before any writes P
       // over them
-      xmax[((j & 1) * 2 + hc) * BM + row] = mx;
-      ok = pair_sync_and(q4, ok);
+      float* xm = xmax + (j & 1) * 4 * BM + row;
+      xm[hq * BM] = mx;
+      ok = quad_sync_and(q4, ok);
       fence_after_sync();
       if (!ok) break;
-      mx = fmaxf(mx, xmax[((j & 1) * 2 + (hc ^ 1)) * BM + row]);
+      mx = fmaxf(fmaxf(xm[0], xm[BM]), fmaxf(xm[2 * BM], xm[3 * BM]));
       const float m_new = fmaxf(m, mx);
       float factor = 1.f;
       bool resc = false;
@@ -403,18 +400,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (__any_sync(0xFFFFFFFFu, resc)) {
         // O holds PV_0 .. PV_{j-1}; the last of them may still be running.
-        // Each thread rescales its half of the row's 256 columns.
+        // Each thread rescales a quarter of the row's 256 columns.
         const int jp = j - 1;
         ok = __all_sync(0xFFFFFFFFu, wait(PV_DONE + (jp & 1), (jp >> 1) & 1) && ok);
         fence_after_sync();
 #pragma unroll 1
-        for (int c = 0; c < HDIM / 64; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
-          tmem_ld32(tl + O_COL + hc * 128 + c * 32, r);
+          tmem_ld32(tl + O_COL + hq * 64 + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          tmem_st32(tl + O_COL + hc * 128 + c * 32, r);
+          tmem_st32(tl + O_COL + hq * 64 + c * 32, r);
         }
         tmem_wait_st();
         if (resc) {
@@ -423,20 +420,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // P_j = 2^(s - m) in bf16 over the first 64 columns of S_j: keys
-      // 64 hc .. + 63 go to columns 32 hc .. + 31, two keys per column
+      // 32 hq .. + 31 go to columns 16 hq .. + 15, two keys per column.
       // x = s scale - m by one paired FMA; 2^x by the SFU, except, on tiles
       // with no masked key, for three pairs in eight, which go to
       // exp2_poly2 on the FMA pipe so that neither unit alone paces the
       // softmax (a masked x = -inf must give exactly 0: SFU)
-      uint32_t pk[32];
+      uint32_t pk[16];
       const uint64_t sc2 = f2(p.scale_log2, p.scale_log2), nm2 = f2(-m, -m);
       uint64_t s4[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const uint32_t* src = c < 16 ? ra : rb;
-        const int e = (c & 15) * 2;
+      for (int c = 0; c < 16; ++c) {
         const uint64_t x2 =
-            f2fma(f2(__uint_as_float(src[e]), __uint_as_float(src[e + 1])), sc2, nm2);
+            f2fma(f2(__uint_as_float(ra[2 * c]), __uint_as_float(ra[2 * c + 1])), sc2, nm2);
         const uint64_t p2 = full && ((kPolyPairs >> (c & 7)) & 1u)
                                 ? exp2_poly2(x2)
                                 : f2(fast_exp2(f2lo(x2)), fast_exp2(f2hi(x2)));
@@ -445,17 +440,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint64_t s2 = f2add(f2add(s4[0], s4[1]), f2add(s4[2], s4[3]));
       l += f2lo(s2) + f2hi(s2);
-      tmem_st32(tl + S_COL + sb * BN + hc * 32, pk);
+      tmem_st16(tl + S_COL + sb * BN + hq * 16, pk);
       tmem_wait_st();
       fence_before_sync();
       mbar_arrive(&bar[P_FULL + sb]);
     }
-    // the row sum of the two halves
-    xsum[hc * BM + row] = l;
+    // the row sum of the four quarters
+    xsum[hq * BM + row] = l;
     if (!ok) *abort_flag = 1;
     epilogue_sync();
-    if (hc == 0) {
-      l += xsum[BM + row];
+    if (hq == 0) {
+      l = ((l + xsum[BM + row]) + xsum[2 * BM + row]) + xsum[3 * BM + row];
       if constexpr (CP) {
         // log-sum-exp merge of (m, l) with what earlier hops left; O and l of
         // this hop are relative to m (a max that may be stale by < 2^8)
@@ -484,14 +479,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (warp < 8) {  // ------------------------------- epilogue (warps 0-7)
+  if (warp < kSoftmaxWarps) {  // --------------------------- epilogue (warps 0-15)
     epilogue_sync();  // inv_l written
     const int jl = ntiles - 1;
     bool ok = wait(PV_DONE + (jl & 1), (jl >> 1) & 1);
     if (!CP && p.gate_offset >= 0) ok = wait(GATE_FULL, 0) && ok;
     ok = __all_sync(0xFFFFFFFFu, ok);
     fence_after_sync();
-    const int qd = warp & 3, hc = warp >> 2;  // TMEM lane quadrant, column half
+    const int qd = warp & 3, hq = warp >> 2;  // TMEM lane quadrant, column quarter
     const int rl = qd * 32 + lane;            // row within the tile
     const uint32_t tq = tmem + (uint32_t(qd * 32) << 16);
     const float inv = inv_l[rl];
@@ -501,8 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float wa = inv, wb = w_hop[rl];
       float* acc = p.acc + (size_t(h) * p.n_qtiles + qt) * (size_t(HDIM) * BM) + rl;
 #pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        const int col0 = hc * 128 + ch * 32;
+      for (int ch = 0; ch < 2; ++ch) {
+        const int col0 = hq * 64 + ch * 32;
         uint32_t o[32];
         tmem_ld32(tq + O_COL + col0, o);
         tmem_wait_ld();
@@ -521,39 +516,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else {
-    // each thread writes its row's 64-byte pieces straight to global memory
-    const bool store = ok && !*abort_flag && m0 + rl < p.rows;
-    uint16_t* orow = p.out + size_t(m0 + rl) * size_t(p.out_row) + h * HDIM;
+      // each thread writes its row's 32-byte pieces straight to global memory
+      constexpr int W = kEpilogueWidth;
+      const bool store = ok && !*abort_flag && m0 + rl < p.rows;
+      uint16_t* orow = p.out + size_t(m0 + rl) * size_t(p.out_row) + h * HDIM;
 #pragma unroll 1
-    for (int ch = 0; ch < 4; ++ch) {
-      const int col0 = hc * 128 + ch * 32;
-      uint32_t o[32];
-      tmem_ld32(tq + O_COL + col0, o);
-      tmem_wait_ld();
-      const int cb = col0 >> 6, c16 = (col0 & 63) >> 3;
-      int phys[4];
+      for (int blk = 0; blk < 64 / W; ++blk) {
+        const int col0 = hq * 64 + blk * W;
+        uint32_t o[W];
+        tmem_ld16(tq + O_COL + col0, o);
+        tmem_wait_ld();
+        // a = bf16(O / l), then the gate y = bf16(a / (1 + exp(-g))) for W
+        // columns at once (hb_epilogue.cuh); the gate tile sits in the K
+        // ring as [4 column blocks][128 rows][128 B], 128B-swizzled
+        uint32_t gw[W / 2], w[W / 2];
+        if (p.gate_offset >= 0) {
+          const int cb = col0 >> 6, c16 = (col0 & 63) >> 3;
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        phys[k] = cb * (BM * 128) + rl * 128 + (((c16 + k) ^ (rl & 7)) << 4);
-      // a = bf16(O / l), then the gate y = bf16(a / (1 + exp(-g))) for 32
-      // columns at once (hb_epilogue.cuh)
-      uint32_t gw[16], w[16];
-      if (p.gate_offset >= 0) {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint4 gv = *reinterpret_cast<const uint4*>(smem + OFF_K + phys[k]);
-          gw[4 * k] = gv.x; gw[4 * k + 1] = gv.y; gw[4 * k + 2] = gv.z; gw[4 * k + 3] = gv.w;
+          for (int k = 0; k < W / 8; ++k) {
+            const int phys = cb * (BM * 128) + rl * 128 + (((c16 + k) ^ (rl & 7)) << 4);
+            const uint4 gv = *reinterpret_cast<const uint4*>(smem + OFF_K + phys);
+            gw[4 * k] = gv.x; gw[4 * k + 1] = gv.y; gw[4 * k + 2] = gv.z; gw[4 * k + 3] = gv.w;
+          }
+          epilogue_block<W, true>(o, inv, gw, w);
+        } else {
+          epilogue_block<W, false>(o, inv, gw, w);
         }
-        epilogue_block32<true>(o, inv, gw, w);
-      } else {
-        epilogue_block32<false>(o, inv, gw, w);
-      }
-      if (store) {
-        uint4* dst = reinterpret_cast<uint4*>(orow + col0);
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + col0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+          for (int k = 0; k < W / 8; ++k)
+            dst[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        }
       }
-    }
     }
   }
 

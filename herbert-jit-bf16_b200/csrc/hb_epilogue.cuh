@@ -1,10 +1,11 @@
-// hb_epilogue.cuh -- the prefill epilogue's arithmetic for 32 consecutive
-// columns of one output row: a = bf16(O / l), then, with the output gate,
-// y = bf16(a / (1 + exp(-g))).  Element by element the result is the bits of
-// f32_to_bf16_cvtne(O * inv) followed by gate_bf16(a, g), the reference's
-// conversion and SigmoidMul steps (src/jit/target/x86/emit_elem.rs:333-420).
+// hb_epilogue.cuh -- the prefill epilogue's arithmetic for a block of W
+// consecutive columns of one output row (W = kEpilogueWidth in the kernel):
+// a = bf16(O / l), then, with the output gate, y = bf16(a / (1 + exp(-g))).
+// Element by element the result is the bits of f32_to_bf16_cvtne(O * inv)
+// followed by gate_bf16(a, g), the reference's conversion and SigmoidMul
+// steps (src/jit/target/x86/emit_elem.rs:333-420).
 //
-// Fast path, for all 32 columns at once:
+// Fast path, for all W columns at once:
 //  * conversions by cvt.rn.bf16x2, which give bf16x2_cvtne's bits unless an
 //    input is denormal or NaN;
 //  * the divisor 1 + exp(-g) on paired lanes (gate_divisor2, the reference's
@@ -55,25 +56,29 @@ HB_DEV float gate_quotient_newton(float a, float d) {
   return __fmaf_rn(e, r, q0);
 }
 
-// One block of 32 columns: o = f32 bits of O, inv = 1 / l, gw = the gate's
+// Columns per block in the prefill kernel's epilogue (and its self-test).
+constexpr int kEpilogueWidth = 16;
+
+// One block of W columns: o = f32 bits of O, inv = 1 / l, gw = the gate's
 // bf16 values two per word (GATE only), w = output bf16 two per word.
 // Returns the number of column pairs that took the exact steps.
-template <bool GATE>
-HB_DEV int epilogue_block32(const uint32_t (&o)[32], float inv, const uint32_t (&gw)[16],
-                            uint32_t (&w)[16]) {
+template <int W, bool GATE>
+HB_DEV int epilogue_block(const uint32_t (&o)[W], float inv, const uint32_t (&gw)[W / 2],
+                          uint32_t (&w)[W / 2]) {
+  constexpr int H = W / 2;
   const uint64_t inv2 = f2(inv, inv);
   int slow = 0;
   if constexpr (!GATE) {
     bool fast = true;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < H; ++i) {
       const uint64_t ov = f2mul(f2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2);
       w[i] = bf16x2_cvt_rn(f2lo(ov), f2hi(ov));
       fast = fast && pair_in_range(f2lo(ov), f2hi(ov), 0x1p-126f);
     }
     if (!fast) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < H; ++i) {
         const uint64_t ov =
             f2mul(f2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2);
         if (!pair_in_range(f2lo(ov), f2hi(ov), 0x1p-126f)) {
@@ -83,10 +88,10 @@ HB_DEV int epilogue_block32(const uint32_t (&o)[32], float inv, const uint32_t (
       }
     }
   } else {
-    float q[32];
+    float q[W];
     bool fast = true;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < H; ++i) {
       const uint64_t ov = f2mul(f2(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), inv2);
       const uint32_t a2 = bf16x2_cvt_rn(f2lo(ov), f2hi(ov));
       const uint64_t d2 = gate_divisor2(gw[i]);
@@ -98,7 +103,7 @@ HB_DEV int epilogue_block32(const uint32_t (&o)[32], float inv, const uint32_t (
     }
     if (!fast) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < H; ++i) {
         if (near_bf16_tie(q[2 * i]) || near_bf16_tie(q[2 * i + 1]) ||
             !pair_in_range(q[2 * i], q[2 * i + 1], 0x1p-100f)) {
           const uint64_t ov =

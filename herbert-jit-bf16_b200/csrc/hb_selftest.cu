@@ -24,7 +24,7 @@ HB_DEV bool same_bf16(uint16_t x, uint16_t y) {
   return x == y || (nx && ny);  // NaN payloads are not compared
 }
 
-HB_DEV uint16_t half_of(const uint32_t (&w)[16], int i) {
+HB_DEV uint16_t half_of(const uint32_t (&w)[kEpilogueWidth / 2], int i) {
   return uint16_t(i & 1 ? w[i >> 1] >> 16 : w[i >> 1] & 0xFFFFu);
 }
 
@@ -33,22 +33,24 @@ HB_DEV void record(unsigned long long* slot, uint64_t element, uint16_t got, uin
     slot[1] = (unsigned long long)got | ((unsigned long long)want << 16);
 }
 
-// element e = a | g << 16; one block = 32 consecutive a for one g
+constexpr int W = kEpilogueWidth;
+
+// element e = a | g << 16; one block = W consecutive a for one g
 __global__ void __launch_bounds__(256) selftest_gate_kernel() {
   unsigned long long bad = 0, slow = 0;
-  const uint64_t nblocks = (uint64_t(1) << 32) / 32;
+  const uint64_t nblocks = (uint64_t(1) << 32) / W;
   for (uint64_t b = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < nblocks;
        b += uint64_t(gridDim.x) * blockDim.x) {
-    const uint32_t e0 = uint32_t(b * 32);
+    const uint32_t e0 = uint32_t(b * W);
     const uint32_t g = e0 >> 16;
-    uint32_t o[32], gw[16], w[16];
+    uint32_t o[W], gw[W / 2], w[W / 2];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = ((e0 + uint32_t(i)) & 0xFFFFu) << 16;
+    for (int i = 0; i < W; ++i) o[i] = ((e0 + uint32_t(i)) & 0xFFFFu) << 16;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) gw[i] = g | (g << 16);
-    slow += epilogue_block32<true>(o, 1.0f, gw, w);
+    for (int i = 0; i < W / 2; ++i) gw[i] = g | (g << 16);
+    slow += epilogue_block<W, true>(o, 1.0f, gw, w);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < W; ++i) {
       const uint16_t a = f32_to_bf16_cvtne(__fmul_rn(__uint_as_float(o[i]), 1.0f));
       const uint16_t want = gate_bf16(a, uint16_t(g));
       const uint16_t got = half_of(w, i);
@@ -62,21 +64,21 @@ __global__ void __launch_bounds__(256) selftest_gate_kernel() {
   if (slow) atomicAdd(&g_selftest[1], slow);
 }
 
-// element = f32 bits of O (with 1 / l = 1); one block = 32 consecutive values
+// element = f32 bits of O (with 1 / l = 1); one block = W consecutive values
 __global__ void __launch_bounds__(256) selftest_plain_kernel() {
   unsigned long long bad = 0, slow = 0;
-  const uint64_t nblocks = (uint64_t(1) << 32) / 32;
+  const uint64_t nblocks = (uint64_t(1) << 32) / W;
   for (uint64_t b = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < nblocks;
        b += uint64_t(gridDim.x) * blockDim.x) {
-    const uint32_t e0 = uint32_t(b * 32);
-    uint32_t o[32], gw[16], w[16];
+    const uint32_t e0 = uint32_t(b * W);
+    uint32_t o[W], gw[W / 2], w[W / 2];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = e0 + uint32_t(i);
+    for (int i = 0; i < W; ++i) o[i] = e0 + uint32_t(i);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) gw[i] = 0;
-    slow += epilogue_block32<false>(o, 1.0f, gw, w);
+    for (int i = 0; i < W / 2; ++i) gw[i] = 0;
+    slow += epilogue_block<W, false>(o, 1.0f, gw, w);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < W; ++i) {
       const uint16_t want = f32_to_bf16_cvtne(__fmul_rn(__uint_as_float(o[i]), 1.0f));
       const uint16_t got = half_of(w, i);
       if (!same_bf16(got, want)) {
