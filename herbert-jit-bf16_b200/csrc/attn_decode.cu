@@ -33,7 +33,13 @@
 // cluster, each CTA leaves its partial in its own shared memory, and after
 // a cluster barrier CTA r merges output slice r from all the partials
 // through distributed shared memory -- no global partials, no atomics, and
-// the merge is spread over the cluster instead of one last CTA.
+// the merge is spread over the cluster instead of one last CTA.  The
+// cluster form is launched with programmatic dependent launch: it lets the
+// next grid on the stream start at once, and before its own
+// griddepcontrol.wait it only prefetches its K/V split and q/gate lines into
+// L2 (prefetches cannot change what a later load returns), so a decode step
+// that follows another pulls its 8 MB from HBM while the previous one
+// computes, and reads nothing, and writes nothing, before that one ends.
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -214,6 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
     fence_mbar_init();
   }
   __syncthreads();
+  // cluster form (launched with programmatic stream serialization): the
+  // next grid on the stream may become resident now and run up to its own
+  // griddep_wait() while this one works
+  if constexpr (CL) griddep_launch_dependents();
 
   if (!CL && ((reinterpret_cast<uintptr_t>(kbase) | reinterpret_cast<uintptr_t>(vbase) |
                reinterpret_cast<uintptr_t>(d.q) | reinterpret_cast<uintptr_t>(d.output)) & 15) != 0) {
@@ -223,6 +233,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
 
   if (warp == kConsumerWarps) {  // ---------------------------- producer
     if (lane == 0) {
+      if constexpr (CL) {
+        // this split's K and V into L2 while the previous grid finishes;
+        // every load that returns data waits for it
+        if (p1 > p0) {
+          const uint32_t bytes = uint32_t(p1 - p0) * HD * 2u;
+          bulk_prefetch_l2(kbase + p0 * HD, bytes);
+          bulk_prefetch_l2(vbase + p0 * HD, bytes);
+        }
+        griddep_wait();
+      }
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % kStages;
         if (t >= kStages && !mbar_wait(&empty[s], ((t / kStages) - 1) & 1)) {
@@ -248,6 +268,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
   // ------------------------------------------------------------ consumers
   const int h0 = kh * G;  // first query head of the group
   const uint16_t* qrow = d.q + int64_t(row) * p.q_row;
+  if constexpr (CL) {
+    // the group's q and gate lines into L2, then wait for the previous grid
+    // (q, the gate and the newest K/V rows may be its outputs)
+    constexpr int LINES = HD * 2 / 128;  // 128-byte lines per head
+    if (int(threadIdx.x) < G * LINES) {
+      const int g = threadIdx.x / LINES, ln = threadIdx.x % LINES;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(
+          reinterpret_cast<const char*>(qrow + int64_t(h0 + g) * p.q_head) + ln * 128));
+      if (p.gate_offset >= 0)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(
+            reinterpret_cast<const char*>(qrow + p.gate_offset + int64_t(h0 + g) * HD) + ln * 128));
+    }
+    griddep_wait();
+  }
   // q and the accumulators as paired f32 lanes (dims 2k, 2k+1): one
   // paired FMA per two products
   constexpr int DP2 = DPL / 2;
@@ -653,13 +687,17 @@ cudaError_t launch(DecodeParams p, int units_z, bool single, int64_t max_n, cuda
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = st;
-        cudaLaunchAttribute at[1];
+        cudaLaunchAttribute at[2];
         at[0].id = cudaLaunchAttributeClusterDimension;
         at[0].val.clusterDim.x = p.nsplit;
         at[0].val.clusterDim.y = 1;
         at[0].val.clusterDim.z = 1;
+        // programmatic dependent launch: resident early, K/V prefetched into
+        // L2 before griddepcontrol.wait, everything else after it
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = at;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = 2;
         return cudaLaunchKernelEx(&cfg, attn_decode_kernel<HD, G, true>, p);
       }
     }

@@ -224,6 +224,20 @@ HB_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
       : "memory");
 }
 
+// Hint: bring `bytes` (a multiple of 16) from 16-byte-aligned global memory
+// into L2.  A prefetch has no effect on the values any load returns (L2 is
+// the point of coherence), so it may run before griddep_wait().
+HB_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Programmatic dependent launch.  griddep_wait() returns once the grids this
+// one depends on have completed and their memory is visible (at once when
+// the launch had no programmatic dependency); griddep_launch_dependents()
+// lets the next grid on the stream be scheduled before this one ends.
+HB_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+HB_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 HB_DEV void record_status(int* status, int code) {
   if (status) atomicMax(status, code);
 }
