@@ -9,9 +9,11 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
   batch    batched decode, 64 sequences, L ~ U{1024..32768}              GB/s
   cp       causal prefill SDPA at S 131072, context parallel over the GPUs
            (zig-zag shards, K/V ring by NCCL send/recv, LSE merge)      TFLOP/s
+  front    attention front end of a 4096-row block: q/k head norms,
+           partial RoPE, KV append                                      GB/s
 A step is one pass of the path over one batch: one prefill / one decode step /
 one GDN prefill + 256 steps / one decode step of the whole batch / one
-131072-token prefill.  The ring holds NCCL calls, so `cp` steps are issued
+131072-token prefill / one front-end call.  The ring holds NCCL calls, so `cp` steps are issued
 eagerly between the CUDA events instead of from a CUDA graph (a step lasts
 tens of milliseconds; launch costs are microseconds).
 
@@ -43,6 +45,7 @@ PREFILL_S = 4096
 DECODE_N = 2048
 GDN_T, GDN_STEPS = 4096, 256
 CP_S = 131072
+FRONT_ROTARY = 64  # Qwen3.5: partial_rotary_factor 0.25 of head_dim 256
 L2_BYTES = 126 << 20
 
 # dram bytes (read + write) of one launch of the dominant kernel, from the
@@ -51,7 +54,7 @@ L2_BYTES = 126 << 20
 # capture by the bytes processed), gdn_prefill_decode_t4096.md (prep + scan,
 # one chunked prefill); cp: the 131072-token launch is too large to capture.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_455_424, "gdn": 500_502_272,
-               "batch": 4_452_000_000, "cp": None}
+               "batch": 4_452_000_000, "cp": None, "front": None}
 
 
 def peaks():
@@ -455,9 +458,76 @@ class CpWorkload(Workload):
                 "gate": "sigmoid", "chunk": self.chunk}
 
 
+def front_bytes(rows, heads=HQ, kv_heads=HKV, hd=HD, rotary=FRONT_ROTARY):
+    """Algorithmic bytes of one front-end call: q heads read and written, k
+    read and written (in place) and written to the cache, v read and written
+    to the cache, the two table rows read."""
+    return rows * (2 * heads * hd * 2 + 3 * kv_heads * hd * 2 + 2 * kv_heads * hd * 2
+                   + 2 * (rotary // 2) * 2)
+
+
+class FrontWorkload(Workload):
+    """Head-norm-rope of q and k plus kv-append for one 4096-row block at
+    Qwen3.5 geometry (the front end of the S = 4096 prefill)."""
+
+    def __init__(self, device, rows=PREFILL_S, seed=0x5EED0006):
+        import torch
+        import herbert_b200 as hb
+        self.hb, self.rows = hb, rows
+        gen = torch.Generator(device=device).manual_seed(seed)
+        qd, kvd = HQ * HD, HKV * HD
+        per_set = (rows * 2 * qd + 2 * rows * kvd + 2 * HKV * rows * HD) * 2
+        self.R = self.rotation(per_set)
+        self.sets = []
+        for _ in range(self.R):
+            self.sets.append((_randn_bf16((rows, 2 * qd), gen, device),
+                              _randn_bf16((rows, kvd), gen, device),
+                              _randn_bf16((rows, kvd), gen, device),
+                              torch.empty((HKV, rows, HD), dtype=torch.bfloat16, device=device),
+                              torch.empty((HKV, rows, HD), dtype=torch.bfloat16, device=device)))
+        self.q_norm = (0.1 * torch.randn(HD, generator=gen, device=device)).to(torch.bfloat16)
+        self.k_norm = (0.1 * torch.randn(HD, generator=gen, device=device)).to(torch.bfloat16)
+        half = FRONT_ROTARY // 2
+        pos = torch.arange(rows, dtype=torch.float64, device=device)[:, None]
+        inv = 1e7 ** (-torch.arange(half, dtype=torch.float64, device=device) * 2 / FRONT_ROTARY)
+        self.cos = torch.cos(pos * inv).to(torch.bfloat16)
+        self.sin = torch.sin(pos * inv).to(torch.bfloat16)
+        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
+        self.kv = hb.KvSpec(heads=HKV, head_dim=HD, stride=rows * HD, capacity=rows,
+                            max_batch=rows)
+        self.work = front_bytes(rows)
+        self.units = "GB/s"
+        q, k, v, _, _ = self.sets[0]
+        self.h_in = [t.cpu().pin_memory() for t in (q, k, v)]
+        self.h_out = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
+        self.set_bytes = per_set
+
+    def step(self, i=0):
+        q, k, v, keys, values = self.sets[i % self.R]
+        self.hb.attn_front(self.spec, self.kv, q, k, v, self.q_norm, self.k_norm, self.cos,
+                           self.sin, rows=self.rows, past=0, rotary=FRONT_ROTARY, eps=1e-6,
+                           gemma=True, keys=keys, values=values)
+
+    def e2e_step(self, i=0):
+        q, k, v, _, _ = self.sets[0]
+        for d, h in zip((q, k, v), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step(0)
+        self.h_out.copy_(q, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "attention front end: q/k GemmaRMSNorm head norms + partial RoPE "
+                "(64 of 256) + KV append, one 4096-row block", "rows": self.rows,
+                "q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "rotary": FRONT_ROTARY}
+
+
 METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
-          "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s"}
-BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor"}
+          "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s",
+          "front": "attn front end HBM GB/s"}
+BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor",
+         "front": "hbm"}
 STRONG = ("batch", "cp")  # total work fixed as the GPUs grow
 
 
@@ -472,6 +542,8 @@ def make_workload(cfg, device, rank, world):
         return BatchWorkload(device, rank, world)
     if cfg == "cp":
         return CpWorkload(device, rank, world)
+    if cfg == "front":
+        return FrontWorkload(device)
     raise SystemExit(f"unknown config {cfg}")
 
 
@@ -679,6 +751,17 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
             heads=HQ, gqa=HQ // HKV, head_dim=HD, q_row=inp.q_row, q_head=HD,
             out_row=inp.out_row, gate_offset=inp.gate_offset, kv_stride=inp.kv_stride,
             scale=inp.scale, impl=impl, use_block=0, threads=threads)
+    elif cfg == "front":
+        from herbert_b200.inputs import FrontInputs
+        rows = 256
+        f = FrontInputs(rows, 0, capacity=rows)
+        work = front_bytes(rows)
+        unit, scale = "GB/s", 1e9
+        sample = f"{rows} rows of the 4096-row block (one thread)"
+        threads = 1
+        fn = lambda: oracle.attn_front(  # noqa: E731
+            f.q, f.k, f.v, f.q_norm, f.k_norm, f.cos, f.sin, heads=HQ, kv_heads=HKV,
+            head_dim=HD, rotary=FRONT_ROTARY, past=0, keys=f.keys, values=f.values, impl=impl)
     else:  # gdn
         T = 64
         d = DeltaInputs(T)

@@ -366,6 +366,68 @@ hb_status hb_kv_append(const hb_kv_spec* s, const hb_kv_call* c, hb_stream_t str
   return HB_OK;
 }
 
+hb_status hb_attn_front(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
+                        const hb_front_call* c, hb_stream_t stream) {
+  hb_status r = check_spec(s);
+  if (r != HB_OK) return r;
+  if (!kv || !f || !c) return fail(HB_ERR_ARG, "kv spec, front spec or call is null");
+  const int64_t hkv = s->heads / s->gqa;
+  if (kv->heads != hkv || kv->head_dim != s->head_dim)
+    return fail(HB_DECLINE_GEOMETRY, "KV spec (heads %lld, head_dim %lld) does not match the "
+                "attention spec (%lld KV heads, head_dim %lld)",
+                (long long)kv->heads, (long long)kv->head_dim, (long long)hkv,
+                (long long)s->head_dim);
+  if (!front_serves(s->head_dim, f->rotary))
+    return fail(HB_DECLINE_HEAD_DIM, "head_dim %lld / rotary %lld out of domain (served: head_dim "
+                "128 or 256, rotary a multiple of 32 up to head_dim)",
+                (long long)s->head_dim, (long long)f->rotary);
+  if (!(f->eps == f->eps) || f->eps < 0.f) return fail(HB_ERR_ARG, "eps is NaN or negative");
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty shape (rows=%lld)", (long long)c->rows);
+  if (c->past < 0) return fail(HB_ERR_ARG, "negative past");
+  if (!c->q || !c->k || !c->v || !c->q_norm || !c->k_norm ||
+      (f->rotary > 0 && (!c->cos || !c->sin)) || (!c->keys != !c->values))
+    return fail(HB_ERR_ARG, "null front-end pointer");
+  const void* ptrs[] = {c->q, c->k, c->v, c->q_norm, c->k_norm, c->cos, c->sin, c->keys, c->values};
+  for (const void* ptr : ptrs)
+    if (ptr && !aligned16(ptr)) return fail(HB_ERR_ARG, "front-end pointers must be 16-byte aligned");
+  if (c->rows > 0x3FFFFFFF / (s->heads + hkv) || c->past > kI32Half)
+    return fail(HB_ERR_ARG, "rows or past out of range");
+  if (c->keys) {
+    const bool valid = kv->max_batch > 0 && kv->capacity >= kv->max_batch &&
+                       kv->capacity * kv->head_dim <= kv->stride && kv->stride <= 0x3FFFFFFF &&
+                       kv->stride % 8 == 0;
+    if (!valid) return fail(HB_DECLINE_GEOMETRY, "invalid generated KV reserve geometry");
+    if (c->rows > kv->max_batch || c->past + c->rows > kv->capacity)
+      return fail(HB_ERR_ARG, "append of %lld rows at %lld exceeds the reserve (capacity %lld, batch %lld)",
+                  (long long)c->rows, (long long)c->past, (long long)kv->capacity,
+                  (long long)kv->max_batch);
+  }
+  FrontLaunch L;
+  L.q = c->q;
+  L.k = c->k;
+  L.v = c->v;
+  L.q_norm = c->q_norm;
+  L.k_norm = c->k_norm;
+  L.cos = c->cos;
+  L.sin = c->sin;
+  L.keys = c->keys;
+  L.values = c->values;
+  L.q_row = s->q_row;
+  L.kv_row = hkv * s->head_dim;
+  L.kv_stride = kv->stride;
+  L.past = c->past;
+  L.rows = c->rows;
+  L.heads = s->heads;
+  L.kv_heads = hkv;
+  L.head_dim = s->head_dim;
+  L.rotary = f->rotary;
+  L.eps = f->eps;
+  L.gemma = f->gemma != 0;
+  cudaError_t e = launch_attn_front(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attn_front launch");
+  return HB_OK;
+}
+
 static hb_status check_gdn(const hb_gdn_shape* s, const hb_gdn_call* c) {
   if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or call is null");
   const int64_t lim = int64_t(1) << 16;

@@ -88,6 +88,25 @@ cudaError_t launch_attn_cp_finish(const PrefillLaunch& L, cudaStream_t st);
 // ------------------------------------------------------------ kv append
 cudaError_t launch_kv_append(const hb_kv_spec& s, const hb_kv_call& c, cudaStream_t st);
 
+// ------------------------------------------- attention front end (norm, RoPE)
+struct FrontLaunch {
+  uint16_t* q;
+  uint16_t* k;
+  const uint16_t* v;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  const uint16_t* cos;
+  const uint16_t* sin;
+  uint16_t* keys;    // nullptr: no append
+  uint16_t* values;
+  int64_t q_row, kv_row, kv_stride, past, rows;
+  int64_t heads, kv_heads, head_dim, rotary;
+  float eps;
+  bool gemma;
+};
+bool front_serves(int64_t head_dim, int64_t rotary);
+cudaError_t launch_attn_front(const FrontLaunch& L, cudaStream_t st);
+
 // ------------------------------------------------------------ gdn decode
 struct GdnLaunch {
   hb_gdn_shape shape;

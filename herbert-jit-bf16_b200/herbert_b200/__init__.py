@@ -76,6 +76,17 @@ class KvCall(ctypes.Structure):
                 ("input_values", c_void_p), ("rows", c_int64), ("past", c_int64)]
 
 
+class FrontSpec(ctypes.Structure):
+    """hb_front_spec: rotated elements per head, RMSNorm epsilon, Gemma weight form."""
+    _fields_ = [("rotary", c_int64), ("eps", c_float), ("gemma", c_int32)]
+
+
+class FrontCall(ctypes.Structure):
+    _fields_ = [("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("q_norm", c_void_p),
+                ("k_norm", c_void_p), ("cos", c_void_p), ("sin", c_void_p), ("keys", c_void_p),
+                ("values", c_void_p), ("rows", c_int64), ("past", c_int64)]
+
+
 class DeltaShape(ctypes.Structure):
     _fields_ = [("nk", c_int64), ("nv", c_int64), ("hkd", c_int64), ("hvd", c_int64)]
 
@@ -116,6 +127,8 @@ _SIGNATURES = {
     "hb_attn_prefill": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
                                        c_void_p]),
     "hb_kv_append": (ctypes.c_int, [_P(KvSpec), _P(KvCall), c_void_p]),
+    "hb_attn_front": (ctypes.c_int, [_P(AttentionSpec), _P(KvSpec), _P(FrontSpec), _P(FrontCall),
+                                     c_void_p]),
     "hb_gdn_decode": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceCall), c_void_p]),
     "hb_gdn_prefill_workspace_bytes": (c_size_t, [_P(DeltaShape), c_int64]),
     "hb_gdn_prefill": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceCall), c_void_p, c_size_t,
@@ -280,6 +293,19 @@ def kv_append(spec: KvSpec, keys, values, input_keys, input_values, *, rows: int
     call = KvCall(keys=_ptr(keys), values=_ptr(values), input_keys=_ptr(input_keys),
                   input_values=_ptr(input_values), rows=rows, past=past)
     check(lib().hb_kv_append(ctypes.byref(spec), ctypes.byref(call), _stream(stream)))
+
+
+def attn_front(spec: AttentionSpec, kv: KvSpec, q, k, v, q_norm, k_norm, cos, sin, *,
+               rows: int, past: int, rotary: int, eps: float = 1e-6, gemma: bool = True,
+               keys=None, values=None, stream=None) -> None:
+    """Head-norm-rope of q and k in place, then k and v into the cache (keys/values None:
+    no append).  Device tensors of bf16 bits."""
+    front = FrontSpec(rotary=rotary, eps=eps, gemma=int(gemma))
+    call = FrontCall(q=_ptr(q), k=_ptr(k), v=_ptr(v), q_norm=_ptr(q_norm), k_norm=_ptr(k_norm),
+                     cos=_ptr(cos), sin=_ptr(sin), keys=_ptr(keys), values=_ptr(values),
+                     rows=rows, past=past)
+    check(lib().hb_attn_front(ctypes.byref(spec), ctypes.byref(kv), ctypes.byref(front),
+                              ctypes.byref(call), _stream(stream)))
 
 
 def delta_recurrence(shape: DeltaShape, state, out, qkv, beta, decay, *, rows: int,

@@ -102,3 +102,38 @@ def lpt_assign(sizes, parts: int):
         bins[j].append(int(i))
         load[j] += int(sizes[i])
     return bins
+
+
+class FrontInputs:
+    """One call of the attention front end (head-norm-rope + kv-append).
+
+    q      : [rows, q_row] bf16 bits (the heads' part is transformed)
+    k, v   : [rows, kv_heads*head_dim] bf16 bits
+    q_norm, k_norm : [head_dim] bf16 bits, N(0, 0.1) (Gemma-form weights
+             are small deviations around 0)
+    cos, sin : [capacity, rotary/2] bf16 bits of the RoPE angles
+             pos * 1e7^(-2j/rotary) (Qwen3.5's rope theta)
+    keys, values : [kv_heads, capacity, head_dim] bf16 bits (prior content)
+    """
+
+    def __init__(self, rows, past, heads=QWEN_HEADS, kv_heads=QWEN_KV_HEADS,
+                 head_dim=QWEN_HEAD_DIM, rotary=64, gated=True, gemma=True, capacity=None,
+                 seed=0xF407):
+        self.rows, self.past, self.heads, self.kv_heads = rows, past, heads, kv_heads
+        self.head_dim, self.rotary, self.gemma = head_dim, rotary, gemma
+        self.capacity = capacity or past + rows + 3
+        qd = heads * head_dim
+        self.q_row = 2 * qd if gated else qd
+        self.gated = gated
+        self.q = normal_bf16((rows, self.q_row), seed)
+        self.k = normal_bf16((rows, kv_heads * head_dim), seed + 1)
+        self.v = normal_bf16((rows, kv_heads * head_dim), seed + 2)
+        self.q_norm = f32_to_bf16_bits(np.random.default_rng(seed + 3).standard_normal(head_dim) * 0.1)
+        self.k_norm = f32_to_bf16_bits(np.random.default_rng(seed + 4).standard_normal(head_dim) * 0.1)
+        half = max(rotary // 2, 1)
+        pos = np.arange(self.capacity, dtype=np.float64)[:, None]
+        inv_freq = 1e7 ** (-np.arange(half, dtype=np.float64) * 2 / max(rotary, 2))
+        self.cos = f32_to_bf16_bits(np.cos(pos * inv_freq))
+        self.sin = f32_to_bf16_bits(np.sin(pos * inv_freq))
+        self.keys = normal_bf16((kv_heads, self.capacity, head_dim), seed + 5)
+        self.values = normal_bf16((kv_heads, self.capacity, head_dim), seed + 6)

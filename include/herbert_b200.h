@@ -260,6 +260,41 @@ typedef struct hb_kv_call {
 } hb_kv_call;
 HB_API hb_status hb_kv_append(const hb_kv_spec *spec, const hb_kv_call *call, hb_stream_t stream);
 
+/*
+ * Attention front end of one layer: the head-norm-rope nodes of q and of k
+ * and the kv-append node, in one launch (src/jit/schedule/lowering.rs:549-592;
+ * per head src/jit/target/x86/execution/transforms.rs:30-81).  For each row
+ * r (position past + r) and each q head, then each k head, in place:
+ *   y = bf16((x * rsqrt(sum x^2 / head_dim + eps)) * w')   ElemOp::RmsNormGemma
+ *       (w' = 1 + w in f32) or ElemOp::RmsNorm (w' = w)   (emit_elem.rs:242-330)
+ *   then ElemOp::Rope on elements [0, rotary): pairs (j, j + rotary/2) rotated
+ *   by table row past + r of cos/sin                        (emit_elem.rs:479-514)
+ * then K[h][past + r][:] <- k[r][h][:] and V[h][past + r][:] <- v[r][h][:]
+ * (as hb_kv_append).  Results are the reference's bits.
+ */
+typedef struct hb_front_spec {
+    int64_t rotary;   /* rotated elements per head (Qwen3.5: 64), multiple of 32, <= head_dim */
+    float eps;        /* RMSNorm epsilon (Qwen3.5: 1e-6)                                   */
+    int32_t gemma;    /* 1: w' = 1 + w (GemmaRMSNorm, Qwen3.5), 0: w' = w                   */
+} hb_front_spec;
+typedef struct hb_front_call {
+    uint16_t *q;              /* query rows, stride spec.q_row; heads*head_dim elements per row
+                                 transformed in place (the gate after them is not touched) */
+    uint16_t *k;              /* key rows [rows][kv_heads*head_dim], transformed in place   */
+    const uint16_t *v;        /* value rows [rows][kv_heads*head_dim]                       */
+    const uint16_t *q_norm;   /* [head_dim] bf16 weight of the q head norm                  */
+    const uint16_t *k_norm;   /* [head_dim] bf16 weight of the k head norm                  */
+    const uint16_t *cos;      /* [positions][rotary/2] bf16, row past + r used by row r      */
+    const uint16_t *sin;
+    uint16_t *keys;           /* the layer's K cache (hb_kv_spec layout); NULL: no append  */
+    uint16_t *values;         /* the layer's V cache                                        */
+    int64_t rows;
+    int64_t past;             /* position of row 0                                          */
+} hb_front_call;
+HB_API hb_status hb_attn_front(const hb_attn_spec *spec, const hb_kv_spec *kv,
+                               const hb_front_spec *front, const hb_front_call *call,
+                               hb_stream_t stream);
+
 /* ------------------------------------------------------------- DeltaNet */
 
 /* DeltaNet geometry: Shape (src/jit/execution/abi.rs:266-307) without the conv width. */

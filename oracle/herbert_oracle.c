@@ -500,6 +500,152 @@ int orc_attention(const uint16_t *q, const uint16_t *keys, const uint16_t *value
 
 /* -------------------------------------------------------------- DeltaNet */
 
+/* ------------------------------------------- head norm, RoPE, KV append */
+
+/* ElemOp::RmsNorm / RmsNormGemma of one head, in place
+ * (src/jit/emit_elem.rs:22-41; emitter src/jit/target/x86/emit_elem.rs:242-330):
+ * pass 1 sums x^2 with one vdpbf16ps per 32-element block, block c into
+ * chain c % min(4, blocks), adds the chains 0 + 1, + 2, + 3 (vaddps) and
+ * reduces with hsum (emit_elem.rs:177-186); then, in scalar f32,
+ * x (1/dim), + eps, vsqrtss, 1 / x (vdivss).  Pass 2 per element:
+ * y = bf16((x * inv) * w'), w' = w widened, + 1.0 in f32 for the Gemma
+ * form (never folded into the bf16 weight). */
+static void rms_norm_head_scalar(uint16_t *x, const uint16_t *w, size_t dim, float eps,
+                                 int gemma) {
+    size_t nb = dim / 32, na = nb < 4 ? nb : 4;
+    float acc[4][16];
+    memset(acc, 0, sizeof acc);
+    for (size_t c = 0; c < nb; c++) orc_dpbf16_scalar(acc[c % na], x + 32 * c, x + 32 * c);
+    float a0[16];
+    for (int i = 0; i < 16; i++) {
+        float t = acc[0][i];
+        for (size_t k = 1; k < na; k++) t = t + acc[k][i];
+        a0[i] = t;
+    }
+    float s = hsum16(a0);
+    s = s * (1.0f / (float)dim);
+    s = s + eps;
+    s = sqrtf(s);
+    const float inv = 1.0f / s;
+    for (size_t i = 0; i < dim; i++) {
+        float xw = orc_bf16_to_f32(x[i]);
+        float ww = orc_bf16_to_f32(w[i]);
+        if (gemma) ww = ww + 1.0f;
+        xw = xw * inv;
+        xw = xw * ww;
+        x[i] = orc_f32_to_bf16_cvtne(xw);
+    }
+}
+
+/* ElemOp::Rope on the first `rotary` elements of one head, in place
+ * (src/jit/emit_elem.rs:100-113; emitter src/jit/target/x86/emit_elem.rs:479-514):
+ * pairs (j, j + rotary/2), a' = a c - b s as vmulps then vfnmadd231ps,
+ * b' = a s + b c as vmulps then vfmadd231ps, each rounded by
+ * vcvtneps2bf16.  cos/sin hold rotary/2 bf16 entries for the position. */
+static void rope_head_scalar(uint16_t *x, const uint16_t *cosr, const uint16_t *sinr,
+                             size_t rotary) {
+    const size_t half = rotary / 2;
+    for (size_t j = 0; j < half; j++) {
+        const float a = orc_bf16_to_f32(x[j]), b = orc_bf16_to_f32(x[j + half]);
+        const float c = orc_bf16_to_f32(cosr[j]), sn = orc_bf16_to_f32(sinr[j]);
+        float ra = a * c;
+        ra = fmaf(-b, sn, ra);
+        float rb = a * sn;
+        rb = fmaf(b, c, rb);
+        x[j] = orc_f32_to_bf16_cvtne(ra);
+        x[j + half] = orc_f32_to_bf16_cvtne(rb);
+    }
+}
+
+#if ORC_X86
+/* The same two emitted kernels, instruction by instruction. */
+AVX512_TARGET static void rms_norm_head_avx512(uint16_t *x, const uint16_t *w, size_t dim,
+                                               float eps, int gemma) {
+    size_t nb = dim / 32, na = nb < 4 ? nb : 4;
+    __m512 acc[4] = {_mm512_setzero_ps(), _mm512_setzero_ps(), _mm512_setzero_ps(),
+                     _mm512_setzero_ps()};
+    for (size_t c = 0; c < nb; c++) {
+        __m512bh xx = (__m512bh)_mm512_loadu_si512(x + 32 * c);
+        acc[c % na] = _mm512_dpbf16_ps(acc[c % na], xx, xx);
+    }
+    for (size_t k = 1; k < na; k++) acc[0] = _mm512_add_ps(acc[0], acc[k]);
+    __m128 s = _mm_set_ss(hsum_hw(acc[0]));
+    s = _mm_mul_ss(s, _mm_set_ss(1.0f / (float)dim));
+    s = _mm_add_ss(s, _mm_set_ss(eps));
+    s = _mm_sqrt_ss(s);
+    s = _mm_div_ss(_mm_set_ss(1.0f), s);
+    const __m512 inv = _mm512_set1_ps(_mm_cvtss_f32(s));
+    for (size_t i = 0; i < dim; i += 16) {
+        __m512 xw = load_bf16_f32(x + i), ww = load_bf16_f32(w + i);
+        if (gemma) ww = _mm512_add_ps(ww, bcast(1.0f));
+        xw = _mm512_mul_ps(xw, inv);
+        xw = _mm512_mul_ps(xw, ww);
+        _mm256_storeu_si256((__m256i *)(x + i), (__m256i)_mm512_cvtneps_pbh(xw));
+    }
+}
+
+AVX512_TARGET static void rope_head_avx512(uint16_t *x, const uint16_t *cosr,
+                                           const uint16_t *sinr, size_t rotary) {
+    const size_t half = rotary / 2;
+    for (size_t j = 0; j < half; j += 16) {
+        const __m512 a = load_bf16_f32(x + j), b = load_bf16_f32(x + j + half);
+        const __m512 co = load_bf16_f32(cosr + j), sn = load_bf16_f32(sinr + j);
+        __m512 ra = _mm512_mul_ps(a, co);
+        ra = _mm512_fnmadd_ps(b, sn, ra);
+        __m512 rb = _mm512_mul_ps(a, sn);
+        rb = _mm512_fmadd_ps(b, co, rb);
+        _mm256_storeu_si256((__m256i *)(x + j), (__m256i)_mm512_cvtneps_pbh(ra));
+        _mm256_storeu_si256((__m256i *)(x + j + half), (__m256i)_mm512_cvtneps_pbh(rb));
+    }
+}
+#endif
+
+int orc_attn_front(uint16_t *q, size_t q_row, size_t heads, uint16_t *k, const uint16_t *v,
+                   size_t kv_row, size_t kv_heads, size_t head_dim, const uint16_t *q_norm,
+                   const uint16_t *k_norm, const uint16_t *cos_tab, const uint16_t *sin_tab,
+                   size_t rotary, float eps, int gemma, uint16_t *keys, uint16_t *values,
+                   size_t kv_stride, size_t rows, size_t past, int impl) {
+    if (head_dim == 0 || head_dim % 32 || rotary % 32 || rotary > head_dim) return -1;
+    void (*norm)(uint16_t *, const uint16_t *, size_t, float, int) = rms_norm_head_scalar;
+    void (*rope)(uint16_t *, const uint16_t *, const uint16_t *, size_t) = rope_head_scalar;
+    if (impl == 1) {
+#if ORC_X86
+        if (!orc_has_avx512bf16()) return -1;
+        norm = rms_norm_head_avx512;
+        rope = rope_head_avx512;
+#else
+        return -1;
+#endif
+    }
+    const size_t half = rotary / 2;
+    /* head-norm-rope of q, then of k (src/jit/schedule/lowering.rs:549-578,
+     * heads in order within a row, src/jit/target/x86/execution/transforms.rs:30-81):
+     * row r uses the table row of its position past + r */
+    for (size_t r = 0; r < rows; r++) {
+        const uint16_t *cr = cos_tab + (past + r) * half, *sr = sin_tab + (past + r) * half;
+        for (size_t h = 0; h < heads; h++) {
+            uint16_t *x = q + r * q_row + h * head_dim;
+            norm(x, q_norm, head_dim, eps, gemma);
+            if (rotary) rope(x, cr, sr, rotary);
+        }
+        for (size_t h = 0; h < kv_heads; h++) {
+            uint16_t *x = k + r * kv_row + h * head_dim;
+            norm(x, k_norm, head_dim, eps, gemma);
+            if (rotary) rope(x, cr, sr, rotary);
+        }
+    }
+    /* kv-append (lowering.rs:579-592; src/jit/target/x86/execution/kv.rs:17-69) */
+    if (keys && values)
+        for (size_t r = 0; r < rows; r++)
+            for (size_t h = 0; h < kv_heads; h++) {
+                memcpy(keys + h * kv_stride + (past + r) * head_dim, k + r * kv_row + h * head_dim,
+                       head_dim * 2);
+                memcpy(values + h * kv_stride + (past + r) * head_dim, v + r * kv_row + h * head_dim,
+                       head_dim * 2);
+            }
+    return 0;
+}
+
 /* l2norm (delta.rs:28-62): left-to-right sum of squares, separate multiply
  * and add, then + eps, sqrt, 1/x, multiply. */
 void orc_l2norm(float *x, size_t dim, float eps) {

@@ -126,6 +126,18 @@ int orc_gdn_layer(float *qkv, float *state, float *out, const float *beta,
 
 /* Deterministic inputs: splitmix64 stream, Box-Muller N(0,1) in double,
  * rounded to bf16 (RNE) -- the generator the fixtures use. */
+/* Attention front end of one layer: head-norm-rope of the q heads and of the
+ * k heads, then kv-append (src/jit/schedule/lowering.rs:549-592).  q rows
+ * [rows][q_row] (the first heads*head_dim elements are transformed), k and
+ * v rows [rows][kv_row]; tables [positions][rotary/2]; keys/values may be
+ * NULL (no append).  impl 0: scalar restatement, 1: AVX-512 BF16
+ * transcription (-1 when the CPU lacks it). */
+int orc_attn_front(uint16_t *q, size_t q_row, size_t heads, uint16_t *k, const uint16_t *v,
+                   size_t kv_row, size_t kv_heads, size_t head_dim, const uint16_t *q_norm,
+                   const uint16_t *k_norm, const uint16_t *cos_tab, const uint16_t *sin_tab,
+                   size_t rotary, float eps, int gemma, uint16_t *keys, uint16_t *values,
+                   size_t kv_stride, size_t rows, size_t past, int impl);
+
 void orc_fill_normal_bf16(uint16_t *x, size_t n, uint64_t seed);
 void orc_fill_normal_f64(double *x, size_t n, uint64_t seed);
 

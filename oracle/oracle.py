@@ -13,7 +13,10 @@ The C file restates the reference's x86 AVX-512 BF16 attention-path kernels
   src/jit/target/x86/emit_sdpa/x86/prefill.rs:733-912;
 * output gate ``ElemOp::SigmoidMul`` -- src/jit/target/x86/emit_elem.rs:333-420;
 * DeltaNet L2 norm and recurrence -- src/jit/target/x86/execution/delta.rs:28-62,
-  519-607; src/jit/target/x86/emit_recurrence.rs:108-217.
+  519-607; src/jit/target/x86/emit_recurrence.rs:108-217;
+* attention front end (head-norm-rope of q and k, kv-append) --
+  src/jit/schedule/lowering.rs:549-592, src/jit/target/x86/emit_elem.rs:242-330,
+  479-514, src/jit/target/x86/execution/transforms.rs:30-81.
 
 Parity is unpinned by reference outputs (the Rust reference cannot be built
 in this image and ships no golden vectors); the restatement is pinned to the
@@ -87,6 +90,10 @@ def lib():
                                     _sz, ctypes.c_int, ctypes.c_float, ctypes.c_int,
                                     ctypes.c_int]
         L.orc_gdn_layer.restype = ctypes.c_int
+        L.orc_attn_front.argtypes = [_u16p, _sz, _sz, _u16p, _u16p, _sz, _sz, _sz, _u16p, _u16p,
+                                     _u16p, _u16p, _sz, ctypes.c_float, ctypes.c_int, _u16p,
+                                     _u16p, _sz, _sz, _sz, ctypes.c_int]
+        L.orc_attn_front.restype = ctypes.c_int
         L.orc_fill_normal_bf16.argtypes = [_u16p, _sz, ctypes.c_uint64]
         L.orc_fill_normal_f64.argtypes = [_f64p, _sz, ctypes.c_uint64]
         _lib = L
@@ -188,6 +195,37 @@ def attention(q, keys, values, *, rows, past, heads, gqa, head_dim, q_row, q_hea
 
 
 # -------------------------------------------------------------- DeltaNet
+
+def attn_front(q, k, v, q_norm, k_norm, cos, sin, *, heads, kv_heads, head_dim, rotary, past,
+               eps=1e-6, gemma=True, keys=None, values=None, impl=0):
+    """Head-norm-rope of q and k, then kv-append (src/jit/schedule/lowering.rs:549-592).
+
+    q [rows][q_row], k/v [rows][kv_heads*head_dim], norms [head_dim], tables
+    [positions][rotary/2], caches [kv_heads][capacity][head_dim] (bf16 bits).
+    Returns (q, k, keys, values) as new arrays; the inputs are not modified."""
+    q = np.ascontiguousarray(q, dtype=np.uint16).copy()
+    k = np.ascontiguousarray(k, dtype=np.uint16).copy()
+    v = np.ascontiguousarray(v, dtype=np.uint16)
+    rows = q.shape[0]
+    if keys is not None:
+        keys = np.ascontiguousarray(keys, dtype=np.uint16).copy()
+        values = np.ascontiguousarray(values, dtype=np.uint16).copy()
+        kv_stride = keys.shape[1] * keys.shape[2]
+        kp, vp = _p(keys, _u16p), _p(values, _u16p)
+    else:
+        kv_stride, kp, vp = 0, None, None
+    qn = np.ascontiguousarray(q_norm, dtype=np.uint16)
+    kn = np.ascontiguousarray(k_norm, dtype=np.uint16)
+    ct = np.ascontiguousarray(cos, dtype=np.uint16)
+    st = np.ascontiguousarray(sin, dtype=np.uint16)
+    rc = lib().orc_attn_front(_p(q, _u16p), q.shape[1], heads, _p(k, _u16p), _p(v, _u16p),
+                              k.shape[1], kv_heads, head_dim, _p(qn, _u16p), _p(kn, _u16p),
+                              _p(ct, _u16p), _p(st, _u16p), rotary, eps, int(gemma), kp, vp,
+                              kv_stride, rows, past, impl)
+    if rc != 0:
+        raise RuntimeError(f"orc_attn_front refused (impl={impl})")
+    return q, k, keys, values
+
 
 def l2norm(x, eps=1e-6):
     x = np.array(x, dtype=np.float32, copy=True)

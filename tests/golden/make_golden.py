@@ -18,8 +18,9 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "herbert-jit-bf16_b200"),
                 os.path.join(ROOT, "tests")]
 
-from herbert_b200.inputs import AttentionInputs, DeltaInputs  # noqa: E402
+from herbert_b200.inputs import AttentionInputs, DeltaInputs, FrontInputs  # noqa: E402
 from harness import oracle_attention, oracle_gdn  # noqa: E402
+import oracle as O  # noqa: E402
 
 ATTN_CASES = {
     # name: (rows, past, heads, kv_heads, head_dim, gated)
@@ -51,6 +52,17 @@ def main():
         np.savez_compressed(os.path.join(HERE, name + ".npz"), qkv=inp.qkv, beta=inp.beta,
                             decay=inp.decay, state0=inp.state, out=out, state=st,
                             meta=np.array([rows, nk, nv, hkd, hvd], np.int64))
+    # attention front end (head-norm-rope + kv-append), Qwen3.5 geometry
+    f = FrontInputs(5, 9, seed=0x60D2)
+    q, k, keys, values = O.attn_front(f.q, f.k, f.v, f.q_norm, f.k_norm, f.cos, f.sin,
+                                      heads=f.heads, kv_heads=f.kv_heads, head_dim=f.head_dim,
+                                      rotary=f.rotary, past=f.past, gemma=f.gemma, keys=f.keys,
+                                      values=f.values)
+    np.savez_compressed(os.path.join(HERE, "front_rows5_past9.npz"), q=f.q, k=f.k, v=f.v,
+                        q_norm=f.q_norm, k_norm=f.k_norm, cos=f.cos, sin=f.sin, keys0=f.keys,
+                        values0=f.values, q_out=q, k_out=k, keys=keys, values=values,
+                        meta=np.array([f.rows, f.past, f.heads, f.kv_heads, f.head_dim, f.rotary,
+                                       int(f.gemma), int(f.gated)], np.int64))
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 
