@@ -280,8 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16(BM, BN, false, false);
       constexpr uint32_t idPV = idesc_bf16(BM, HDIM, false, true);
-      const uint32_t qb = smem_u32(smem + OFF_Q), kb = smem_u32(smem + OFF_K),
-                     vb = smem_u32(smem + OFF_V);
+      const uint64_t qd0 = sw128_desc(smem_u32(smem + OFF_Q), 16, 1024),
+                     kd0 = sw128_desc(smem_u32(smem + OFF_K), 16, 1024),
+                     vd0 = sw128_desc(smem_u32(smem + OFF_V), 4096, 1024);
       // S_j = Q K_j^T (M128 N128 K256) into TMEM buffer j % 2; that buffer
       // held P_{j-2}, so PV_{j-2} must have completed
       auto issue_s = [&](int j) -> bool {
@@ -292,8 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_after_sync();
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) {
-            const uint64_t a = sw128_desc(qb + b * SLOT + k4 * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(kb + b * SLOT + k4 * 32, 16, 1024);
+            const uint64_t a = desc_add(qd0, b * SLOT + k4 * 32);
+            const uint64_t bd = desc_add(kd0, b * SLOT + k4 * 32);
             mma_bf16_ss(tmem + S_COL + sb * BN, a, bd, idS, b > 0 || k4 > 0);
           }
           mma_commit(&bar[K_EMPTY + b]);
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k2 = 0; k2 < 2; ++k2) {
             const int kk = c * 2 + k2;
-            const uint64_t bd = sw128_desc(vb + sl * SLOT + k2 * 2048, 4096, 1024);
+            const uint64_t bd = desc_add(vd0, sl * SLOT + k2 * 2048);
             mma_bf16_ts(tmem + O_COL, tmem + S_COL + sb * BN + kk * 8, bd, idPV, j > 0 || kk > 0);
           }
           mma_commit(&bar[V_EMPTY + sl]);

@@ -186,10 +186,11 @@ __global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const PrepParams p) {
   // ---- MMA 1: [K; Q] K^T -> TMEM cols [0, 64)
   if (tid == 0) {
     constexpr uint32_t id = idesc_bf16(128, 64, false, false);
+    const uint64_t sad = sw128_desc(sa, 16, 1024);
 #pragma unroll
     for (int kk = 0; kk < DK / 16; ++kk) {
-      const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-      mma_bf16_ss(tmem, sw128_desc(sa + off, 16, 1024), sw128_desc(sa + off, 16, 1024), id, kk > 0);
+      const uint64_t d = desc_add(sad, (kk >> 2) * 16384 + (kk & 3) * 32);
+      mma_bf16_ss(tmem, d, d, id, kk > 0);
     }
     mma_commit(&bar[0]);
   }
@@ -349,16 +350,17 @@ __global__ void __launch_bounds__(256, 1) gdn_prep_kernel(const PrepParams p) {
   // ---- MMA 2: W = [T0 bg0; T1 bg1] K -> cols [0,128); MMA 3: U -> cols [128,256)
   if (tid == 0) {
     constexpr uint32_t id = idesc_bf16(128, 128, false, true);
-    const uint32_t s2 = smem_u32(smem + P_S2), s3 = smem_u32(smem + P_S3),
-                   sv = smem_u32(smem + P_SV);
+    const uint64_t s2d = sw128_desc(smem_u32(smem + P_S2), 16, 1024),
+                   s3d = sw128_desc(smem_u32(smem + P_S3), 16, 1024),
+                   svd = sw128_desc(smem_u32(smem + P_SV), 16384, 1024),
+                   sak = sw128_desc(sa, 16384, 1024);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk)
-      mma_bf16_ss(tmem, sw128_desc(s2 + kk * 32, 16, 1024), sw128_desc(sa + kk * 2048, 16384, 1024),
-                  id, kk > 0);
+      mma_bf16_ss(tmem, desc_add(s2d, kk * 32), desc_add(sak, kk * 2048), id, kk > 0);
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk)
-      mma_bf16_ss(tmem + 128, sw128_desc(s3 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                  sw128_desc(sv + kk * 2048, 16384, 1024), id, kk > 0);
+      mma_bf16_ss(tmem + 128, desc_add(s3d, (kk >> 2) * 16384 + (kk & 3) * 32),
+                  desc_add(svd, kk * 2048), id, kk > 0);
     mma_commit(&bar[1]);
   }
   __syncwarp();
@@ -537,27 +539,28 @@ __global__ void __launch_bounds__(192, 1) gdn_scan_kernel(const ScanParams p) {
     if (lane == 0) {
       constexpr uint32_t id1 = idesc_bf16(128, BV, false, true);
       constexpr uint32_t id3 = idesc_bf16(128, BV, true, true);
-      const uint32_t sb = smem_u32(smem + S_SB), dl = smem_u32(smem + S_D);
+      const uint64_t sbd = sw128_desc(smem_u32(smem + S_SB), 8192, 1024),
+                     dld = sw128_desc(smem_u32(smem + S_D), 8192, 1024);
       for (int c = 0; c < nc; ++c) {
         const int s = c & 1;
         const uint32_t st = smem_u32(smem + s * STAGE);
+        const uint64_t a1d = sw128_desc(st + S_A1, 16, 1024), a2d = sw128_desc(st + S_A2, 16, 1024),
+                       ktd = sw128_desc(st + S_KT, 8192, 1024);
         if (!wait(FULL + s, (c >> 1) & 1) || !wait(SBF_READY, c & 1)) break;
         fence_after_sync();
         // D0 = [W; Qg] S0  (M128 N64 K128)
 #pragma unroll
         for (int kk = 0; kk < DK / 16; ++kk)
-          mma_bf16_ss(tmem, sw128_desc(st + S_A1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                      sw128_desc(sb + kk * 2048, 8192, 1024), id1, kk > 0);
+          mma_bf16_ss(tmem, desc_add(a1d, (kk >> 2) * 16384 + (kk & 3) * 32),
+                      desc_add(sbd, kk * 2048), id1, kk > 0);
         mma_commit(&bar[D0_FULL]);
         if (!wait(DELTA_FULL, c & 1) || !wait(S_SCALED, c & 1)) break;
         fence_after_sync();
         // D0 += [0; M] D  (rows 64-127 become O);  S += Kt^T D
 #pragma unroll
         for (int kk = 0; kk < C / 16; ++kk) {
-          mma_bf16_ss(tmem, sw128_desc(st + S_A2 + kk * 32, 16, 1024),
-                      sw128_desc(dl + kk * 2048, 8192, 1024), id1, true);
-          mma_bf16_ss(tmem + 64, sw128_desc(st + S_KT + kk * 2048, 8192, 1024),
-                      sw128_desc(dl + kk * 2048, 8192, 1024), id3, true);
+          mma_bf16_ss(tmem, desc_add(a2d, kk * 32), desc_add(dld, kk * 2048), id1, true);
+          mma_bf16_ss(tmem + 64, desc_add(ktd, kk * 2048), desc_add(dld, kk * 2048), id3, true);
         }
         mma_commit(&bar[STEP_DONE]);
         mma_commit(&bar[EMPTY + s]);

@@ -56,6 +56,10 @@ cudaError_t noalloc_scratch(void** ptr);
 int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms);
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
+// The tensor-core form for one sequence of at most 16 x 128 positions at
+// head_dim 256: returns false (nothing launched) when the call is not in
+// its domain, else launches and sets *err.
+bool launch_attn_decode_mma(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err);
 
 // ---------------------------------------------------------- attn prefill
 struct PrefillLaunch {

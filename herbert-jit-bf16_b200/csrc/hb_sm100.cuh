@@ -44,6 +44,13 @@ HB_DEV void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {
                : "memory");
 }
 
+HB_DEV void tma_prefetch_l2_3d(const CUtensorMap* m, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
 HB_DEV void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
@@ -173,6 +180,14 @@ HB_DEV uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   d |= uint64_t(2) << 61;  // SWIZZLE_128B
   return d;
 }
+
+// The descriptor of the same operand layout `byte_off` bytes further on:
+// the start-address field holds address >> 4 in its low 14 bits, and
+// shared-memory addresses stay below 2^18, so the field never carries.
+// Built once per buffer and advanced per MMA, a descriptor costs one add
+// instead of the field packing (the issue loop of an MMA warp is on the
+// critical path of the kernels that use it).
+HB_DEV uint64_t desc_add(uint64_t desc, uint32_t byte_off) { return desc + (byte_off >> 4); }
 
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {

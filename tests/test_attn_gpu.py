@@ -26,6 +26,13 @@ DECODE_CASES = [
     (1, 700, 8, 8, 128, False),     # gqa 1, head_dim 128
     (2, 300, 16, 2, 128, True),     # gqa 8
     (1, 333, 8, 4, 256, True),      # gqa 2
+    # one sequence of 129 .. 2048 positions at head_dim 256: the tensor-core
+    # cluster form (one 128-position tile per CTA)
+    (1, 128, 16, 4, 256, True),     # two tiles, the second holding one position
+    (3, 382, 16, 4, 256, True),     # rows > 1: the fourth tile is empty for rows 0 and 1
+    (1, 1000, 16, 2, 256, True),    # gqa 8
+    (1, 600, 4, 4, 256, False),     # gqa 1, no gate
+    (2, 1500, 16, 4, 256, True),
 ]
 
 
