@@ -17,8 +17,9 @@
 //                        and sum reduced over the tile's 128 positions
 //   O^T = V_t^T P^T      tcgen05 M128 N16 K128 twice (dims 0-127, 128-255):
 //                        V MN-major as the A operand, P^T (bf16) as B
-// The (O, m, l) partial stays in shared memory; after a cluster barrier CTA
-// r merges output slice r of all partials (DSMEM loads), divides by l,
+// Each CTA stores its (m, l) and, to CTA r, the slice of its O partial that
+// r merges into r's shared memory (DSMEM stores); after one cluster barrier
+// CTA r merges output slice r from its own shared memory, divides by l,
 // rounds to bf16 and applies the gate with the reference's steps.  Warp 4
 // loads K and V by TMA (no multicast) and issues the MMAs (lane 0).
 //
@@ -49,7 +50,9 @@ constexpr int M_OFF_P = M_OFF_Q + 8192;     // P^T: 2 blocks [16 rows][128 B]
 constexpr int M_OFF_PART = M_OFF_P + 4096;  // partial: O [G][256] f32, then m[G], l[G]
 constexpr int M_PART_MAX = 8 * HDM * 4 + 64;
 constexpr int M_OFF_RED = M_OFF_PART + M_PART_MAX;  // [2][4 warps][16] maxima, sums
-constexpr int M_OFF_BAR = M_OFF_RED + 2 * 4 * 16 * 4;
+constexpr int M_OFF_RML = M_OFF_RED + 2 * 4 * 16 * 4;  // [16 splits][16]: m[G], l[G] received
+constexpr int M_OFF_RBUF = M_OFF_RML + 16 * 16 * 4;     // received output quads (<= 528 float4)
+constexpr int M_OFF_BAR = M_OFF_RBUF + 528 * 16;
 constexpr int M_SMEM = M_OFF_BAR + 64 + 1024;  // + alignment slack
 constexpr uint32_t M_TMEM_COLS = 64;  // S^T [0, 16), O^T [16, 48)
 enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3 };
@@ -82,18 +85,17 @@ HB_DEV uint32_t dsmem_addr_m(const void* local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
   return r;
 }
-HB_DEV float dsmem_ld_m(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+HB_DEV void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
-HB_DEV float4 dsmem_ld4_m(uint32_t addr) {
-  float4 v;
-  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-      : "r"(addr));
-  return v;
+HB_DEV void st_cluster_v4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
 }
+// Split cluster barrier: arrive early (this CTA has started), wait later.
+HB_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+HB_DEV void cluster_wait_m() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 HB_DEV void cluster_sync_m() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
                    "memory");
@@ -139,6 +141,7 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   fence_after_sync();
   const uint32_t tmem = *tslot;
   griddep_launch_dependents();
+  cluster_arrive_relaxed();  // waited for before the first store into a peer
 
   auto wait = [&](int b, uint32_t parity) -> bool {
     if (*abort_flag) return false;
@@ -308,73 +311,64 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   }
 
   // ------------------------------------------------ merge across the cluster
+  // Every CTA stores its (m, l) into every peer, and into CTA s the output
+  // quads s merges (quads [s nqs, (s + 1) nqs)); after one cluster barrier
+  // each CTA merges its slice from its own shared memory and nothing reads
+  // a peer any more.
+  constexpr int Q4 = G * HDM / 4;
+  const int nqs = (Q4 + ns - 1) / ns;  // quads per slice (the last one may be short)
+  float* rml = reinterpret_cast<float*>(smem + M_OFF_RML);      // [split][16]
+  float4* rbuf = reinterpret_cast<float4*>(smem + M_OFF_RBUF);  // [split][nqs]
+  if (warp < 4) nbar_sync(2, 128);  // this CTA's partial is complete
+  __syncwarp();
+  cluster_wait_m();  // every CTA of the cluster has started
+  if (warp < 4) {
+    for (int i = tid; i < ns * 2 * G; i += 128) {
+      const int sp = i / (2 * G), k = i % (2 * G);
+      st_cluster_f32(dsmem_addr_m(rml + split * 16 + k, uint32_t(sp)), cpart[G * HDM + k]);
+    }
+    for (int q = tid; q < Q4; q += 128) {
+      const int sp = q / nqs, qi = q - sp * nqs;
+      st_cluster_v4(dsmem_addr_m(rbuf + split * nqs + qi, uint32_t(sp)),
+                    *reinterpret_cast<const float4*>(cpart + q * 4));
+    }
+  }
   fence_before_sync();
   __syncwarp();
-  cluster_sync_m();  // every CTA's partial is complete
+  cluster_sync_m();  // every store into this CTA has landed
   if (warp < 4) {
-    // scratch over the K tile (its products are done)
-    float* sml = reinterpret_cast<float*>(smem + M_OFF_K);  // [ns][2G]: m then l of every split
-    float* smw = sml + ns * 2 * G;                          // [ns][G]: 2^(m_s - M)
-    float* smL = smw + ns * G;                              // [G]: merged sums
-    float4* red = reinterpret_cast<float4*>(smem + M_OFF_K + 8192);  // [ns][nq]
-    constexpr int Q4 = G * HDM / 4;
-    const int qb = split * Q4 / ns, qe = (split + 1) * Q4 / ns, nq = qe - qb;
-    for (int i = tid; i < ns * 2 * G; i += 128)
-      sml[i] = dsmem_ld_m(dsmem_addr_m(cpart + G * HDM + (i % (2 * G)), uint32_t(i / (2 * G))));
-    nbar_sync(2, 128);
-    if (tid < G) {
-      float M = -INFINITY;
-      for (int sp = 0; sp < ns; ++sp) M = fmaxf(M, sml[sp * 2 * G + tid]);
+    // the splits' weights 2^(m_r - M) and the merged sums, one warp per head
+    float* wb = reinterpret_cast<float*>(smem + M_OFF_K);  // [split][16] (the K tile is done)
+    float* Lb = wb + 16 * 16;                              // [G]
+    for (int g = warp; g < G; g += 4) {
+      const float mv = lane < ns ? rml[lane * 16 + g] : -INFINITY;
+      const float lv = lane < ns ? rml[lane * 16 + G + g] : 0.f;
+      const float M = warp_max(mv);
       const float Mu = M == -INFINITY ? 0.f : M;
-      float Ls = 0.f;
-      for (int sp = 0; sp < ns; ++sp) {
-        const float w = fast_exp2(sml[sp * 2 * G + tid] - Mu);
-        smw[sp * G + tid] = w;
-        Ls += sml[sp * 2 * G + G + tid] * w;
-      }
-      smL[tid] = Ls;
+      const float w = lane < ns ? fast_exp2(mv - Mu) : 0.f;
+      const float L = warp_sum(lv * w);
+      if (lane < ns) wb[lane * 16 + g] = w;
+      if (lane == 0) Lb[g] = L;
     }
     nbar_sync(2, 128);
-    // one 16-byte read per (output quad, split), all in flight, then the
-    // splits of each quad summed through shared memory
-    for (int idx = tid; idx < nq * ns; idx += 128) {
-      const int sp = idx / nq, qi = idx % nq, e = (qb + qi) * 4, g = e / HDM;
-      const float4 v = dsmem_ld4_m(dsmem_addr_m(cpart + e, uint32_t(sp)));
-      const float w = smw[sp * G + g];
-      red[idx] = make_float4(w * v.x, w * v.y, w * v.z, w * v.w);
-    }
-    nbar_sync(2, 128);
+    // one output element per thread: the splits' weighted sum, / l, bf16,
+    // the gate with the reference's steps
+    const int q0 = split * nqs, nq = max(0, min(nqs, Q4 - q0));
     uint16_t* orow = p.out + int64_t(row) * p.out_row;
     if (!*abort_flag) {
-      for (int qi = tid; qi < nq; qi += 128) {
-        const int e = (qb + qi) * 4, g = e / HDM, dd = e % HDM, hq = h0 + g;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int sp = 0; sp < ns; ++sp) {
-          const float4 v = red[sp * nq + qi];
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        const float Ls = smL[g];
+      const float* rf = reinterpret_cast<const float*>(rbuf);
+      for (int t = tid; t < 4 * nq; t += 128) {
+        const int e = q0 * 4 + t, g = e / HDM, dd = e % HDM;
+        float acc = 0.f;
+        for (int r = 0; r < ns; ++r) acc = fmaf(wb[r * 16 + g], rf[r * nqs * 4 + t], acc);
+        const float Ls = Lb[g];
         const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-        uint16_t a[4] = {f32_to_bf16_cvtne(acc.x * inv), f32_to_bf16_cvtne(acc.y * inv),
-                         f32_to_bf16_cvtne(acc.z * inv), f32_to_bf16_cvtne(acc.w * inv)};
-        if (p.gate_offset >= 0) {
-          const uint2 gw =
-              *reinterpret_cast<const uint2*>(qrow + p.gate_offset + int64_t(hq) * HDM + dd);
-          a[0] = gate_bf16(a[0], uint16_t(gw.x & 0xFFFFu));
-          a[1] = gate_bf16(a[1], uint16_t(gw.x >> 16));
-          a[2] = gate_bf16(a[2], uint16_t(gw.y & 0xFFFFu));
-          a[3] = gate_bf16(a[3], uint16_t(gw.y >> 16));
-        }
-        *reinterpret_cast<uint2*>(orow + int64_t(hq) * HDM + dd) =
-            make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
+        uint16_t a = f32_to_bf16_cvtne(acc * inv);
+        if (p.gate_offset >= 0) a = gate_bf16(a, qrow[p.gate_offset + int64_t(h0 + g) * HDM + dd]);
+        orow[int64_t(h0 + g) * HDM + dd] = a;
       }
     }
   }
-  __syncwarp();
-  cluster_sync_m();  // the peers are done reading this CTA's partial
   if (warp == 4) {
     fence_after_sync();
     tmem_dealloc(tmem, M_TMEM_COLS);
