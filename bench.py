@@ -53,8 +53,8 @@ L2_BYTES = 126 << 20
 # attn_decode_n2048.md, attn_decode_batch64.md (scaled from the n = 2048
 # capture by the bytes processed), gdn_prefill_decode_t4096.md (prep + scan,
 # one chunked prefill); cp: the 131072-token launch is too large to capture.
-NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_455_424, "gdn": 500_502_272,
-               "batch": 4_452_000_000, "cp": None, "front": None}
+NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
+               "batch": 4_452_000_000, "cp": None, "front": 56_784_128}
 
 
 def peaks():
