@@ -11,9 +11,12 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
            (zig-zag shards, K/V ring by NCCL send/recv, LSE merge)      TFLOP/s
   front    attention front end of a 4096-row block: q/k head norms,
            partial RoPE, KV append                                      GB/s
+  gdn_front  DeltaNet front end of a 4096-row block: causal conv + SiLU
+           over qkv (8192 channels, K 4), beta/decay gates               GB/s
+  gdn_norm   DeltaNet gated RMS norm of a 4096-row block (32 V heads)    GB/s
 A step is one pass of the path over one batch: one prefill / one decode step /
 one GDN prefill + 256 steps / one decode step of the whole batch / one
-131072-token prefill / one front-end call.  The ring holds NCCL calls, so `cp` steps are issued
+131072-token prefill / one front-end (or gated-norm) call.  The ring holds NCCL calls, so `cp` steps are issued
 eagerly between the CUDA events instead of from a CUDA graph (a step lasts
 tens of milliseconds; launch costs are microseconds).
 
@@ -54,7 +57,8 @@ L2_BYTES = 126 << 20
 # capture by the bytes processed), gdn_prefill_decode_t4096.md (prep + scan,
 # one chunked prefill); cp: the 131072-token launch is too large to capture.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
-               "batch": 4_452_000_000, "cp": None, "front": 56_784_128}
+               "batch": 4_452_000_000, "cp": None, "front": 56_784_128, "gdn_front": None,
+               "gdn_norm": None}
 
 
 def peaks():
@@ -523,11 +527,128 @@ class FrontWorkload(Workload):
                 "q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "rotary": FRONT_ROTARY}
 
 
+def gdn_front_bytes(rows, nk=NK, nv=NV, hkd=HKD, hvd=HVD, ck=4):
+    """Algorithmic bytes of one DeltaNet front-end call: qkv read and written
+    (in place), the conv state read and written, the conv weights, ab read,
+    beta and decay written, dt_bias and a_log."""
+    conv = 2 * nk * hkd + nv * hvd
+    return (rows * conv * 4 * 2 + conv * ck * 4 * 2 + conv * ck * 2 + rows * 2 * nv * 4
+            + rows * nv * 4 * 2 + nv * 2 + nv * 4)
+
+
+def gdn_norm_bytes(rows, nv=NV, hvd=HVD):
+    """Algorithmic bytes of one gated-norm call: x and z read (f32), the bf16
+    output written, the weight read (the f32 copy is not written)."""
+    return rows * nv * hvd * (4 + 4 + 2) + hvd * 2
+
+
+class GdnFrontWorkload(Workload):
+    """Causal conv + SiLU over the qkv projection (in place) and the beta /
+    decay gates for one 4096-row block at Qwen3.5 geometry."""
+
+    def __init__(self, device, rows=GDN_T, seed=0x5EED0007):
+        import torch
+        import herbert_b200 as hb
+        self.hb, self.rows = hb, rows
+        gen = torch.Generator(device=device).manual_seed(seed)
+        conv = 2 * NK * HKD + NV * HVD
+        self.shape = hb.DeltaShape(nk=NK, nv=NV, hkd=HKD, hvd=HVD)
+        per_set = rows * conv * 4 + rows * 2 * NV * 4 + rows * NV * 4 * 2
+        self.R = self.rotation(per_set)
+        self.sets = []
+        for _ in range(self.R):
+            self.sets.append((torch.randn((rows, conv), generator=gen, device=device),
+                              2.0 * torch.randn((rows, 2 * NV), generator=gen, device=device),
+                              torch.empty((rows, NV), dtype=torch.float32, device=device),
+                              torch.empty((rows, NV), dtype=torch.float32, device=device)))
+        self.state = torch.randn((conv, 4), generator=gen, device=device)
+        self.weight = (0.25 * torch.randn((conv, 4), generator=gen, device=device)).to(
+            torch.bfloat16)
+        dt = torch.exp(torch.empty(NV, device=device).uniform_(-6.9, -2.3, generator=gen))
+        self.dt_bias = (dt + torch.log(-torch.expm1(-dt))).to(torch.bfloat16)
+        self.a_log = torch.log(torch.empty(NV, device=device).uniform_(1.0, 16.0, generator=gen))
+        self.ws = hb.Workspace(256, device)
+        self.work = gdn_front_bytes(rows)
+        self.units = "GB/s"
+        qkv, ab, beta, decay = self.sets[0]
+        self.h_in = [t.cpu().pin_memory() for t in (qkv, ab)]
+        self.h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (qkv, beta, decay)]
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(*self.h_out)
+        self.set_bytes = per_set
+
+    def step(self, i=0):
+        qkv, ab, beta, decay = self.sets[i % self.R]
+        self.hb.delta_front(self.shape, qkv, self.state, self.weight, ab, self.dt_bias,
+                            self.a_log, beta, decay, rows=self.rows, ck=4, workspace=self.ws)
+
+    def e2e_step(self, i=0):
+        qkv, ab, beta, decay = self.sets[0]
+        for d, h in zip((qkv, ab), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step(0)
+        for h, d in zip(self.h_out, (qkv, beta, decay)):
+            h.copy_(d, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "DeltaNet front end: causal depthwise conv (K 4) + SiLU over the "
+                "qkv projection in place, beta/decay gates; one 4096-row block", "rows": self.rows,
+                "key_heads": NK, "value_heads": NV, "head_k_dim": HKD, "head_v_dim": HVD,
+                "conv_channels": 2 * NK * HKD + NV * HVD}
+
+
+class GdnNormWorkload(Workload):
+    """Gated RMS norm of the recurrence output for one 4096-row block at
+    Qwen3.5 geometry (bf16 output only, the out-projection's input)."""
+
+    def __init__(self, device, rows=GDN_T, seed=0x5EED0008):
+        import torch
+        import herbert_b200 as hb
+        self.hb, self.rows = hb, rows
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.shape = hb.DeltaShape(nk=NK, nv=NV, hkd=HKD, hvd=HVD)
+        vd = NV * HVD
+        per_set = rows * vd * (4 + 4 + 2)
+        self.R = self.rotation(per_set)
+        self.sets = []
+        for _ in range(self.R):
+            self.sets.append((0.05 * torch.randn((rows, vd), generator=gen, device=device),
+                              torch.randn((rows, vd), generator=gen, device=device),
+                              torch.empty((rows, vd), dtype=torch.bfloat16, device=device)))
+        self.weight = (1.0 + 0.1 * torch.randn(HVD, generator=gen, device=device)).to(
+            torch.bfloat16)
+        self.work = gdn_norm_bytes(rows)
+        self.units = "GB/s"
+        x, z, out = self.sets[0]
+        self.h_in = [t.cpu().pin_memory() for t in (x, z)]
+        self.h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
+        self.set_bytes = per_set
+
+    def step(self, i=0):
+        x, z, out = self.sets[i % self.R]
+        self.hb.delta_gated_norm(self.shape, x, z, self.weight, out, rows=self.rows, eps=1e-6)
+
+    def e2e_step(self, i=0):
+        x, z, out = self.sets[0]
+        for d, h in zip((x, z), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step(0)
+        self.h_out.copy_(out, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "DeltaNet gated RMS norm: y = rmsnorm(x) w silu(z) per V head, bf16 "
+                "out; one 4096-row block", "rows": self.rows, "value_heads": NV,
+                "head_v_dim": HVD}
+
+
 METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
           "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s",
-          "front": "attn front end HBM GB/s"}
+          "front": "attn front end HBM GB/s", "gdn_front": "GDN front end HBM GB/s",
+          "gdn_norm": "GDN gated norm HBM GB/s"}
 BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor",
-         "front": "hbm"}
+         "front": "hbm", "gdn_front": "hbm", "gdn_norm": "hbm"}
 STRONG = ("batch", "cp")  # total work fixed as the GPUs grow
 
 
@@ -544,6 +665,10 @@ def make_workload(cfg, device, rank, world):
         return CpWorkload(device, rank, world)
     if cfg == "front":
         return FrontWorkload(device)
+    if cfg == "gdn_front":
+        return GdnFrontWorkload(device)
+    if cfg == "gdn_norm":
+        return GdnNormWorkload(device)
     raise SystemExit(f"unknown config {cfg}")
 
 
@@ -667,7 +792,7 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "strong" if cfg in STRONG else "weak",
             "vs_baseline": None,
-            "dtype": "bf16" if cfg != "gdn" else "f32",
+            "dtype": "f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else "bf16",
             "data": "synthetic",
             "config": dict(wl.describe(), parallelism=(
                 f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
@@ -762,6 +887,22 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
         fn = lambda: oracle.attn_front(  # noqa: E731
             f.q, f.k, f.v, f.q_norm, f.k_norm, f.cos, f.sin, heads=HQ, kv_heads=HKV,
             head_dim=HD, rotary=FRONT_ROTARY, past=0, keys=f.keys, values=f.values, impl=impl)
+    elif cfg in ("gdn_front", "gdn_norm"):
+        from herbert_b200.inputs import DeltaFrontInputs
+        rows = 256
+        d = DeltaFrontInputs(rows)
+        unit, scale = "GB/s", 1e9
+        threads = 1
+        sample = f"{rows} rows of the 4096-row block (one thread)"
+        if cfg == "gdn_front":
+            work = gdn_front_bytes(rows)
+
+            def fn():
+                oracle.gdn_conv(d.qkv, d.conv_state, d.conv_weight, impl)
+                oracle.gdn_gates(d.ab, d.dt_bias, d.a_log)
+        else:
+            work = gdn_norm_bytes(rows)
+            fn = lambda: oracle.gdn_gated_norm(d.x, d.z, d.norm_weight, 1e-6, impl)  # noqa: E731
     else:  # gdn
         T = 64
         d = DeltaInputs(T)
@@ -802,7 +943,7 @@ def run_reference(args):
         "metric": METRIC[cfg], "value": v, "unit": base["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong" if cfg in STRONG else "weak", "vs_baseline": None,
-        "dtype": "bf16" if cfg != "gdn" else "f32", "data": "synthetic",
+        "dtype": "f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else "bf16", "data": "synthetic",
         "config": {"workload": cfg, "note": "CPU restatement of the reference's x86 AVX-512 BF16 "
                    "kernels (Rust reference not buildable here)"},
         "cpu_baseline": dict(base, value=v),

@@ -1,0 +1,412 @@
+// gdn_front.cu -- the DeltaNet front and back ends of one layer on sm_100a:
+// the causal depthwise conv + SiLU over the qkv projection and the beta /
+// decay gates (one launch), and the gated RMS norm of the recurrence output.
+//
+// Replaces, for the x86 AVX-512 path of the reference:
+//  * delta-causal-convolution (src/jit/target/x86/execution/delta.rs:609-705):
+//    per channel, state[0..ck) <- state[1..ck) ++ x, y = silu(sum_j state_j w_j).
+//    Channels of full 16-channel blocks at ck = 4 take the vector kernel
+//    (src/jit/target/x86/emit_conv.rs:141-211): products summed as
+//    (p0 + p1) + (p2 + p3), SiLU g / (1 + exp(min(0 - g, 88))) with the emitted
+//    exp polynomial.  The other channels (a ragged last block, or every channel
+//    when ck != 4) take the scalar body (delta_scalar.rs:85-155): products
+//    added in tap order from +0, SiLU with the scalar exp of -g.
+//  * the gate part of delta-l2-gates (delta.rs:290-389), task row*nv + h:
+//    beta = 1 / (exp(-b) + 1); dt = a + bf16(dt_bias); dt = log(exp(dt) + 1)
+//    unless dt > 20; decay = exp((-exp(a_log)) dt).
+//  * delta-normed-gate (delta.rs:706-774): per (row, V head) of width dim,
+//    inv = 1 / sqrt(sum x^2 / dim + eps); y = ((x inv) w) silu(z).  dim a
+//    multiple of 16 up to 128 takes the vector kernel
+//    (src/jit/target/x86/emit_gated_norm.rs:112-169: sum of squares in
+//    min(4, dim/16) FMA chains of 16 lanes, chains added in order, the hsum
+//    tree; SiLU with the exp polynomial; bf16 by vcvtneps2bf16); other widths
+//    the scalar body (delta_scalar.rs:159-239: sum in order from +0, scalar
+//    exp, bf16 by the wrapping integer rounding).
+//
+// The scalar exp and log are the reference's emitted routines
+// (src/jit/target/x86/execution/math.rs, FMA form): the published Arm
+// optimized-routines expf / logf, evaluated in double.  Every step below is
+// one IEEE operation of the reference's sequence, so results are its bits
+// (NaN payloads excepted).
+//
+// Layout in HBM (the reference's): qkv [rows][conv] f32 (conv = 2 nk hkd +
+// nv hvd), conv state [conv][ck] f32, conv weights [conv][ck] bf16, ab
+// [rows][2 nv] f32 (a then b), beta / decay [rows][nv] f32; gated norm x, z
+// [rows][nv hvd] f32, weight [hvd] bf16, out [rows][nv hvd] bf16.
+//
+// Conv decomposition: one CTA per strip of 32 channels walks every row of
+// the strip, so the in-place update needs no ordering between CTAs.  TMA
+// brings boxes of 64 rows x 32 channels (8 KB) into a six-slot ring; a box
+// stays resident while the next one is computed (its last rows are that
+// box's taps), so four boxes are in flight while one is computed.  Thread
+// (g, l) computes channel l of rows g, g + 8, .. of a box and stores
+// straight to HBM (a warp writes one 128-byte row segment).  HBM-bound: every element is read once and
+// written once.  Gates: CTAs past the strips, one task per thread.
+// Gated norm: one warp per (row, V head).
+
+#include <cuda.h>
+
+#include "hb_internal.h"
+#include "hb_sm100.cuh"
+
+namespace hb {
+namespace {
+
+// ----------------------------------------------------- scalar exp and log
+
+// Table data of the published expf / logf algorithm (Arm optimized-routines,
+// the reference's src/jit/execution/math_data.rs).  kExpT[i] is
+// bits(2^(i/32)) - (i << 47); kLogT[i] = {invc_i, log(1/invc_i)}.
+__device__ const uint64_t kExpT[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+__device__ const uint64_t kLogT[16][2] = {
+    {0x3ff661ec79f8f3beull, 0xbfd57bf7808caadeull}, {0x3ff571ed4aaf883dull, 0xbfd2bef0a7c06ddbull},
+    {0x3ff49539f0f010b0ull, 0xbfd01eae7f513a67ull}, {0x3ff3c995b0b80385ull, 0xbfcb31d8a68224e9ull},
+    {0x3ff30d190c8864a5ull, 0xbfc6574f0ac07758ull}, {0x3ff25e227b0b8ea0ull, 0xbfc1aa2bc79c8100ull},
+    {0x3ff1bb4a4a1a343full, 0xbfba4e76ce8c0e5eull}, {0x3ff12358f08ae5baull, 0xbfb1973c5a611cccull},
+    {0x3ff0953f419900a7ull, 0xbfa252f438e10c1eull}, {0x3ff0000000000000ull, 0x0000000000000000ull},
+    {0x3fee608cfd9a47acull, 0x3faaa5aa5df25984ull}, {0x3feca4b31f026aa0ull, 0x3fbc5e53aa362eb4ull},
+    {0x3feb2036576afce6ull, 0x3fc526e57720db08ull}, {0x3fe9c2d163a1aa2dull, 0x3fcbc2860d224770ull},
+    {0x3fe886e6037841edull, 0x3fd1058bc8a07ee1ull}, {0x3fe767dcf5534862ull, 0x3fd4043057b6ee09ull}};
+
+HB_DEV double dbits(uint64_t b) { return __longlong_as_double(static_cast<long long>(b)); }
+
+// exp (math.rs:23-104).  |x| >= 88: -inf -> 0, NaN / +inf -> x + x,
+// x > 88.72284 -> +inf, x < -103.972084 -> 0, else the core.  Core:
+// z = (32/ln2) x + 1.5*2^52 fused, k = low bits of z, r = (32/ln2) x - (z -
+// 1.5*2^52) fused, s = table[k % 32] with k/32 added to the exponent,
+// y = ((E0 r + E1) r^2 + (E2 r + 1)) s, rounded to f32.
+HB_DEV float expf_ref(float x) {
+  const uint32_t ux = __float_as_uint(x), ax = ux & 0x7FFFFFFFu;
+  if (ax >= 0x42B00000u) {
+    if (ux == 0xFF800000u) return 0.0f;
+    if (ax >= 0x7F800000u) return __fadd_rn(x, x);
+    if (x > 88.72284f) return __uint_as_float(0x7F800000u);
+    if (x < -103.972084f) return 0.0f;
+  }
+  const double inv = dbits(0x40471547652b82feull), shift = dbits(0x4338000000000000ull);
+  const double xd = static_cast<double>(x);
+  const double z = __fma_rn(inv, xd, shift);
+  const uint64_t ki = static_cast<uint64_t>(__double_as_longlong(z));
+  const double kd = __dsub_rn(z, shift);
+  const double r = __fma_rn(inv, xd, -kd);
+  const double s = dbits(kExpT[ki & 31] + (ki << 47));
+  const double p = __fma_rn(r, dbits(0x3ebc6af84b912394ull), dbits(0x3f2ebfce50fac4f3ull));
+  const double r2 = __dmul_rn(r, r);
+  const double q = __fma_rn(r, dbits(0x3f962e42ff0c52d6ull), 1.0);
+  return __double2float_rn(__dmul_rn(__fma_rn(p, r2, q), s));
+}
+
+// log (math.rs:114-199).  1 -> +0; outside the positive normal range:
+// +-0 -> -inf, +inf -> +inf, NaN / negative -> NaN, subnormals scaled by
+// 2^23.  Core: tmp = ix - 0x3f330000 gives subinterval i (bits 19..22) and
+// exponent k (tmp >> 23, arithmetic); z = x 2^-k; r = z invc - 1 fused,
+// y0 = k ln2 + logc fused, y = (L0 r^2 + (L1 r + L2)) r^2 + (r + y0).
+HB_DEV float logf_ref(float x) {
+  uint32_t ix = __float_as_uint(x);
+  if (ix == 0x3F800000u) return 0.0f;
+  if (ix - 0x00800000u > 0x7EFFFFFFu) {
+    if (ix * 2u == 0u) return __uint_as_float(0xFF800000u);
+    if (ix == 0x7F800000u) return x;
+    if (ix * 2u >= 0xFF000000u || (ix & 0x80000000u)) return __uint_as_float(0x7FC00000u);
+    ix = __float_as_uint(__fmul_rn(x, 8388608.0f)) - (23u << 23);
+  }
+  const uint32_t tmp = ix - 0x3F330000u;
+  const int i = static_cast<int>((tmp >> 19) & 15u);
+  const int k = static_cast<int32_t>(tmp) >> 23;
+  const double z = static_cast<double>(__uint_as_float(ix - (tmp & 0xFF800000u)));
+  const double r = __fma_rn(z, dbits(kLogT[i][0]), -1.0);
+  const double y0 = __fma_rn(static_cast<double>(k), dbits(0x3fe62e42fefa39efull), dbits(kLogT[i][1]));
+  double y = __fma_rn(r, dbits(0x3fd5575b0be00b6aull), dbits(0xbfdffffef20a4123ull));
+  const double r2 = __dmul_rn(r, r);
+  const double yr = __dadd_rn(r, y0);
+  y = __fma_rn(r2, dbits(0xbfd00ea348b88334ull), y);
+  return __double2float_rn(__fma_rn(r2, y, yr));
+}
+
+HB_DEV float neg(float x) { return __uint_as_float(__float_as_uint(x) ^ 0x80000000u); }
+
+// SiLU of the vector kernels: g / (1 + exp(min(0 - g, 88))), the polynomial
+// exp (vminps gives 88 for NaN, as fminf).
+HB_DEV float silu_poly(float g) {
+  float e = fminf(__fsub_rn(0.0f, g), 88.0f);
+  e = __fadd_rn(exp_poly(e), 1.0f);
+  return __fdiv_rn(g, e);
+}
+
+// SiLU of the scalar bodies: g / (exp(-g) + 1) with the scalar exp.
+HB_DEV float silu_scalar(float g) { return __fdiv_rn(g, __fadd_rn(expf_ref(neg(g)), 1.0f)); }
+
+// --------------------------------------------------------- conv + gates
+
+constexpr int kStrip = 32;   // channels per CTA: one 128-byte row segment
+constexpr int kBox = 64;     // rows per TMA box
+constexpr int kStages = 6;   // ring slots (one computed, one resident, four in flight)
+constexpr int kFrontThreads = 256;
+constexpr int kRowGroups = kFrontThreads / kStrip;  // 8
+constexpr int kMaxCk = 8;
+
+struct FrontParams {
+  float* qkv;
+  float* state;
+  const uint16_t* weight;
+  int conv, rows, ck, vec_channels, nbox, box_rows, n_strips;
+  const float* ab;
+  const uint16_t* dt_bias;
+  const float* a_log;
+  float* beta;
+  float* decay;
+  int nv, n_tasks;
+  int* status;
+};
+
+struct __align__(128) FrontSmem {
+  float ring[kStages][kBox][kStrip];
+  float old_state[kStrip][kMaxCk];
+  uint64_t full[kStages];
+  int abort;
+};
+
+// One gate task (delta.rs:290-389).
+__device__ void gate_task(const FrontParams& p, int task) {
+  const int row = task / p.nv, h = task - row * p.nv;
+  const float* r = p.ab + static_cast<size_t>(row) * 2 * p.nv;
+  const float e = __fadd_rn(expf_ref(neg(r[p.nv + h])), 1.0f);
+  p.beta[task] = __fdiv_rn(1.0f, e);
+  float dt = __fadd_rn(r[h], bf16_to_f32(p.dt_bias[h]));
+  if (!(dt > 20.0f)) dt = logf_ref(__fadd_rn(expf_ref(dt), 1.0f));
+  const float m = neg(expf_ref(p.a_log[h]));
+  p.decay[task] = expf_ref(__fmul_rn(m, dt));
+}
+
+__global__ void __launch_bounds__(kFrontThreads)
+    gdn_front_kernel(const __grid_constant__ CUtensorMap tmX, const FrontParams p) {
+  if (static_cast<int>(blockIdx.x) >= p.n_strips) {
+    const int task = (static_cast<int>(blockIdx.x) - p.n_strips) * kFrontThreads + threadIdx.x;
+    if (task < p.n_tasks) gate_task(p, task);
+    return;
+  }
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  FrontSmem& S = *reinterpret_cast<FrontSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, l = tid % kStrip, g = tid / kStrip;
+  const int c0 = blockIdx.x * kStrip, c = c0 + l;
+  const bool active = c < p.conv;
+  const int ck = p.ck;
+  const uint32_t box_bytes = uint32_t(p.box_rows) * kStrip * 4u;
+
+  if (tid == 0) {
+    sm100::prefetch_tmap(&tmX);
+    for (int s = 0; s < kStages; s++) mbar_init(&S.full[s], 1);
+    fence_mbar_init();
+    S.abort = 0;
+    for (int j = 0; j < kStages - 1 && j < p.nbox; j++) {
+      mbar_arrive_expect_tx(&S.full[j], box_bytes);
+      sm100::tma_load_2d(&S.ring[j][0][0], &tmX, &S.full[j], c0, j * kBox);
+    }
+  }
+  if (g == 0 && active)
+    for (int m = 0; m < ck; m++) S.old_state[l][m] = p.state[static_cast<size_t>(c) * ck + m];
+  __syncthreads();
+
+  const bool vec = c < p.vec_channels;
+  const uint16_t* wc = p.weight + static_cast<size_t>(active ? c : 0) * ck;
+  float w[4];
+#pragma unroll
+  for (int m = 0; m < 4; m++) w[m] = vec ? bf16_to_f32(wc[m]) : 0.0f;
+
+  for (int j = 0; j < p.nbox; j++) {
+    const int s = j % kStages, sp = (j + kStages - 1) % kStages;
+    if (!mbar_wait(&S.full[s], (j / kStages) & 1)) S.abort = 1;
+    // input x of row r (r >= j*kBox - kBox): this box, the previous one, or
+    // the state before the block
+    auto tap = [&](int r) -> float {
+      if (r >= j * kBox) return S.ring[s][r - j * kBox][l];
+      if (r >= 0) return S.ring[sp][r - (j - 1) * kBox][l];
+      return S.old_state[l][ck + r];
+    };
+    if (active) {
+#pragma unroll 2
+      for (int i = 0; i < kBox / kRowGroups; i++) {
+        const int r = j * kBox + g + i * kRowGroups;
+        if (r >= p.rows || r - j * kBox >= p.box_rows) break;
+        float y;
+        if (vec) {
+          const float p0 = __fmul_rn(tap(r - 3), w[0]), p1 = __fmul_rn(tap(r - 2), w[1]);
+          const float p2 = __fmul_rn(tap(r - 1), w[2]), p3 = __fmul_rn(tap(r), w[3]);
+          y = silu_poly(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)));
+        } else {
+          float acc = 0.0f;
+          for (int m = 0; m < ck; m++)
+            acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(wc[m]), tap(r - ck + 1 + m)));
+          y = silu_scalar(acc);
+        }
+        p.qkv[static_cast<size_t>(r) * p.conv + c] = y;
+      }
+    }
+    __syncthreads();
+    if (S.abort) {
+      if (tid == 0) {
+        // leave no copy in flight into this CTA's shared memory: boxes j ..
+        // j + kStages - 2 have been issued (bounded waits)
+        record_status(p.status, kStatusTimeout);
+        const int issued = min(p.nbox - 1, j + kStages - 2);
+        for (int b = j; b <= issued; b++) mbar_wait(&S.full[b % kStages], (b / kStages) & 1);
+      }
+      return;
+    }
+    // box j - 1 is no longer needed: its slot takes box j + kStages - 1
+    if (tid == 0 && j + kStages - 1 < p.nbox) {
+      const int jn = j + kStages - 1;
+      mbar_arrive_expect_tx(&S.full[sp], box_bytes);
+      sm100::tma_load_2d(&S.ring[sp][0][0], &tmX, &S.full[sp], c0, jn * kBox);
+    }
+    if (j == p.nbox - 1 && g == 0 && active) {
+      // the state after the block: the last ck inputs (boxes j and j - 1
+      // are still resident: nothing is loaded after the last box)
+      for (int m = 0; m < ck; m++) p.state[static_cast<size_t>(c) * ck + m] = tap(p.rows - ck + m);
+    }
+  }
+}
+
+// ------------------------------------------------------------ gated norm
+
+constexpr int kNormThreads = 256;
+
+struct NormParams {
+  const float* x;
+  const float* z;
+  const uint16_t* weight;
+  uint16_t* out;
+  float* out_f32;
+  long long n_rows;
+  int dim;
+  float eps;
+};
+
+__global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_kernel(const NormParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (row >= p.n_rows) return;
+  const int dim = p.dim;
+  const size_t base = static_cast<size_t>(row) * dim;
+  const float* x = p.x + base;
+  const float* z = p.z + base;
+  if (dim % 16 == 0 && dim <= 128) {
+    // Lane (l, h) = (lane % 16, lane / 16) holds zmm lane l of blocks
+    // 2h, 2h + 1, 2h + 4, 2h + 5: chains 2h and 2h + 1 of the sum of squares
+    // (block b feeds chain b % 4; absent chains stay +0, which adds exactly).
+    const int l = lane & 15, h = lane >> 4, nb = dim / 16;
+    float xv[4], acc[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int b = 2 * h + (k & 1) + 4 * (k >> 1);
+      xv[k] = b < nb ? x[16 * b + l] : 0.0f;
+      if (b < nb) acc[k & 1] = __fmaf_rn(xv[k], xv[k], acc[k & 1]);
+    }
+    // chains added in order: ((c0 + c1) + c2) + c3, on the lanes l < 16
+    const float c2 = __shfl_down_sync(0xFFFFFFFFu, acc[0], 16);
+    const float c3 = __shfl_down_sync(0xFFFFFFFFu, acc[1], 16);
+    float s = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), c2), c3);
+    // hsum: (l, l+8), (l, l+4), then the two hadds
+    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 8));
+    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 4));
+    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 1));
+    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 2));
+    s = __shfl_sync(0xFFFFFFFFu, s, 0);
+    s = __fadd_rn(__fdiv_rn(s, static_cast<float>(dim)), p.eps);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(s));
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int b = 2 * h + (k & 1) + 4 * (k >> 1);
+      if (b >= nb) continue;
+      const int d = 16 * b + l;
+      float y = __fmul_rn(__fmul_rn(xv[k], inv), bf16_to_f32(p.weight[d]));
+      y = __fmul_rn(y, silu_poly(z[d]));
+      if (p.out_f32) p.out_f32[base + d] = y;
+      p.out[base + d] = f32_to_bf16_cvtne(y);
+    }
+    return;
+  }
+  // scalar body: the sum in order from +0 (every lane, same bits)
+  float s = 0.0f;
+  for (int d = 0; d < dim; d++) s = __fadd_rn(s, __fmul_rn(x[d], x[d]));
+  s = __fadd_rn(__fdiv_rn(s, static_cast<float>(dim)), p.eps);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(s));
+  __syncwarp();  // every lane has read x before any lane writes y over it
+  for (int d = lane; d < dim; d += 32) {
+    const float silu = silu_scalar(z[d]);
+    const float y = __fmul_rn(__fmul_rn(__fmul_rn(x[d], inv), bf16_to_f32(p.weight[d])), silu);
+    if (p.out_f32) p.out_f32[base + d] = y;
+    const uint32_t u = __float_as_uint(y);
+    p.out[base + d] = static_cast<uint16_t>((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+  }
+}
+
+}  // namespace
+
+bool gdn_front_serves(int64_t conv, int64_t ck) {
+  return ck >= 1 && ck <= kMaxCk && conv > 0 && conv % 4 == 0;
+}
+
+cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st) {
+  FrontParams p;
+  p.qkv = L.qkv;
+  p.state = L.state;
+  p.weight = L.weight;
+  p.conv = static_cast<int>(L.conv);
+  p.rows = static_cast<int>(L.rows);
+  p.ck = static_cast<int>(L.ck);
+  p.vec_channels = L.ck == 4 ? static_cast<int>(L.conv / 16 * 16) : 0;
+  p.box_rows = static_cast<int>(L.rows < kBox ? L.rows : kBox);
+  p.nbox = static_cast<int>((L.rows + kBox - 1) / kBox);
+  p.n_strips = static_cast<int>((L.conv + kStrip - 1) / kStrip);
+  p.ab = L.ab;
+  p.dt_bias = L.dt_bias;
+  p.a_log = L.a_log;
+  p.beta = L.beta;
+  p.decay = L.decay;
+  p.nv = static_cast<int>(L.nv);
+  p.n_tasks = static_cast<int>(L.rows * L.nv);
+  p.status = L.status;
+  CUtensorMap tm;
+  if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.qkv, uint64_t(L.rows), uint64_t(L.conv),
+                 uint64_t(L.conv), uint32_t(p.box_rows), kStrip, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  const size_t smem = sizeof(FrontSmem) + 1024;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int gate_ctas = (p.n_tasks + kFrontThreads - 1) / kFrontThreads;
+  gdn_front_kernel<<<p.n_strips + gate_ctas, kFrontThreads, smem, st>>>(tm, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gdn_gated_norm(const GdnNormLaunch& L, cudaStream_t st) {
+  NormParams p;
+  p.x = L.x;
+  p.z = L.z;
+  p.weight = L.weight;
+  p.out = L.out;
+  p.out_f32 = L.out_f32;
+  p.n_rows = L.rows * L.nv;
+  p.dim = static_cast<int>(L.hvd);
+  p.eps = L.eps;
+  const long long warps = kNormThreads / 32;
+  const long long ctas = (p.n_rows + warps - 1) / warps;
+  gdn_gated_norm_kernel<<<static_cast<unsigned>(ctas), kNormThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace hb

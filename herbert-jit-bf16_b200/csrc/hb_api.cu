@@ -468,6 +468,73 @@ static bool gdn_chunked(const hb_gdn_shape* s, const hb_gdn_call* c) {
          c->rows < (int64_t(1) << 31);
 }
 
+static hb_status check_gdn_shape(const hb_gdn_shape* s) {
+  const int64_t lim = int64_t(1) << 16;
+  if (s->nk <= 0 || s->nv <= 0 || s->nv % s->nk || s->hkd <= 0 || s->hvd <= 0 || s->nk > lim ||
+      s->nv > lim || s->hkd > lim || s->hvd > lim ||
+      (2 * s->nk * s->hkd + s->nv * s->hvd) > 0x7FFFFFFF / 16)
+    return fail(HB_DECLINE_GEOMETRY, "invalid generated DeltaNet geometry");
+  return HB_OK;
+}
+
+hb_status hb_gdn_front(const hb_gdn_shape* s, const hb_gdn_front_call* c, void* ws, size_t ws_bytes,
+                       hb_stream_t stream) {
+  if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or front call is null");
+  hb_status r = check_gdn_shape(s);
+  if (r != HB_OK) return r;
+  const int64_t conv = 2 * s->nk * s->hkd + s->nv * s->hvd;
+  if (!gdn_front_serves(conv, c->ck))
+    return fail(HB_DECLINE_GEOMETRY, "DeltaNet conv not served (ck 1..8, conv width a multiple of 4)");
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
+  if (c->rows >= (int64_t(1) << 31) / s->nv || c->rows * conv >= (int64_t(1) << 40))
+    return fail(HB_ERR_ARG, "DeltaNet block too long");
+  if (!c->qkv || !c->conv_state || !c->conv_weight || !c->ab || !c->dt_bias || !c->a_log ||
+      !c->beta || !c->decay)
+    return fail(HB_ERR_ARG, "null DeltaNet front pointer");
+  if (!aligned16(c->qkv)) return fail(HB_ERR_ARG, "qkv must be 16-byte aligned");
+  if ((r = check_ws(ws, ws_bytes, kWsHeader)) != HB_OK) return r;
+  GdnFrontLaunch L;
+  L.qkv = c->qkv;
+  L.state = c->conv_state;
+  L.weight = c->conv_weight;
+  L.ab = c->ab;
+  L.dt_bias = c->dt_bias;
+  L.a_log = c->a_log;
+  L.beta = c->beta;
+  L.decay = c->decay;
+  L.rows = c->rows;
+  L.conv = conv;
+  L.ck = c->ck;
+  L.nv = s->nv;
+  L.status = static_cast<int*>(ws);
+  cudaError_t e = launch_gdn_front(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_front launch");
+  return HB_OK;
+}
+
+hb_status hb_gdn_gated_norm(const hb_gdn_shape* s, const hb_gdn_norm_call* c, hb_stream_t stream) {
+  if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or norm call is null");
+  hb_status r = check_gdn_shape(s);
+  if (r != HB_OK) return r;
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
+  if (c->rows >= (int64_t(1) << 40) / (s->nv * s->hvd)) return fail(HB_ERR_ARG, "DeltaNet block too long");
+  if (!c->x || !c->z || !c->weight || !c->out) return fail(HB_ERR_ARG, "null DeltaNet norm pointer");
+  if (!(c->eps >= 0.f) || c->eps == INFINITY) return fail(HB_ERR_ARG, "invalid gated-norm eps");
+  GdnNormLaunch L;
+  L.x = c->x;
+  L.z = c->z;
+  L.weight = c->weight;
+  L.out = c->out;
+  L.out_f32 = c->out_f32;
+  L.rows = c->rows;
+  L.nv = s->nv;
+  L.hvd = s->hvd;
+  L.eps = c->eps;
+  cudaError_t e = launch_gdn_gated_norm(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_gated_norm launch");
+  return HB_OK;
+}
+
 size_t hb_gdn_prefill_workspace_bytes(const hb_gdn_shape* s, int64_t rows) {
   if (!s || rows <= 0) return kWsHeader;
   if (!gdn_prefill_serves(*s)) return kWsHeader;

@@ -111,6 +111,32 @@ struct FrontLaunch {
 bool front_serves(int64_t head_dim, int64_t rotary);
 cudaError_t launch_attn_front(const FrontLaunch& L, cudaStream_t st);
 
+// ------------------------------------------------- gdn front / gated norm
+struct GdnFrontLaunch {
+  float* qkv;               // [rows][conv], conv + SiLU in place
+  float* state;             // [conv][ck]
+  const uint16_t* weight;   // [conv][ck] bf16
+  const float* ab;          // [rows][2 nv]
+  const uint16_t* dt_bias;  // [nv] bf16
+  const float* a_log;       // [nv]
+  float* beta;              // [rows][nv]
+  float* decay;             // [rows][nv]
+  int64_t rows, conv, ck, nv;
+  int* status;
+};
+struct GdnNormLaunch {
+  const float* x;
+  const float* z;
+  const uint16_t* weight;
+  uint16_t* out;
+  float* out_f32;  // nullptr: not written
+  int64_t rows, nv, hvd;
+  float eps;
+};
+bool gdn_front_serves(int64_t conv, int64_t ck);
+cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st);
+cudaError_t launch_gdn_gated_norm(const GdnNormLaunch& L, cudaStream_t st);
+
 // ------------------------------------------------------------ gdn decode
 struct GdnLaunch {
   hb_gdn_shape shape;

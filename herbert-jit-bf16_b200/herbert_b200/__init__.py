@@ -97,6 +97,19 @@ class RecurrenceCall(ctypes.Structure):
                 ("l2", c_int32), ("eps", c_float)]
 
 
+class GdnFrontCall(ctypes.Structure):
+    """hb_gdn_front_call: conv + SiLU in place over qkv, then the beta/decay gates."""
+    _fields_ = [("qkv", c_void_p), ("conv_state", c_void_p), ("conv_weight", c_void_p),
+                ("ab", c_void_p), ("dt_bias", c_void_p), ("a_log", c_void_p), ("beta", c_void_p),
+                ("decay", c_void_p), ("rows", c_int64), ("ck", c_int64)]
+
+
+class GdnNormCall(ctypes.Structure):
+    """hb_gdn_norm_call: the gated RMS norm of the recurrence output."""
+    _fields_ = [("x", c_void_p), ("z", c_void_p), ("weight", c_void_p), ("out", c_void_p),
+                ("out_f32", c_void_p), ("rows", c_int64), ("eps", c_float)]
+
+
 class CpSpec(ctypes.Structure):
     """hb_cp_spec: a zig-zag sharded sequence of 2*ranks*chunk positions."""
     _fields_ = [("ranks", c_int32), ("rank", c_int32), ("chunk", c_int64)]
@@ -133,6 +146,9 @@ _SIGNATURES = {
     "hb_gdn_prefill_workspace_bytes": (c_size_t, [_P(DeltaShape), c_int64]),
     "hb_gdn_prefill": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceCall), c_void_p, c_size_t,
                                       c_void_p]),
+    "hb_gdn_front": (ctypes.c_int, [_P(DeltaShape), _P(GdnFrontCall), c_void_p, c_size_t,
+                                    c_void_p]),
+    "hb_gdn_gated_norm": (ctypes.c_int, [_P(DeltaShape), _P(GdnNormCall), c_void_p]),
     "hb_cp_hop_source": (c_int32, [_P(CpSpec), c_int32]),
     "hb_cp_row_position": (c_int64, [_P(CpSpec), c_int32, c_int64]),
     "hb_attn_prefill_cp_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(CpSpec)]),
@@ -329,6 +345,31 @@ def delta_recurrence(shape: DeltaShape, state, out, qkv, beta, decay, *, rows: i
     check(L.hb_gdn_prefill(ctypes.byref(shape), ctypes.byref(call), c_void_p(workspace.ptr),
                            workspace.nbytes, _stream(stream)))
     return workspace
+
+
+def delta_front(shape: DeltaShape, qkv, conv_state, conv_weight, ab, dt_bias, a_log, beta,
+                decay, *, rows: int, ck: int = 4, workspace: Workspace | None = None,
+                stream=None) -> Workspace:
+    """The delta-causal-convolution node (conv + SiLU in place over qkv, conv_state
+    updated) and the gate part of delta-l2-gates (beta, decay) in one launch.
+    f32 tensors except conv_weight and dt_bias (bf16 bits)."""
+    if workspace is None:
+        workspace = Workspace(256, qkv.device, stream)
+    call = GdnFrontCall(qkv=_ptr(qkv), conv_state=_ptr(conv_state), conv_weight=_ptr(conv_weight),
+                        ab=_ptr(ab), dt_bias=_ptr(dt_bias), a_log=_ptr(a_log), beta=_ptr(beta),
+                        decay=_ptr(decay), rows=rows, ck=ck)
+    check(lib().hb_gdn_front(ctypes.byref(shape), ctypes.byref(call), c_void_p(workspace.ptr),
+                             workspace.nbytes, _stream(stream)))
+    return workspace
+
+
+def delta_gated_norm(shape: DeltaShape, x, z, weight, out, *, rows: int, eps: float = 1e-6,
+                     out_f32=None, stream=None) -> None:
+    """The delta-normed-gate node: out (bf16 bits) = ((x inv_rms) w) silu(z) per V head;
+    out_f32 (optional, may be x) receives the f32 values."""
+    call = GdnNormCall(x=_ptr(x), z=_ptr(z), weight=_ptr(weight), out=_ptr(out),
+                       out_f32=_ptr(out_f32), rows=rows, eps=eps)
+    check(lib().hb_gdn_gated_norm(ctypes.byref(shape), ctypes.byref(call), _stream(stream)))
 
 
 # ------------------------------------------------- context-parallel prefill

@@ -137,3 +137,35 @@ class FrontInputs:
         self.sin = f32_to_bf16_bits(np.sin(pos * inv_freq))
         self.keys = normal_bf16((kv_heads, self.capacity, head_dim), seed + 5)
         self.values = normal_bf16((kv_heads, self.capacity, head_dim), seed + 6)
+
+
+class DeltaFrontInputs:
+    """One call of the DeltaNet front end (conv + SiLU, gates) and of the gated
+    norm, Qwen3.5 geometry by default.
+
+    qkv        : [rows, conv] f32 projection output, N(0, 1)
+    conv_state : [conv, ck] f32, N(0, 1) (the last ck inputs of an earlier block)
+    conv_weight: [conv, ck] bf16 bits, N(0, 0.25)
+    ab         : [rows, 2*nv] f32, a then b projections, N(0, 2)
+    dt_bias    : [nv] bf16 bits, softplus^-1 of dt ~ logU(1e-3, 1e-1) (the usual init)
+    a_log      : [nv] f32, log U(1, 16)
+    x, z       : [rows, nv*hvd] f32, recurrence output N(0, 0.05) and gate N(0, 1)
+    norm_weight: [hvd] bf16 bits, 1 + N(0, 0.1)
+    """
+
+    def __init__(self, rows, nk=QWEN_NK, nv=QWEN_NV, hkd=QWEN_HKD, hvd=QWEN_HVD, ck=4,
+                 seed=0xDE17A):
+        self.rows, self.nk, self.nv, self.hkd, self.hvd, self.ck = rows, nk, nv, hkd, hvd, ck
+        self.conv = 2 * nk * hkd + nv * hvd
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        self.qkv = rng.standard_normal((rows, self.conv), dtype=f32)
+        self.conv_state = rng.standard_normal((self.conv, ck), dtype=f32)
+        self.conv_weight = f32_to_bf16_bits(rng.standard_normal((self.conv, ck)) * 0.25)
+        self.ab = (rng.standard_normal((rows, 2 * nv)) * 2.0).astype(f32)
+        dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), nv))
+        self.dt_bias = f32_to_bf16_bits(dt + np.log(-np.expm1(-dt)))
+        self.a_log = np.log(rng.uniform(1.0, 16.0, nv)).astype(f32)
+        self.x = (rng.standard_normal((rows, nv * hvd)) * 0.05).astype(f32)
+        self.z = rng.standard_normal((rows, nv * hvd), dtype=f32)
+        self.norm_weight = f32_to_bf16_bits(1.0 + rng.standard_normal(hvd) * 0.1)

@@ -339,6 +339,57 @@ HB_API hb_status hb_gdn_prefill(const hb_gdn_shape *shape, const hb_gdn_call *ca
                          size_t workspace_bytes, hb_stream_t stream);
 
 /*
+ * DeltaNet front end of one layer, in one launch: the delta-causal-convolution
+ * node (src/jit/target/x86/execution/delta.rs:609-705) and the gate part of
+ * delta-l2-gates (delta.rs:290-389; its L2 part is hb_gdn_call.l2).  Per
+ * channel c of qkv, positions in order:
+ *   state[c][0..ck) <- state[c][1..ck) ++ qkv[r][c];  qkv[r][c] <- silu(sum_j state[c][j] w[c][j])
+ * in the vector kernel's form (src/jit/target/x86/emit_conv.rs) for the
+ * channels of full 16-channel blocks at ck = 4, the scalar body's
+ * (delta_scalar.rs:85-155) for the others; per (row, V head) h:
+ *   beta = 1 / (exp(-b) + 1); dt = a + dt_bias[h]; dt = log(exp(dt) + 1) unless dt > 20;
+ *   decay = exp(-exp(a_log[h]) * dt)
+ * with the reference's scalar exp / log (execution/math.rs).  Results are
+ * the reference's bits.  The workspace holds only the status word
+ * (hb_workspace_status reports a bounded wait that ran out).
+ */
+typedef struct hb_gdn_front_call {
+    float *qkv;                   /* [rows][2*nk*hkd + nv*hvd] f32 (conv width a multiple of 4,
+                                     16-byte aligned): conv + SiLU in place                    */
+    float *conv_state;            /* [conv][ck] f32: the last ck inputs; read and updated       */
+    const uint16_t *conv_weight;  /* [conv][ck] bf16                                            */
+    const float *ab;              /* [rows][2*nv] f32: a (dt) then b (beta) projections         */
+    const uint16_t *dt_bias;      /* [nv] bf16                                                  */
+    const float *a_log;           /* [nv] f32                                                   */
+    float *beta;                  /* [rows][nv] f32 out                                         */
+    float *decay;                 /* [rows][nv] f32 out                                         */
+    int64_t rows;                 /* positions (>= 1)                                           */
+    int64_t ck;                   /* conv kernel length, 1..8 (Qwen3.5: 4)                      */
+} hb_gdn_front_call;
+HB_API hb_status hb_gdn_front(const hb_gdn_shape *shape, const hb_gdn_front_call *call,
+                              void *workspace, size_t workspace_bytes, hb_stream_t stream);
+
+/*
+ * Gated RMS norm of the recurrence output, the delta-normed-gate node
+ * (src/jit/target/x86/execution/delta.rs:706-774): per (row, V head) of
+ * width hvd, y = ((x * 1/sqrt(sum x^2 / hvd + eps)) * w) * silu(z), in the
+ * vector kernel's form (src/jit/target/x86/emit_gated_norm.rs) at hvd a
+ * multiple of 16 up to 128, the scalar body's (delta_scalar.rs:159-239)
+ * otherwise.  Results are the reference's bits.
+ */
+typedef struct hb_gdn_norm_call {
+    const float *x;           /* [rows][nv*hvd] f32 recurrence output                          */
+    const float *z;           /* [rows][nv*hvd] f32 gate projection                            */
+    const uint16_t *weight;   /* [hvd] bf16 norm weight                                        */
+    uint16_t *out;            /* [rows][nv*hvd] bf16: the out-projection input                 */
+    float *out_f32;           /* y in f32 (the reference writes it over x); NULL: not written  */
+    int64_t rows;
+    float eps;                /* the config's rms_norm_eps (Qwen3.5: 1e-6)                     */
+} hb_gdn_norm_call;
+HB_API hb_status hb_gdn_gated_norm(const hb_gdn_shape *shape, const hb_gdn_norm_call *call,
+                                   hb_stream_t stream);
+
+/*
  * Self-test, no counterpart in the reference: runs the arithmetic of
  * hb_attn_prefill's epilogue (O / l rounded to bf16, then the output gate)
  * over every pair of bf16 values (a, g) and over every f32 value of O / l,

@@ -739,6 +739,385 @@ int orc_gdn_layer(float *qkv, float *state, float *out, const float *beta,
     return 0;
 }
 
+/* ----------------------------------------------- DeltaNet front end */
+
+/* The scalar f32 exp and log the reference emits for the gates and the
+ * scalar conv / gated-norm bodies (src/jit/target/x86/execution/math.rs:23-104
+ * exp, 114-199 log; FMA form, the one the lowering selects,
+ * src/jit/schedule/lowering.rs:805-807,952).  The algorithm is the published
+ * one of Arm optimized-routines (expf: 32-entry 2^(i/32) table, cubic in
+ * double; logf: 16 subintervals, invc/logc table, cubic in double), which is
+ * also glibc's expf/logf since 2.27/2.28.  Tables (src/jit/execution/math_data.rs):
+ * EXPF_T[i] = bits(RN(2^(i/32))) - (i << 47); LOGF_T[i] = {invc_i, RN(-ln invc_i)}.
+ * Constants of the evaluation: the reference's INV, SHIFT, E0..E2, LN2, L0..L2. */
+static const uint64_t EXPF_T[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+static const uint64_t LOGF_T[16][2] = {
+    {0x3ff661ec79f8f3beull, 0xbfd57bf7808caadeull}, {0x3ff571ed4aaf883dull, 0xbfd2bef0a7c06ddbull},
+    {0x3ff49539f0f010b0ull, 0xbfd01eae7f513a67ull}, {0x3ff3c995b0b80385ull, 0xbfcb31d8a68224e9ull},
+    {0x3ff30d190c8864a5ull, 0xbfc6574f0ac07758ull}, {0x3ff25e227b0b8ea0ull, 0xbfc1aa2bc79c8100ull},
+    {0x3ff1bb4a4a1a343full, 0xbfba4e76ce8c0e5eull}, {0x3ff12358f08ae5baull, 0xbfb1973c5a611cccull},
+    {0x3ff0953f419900a7ull, 0xbfa252f438e10c1eull}, {0x3ff0000000000000ull, 0x0000000000000000ull},
+    {0x3fee608cfd9a47acull, 0x3faaa5aa5df25984ull}, {0x3feca4b31f026aa0ull, 0x3fbc5e53aa362eb4ull},
+    {0x3feb2036576afce6ull, 0x3fc526e57720db08ull}, {0x3fe9c2d163a1aa2dull, 0x3fcbc2860d224770ull},
+    {0x3fe886e6037841edull, 0x3fd1058bc8a07ee1ull}, {0x3fe767dcf5534862ull, 0x3fd4043057b6ee09ull}};
+#define EXPF_INV 0x40471547652b82feull   /* 32 / ln 2 */
+#define EXPF_SHIFT 0x4338000000000000ull /* 1.5 * 2^52 */
+#define EXPF_E0 0x3ebc6af84b912394ull
+#define EXPF_E1 0x3f2ebfce50fac4f3ull
+#define EXPF_E2 0x3f962e42ff0c52d6ull
+#define LOGF_LN2 0x3fe62e42fefa39efull
+#define LOGF_L0 0xbfd00ea348b88334ull
+#define LOGF_L1 0x3fd5575b0be00b6aull
+#define LOGF_L2 0xbfdffffef20a4123ull
+
+static inline double b2d(uint64_t b) { double d; memcpy(&d, &b, 8); return d; }
+static inline uint64_t d2b(double d) { uint64_t b; memcpy(&b, &d, 8); return b; }
+
+void orc_mathf_tables(uint64_t *exp_tab, uint64_t *log_tab) {
+    memcpy(exp_tab, EXPF_T, sizeof EXPF_T);
+    memcpy(log_tab, LOGF_T, sizeof LOGF_T);
+}
+
+/* exp (math.rs:23-104): |x| >= 88 goes to the special cases (-inf -> 0,
+ * NaN/+inf -> x + x, x > 88.72284 -> +inf, x < -103.972084 -> 0, else the
+ * core); core: z = INV*x + SHIFT (fused), k from z's low bits,
+ * r = INV*x - (z - SHIFT) (fused), s = 2^(k/32) from the table with k/32 in
+ * the exponent, y = ((E0 r + E1) r^2 + (E2 r + 1)) s, rounded to f32. */
+float orc_expf_arm(float x) {
+    const uint32_t ux = f2u(x), ax = ux & 0x7FFFFFFFu;
+    if (ax >= f2u(88.0f)) {
+        if (ux == 0xFF800000u) return 0.0f;
+        if (ax >= 0x7F800000u) return x + x;
+        if (x > 88.72284f) return u2f(0x7F800000u);
+        if (x < -103.972084f) return 0.0f;
+    }
+    const double xd = (double)x, inv = b2d(EXPF_INV), shift = b2d(EXPF_SHIFT);
+    const double z = fma(inv, xd, shift);
+    const uint64_t ki = d2b(z);
+    const double kd = z - shift;
+    const double r = fma(inv, xd, -kd);
+    const double s = b2d(EXPF_T[ki & 31] + (ki << 47));
+    const double p = fma(r, b2d(EXPF_E0), b2d(EXPF_E1));
+    const double r2 = r * r;
+    const double q = fma(r, b2d(EXPF_E2), 1.0);
+    const double y = fma(p, r2, q) * s;
+    return (float)y;
+}
+
+/* log (math.rs:114-199): 1 -> +0; outside the normal positive range: +-0 ->
+ * -inf, +inf -> +inf, NaN / negative -> NaN ((x - x) / (x - x)), subnormals
+ * scaled by 2^23; core: tmp = ix - 0x3f330000 picks subinterval i and
+ * exponent k, z = x / 2^k in [0x3f330000, ..), r = z invc - 1 (fused),
+ * y0 = k ln2 + logc (fused), y = (L0 r^2 + (L1 r + L2)) r^2 + (r + y0). */
+float orc_logf_arm(float x) {
+    uint32_t ix = f2u(x);
+    if (ix == 0x3F800000u) return 0.0f;
+    if (ix - 0x00800000u > 0x7EFFFFFFu) {
+        if ((uint32_t)(ix * 2u) == 0) return u2f(0xFF800000u);
+        if (ix == 0x7F800000u) return x;
+        if ((uint32_t)(ix * 2u) >= 0xFF000000u || (ix & 0x80000000u)) {
+            float t = x - x;
+            return t / t;
+        }
+        ix = f2u(x * 8388608.0f) - (23u << 23);
+    }
+    const uint32_t tmp = ix - 0x3F330000u;
+    const int i = (int)((tmp >> 19) & 15);
+    const int k = (int32_t)tmp >> 23;
+    const uint32_t iz = ix - (tmp & 0xFF800000u);
+    const double z = (double)u2f(iz);
+    const double r = fma(z, b2d(LOGF_T[i][0]), -1.0);
+    const double y0 = fma((double)k, b2d(LOGF_LN2), b2d(LOGF_T[i][1]));
+    double y = fma(r, b2d(LOGF_L1), b2d(LOGF_L2));
+    const double r2 = r * r;
+    const double yr = r + y0;
+    y = fma(r2, b2d(LOGF_L0), y);
+    y = fma(r2, y, yr);
+    return (float)y;
+}
+
+void orc_expf_arm_array(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = orc_expf_arm(x[i]);
+}
+void orc_logf_arm_array(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = orc_logf_arm(x[i]);
+}
+/* glibc's own expf / logf over an array: the independent implementation of
+ * the same published algorithm that the restatement is checked against. */
+void orc_expf_libm_array(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = expf(x[i]);
+}
+void orc_logf_libm_array(const float *x, float *y, size_t n) {
+    for (size_t i = 0; i < n; i++) y[i] = logf(x[i]);
+}
+
+/* Bit patterns 0, stride, 2 stride, ... (all of them at stride 1) through
+ * the restatement and through glibc; returns the count that differ
+ * (NaN results compare as NaN).  which 0: exp, 1: log. */
+uint64_t orc_mathf_sweep(uint32_t stride, int which) {
+    uint64_t bad = 0;
+    for (uint64_t u = 0; u <= 0xFFFFFFFFull; u += stride) {
+        const float x = u2f((uint32_t)u);
+        const float a = which ? orc_logf_arm(x) : orc_expf_arm(x);
+        const float b = which ? logf(x) : expf(x);
+        if (a != a && b != b) continue;
+        if (f2u(a) != f2u(b)) bad++;
+    }
+    return bad;
+}
+
+/* The integer round-to-nearest-even of the scalar bodies
+ * (src/jit/target/x86/execution/delta_scalar.rs:217-226): wrapping, no
+ * special case for NaN, infinities or denormals. */
+static inline uint16_t bf16_int_rne(float x) {
+    const uint32_t u = f2u(x);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+/* One channel of the scalar conv body (delta_scalar.rs:85-155): state
+ * shifted left, x appended, sum from +0 in tap order (multiply, then add),
+ * SiLU g / (1 + exp(-g)) with the scalar exp. */
+static float conv_channel_scalar(float x, const uint16_t *w, float *st, size_t ck) {
+    for (size_t j = 0; j + 1 < ck; j++) st[j] = st[j + 1];
+    st[ck - 1] = x;
+    float acc = 0.0f;
+    for (size_t j = 0; j < ck; j++) {
+        float p = orc_bf16_to_f32(w[j]) * st[j];
+        acc = acc + p;
+    }
+    float e = orc_expf_arm(u2f(f2u(acc) ^ 0x80000000u));
+    e = e + 1.0f;
+    return acc / e;
+}
+
+/* One channel of the vector conv kernel (src/jit/target/x86/emit_conv.rs:
+ * 141-211), K = 4: the same state update; products of the new state and the
+ * widened weights, summed as (p0 + p1) + (p2 + p3); SiLU with the emitted
+ * exp polynomial, e = min(0 - g, 88). */
+static float conv_channel_vec(float x, const uint16_t *w, float *st) {
+    st[0] = st[1]; st[1] = st[2]; st[2] = st[3]; st[3] = x;
+    float p0 = st[0] * orc_bf16_to_f32(w[0]), p1 = st[1] * orc_bf16_to_f32(w[1]);
+    float p2 = st[2] * orc_bf16_to_f32(w[2]), p3 = st[3] * orc_bf16_to_f32(w[3]);
+    float g = (p0 + p1) + (p2 + p3);
+    float e = x86_min(0.0f - g, EXP_MAX88);
+    e = orc_exp_poly(e);
+    e = e + 1.0f;
+    return g / e;
+}
+
+#if ORC_X86
+/* The vector conv kernel on the AVX-512 instructions it emits
+ * (emit_conv.rs:141-211) for one position and one block of 16 channels. */
+AVX512_TARGET static void conv_block_avx512(float *data, const uint16_t *w, float *state) {
+    __m512 x = _mm512_loadu_ps(data);
+    __m512 s[4], ns[4], wv[4];
+    for (int b = 0; b < 4; b++) s[b] = _mm512_loadu_ps(state + 16 * b);
+    for (int b = 0; b < 4; b++) {
+        __m512 hi = b < 3 ? s[b + 1] : s[b];
+        ns[b] = _mm512_castsi512_ps(_mm512_alignr_epi32(_mm512_castps_si512(hi), _mm512_castps_si512(s[b]), 1));
+        /* lane 4c+3 <- x[4b + c] */
+        __m512i ix = _mm512_set_epi32(4 * b + 3, 0, 0, 0, 4 * b + 2, 0, 0, 0, 4 * b + 1, 0, 0, 0, 4 * b, 0, 0, 0);
+        ns[b] = _mm512_mask_permutexvar_ps(ns[b], (__mmask16)0x8888, ix, x);
+        _mm512_storeu_ps(state + 16 * b, ns[b]);
+    }
+    for (int b = 0; b < 4; b++) {
+        __m256i h = _mm256_loadu_si256((const __m256i *)(w + 16 * b));
+        wv[b] = _mm512_castsi512_ps(_mm512_slli_epi32(_mm512_cvtepu16_epi32(h), 16));
+        __m512 p = _mm512_mul_ps(wv[b], ns[b]);
+        __m512 t = _mm512_castsi512_ps(_mm512_alignr_epi32(_mm512_castps_si512(p), _mm512_castps_si512(p), 1));
+        p = _mm512_add_ps(p, t);
+        t = _mm512_castsi512_ps(_mm512_alignr_epi32(_mm512_castps_si512(p), _mm512_castps_si512(p), 2));
+        wv[b] = _mm512_add_ps(p, t);
+    }
+    const __m512i idx_g = _mm512_set_epi32(0, 0, 0, 0, 0, 0, 0, 0, 28, 24, 20, 16, 12, 8, 4, 0);
+    __m512 g = _mm512_permutex2var_ps(wv[0], idx_g, wv[1]);
+    __m512 g2 = _mm512_permutex2var_ps(wv[2], idx_g, wv[3]);
+    g = _mm512_castsi512_ps(_mm512_inserti64x4(_mm512_castps_si512(g), _mm512_castsi512_si256(_mm512_castps_si512(g2)), 1));
+    __m512 e = _mm512_sub_ps(_mm512_setzero_ps(), g);
+    e = _mm512_min_ps(e, bcast(EXP_MAX88));
+    e = exp16(e);
+    e = _mm512_add_ps(e, bcast(1.0f));
+    e = _mm512_div_ps(g, e);
+    _mm512_storeu_ps(data, e);
+}
+
+/* The gated-norm kernel on its AVX-512 instructions
+ * (src/jit/target/x86/emit_gated_norm.rs:112-169), one row. */
+AVX512_TARGET static void gated_norm_row_avx512(float *out, const float *z, const uint16_t *w,
+                                                uint16_t *out_bf16, size_t dim, float eps) {
+    const size_t nb = dim / 16, n_acc = nb < 4 ? nb : 4;
+    __m512 acc[4] = {_mm512_setzero_ps(), _mm512_setzero_ps(), _mm512_setzero_ps(),
+                     _mm512_setzero_ps()};
+    for (size_t b = 0; b < nb; b++) {
+        __m512 ld = _mm512_loadu_ps(out + 16 * b);
+        acc[b % n_acc] = _mm512_fmadd_ps(ld, ld, acc[b % n_acc]);
+    }
+    for (size_t a = 1; a < n_acc; a++) acc[0] = _mm512_add_ps(acc[0], acc[a]);
+    __m128 s = _mm_set_ss(hsum_hw(acc[0]));
+    s = _mm_div_ss(s, _mm_set_ss((float)dim));
+    s = _mm_add_ss(s, _mm_set_ss(eps));
+    s = _mm_sqrt_ss(s);
+    s = _mm_div_ss(_mm_set_ss(1.0f), s);
+    const __m512 inv = _mm512_broadcastss_ps(s);
+    for (size_t b = 0; b < nb; b++) {
+        __m256i h = _mm256_loadu_si256((const __m256i *)(w + 16 * b));
+        __m512 wb = _mm512_castsi512_ps(_mm512_slli_epi32(_mm512_cvtepu16_epi32(h), 16));
+        __m512 x = _mm512_mul_ps(_mm512_loadu_ps(out + 16 * b), inv);
+        x = _mm512_mul_ps(x, wb);
+        __m512 zz = _mm512_loadu_ps(z + 16 * b);
+        __m512 e = _mm512_sub_ps(_mm512_setzero_ps(), zz);
+        e = _mm512_min_ps(e, bcast(EXP_MAX88));
+        e = exp16(e);
+        e = _mm512_add_ps(e, bcast(1.0f));
+        e = _mm512_div_ps(zz, e);
+        x = _mm512_mul_ps(x, e);
+        _mm512_storeu_ps(out + 16 * b, x);
+        _mm256_storeu_si256((__m256i *)(out_bf16 + 16 * b), (__m256i)_mm512_cvtneps_pbh(x));
+    }
+}
+#endif
+
+/* delta-causal-convolution (src/jit/target/x86/execution/delta.rs:609-705):
+ * per block of 16 channels, positions in order; full blocks take the vector
+ * kernel when K = 4, the tail block (and every block when K != 4) the
+ * scalar body.  data [rows][conv] in place, state [conv][ck], w [conv][ck].
+ * impl 0: restatement, 1: AVX-512 transcription of the vector kernel. */
+int orc_gdn_conv(float *data, size_t rows, size_t conv, const uint16_t *w, float *state,
+                 size_t ck, int impl) {
+    if (ck == 0 || conv == 0) return -2;
+#if ORC_X86
+    if (impl == 1 && !orc_has_avx512bf16()) return -1;
+#else
+    if (impl == 1) return -1;
+#endif
+    const size_t full = ck == 4 ? conv / 16 : 0;
+    for (size_t blk = 0; blk * 16 < conv; blk++) {
+        const size_t c0 = blk * 16, n = conv - c0 < 16 ? conv - c0 : 16;
+        for (size_t t = 0; t < rows; t++) {
+            float *row = data + t * conv + c0;
+            if (blk < full) {
+#if ORC_X86
+                if (impl == 1) { conv_block_avx512(row, w + c0 * 4, state + c0 * 4); continue; }
+#endif
+                for (size_t c = 0; c < 16; c++)
+                    row[c] = conv_channel_vec(row[c], w + (c0 + c) * 4, state + (c0 + c) * 4);
+            } else {
+                for (size_t c = 0; c < n; c++)
+                    row[c] = conv_channel_scalar(row[c], w + (c0 + c) * ck, state + (c0 + c) * ck, ck);
+            }
+        }
+    }
+    return 0;
+}
+
+/* The gate part of delta-l2-gates (delta.rs:290-389), task row*nv + h:
+ *   beta  = 1 / (exp(-b) + 1),           b = ab[row][nv + h]
+ *   dt    = a + bf16(dt_bias[h]),         a = ab[row][h]
+ *   dt    = log(exp(dt) + 1) unless dt > 20
+ *   decay = exp((-exp(a_log[h])) * dt)
+ * with the scalar exp / log. */
+void orc_gdn_gates(const float *ab, const uint16_t *dt_bias, const float *a_log, float *beta,
+                   float *decay, size_t rows, size_t nv) {
+    for (size_t t = 0; t < rows; t++)
+        for (size_t h = 0; h < nv; h++) {
+            const float *r = ab + t * 2 * nv;
+            float e = orc_expf_arm(u2f(f2u(r[nv + h]) ^ 0x80000000u));
+            e = e + 1.0f;
+            beta[t * nv + h] = 1.0f / e;
+            float dt = r[h] + orc_bf16_to_f32(dt_bias[h]);
+            if (!(dt > 20.0f)) {
+                float ed = orc_expf_arm(dt);
+                ed = ed + 1.0f;
+                dt = orc_logf_arm(ed);
+            }
+            float m = u2f(f2u(orc_expf_arm(a_log[h])) ^ 0x80000000u);
+            decay[t * nv + h] = orc_expf_arm(m * dt);
+        }
+}
+
+/* delta-normed-gate (delta.rs:706-774), one row of width dim each:
+ * dim % 16 == 0 and dim <= 128: the vector kernel (emit_gated_norm.rs) --
+ * sum of squares in min(4, dim/16) FMA chains over 16 lanes, chains added in
+ * order, horizontal sum (l, l+8) -> (l, l+4) -> hadd -> hadd; then
+ * s / dim + eps, sqrt, 1 / .; y = ((x inv) w) (z / (1 + exp(min(0 - z, 88))))
+ * with the exp polynomial; bf16 by vcvtneps2bf16.  Otherwise the scalar body
+ * (delta_scalar.rs:159-239): sum from +0 in order (multiply, add), the scalar
+ * exp of -z, bf16 by the wrapping integer rounding.  out is the f32 input
+ * and receives y in place. */
+int orc_gdn_gated_norm(float *out, const float *z, const uint16_t *w, uint16_t *out_bf16,
+                       size_t n_rows, size_t dim, float eps, int impl) {
+    if (dim == 0) return -2;
+#if ORC_X86
+    if (impl == 1 && !orc_has_avx512bf16()) return -1;
+#else
+    if (impl == 1) return -1;
+#endif
+    const int vec = dim % 16 == 0 && dim <= 128;
+    for (size_t r = 0; r < n_rows; r++) {
+        float *x = out + r * dim;
+        const float *zr = z + r * dim;
+        uint16_t *ob = out_bf16 + r * dim;
+        if (vec) {
+#if ORC_X86
+            if (impl == 1) { gated_norm_row_avx512(x, zr, w, ob, dim, eps); continue; }
+#endif
+            const size_t nb = dim / 16, n_acc = nb < 4 ? nb : 4;
+            float acc[4][16];
+            memset(acc, 0, sizeof acc);
+            for (size_t b = 0; b < nb; b++)
+                for (int l = 0; l < 16; l++)
+                    acc[b % n_acc][l] = fmaf(x[16 * b + l], x[16 * b + l], acc[b % n_acc][l]);
+            for (size_t a = 1; a < n_acc; a++)
+                for (int l = 0; l < 16; l++) acc[0][l] = acc[0][l] + acc[a][l];
+            float s = hsum16(acc[0]);
+            s = s / (float)dim;
+            s = s + eps;
+            s = sqrtf(s);
+            const float inv = 1.0f / s;
+            for (size_t d = 0; d < dim; d++) {
+                float y = x[d] * inv;
+                y = y * orc_bf16_to_f32(w[d]);
+                float e = x86_min(0.0f - zr[d], EXP_MAX88);
+                e = orc_exp_poly(e);
+                e = e + 1.0f;
+                e = zr[d] / e;
+                y = y * e;
+                x[d] = y;
+                ob[d] = orc_f32_to_bf16_cvtne(y);
+            }
+        } else {
+            float s = 0.0f;
+            for (size_t d = 0; d < dim; d++) {
+                float t = x[d] * x[d];
+                s = s + t;
+            }
+            s = s / (float)dim;
+            s = s + eps;
+            s = sqrtf(s);
+            const float inv = 1.0f / s;
+            for (size_t d = 0; d < dim; d++) {
+                float e = orc_expf_arm(u2f(f2u(zr[d]) ^ 0x80000000u));
+                e = e + 1.0f;
+                const float silu = zr[d] / e;
+                float y = x[d] * inv;
+                y = y * orc_bf16_to_f32(w[d]);
+                y = y * silu;
+                x[d] = y;
+                ob[d] = bf16_int_rne(y);
+            }
+        }
+    }
+    return 0;
+}
+
 /* ------------------------------------------------------------- inputs */
 
 static inline uint64_t splitmix64(uint64_t *s) {

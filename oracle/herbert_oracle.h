@@ -138,6 +138,30 @@ int orc_attn_front(uint16_t *q, size_t q_row, size_t heads, uint16_t *k, const u
                    size_t rotary, float eps, int gemma, uint16_t *keys, uint16_t *values,
                    size_t kv_stride, size_t rows, size_t past, int impl);
 
+/* DeltaNet front end (src/jit/target/x86/execution/delta.rs:290-389, 609-774).
+ * The reference's scalar exp / log (math.rs, FMA form: Arm optimized-routines
+ * expf / logf) and their tables (32 exp entries, 16 {invc, logc} pairs). */
+float orc_expf_arm(float x);
+float orc_logf_arm(float x);
+void orc_mathf_tables(uint64_t *exp_tab, uint64_t *log_tab);
+void orc_expf_arm_array(const float *x, float *y, size_t n);
+void orc_logf_arm_array(const float *x, float *y, size_t n);
+void orc_expf_libm_array(const float *x, float *y, size_t n);
+void orc_logf_libm_array(const float *x, float *y, size_t n);
+uint64_t orc_mathf_sweep(uint32_t stride, int which);
+/* Causal depthwise conv + SiLU over rows, in place on data [rows][conv];
+ * state [conv][ck] and weights [conv][ck] (bf16).  impl 0: restatement,
+ * 1: AVX-512 transcription of the K = 4 vector kernel (-1 without it). */
+int orc_gdn_conv(float *data, size_t rows, size_t conv, const uint16_t *w, float *state,
+                 size_t ck, int impl);
+/* beta / decay of rows x nv tasks from ab [rows][2*nv] (a then b). */
+void orc_gdn_gates(const float *ab, const uint16_t *dt_bias, const float *a_log, float *beta,
+                   float *decay, size_t rows, size_t nv);
+/* Gated RMS norm of n_rows rows of width dim: out (f32, in place) and
+ * out_bf16.  impl as orc_gdn_conv. */
+int orc_gdn_gated_norm(float *out, const float *z, const uint16_t *w, uint16_t *out_bf16,
+                       size_t n_rows, size_t dim, float eps, int impl);
+
 void orc_fill_normal_bf16(uint16_t *x, size_t n, uint64_t seed);
 void orc_fill_normal_f64(double *x, size_t n, uint64_t seed);
 

@@ -16,7 +16,10 @@ The C file restates the reference's x86 AVX-512 BF16 attention-path kernels
   519-607; src/jit/target/x86/emit_recurrence.rs:108-217;
 * attention front end (head-norm-rope of q and k, kv-append) --
   src/jit/schedule/lowering.rs:549-592, src/jit/target/x86/emit_elem.rs:242-330,
-  479-514, src/jit/target/x86/execution/transforms.rs:30-81.
+  479-514, src/jit/target/x86/execution/transforms.rs:30-81;
+* DeltaNet front end: causal conv + SiLU, beta/decay gates, gated RMS norm --
+  src/jit/target/x86/execution/delta.rs:290-389, 609-774, delta_scalar.rs:85-239,
+  src/jit/target/x86/emit_conv.rs, emit_gated_norm.rs, execution/math.rs.
 
 Parity is unpinned by reference outputs (the Rust reference cannot be built
 in this image and ships no golden vectors); the restatement is pinned to the
@@ -94,6 +97,19 @@ def lib():
                                      _u16p, _u16p, _sz, ctypes.c_float, ctypes.c_int, _u16p,
                                      _u16p, _sz, _sz, _sz, ctypes.c_int]
         L.orc_attn_front.restype = ctypes.c_int
+        _u64p = ctypes.POINTER(ctypes.c_uint64)
+        for fn in ("orc_expf_arm_array", "orc_logf_arm_array", "orc_expf_libm_array",
+                   "orc_logf_libm_array"):
+            getattr(L, fn).argtypes = [_f32p, _f32p, _sz]
+        L.orc_mathf_tables.argtypes = [_u64p, _u64p]
+        L.orc_mathf_sweep.argtypes = [ctypes.c_uint32, ctypes.c_int]
+        L.orc_mathf_sweep.restype = ctypes.c_uint64
+        L.orc_gdn_conv.argtypes = [_f32p, _sz, _sz, _u16p, _f32p, _sz, ctypes.c_int]
+        L.orc_gdn_conv.restype = ctypes.c_int
+        L.orc_gdn_gates.argtypes = [_f32p, _u16p, _f32p, _f32p, _f32p, _sz, _sz]
+        L.orc_gdn_gated_norm.argtypes = [_f32p, _f32p, _u16p, _u16p, _sz, _sz, ctypes.c_float,
+                                         ctypes.c_int]
+        L.orc_gdn_gated_norm.restype = ctypes.c_int
         L.orc_fill_normal_bf16.argtypes = [_u16p, _sz, ctypes.c_uint64]
         L.orc_fill_normal_f64.argtypes = [_f64p, _sz, ctypes.c_uint64]
         _lib = L
@@ -252,3 +268,88 @@ def gdn_layer(qkv, state, beta, decay, *, nk, nv, hkd, hvd, l2=True, eps=1e-6, f
     if rc != 0:
         raise RuntimeError(f"orc_gdn_layer rc={rc}")
     return out, state, qkv
+
+
+# ------------------------------------------------------ DeltaNet front end
+
+def _f32_array(fn, x):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    getattr(lib(), fn)(_p(x, _f32p), _p(y, _f32p), x.size)
+    return y
+
+
+def expf_arm(x):
+    """The reference's scalar exp (Arm optimized-routines expf, FMA form)."""
+    return _f32_array("orc_expf_arm_array", x)
+
+
+def logf_arm(x):
+    """The reference's scalar log (Arm optimized-routines logf, FMA form)."""
+    return _f32_array("orc_logf_arm_array", x)
+
+
+def expf_libm(x):
+    return _f32_array("orc_expf_libm_array", x)
+
+
+def logf_libm(x):
+    return _f32_array("orc_logf_libm_array", x)
+
+
+def mathf_sweep(stride, which):
+    """Bit patterns at `stride` through the restatement and glibc (0 exp, 1 log):
+    the count of differing results."""
+    return int(lib().orc_mathf_sweep(stride, which))
+
+
+def mathf_tables():
+    """(exp table [32] u64, log table [16][2] u64) of the restatement."""
+    e = np.empty(32, dtype=np.uint64)
+    g = np.empty(32, dtype=np.uint64)
+    lib().orc_mathf_tables(e.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+                           g.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)))
+    return e, g.reshape(16, 2)
+
+
+def gdn_conv(qkv, state, weight, impl=0):
+    """delta-causal-convolution: qkv [rows, conv] f32, state [conv, ck] f32,
+    weight [conv, ck] bf16 bits.  Returns (y, new_state) as new arrays."""
+    y = np.array(qkv, dtype=np.float32, copy=True, order="C")
+    st = np.array(state, dtype=np.float32, copy=True, order="C")
+    w = np.ascontiguousarray(weight, dtype=np.uint16)
+    rows, conv = y.shape
+    rc = lib().orc_gdn_conv(_p(y, _f32p), rows, conv, _p(w, _u16p), _p(st, _f32p), st.shape[1],
+                            impl)
+    if rc != 0:
+        raise RuntimeError(f"orc_gdn_conv rc={rc} (impl={impl})")
+    return y, st
+
+
+def gdn_gates(ab, dt_bias, a_log):
+    """beta, decay [rows, nv] from ab [rows, 2*nv] f32, dt_bias [nv] bf16 bits,
+    a_log [nv] f32."""
+    ab = np.ascontiguousarray(ab, dtype=np.float32)
+    rows, nv = ab.shape[0], ab.shape[1] // 2
+    db = np.ascontiguousarray(dt_bias, dtype=np.uint16)
+    al = np.ascontiguousarray(a_log, dtype=np.float32)
+    beta = np.empty((rows, nv), dtype=np.float32)
+    decay = np.empty((rows, nv), dtype=np.float32)
+    lib().orc_gdn_gates(_p(ab, _f32p), _p(db, _u16p), _p(al, _f32p), _p(beta, _f32p),
+                        _p(decay, _f32p), rows, nv)
+    return beta, decay
+
+
+def gdn_gated_norm(x, z, weight, eps=1e-6, impl=0):
+    """delta-normed-gate over rows of width weight.size: x, z [..., dim] f32.
+    Returns (y f32, y bf16 bits)."""
+    y = np.array(x, dtype=np.float32, copy=True, order="C")
+    zz = np.ascontiguousarray(z, dtype=np.float32)
+    w = np.ascontiguousarray(weight, dtype=np.uint16)
+    dim = w.size
+    ob = np.empty(y.shape, dtype=np.uint16)
+    rc = lib().orc_gdn_gated_norm(_p(y, _f32p), _p(zz, _f32p), _p(w, _u16p), _p(ob, _u16p),
+                                  y.size // dim, dim, ctypes.c_float(eps), impl)
+    if rc != 0:
+        raise RuntimeError(f"orc_gdn_gated_norm rc={rc} (impl={impl})")
+    return y, ob

@@ -18,7 +18,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path[:0] = [os.path.join(ROOT, "oracle"), os.path.join(ROOT, "herbert-jit-bf16_b200"),
                 os.path.join(ROOT, "tests")]
 
-from herbert_b200.inputs import AttentionInputs, DeltaInputs, FrontInputs  # noqa: E402
+from herbert_b200.inputs import AttentionInputs, DeltaFrontInputs, DeltaInputs, FrontInputs  # noqa: E402,E501
 from harness import oracle_attention, oracle_gdn  # noqa: E402
 import oracle as O  # noqa: E402
 
@@ -63,6 +63,19 @@ def main():
                         values0=f.values, q_out=q, k_out=k, keys=keys, values=values,
                         meta=np.array([f.rows, f.past, f.heads, f.kv_heads, f.head_dim, f.rotary,
                                        int(f.gemma), int(f.gated)], np.int64))
+    # DeltaNet front end (conv + SiLU, gates) and gated norm: conv width 68
+    # (four vector blocks and a scalar tail of 4), V head width 16
+    d = DeltaFrontInputs(5, nk=1, nv=2, hkd=18, hvd=16, seed=0x60D3)
+    d.qkv.reshape(-1)[:3] = [0.0, 1e30, -np.inf]
+    y, st = O.gdn_conv(d.qkv, d.conv_state, d.conv_weight)
+    beta, decay = O.gdn_gates(d.ab, d.dt_bias, d.a_log)
+    yn, ob = O.gdn_gated_norm(d.x, d.z, d.norm_weight)
+    np.savez_compressed(os.path.join(HERE, "gdn_front_rows5.npz"), qkv=d.qkv,
+                        conv_state=d.conv_state, conv_weight=d.conv_weight, ab=d.ab,
+                        dt_bias=d.dt_bias, a_log=d.a_log, x=d.x, z=d.z, norm_weight=d.norm_weight,
+                        qkv_out=y, conv_state_out=st, beta=beta, decay=decay, norm_f32=yn,
+                        norm_bf16=ob, meta=np.array([d.rows, d.nk, d.nv, d.hkd, d.hvd, d.ck],
+                                                    np.int64))
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

@@ -37,7 +37,8 @@ def test_record_layouts_match_the_header(tmp_path):
             "hb_decode_seq": hb.DecodeSeq, "hb_kv_spec": hb.KvSpec, "hb_kv_call": hb.KvCall,
             "hb_gdn_shape": hb.DeltaShape, "hb_gdn_call": hb.RecurrenceCall,
             "hb_cp_spec": hb.CpSpec, "hb_front_spec": hb.FrontSpec,
-            "hb_front_call": hb.FrontCall}
+            "hb_front_call": hb.FrontCall, "hb_gdn_front_call": hb.GdnFrontCall,
+            "hb_gdn_norm_call": hb.GdnNormCall}
     body = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{hb.HEADER_PATH}"',
             "int main(void){"]
     for c, py in recs.items():
