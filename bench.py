@@ -55,10 +55,12 @@ L2_BYTES = 126 << 20
 # committed ncu summaries under profiles/: attn_prefill_s4096.md,
 # attn_decode_n2048.md, attn_decode_batch64.md (scaled from the n = 2048
 # capture by the bytes processed), gdn_prefill_decode_t4096.md (prep + scan,
-# one chunked prefill); cp: the 131072-token launch is too large to capture.
+# one chunked prefill), gdn_front_s4096.md and gdn_gated_norm_s4096.md (DRAM
+# byte rate x duration of one launch); cp: the 131072-token launch is too
+# large to capture.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
-               "batch": 4_452_000_000, "cp": None, "front": 56_784_128, "gdn_front": None,
-               "gdn_norm": None}
+               "batch": 4_452_000_000, "cp": None, "front": 56_784_128,
+               "gdn_front": 213_700_000, "gdn_norm": 153_000_000}
 
 
 def peaks():

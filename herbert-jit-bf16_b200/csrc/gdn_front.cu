@@ -14,7 +14,7 @@
 //  * the gate part of delta-l2-gates (delta.rs:290-389), task row*nv + h:
 //    beta = 1 / (exp(-b) + 1); dt = a + bf16(dt_bias); dt = log(exp(dt) + 1)
 //    unless dt > 20; decay = exp((-exp(a_log)) dt).
-//  * delta-normed-gate (delta.rs:706-774): per (row, V head) of width dim,
+//  * delta-gated-norm (delta.rs:706-774): per (row, V head) of width dim,
 //    inv = 1 / sqrt(sum x^2 / dim + eps); y = ((x inv) w) silu(z).  dim a
 //    multiple of 16 up to 128 takes the vector kernel
 //    (src/jit/target/x86/emit_gated_norm.rs:112-169: sum of squares in
@@ -36,15 +36,19 @@
 //
 // Conv decomposition: one CTA per strip of 32 channels walks every row of
 // the strip, so the in-place update needs no ordering between CTAs.  TMA
-// brings boxes of 64 rows x 32 channels (8 KB) into a six-slot ring; a box
-// stays resident while the next one is computed (its last rows are that
-// box's taps), so four boxes are in flight while one is computed.  Thread
-// (g, l) computes channel l of rows g, g + 8, .. of a box and stores
-// straight to HBM (a warp writes one 128-byte row segment).  HBM-bound: every element is read once and
-// written once.  Gates: CTAs past the strips, one task per thread.
-// Gated norm: one warp per (row, V head).
+// brings boxes of 128 rows x 32 channels (16 KB) into a five-slot ring; a
+// box stays resident while the next one is computed (its last rows are that
+// box's first taps), so three boxes are in flight while one is computed.
+// Warp w of 16 owns rows [8w, 8w + 8) of a box, lane l channel l: a thread
+// reads its 11-row tap window from shared memory once and stores 8 outputs
+// straight to HBM (a warp writes one 128-byte row segment per row).
+// HBM-bound: every element is read once and written once.  The gate tasks
+// are spread over the same CTAs, computed while their first boxes arrive.
+// Gated norm: a warp per (row, V head), striding over the rows.
 
 #include <cuda.h>
+
+#include <algorithm>
 
 #include "hb_internal.h"
 #include "hb_sm100.cuh"
@@ -133,12 +137,15 @@ HB_DEV float logf_ref(float x) {
 
 HB_DEV float neg(float x) { return __uint_as_float(__float_as_uint(x) ^ 0x80000000u); }
 
-// SiLU of the vector kernels: g / (1 + exp(min(0 - g, 88))), the polynomial
-// exp (vminps gives 88 for NaN, as fminf).
-HB_DEV float silu_poly(float g) {
-  float e = fminf(__fsub_rn(0.0f, g), 88.0f);
-  e = __fadd_rn(exp_poly(e), 1.0f);
-  return __fdiv_rn(g, e);
+// SiLU of the vector kernels, g / (1 + exp(min(0 - g, 88))) with the
+// polynomial exp (vminps gives 88 for NaN, as fminf), on two lanes (g0, g1),
+// paired where the bits allow.
+HB_DEV void silu_poly2(float g0, float g1, float& y0, float& y1) {
+  const uint64_t ng = f2sub(f2(0.0f, 0.0f), f2(g0, g1));
+  const uint64_t e = f2add(exp_poly2(f2(fminf(f2lo(ng), 88.0f), fminf(f2hi(ng), 88.0f))),
+                           f2(1.0f, 1.0f));
+  y0 = __fdiv_rn(g0, f2lo(e));
+  y1 = __fdiv_rn(g1, f2hi(e));
 }
 
 // SiLU of the scalar bodies: g / (exp(-g) + 1) with the scalar exp.
@@ -146,18 +153,18 @@ HB_DEV float silu_scalar(float g) { return __fdiv_rn(g, __fadd_rn(expf_ref(neg(g
 
 // --------------------------------------------------------- conv + gates
 
-constexpr int kStrip = 32;   // channels per CTA: one 128-byte row segment
-constexpr int kBox = 64;     // rows per TMA box
-constexpr int kStages = 6;   // ring slots (one computed, one resident, four in flight)
-constexpr int kFrontThreads = 256;
-constexpr int kRowGroups = kFrontThreads / kStrip;  // 8
+constexpr int kStrip = 32;                      // channels per CTA: one 128-byte row segment
+constexpr int kRun = 8;                         // consecutive rows per thread
+constexpr int kBox = 128;                       // rows per TMA box (16 KB)
+constexpr int kStages = 5;                      // ring slots: computed, resident, three in flight
+constexpr int kFrontThreads = kBox / kRun * 32; // 512: warp w owns rows [8w, 8w + 8) of a box
 constexpr int kMaxCk = 8;
 
 struct FrontParams {
   float* qkv;
   float* state;
   const uint16_t* weight;
-  int conv, rows, ck, vec_channels, nbox, box_rows, n_strips;
+  int conv, rows, ck, vec_channels, nbox, box_rows;
   const float* ab;
   const uint16_t* dt_bias;
   const float* a_log;
@@ -188,15 +195,10 @@ __device__ void gate_task(const FrontParams& p, int task) {
 
 __global__ void __launch_bounds__(kFrontThreads)
     gdn_front_kernel(const __grid_constant__ CUtensorMap tmX, const FrontParams p) {
-  if (static_cast<int>(blockIdx.x) >= p.n_strips) {
-    const int task = (static_cast<int>(blockIdx.x) - p.n_strips) * kFrontThreads + threadIdx.x;
-    if (task < p.n_tasks) gate_task(p, task);
-    return;
-  }
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   FrontSmem& S = *reinterpret_cast<FrontSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x, l = tid % kStrip, g = tid / kStrip;
+  const int tid = threadIdx.x, l = tid % kStrip, w = tid / kStrip;
   const int c0 = blockIdx.x * kStrip, c = c0 + l;
   const bool active = c < p.conv;
   const int ck = p.ck;
@@ -212,43 +214,70 @@ __global__ void __launch_bounds__(kFrontThreads)
       sm100::tma_load_2d(&S.ring[j][0][0], &tmX, &S.full[j], c0, j * kBox);
     }
   }
-  if (g == 0 && active)
+  if (w == 0 && active)
     for (int m = 0; m < ck; m++) S.old_state[l][m] = p.state[static_cast<size_t>(c) * ck + m];
+  // the gates while the first boxes arrive: task blockIdx.x * 512 + tid, strided
+  for (int t = blockIdx.x * kFrontThreads + tid; t < p.n_tasks; t += gridDim.x * kFrontThreads)
+    gate_task(p, t);
   __syncthreads();
 
   const bool vec = c < p.vec_channels;
   const uint16_t* wc = p.weight + static_cast<size_t>(active ? c : 0) * ck;
-  float w[4];
-#pragma unroll
-  for (int m = 0; m < 4; m++) w[m] = vec ? bf16_to_f32(wc[m]) : 0.0f;
+  float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
+  if (vec) {
+    w0 = bf16_to_f32(wc[0]);
+    w1 = bf16_to_f32(wc[1]);
+    w2 = bf16_to_f32(wc[2]);
+    w3 = bf16_to_f32(wc[3]);
+  }
 
   for (int j = 0; j < p.nbox; j++) {
     const int s = j % kStages, sp = (j + kStages - 1) % kStages;
     if (!mbar_wait(&S.full[s], (j / kStages) & 1)) S.abort = 1;
-    // input x of row r (r >= j*kBox - kBox): this box, the previous one, or
-    // the state before the block
+    // input x of row r of the block, r >= j*kBox - 7: this box, the
+    // previous one, or the state before the block
     auto tap = [&](int r) -> float {
       if (r >= j * kBox) return S.ring[s][r - j * kBox][l];
       if (r >= 0) return S.ring[sp][r - (j - 1) * kBox][l];
       return S.old_state[l][ck + r];
     };
-    if (active) {
-#pragma unroll 2
-      for (int i = 0; i < kBox / kRowGroups; i++) {
-        const int r = j * kBox + g + i * kRowGroups;
-        if (r >= p.rows || r - j * kBox >= p.box_rows) break;
-        float y;
-        if (vec) {
-          const float p0 = __fmul_rn(tap(r - 3), w[0]), p1 = __fmul_rn(tap(r - 2), w[1]);
-          const float p2 = __fmul_rn(tap(r - 1), w[2]), p3 = __fmul_rn(tap(r), w[3]);
-          y = silu_poly(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)));
+    const int r0 = j * kBox + w * kRun;
+    const int n = min(kRun, p.rows - r0);  // rows of this run (<= 0: none)
+    if (active && n > 0) {
+      float* out = p.qkv + static_cast<size_t>(r0) * p.conv + c;
+      if (vec) {
+        // window x[r0 - 3 .. r0 + 7]: only warp 0 reaches into the previous
+        // box or the state
+        float x[kRun + 3];
+        if (w == 0) {
+#pragma unroll
+          for (int t = 0; t < 3; t++) x[t] = tap(r0 - 3 + t);
         } else {
+#pragma unroll
+          for (int t = 0; t < 3; t++) x[t] = S.ring[s][w * kRun - 3 + t][l];
+        }
+#pragma unroll
+        for (int t = 0; t < kRun; t++) x[3 + t] = S.ring[s][w * kRun + t][l];
+        // rows t and t + 1 on paired lanes: g = (p0 + p1) + (p2 + p3)
+#pragma unroll
+        for (int t = 0; t < kRun; t += 2) {
+          const uint64_t a = f2add(f2(__fmul_rn(x[t], w0), __fmul_rn(x[t + 1], w0)),
+                                   f2(__fmul_rn(x[t + 1], w1), __fmul_rn(x[t + 2], w1)));
+          const uint64_t b = f2add(f2(__fmul_rn(x[t + 2], w2), __fmul_rn(x[t + 3], w2)),
+                                   f2(__fmul_rn(x[t + 3], w3), __fmul_rn(x[t + 4], w3)));
+          const uint64_t g = f2add(a, b);
+          float y0, y1;
+          silu_poly2(f2lo(g), f2hi(g), y0, y1);
+          if (t < n) out[static_cast<size_t>(t) * p.conv] = y0;
+          if (t + 1 < n) out[static_cast<size_t>(t + 1) * p.conv] = y1;
+        }
+      } else {
+        for (int t = 0; t < n; t++) {
           float acc = 0.0f;
           for (int m = 0; m < ck; m++)
-            acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(wc[m]), tap(r - ck + 1 + m)));
-          y = silu_scalar(acc);
+            acc = __fadd_rn(acc, __fmul_rn(bf16_to_f32(wc[m]), tap(r0 + t - ck + 1 + m)));
+          out[static_cast<size_t>(t) * p.conv] = silu_scalar(acc);
         }
-        p.qkv[static_cast<size_t>(r) * p.conv + c] = y;
       }
     }
     __syncthreads();
@@ -268,7 +297,7 @@ __global__ void __launch_bounds__(kFrontThreads)
       mbar_arrive_expect_tx(&S.full[sp], box_bytes);
       sm100::tma_load_2d(&S.ring[sp][0][0], &tmX, &S.full[sp], c0, jn * kBox);
     }
-    if (j == p.nbox - 1 && g == 0 && active) {
+    if (j == p.nbox - 1 && w == 0 && active) {
       // the state after the block: the last ck inputs (boxes j and j - 1
       // are still resident: nothing is loaded after the last box)
       for (int m = 0; m < ck; m++) p.state[static_cast<size_t>(c) * ck + m] = tap(p.rows - ck + m);
@@ -291,25 +320,49 @@ struct NormParams {
   float eps;
 };
 
-__global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_kernel(const NormParams p) {
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * (kNormThreads / 32) + (threadIdx.x >> 5);
-  if (row >= p.n_rows) return;
-  const int dim = p.dim;
-  const size_t base = static_cast<size_t>(row) * dim;
-  const float* x = p.x + base;
-  const float* z = p.z + base;
-  if (dim % 16 == 0 && dim <= 128) {
-    // Lane (l, h) = (lane % 16, lane / 16) holds zmm lane l of blocks
-    // 2h, 2h + 1, 2h + 4, 2h + 5: chains 2h and 2h + 1 of the sum of squares
-    // (block b feeds chain b % 4; absent chains stay +0, which adds exactly).
-    const int l = lane & 15, h = lane >> 4, nb = dim / 16;
-    float xv[4], acc[2] = {0.0f, 0.0f};
+// bf16x2_cvtne with the special-case fix-ups only when a value needs them
+// (zero, denormal, infinite or NaN): the hardware conversion alone is the
+// reference's rounding for every other value.
+HB_DEV uint32_t bf16x2_cvtne_fast(float lo, float hi) {
+  const uint32_t el = __float_as_uint(lo) & 0x7F800000u, eh = __float_as_uint(hi) & 0x7F800000u;
+  const bool plain = el != 0u && el != 0x7F800000u && eh != 0u && eh != 0x7F800000u;
+  if (__builtin_expect(plain, 1)) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  return bf16x2_cvtne(lo, hi);
+}
+
+// The vector kernel's form at dim = 16 NB (NB <= 8).  A warp walks rows
+// (row, V head) with a stride of the grid's warps, the weights held in
+// registers.  Lane (l, h) = (lane % 16, lane / 16) holds zmm lane l of
+// blocks 2h, 2h + 1, 2h + 4, 2h + 5: chains 2h and 2h + 1 of the sum of
+// squares (block b feeds chain b % 4; absent chains stay +0, which adds
+// exactly).
+template <int NB>
+__global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_vec(const NormParams p) {
+  constexpr int dim = 16 * NB;
+  const int lane = threadIdx.x & 31, l = lane & 15, h = lane >> 4;
+  const long long warps = static_cast<long long>(gridDim.x) * (kNormThreads / 32);
+  float wv[4];
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int b = 2 * h + (k & 1) + 4 * (k >> 1);
+    wv[k] = b < NB ? bf16_to_f32(p.weight[16 * b + l]) : 0.0f;
+  }
+  for (long long row = static_cast<long long>(blockIdx.x) * (kNormThreads / 32) + (threadIdx.x >> 5);
+       row < p.n_rows; row += warps) {
+    const size_t base = static_cast<size_t>(row) * dim;
+    const float* x = p.x + base;
+    const float* z = p.z + base;
+    float xv[4], zv[4], acc[2] = {0.0f, 0.0f};
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       const int b = 2 * h + (k & 1) + 4 * (k >> 1);
-      xv[k] = b < nb ? x[16 * b + l] : 0.0f;
-      if (b < nb) acc[k & 1] = __fmaf_rn(xv[k], xv[k], acc[k & 1]);
+      xv[k] = b < NB ? x[16 * b + l] : 0.0f;
+      zv[k] = b < NB ? z[16 * b + l] : 0.0f;
+      if (b < NB) acc[k & 1] = __fmaf_rn(xv[k], xv[k], acc[k & 1]);
     }
     // chains added in order: ((c0 + c1) + c2) + c3, on the lanes l < 16
     const float c2 = __shfl_down_sync(0xFFFFFFFFu, acc[0], 16);
@@ -323,19 +376,39 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_kernel(const Norm
     s = __shfl_sync(0xFFFFFFFFu, s, 0);
     s = __fadd_rn(__fdiv_rn(s, static_cast<float>(dim)), p.eps);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(s));
+    // elements k and k + 1 on paired lanes (absent blocks compute on zeros
+    // and are not stored)
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int b = 2 * h + (k & 1) + 4 * (k >> 1);
-      if (b >= nb) continue;
-      const int d = 16 * b + l;
-      float y = __fmul_rn(__fmul_rn(xv[k], inv), bf16_to_f32(p.weight[d]));
-      y = __fmul_rn(y, silu_poly(z[d]));
-      if (p.out_f32) p.out_f32[base + d] = y;
-      p.out[base + d] = f32_to_bf16_cvtne(y);
+    for (int k = 0; k < 4; k += 2) {
+      const int b0 = 2 * h + 4 * (k >> 1), b1 = b0 + 1;
+      if (b0 >= NB) continue;
+      float s0, s1;
+      silu_poly2(zv[k], zv[k + 1], s0, s1);
+      const float y0 = __fmul_rn(__fmul_rn(__fmul_rn(xv[k], inv), wv[k]), s0);
+      const float y1 = __fmul_rn(__fmul_rn(__fmul_rn(xv[k + 1], inv), wv[k + 1]), s1);
+      const uint32_t o = bf16x2_cvtne_fast(y0, y1);
+      const int d0 = 16 * b0 + l, d1 = 16 * b1 + l;
+      if (p.out_f32) p.out_f32[base + d0] = y0;
+      p.out[base + d0] = static_cast<uint16_t>(o & 0xFFFFu);
+      if (b1 < NB) {
+        if (p.out_f32) p.out_f32[base + d1] = y1;
+        p.out[base + d1] = static_cast<uint16_t>(o >> 16);
+      }
     }
-    return;
   }
-  // scalar body: the sum in order from +0 (every lane, same bits)
+}
+
+// The scalar body's form (other widths), one warp per row: the sum in
+// order from +0 (every lane, same bits), the scalar exp, the integer
+// rounding to bf16.
+__global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const NormParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (row >= p.n_rows) return;
+  const int dim = p.dim;
+  const size_t base = static_cast<size_t>(row) * dim;
+  const float* x = p.x + base;
+  const float* z = p.z + base;
   float s = 0.0f;
   for (int d = 0; d < dim; d++) s = __fadd_rn(s, __fmul_rn(x[d], x[d]));
   s = __fadd_rn(__fdiv_rn(s, static_cast<float>(dim)), p.eps);
@@ -367,7 +440,7 @@ cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st) {
   p.vec_channels = L.ck == 4 ? static_cast<int>(L.conv / 16 * 16) : 0;
   p.box_rows = static_cast<int>(L.rows < kBox ? L.rows : kBox);
   p.nbox = static_cast<int>((L.rows + kBox - 1) / kBox);
-  p.n_strips = static_cast<int>((L.conv + kStrip - 1) / kStrip);
+  const int n_strips = static_cast<int>((L.conv + kStrip - 1) / kStrip);
   p.ab = L.ab;
   p.dt_bias = L.dt_bias;
   p.a_log = L.a_log;
@@ -388,8 +461,7 @@ cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int gate_ctas = (p.n_tasks + kFrontThreads - 1) / kFrontThreads;
-  gdn_front_kernel<<<p.n_strips + gate_ctas, kFrontThreads, smem, st>>>(tm, p);
+  gdn_front_kernel<<<n_strips, kFrontThreads, smem, st>>>(tm, p);
   return cudaGetLastError();
 }
 
@@ -404,8 +476,30 @@ cudaError_t launch_gdn_gated_norm(const GdnNormLaunch& L, cudaStream_t st) {
   p.dim = static_cast<int>(L.hvd);
   p.eps = L.eps;
   const long long warps = kNormThreads / 32;
-  const long long ctas = (p.n_rows + warps - 1) / warps;
-  gdn_gated_norm_kernel<<<static_cast<unsigned>(ctas), kNormThreads, 0, st>>>(p);
+  long long ctas = (p.n_rows + warps - 1) / warps;
+  if (p.dim % 16 == 0 && p.dim <= 128) {
+    // a resident grid (eight CTAs per SM) whose warps stride over the rows
+    static int sms = 0;
+    if (!sms) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (sms <= 0) sms = 148;
+    }
+    ctas = std::min<long long>(ctas, 8LL * sms);
+    switch (p.dim / 16) {
+      case 1: gdn_gated_norm_vec<1><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      case 2: gdn_gated_norm_vec<2><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      case 3: gdn_gated_norm_vec<3><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      case 4: gdn_gated_norm_vec<4><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      case 5: gdn_gated_norm_vec<5><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      case 6: gdn_gated_norm_vec<6><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      case 7: gdn_gated_norm_vec<7><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+      default: gdn_gated_norm_vec<8><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
+    }
+  } else {
+    gdn_gated_norm_scalar<<<static_cast<unsigned>(ctas), kNormThreads, 0, st>>>(p);
+  }
   return cudaGetLastError();
 }
 

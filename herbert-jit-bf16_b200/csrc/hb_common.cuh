@@ -113,6 +113,25 @@ HB_DEV uint32_t bf16x2_cvtne(float lo, float hi) {
   return rl | (rh << 16);
 }
 
+// exp_poly on two lanes: the additions, subtractions and polynomial FMAs
+// paired, the products (which feed paired additions) on the scalar
+// instruction so that none is fused.  Same bits as exp_poly per lane.
+HB_DEV uint64_t exp_poly2(uint64_t x) {
+  const float x0 = fmaxf(f2lo(x), -87.33654f), x1 = fmaxf(f2hi(x), -87.33654f);
+  uint64_t t1 = f2(__fmul_rn(x0, 1.442695f), __fmul_rn(x1, 1.442695f));
+  const uint64_t big = f2add(t1, f2(12582912.0f, 12582912.0f));
+  const uint64_t t2 = f2sub(big, f2(12582912.0f, 12582912.0f));
+  t1 = f2sub(t1, t2);
+  uint64_t p = f2fma(f2(0.00967248f, 0.00967248f), t1, f2(0.05550411f, 0.05550411f));
+  p = f2fma(p, t1, f2(0.2402265f, 0.2402265f));
+  p = f2fma(p, t1, f2(0.6931472f, 0.6931472f));
+  p = f2fma(p, t1, f2(1.0f, 1.0f));
+  const uint32_t r0 = uint32_t(int32_t(uint32_t(big)) - 0x4B400000);
+  const uint32_t r1 = uint32_t(int32_t(uint32_t(big >> 32)) - 0x4B400000);
+  return f2(__fmul_rn(f2lo(p), __uint_as_float((r0 << 23) + 0x3F800000u)),
+            __fmul_rn(f2hi(p), __uint_as_float((r1 << 23) + 0x3F800000u)));
+}
+
 // gate_divisor of the two bf16 gate values in `gw` (lo, hi), with the
 // polynomial steps on paired lanes.
 HB_DEV uint64_t gate_divisor2(uint32_t gw) {

@@ -365,7 +365,7 @@ def delta_front(shape: DeltaShape, qkv, conv_state, conv_weight, ab, dt_bias, a_
 
 def delta_gated_norm(shape: DeltaShape, x, z, weight, out, *, rows: int, eps: float = 1e-6,
                      out_f32=None, stream=None) -> None:
-    """The delta-normed-gate node: out (bf16 bits) = ((x inv_rms) w) silu(z) per V head;
+    """The delta-gated-norm node: out (bf16 bits) = ((x inv_rms) w) silu(z) per V head;
     out_f32 (optional, may be x) receives the f32 values."""
     call = GdnNormCall(x=_ptr(x), z=_ptr(z), weight=_ptr(weight), out=_ptr(out),
                        out_f32=_ptr(out_f32), rows=rows, eps=eps)

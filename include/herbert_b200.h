@@ -370,7 +370,7 @@ HB_API hb_status hb_gdn_front(const hb_gdn_shape *shape, const hb_gdn_front_call
                               void *workspace, size_t workspace_bytes, hb_stream_t stream);
 
 /*
- * Gated RMS norm of the recurrence output, the delta-normed-gate node
+ * Gated RMS norm of the recurrence output, the delta-gated-norm node
  * (src/jit/target/x86/execution/delta.rs:706-774): per (row, V head) of
  * width hvd, y = ((x * 1/sqrt(sum x^2 / hvd + eps)) * w) * silu(z), in the
  * vector kernel's form (src/jit/target/x86/emit_gated_norm.rs) at hvd a

@@ -1043,7 +1043,7 @@ void orc_gdn_gates(const float *ab, const uint16_t *dt_bias, const float *a_log,
         }
 }
 
-/* delta-normed-gate (delta.rs:706-774), one row of width dim each:
+/* delta-gated-norm (delta.rs:706-774), one row of width dim each:
  * dim % 16 == 0 and dim <= 128: the vector kernel (emit_gated_norm.rs) --
  * sum of squares in min(4, dim/16) FMA chains over 16 lanes, chains added in
  * order, horizontal sum (l, l+8) -> (l, l+4) -> hadd -> hadd; then

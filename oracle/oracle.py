@@ -341,7 +341,7 @@ def gdn_gates(ab, dt_bias, a_log):
 
 
 def gdn_gated_norm(x, z, weight, eps=1e-6, impl=0):
-    """delta-normed-gate over rows of width weight.size: x, z [..., dim] f32.
+    """delta-gated-norm over rows of width weight.size: x, z [..., dim] f32.
     Returns (y f32, y bf16 bits)."""
     y = np.array(x, dtype=np.float32, copy=True, order="C")
     zz = np.ascontiguousarray(z, dtype=np.float32)
