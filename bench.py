@@ -14,6 +14,9 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
   gdn_front  DeltaNet front end of a 4096-row block: causal conv + SiLU
            over qkv (8192 channels, K 4), beta/decay gates               GB/s
   gdn_norm   DeltaNet gated RMS norm of a 4096-row block (32 V heads)    GB/s
+  snapshot   snapshot of a hybrid model's state at 32768 positions into a
+           pinned host image in the reference's format (8 attention layers'
+           KV, 24 DeltaNet layers' states, logits); e2e adds the restore  GB/s
 A step is one pass of the path over one batch: one prefill / one decode step /
 one GDN prefill + 256 steps / one decode step of the whole batch / one
 131072-token prefill / one front-end (or gated-norm) call.  The ring holds NCCL calls, so `cp` steps are issued
@@ -60,7 +63,7 @@ L2_BYTES = 126 << 20
 # large to capture.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
                "batch": 4_452_000_000, "cp": None, "front": 56_784_128,
-               "gdn_front": 213_700_000, "gdn_norm": 153_000_000}
+               "gdn_front": 213_700_000, "gdn_norm": 153_000_000, "snapshot": None}
 
 
 def peaks():
@@ -645,12 +648,94 @@ class GdnNormWorkload(Workload):
                 "head_v_dim": HVD}
 
 
+SNAP_LAYERS, SNAP_EVERY, SNAP_POS = 32, 4, 32768  # every 4th layer full attention
+SNAP_VOCAB = 248_320
+
+
+class SnapshotWorkload(Workload):
+    """One sequence's state at SNAP_POS positions: the KV of the full-attention
+    layers (Hkv 4, d 256, reserve SNAP_POS), the DeltaNet conv and recurrent
+    states of the others, the logits; a step is one hb_snapshot_take into a
+    pinned host image in the reference's format.  The host link's rate is
+    measured in the same run by one contiguous pinned copy of the same size."""
+    graphable = False  # the take writes the image's header on the host
+
+    def __init__(self, device, seed=0x5EED0009):
+        import numpy as np
+        import torch
+        import herbert_b200 as hb
+        self.hb = hb
+        gen = torch.Generator(device=device).manual_seed(seed)
+        hds = [HD if l % SNAP_EVERY == SNAP_EVERY - 1 else 0 for l in range(SNAP_LAYERS)]
+        n_delta = hds.count(0)
+        offsets = np.concatenate([[0], np.cumsum([2 * HKV * SNAP_POS * h for h in hds])])
+        conv = n_delta * (2 * NK * HKD + NV * HVD) * 4
+        rec = n_delta * NV * HKD * HVD
+        logits = -(-SNAP_VOCAB // 16) * 16
+        self.geo = hb.Geometry(offsets, HKV, SNAP_POS, conv, rec, logits)
+        self.kv = torch.randint(-32768, 32767, (int(offsets[-1]),), dtype=torch.int16,
+                                device=device, generator=gen)
+        self.conv = torch.randn(conv, generator=gen, device=device)
+        self.rec = torch.randn(rec, generator=gen, device=device)
+        self.logits = torch.randint(-32768, 32767, (logits,), dtype=torch.int16, device=device,
+                                    generator=gen)
+        self.nbytes = hb.snapshot_bytes(self.geo, SNAP_POS)
+        self.image = torch.empty(self.nbytes, dtype=torch.uint8).pin_memory()
+        self.flat = torch.empty(int(offsets[-1]) * 2 + conv * 4 + rec * 4 + logits * 2,
+                                dtype=torch.uint8, device=device)
+        self.work = self.nbytes
+        self.units = "GB/s"
+        self.R = 1
+        self.set_bytes = self.nbytes
+        self.h2d = self.nbytes
+        self.d2h = self.nbytes
+
+    def step(self, i=0):
+        self.hb.snapshot_take(self.geo, self.kv, self.conv, self.rec, self.logits, self.image,
+                              pos=SNAP_POS, max_positions=SNAP_POS)
+
+    def e2e_step(self, i=0):
+        self.step(i)
+        self.hb.snapshot_restore(self.geo, self.kv, self.conv, self.rec, self.logits, self.image,
+                                 p=SNAP_POS)
+
+    def kernel_probe(self, reps=3):
+        """(bytes, seconds) of one take, and the rate of a contiguous pinned
+        device-to-host copy of the same bytes (the host link's ceiling)."""
+        import torch
+        st = torch.cuda.current_stream()
+
+        def timed(fn):
+            fn()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            a.record(st)
+            for _ in range(reps):
+                fn()
+            b.record(st)
+            torch.cuda.synchronize()
+            return a.elapsed_time(b) / 1e3 / reps
+
+        t_take = timed(self.step)
+        t_flat = timed(lambda: self.image[:self.flat.numel()].copy_(self.flat, non_blocking=True))
+        self.link_gbs = self.flat.numel() / t_flat / 1e9
+        return self.nbytes, t_take
+
+    def describe(self):
+        return {"workload": "snapshot of one sequence's state (reference Instantaneous format) "
+                "into a pinned host image", "positions": SNAP_POS, "layers": SNAP_LAYERS,
+                "attention_layers": SNAP_LAYERS // SNAP_EVERY, "kv_heads": HKV, "head_dim": HD,
+                "deltanet_layers": SNAP_LAYERS - SNAP_LAYERS // SNAP_EVERY,
+                "image_bytes": self.nbytes}
+
+
 METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
           "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s",
           "front": "attn front end HBM GB/s", "gdn_front": "GDN front end HBM GB/s",
-          "gdn_norm": "GDN gated norm HBM GB/s"}
+          "gdn_norm": "GDN gated norm HBM GB/s", "snapshot": "snapshot take GB/s"}
 BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor",
-         "front": "hbm", "gdn_front": "hbm", "gdn_norm": "hbm"}
+         "front": "hbm", "gdn_front": "hbm", "gdn_norm": "hbm", "snapshot": "host link"}
 STRONG = ("batch", "cp")  # total work fixed as the GPUs grow
 
 
@@ -671,6 +756,8 @@ def make_workload(cfg, device, rank, world):
         return GdnFrontWorkload(device)
     if cfg == "gdn_norm":
         return GdnNormWorkload(device)
+    if cfg == "snapshot":
+        return SnapshotWorkload(device)
     raise SystemExit(f"unknown config {cfg}")
 
 
@@ -774,7 +861,10 @@ def run_ours(args):
         # cap: its denominator is the sustained GEMM figure, else the burst one
         sustained = t_dev >= 0.5
         bf16_peak = pk["bf16_sustained"] if sustained else pk["bf16"]
-        if probe is not None:
+        if probe is not None and cfg == "snapshot":
+            achieved = probe[0] / probe[1] / 1e9
+            peak, unit = round(wl.link_gbs, 3), "GB/s"
+        elif probe is not None:
             achieved = probe[0] / probe[1] / 1e12
             peak, unit = bf16_peak, "TFLOP/s"
         elif BOUND[cfg] == "tensor":
@@ -794,7 +884,8 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "strong" if cfg in STRONG else "weak",
             "vs_baseline": None,
-            "dtype": "f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else "bf16",
+            "dtype": ("f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else
+                      "bytes" if cfg == "snapshot" else "bf16"),
             "data": "synthetic",
             "config": dict(wl.describe(), parallelism=(
                 f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
@@ -821,9 +912,14 @@ def run_ours(args):
             line["roofline"]["kernel"] = (
                 "gdn_prep_kernel + gdn_scan_kernel (one chunked prefill of T tokens)"
                 if cfg == "gdn" else
+                "hb_snapshot_take: one 2-D copy per (layer, K|V) and one per state"
+                if cfg == "snapshot" else
                 "attn_prefill_kernel over the whole sequence" if world == 1 else
                 "attn_prefill_kernel<CP> hop over the rank's own shard (hop 0)")
             line["roofline"]["launch_ms"] = round(probe[1] * 1e3, 4)
+            if cfg == "snapshot":
+                line["roofline"]["peak_source"] = ("a contiguous pinned device-to-host copy of "
+                                                   "the same bytes, measured in this run")
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -905,6 +1001,23 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
         else:
             work = gdn_norm_bytes(rows)
             fn = lambda: oracle.gdn_gated_norm(d.x, d.z, d.norm_weight, 1e-6, impl)  # noqa: E731
+    elif cfg == "snapshot":
+        sys.path[:0] = [os.path.join(ROOT, "oracle")]
+        import snapshot as S
+        pos = 2048
+        hds = [HD if l % SNAP_EVERY == SNAP_EVERY - 1 else 0 for l in range(SNAP_LAYERS)]
+        n_delta = hds.count(0)
+        r = S.seeded_runner(HKV, pos, hds, n_delta * (2 * NK * HKD + NV * HVD) * 4,
+                            n_delta * NV * HKD * HVD, -(-SNAP_VOCAB // 16) * 16, pos, 1)
+        slot = S.snapshot_reserve(r, pos)
+        work = len(S.write_to((S.snapshot_take(r, slot), slot)[1]))
+        unit, scale = "GB/s", 1e9
+        threads = 1
+        sample = f"the same state at {pos} positions (one thread, numpy)"
+
+        def fn():
+            S.snapshot_take(r, slot)
+            S.write_to(slot)
     else:  # gdn
         T = 64
         d = DeltaInputs(T)
@@ -945,7 +1058,8 @@ def run_reference(args):
         "metric": METRIC[cfg], "value": v, "unit": base["unit"], "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong" if cfg in STRONG else "weak", "vs_baseline": None,
-        "dtype": "f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else "bf16", "data": "synthetic",
+        "dtype": ("f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else
+                  "bytes" if cfg == "snapshot" else "bf16"), "data": "synthetic",
         "config": {"workload": cfg, "note": "CPU restatement of the reference's x86 AVX-512 BF16 "
                    "kernels (Rust reference not buildable here)"},
         "cpu_baseline": dict(base, value=v),

@@ -110,6 +110,18 @@ class GdnNormCall(ctypes.Structure):
                 ("out_f32", c_void_p), ("rows", c_int64), ("eps", c_float)]
 
 
+class StateGeometry(ctypes.Structure):
+    """hb_state_geometry: where a sequence's state lives on the device."""
+    _fields_ = [("kv_offsets", c_void_p), ("n_layers", c_int64), ("kv_heads", c_int64),
+                ("kv_reserve", c_int64), ("conv_len", c_int64), ("recurrent_len", c_int64),
+                ("logits_len", c_int64)]
+
+
+class StateBuffers(ctypes.Structure):
+    _fields_ = [("kv", c_void_p), ("dn_conv", c_void_p), ("dn_recurrent", c_void_p),
+                ("logits", c_void_p)]
+
+
 class CpSpec(ctypes.Structure):
     """hb_cp_spec: a zig-zag sharded sequence of 2*ranks*chunk positions."""
     _fields_ = [("ranks", c_int32), ("rank", c_int32), ("chunk", c_int64)]
@@ -149,6 +161,12 @@ _SIGNATURES = {
     "hb_gdn_front": (ctypes.c_int, [_P(DeltaShape), _P(GdnFrontCall), c_void_p, c_size_t,
                                     c_void_p]),
     "hb_gdn_gated_norm": (ctypes.c_int, [_P(DeltaShape), _P(GdnNormCall), c_void_p]),
+    "hb_snapshot_bytes": (c_size_t, [_P(StateGeometry), c_int64]),
+    "hb_snapshot_take": (ctypes.c_int, [_P(StateGeometry), _P(StateBuffers), c_int64, c_int64,
+                                        c_void_p, c_size_t, c_void_p]),
+    "hb_snapshot_restore": (ctypes.c_int, [_P(StateGeometry), _P(StateBuffers), c_void_p,
+                                           c_size_t, c_int64, c_void_p]),
+    "hb_snapshot_info": (ctypes.c_int, [c_void_p, c_size_t, _P(c_int64), _P(c_int32)]),
     "hb_cp_hop_source": (c_int32, [_P(CpSpec), c_int32]),
     "hb_cp_row_position": (c_int64, [_P(CpSpec), c_int32, c_int64]),
     "hb_attn_prefill_cp_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(CpSpec)]),
@@ -370,6 +388,60 @@ def delta_gated_norm(shape: DeltaShape, x, z, weight, out, *, rows: int, eps: fl
     call = GdnNormCall(x=_ptr(x), z=_ptr(z), weight=_ptr(weight), out=_ptr(out),
                        out_f32=_ptr(out_f32), rows=rows, eps=eps)
     check(lib().hb_gdn_gated_norm(ctypes.byref(shape), ctypes.byref(call), _stream(stream)))
+
+
+# --------------------------------------------------------------- snapshot
+
+class Geometry:
+    """hb_state_geometry plus the kv_offsets array it points to (kept alive)."""
+
+    def __init__(self, kv_offsets, kv_heads, kv_reserve, conv_len=0, recurrent_len=0,
+                 logits_len=0):
+        import numpy as np
+        self.offsets = np.ascontiguousarray(kv_offsets, dtype=np.int64)
+        self.c = StateGeometry(kv_offsets=self.offsets.ctypes.data, n_layers=self.offsets.size - 1,
+                               kv_heads=kv_heads, kv_reserve=kv_reserve, conv_len=conv_len,
+                               recurrent_len=recurrent_len, logits_len=logits_len)
+
+
+def _host_ptr(image):
+    """Address and byte size of a host image: a numpy array or a CPU torch tensor."""
+    if hasattr(image, "data_ptr"):
+        return int(image.data_ptr()), int(image.numel() * image.element_size())
+    return int(image.ctypes.data), int(image.nbytes)
+
+
+def snapshot_bytes(geo: Geometry, max_positions: int) -> int:
+    return int(lib().hb_snapshot_bytes(ctypes.byref(geo.c), max_positions))
+
+
+def snapshot_take(geo: Geometry, kv, dn_conv, dn_recurrent, logits, image, *, pos: int,
+                  max_positions: int, stream=None) -> None:
+    """snapshot_take + write_to: the state at `pos` into the host image (stream-ordered;
+    synchronise before reading the image)."""
+    bufs = StateBuffers(kv=_ptr(kv), dn_conv=_ptr(dn_conv), dn_recurrent=_ptr(dn_recurrent),
+                        logits=_ptr(logits))
+    ptr, nbytes = _host_ptr(image)
+    check(lib().hb_snapshot_take(ctypes.byref(geo.c), ctypes.byref(bufs), pos, max_positions,
+                                 c_void_p(ptr), nbytes, _stream(stream)))
+
+
+def snapshot_restore(geo: Geometry, kv, dn_conv, dn_recurrent, logits, image, *, p: int,
+                     stream=None) -> None:
+    """Instantaneous::read + restore_from: the image's state truncated to `p` positions."""
+    bufs = StateBuffers(kv=_ptr(kv), dn_conv=_ptr(dn_conv), dn_recurrent=_ptr(dn_recurrent),
+                        logits=_ptr(logits))
+    ptr, nbytes = _host_ptr(image)
+    check(lib().hb_snapshot_restore(ctypes.byref(geo.c), ctypes.byref(bufs), c_void_p(ptr),
+                                    nbytes, p, _stream(stream)))
+
+
+def snapshot_info(image) -> tuple:
+    """(pos, restorable_below) of an image."""
+    ptr, nbytes = _host_ptr(image)
+    pos, below = c_int64(0), c_int32(0)
+    check(lib().hb_snapshot_info(c_void_p(ptr), nbytes, ctypes.byref(pos), ctypes.byref(below)))
+    return int(pos.value), bool(below.value)
 
 
 # ------------------------------------------------- context-parallel prefill

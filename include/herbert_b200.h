@@ -389,6 +389,72 @@ typedef struct hb_gdn_norm_call {
 HB_API hb_status hb_gdn_gated_norm(const hb_gdn_shape *shape, const hb_gdn_norm_call *call,
                                    hb_stream_t stream);
 
+/* ------------------------------------------------------------- snapshot */
+
+/*
+ * Snapshot / restore of a sequence's device state in the reference's
+ * serialized `Instantaneous` format, version 1 (src/jit/model.rs:100-326;
+ * take src/jit/model.rs:732-774, restore :786-857).  The image, all
+ * little-endian, is
+ *   u32 1 | u64 n, u64 kv_offsets[n] | u64 n, u64 snap_offsets[n] |
+ *   u64 n, u64 snap_positions[n] | u64 n, u16 kv[n] | u64 n, u16 logits[n] |
+ *   u64 n, f32 dn_conv[n] | u64 n, f32 dn_recurrent[n] | u64 pos
+ * with snap_positions[l] = min(kv_reserve, max_positions) on a layer with a
+ * cache (0 without), the snapshot KV of layer l at snap_offsets[l] laid out as
+ * the device cache [K|V][kv_heads][snap_positions[l]][head_dim].  Written
+ * once to disk, an image is the reference's file (Instantaneous::write_to,
+ * :270-287); a file it wrote restores here.
+ *
+ * The slot is the image itself, in host memory (pinned for full DMA speed):
+ * a take moves the first `pos` positions of every head with one 2-D copy
+ * per (layer, K|V), and the states and logits with one copy each, straight
+ * to their place in the image; a restore copies the first `p` positions
+ * back.  Positions of the slot beyond `pos` are written as zeros (the bytes
+ * of a freshly reserved slot).  Copies are stream-ordered: the image is
+ * complete, and the device state restored, when `stream` reaches them.
+ */
+typedef struct hb_state_geometry {
+    const int64_t *kv_offsets;  /* [n_layers + 1] offsets (bf16 elements) of each layer's cache in
+                                   the device KV buffer: Runner::kv_offsets (model.rs:545-559)  */
+    int64_t n_layers;
+    int64_t kv_heads;           /* n_kv_heads                                                    */
+    int64_t kv_reserve;         /* positions reserved per head (kv_reserve_tokens)               */
+    int64_t conv_len;           /* f32 elements of the DeltaNet conv states, all layers          */
+    int64_t recurrent_len;      /* f32 elements of the DeltaNet recurrent states, all layers     */
+    int64_t logits_len;         /* bf16 logits of the last token (vocab rounded up to 16)        */
+} hb_state_geometry;
+typedef struct hb_state_buffers {  /* device memory */
+    uint16_t *kv;
+    float *dn_conv;
+    float *dn_recurrent;
+    uint16_t *logits;
+} hb_state_buffers;
+
+/* Bytes of the image of a slot reserved for `max_positions` (snapshot_reserve,
+ * model.rs:675-699); 0 for an invalid geometry. */
+HB_API size_t hb_snapshot_bytes(const hb_state_geometry *geometry, int64_t max_positions);
+/* snapshot_take: the state at position `pos` into `image` (hb_snapshot_bytes
+ * bytes).  Refused (HB_ERR_ARG, nothing copied) when a layer holds more
+ * positions than the slot (pos > min(kv_reserve, max_positions)). */
+HB_API hb_status hb_snapshot_take(const hb_state_geometry *geometry, const hb_state_buffers *state,
+                                  int64_t pos, int64_t max_positions, void *image,
+                                  size_t image_bytes, hb_stream_t stream);
+/* Instantaneous::read + restore_from: validates the image (format version,
+ * every length bounded by 64 GiB and by image_bytes, self-consistent
+ * offsets) and the request, then restores the state truncated to `p`
+ * positions.  Refusals, before any copy: HB_ERR_ARG for another format
+ * version, a corrupted image, p > pos, or p < pos when the model has a
+ * recurrent state; HB_DECLINE_GEOMETRY for an image of another geometry
+ * (kv_offsets or state lengths differ). */
+HB_API hb_status hb_snapshot_restore(const hb_state_geometry *geometry, const hb_state_buffers *state,
+                                     const void *image, size_t image_bytes, int64_t p,
+                                     hb_stream_t stream);
+/* The position an image holds and Instantaneous::restorable_at(p) for each
+ * p: *restorable_below = 1 when positions below *pos restore too (no
+ * recurrent state).  Validates as hb_snapshot_restore. */
+HB_API hb_status hb_snapshot_info(const void *image, size_t image_bytes, int64_t *pos,
+                                  int32_t *restorable_below);
+
 /*
  * Self-test, no counterpart in the reference: runs the arithmetic of
  * hb_attn_prefill's epilogue (O / l rounded to bf16, then the output gate)

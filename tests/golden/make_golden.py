@@ -76,7 +76,17 @@ def main():
                         qkv_out=y, conv_state_out=st, beta=beta, decay=decay, norm_f32=yn,
                         norm_bf16=ob, meta=np.array([d.rows, d.nk, d.nv, d.hkd, d.hvd, d.ck],
                                                     np.int64))
-    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
+    # snapshot image of a hybrid state (two cached layers among eight, DeltaNet
+    # states, logits) at position 21 in a 32-position slot, as the reference's
+    # Instantaneous::write_to lays it out
+    import snapshot as S
+    r = S.seeded_runner(2, 40, [0, 0, 0, 64, 0, 0, 0, 64], 6 * 96 * 4, 6 * 2 * 16 * 16, 48, 21,
+                        0x60D4)
+    slot = S.snapshot_reserve(r, 32)
+    S.snapshot_take(r, slot)
+    with open(os.path.join(HERE, "snapshot_hybrid.bin"), "wb") as f:
+        f.write(S.write_to(slot))
+    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith((".npz", ".bin"))))
 
 
 if __name__ == "__main__":

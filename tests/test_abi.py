@@ -38,7 +38,8 @@ def test_record_layouts_match_the_header(tmp_path):
             "hb_gdn_shape": hb.DeltaShape, "hb_gdn_call": hb.RecurrenceCall,
             "hb_cp_spec": hb.CpSpec, "hb_front_spec": hb.FrontSpec,
             "hb_front_call": hb.FrontCall, "hb_gdn_front_call": hb.GdnFrontCall,
-            "hb_gdn_norm_call": hb.GdnNormCall}
+            "hb_gdn_norm_call": hb.GdnNormCall, "hb_state_geometry": hb.StateGeometry,
+            "hb_state_buffers": hb.StateBuffers}
     body = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{hb.HEADER_PATH}"',
             "int main(void){"]
     for c, py in recs.items():
