@@ -659,6 +659,7 @@ class SnapshotWorkload(Workload):
     pinned host image in the reference's format.  The host link's rate is
     measured in the same run by one contiguous pinned copy of the same size."""
     graphable = False  # the take writes the image's header on the host
+    launches_per_step = 0  # copies only: 2 per attention layer (K, V) + 3 (states, logits)
 
     def __init__(self, device, seed=0x5EED0009):
         import numpy as np
@@ -906,6 +907,8 @@ def run_ours(args):
                     "unit": wl.units, "h2d_bytes_per_step": int(wl.h2d),
                     "d2h_bytes_per_step": int(wl.d2h)},
             "gpu_launches": int(wl.launches_per_step * args.steps),
+            **({"dma_copies": (2 * (SNAP_LAYERS // SNAP_EVERY) + 3) * args.steps}
+               if cfg == "snapshot" else {}),
             "clocks": clocks,
         }
         if probe is not None:
@@ -1037,8 +1040,9 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
     val = work * reps / el / scale
     return {"value": round(val, 6), "unit": unit, "cores": threads,
             "kind": "port",
-            "sample": sample + f", repeated {reps}x in {el:.1f} s; "
-                      f"{'AVX512-BF16 transcription' if impl else 'portable emulation'}"}
+            "sample": sample + f", repeated {reps}x in {el:.1f} s" + (
+                "" if cfg == "snapshot" else
+                f"; {'AVX512-BF16 transcription' if impl else 'portable emulation'}")}
 
 
 def run_reference(args):
