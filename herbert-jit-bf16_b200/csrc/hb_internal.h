@@ -169,6 +169,10 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const v
                uint64_t rows, uint64_t cols, uint64_t row_stride_elems, uint32_t box_rows,
                uint32_t box_cols, CUtensorMapSwizzle swizzle);
 
+// A state geometry (hb_state_geometry) that the snapshot and mount entry
+// points accept: layer offsets multiples of 2 x kv_heads x kv_reserve.
+hb_status check_state_geometry(const hb_state_geometry* g);
+
 // Host-side checks and error reporting shared by the API translation units
 // (hb_api.cu): a failure sets the thread-local message of hb_last_error.
 hb_status fail(hb_status s, const char* fmt, ...);

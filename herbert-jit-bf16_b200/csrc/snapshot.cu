@@ -45,7 +45,7 @@ struct Geo {
   }
 };
 
-hb_status check_geometry(const hb_state_geometry* g, Geo* out) {
+hb_status check_geometry_(const hb_state_geometry* g, Geo* out) {
   out->g = g;
   if (!g || !g->kv_offsets) return fail(HB_ERR_ARG, "state geometry or kv_offsets is null");
   const int64_t lim = int64_t(1) << 40;
@@ -159,20 +159,26 @@ cudaError_t copy_flat(void* dst, const void* src, size_t bytes, cudaMemcpyKind k
 }
 
 }  // namespace
+
+hb_status check_state_geometry(const hb_state_geometry* g) {
+  Geo G;
+  return check_geometry_(g, &G);
+}
+
 }  // namespace hb
 
 using namespace hb;
 
 size_t hb_snapshot_bytes(const hb_state_geometry* g, int64_t max_positions) {
   Geo G;
-  if (check_geometry(g, &G) != HB_OK || max_positions < 0) return 0;
+  if (check_geometry_(g, &G) != HB_OK || max_positions < 0) return 0;
   return image_bytes_for(G, max_positions);
 }
 
 hb_status hb_snapshot_take(const hb_state_geometry* g, const hb_state_buffers* b, int64_t pos,
                            int64_t max_positions, void* image, size_t image_bytes, hb_stream_t stream) {
   Geo G;
-  hb_status r = check_geometry(g, &G);
+  hb_status r = check_geometry_(g, &G);
   if (r != HB_OK) return r;
   if (!b || !image) return fail(HB_ERR_ARG, "state buffers or image is null");
   if (pos < 0 || max_positions < 0 || pos > g->kv_reserve)
@@ -258,7 +264,7 @@ hb_status hb_snapshot_take(const hb_state_geometry* g, const hb_state_buffers* b
 hb_status hb_snapshot_restore(const hb_state_geometry* g, const hb_state_buffers* b, const void* image,
                               size_t image_bytes, int64_t p, hb_stream_t stream) {
   Geo G;
-  hb_status r = check_geometry(g, &G);
+  hb_status r = check_geometry_(g, &G);
   if (r != HB_OK) return r;
   if (!b) return fail(HB_ERR_ARG, "state buffers are null");
   Image im;

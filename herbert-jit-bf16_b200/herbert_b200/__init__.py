@@ -122,6 +122,35 @@ class StateBuffers(ctypes.Structure):
                 ("logits", c_void_p)]
 
 
+HB_LAYER_ATTENTION, HB_LAYER_DELTA = 1, 2
+
+
+class MountDesc(ctypes.Structure):
+    """hb_mount_desc: the model's layers bound to one sequence's state."""
+    _fields_ = [("geometry", ctypes.POINTER(StateGeometry)), ("state", ctypes.POINTER(StateBuffers)),
+                ("layer_kinds", c_void_p), ("attn", AttentionSpec), ("attn_scale", c_float),
+                ("rotary", c_int64), ("cos", c_void_p), ("sin", c_void_p), ("norm_eps", c_float),
+                ("gemma", c_int32), ("delta", DeltaShape), ("conv_kernel", c_int64),
+                ("conv_stride", c_int64), ("recurrent_stride", c_int64), ("max_rows", c_int64)]
+
+
+class LayerRoute(ctypes.Structure):
+    _fields_ = [("kind", c_int32), ("delta_index", c_int32), ("keys", c_void_p),
+                ("values", c_void_p), ("kv_stride", c_int64), ("conv_state", c_void_p),
+                ("recurrent_state", c_void_p)]
+
+
+class MountAttentionCall(ctypes.Structure):
+    _fields_ = [("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("q_norm", c_void_p),
+                ("k_norm", c_void_p), ("out", c_void_p), ("rows", c_int64), ("pos", c_int64)]
+
+
+class MountDeltaCall(ctypes.Structure):
+    _fields_ = [("qkv", c_void_p), ("ab", c_void_p), ("z", c_void_p), ("conv_weight", c_void_p),
+                ("dt_bias", c_void_p), ("a_log", c_void_p), ("norm_weight", c_void_p),
+                ("out", c_void_p), ("out_f32", c_void_p), ("rows", c_int64)]
+
+
 class CpSpec(ctypes.Structure):
     """hb_cp_spec: a zig-zag sharded sequence of 2*ranks*chunk positions."""
     _fields_ = [("ranks", c_int32), ("rank", c_int32), ("chunk", c_int64)]
@@ -167,6 +196,12 @@ _SIGNATURES = {
     "hb_snapshot_restore": (ctypes.c_int, [_P(StateGeometry), _P(StateBuffers), c_void_p,
                                            c_size_t, c_int64, c_void_p]),
     "hb_snapshot_info": (ctypes.c_int, [c_void_p, c_size_t, _P(c_int64), _P(c_int32)]),
+    "hb_mount_route": (ctypes.c_int, [_P(MountDesc), c_int64, _P(LayerRoute)]),
+    "hb_mount_create": (ctypes.c_int, [_P(MountDesc), _P(c_void_p)]),
+    "hb_mount_destroy": (None, [c_void_p]),
+    "hb_mount_status": (ctypes.c_int, [c_void_p, c_void_p]),
+    "hb_mount_attention": (ctypes.c_int, [c_void_p, c_int64, _P(MountAttentionCall), c_void_p]),
+    "hb_mount_delta": (ctypes.c_int, [c_void_p, c_int64, _P(MountDeltaCall), c_void_p]),
     "hb_cp_hop_source": (c_int32, [_P(CpSpec), c_int32]),
     "hb_cp_row_position": (c_int64, [_P(CpSpec), c_int32, c_int64]),
     "hb_attn_prefill_cp_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(CpSpec)]),
@@ -442,6 +477,77 @@ def snapshot_info(image) -> tuple:
     pos, below = c_int64(0), c_int32(0)
     check(lib().hb_snapshot_info(c_void_p(ptr), nbytes, ctypes.byref(pos), ctypes.byref(below)))
     return int(pos.value), bool(below.value)
+
+
+# ------------------------------------------------------------------ mount
+
+def mount_desc(geo: Geometry, kinds, *, kv=None, dn_conv=None, dn_recurrent=None, logits=None,
+               attn: AttentionSpec | None = None, attn_scale=0.0625, rotary=64, cos=None,
+               sin=None, norm_eps=1e-6, gemma=True, delta: DeltaShape | None = None,
+               conv_kernel=4, conv_stride=0, recurrent_stride=0, max_rows=1):
+    """An hb_mount_desc and the objects it points to (returned together so that
+    they stay alive).  Buffers are device tensors or raw addresses."""
+    import numpy as np
+    addr = lambda t: t if isinstance(t, int) else _ptr(t)  # noqa: E731
+    k = np.ascontiguousarray(kinds, dtype=np.int32)
+    bufs = StateBuffers(kv=addr(kv), dn_conv=addr(dn_conv), dn_recurrent=addr(dn_recurrent),
+                        logits=addr(logits))
+    d = MountDesc(geometry=ctypes.pointer(geo.c), state=ctypes.pointer(bufs),
+                  layer_kinds=k.ctypes.data, attn=attn or attention_spec(),
+                  attn_scale=attn_scale, rotary=rotary, cos=addr(cos), sin=addr(sin),
+                  norm_eps=norm_eps, gemma=int(gemma),
+                  delta=delta or DeltaShape(nk=16, nv=32, hkd=128, hvd=128),
+                  conv_kernel=conv_kernel, conv_stride=conv_stride,
+                  recurrent_stride=recurrent_stride, max_rows=max_rows)
+    return d, (geo, k, bufs)
+
+
+def mount_route(desc: MountDesc, layer: int) -> LayerRoute:
+    r = LayerRoute()
+    check(lib().hb_mount_route(ctypes.byref(desc), layer, ctypes.byref(r)))
+    return r
+
+
+class Mount:
+    """hb_mount: the per-layer routing of a pass (owns its workspaces)."""
+
+    def __init__(self, desc: MountDesc, keep=()):
+        self._keep = keep
+        self.h = c_void_p()
+        check(lib().hb_mount_create(ctypes.byref(desc), ctypes.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            lib().hb_mount_destroy(self.h)
+            self.h = c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def status(self, stream=None):
+        check(lib().hb_mount_status(self.h, _stream(stream)))
+
+    def attention(self, layer, q, k, v, q_norm, k_norm, out, *, rows, pos, stream=None):
+        c = MountAttentionCall(q=_ptr(q), k=_ptr(k), v=_ptr(v), q_norm=_ptr(q_norm),
+                               k_norm=_ptr(k_norm), out=_ptr(out), rows=rows, pos=pos)
+        check(lib().hb_mount_attention(self.h, layer, ctypes.byref(c), _stream(stream)))
+
+    def delta(self, layer, qkv, ab, z, conv_weight, dt_bias, a_log, norm_weight, out, *, rows,
+              out_f32=None, stream=None):
+        c = MountDeltaCall(qkv=_ptr(qkv), ab=_ptr(ab), z=_ptr(z), conv_weight=_ptr(conv_weight),
+                           dt_bias=_ptr(dt_bias), a_log=_ptr(a_log),
+                           norm_weight=_ptr(norm_weight), out=_ptr(out), out_f32=_ptr(out_f32),
+                           rows=rows)
+        check(lib().hb_mount_delta(self.h, layer, ctypes.byref(c), _stream(stream)))
 
 
 # ------------------------------------------------- context-parallel prefill

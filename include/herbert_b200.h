@@ -455,6 +455,94 @@ HB_API hb_status hb_snapshot_restore(const hb_state_geometry *geometry, const hb
 HB_API hb_status hb_snapshot_info(const void *image, size_t image_bytes, int64_t *pos,
                                   int32_t *restorable_below);
 
+/* --------------------------------------------------------------- mount */
+
+/*
+ * Routing of a model pass to the kernels: what the reference's lowering does
+ * per layer when it mounts a regime (src/jit/model/mounted.rs:237-380) --
+ * bind each layer to its slice of the sequence's state (the KV cache of an
+ * attention layer at kv_offsets[layer], keys then values; the conv and
+ * recurrent slots of the d-th DeltaNet layer at d * conv_stride and
+ * d * recurrent_stride) and run the layer's mixer nodes for a block of rows:
+ *   attention layer: head-norm-rope of q and k + kv-append (hb_attn_front),
+ *     then the attention and gate nodes (hb_attn_decode for one row,
+ *     hb_attn_prefill otherwise)     (src/jit/schedule/lowering.rs:549-666)
+ *   DeltaNet layer: conv + gates (hb_gdn_front), L2 + recurrence
+ *     (hb_gdn_prefill: the reference's order below 128 rows, chunked above),
+ *     gated norm (hb_gdn_gated_norm)  (src/jit/schedule/lowering.rs:897-1010)
+ * The projections around the mixers stay with the caller.  A mount owns
+ * every workspace and scratch buffer its calls need, allocated once by
+ * hb_mount_create: nothing allocates during a pass, and a pass may be
+ * captured in a CUDA graph.
+ */
+typedef struct hb_mount hb_mount;  /* opaque */
+enum { HB_LAYER_ATTENTION = 1, HB_LAYER_DELTA = 2 };
+typedef struct hb_mount_desc {
+    const hb_state_geometry *geometry;  /* the sequence's state (as for the snapshot)            */
+    const hb_state_buffers *state;      /* its device buffers                                    */
+    const int32_t *layer_kinds;         /* [geometry->n_layers]: HB_LAYER_ATTENTION / _DELTA      */
+    hb_attn_spec attn;                  /* attention layers (heads / gqa = geometry kv_heads)    */
+    float attn_scale;                   /* softmax scale                                         */
+    int64_t rotary;                     /* rotated elements per head                             */
+    const uint16_t *cos;                /* RoPE tables [kv_reserve][rotary/2] bf16, device        */
+    const uint16_t *sin;
+    float norm_eps;                     /* head-norm and gated-norm epsilon (config rms_norm_eps) */
+    int32_t gemma;                      /* head-norm weight form (1: 1 + w, Qwen3.5)              */
+    hb_gdn_shape delta;                 /* DeltaNet layers                                       */
+    int64_t conv_kernel;                /* conv kernel length (4)                                */
+    int64_t conv_stride;                /* f32 elements of one layer's conv slot (>= conv x ck)   */
+    int64_t recurrent_stride;           /* f32 elements of one recurrent slot (>= nv hkd hvd)     */
+    int64_t max_rows;                   /* the largest block a pass feeds (<= kv_reserve)         */
+} hb_mount_desc;
+/* Where a layer's mixer reads and writes its state. */
+typedef struct hb_layer_route {
+    int32_t kind;              /* HB_LAYER_ATTENTION or HB_LAYER_DELTA                           */
+    int32_t delta_index;       /* DeltaNet layers: index among them; -1 otherwise                */
+    uint16_t *keys;            /* attention: the layer's K cache, [kv_heads][kv_reserve][d]       */
+    uint16_t *values;          /* its V cache                                                    */
+    int64_t kv_stride;         /* elements between KV heads                                      */
+    float *conv_state;         /* DeltaNet: the layer's conv slot                                */
+    float *recurrent_state;    /* its recurrent slot                                             */
+} hb_layer_route;
+/* Validates the description as the lowering does (a DeltaNet layer has no
+ * KV and fits its slots; an attention layer's KV is heads x kv_reserve x
+ * head_dim) and gives layer `layer`'s route; host only, no allocation.
+ * HB_DECLINE_GEOMETRY for a plan mismatch. */
+HB_API hb_status hb_mount_route(const hb_mount_desc *desc, int64_t layer, hb_layer_route *route);
+/* hb_mount_route's checks for every layer, then the workspaces and scratch. */
+HB_API hb_status hb_mount_create(const hb_mount_desc *desc, hb_mount **mount);
+HB_API void hb_mount_destroy(hb_mount *mount);
+/* The status word of the mount's workspaces (as hb_workspace_status). */
+HB_API hb_status hb_mount_status(hb_mount *mount, hb_stream_t stream);
+
+typedef struct hb_mount_attention_call {
+    uint16_t *q;               /* [rows][attn.q_row]: heads (normed and rotated in place), gates  */
+    uint16_t *k;               /* [rows][kv_heads*d]: normed and rotated in place, then cached     */
+    const uint16_t *v;         /* [rows][kv_heads*d]: cached                                       */
+    const uint16_t *q_norm;    /* [d] bf16 head-norm weights of the layer                          */
+    const uint16_t *k_norm;
+    uint16_t *out;             /* [rows][attn.out_row] bf16                                        */
+    int64_t rows;              /* 1 .. max_rows                                                     */
+    int64_t pos;               /* position of row 0 (pos + rows <= kv_reserve)                      */
+} hb_mount_attention_call;
+HB_API hb_status hb_mount_attention(hb_mount *mount, int64_t layer, const hb_mount_attention_call *call,
+                                    hb_stream_t stream);
+
+typedef struct hb_mount_delta_call {
+    float *qkv;                   /* [rows][2 nk hkd + nv hvd]: conv + SiLU in place             */
+    const float *ab;              /* [rows][2 nv]                                                */
+    const float *z;               /* [rows][nv hvd] gate projection                              */
+    const uint16_t *conv_weight;  /* [conv][ck] bf16                                             */
+    const uint16_t *dt_bias;      /* [nv] bf16                                                   */
+    const float *a_log;           /* [nv]                                                        */
+    const uint16_t *norm_weight;  /* [hvd] bf16                                                  */
+    uint16_t *out;                /* [rows][nv hvd] bf16: the out-projection's input             */
+    float *out_f32;               /* optional f32 copy of out (NULL: not written)                */
+    int64_t rows;                 /* 1 .. max_rows                                               */
+} hb_mount_delta_call;
+HB_API hb_status hb_mount_delta(hb_mount *mount, int64_t layer, const hb_mount_delta_call *call,
+                                hb_stream_t stream);
+
 /*
  * Self-test, no counterpart in the reference: runs the arithmetic of
  * hb_attn_prefill's epilogue (O / l rounded to bf16, then the output gate)
