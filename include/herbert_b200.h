@@ -473,7 +473,8 @@ HB_API hb_status hb_snapshot_info(const void *image, size_t image_bytes, int64_t
  * The projections around the mixers stay with the caller.  A mount owns
  * every workspace and scratch buffer its calls need, allocated once by
  * hb_mount_create: nothing allocates during a pass, and a pass may be
- * captured in a CUDA graph.
+ * captured in a CUDA graph.  Calls on one mount share that scratch: order
+ * them on one stream (or with events).
  */
 typedef struct hb_mount hb_mount;  /* opaque */
 enum { HB_LAYER_ATTENTION = 1, HB_LAYER_DELTA = 2 };
