@@ -14,6 +14,10 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
   gdn_front  DeltaNet front end of a 4096-row block: causal conv + SiLU
            over qkv (8192 channels, K 4), beta/decay gates               GB/s
   gdn_norm   DeltaNet gated RMS norm of a 4096-row block (32 V heads)    GB/s
+  mixers     one decode token through the mixers of all 32 layers of a hybrid
+           model (8 attention at 32768 positions, 24 DeltaNet) routed by an
+           hb_mount: per layer the front end, attention or recurrence, and
+           the gated norm; the projections are not part of it             tok/s
   snapshot   snapshot of a hybrid model's state at 32768 positions into a
            pinned host image in the reference's format (8 attention layers'
            KV, 24 DeltaNet layers' states, logits); e2e adds the restore  GB/s
@@ -63,7 +67,8 @@ L2_BYTES = 126 << 20
 # large to capture.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
                "batch": 4_452_000_000, "cp": None, "front": 56_784_128,
-               "gdn_front": 213_700_000, "gdn_norm": 153_000_000, "snapshot": None}
+               "gdn_front": 213_700_000, "gdn_norm": 153_000_000, "snapshot": None,
+               "mixers": None}
 
 
 def peaks():
@@ -731,12 +736,123 @@ class SnapshotWorkload(Workload):
                 "image_bytes": self.nbytes}
 
 
+def mixer_step_bytes(pos=SNAP_POS):
+    """Algorithmic bytes of one decode token through the hybrid model's mixers:
+    per attention layer the K and V read (pos + 1 positions), the new k and v
+    written, q and gate read and q written back, the output written; per
+    DeltaNet layer the recurrent state read and written, the conv state read
+    and written with its weights, the qkv row read and written, ab, z read,
+    the bf16 output written."""
+    n_attn = SNAP_LAYERS // SNAP_EVERY
+    n_delta = SNAP_LAYERS - n_attn
+    n = pos + 1
+    attn = 2 * HKV * n * HD * 2 + 2 * HKV * HD * 2 * 2 + 2 * HQ * HD * 2 + HQ * HD * 2 * 2
+    conv = 2 * NK * HKD + NV * HVD
+    delta = (2 * NV * HKD * HVD * 4 + conv * 4 * (4 * 2 + 2) + conv * 4 * 2 + 2 * NV * 4
+             + NV * HVD * 4 + NV * HVD * 2)
+    return n_attn * attn + n_delta * delta
+
+
+class MixersWorkload(Workload):
+    """One decode token through every layer's mixer of a 32-layer hybrid
+    (every 4th layer full attention over SNAP_POS cached positions, the others
+    DeltaNet), routed by an hb_mount; one CUDA graph holds the 32 mixer calls."""
+
+    def __init__(self, device, seed=0x5EED000A):
+        import numpy as np
+        import torch
+        import herbert_b200 as hb
+        self.hb = hb
+        gen = torch.Generator(device=device).manual_seed(seed)
+        kinds = [hb.HB_LAYER_ATTENTION if l % SNAP_EVERY == SNAP_EVERY - 1 else hb.HB_LAYER_DELTA
+                 for l in range(SNAP_LAYERS)]
+        self.kinds = kinds
+        n_delta = kinds.count(hb.HB_LAYER_DELTA)
+        res = SNAP_POS
+        offsets = np.concatenate([[0], np.cumsum([2 * HKV * res * HD if k == hb.HB_LAYER_ATTENTION
+                                                  else 0 for k in kinds])])
+        conv = 2 * NK * HKD + NV * HVD
+        self.geo = hb.Geometry(offsets, HKV, res, n_delta * conv * 4, n_delta * NV * HKD * HVD, 16)
+        self.kv = _randn_bf16((int(offsets[-1]),), gen, device)
+        self.dn_conv = torch.randn(n_delta * conv * 4, generator=gen, device=device)
+        self.dn_rec = 0.05 * torch.randn(n_delta * NV * HKD * HVD, generator=gen, device=device)
+        self.logits = torch.zeros(16, dtype=torch.bfloat16, device=device)
+        half = 32
+        pos = torch.arange(res, dtype=torch.float64, device=device)[:, None]
+        inv = 1e7 ** (-torch.arange(half, dtype=torch.float64, device=device) * 2 / 64)
+        self.cos = torch.cos(pos * inv).to(torch.bfloat16)
+        self.sin = torch.sin(pos * inv).to(torch.bfloat16)
+        desc, keep = hb.mount_desc(
+            self.geo, kinds, kv=self.kv, dn_conv=self.dn_conv, dn_recurrent=self.dn_rec,
+            logits=self.logits, attn=hb.attention_spec(HQ, HQ // HKV, HD, True),
+            attn_scale=1.0 / 16, rotary=64, cos=self.cos, sin=self.sin, norm_eps=1e-6,
+            gemma=True, delta=hb.DeltaShape(nk=NK, nv=NV, hkd=HKD, hvd=HVD), conv_kernel=4,
+            conv_stride=conv * 4, recurrent_stride=NV * HKD * HVD, max_rows=1)
+        self.mount = hb.Mount(desc, keep)
+        qd = HQ * HD
+        self.q = _randn_bf16((1, 2 * qd), gen, device)
+        self.k = _randn_bf16((1, HKV * HD), gen, device)
+        self.v = _randn_bf16((1, HKV * HD), gen, device)
+        self.q_norm = (0.1 * torch.randn(HD, generator=gen, device=device)).to(torch.bfloat16)
+        self.k_norm = (0.1 * torch.randn(HD, generator=gen, device=device)).to(torch.bfloat16)
+        self.attn_out = torch.empty((1, qd), dtype=torch.bfloat16, device=device)
+        self.qkv = torch.randn((1, conv), generator=gen, device=device)
+        self.ab = 2.0 * torch.randn((1, 2 * NV), generator=gen, device=device)
+        self.z = torch.randn((1, NV * HVD), generator=gen, device=device)
+        self.conv_w = (0.25 * torch.randn((conv, 4), generator=gen, device=device)).to(
+            torch.bfloat16)
+        dt = torch.exp(torch.empty(NV, device=device).uniform_(-6.9, -2.3, generator=gen))
+        self.dt_bias = (dt + torch.log(-torch.expm1(-dt))).to(torch.bfloat16)
+        self.a_log = torch.log(torch.empty(NV, device=device).uniform_(1.0, 16.0, generator=gen))
+        self.norm_w = (1.0 + 0.1 * torch.randn(HVD, generator=gen, device=device)).to(
+            torch.bfloat16)
+        self.delta_out = torch.empty((1, NV * HVD), dtype=torch.bfloat16, device=device)
+        self.work = 1  # tokens
+        self.units = "tok/s"
+        self.bytes_per_step = mixer_step_bytes()
+        self.R = 1
+        self.set_bytes = self.bytes_per_step
+        self.launches_per_step = (SNAP_LAYERS // SNAP_EVERY) * 2 + n_delta * 3
+        self.h_in = [self.q.cpu().pin_memory(), self.qkv.cpu().pin_memory()]
+        self.h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory()
+                      for t in (self.attn_out, self.delta_out)]
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(*self.h_out)
+
+    def step(self, i=0):
+        pos = SNAP_POS - 1
+        for layer, kind in enumerate(self.kinds):
+            if kind == self.hb.HB_LAYER_ATTENTION:
+                self.mount.attention(layer, self.q, self.k, self.v, self.q_norm, self.k_norm,
+                                     self.attn_out, rows=1, pos=pos)
+            else:
+                self.mount.delta(layer, self.qkv, self.ab, self.z, self.conv_w, self.dt_bias,
+                                 self.a_log, self.norm_w, self.delta_out, rows=1)
+
+    def e2e_step(self, i=0):
+        for d, h in zip((self.q, self.qkv), self.h_in):
+            d.copy_(h, non_blocking=True)
+        self.step(i)
+        for h, d in zip(self.h_out, (self.attn_out, self.delta_out)):
+            h.copy_(d, non_blocking=True)
+
+    def describe(self):
+        return {"workload": "one decode token through the mixers of a 32-layer hybrid model "
+                "routed by hb_mount (projections excluded)", "positions": SNAP_POS,
+                "attention_layers": SNAP_LAYERS // SNAP_EVERY,
+                "deltanet_layers": SNAP_LAYERS - SNAP_LAYERS // SNAP_EVERY, "q_heads": HQ,
+                "kv_heads": HKV, "head_dim": HD, "value_heads": NV, "head_k_dim": HKD,
+                "bytes_per_token": self.bytes_per_step}
+
+
 METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
           "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s",
           "front": "attn front end HBM GB/s", "gdn_front": "GDN front end HBM GB/s",
-          "gdn_norm": "GDN gated norm HBM GB/s", "snapshot": "snapshot take GB/s"}
+          "gdn_norm": "GDN gated norm HBM GB/s", "snapshot": "snapshot take GB/s",
+          "mixers": "mixer decode tok/s"}
 BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor",
-         "front": "hbm", "gdn_front": "hbm", "gdn_norm": "hbm", "snapshot": "host link"}
+         "front": "hbm", "gdn_front": "hbm", "gdn_norm": "hbm", "snapshot": "host link",
+         "mixers": "hbm"}
 STRONG = ("batch", "cp")  # total work fixed as the GPUs grow
 
 
@@ -759,6 +875,8 @@ def make_workload(cfg, device, rank, world):
         return GdnNormWorkload(device)
     if cfg == "snapshot":
         return SnapshotWorkload(device)
+    if cfg == "mixers":
+        return MixersWorkload(device)
     raise SystemExit(f"unknown config {cfg}")
 
 
@@ -871,6 +989,9 @@ def run_ours(args):
         elif BOUND[cfg] == "tensor":
             achieved = per_launch / kernel_s / 1e12
             peak, unit = bf16_peak, "TFLOP/s"
+        elif cfg == "mixers":
+            achieved = wl.bytes_per_step / kernel_s / 1e9
+            peak, unit = pk["hbm"], "GB/s"
         else:
             achieved = per_launch / kernel_s / 1e9
             peak, unit = pk["hbm"], "GB/s"
@@ -886,7 +1007,8 @@ def run_ours(args):
             "scaling": "strong" if cfg in STRONG else "weak",
             "vs_baseline": None,
             "dtype": ("f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else
-                      "bytes" if cfg == "snapshot" else "bf16"),
+                      "bytes" if cfg == "snapshot" else
+                      "bf16 attention, f32 DeltaNet" if cfg == "mixers" else "bf16"),
             "data": "synthetic",
             "config": dict(wl.describe(), parallelism=(
                 f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
@@ -1004,6 +1126,35 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
         else:
             work = gdn_norm_bytes(rows)
             fn = lambda: oracle.gdn_gated_norm(d.x, d.z, d.norm_weight, 1e-6, impl)  # noqa: E731
+    elif cfg == "mixers":
+        from herbert_b200.inputs import DeltaFrontInputs, FrontInputs
+        pos = SNAP_POS - 1
+        inp = AttentionInputs(1, pos)
+        f = FrontInputs(1, pos, capacity=pos + 1)
+        d = DeltaFrontInputs(1)
+        state = np.zeros((NV, HKD, HVD), np.float32)
+        n_attn = SNAP_LAYERS // SNAP_EVERY
+        work = 1
+        unit, scale = "tok/s", 1.0
+        sample = (f"one token through {n_attn} attention mixers at {SNAP_POS} positions and "
+                  f"{SNAP_LAYERS - n_attn} DeltaNet mixers, all host threads")
+
+        def fn():
+            for _ in range(n_attn):
+                oracle.attn_front(f.q, f.k, f.v, f.q_norm, f.k_norm, f.cos, f.sin, heads=HQ,
+                                  kv_heads=HKV, head_dim=HD, rotary=FRONT_ROTARY, past=pos,
+                                  impl=impl)
+                oracle.attention(inp.q.ravel(), inp.keys.ravel(), inp.values.ravel(), rows=1,
+                                 past=pos, heads=HQ, gqa=HQ // HKV, head_dim=HD, q_row=inp.q_row,
+                                 q_head=HD, out_row=inp.out_row, gate_offset=inp.gate_offset,
+                                 kv_stride=inp.kv_stride, scale=inp.scale, impl=impl,
+                                 use_block=0, threads=threads)
+            for _ in range(SNAP_LAYERS - n_attn):
+                y, _ = oracle.gdn_conv(d.qkv, d.conv_state, d.conv_weight, impl)
+                b, dc = oracle.gdn_gates(d.ab, d.dt_bias, d.a_log)
+                out, _, _ = oracle.gdn_layer(y, state, b, dc, nk=NK, nv=NV, hkd=HKD, hvd=HVD,
+                                             threads=threads)
+                oracle.gdn_gated_norm(out, d.z, d.norm_weight, 1e-6, impl)
     elif cfg == "snapshot":
         sys.path[:0] = [os.path.join(ROOT, "oracle")]
         import snapshot as S
@@ -1041,7 +1192,7 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
     return {"value": round(val, 6), "unit": unit, "cores": threads,
             "kind": "port",
             "sample": sample + f", repeated {reps}x in {el:.1f} s" + (
-                "" if cfg == "snapshot" else
+                "" if cfg in ("snapshot",) else
                 f"; {'AVX512-BF16 transcription' if impl else 'portable emulation'}")}
 
 
@@ -1063,7 +1214,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong" if cfg in STRONG else "weak", "vs_baseline": None,
         "dtype": ("f32" if cfg in ("gdn", "gdn_front", "gdn_norm") else
-                  "bytes" if cfg == "snapshot" else "bf16"), "data": "synthetic",
+                  "bytes" if cfg == "snapshot" else
+                  "bf16 attention, f32 DeltaNet" if cfg == "mixers" else "bf16"),
+        "data": "synthetic",
         "config": {"workload": cfg, "note": "CPU restatement of the reference's x86 AVX-512 BF16 "
                    "kernels (Rust reference not buildable here)"},
         "cpu_baseline": dict(base, value=v),
