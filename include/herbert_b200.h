@@ -510,7 +510,9 @@ typedef struct hb_layer_route {
  * head_dim) and gives layer `layer`'s route; host only, no allocation.
  * HB_DECLINE_GEOMETRY for a plan mismatch. */
 HB_API hb_status hb_mount_route(const hb_mount_desc *desc, int64_t layer, hb_layer_route *route);
-/* hb_mount_route's checks for every layer, then the workspaces and scratch. */
+/* hb_mount_route's checks for every layer, then the workspaces and scratch.
+ * The mount copies the description's records but keeps its device pointers
+ * (state buffers, RoPE tables): those must outlive the mount. */
 HB_API hb_status hb_mount_create(const hb_mount_desc *desc, hb_mount **mount);
 HB_API void hb_mount_destroy(hb_mount *mount);
 /* The status word of the mount's workspaces (as hb_workspace_status). */
