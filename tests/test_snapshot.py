@@ -218,3 +218,42 @@ def test_device_round_trip_through_a_pinned_image():
     for a, b in zip(src, dst):
         assert torch.equal(a, b)
     assert hb.snapshot_info(image) == (40, False)
+
+
+def test_corrupted_images_are_refused_never_crash():
+    # A file from disk may be truncated or damaged anywhere: parsing must end
+    # in a named status.  Fake device pointers: skipped where a GPU could
+    # receive a copy (an image damaged only in its payload passes validation).
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("fake-pointer refusals run on hosts without a GPU only")
+    r = _runner("hybrid", 12)
+    geo = _geo(r)
+    img = _oracle_image(r, 20)
+    head = 4 + 8 * (1 + 9) + 8 * (1 + 9) + 8 * (1 + 8) + 8   # through the kv length field
+    rng = np.random.default_rng(0xF022)
+    allowed = {hb.HB_OK, hb.HB_ERR_ARG, hb.HB_DECLINE_GEOMETRY, hb.HB_ERR_CUDA}
+    for trial in range(400):
+        b = bytearray(img)
+        kind = trial % 4
+        if kind == 0:                                   # truncated anywhere
+            b = b[:int(rng.integers(0, len(b)))]
+        elif kind == 1:                                 # a byte of the header flipped
+            i = int(rng.integers(0, head))
+            b[i] ^= int(rng.integers(1, 256))
+        elif kind == 2:                                 # a hostile 64-bit field
+            i = 4 + 8 * int(rng.integers(0, (head - 4) // 8))
+            hostile = [0, 1, 2**31, 2**40, 2**63, 2**64 - 1]
+            struct.pack_into("<Q", b, i, hostile[int(rng.integers(0, len(hostile)))])
+        else:                                           # the trailing pos field
+            struct.pack_into("<Q", b, len(b) - 8, int(rng.integers(0, 2**63)))
+        data = bytes(b) if b else b"\0"
+        a = np.frombuffer(data, np.uint8)
+        pos, below = ctypes.c_int64(0), ctypes.c_int32(0)
+        st = hb.lib().hb_snapshot_info(ctypes.c_void_p(a.ctypes.data), len(b), ctypes.byref(pos),
+                                       ctypes.byref(below))
+        assert st in (hb.HB_OK, hb.HB_ERR_ARG)
+        st = _restore_status(geo, data[:len(b)] if b else b"", 12)
+        assert st in allowed, (trial, st)
+        if kind in (0, 1, 2) and st == hb.HB_OK:
+            raise AssertionError(f"trial {trial}: a damaged header was accepted")
