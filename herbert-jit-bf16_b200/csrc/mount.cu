@@ -46,8 +46,10 @@ hb_status check_desc(const hb_mount_desc* d) {
   hb_status r = check_state_geometry(d->geometry);
   if (r != HB_OK) return r;
   const hb_state_geometry* g = d->geometry;
-  if (d->max_rows < 1 || d->max_rows > g->kv_reserve)
-    return fail(HB_ERR_ARG, "max_rows must be in 1 .. kv_reserve");
+  // the workspaces are sized over every block size up to max_rows (create)
+  constexpr int64_t kMaxBlockRows = int64_t(1) << 20;
+  if (d->max_rows < 1 || d->max_rows > g->kv_reserve || d->max_rows > kMaxBlockRows)
+    return fail(HB_ERR_ARG, "max_rows must be in 1 .. min(kv_reserve, 2^20)");
   bool any_attn = false, any_delta = false;
   for (int64_t l = 0; l < g->n_layers; l++) {
     if (d->layer_kinds[l] == HB_LAYER_ATTENTION) any_attn = true;

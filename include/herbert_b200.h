@@ -493,7 +493,7 @@ typedef struct hb_mount_desc {
     int64_t conv_kernel;                /* conv kernel length (4)                                */
     int64_t conv_stride;                /* f32 elements of one layer's conv slot (>= conv x ck)   */
     int64_t recurrent_stride;           /* f32 elements of one recurrent slot (>= nv hkd hvd)     */
-    int64_t max_rows;                   /* the largest block a pass feeds (<= kv_reserve)         */
+    int64_t max_rows;                   /* the largest block a pass feeds (<= kv_reserve, 2^20)   */
 } hb_mount_desc;
 /* Where a layer's mixer reads and writes its state. */
 typedef struct hb_layer_route {

@@ -82,6 +82,10 @@ def test_the_lowerings_refusals():
     assert _status(_desc(geo, attn=hb.attention_spec(16, 2, HD, True))[0]) == hb.HB_DECLINE_GEOMETRY
     assert _status(_desc(geo, rotary=48)[0]) == hb.HB_DECLINE_HEAD_DIM
     assert _status(_desc(geo, max_rows=RESERVE + 1)[0]) == hb.HB_ERR_ARG
+    big = hb.Geometry([0, 0, 2 * HKV * (1 << 21) * HD, 2 * HKV * (1 << 21) * HD,
+                       4 * HKV * (1 << 21) * HD], HKV, 1 << 21, 2 * CONV_STRIDE, 2 * REC_STRIDE, 16)
+    assert _status(_desc(big, max_rows=(1 << 20) + 1)[0]) == hb.HB_ERR_ARG
+    assert _status(_desc(big, max_rows=1 << 20)[0]) == hb.HB_OK
     assert _status(_desc(geo, cos=0)[0]) == hb.HB_ERR_ARG
     assert _status(_desc(geo, norm_eps=float("nan"))[0]) == hb.HB_ERR_ARG
     assert _status(_desc(geo, [1, 2, 9, 2])[0]) == hb.HB_ERR_ARG
