@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(256)
 
 size_t cp_acc_bytes(int64_t heads, int64_t rows) {
   const int64_t nqt = (rows + BM - 1) / BM;
-  return size_t(heads * nqt) * BM * (HDIM + 2) * sizeof(float);
+  return size_t(mul_sat(mul_sat(heads, nqt), int64_t(BM) * (HDIM + 2) * sizeof(float)));
 }
 
 cudaError_t launch_attn_cp_finish(const PrefillLaunch& L, cudaStream_t st) {

@@ -85,13 +85,19 @@ bool valid_cp(const hb_cp_spec* cp) {
   return cp && cp->ranks >= 1 && cp->rank >= 0 && cp->rank < cp->ranks && cp->chunk > 0;
 }
 
+// The whole sequence, 2 x ranks x chunk positions, stays below 2^31 (written
+// as a division: the product itself could overflow on a hostile record).
+bool cp_sequence_ok(const hb_cp_spec* cp) {
+  return cp->chunk < (int64_t(1) << 31) / (int64_t(2) * cp->ranks);
+}
+
 int64_t chunk_position(const hb_cp_spec* cp, int32_t rank, int second) {
   return (second ? int64_t(2) * cp->ranks - 1 - rank : int64_t(rank)) * cp->chunk;
 }
 
 // K and V of one shard: [kv_head][2*chunk][head_dim] bf16 each.
 size_t shard_bytes(const hb_attn_spec* s, const hb_cp_spec* cp) {
-  return size_t(s->heads / s->gqa) * size_t(2 * cp->chunk) * size_t(s->head_dim) * 2;
+  return size_t(mul_sat(mul_sat(s->heads / s->gqa, 2 * cp->chunk), s->head_dim * 2));
 }
 
 struct CpPlan {
@@ -116,9 +122,9 @@ hb_status check_cp(const hb_attn_spec* s, const hb_cp_spec* cp, const hb_attn_ca
   if (cp->chunk % kCpTile)
     return fail(HB_DECLINE_GEOMETRY, "chunk %lld is not a multiple of %lld", (long long)cp->chunk,
                 (long long)kCpTile);
-  if (int64_t(2) * cp->ranks * cp->chunk >= (int64_t(1) << 31))
-    return fail(HB_DECLINE_GEOMETRY, "sequence of %lld positions is above 2^31",
-                (long long)(int64_t(2) * cp->ranks * cp->chunk));
+  if (!cp_sequence_ok(cp))
+    return fail(HB_DECLINE_GEOMETRY, "sequence of 2 x %d ranks x %lld positions is above 2^31",
+                int(cp->ranks), (long long)cp->chunk);
   if ((r = check_call(s, c)) != HB_OK) return r;
   if (c->rows != 2 * cp->chunk || c->past != 0)
     return fail(HB_ERR_ARG, "a shard has rows = 2*chunk = %lld and past = 0 (got rows %lld, past %lld)",
@@ -188,17 +194,20 @@ extern "C" {
 
 int32_t hb_cp_hop_source(const hb_cp_spec* cp, int32_t hop) {
   if (!valid_cp(cp) || hop < 0 || hop >= cp->ranks) return -1;
-  return (cp->rank - hop + cp->ranks) % cp->ranks;
+  return int32_t((int64_t(cp->rank) - hop + cp->ranks) % cp->ranks);
 }
 
 int64_t hb_cp_row_position(const hb_cp_spec* cp, int32_t rank, int64_t row) {
-  if (!valid_cp(cp) || rank < 0 || rank >= cp->ranks || row < 0 || row >= 2 * cp->chunk) return -1;
+  if (!valid_cp(cp) || !cp_sequence_ok(cp) || rank < 0 || rank >= cp->ranks || row < 0 ||
+      row >= 2 * cp->chunk)
+    return -1;
   return row < cp->chunk ? chunk_position(cp, rank, 0) + row
                          : chunk_position(cp, rank, 1) + (row - cp->chunk);
 }
 
 size_t hb_attn_prefill_cp_workspace_bytes(const hb_attn_spec* s, const hb_cp_spec* cp) {
-  if (check_spec(s) != HB_OK || !valid_cp(cp) || !prefill_serves(s->head_dim)) return 0;
+  if (check_spec(s) != HB_OK || !valid_cp(cp) || !cp_sequence_ok(cp) || !prefill_serves(s->head_dim))
+    return 0;
   return plan_cp(s, cp).bytes;
 }
 

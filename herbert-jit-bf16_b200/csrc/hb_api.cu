@@ -40,6 +40,14 @@ hb_status cuda_fail(cudaError_t e, const char* what) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 constexpr int64_t kI32Half = 0x3FFFFFFF;  // i32::MAX / 2, the reference's bound
+// Ranges far beyond any model, chosen so that every product the checks and
+// the planner form fits in 64 bits: rows x past < 2^62, positions x head_dim
+// < 2^48.
+constexpr int64_t kMaxRows = int64_t(1) << 24;
+constexpr int64_t kMaxPositions = int64_t(1) << 38;
+inline bool call_in_range(int64_t rows, int64_t past) {
+  return rows >= 0 && rows <= kMaxRows && past >= 0 && past <= kMaxPositions;
+}
 
 // AttentionSpec checks of the tile selector, plus the head_dim domain.
 hb_status check_spec(const hb_attn_spec* s) {
@@ -48,10 +56,11 @@ hb_status check_spec(const hb_attn_spec* s) {
   if (s->heads <= 0 || s->gqa <= 0 || s->head_dim <= 0)
     return fail(HB_DECLINE_EMPTY, "empty shape (heads=%lld gqa=%lld head_dim=%lld)",
                 (long long)s->heads, (long long)s->gqa, (long long)s->head_dim);
-  if (s->heads % s->gqa || s->q_head < s->head_dim || s->heads * s->q_head > s->q_row ||
-      s->heads * s->head_dim > s->out_row || s->heads > kI32Half || s->gqa > kI32Half ||
-      s->head_dim > kI32Half || s->q_row > kI32Half || s->q_head > kI32Half ||
-      s->out_row > kI32Half)
+  // each field bounded before it enters a product (no check overflows)
+  if (s->heads > kI32Half || s->gqa > kI32Half || s->head_dim > kI32Half || s->q_row > kI32Half ||
+      s->q_head > kI32Half || s->out_row > kI32Half || s->gate_offset > kI32Half ||
+      s->heads % s->gqa || s->q_head < s->head_dim || s->heads * s->q_head > s->q_row ||
+      s->heads * s->head_dim > s->out_row)
     return fail(HB_DECLINE_GEOMETRY, "invalid generated attention geometry");
   if (s->gate_offset >= 0 && s->gate_offset + s->heads * s->head_dim > s->q_row)
     return fail(HB_DECLINE_GEOMETRY, "gate_offset %lld + heads*head_dim exceeds q_row %lld",
@@ -74,6 +83,9 @@ hb_status check_call(const hb_attn_spec* s, const hb_attn_call* c) {
   if (!aligned16(c->q) || !aligned16(c->keys) || !aligned16(c->values) || !aligned16(c->output))
     return fail(HB_ERR_ARG, "q/keys/values/output must be 16-byte aligned");
   if (c->past < 0) return fail(HB_ERR_ARG, "negative past");
+  if (!call_in_range(c->rows, c->past) || c->capacity > kMaxPositions)
+    return fail(HB_ERR_ARG, "rows %lld / past %lld / capacity %lld beyond the served range",
+                (long long)c->rows, (long long)c->past, (long long)c->capacity);
   const int64_t n_max = c->past + c->rows;
   if (c->kv_stride % 8) return fail(HB_ERR_ARG, "kv_stride must be a multiple of 8 elements");
   if (c->kv_stride < n_max * s->head_dim)
@@ -98,17 +110,20 @@ DecodePlan plan_decode(const hb_attn_spec* s, int64_t nseq, int64_t rows, int64_
                        int64_t total_positions) {
   DecodePlan p;
   const int64_t hkv = s->heads / s->gqa;
-  p.units = nseq * rows * hkv;
-  p.chunk = decode_chunk(total_positions * hkv, max_n, device_sms());
+  p.units = mul_sat(mul_sat(nseq, rows), hkv);
+  p.chunk = decode_chunk(mul_sat(total_positions, hkv), max_n, device_sms());
   p.nsplit = int((max_n + p.chunk - 1) / p.chunk);
   p.counters_off = kWsHeader;
-  p.partials_off = p.counters_off + align256(size_t(p.units) * sizeof(unsigned));
-  p.bytes = p.partials_off + align256(size_t(p.units) * size_t(p.nsplit) *
-                                      decode_partial_floats(s->gqa, s->head_dim) * sizeof(float));
+  p.partials_off = p.counters_off + align256(size_t(mul_sat(p.units, sizeof(unsigned))));
+  const int64_t partial_bytes =
+      mul_sat(mul_sat(p.units, p.nsplit),
+              mul_sat(int64_t(decode_partial_floats(s->gqa, s->head_dim)), sizeof(float)));
+  p.bytes = p.partials_off + align256(size_t(partial_bytes));
   return p;
 }
 
 // Positions summed over the rows of one sequence: row r sees past + r + 1.
+// (rows and past within call_in_range: the sum fits in 64 bits)
 int64_t row_positions(int64_t past, int64_t rows) { return rows * past + rows * (rows + 1) / 2; }
 
 }  // namespace
@@ -183,7 +198,7 @@ hb_status hb_workspace_status(void* ws, size_t bytes, hb_stream_t stream) {
 }
 
 size_t hb_attn_decode_workspace_bytes(const hb_attn_spec* s, const hb_attn_call* c) {
-  if (check_spec(s) != HB_OK || !c || c->rows <= 0 || c->past < 0) return 0;
+  if (check_spec(s) != HB_OK || !c || c->rows <= 0 || !call_in_range(c->rows, c->past)) return 0;
   return plan_decode(s, 1, c->rows, c->past + c->rows, row_positions(c->past, c->rows)).bytes;
 }
 
@@ -261,7 +276,9 @@ hb_status hb_attn_decode(const hb_attn_spec* s, const hb_attn_call* c, void* ws,
 
 size_t hb_attn_decode_batch_workspace_bytes(const hb_attn_spec* s, int64_t nseq, int64_t max_past,
                                             int64_t sum_past) {
-  if (check_spec(s) != HB_OK || nseq <= 0 || max_past < 0) return 0;
+  if (check_spec(s) != HB_OK || nseq <= 0 || nseq > 65535 || max_past < 0 ||
+      max_past > kMaxPositions || sum_past > kMaxPositions * 65535)
+    return 0;
   const int64_t total = sum_past > 0 ? sum_past + nseq : nseq * (max_past + 1);
   return plan_decode(s, nseq, 1, max_past + 1, total).bytes;
 }
@@ -275,6 +292,8 @@ hb_status hb_attn_decode_batch(const hb_attn_spec* s, const hb_decode_seq* seqs,
   if (!seqs) return fail(HB_ERR_ARG, "sequence table is null");
   if (max_past < 0) return fail(HB_ERR_ARG, "negative max_past");
   if (nseq > 65535) return fail(HB_DECLINE_GEOMETRY, "at most 65535 sequences per call");
+  if (max_past > kMaxPositions || sum_past > kMaxPositions * 65535)
+    return fail(HB_ERR_ARG, "max_past / sum_past beyond the served range");
   const int64_t total = sum_past > 0 ? sum_past + nseq : nseq * (max_past + 1);
   const DecodePlan pl = plan_decode(s, nseq, 1, max_past + 1, total);
   if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
@@ -315,7 +334,7 @@ static bool prefill_on_tensor_cores(const hb_attn_spec* s, const hb_attn_call* c
 }
 
 size_t hb_attn_prefill_workspace_bytes(const hb_attn_spec* s, const hb_attn_call* c) {
-  if (check_spec(s) != HB_OK || !c || c->rows <= 0 || c->past < 0) return 0;
+  if (check_spec(s) != HB_OK || !c || c->rows <= 0 || !call_in_range(c->rows, c->past)) return 0;
   if (prefill_on_tensor_cores(s, c)) return kWsHeader;
   return hb_attn_decode_workspace_bytes(s, c);
 }
@@ -350,14 +369,16 @@ hb_status hb_attn_prefill(const hb_attn_spec* s, const hb_attn_call* c, void* ws
 
 hb_status hb_kv_append(const hb_kv_spec* s, const hb_kv_call* c, hb_stream_t stream) {
   if (!s || !c) return fail(HB_ERR_ARG, "kv spec or call is null");
-  const bool valid = s->heads > 0 && s->head_dim > 0 && s->max_batch > 0 &&
-                     s->capacity >= s->max_batch && s->capacity * s->head_dim <= s->stride &&
-                     s->heads * s->head_dim * 2 <= 0x7FFFFFFF && s->stride <= 0x3FFFFFFF;
+  // bounds before products: no check may overflow on a hostile record
+  const bool valid = s->heads > 0 && s->head_dim > 0 && s->max_batch > 0 && s->stride > 0 &&
+                     s->stride <= 0x3FFFFFFF && s->head_dim <= s->stride &&
+                     s->heads <= 0x7FFFFFFF / (2 * s->head_dim) && s->capacity >= s->max_batch &&
+                     s->capacity <= s->stride / s->head_dim;
   if (!valid) return fail(HB_DECLINE_GEOMETRY, "invalid generated KV reserve geometry");
   if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty KV append");
   if (!c->keys || !c->values || !c->input_keys || !c->input_values)
     return fail(HB_ERR_ARG, "null KV append pointer");
-  if (c->rows > s->max_batch || c->past < 0 || c->past + c->rows > s->capacity)
+  if (c->rows > s->max_batch || c->past < 0 || c->past > s->capacity - c->rows)
     return fail(HB_ERR_ARG, "append of %lld rows at %lld exceeds the reserve (capacity %lld, batch %lld)",
                 (long long)c->rows, (long long)c->past, (long long)s->capacity,
                 (long long)s->max_batch);
@@ -536,7 +557,11 @@ hb_status hb_gdn_gated_norm(const hb_gdn_shape* s, const hb_gdn_norm_call* c, hb
 }
 
 size_t hb_gdn_prefill_workspace_bytes(const hb_gdn_shape* s, int64_t rows) {
-  if (!s || rows <= 0) return kWsHeader;
+  // blocks the chunked kernels never take (rows >= 2^31, heads beyond the
+  // geometry's limit) need only the header
+  if (!s || rows <= 0 || rows >= (int64_t(1) << 31) || s->nk > (int64_t(1) << 16) ||
+      s->nv > (int64_t(1) << 16))
+    return kWsHeader;
   if (!gdn_prefill_serves(*s)) return kWsHeader;
   return gdn_prefill_plan(*s, rows).bytes;
 }

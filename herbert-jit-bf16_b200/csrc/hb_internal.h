@@ -173,6 +173,14 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const v
 // points accept: layer offsets multiples of 2 x kv_heads x kv_reserve.
 hb_status check_state_geometry(const hb_state_geometry* g);
 
+// a x b for non-negative a, b, saturated at 2^62: a size no check accepts,
+// so a hostile request is refused instead of wrapping around.
+inline int64_t mul_sat(int64_t a, int64_t b) {
+  int64_t r;
+  if (__builtin_mul_overflow(a, b, &r) || r > (int64_t(1) << 62)) return int64_t(1) << 62;
+  return r;
+}
+
 // Host-side checks and error reporting shared by the API translation units
 // (hb_api.cu): a failure sets the thread-local message of hb_last_error.
 hb_status fail(hb_status s, const char* fmt, ...);
