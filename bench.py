@@ -1158,20 +1158,22 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
     elif cfg == "snapshot":
         sys.path[:0] = [os.path.join(ROOT, "oracle")]
         import snapshot as S
-        pos = 2048
         hds = [HD if l % SNAP_EVERY == SNAP_EVERY - 1 else 0 for l in range(SNAP_LAYERS)]
         n_delta = hds.count(0)
-        r = S.seeded_runner(HKV, pos, hds, n_delta * (2 * NK * HKD + NV * HVD) * 4,
-                            n_delta * NV * HKD * HVD, -(-SNAP_VOCAB // 16) * 16, pos, 1)
-        slot = S.snapshot_reserve(r, pos)
-        work = len(S.write_to((S.snapshot_take(r, slot), slot)[1]))
+        r = S.Runner(HKV, SNAP_POS, hds, n_delta * (2 * NK * HKD + NV * HVD) * 4,
+                     n_delta * NV * HKD * HVD, -(-SNAP_VOCAB // 16) * 16)
+        r.kv[:] = np.arange(r.kv.size, dtype=np.uint64).astype(np.uint16)  # any bits
+        r.pos = SNAP_POS
+        slot = np.zeros(len(S.image_c(r, SNAP_POS)), np.uint8)  # reserved once
+        work = slot.size
         unit, scale = "GB/s", 1e9
         threads = 1
-        sample = f"the same state at {pos} positions (one thread, numpy)"
+        sample = (f"the same state at {SNAP_POS} positions: the C restatement of take + "
+                  "write_to into a slot reserved once (memcpy per head, one thread, as the "
+                  "reference copies)")
 
         def fn():
-            S.snapshot_take(r, slot)
-            S.write_to(slot)
+            S.image_c(r, SNAP_POS, out=slot)
     else:  # gdn
         T = 64
         d = DeltaInputs(T)

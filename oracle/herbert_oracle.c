@@ -1118,6 +1118,73 @@ int orc_gdn_gated_norm(float *out, const float *z, const uint16_t *w, uint16_t *
     return 0;
 }
 
+/* ------------------------------------------------------------ snapshot */
+
+/* snapshot_reserve(max_positions) + snapshot_take + Instantaneous::write_to
+ * (src/jit/model.rs:270-287, 675-774) in one pass, the KV copied head by
+ * head with memcpy as the reference's take does: the image of a fresh slot
+ * (zeros past pos).  Returns the image's size; out may be NULL to ask it, or
+ * -1 for a state longer than the slot. */
+static size_t put64(uint8_t *o, size_t at, uint64_t v) {
+    if (o) memcpy(o + at, &v, 8);
+    return at + 8;
+}
+long long orc_snapshot_image(const uint16_t *kv, const int64_t *kv_offsets, size_t n_layers,
+                             size_t kv_heads, size_t kv_reserve, size_t max_positions, size_t pos,
+                             const float *conv, size_t conv_len, const float *rec, size_t rec_len,
+                             const uint16_t *logits, size_t logits_len, uint8_t *out) {
+    size_t at = 0, snap = 0;
+    const uint32_t version = 1;
+    if (out) memcpy(out, &version, 4);
+    at = 4;
+    at = put64(out, at, n_layers + 1);
+    for (size_t l = 0; l <= n_layers; l++) at = put64(out, at, (uint64_t)kv_offsets[l]);
+    at = put64(out, at, n_layers + 1);
+    for (size_t l = 0; l <= n_layers; l++) {
+        at = put64(out, at, snap);
+        if (l < n_layers) {
+            const size_t st = (size_t)(kv_offsets[l + 1] - kv_offsets[l]) / (2 * kv_heads);
+            const size_t cap = st ? (kv_reserve < max_positions ? kv_reserve : max_positions) : 0;
+            if (st && pos > cap) return -1;
+            snap += 2 * kv_heads * cap * (st / kv_reserve);
+        }
+    }
+    at = put64(out, at, n_layers);
+    for (size_t l = 0; l < n_layers; l++) {
+        const size_t st = (size_t)(kv_offsets[l + 1] - kv_offsets[l]) / (2 * kv_heads);
+        at = put64(out, at, st ? (kv_reserve < max_positions ? kv_reserve : max_positions) : 0);
+    }
+    at = put64(out, at, snap);
+    size_t dst = at;
+    for (size_t l = 0; l < n_layers; l++) {
+        const size_t st = (size_t)(kv_offsets[l + 1] - kv_offsets[l]) / (2 * kv_heads);
+        if (!st) continue;
+        const size_t hd = st / kv_reserve;
+        const size_t cap = kv_reserve < max_positions ? kv_reserve : max_positions;
+        for (size_t half = 0; half < 2; half++)
+            for (size_t h = 0; h < kv_heads; h++) {
+                if (out) {
+                    const uint16_t *src = kv + kv_offsets[l] + (half * kv_heads + h) * st;
+                    memcpy(out + dst, src, pos * hd * 2);
+                    memset(out + dst + pos * hd * 2, 0, (cap - pos) * hd * 2);
+                }
+                dst += cap * hd * 2;
+            }
+    }
+    at = dst;
+    at = put64(out, at, logits_len);
+    if (out) memcpy(out + at, logits, logits_len * 2);
+    at += logits_len * 2;
+    at = put64(out, at, conv_len);
+    if (out) memcpy(out + at, conv, conv_len * 4);
+    at += conv_len * 4;
+    at = put64(out, at, rec_len);
+    if (out) memcpy(out + at, rec, rec_len * 4);
+    at += rec_len * 4;
+    at = put64(out, at, pos);
+    return (long long)at;
+}
+
 /* ------------------------------------------------------------- inputs */
 
 static inline uint64_t splitmix64(uint64_t *s) {

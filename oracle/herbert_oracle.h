@@ -162,6 +162,14 @@ void orc_gdn_gates(const float *ab, const uint16_t *dt_bias, const float *a_log,
 int orc_gdn_gated_norm(float *out, const float *z, const uint16_t *w, uint16_t *out_bf16,
                        size_t n_rows, size_t dim, float eps, int impl);
 
+/* The snapshot image of the state at `pos` in a slot reserved for
+ * max_positions (src/jit/model.rs:270-287, 675-774); out NULL asks the size;
+ * -1 when pos does not fit the slot. */
+long long orc_snapshot_image(const uint16_t *kv, const int64_t *kv_offsets, size_t n_layers,
+                             size_t kv_heads, size_t kv_reserve, size_t max_positions, size_t pos,
+                             const float *conv, size_t conv_len, const float *rec, size_t rec_len,
+                             const uint16_t *logits, size_t logits_len, uint8_t *out);
+
 void orc_fill_normal_bf16(uint16_t *x, size_t n, uint64_t seed);
 void orc_fill_normal_f64(double *x, size_t n, uint64_t seed);
 

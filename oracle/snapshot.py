@@ -184,3 +184,34 @@ def seeded_runner(kv_heads, kv_reserve, head_dims, conv_len, recurrent_len, logi
     r.logits[:] = rng.integers(0, 1 << 16, logits_len, dtype=np.uint16)
     r.pos = pos
     return r
+
+
+def image_c(r: Runner, max_positions: int, out=None):
+    """The same image as write_to(snapshot_take(reserve(max_positions))), made by
+    the oracle's C restatement (memcpy per head, as the reference copies).
+    With `out` (a uint8 array of the image's size, reserved once as the
+    reference reserves its slot) the image is written there and `out` is
+    returned; else a new bytes object."""
+    import ctypes
+    import oracle as O
+    L = O.lib()
+    fn = L.orc_snapshot_image
+    fn.restype = ctypes.c_longlong
+    u16, f32 = ctypes.POINTER(ctypes.c_uint16), ctypes.POINTER(ctypes.c_float)
+    offs = np.asarray(r.kv_offsets, np.int64)
+    args = [r.kv.ctypes.data_as(u16), offs.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+            ctypes.c_size_t(r.n_layers), ctypes.c_size_t(r.kv_heads),
+            ctypes.c_size_t(r.kv_reserve), ctypes.c_size_t(max_positions), ctypes.c_size_t(r.pos),
+            r.dn_conv.ctypes.data_as(f32), ctypes.c_size_t(r.dn_conv.size),
+            r.dn_recurrent.ctypes.data_as(f32), ctypes.c_size_t(r.dn_recurrent.size),
+            r.logits.ctypes.data_as(u16), ctypes.c_size_t(r.logits.size)]
+    if out is not None:
+        if fn(*args, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))) < 0:
+            raise ValueError("the state holds more positions than the slot")
+        return out
+    n = fn(*args, None)
+    if n < 0:
+        raise ValueError("the state holds more positions than the slot")
+    buf = np.empty(n, np.uint8)
+    fn(*args, buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)))
+    return buf.tobytes()

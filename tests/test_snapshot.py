@@ -64,6 +64,17 @@ def test_oracle_round_trip(name):
     assert np.array_equal(fresh.dn_recurrent, r.dn_recurrent) and fresh.pos == 17
 
 
+@pytest.mark.parametrize("name", sorted(GEOMETRIES))
+@pytest.mark.parametrize("pos,max_positions", [(17, 25), (0, 5), (8, 1000)])
+def test_oracle_c_image_equals_the_restatement(name, pos, max_positions):
+    pos = min(pos, GEOMETRIES[name][1])
+    r = _runner(name, pos)
+    want = _oracle_image(r, max_positions)
+    assert S.image_c(r, max_positions) == want
+    slot = np.full(len(want), 0xCD, np.uint8)   # a reused slot is fully rewritten
+    assert S.image_c(r, max_positions, out=slot).tobytes() == want
+
+
 def test_oracle_refusals():
     r = _runner("hybrid", 30)
     s = S.snapshot_reserve(r, 20)
