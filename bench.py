@@ -58,13 +58,13 @@ CP_S = 131072
 FRONT_ROTARY = 64  # Qwen3.5: partial_rotary_factor 0.25 of head_dim 256
 L2_BYTES = 126 << 20
 
-# dram bytes (read + write) of one launch of the dominant kernel, from the
-# committed ncu summaries under profiles/: attn_prefill_s4096.md,
-# attn_decode_n2048.md, attn_decode_batch64.md (scaled from the n = 2048
-# capture by the bytes processed), gdn_prefill_decode_t4096.md (prep + scan,
-# one chunked prefill), gdn_front_s4096.md and gdn_gated_norm_s4096.md (DRAM
-# byte rate x duration of one launch); cp: the 131072-token launch is too
-# large to capture.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# each configuration's dominant kernel, as an ncu capture of this script's
+# own command measured them.  ncu runs outside the timed run (a capture
+# replays kernels and is never timed), so the figures are constants here;
+# batch is scaled from the n = 2048 decode capture by the bytes processed,
+# gdn covers the chunked prefill's kernels of one prefill, and None marks a
+# configuration whose launch was not captured.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
                "batch": 4_452_000_000, "cp": None, "front": 56_784_128,
                "gdn_front": 213_700_000, "gdn_norm": 153_000_000, "snapshot": None,

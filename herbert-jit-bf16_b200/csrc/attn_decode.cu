@@ -43,9 +43,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
-#include <mutex>
-
 #include "hb_common.cuh"
+#include "hb_host.h"
 #include "hb_internal.h"
 
 namespace hb {
@@ -54,25 +53,15 @@ namespace hb {
 // that may not allocate device memory still get split-KV decoding.  Every
 // device that loads the library holds these bytes until the process exits.
 // In host code the name is only a host-side stand-in for the symbol; the
-// device address comes from cudaGetSymbolAddress (noalloc_scratch below).
+// device address comes from cudaGetSymbolAddress (noalloc_scratch below),
+// looked up once per device and context: a context that ends (for instance
+// by cudaDeviceReset) takes its module and the array's mapping with it, and
+// the next call in a new context looks the address up again.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[HB_NOALLOC_SCRATCH_BYTES];
 
 cudaError_t noalloc_scratch(void** ptr) {
-  static std::mutex mu;
-  static void* addr[64] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);  // with `dev` current
-    if (e != cudaSuccess) return e;
-    addr[dev] = p;
-  }
-  *ptr = addr[dev];
-  return cudaSuccess;
+  static SymbolCache cache;
+  return symbol_address(cache, reinterpret_cast<const void*>(&g_noalloc_scratch), ptr);
 }
 
 namespace {

@@ -30,6 +30,7 @@
 #include <mutex>
 #include <vector>
 
+#include "hb_host.h"
 #include "hb_internal.h"
 
 namespace hb {
@@ -46,6 +47,8 @@ struct NcclApi {
   ncclResult_t (*group_start)();
   ncclResult_t (*group_end)();
   const char* (*error_string)(ncclResult_t);
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*);
+  ncclResult_t (*comm_abort)(ncclComm_t);
 };
 
 // The NCCL already loaded in the process (torch's, for instance) if there is
@@ -72,6 +75,9 @@ const NcclApi* nccl_api() {
     api.group_start = reinterpret_cast<decltype(api.group_start)>(sym("ncclGroupStart"));
     api.group_end = reinterpret_cast<decltype(api.group_end)>(sym("ncclGroupEnd"));
     api.error_string = reinterpret_cast<decltype(api.error_string)>(sym("ncclGetErrorString"));
+    api.comm_get_async_error =
+        reinterpret_cast<decltype(api.comm_get_async_error)>(sym("ncclCommGetAsyncError"));
+    api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(sym("ncclCommAbort"));
     ok = all;
   });
   return ok ? &api : nullptr;
@@ -272,6 +278,43 @@ hb_status hb_cp_comm_destroy(void* comm) {
   ncclResult_t r = n->comm_destroy(static_cast<ncclComm_t>(comm));
   if (r != ncclSuccess) return nccl_fail(n, r, "ncclCommDestroy");
   return HB_OK;
+}
+
+hb_status hb_cp_wait(void* comm, hb_stream_t stream, double timeout_s) {
+  if (!(timeout_s >= 0.0)) return fail(HB_ERR_ARG, "timeout is negative or NaN");
+  const NcclApi* n = comm ? nccl_api() : nullptr;
+  if (comm && !n) return fail(HB_ERR_NCCL, "libnccl.so.2 could not be loaded");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ncclComm_t nc = static_cast<ncclComm_t>(comm);
+  ncclResult_t async = ncclSuccess;
+  cudaError_t qerr = cudaSuccess;
+  const WaitResult w = wait_with_deadline(
+      [&] {
+        qerr = cudaStreamQuery(st);
+        return qerr == cudaSuccess ? 0 : qerr == cudaErrorNotReady ? 1 : 2;
+      },
+      [&] {
+        if (!nc) return false;
+        ncclResult_t r = ncclSuccess;
+        if (n->comm_get_async_error(nc, &r) != ncclSuccess) r = ncclInternalError;
+        if (r != ncclSuccess && r != ncclInProgress) async = r;
+        return async != ncclSuccess;
+      },
+      monotonic_seconds, sleep_poll_interval, timeout_s);
+  if (w == WaitResult::kDone) return HB_OK;
+  // abort, so that the peers' transfers that wait on this rank end too
+  if (nc) n->comm_abort(nc);
+  switch (w) {
+    case WaitResult::kTimeout:
+      return fail(HB_ERR_TIMEOUT, "the ring did not complete within %.3f s; communicator aborted",
+                  timeout_s);
+    case WaitResult::kCommError:
+      return fail(HB_ERR_NCCL, "the communicator reported %s; communicator aborted",
+                  n->error_string(async));
+    default:
+      return fail(HB_ERR_CUDA, "stream query failed: %s%s", cudaGetErrorString(qerr),
+                  nc ? "; communicator aborted" : "");
+  }
 }
 
 hb_status hb_attn_prefill_cp(const hb_attn_spec* s, const hb_cp_spec* cp, const hb_attn_call* c,

@@ -41,6 +41,7 @@ struct GdnParams {
   int nk, nv, hvd;
   int l2;
   float eps, scale;
+  int* status;  // device status word: the caller's workspace or the per-device word
 };
 
 // Sequential L2 of one head held in shared memory: sum of squares left to
@@ -60,10 +61,6 @@ HB_DEV float l2_inverse(const float* x, float eps) {
   sum = __fadd_rn(sum, eps);
   return __fdiv_rn(1.0f, __fsqrt_rn(sum));
 }
-
-// Set when a TMA wait of the decode kernel ran out (the call's outputs are
-// then not written); there is no workspace to carry a per-call status.
-__device__ int g_gdn_decode_timeout = 0;
 
 template <int HKD>
 __global__ void __launch_bounds__(32)
@@ -129,7 +126,8 @@ __global__ void __launch_bounds__(32)
         sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
       }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar, 0))) {
-        if (lane == 0) atomicExch(&g_gdn_decode_timeout, 1);
+        // the call's outputs are not written; the status word tells the caller
+        if (lane == 0) record_status(p.status, kStatusTimeout);
         mbar_wait(&bar, 0);  // a second bounded wait for the copy in flight
         return;
       }
@@ -203,6 +201,7 @@ cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st) {
   p.l2 = L.call.l2;
   p.eps = L.call.eps;
   p.scale = L.scale;
+  p.status = L.status;
   // the state as [nv*hkd rows][hvd columns] f32, tiles [hkd rows][32 columns]
   CUtensorMap tm;
   if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.call.state,

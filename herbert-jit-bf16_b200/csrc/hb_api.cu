@@ -8,6 +8,7 @@
 //  - SDPA shape:         SdpaShape::check (src/jit/ir.rs:140-160), Decline (:177-230)
 //  - KV geometry:        KvSpec::validate (src/jit/execution/abi.rs:75-103)
 //  - DeltaNet geometry:  Shape::check (src/jit/execution/abi.rs:283-306)
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -16,6 +17,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "hb_host.h"
 #include "hb_internal.h"
 
 namespace hb {
@@ -136,6 +138,59 @@ hb_status check_ws(void* ws, size_t have, size_t need) {
   return HB_OK;
 }
 
+// Status word of the entry points that take no workspace (hb_gdn_decode,
+// hb_attn_decode_noalloc): zero when the module loads, raised by a kernel
+// whose bounded wait ran out, read and cleared by hb_device_status.
+static __device__ int g_device_status;
+
+namespace {
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
+// A driver function reached through the runtime's entry point, so that the
+// library keeps no link-time libcuda dependency (it loads on machines
+// without a driver, where only the host-side checks run).
+template <class Fn>
+Fn driver_fn(const char* name) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(ptr);
+}
+
+// Unique id of the current context (0 on success), non-zero without one.
+int current_context_id(unsigned long long* id) {
+  static const CtxGetCurrentFn get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  if (!get_current || !get_id) return 1;
+  CUcontext c = nullptr;
+  if (get_current(&c) != CUDA_SUCCESS || !c) return 1;
+  return get_id(c, id) == CUDA_SUCCESS ? 0 : 1;
+}
+
+}  // namespace
+
+cudaError_t symbol_address(SymbolCache& cache, const void* symbol, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const int r = cache.get(dev, current_context_id,
+                          [symbol](void** p) { return int(cudaGetSymbolAddress(p, symbol)); }, out);
+  if (r < 0) return cudaErrorInvalidDevice;
+  return cudaError_t(r);
+}
+
+cudaError_t device_status_word(int** out) {
+  static SymbolCache cache;
+  void* p = nullptr;
+  cudaError_t e = symbol_address(cache, reinterpret_cast<const void*>(&g_device_status), &p);
+  *out = static_cast<int*>(p);
+  return e;
+}
+
 int device_sms() {
   static int cache[64] = {0};
   int dev = 0;
@@ -183,18 +238,32 @@ hb_status hb_workspace_init(void* ws, size_t bytes, hb_stream_t stream) {
   return HB_OK;
 }
 
-hb_status hb_workspace_status(void* ws, size_t bytes, hb_stream_t stream) {
-  if (!ws || bytes < kWsHeader) return fail(HB_ERR_WORKSPACE, "workspace null or under 256 bytes");
+// Reads the device status word at `word` on `stream`, clears it when set,
+// and turns its code into a status.
+static hb_status read_status_word(int* word, hb_stream_t stream, const char* what) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int code = 0;
-  cudaError_t e = cudaMemcpyAsync(&code, ws, sizeof code, cudaMemcpyDeviceToHost, st);
+  cudaError_t e = cudaMemcpyAsync(&code, word, sizeof code, cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) return cuda_fail(e, "hb_workspace_status");
+  if (e != cudaSuccess) return cuda_fail(e, what);
   if (code == 0) return HB_OK;
-  e = cudaMemsetAsync(ws, 0, sizeof code, st);
-  if (e != cudaSuccess) return cuda_fail(e, "hb_workspace_status");
+  e = cudaMemsetAsync(word, 0, sizeof code, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, what);
   if (code == kStatusTimeout) return fail(HB_ERR_TIMEOUT, "a bounded device wait ran out");
   return fail(HB_ERR_ARG, "a kernel met a misaligned or invalid table entry (code %d)", code);
+}
+
+hb_status hb_workspace_status(void* ws, size_t bytes, hb_stream_t stream) {
+  if (!ws || bytes < kWsHeader) return fail(HB_ERR_WORKSPACE, "workspace null or under 256 bytes");
+  return read_status_word(static_cast<int*>(ws), stream, "hb_workspace_status");
+}
+
+hb_status hb_device_status(hb_stream_t stream) {
+  int* word = nullptr;
+  cudaError_t e = device_status_word(&word);
+  if (e != cudaSuccess) return cuda_fail(e, "hb_device_status set-up");
+  return read_status_word(word, stream, "hb_device_status");
 }
 
 size_t hb_attn_decode_workspace_bytes(const hb_attn_spec* s, const hb_attn_call* c) {
@@ -205,7 +274,7 @@ size_t hb_attn_decode_workspace_bytes(const hb_attn_spec* s, const hb_attn_call*
 // Launches the decode kernel of one sequence on a validated call with the
 // workspace `ws` laid out by plan `pl`.
 static hb_status decode_launch(const hb_attn_spec* s, const hb_attn_call* c, const DecodePlan& pl,
-                               void* ws, hb_stream_t stream) {
+                               void* ws, hb_stream_t stream, int* status = nullptr) {
   DecodeLaunch L;
   L.seqs = nullptr;
   L.one.q = c->q;
@@ -227,7 +296,7 @@ static hb_status decode_launch(const hb_attn_spec* s, const hb_attn_call* c, con
   L.chunk = pl.chunk;
   L.nsplit = pl.nsplit;
   char* base = static_cast<char*>(ws);
-  L.status = reinterpret_cast<int*>(base);
+  L.status = status ? status : reinterpret_cast<int*>(base);
   L.counters = reinterpret_cast<unsigned*>(base + pl.counters_off);
   L.partials = reinterpret_cast<float*>(base + pl.partials_off);
   cudaError_t e = launch_attn_decode(L, reinterpret_cast<cudaStream_t>(stream));
@@ -246,10 +315,11 @@ static hb_status decode_common(const hb_attn_spec* s, const hb_attn_call* c, voi
 }
 
 // The allocation-free variant: the same kernel and plan, with the static
-// scratch of attn_decode.cu as its workspace.  Its status word and split
-// counters must start at zero, and the array keeps whatever the previous
-// call left, so they are cleared (one cudaMemsetAsync, no allocation) on
-// `stream` before the launch.
+// scratch of attn_decode.cu as its workspace.  Its split counters must start
+// at zero, and the array keeps whatever the previous call left, so they are
+// cleared (one cudaMemsetAsync, no allocation) on `stream` before the
+// launch.  A bounded wait that runs out is recorded in the per-device status
+// word (hb_device_status), which no later call clears.
 hb_status hb_attn_decode_noalloc(const hb_attn_spec* s, const hb_attn_call* c,
                                  hb_stream_t stream) {
   hb_status r = check_spec(s);
@@ -264,9 +334,16 @@ hb_status hb_attn_decode_noalloc(const hb_attn_spec* s, const hb_attn_call* c,
   void* scratch = nullptr;
   cudaError_t e = noalloc_scratch(&scratch);
   if (e != cudaSuccess) return cuda_fail(e, "hb_attn_decode_noalloc scratch set-up");
-  e = cudaMemsetAsync(scratch, 0, pl.partials_off, reinterpret_cast<cudaStream_t>(stream));
+  int* status = nullptr;
+  if ((e = device_status_word(&status)) != cudaSuccess)
+    return cuda_fail(e, "hb_attn_decode_noalloc status set-up");
+  // the split counters start at zero; the status word is the per-device
+  // one, kept until hb_device_status reads it
+  char* base = static_cast<char*>(scratch);
+  e = cudaMemsetAsync(base + pl.counters_off, 0, pl.partials_off - pl.counters_off,
+                      reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hb_attn_decode_noalloc scratch clear");
-  return decode_launch(s, c, pl, scratch, stream);
+  return decode_launch(s, c, pl, scratch, stream, status);
 }
 
 hb_status hb_attn_decode(const hb_attn_spec* s, const hb_attn_call* c, void* ws, size_t ws_bytes,
@@ -466,16 +543,26 @@ static hb_status check_gdn(const hb_gdn_shape* s, const hb_gdn_call* c) {
   return HB_OK;
 }
 
-hb_status hb_gdn_decode(const hb_gdn_shape* s, const hb_gdn_call* c, hb_stream_t stream) {
-  hb_status r = check_gdn(s, c);
-  if (r != HB_OK) return r;
+// The recurrence on a validated call; its status word is `status`.
+static hb_status gdn_decode_launch(const hb_gdn_shape* s, const hb_gdn_call* c, int* status,
+                                   hb_stream_t stream) {
   GdnLaunch L;
   L.shape = *s;
   L.call = *c;
   L.scale = 1.0f / std::sqrt(float(s->hkd));
+  L.status = status;
   cudaError_t e = launch_gdn_decode(L, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gdn_decode launch");
   return HB_OK;
+}
+
+hb_status hb_gdn_decode(const hb_gdn_shape* s, const hb_gdn_call* c, hb_stream_t stream) {
+  hb_status r = check_gdn(s, c);
+  if (r != HB_OK) return r;
+  int* status = nullptr;
+  cudaError_t e = device_status_word(&status);
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_decode status set-up");
+  return gdn_decode_launch(s, c, status, stream);
 }
 
 // Positions from which the chunked tensor-core kernels take a block; shorter
@@ -570,13 +657,17 @@ hb_status hb_gdn_prefill(const hb_gdn_shape* s, const hb_gdn_call* c, void* ws, 
                          hb_stream_t stream) {
   hb_status r = check_gdn(s, c);
   if (r != HB_OK) return r;
-  if (!gdn_chunked(s, c)) return hb_gdn_decode(s, c, stream);
+  if (!gdn_chunked(s, c)) {  // the recurrence in order, its status in the workspace
+    if ((r = check_ws(ws, ws_bytes, kWsHeader)) != HB_OK) return r;
+    return gdn_decode_launch(s, c, static_cast<int*>(ws), stream);
+  }
   const GdnPrefillPlan pl = gdn_prefill_plan(*s, c->rows);
   if ((r = check_ws(ws, ws_bytes, pl.bytes)) != HB_OK) return r;
   GdnLaunch L;
   L.shape = *s;
   L.call = *c;
   L.scale = 1.0f / std::sqrt(float(s->hkd));
+  L.status = static_cast<int*>(ws);
   cudaError_t e = launch_gdn_prefill(L, pl, ws, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gdn_prefill launch");
   return HB_OK;

@@ -222,12 +222,13 @@ HB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete; false after kSpinCycles.
-HB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Waits for phase `parity` of `bar` to complete; false after `limit` SM
+// cycles (kSpinCycles, about a second, in every product kernel).
+HB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, long long limit = kSpinCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kSpinCycles) return false;
+    if (clock64() - t0 > limit) return false;
   }
   return true;
 }

@@ -51,7 +51,7 @@ struct DecodeLaunch {
 };
 bool decode_serves(int64_t head_dim, int64_t gqa);
 // Device address of the static scratch of hb_attn_decode_noalloc on the
-// current device (looked up on the first call per device).
+// current device (looked up on the first call per device and context).
 cudaError_t noalloc_scratch(void** ptr);
 int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms);
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
@@ -142,6 +142,7 @@ struct GdnLaunch {
   hb_gdn_shape shape;
   hb_gdn_call call;
   float scale;  // 1/sqrt(hkd), f32 as the reference computes it
+  int* status;  // device status word (workspace header or device_status_word)
 };
 bool gdn_decode_serves(const hb_gdn_shape& s);
 cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st);
@@ -158,6 +159,17 @@ cudaError_t launch_gdn_prefill(const GdnLaunch& L, const GdnPrefillPlan& pl, voi
 
 // Number of SMs of the current device (cached per device).
 int device_sms();
+
+// Device address, in the current context, of a file-scope __device__
+// variable (`symbol` is the variable's address in host code, i.e. its
+// host-side stand-in), cached per device and context (hb_host.h).
+class SymbolCache;
+cudaError_t symbol_address(SymbolCache& cache, const void* symbol, void** out);
+
+// Device address of the status word of the entry points that take no
+// workspace (hb_gdn_decode, hb_attn_decode_noalloc) on the current device;
+// hb_device_status reads and clears it.
+cudaError_t device_status_word(int** out);
 
 // TMA tensor maps (hb_tma.cu): a rank-`rank` tiled map, element strides in
 // bytes for dimensions 1.., no interleave, zero fill out of bounds; and the

@@ -16,6 +16,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <vector>
 
 #include "hb_internal.h"
@@ -34,6 +35,14 @@ struct hb_mount {
   float* beta = nullptr;
   float* decay = nullptr;
   float* rec_out = nullptr;
+  // Set by the first failure after a call entered execution (a node
+  // launched, so state may be half updated) or by a device-side status;
+  // every later mixer call is refused with it until hb_mount_reset, as a
+  // failed call poisons the reference's execution session until its owner
+  // resets or restores the model (src/jit/execution/runtime.rs:144-151,
+  // 310-327; src/jit/execution/program.rs:289).
+  hb_status poison = HB_OK;
+  char poison_msg[256] = "";
 };
 
 namespace hb {
@@ -126,6 +135,30 @@ void release(hb_mount* m) {
   delete m;
 }
 
+// Records the first failure of a call that entered execution and returns it.
+hb_status poison(hb_mount* m, hb_status r) {
+  if (r != HB_OK && m->poison == HB_OK) {
+    m->poison = r;
+    snprintf(m->poison_msg, sizeof m->poison_msg, "%s", hb_last_error());
+  }
+  return r;
+}
+
+hb_status refuse_if_poisoned(const hb_mount* m) {
+  if (m->poison == HB_OK) return HB_OK;
+  return fail(m->poison, "the mount needs hb_mount_reset after a failed call (%s: %s)",
+              hb_status_name(m->poison), m->poison_msg);
+}
+
+// A node's status once an earlier node of the same call has launched, or
+// when the node itself failed past its checks (a launch or device error):
+// either way the state may be half updated.
+hb_status after_entry(hb_mount* m, hb_status r, bool entered) {
+  if (r == HB_OK) return r;
+  if (entered || r == HB_ERR_CUDA || r == HB_ERR_TIMEOUT || r == HB_ERR_NCCL) return poison(m, r);
+  return r;
+}
+
 hb_status layer_of(hb_mount* m, int64_t layer, int32_t kind, hb_layer_route* r) {
   if (!m) return fail(HB_ERR_ARG, "mount is null");
   if (layer < 0 || layer >= m->geo.n_layers) return fail(HB_ERR_ARG, "layer %lld out of range", static_cast<long long>(layer));
@@ -214,9 +247,26 @@ void hb_mount_destroy(hb_mount* m) {
 hb_status hb_mount_status(hb_mount* m, hb_stream_t stream) {
   if (!m) return fail(HB_ERR_ARG, "mount is null");
   hb_status r = HB_OK;
-  if (m->attn_ws && (r = hb_workspace_status(m->attn_ws, m->attn_ws_bytes, stream)) != HB_OK) return r;
-  if (m->gdn_ws && (r = hb_workspace_status(m->gdn_ws, m->gdn_ws_bytes, stream)) != HB_OK) return r;
-  if (m->front_ws && (r = hb_workspace_status(m->front_ws, kWsHeader, stream)) != HB_OK) return r;
+  if (m->attn_ws && (r = hb_workspace_status(m->attn_ws, m->attn_ws_bytes, stream)) != HB_OK)
+    return poison(m, r);
+  if (m->gdn_ws && (r = hb_workspace_status(m->gdn_ws, m->gdn_ws_bytes, stream)) != HB_OK)
+    return poison(m, r);
+  if (m->front_ws && (r = hb_workspace_status(m->front_ws, kWsHeader, stream)) != HB_OK)
+    return poison(m, r);
+  return refuse_if_poisoned(m);
+}
+
+int hb_mount_needs_reset(const hb_mount* m) { return m && m->poison != HB_OK; }
+
+hb_status hb_mount_reset(hb_mount* m, hb_stream_t stream) {
+  if (!m) return fail(HB_ERR_ARG, "mount is null");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  for (void* ws : {m->attn_ws, m->gdn_ws, m->front_ws})
+    if (ws && e == cudaSuccess) e = cudaMemsetAsync(ws, 0, kWsHeader, st);
+  if (e != cudaSuccess) return cuda_fail(e, "hb_mount_reset");
+  m->poison = HB_OK;
+  m->poison_msg[0] = 0;
   return HB_OK;
 }
 
@@ -228,6 +278,7 @@ hb_status hb_mount_attention(hb_mount* m, int64_t layer, const hb_mount_attentio
   const int64_t res = m->geo.kv_reserve;
   if (c->rows < 1 || c->rows > m->desc.max_rows) return fail(HB_ERR_ARG, "rows outside 1 .. max_rows");
   if (c->pos < 0 || c->pos + c->rows > res) return fail(HB_ERR_ARG, "positions beyond the cache");
+  if ((r = refuse_if_poisoned(m)) != HB_OK) return r;
   const hb_attn_spec& spec = m->desc.attn;
   const int64_t hd = spec.head_dim;
   // head-norm-rope of q and k, kv-append (lowering.rs:549-592)
@@ -253,7 +304,7 @@ hb_status hb_mount_attention(hb_mount* m, int64_t layer, const hb_mount_attentio
   fc.values = rt.values;
   fc.rows = c->rows;
   fc.past = c->pos;
-  if ((r = hb_attn_front(&spec, &kv, &front, &fc, stream)) != HB_OK) return r;
+  if ((r = hb_attn_front(&spec, &kv, &front, &fc, stream)) != HB_OK) return after_entry(m, r, false);
   // attention + output gate (lowering.rs:600-666), by regime
   hb_attn_call ac{};
   ac.q = c->q;
@@ -265,8 +316,9 @@ hb_status hb_mount_attention(hb_mount* m, int64_t layer, const hb_mount_attentio
   ac.kv_stride = rt.kv_stride;
   ac.capacity = res;
   ac.scale = m->desc.attn_scale;
-  if (c->rows == 1) return hb_attn_decode(&spec, &ac, m->attn_ws, m->attn_ws_bytes, stream);
-  return hb_attn_prefill(&spec, &ac, m->attn_ws, m->attn_ws_bytes, stream);
+  if (c->rows == 1)
+    return after_entry(m, hb_attn_decode(&spec, &ac, m->attn_ws, m->attn_ws_bytes, stream), true);
+  return after_entry(m, hb_attn_prefill(&spec, &ac, m->attn_ws, m->attn_ws_bytes, stream), true);
 }
 
 hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* c, hb_stream_t stream) {
@@ -275,6 +327,7 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   if (r != HB_OK) return r;
   if (!c) return fail(HB_ERR_ARG, "DeltaNet call is null");
   if (c->rows < 1 || c->rows > m->desc.max_rows) return fail(HB_ERR_ARG, "rows outside 1 .. max_rows");
+  if ((r = refuse_if_poisoned(m)) != HB_OK) return r;
   const hb_gdn_shape& shape = m->desc.delta;
   // delta-causal-convolution + the gates of delta-l2-gates (lowering.rs:904-961)
   hb_gdn_front_call fc{};
@@ -288,7 +341,8 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   fc.decay = m->decay;
   fc.rows = c->rows;
   fc.ck = m->desc.conv_kernel;
-  if ((r = hb_gdn_front(&shape, &fc, m->front_ws, kWsHeader, stream)) != HB_OK) return r;
+  if ((r = hb_gdn_front(&shape, &fc, m->front_ws, kWsHeader, stream)) != HB_OK)
+    return after_entry(m, r, false);
   // the L2 of delta-l2-gates + delta-causal-recurrence (lowering.rs:935-986)
   hb_gdn_call gc{};
   gc.state = rt.recurrent_state;
@@ -299,7 +353,8 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   gc.rows = c->rows;
   gc.l2 = 1;
   gc.eps = kDeltaL2Eps;
-  if ((r = hb_gdn_prefill(&shape, &gc, m->gdn_ws, m->gdn_ws_bytes, stream)) != HB_OK) return r;
+  if ((r = hb_gdn_prefill(&shape, &gc, m->gdn_ws, m->gdn_ws_bytes, stream)) != HB_OK)
+    return after_entry(m, r, true);
   // delta-gated-norm (lowering.rs:987-1010)
   hb_gdn_norm_call nc{};
   nc.x = m->rec_out;
@@ -309,5 +364,5 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   nc.out_f32 = c->out_f32;
   nc.rows = c->rows;
   nc.eps = m->desc.norm_eps;
-  return hb_gdn_gated_norm(&shape, &nc, stream);
+  return after_entry(m, hb_gdn_gated_norm(&shape, &nc, stream), true);
 }

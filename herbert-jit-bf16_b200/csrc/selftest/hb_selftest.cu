@@ -4,11 +4,16 @@
 // result compared with the exact per-element steps (f32_to_bf16_cvtne and
 // gate_bf16).  Random parity inputs cannot reach the rare cases the fast
 // path must send to the exact steps; this covers the whole input domain.
+//
+// Test-only: built into libherbert_b200_selftest.so (hb_selftest.h), never
+// into the product library.
 #include <cuda_runtime.h>
 
-#include "hb_common.cuh"
-#include "hb_epilogue.cuh"
-#include "hb_internal.h"
+#include <cstdio>
+
+#include "../hb_common.cuh"
+#include "../hb_epilogue.cuh"
+#include "hb_selftest.h"
 
 namespace hb {
 namespace {
@@ -94,9 +99,19 @@ __global__ void __launch_bounds__(256) selftest_plain_kernel() {
 }  // namespace
 }  // namespace hb
 
-extern "C" hb_status hb_selftest_prefill_epilogue(uint64_t* out, hb_stream_t stream) {
+namespace {
+thread_local char g_msg[256] = "";
+int selftest_fail(int code, const char* what, cudaError_t e) {
+  snprintf(g_msg, sizeof g_msg, "%s: %s", what, e == cudaSuccess ? "" : cudaGetErrorString(e));
+  return code;
+}
+}  // namespace
+
+extern "C" const char* hbt_last_error(void) { return g_msg; }
+
+extern "C" int hbt_prefill_epilogue(uint64_t* out, hb_stream_t stream) {
   using namespace hb;
-  if (!out) return fail(HB_ERR_ARG, "hb_selftest_prefill_epilogue: out is null");
+  if (!out) return selftest_fail(HB_ERR_ARG, "hbt_prefill_epilogue: out is null", cudaSuccess);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   void* slots = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&slots, g_selftest);
@@ -107,13 +122,13 @@ extern "C" hb_status hb_selftest_prefill_epilogue(uint64_t* out, hb_stream_t str
     e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  if (e != cudaSuccess) return cuda_fail(e, "hb_selftest_prefill_epilogue set-up");
+  if (e != cudaSuccess) return selftest_fail(HB_ERR_CUDA, "hbt_prefill_epilogue set-up", e);
   selftest_gate_kernel<<<unsigned(sms * 4), 256, 0, st>>>();
   selftest_plain_kernel<<<unsigned(sms * 4), 256, 0, st>>>();
   e = cudaGetLastError();
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(out, slots, sizeof(unsigned long long) * 8, cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  if (e != cudaSuccess) return cuda_fail(e, "hb_selftest_prefill_epilogue");
+  if (e != cudaSuccess) return selftest_fail(HB_ERR_CUDA, "hbt_prefill_epilogue", e);
   return HB_OK;
 }

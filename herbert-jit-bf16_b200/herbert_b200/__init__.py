@@ -168,11 +168,11 @@ _SIGNATURES = {
     "hb_status_name": (ctypes.c_char_p, [ctypes.c_int]),
     "hb_workspace_init": (ctypes.c_int, [c_void_p, c_size_t, c_void_p]),
     "hb_workspace_status": (ctypes.c_int, [c_void_p, c_size_t, c_void_p]),
+    "hb_device_status": (ctypes.c_int, [c_void_p]),
     "hb_attn_decode_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionCall)]),
     "hb_attn_decode": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
                                       c_void_p]),
     "hb_attn_decode_noalloc": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p]),
-    "hb_selftest_prefill_epilogue": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), c_void_p]),
     "hb_attn_decode_batch_workspace_bytes": (c_size_t, [_P(AttentionSpec), c_int64, c_int64,
                                                         c_int64]),
     "hb_attn_decode_batch": (ctypes.c_int, [_P(AttentionSpec), c_void_p, c_int64, c_int64,
@@ -200,6 +200,8 @@ _SIGNATURES = {
     "hb_mount_create": (ctypes.c_int, [_P(MountDesc), _P(c_void_p)]),
     "hb_mount_destroy": (None, [c_void_p]),
     "hb_mount_status": (ctypes.c_int, [c_void_p, c_void_p]),
+    "hb_mount_needs_reset": (ctypes.c_int, [c_void_p]),
+    "hb_mount_reset": (ctypes.c_int, [c_void_p, c_void_p]),
     "hb_mount_attention": (ctypes.c_int, [c_void_p, c_int64, _P(MountAttentionCall), c_void_p]),
     "hb_mount_delta": (ctypes.c_int, [c_void_p, c_int64, _P(MountDeltaCall), c_void_p]),
     "hb_cp_hop_source": (c_int32, [_P(CpSpec), c_int32]),
@@ -213,6 +215,7 @@ _SIGNATURES = {
     "hb_cp_comm_unique_id": (ctypes.c_int, [c_void_p]),
     "hb_cp_comm_init": (ctypes.c_int, [_P(c_void_p), c_int32, c_void_p, c_int32]),
     "hb_cp_comm_destroy": (ctypes.c_int, [c_void_p]),
+    "hb_cp_wait": (ctypes.c_int, [c_void_p, c_void_p, ctypes.c_double]),
     "hb_attn_prefill_cp": (ctypes.c_int, [_P(AttentionSpec), _P(CpSpec), _P(AttentionCall),
                                           c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
 }
@@ -233,6 +236,34 @@ def lib():
             f.argtypes = args
         _lib = L
     return _lib
+
+
+SELFTEST_LIB_PATH = os.path.join(PKG_DIR, "libherbert_b200_selftest.so")
+_selftest = None
+
+# the test-only companion library (csrc/selftest/hb_selftest.h)
+_SELFTEST_SIGNATURES = {
+    "hbt_last_error": (ctypes.c_char_p, []),
+    "hbt_prefill_epilogue": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint64), c_void_p]),
+    "hbt_wait_timeout": (ctypes.c_int, [c_void_p, c_size_t, ctypes.c_longlong, ctypes.c_int,
+                                        c_void_p]),
+}
+
+
+def selftest_lib():
+    """Load the test-only library of device self-tests (never used by the
+    product path)."""
+    global _selftest
+    if _selftest is None:
+        if not os.path.exists(SELFTEST_LIB_PATH):
+            raise ImportError(f"{SELFTEST_LIB_PATH} is missing: run __graft_entry__.build()")
+        L = ctypes.CDLL(SELFTEST_LIB_PATH)
+        for name, (res, args) in _SELFTEST_SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _selftest = L
+    return _selftest
 
 
 def status_name(status: int) -> str:
@@ -536,6 +567,15 @@ class Mount:
     def status(self, stream=None):
         check(lib().hb_mount_status(self.h, _stream(stream)))
 
+    @property
+    def needs_reset(self) -> bool:
+        return bool(lib().hb_mount_needs_reset(self.h))
+
+    def reset(self, stream=None):
+        """Clear the poison of a failed call, once the caller has restored or
+        cleared the state it may have touched."""
+        check(lib().hb_mount_reset(self.h, _stream(stream)))
+
     def attention(self, layer, q, k, v, q_norm, k_norm, out, *, rows, pos, stream=None):
         c = MountAttentionCall(q=_ptr(q), k=_ptr(k), v=_ptr(v), q_norm=_ptr(q_norm),
                                k_norm=_ptr(k_norm), out=_ptr(out), rows=rows, pos=pos)
@@ -636,6 +676,15 @@ class CpComm:
         if self.handle is not None and self.handle.value:
             check(lib().hb_cp_comm_destroy(self.handle))
         self.handle = None
+
+    def wait(self, stream=None, timeout_s: float = 60.0) -> None:
+        """Wait for the ring's work on ``stream`` with a deadline; on a timeout
+        or a communicator error the communicator is aborted (and released) and
+        the error raised."""
+        rc = lib().hb_cp_wait(self.handle, _stream(stream), float(timeout_s))
+        if rc in (HB_ERR_TIMEOUT, HB_ERR_NCCL, HB_ERR_CUDA):
+            self.handle = None  # aborted by the library: never destroy it again
+        check(rc)
 
 
 def prefill_cp(spec: AttentionSpec, cp: CpSpec, q, keys, values, out, *, kv_stride: int,

@@ -58,7 +58,7 @@ typedef enum hb_status {
     HB_ERR_WORKSPACE = 11,    /* workspace too small or misaligned            */
     HB_ERR_CUDA = 12,         /* a CUDA runtime call failed                   */
     HB_ERR_TIMEOUT = 13,      /* a bounded device wait ran out                */
-    HB_ERR_NCCL = 14          /* reserved for multi-GPU entry points          */
+    HB_ERR_NCCL = 14          /* the ring's communicator reported an error    */
 } hb_status;
 
 /* Library version, (major << 16) | minor. */
@@ -73,6 +73,12 @@ HB_API hb_status hb_workspace_init(void *workspace, size_t bytes, hb_stream_t st
  * HB_ERR_TIMEOUT if a kernel's bounded wait ran out, HB_ERR_ARG if a kernel
  * met a misaligned table entry.  Synchronises `stream`. */
 HB_API hb_status hb_workspace_status(void *workspace, size_t bytes, hb_stream_t stream);
+/* The same for the entry points that take no workspace (hb_gdn_decode,
+ * hb_attn_decode_noalloc): one status word per device, in static device
+ * memory, raised by any of their calls on the current device and kept until
+ * this call reads and clears it.  Synchronises `stream`.  No counterpart in
+ * the reference, whose calls fail synchronously (src/jit/execution/plan.rs:6). */
+HB_API hb_status hb_device_status(hb_stream_t stream);
 
 /* ------------------------------------------------------------------ SDPA */
 
@@ -142,10 +148,14 @@ HB_API hb_status hb_attn_decode(const hb_attn_spec *spec, const hb_attn_call *ca
  * hb_attn_decode_workspace_bytes) is refused with HB_ERR_WORKSPACE before
  * anything is launched.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress) -- make that first call before any
- * stream capture.  Each call clears the part of the array that must start at
- * zero (one cudaMemsetAsync on `stream`) and then launches; the array is
- * shared by all calls on a device, so calls whose executions overlap on the
- * GPU (different streams without ordering) race and give wrong results.
+ * stream capture; the address is looked up again only when the device's
+ * context changes (after cudaDeviceReset, for instance).  Each call clears
+ * the part of the array that must start at zero (one cudaMemsetAsync on
+ * `stream`) and then launches; the array is shared by all calls on a device,
+ * so calls whose executions overlap on the GPU (different streams without
+ * ordering) race and give wrong results.  A bounded device wait that runs
+ * out (the output is then incomplete) is reported by hb_device_status, not
+ * by the return value, which only covers the host-side checks and launch.
  */
 #define HB_NOALLOC_SCRATCH_BYTES (4u << 20)
 HB_API hb_status hb_attn_decode_noalloc(const hb_attn_spec *spec, const hb_attn_call *call,
@@ -238,6 +248,18 @@ HB_API hb_status hb_attn_prefill_cp(const hb_attn_spec *spec, const hb_cp_spec *
                              const hb_attn_call *call, void *comm, void *workspace,
                              size_t workspace_bytes, hb_stream_t stream, hb_stream_t comm_stream);
 
+/* Host wait with a deadline on a ring call: polls `stream` (the ring's
+ * compute stream; its completion implies every transfer's) and the
+ * communicator's asynchronous error until the work completes or `timeout_s`
+ * seconds pass.  HB_OK when complete.  On a timeout (HB_ERR_TIMEOUT), an
+ * error the communicator reports (HB_ERR_NCCL) or a failed stream query
+ * (HB_ERR_CUDA) the communicator is aborted (ncclCommAbort), which ends the
+ * transfers of the peers that wait on this rank: it is then released and
+ * must not be used or destroyed again; the ranks make a new one.  `comm`
+ * NULL waits on the stream alone.  No counterpart in the reference, whose
+ * pool waits without a deadline (src/pool/thread_pool.rs:261-290). */
+HB_API hb_status hb_cp_wait(void *comm, hb_stream_t stream, double timeout_s);
+
 /* KV cache geometry: KvSpec (src/jit/execution/abi.rs:57-104). */
 typedef struct hb_kv_spec {
     int64_t heads;      /* KV heads                        */
@@ -323,7 +345,10 @@ typedef struct hb_gdn_call {
  * delta-causal-recurrence node (RecurrenceFn, src/jit/emit_recurrence.rs:63-73;
  * x86 src/jit/target/x86/emit_recurrence.rs:108-217; traversal
  * src/jit/target/x86/execution/delta.rs:519-607) with the default non-FMA
- * order, so the state and outputs are the reference's bits.
+ * order, so the state and outputs are the reference's bits.  It takes no
+ * workspace, as RecurrenceFn takes no scratch: a bounded device wait that
+ * runs out (state and outputs then unwritten) is reported by
+ * hb_device_status.
  */
 HB_API hb_status hb_gdn_decode(const hb_gdn_shape *shape, const hb_gdn_call *call, hb_stream_t stream);
 
@@ -515,8 +540,21 @@ HB_API hb_status hb_mount_route(const hb_mount_desc *desc, int64_t layer, hb_lay
  * (state buffers, RoPE tables): those must outlive the mount. */
 HB_API hb_status hb_mount_create(const hb_mount_desc *desc, hb_mount **mount);
 HB_API void hb_mount_destroy(hb_mount *mount);
-/* The status word of the mount's workspaces (as hb_workspace_status). */
+/* The status word of the mount's workspaces (as hb_workspace_status).  A
+ * device-side failure it finds poisons the mount (below); on a poisoned
+ * mount it returns the first failure's status. */
 HB_API hb_status hb_mount_status(hb_mount *mount, hb_stream_t stream);
+/* A mixer call that fails after it entered execution (a node launched, so
+ * state may be half updated), or a failure hb_mount_status finds, poisons the
+ * mount: every later hb_mount_attention / hb_mount_delta is refused with the
+ * first failure's status until hb_mount_reset, as a failed call poisons the
+ * reference's execution session until its owner resets or restores the model
+ * (src/jit/execution/runtime.rs:144-151, 310-327; program.rs:289).  Refusals
+ * before any launch (declines, bad arguments) do not poison.  Reset after the
+ * caller has restored (hb_snapshot_restore) or cleared every state buffer the
+ * failed call may have touched; it clears the workspaces' status words. */
+HB_API int hb_mount_needs_reset(const hb_mount *mount);
+HB_API hb_status hb_mount_reset(hb_mount *mount, hb_stream_t stream);
 
 typedef struct hb_mount_attention_call {
     uint16_t *q;               /* [rows][attn.q_row]: heads (normed and rotated in place), gates  */
@@ -545,19 +583,6 @@ typedef struct hb_mount_delta_call {
 } hb_mount_delta_call;
 HB_API hb_status hb_mount_delta(hb_mount *mount, int64_t layer, const hb_mount_delta_call *call,
                                 hb_stream_t stream);
-
-/*
- * Self-test, no counterpart in the reference: runs the arithmetic of
- * hb_attn_prefill's epilogue (O / l rounded to bf16, then the output gate)
- * over every pair of bf16 values (a, g) and over every f32 value of O / l,
- * and compares each result with the exact per-element steps.  Synchronous
- * on `stream`; tens of milliseconds on a B200.  out[8]: [0] gate
- * mismatches, [1] column pairs the fast path sent to the exact steps,
- * [2] first mismatching element + 1 (a | g << 16; 0 = none), [3] its result
- * | expected << 16; [4..7] the same for the O / l rounding (element = the
- * f32 bits).
- */
-HB_API hb_status hb_selftest_prefill_epilogue(uint64_t *out, hb_stream_t stream);
 
 #ifdef __cplusplus
 }

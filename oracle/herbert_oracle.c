@@ -749,7 +749,33 @@ int orc_gdn_layer(float *qkv, float *state, float *out, const float *beta,
  * double; logf: 16 subintervals, invc/logc table, cubic in double), which is
  * also glibc's expf/logf since 2.27/2.28.  Tables (src/jit/execution/math_data.rs):
  * EXPF_T[i] = bits(RN(2^(i/32))) - (i << 47); LOGF_T[i] = {invc_i, RN(-ln invc_i)}.
- * Constants of the evaluation: the reference's INV, SHIFT, E0..E2, LN2, L0..L2. */
+ * Constants of the evaluation: the reference's INV, SHIFT, E0..E2, LN2, L0..L2.
+ *
+ * EXPF_T and LOGF_T are data of Arm optimized-routines (math/exp2f_data.c,
+ * math/logf_data.c at revision 22bc70e01a192aaeac161143353315f051f3e647),
+ * used under the MIT option of its "MIT OR Apache-2.0 WITH LLVM-exception"
+ * licence:
+ *
+ *   Copyright (c) 1999-2022, Arm Limited.  SPDX-License-Identifier: MIT
+ *
+ *   Permission is hereby granted, free of charge, to any person obtaining a
+ *   copy of this software and associated documentation files (the
+ *   "Software"), to deal in the Software without restriction, including
+ *   without limitation the rights to use, copy, modify, merge, publish,
+ *   distribute, sublicense, and/or sell copies of the Software, and to permit
+ *   persons to whom the Software is furnished to do so, subject to the
+ *   following conditions:
+ *
+ *   The above copyright notice and this permission notice shall be included
+ *   in all copies or substantial portions of the Software.
+ *
+ *   THE SOFTWARE IS PROVIDED "AS IS", WITHOUT WARRANTY OF ANY KIND, EXPRESS
+ *   OR IMPLIED, INCLUDING BUT NOT LIMITED TO THE WARRANTIES OF
+ *   MERCHANTABILITY, FITNESS FOR A PARTICULAR PURPOSE AND NONINFRINGEMENT. IN
+ *   NO EVENT SHALL THE AUTHORS OR COPYRIGHT HOLDERS BE LIABLE FOR ANY CLAIM,
+ *   DAMAGES OR OTHER LIABILITY, WHETHER IN AN ACTION OF CONTRACT, TORT OR
+ *   OTHERWISE, ARISING FROM, OUT OF OR IN CONNECTION WITH THE SOFTWARE OR THE
+ *   USE OR OTHER DEALINGS IN THE SOFTWARE. */
 static const uint64_t EXPF_T[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,

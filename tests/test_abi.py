@@ -129,3 +129,20 @@ def test_status_names():
     assert hb.status_name(0) == "HB_OK"
     assert hb.status_name(hb.HB_ERR_TIMEOUT) == "HB_ERR_TIMEOUT"
     assert hb.version() >= (0, 1)
+
+
+def test_ring_wait_refuses_a_bad_deadline():
+    # checked on the host before any CUDA or NCCL call
+    for t in (float("nan"), -1.0):
+        assert hb.lib().hb_cp_wait(None, None, t) == hb.HB_ERR_ARG
+        assert "timeout" in hb.last_error()
+
+
+def test_selftests_live_outside_the_product_library():
+    # the device self-tests are in the test-only companion library
+    nm = subprocess.run(["nm", "-D", "--defined-only", hb.LIB_PATH], capture_output=True,
+                        text=True, check=True).stdout
+    assert "selftest" not in nm and "hbt_" not in nm
+    T = hb.selftest_lib()
+    for name in hb._SELFTEST_SIGNATURES:
+        assert hasattr(T, name), name

@@ -24,6 +24,8 @@ def test_recurrent_is_bit_exact(cuda_device, rows, nk, nv, hkd, hvd, l2, warm):
     ref_out, ref_st = oracle_gdn(inp, l2=l2)
     assert np.array_equal(out.view(np.uint32), ref_out.view(np.uint32))
     assert np.array_equal(st.view(np.uint32), ref_st.view(np.uint32))
+    import herbert_b200 as hb  # the recurrence reports through the per-device status word
+    assert hb.lib().hb_device_status(None) == hb.HB_OK, hb.last_error()
 
 
 @pytest.mark.parametrize("name", GDN_FIXTURES)

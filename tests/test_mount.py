@@ -193,3 +193,51 @@ def test_delta_layer_matches_the_oracle(rows):
         assert rel_frob(recs[REC_STRIDE:], rec.ravel()) <= 1e-2
         assert rel_frob(out_f32.cpu().numpy(), yn) <= 1e-2
     assert np.array_equal(m.kv.cpu().numpy().view(np.uint16), m.kv0)  # no KV touched
+
+
+@pytest.mark.gpu
+def test_a_failed_call_poisons_the_mount_until_reset():
+    """A call that fails after its first node launched leaves the layer's
+    state half updated: the mount refuses every later mixer call (before any
+    launch) until its owner restores the state and resets it, as a failed
+    call poisons the reference's execution session."""
+    import torch
+    m = _Model(0xD77)
+    rows, layer, slot = 6, 2, 1
+    inp = DeltaFrontInputs(rows, nk=NK, nv=NV, hkd=HKD, hvd=HVD, seed=0xD78)
+    out = torch.empty((rows, NV * HVD), dtype=torch.int16, device="cuda")
+    args = [_dev(inp.qkv), _dev(inp.ab), _dev(inp.z), _dev(inp.conv_weight), _dev(inp.dt_bias),
+            _dev(inp.a_log), _dev(inp.norm_weight), out]
+    bad = list(args)
+    bad[2] = None  # the gated norm refuses a null z, after the conv and the recurrence ran
+    assert not m.mount.needs_reset
+    with pytest.raises(hb.HBError) as e:
+        m.mount.delta(layer, *bad, rows=rows)
+    assert e.value.status == hb.HB_ERR_ARG
+    assert m.mount.needs_reset
+    torch.cuda.synchronize()
+    conv_after, rec_after = m.conv.clone(), m.rec.clone()
+    assert not torch.equal(m.conv.cpu(), torch.from_numpy(m.conv0))  # the conv state moved
+    # refused, nothing launched: the state stays as the failed call left it
+    for call in (lambda: m.mount.delta(layer, *args, rows=rows),
+                 lambda: m.mount.delta(0, *args, rows=rows)):
+        with pytest.raises(hb.HBError) as e2:
+            call()
+        assert e2.value.status == hb.HB_ERR_ARG and "hb_mount_reset" in str(e2.value)
+    with pytest.raises(hb.HBError):
+        m.mount.status()
+    torch.cuda.synchronize()
+    assert torch.equal(m.conv, conv_after) and torch.equal(m.rec, rec_after)
+    # the owner restores the state it holds, then resets the mount
+    m.conv.copy_(torch.from_numpy(m.conv0))
+    m.rec.copy_(torch.from_numpy(m.rec0))
+    m.mount.reset()
+    assert not m.mount.needs_reset
+    m.mount.delta(layer, *args, rows=rows)
+    torch.cuda.synchronize()
+    m.mount.status()
+    st, rec, yn, yb = _delta_oracle(inp, m.conv0[slot * CONV_STRIDE:(slot + 1) * CONV_STRIDE]
+                                    .reshape(CONV, CK),
+                                    m.rec0[slot * REC_STRIDE:(slot + 1) * REC_STRIDE])
+    assert np.array_equal(m.conv.cpu().numpy()[CONV_STRIDE:], st.ravel())
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), yb)

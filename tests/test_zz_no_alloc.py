@@ -42,6 +42,9 @@ def test_noalloc_matches_workspace_entry_point(cuda_device, rows, past):
         assert rc == hb.HB_OK, hb.last_error()
         torch.cuda.synchronize()
         assert_sdpa_close(bits_of(out), ref, f"noalloc rows={rows} past={past}")
+    # no bounded wait ran out: the per-device status word these calls report
+    # through is clear
+    assert hb.lib().hb_device_status(None) == hb.HB_OK, hb.last_error()
 
 
 def test_noalloc_refuses_calls_beyond_its_scratch(cuda_device):
