@@ -3,12 +3,15 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
 Configurations (BASELINE.json "configs", synthetic seeded data):
-  prefill  causal prefill SDPA, S 4096, Hq 16 / Hkv 4 / d 256, gated     TFLOP/s  (default)
+  prefill  causal prefill SDPA, S 4096, Hq 16 / Hkv 4 / d 256, gated     TFLOP/s
   decode   one decode step, n 2048, same heads, gated                    GB/s
   gdn      GatedDeltaNet: prefill T 4096 then 256 decode steps           tok/s
   batch    batched decode, 64 sequences, L ~ U{1024..32768}              GB/s
   cp       causal prefill SDPA at S 131072, context parallel over the GPUs
-           (zig-zag shards, K/V ring by NCCL send/recv, LSE merge)      TFLOP/s
+           (zig-zag shards, K/V ring by NCCL send/recv, LSE merge)      TFLOP/s  (default)
+           one GPU runs the whole sequence through the single-GPU kernel
+  cp_hops  the ring's hop kernel alone: rank 3 of an 8-rank ring emulated on
+           one GPU (all shards resident, no transport), hops + finish   TFLOP/s
   front    attention front end of a 4096-row block: q/k head norms,
            partial RoPE, KV append                                      GB/s
   gdn_front  DeltaNet front end of a 4096-row block: causal conv + SiLU
@@ -23,9 +26,13 @@ Configurations (BASELINE.json "configs", synthetic seeded data):
            KV, 24 DeltaNet layers' states, logits); e2e adds the restore  GB/s
 A step is one pass of the path over one batch: one prefill / one decode step /
 one GDN prefill + 256 steps / one decode step of the whole batch / one
-131072-token prefill / one front-end (or gated-norm) call.  The ring holds NCCL calls, so `cp` steps are issued
-eagerly between the CUDA events instead of from a CUDA graph (a step lasts
-tens of milliseconds; launch costs are microseconds).
+131072-token prefill / one front-end (or gated-norm) call.  The ring holds
+NCCL calls, so `cp` steps are issued eagerly between the CUDA events instead
+of from a CUDA graph (a step lasts tens of milliseconds; launch costs are
+microseconds).
+
+`--gpus N` without torchrun starts N ranks with torch.distributed.run;
+under torchrun N must equal WORLD_SIZE.
 
 `value` is device-timed with CUDA events on the launching stream around one
 CUDA-graph replay of K steps, inputs resident in HBM and rotated over copies
@@ -242,10 +249,6 @@ class PrefillWorkload(_AttnWorkload):
         self.work = prefill_flops(S)
         self.units = "TFLOP/s"
 
-    def describe(self):
-        return {"workload": "causal prefill SDPA (BASELINE configs[1])", "seq_len": self.S,
-                "q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "gate": "sigmoid",
-                "past": 0}
 
 
 class DecodeWorkload(_AttnWorkload):
@@ -257,10 +260,6 @@ class DecodeWorkload(_AttnWorkload):
         self.work = 2 * HKV * n * HD * 2 + 3 * HQ * HD * 2  # K+V + q + gate + out bytes
         self.units = "GB/s"
 
-    def describe(self):
-        return {"workload": "single decode step gated SDPA (BASELINE configs[0])",
-                "kv_len": self.n, "q_heads": HQ, "kv_heads": HKV, "head_dim": HD,
-                "gate": "sigmoid"}
 
 
 class GdnWorkload(Workload):
@@ -332,21 +331,18 @@ class GdnWorkload(Workload):
         torch.cuda.synchronize()
         return gdn_prefill_flops(self.T), a.elapsed_time(b) / 1e3 / reps
 
-    def describe(self):
-        return {"workload": "GatedDeltaNet prefill then decode (BASELINE configs[2])",
-                "prefill_tokens": self.T, "decode_steps": self.steps, "key_heads": NK,
-                "value_heads": NV, "head_k_dim": HKD, "head_v_dim": HVD}
 
 
 class BatchWorkload(Workload):
     def __init__(self, device, rank=0, world=1, seed=0x5EED0004):
         import torch
         import herbert_b200 as hb
-        from herbert_b200.inputs import batch_lengths, lpt_assign
+        from herbert_b200.inputs import batch_lengths
         self.hb = hb
         lens = batch_lengths(64, 1024, 32768, seed)
-        # the new token is position L-1: the cache holds L keys
-        mine = lpt_assign(lens, world)[rank]
+        # the new token is position L-1: the cache holds L keys; every rank
+        # derives the same plan (longest first, least-loaded GPU)
+        mine = hb.shard_of(lens, world, rank)
         self.lens = [int(lens[i]) for i in mine]
         gen = torch.Generator(device=device).manual_seed(seed + rank)
         qd = HQ * HD
@@ -383,10 +379,6 @@ class BatchWorkload(Workload):
         self.step()
         self.h_out.copy_(self.out, non_blocking=True)
 
-    def describe(self):
-        return {"workload": "batched decode SDPA, sequences sharded by LPT (BASELINE configs[3])",
-                "sequences": 64, "kv_len": "U{1024..32768} seed 0x5EED0004", "q_heads": HQ,
-                "kv_heads": HKV, "head_dim": HD, "gate": "sigmoid"}
 
 
 class CpWorkload(Workload):
@@ -466,10 +458,58 @@ class CpWorkload(Workload):
         if self.comm is not None:
             self.comm.close()
 
-    def describe(self):
-        return {"workload": "long-context causal prefill SDPA (BASELINE configs[4])",
-                "seq_len": CP_S, "q_heads": HQ, "kv_heads": HKV, "head_dim": HD,
-                "gate": "sigmoid", "chunk": self.chunk}
+
+
+CP_HOPS_RANKS, CP_HOPS_RANK = 8, 3
+
+
+class CpHopsWorkload(Workload):
+    """The hop kernel of the context-parallel ring on one GPU: rank
+    CP_HOPS_RANK of an emulated ring of CP_HOPS_RANKS over the 131072-token
+    sequence, its hops through hb_attn_prefill_cp_hop over every rank's shard
+    (all shards resident, the transport left out) and the finishing step.  A
+    step is that rank's causal work; the hops of a real ring rank are these
+    launches with NCCL transfers beside them."""
+
+    def __init__(self, device, seed=0x5EED000B):
+        import torch
+        import herbert_b200 as hb
+        P, r = CP_HOPS_RANKS, CP_HOPS_RANK
+        c = int(os.environ.get("HB_CP_HOPS_CHUNK", CP_S // (2 * P)))
+        self.hb, self.chunk = hb, c
+        self.cp = hb.cp_spec(P, r, c)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        qd = HQ * HD
+        self.q = _randn_bf16((2 * c, 2 * qd), gen, device)
+        self.shards = [_randn_bf16((2, HKV, 2 * c, HD), gen, device) for _ in range(P)]
+        self.out = torch.empty((2 * c, qd), dtype=torch.bfloat16, device=device)
+        self.spec = hb.attention_spec(HQ, HQ // HKV, HD, True)
+        self.ws = None
+        pos = hb.cp_positions(self.cp, r)
+        self.work = 4 * HQ * HD * sum(p + 1 for p in pos)
+        self.units = "TFLOP/s"
+        self.launches_per_step = P + 1
+        self.R = 1
+        self.set_bytes = _nbytes(self.q, self.out, *self.shards)
+        self.h_in = [self.q.cpu().pin_memory()]
+        self.h_out = torch.empty(self.out.shape, dtype=self.out.dtype).pin_memory()
+        self.h2d = _nbytes(*self.h_in)
+        self.d2h = _nbytes(self.h_out)
+
+    def step(self, i=0):
+        kvs = 2 * self.chunk * HD
+        for hop in range(CP_HOPS_RANKS):
+            sh = self.shards[self.hb.cp_hop_source(self.cp, hop)]
+            self.ws = self.hb.prefill_cp_hop(self.spec, self.cp, self.q, sh[0], sh[1], self.out,
+                                             hop, kv_stride=kvs, workspace=self.ws)
+        own = self.shards[CP_HOPS_RANK]
+        self.hb.prefill_cp_finish(self.spec, self.cp, self.q, own[0], own[1], self.out,
+                                  kv_stride=kvs, workspace=self.ws)
+
+    def e2e_step(self, i=0):
+        self.q.copy_(self.h_in[0], non_blocking=True)
+        self.step()
+        self.h_out.copy_(self.out, non_blocking=True)
 
 
 def front_bytes(rows, heads=HQ, kv_heads=HKV, hd=HD, rotary=FRONT_ROTARY):
@@ -531,10 +571,6 @@ class FrontWorkload(Workload):
         self.step(0)
         self.h_out.copy_(q, non_blocking=True)
 
-    def describe(self):
-        return {"workload": "attention front end: q/k GemmaRMSNorm head norms + partial RoPE "
-                "(64 of 256) + KV append, one 4096-row block", "rows": self.rows,
-                "q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "rotary": FRONT_ROTARY}
 
 
 def gdn_front_bytes(rows, nk=NK, nv=NV, hkd=HKD, hvd=HVD, ck=4):
@@ -600,11 +636,6 @@ class GdnFrontWorkload(Workload):
         for h, d in zip(self.h_out, (qkv, beta, decay)):
             h.copy_(d, non_blocking=True)
 
-    def describe(self):
-        return {"workload": "DeltaNet front end: causal depthwise conv (K 4) + SiLU over the "
-                "qkv projection in place, beta/decay gates; one 4096-row block", "rows": self.rows,
-                "key_heads": NK, "value_heads": NV, "head_k_dim": HKD, "head_v_dim": HVD,
-                "conv_channels": 2 * NK * HKD + NV * HVD}
 
 
 class GdnNormWorkload(Workload):
@@ -647,10 +678,6 @@ class GdnNormWorkload(Workload):
         self.step(0)
         self.h_out.copy_(out, non_blocking=True)
 
-    def describe(self):
-        return {"workload": "DeltaNet gated RMS norm: y = rmsnorm(x) w silu(z) per V head, bf16 "
-                "out; one 4096-row block", "rows": self.rows, "value_heads": NV,
-                "head_v_dim": HVD}
 
 
 SNAP_LAYERS, SNAP_EVERY, SNAP_POS = 32, 4, 32768  # every 4th layer full attention
@@ -728,12 +755,6 @@ class SnapshotWorkload(Workload):
         self.link_gbs = self.flat.numel() / t_flat / 1e9
         return self.nbytes, t_take
 
-    def describe(self):
-        return {"workload": "snapshot of one sequence's state (reference Instantaneous format) "
-                "into a pinned host image", "positions": SNAP_POS, "layers": SNAP_LAYERS,
-                "attention_layers": SNAP_LAYERS // SNAP_EVERY, "kv_heads": HKV, "head_dim": HD,
-                "deltanet_layers": SNAP_LAYERS - SNAP_LAYERS // SNAP_EVERY,
-                "image_bytes": self.nbytes}
 
 
 def mixer_step_bytes(pos=SNAP_POS):
@@ -836,21 +857,84 @@ class MixersWorkload(Workload):
         for h, d in zip(self.h_out, (self.attn_out, self.delta_out)):
             h.copy_(d, non_blocking=True)
 
-    def describe(self):
-        return {"workload": "one decode token through the mixers of a 32-layer hybrid model "
-                "routed by hb_mount (projections excluded)", "positions": SNAP_POS,
-                "attention_layers": SNAP_LAYERS // SNAP_EVERY,
-                "deltanet_layers": SNAP_LAYERS - SNAP_LAYERS // SNAP_EVERY, "q_heads": HQ,
-                "kv_heads": HKV, "head_dim": HD, "value_heads": NV, "head_k_dim": HKD,
-                "bytes_per_token": self.bytes_per_step}
+
+
+def config_of(cfg, world):
+    """The `config` object of the JSON line; both arms print the same one."""
+    attn = {"q_heads": HQ, "kv_heads": HKV, "head_dim": HD, "gate": "sigmoid"}
+    delta = {"key_heads": NK, "value_heads": NV, "head_k_dim": HKD, "head_v_dim": HVD}
+    rotated = ("inputs rotate over copies totalling more than twice the 126 MB L2, so every "
+               "step reads cold inputs")
+    if cfg == "prefill":
+        d = dict(workload="causal prefill SDPA (BASELINE configs[1])", seq_len=PREFILL_S,
+                 past=0, **attn, l2=rotated)
+    elif cfg == "decode":
+        d = dict(workload="single decode step gated SDPA (BASELINE configs[0])",
+                 kv_len=DECODE_N, **attn, l2=rotated)
+    elif cfg == "gdn":
+        d = dict(workload="GatedDeltaNet prefill then decode (BASELINE configs[2])",
+                 prefill_tokens=GDN_T, decode_steps=GDN_STEPS, **delta, l2=rotated)
+    elif cfg == "batch":
+        d = dict(workload="batched decode SDPA, sequences sharded by the library's plan "
+                 "(BASELINE configs[3])", sequences=64, kv_len="U{1024..32768} seed 0x5EED0004",
+                 **attn, l2="inputs larger than L2: every step streams all caches of the GPU "
+                 "(4.4 GB in all)")
+    elif cfg == "cp":
+        d = dict(workload="long-context causal prefill SDPA (BASELINE configs[4])",
+                 seq_len=CP_S, **attn, chunk=CP_S // (2 * world),
+                 l2="inputs larger than L2: each GPU reads at least 0.3 GB of q, K and V per "
+                 "step (2.7 GB on one GPU)")
+    elif cfg == "cp_hops":
+        d = dict(workload="one rank's hops of an emulated context-parallel ring on one GPU "
+                 "(the hop kernel of BASELINE configs[4])", seq_len=CP_S, **attn,
+                 ring_ranks=CP_HOPS_RANKS, rank=CP_HOPS_RANK, chunk=CP_S // (2 * CP_HOPS_RANKS),
+                 l2="inputs larger than L2 (q rows 268 MB, 8 shards of 67 MB)")
+    elif cfg == "front":
+        d = dict(workload="attention front end: q/k GemmaRMSNorm head norms + partial RoPE "
+                 "(64 of 256) + KV append, one 4096-row block", rows=PREFILL_S,
+                 q_heads=HQ, kv_heads=HKV, head_dim=HD, rotary=FRONT_ROTARY, l2=rotated)
+    elif cfg == "gdn_front":
+        d = dict(workload="DeltaNet front end: causal depthwise conv (K 4) + SiLU over the "
+                 "qkv projection in place, beta/decay gates; one 4096-row block", rows=GDN_T,
+                 **delta, conv_channels=2 * NK * HKD + NV * HVD, l2=rotated)
+    elif cfg == "gdn_norm":
+        d = dict(workload="DeltaNet gated RMS norm: y = rmsnorm(x) w silu(z) per V head, bf16 "
+                 "out; one 4096-row block", rows=GDN_T, value_heads=NV, head_v_dim=HVD,
+                 l2=rotated)
+    elif cfg == "snapshot":
+        d = dict(workload="snapshot of one sequence's state (reference Instantaneous format) "
+                 "into a pinned host image", positions=SNAP_POS, layers=SNAP_LAYERS,
+                 attention_layers=SNAP_LAYERS // SNAP_EVERY, kv_heads=HKV, head_dim=HD,
+                 deltanet_layers=SNAP_LAYERS - SNAP_LAYERS // SNAP_EVERY,
+                 l2="the 1.1 GB state is larger than L2")
+    elif cfg == "mixers":
+        d = dict(workload="one decode token through the mixers of a 32-layer hybrid model "
+                 "routed by hb_mount (projections excluded)", positions=SNAP_POS,
+                 attention_layers=SNAP_LAYERS // SNAP_EVERY,
+                 deltanet_layers=SNAP_LAYERS - SNAP_LAYERS // SNAP_EVERY, **attn,
+                 value_heads=NV, head_k_dim=HKD, bytes_per_token=mixer_step_bytes(),
+                 l2="8 caches of 134 MB and 24 DeltaNet states per token, larger than L2")
+    else:
+        raise SystemExit(f"unknown config {cfg}")
+    if cfg == "batch":
+        par = f"sequences sharded over {world} GPUs, no collective"
+    elif cfg == "cp":
+        par = (f"context parallel over {world} GPUs: zig-zag shards, K/V ring by NCCL "
+               "send/recv, log-sum-exp merge" if world > 1 else "one GPU, whole sequence")
+    else:
+        par = f"{world} independent replicas"
+    d["parallelism"] = par
+    return d
 
 
 METRIC = {"prefill": "prefill SDPA TFLOP/s", "decode": "attn decode HBM GB/s",
           "gdn": "GDN tok/s", "batch": "attn decode HBM GB/s", "cp": "prefill SDPA TFLOP/s",
+          "cp_hops": "prefill SDPA TFLOP/s",
           "front": "attn front end HBM GB/s", "gdn_front": "GDN front end HBM GB/s",
           "gdn_norm": "GDN gated norm HBM GB/s", "snapshot": "snapshot take GB/s",
           "mixers": "mixer decode tok/s"}
 BOUND = {"prefill": "tensor", "decode": "hbm", "gdn": "tensor", "batch": "hbm", "cp": "tensor",
+         "cp_hops": "tensor",
          "front": "hbm", "gdn_front": "hbm", "gdn_norm": "hbm", "snapshot": "host link",
          "mixers": "hbm"}
 STRONG = ("batch", "cp")  # total work fixed as the GPUs grow
@@ -867,6 +951,8 @@ def make_workload(cfg, device, rank, world):
         return BatchWorkload(device, rank, world)
     if cfg == "cp":
         return CpWorkload(device, rank, world)
+    if cfg == "cp_hops":
+        return CpHopsWorkload(device)
     if cfg == "front":
         return FrontWorkload(device)
     if cfg == "gdn_front":
@@ -1010,15 +1096,12 @@ def run_ours(args):
                       "bytes" if cfg == "snapshot" else
                       "bf16 attention, f32 DeltaNet" if cfg == "mixers" else "bf16"),
             "data": "synthetic",
-            "config": dict(wl.describe(), parallelism=(
-                f"sequences sharded over {world} GPUs, no collective" if cfg == "batch"
-                else (f"context parallel over {world} GPUs: zig-zag shards, K/V ring by NCCL "
-                      "send/recv, log-sum-exp merge" if world > 1 else "one GPU, whole sequence")
-                if cfg == "cp" else f"{world} independent replicas"),
-                l2=f"inputs rotate over {wl.R} copies ({wl.R * wl.set_bytes / 2**20:.0f} MiB) per GPU",
-                timing=(f"one CUDA graph of {args.steps} steps between CUDA events"
-                        if wl.graphable else
-                        f"{args.steps} steps issued eagerly between CUDA events")),
+            "config": config_of(cfg, world),
+            "timing": (f"one CUDA graph of {args.steps} steps between CUDA events"
+                       if wl.graphable else
+                       f"{args.steps} steps issued eagerly between CUDA events") + (
+                           f"; inputs rotate over {wl.R} copies "
+                           f"({wl.R * wl.set_bytes / 2**20:.0f} MiB) per GPU" if wl.R > 1 else ""),
             "roofline": {"bound": BOUND[cfg], "achieved": round(achieved, 3), "peak": peak,
                          "unit": unit, "frac": round(achieved / peak, 4),
                          "peak_source": pk["source"] + (
@@ -1075,7 +1158,7 @@ def cpu_baseline(cfg, budget_s=10.0, threads=0):
     oracle.build()
     threads = threads or _cpu_threads()
     impl = 1 if oracle.has_avx512bf16() else 0
-    if cfg in ("prefill", "cp"):
+    if cfg in ("prefill", "cp", "cp_hops"):
         S = PREFILL_S if cfg == "prefill" else CP_S
         rows = (256 if impl else 32) if cfg == "prefill" else (16 if impl else 2)
         past = S - rows
@@ -1219,8 +1302,9 @@ def run_reference(args):
                   "bytes" if cfg == "snapshot" else
                   "bf16 attention, f32 DeltaNet" if cfg == "mixers" else "bf16"),
         "data": "synthetic",
-        "config": {"workload": cfg, "note": "CPU restatement of the reference's x86 AVX-512 BF16 "
-                   "kernels (Rust reference not buildable here)"},
+        "config": config_of(cfg, world),
+        "note": ("CPU restatement of the reference's x86 AVX-512 BF16 kernels (the Rust "
+                 "reference cannot be built here); rank 0 alone runs it"),
         "cpu_baseline": dict(base, value=v),
         "e2e": {"value": v, "unit": base["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1228,18 +1312,36 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _free_port():
+    import socket
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        return sk.getsockname()[1]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="prefill", choices=sorted(METRIC))
+    ap.add_argument("--config", default="cp", choices=sorted(METRIC))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gpus < 1:
+        raise SystemExit("--gpus must be at least 1")
+    if "WORLD_SIZE" not in os.environ and args.gpus > 1:
+        # not under torchrun: start one rank per GPU on this node
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={args.gpus}", "--master-addr", "127.0.0.1",
+               "--master-port", str(_free_port()), os.path.abspath(__file__)] + sys.argv[1:]
+        raise SystemExit(subprocess.call(cmd))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but {world} ranks were started")
     if args.impl == "reference":
         run_reference(args)
     else:

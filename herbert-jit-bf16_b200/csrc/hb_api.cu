@@ -11,11 +11,15 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <numeric>
+#include <queue>
+#include <vector>
 
 #include "hb_host.h"
 #include "hb_internal.h"
@@ -396,6 +400,41 @@ hb_status hb_attn_decode_batch(const hb_attn_spec* s, const hb_decode_seq* seqs,
   L.partials = reinterpret_cast<float*>(base + pl.partials_off);
   cudaError_t e = launch_attn_decode(L, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode_batch launch");
+  return HB_OK;
+}
+
+hb_status hb_decode_shard_plan(const int64_t* cost, int64_t nseq, int32_t parts, int32_t* part,
+                               int64_t* load) {
+  if (nseq <= 0) return fail(HB_DECLINE_EMPTY, "empty batch");
+  if (!cost || !part) return fail(HB_ERR_ARG, "cost or part is null");
+  if (nseq > (int64_t(1) << 24) || parts < 1 || parts > 4096)
+    return fail(HB_ERR_ARG, "nseq %lld / parts %d out of range (nseq <= 2^24, parts 1..4096)",
+                (long long)nseq, int(parts));
+  int64_t total = 0;
+  for (int64_t i = 0; i < nseq; ++i) {
+    if (cost[i] < 0 || cost[i] >= (int64_t(1) << 62) - total)
+      return fail(HB_ERR_ARG, "cost[%lld] negative or the costs' sum at or above 2^62",
+                  (long long)i);
+    total += cost[i];
+  }
+  std::vector<int64_t> order(static_cast<size_t>(nseq));
+  std::iota(order.begin(), order.end(), int64_t(0));
+  std::stable_sort(order.begin(), order.end(),
+                   [cost](int64_t a, int64_t b) { return cost[a] > cost[b]; });
+  // least-loaded GPU first, the lowest index on a tie
+  typedef std::pair<int64_t, int32_t> Bin;
+  std::priority_queue<Bin, std::vector<Bin>, std::greater<Bin>> bins;
+  for (int32_t g = 0; g < parts; ++g) bins.push(Bin(0, g));
+  std::vector<int64_t> sums(static_cast<size_t>(parts), 0);
+  for (int64_t i : order) {
+    Bin b = bins.top();
+    bins.pop();
+    part[i] = b.second;
+    b.first += cost[i];
+    sums[size_t(b.second)] = b.first;
+    bins.push(b);
+  }
+  if (load) std::copy(sums.begin(), sums.end(), load);
   return HB_OK;
 }
 

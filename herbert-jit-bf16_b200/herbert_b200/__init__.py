@@ -177,6 +177,8 @@ _SIGNATURES = {
                                                         c_int64]),
     "hb_attn_decode_batch": (ctypes.c_int, [_P(AttentionSpec), c_void_p, c_int64, c_int64,
                                             c_int64, c_void_p, c_size_t, c_void_p]),
+    "hb_decode_shard_plan": (ctypes.c_int, [_P(c_int64), c_int64, c_int32, _P(c_int32),
+                                            _P(c_int64)]),
     "hb_attn_prefill_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionCall)]),
     "hb_attn_prefill": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
                                        c_void_p]),
@@ -386,6 +388,23 @@ def seq_table(entries, device="cuda"):
     raw = bytes(arr)
     host = torch.frombuffer(bytearray(raw), dtype=torch.uint8)
     return host.to(device)
+
+
+def shard_plan(costs, parts: int):
+    """hb_decode_shard_plan: the GPU of each sequence (longest first, each to
+    the least-loaded GPU) and each GPU's total cost.  Returns (part, load)."""
+    n = len(costs)
+    c = (c_int64 * n)(*[int(x) for x in costs])
+    part = (c_int32 * n)()
+    load = (c_int64 * parts)()
+    check(lib().hb_decode_shard_plan(c, n, parts, part, load))
+    return list(part), list(load)
+
+
+def shard_of(costs, parts: int, rank: int):
+    """Indices of the sequences GPU ``rank`` serves, in input order."""
+    part, _ = shard_plan(costs, parts)
+    return [i for i, g in enumerate(part) if g == rank]
 
 
 def kv_append(spec: KvSpec, keys, values, input_keys, input_values, *, rows: int, past: int,

@@ -91,19 +91,6 @@ def batch_lengths(nseq=64, lo=1024, hi=32768, seed=0x5EED0004) -> np.ndarray:
     return rng.integers(lo, hi + 1, size=nseq)
 
 
-def lpt_assign(sizes, parts: int):
-    """Longest-processing-time-first assignment of items to `parts` bins
-    (by size); returns a list of index lists."""
-    order = np.argsort(-np.asarray(sizes), kind="stable")
-    load = [0] * parts
-    bins = [[] for _ in range(parts)]
-    for i in order:
-        j = min(range(parts), key=lambda b: (load[b], b))
-        bins[j].append(int(i))
-        load[j] += int(sizes[i])
-    return bins
-
-
 class FrontInputs:
     """One call of the attention front end (head-norm-rope + kv-append).
 

@@ -177,6 +177,22 @@ HB_API hb_status hb_attn_decode_batch(const hb_attn_spec *spec, const hb_decode_
                                void *workspace, size_t workspace_bytes, hb_stream_t stream);
 
 /*
+ * Batched decode over several GPUs, one process per GPU with no collective:
+ * the plan of which GPU serves which sequence.  Sequences are taken in
+ * decreasing order of `cost` (their KV positions, or bytes: the decode step
+ * streams each cache once) and each goes to the GPU with the least cost so
+ * far, the lowest index on a tie -- the longest-processing-time rule, whose
+ * busiest GPU carries at most 4/3 - 1/(3 parts) of the optimal maximum.
+ * part[i] receives the GPU of sequence i, and load[g] (optional, `parts`
+ * entries) the cost assigned to GPU g.  Every rank computes the same plan
+ * from the same costs.  Host only; nseq <= 2^24, parts 1 .. 4096, costs >= 0
+ * with a sum below 2^62.  No counterpart in the reference, where one Runner
+ * serves one sequence (src/jit/model.rs:329-396).
+ */
+HB_API hb_status hb_decode_shard_plan(const int64_t *cost, int64_t nseq, int32_t parts,
+                                      int32_t *part, int64_t *load);
+
+/*
  * Prefill SDPA: causal flash attention over `rows` query rows (tcgen05 MMA,
  * TMEM accumulators).  Replaces the attention node in the prefill regime:
  * SdpaPrefillFn blocks (src/jit/emit_sdpa.rs:173-304;

@@ -233,6 +233,7 @@ def test_a_failed_call_poisons_the_mount_until_reset():
     m.rec.copy_(torch.from_numpy(m.rec0))
     m.mount.reset()
     assert not m.mount.needs_reset
+    args[0] = _dev(inp.qkv)  # the conv ran in place on the failed call's qkv
     m.mount.delta(layer, *args, rows=rows)
     torch.cuda.synchronize()
     m.mount.status()
