@@ -150,7 +150,7 @@ cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st);
 // chunked prefill: workspace sections (bytes from the workspace start)
 struct GdnPrefillPlan {
   int64_t nchunks;
-  size_t off_W, off_Qg, off_Kt, off_M, off_U, off_gl, bytes;
+  size_t off_Ac, off_Pc, off_Kt, off_M, off_U, bytes;
 };
 bool gdn_prefill_serves(const hb_gdn_shape& s);
 GdnPrefillPlan gdn_prefill_plan(const hb_gdn_shape& s, int64_t rows);
