@@ -251,19 +251,30 @@ __global__ void __launch_bounds__(PREP_THREADS, 1)
       // any region is written again
       if (tid == 0) tma_store_wait_read();
       __syncthreads();
+      // sums of squares of all 32 rows first, then the butterflies of all rows
+      // interleaved (independent shuffles pipeline; a chain per row does not)
+      float inv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (t0 + (warp & 1) * 32 + i >= p.rows) x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        inv[i] = x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
+      }
+      if (ten < 2 && p.l2) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) inv[i] += __shfl_xor_sync(0xFFFFFFFFu, inv[i], o);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) inv[i] = rsqrtf(inv[i] + p.eps);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) inv[i] = 1.f;
+      }
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int r = (warp & 1) * 32 + i;
-        if (t0 + r >= p.rows) x[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        float inv = 1.f;
-        if (ten < 2 && p.l2) {
-          float ss = x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-          inv = 1.f / sqrtf(ss + p.eps);
-        }
-        const uint2 w = make_uint2(pack_bf16x2(x[i].x * inv, x[i].y * inv),
-                                   pack_bf16x2(x[i].z * inv, x[i].w * inv));
+        const uint2 w = make_uint2(pack_bf16x2(x[i].x * inv[i], x[i].y * inv[i]),
+                                   pack_bf16x2(x[i].z * inv[i], x[i].w * inv[i]));
         *reinterpret_cast<uint2*>(dst + sw_off(row_off + r, lane * 4, 16384)) = w;
       }
     }
