@@ -31,11 +31,12 @@
 //    blockdiag(M0, M1) [W0; W1] gives M W.  It writes Ac, Pc, Kt, M and U
 //    (bf16) as the scan's shared-memory tile images.
 //  * gdn_scan, one CTA per (value head, half of dv), sequential over chunks:
-//    the state is the bf16 operand in shared memory; per chunk one MMA group
-//    Ac S0 (onto Kt^T U) and [Pc; 0] S0 (onto [M; 0] U) into TMEM, then the
-//    new state is read back, rounded to bf16 for the next chunk, while two
-//    warps store the chunk's output.  Chunk tiles stream in by bulk copies
-//    two chunks ahead.
+//    the state is the bf16 operand in shared memory (two buffers, alternate
+//    chunks); per chunk Ac S0 (onto Kt^T U) into TMEM is the only product on
+//    the chain: the new state is read back and rounded to bf16 for the next
+//    chunk while Pc S0 (onto M U, an M = 64 accumulator) runs and four warps
+//    store the chunk's output.  Chunk tiles stream in by bulk copies two
+//    chunks ahead, prefetched into L2 six chunks ahead.
 // MMA operands are bf16, accumulators f32; the result is not the bits of the
 // sequential recurrence (as for the reference's own chunked kernel) and is
 // held to a relative Frobenius tolerance.
@@ -169,7 +170,8 @@ HB_DEV void inverse_block(const float* A, float* T, float* X, int i, int j) {
 // A persistent CTA per SM walks the (chunk, key head) tiles in chunk order.
 // All 32 row loads of a lane are issued before the first is used, the rows of
 // the next tile are then prefetched into L2 by four tensor prefetches, and a
-// tile's image stores drain while the next tile's rows load.
+// tile's last image stores drain while the next tile's rows load and its
+// first product runs.
 __global__ void __launch_bounds__(PREP_THREADS, 1)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tm_qkv, const PrepParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -247,9 +249,10 @@ __global__ void __launch_bounds__(PREP_THREADS, 1)
                      : "l"(src));
       }
       if (tid == 0 && tile + int(gridDim.x) < ntiles) prefetch_rows(tile + gridDim.x);
-      // the previous tile's image stores must have read their sources before
-      // any region is written again
-      if (tid == 0) tma_store_wait_read();
+      // SA is no store source, and SV's U images were read long ago (their
+      // group precedes Ac and Pc): the rows may be written before the
+      // previous tile's last stores have drained
+      if (tid == 0) store_wait_read_but<1>();
       __syncthreads();
       // sums of squares of all 32 rows first, then the butterflies of all rows
       // interleaved (independent shuffles pipeline; a chain per row does not)
@@ -311,6 +314,9 @@ __global__ void __launch_bounds__(PREP_THREADS, 1)
       G_s[warp * 64 + 2 * lane] = before + a0;
       G_s[warp * 64 + 2 * lane + 1] = s;
     }
+    // the previous tile's Ac and Pc stores must have read M's, W's and S2's
+    // regions before they are written again
+    if (tid == 0) tma_store_wait_read();
     __syncthreads();
     if (!mbar_wait(&bar[0], par)) record_status(p.status, kStatusTimeout);
     __syncthreads();
@@ -623,8 +629,8 @@ constexpr int S_MZ = 49152;       // M [64 rows][128 B]                         
 constexpr int S_KT = 57344;       // Kt [2 blocks][64 rows][128 B]     MN-major A (Kt^T)
 constexpr int S_UH = 73728;       // U columns vb*64.. [64 rows][128 B]             MN-major B
 constexpr int STAGE = 81920;
-constexpr int S_SB = 2 * STAGE;   // state bf16 [128 rows][128 B]                   MN-major B
-constexpr int S_OS = S_SB + 16384;  // output staging [2 buffers][4 warps][2 x [16 rows][128 B]]
+constexpr int S_SB = 2 * STAGE;   // state bf16, 2 x [128 rows][128 B] (alternate chunks) MN-major B
+constexpr int S_OS = S_SB + 2 * 16384;  // output staging [2 buffers][4 warps][2 x [16 rows][128 B]]
 constexpr int S_BAR = S_OS + 2 * 16384;
 constexpr int NSBAR = 10;
 constexpr int S_SMEM = S_BAR + NSBAR * 8 + 16 + 1024;
@@ -726,13 +732,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
       constexpr uint32_t id_s = idesc_bf16(128, BV, false, true);  // state: M = key dim
       constexpr uint32_t id_t = idesc_bf16(128, BV, true, true);   // Kt^T (MN-major A)
       constexpr uint32_t id_o = idesc_bf16(64, BV, false, true);   // outputs: M = 64 positions
-      const uint64_t sbd = sw128_desc(smem_u32(smem + S_SB), 8192, 1024);
       for (int c = 0; c < nc; ++c) {
         const int s = c & 1;
         const uint32_t st = smem_u32(smem + s * STAGE);
         const uint64_t acd = sw128_desc(st + S_AC, 16, 1024), pcd = sw128_desc(st + S_PC, 16, 1024),
                        mzd = sw128_desc(st + S_MZ, 16, 1024), ktd = sw128_desc(st + S_KT, 8192, 1024),
-                       uhd = sw128_desc(st + S_UH, 8192, 1024);
+                       uhd = sw128_desc(st + S_UH, 8192, 1024),
+                       sbd = sw128_desc(smem_u32(smem + S_SB + (c & 1) * 16384), 8192, 1024);
         const uint32_t s_next = tmem + ((c + 1) & 1) * 64, o_buf = tmem + 128 + (c & 1) * 64;
         if (!wait(FULL + s, (c >> 1) & 1)) break;
         if (c >= 2 && !wait(O_FREE + (c & 1), ((c >> 1) - 1) & 1)) break;
@@ -745,15 +751,17 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
         }
         if (!wait(SB_READY, c & 1)) break;
         fence_after_sync();
-        // the chain: Ac S0 and Pc S0, both reading the bf16 state
+        // the chain: Ac S0, then the output's Pc S0 off it (the next state is
+        // written into the other bf16 buffer while this one is still read)
 #pragma unroll
-        for (int kk = 0; kk < DK / 16; ++kk) {
+        for (int kk = 0; kk < DK / 16; ++kk)
           mma_bf16_ss(s_next, desc_add(acd, (kk >> 2) * 16384 + (kk & 3) * 32),
                       desc_add(sbd, kk * 2048), id_s, true);
+        mma_commit(&bar[S_DONE]);
+#pragma unroll
+        for (int kk = 0; kk < DK / 16; ++kk)
           mma_bf16_ss(o_buf, desc_add(pcd, (kk >> 2) * 8192 + (kk & 3) * 32),
                       desc_add(sbd, kk * 2048), id_o, true);
-        }
-        mma_commit(&bar[S_DONE]);
         mma_commit(&bar[O_DONE + (c & 1)]);
         mma_commit(&bar[EMPTY + s]);
       }
@@ -763,10 +771,13 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     const int row = tid;
     const uint32_t lq = uint32_t(warp * 32) << 16;
     float* sp = p.state + (int64_t(h) * DK + row) * DV + vb * BV;
-    auto put_bf16 = [&](const float* v) {  // one state row into the bf16 operand
+    // one state row into the bf16 operand of chunk `cn`; the buffer was last
+    // read by chunk cn - 2's products, which completed before S_DONE of cn - 1
+    auto put_bf16 = [&](const float* v, int cn) {
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(smem + S_SB + sw_chunk(row, ch)) = pack8(v + ch * 8);
+        *reinterpret_cast<uint4*>(smem + S_SB + (cn & 1) * 16384 + sw_chunk(row, ch)) =
+            pack8(v + ch * 8);
       fence_proxy_async_smem();
       mbar_arrive(&bar[SB_READY]);
     };
@@ -780,7 +791,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
         v[4 * i + 2] = x.z;
         v[4 * i + 3] = x.w;
       }
-      put_bf16(v);
+      put_bf16(v, 0);
     }
     bool ok = true;
     for (int c = 0; c < nc && ok; ++c) {
@@ -799,7 +810,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
           v[32 + i] = __uint_as_float(b[i]);
         }
         fence_before_sync();
-        put_bf16(v);
+        put_bf16(v, c + 1);
       } else if (ok) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
