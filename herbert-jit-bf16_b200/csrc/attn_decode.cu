@@ -700,8 +700,13 @@ cudaError_t launch(DecodeParams p, int units_z, bool single, int64_t max_n, cuda
 
 // Positions per split: enough CTAs to cover the SMs several times over
 // (load balance across units of unequal length), at least two tiles each.
-int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms) {
-  const int64_t target = int64_t(num_sms) * 8;
+int decode_chunk(int64_t total_positions, int64_t units, int64_t max_n, int num_sms) {
+  // Units of unequal length (a ragged batch) are balanced by about eight
+  // waves of splits; when every unit has max_n positions (one sequence, or a
+  // batch of equal lengths) a single wave of long splits streams the same
+  // bytes with one CTA set-up and a short merge per SM.
+  const bool uniform = total_positions >= mul_sat(units, max_n);
+  const int64_t target = int64_t(num_sms) * (uniform ? 1 : 8);
   int64_t c = (total_positions + target - 1) / target;
   c = (c + kTile - 1) / kTile * kTile;
   if (c < 2 * kTile) c = 2 * kTile;

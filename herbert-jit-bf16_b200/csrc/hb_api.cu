@@ -117,7 +117,7 @@ DecodePlan plan_decode(const hb_attn_spec* s, int64_t nseq, int64_t rows, int64_
   DecodePlan p;
   const int64_t hkv = s->heads / s->gqa;
   p.units = mul_sat(mul_sat(nseq, rows), hkv);
-  p.chunk = decode_chunk(mul_sat(total_positions, hkv), max_n, device_sms());
+  p.chunk = decode_chunk(mul_sat(total_positions, hkv), p.units, max_n, device_sms());
   p.nsplit = int((max_n + p.chunk - 1) / p.chunk);
   p.counters_off = kWsHeader;
   p.partials_off = p.counters_off + align256(size_t(mul_sat(p.units, sizeof(unsigned))));

@@ -53,7 +53,9 @@ bool decode_serves(int64_t head_dim, int64_t gqa);
 // Device address of the static scratch of hb_attn_decode_noalloc on the
 // current device (looked up on the first call per device and context).
 cudaError_t noalloc_scratch(void** ptr);
-int decode_chunk(int64_t total_positions, int64_t max_n, int num_sms);
+// Positions per split of the decode kernel: `total_positions` summed over
+// the `units` (row, KV head) pairs, each at most max_n long.
+int decode_chunk(int64_t total_positions, int64_t units, int64_t max_n, int num_sms);
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
 // The tensor-core form for one sequence of at most 16 x 128 positions at
