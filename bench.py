@@ -70,10 +70,11 @@ L2_BYTES = 126 << 20
 # own command measured them.  ncu runs outside the timed run (a capture
 # replays kernels and is never timed), so the figures are constants here;
 # batch is scaled from the n = 2048 decode capture by the bytes processed,
-# gdn covers the chunked prefill's kernels of one prefill, and None marks a
-# configuration whose launch was not captured.
-NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 500_502_272,
-               "batch": 4_452_000_000, "cp": None, "front": 56_784_128,
+# gdn covers the chunked prefill's kernels of one prefill, cp is the
+# single-GPU prefill of the whole sequence (the ring's hops are other
+# launches), and None marks a configuration whose launch was not captured.
+NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 504_317_696,
+               "batch": 4_452_000_000, "cp": 39_260_000_000, "cp_hops": None, "front": 56_784_128,
                "gdn_front": 213_700_000, "gdn_norm": 153_000_000, "snapshot": None,
                "mixers": None}
 
@@ -463,6 +464,12 @@ class CpWorkload(Workload):
 CP_HOPS_RANKS, CP_HOPS_RANK = 8, 3
 
 
+def cp_hops_chunk():
+    """Chunk of the emulated ring: CP_S / (2 x 8) unless HB_CP_HOPS_CHUNK sets
+    a smaller case (for a full ncu capture of one hop)."""
+    return int(os.environ.get("HB_CP_HOPS_CHUNK", CP_S // (2 * CP_HOPS_RANKS)))
+
+
 class CpHopsWorkload(Workload):
     """The hop kernel of the context-parallel ring on one GPU: rank
     CP_HOPS_RANK of an emulated ring of CP_HOPS_RANKS over the 131072-token
@@ -475,7 +482,7 @@ class CpHopsWorkload(Workload):
         import torch
         import herbert_b200 as hb
         P, r = CP_HOPS_RANKS, CP_HOPS_RANK
-        c = int(os.environ.get("HB_CP_HOPS_CHUNK", CP_S // (2 * P)))
+        c = cp_hops_chunk()
         self.hb, self.chunk = hb, c
         self.cp = hb.cp_spec(P, r, c)
         gen = torch.Generator(device=device).manual_seed(seed)
@@ -887,8 +894,8 @@ def config_of(cfg, world):
     elif cfg == "cp_hops":
         d = dict(workload="one rank's hops of an emulated context-parallel ring on one GPU "
                  "(the hop kernel of BASELINE configs[4])", seq_len=CP_S, **attn,
-                 ring_ranks=CP_HOPS_RANKS, rank=CP_HOPS_RANK, chunk=CP_S // (2 * CP_HOPS_RANKS),
-                 l2="inputs larger than L2 (q rows 268 MB, 8 shards of 67 MB)")
+                 ring_ranks=CP_HOPS_RANKS, rank=CP_HOPS_RANK, chunk=cp_hops_chunk(),
+                 l2="inputs larger than L2 (q rows 268 MB, 8 shards of 67 MB at chunk 8192)")
     elif cfg == "front":
         d = dict(workload="attention front end: q/k GemmaRMSNorm head norms + partial RoPE "
                  "(64 of 256) + KV append, one 4096-row block", rows=PREFILL_S,
@@ -1107,7 +1114,7 @@ def run_ours(args):
                          "peak_source": pk["source"] + (
                              ("" if unit != "TFLOP/s" else
                               " sustained (timed region >= 0.5 s)" if sustained else " burst")),
-                         "traffic": NCU_TRAFFIC.get(cfg)},
+                         "traffic": None if cfg == "cp" and world > 1 else NCU_TRAFFIC.get(cfg)},
             "e2e": {"value": round(value_of(total_work, t_e2e / args.steps, wl.units), 4),
                     "unit": wl.units, "h2d_bytes_per_step": int(wl.h2d),
                     "d2h_bytes_per_step": int(wl.d2h)},
