@@ -18,8 +18,8 @@
 // each way (shared memory in between): with one warp per SM, per-thread
 // loads of 128 strided rows left the step latency-bound on memory
 // parallelism (a loads-and-stores-only kernel took 9 us per step, the TMA
-// tile takes one request).  The L2 norms of q and k run while the tile is
-// in flight.
+// tile takes one request).  The first position's L2 norms run while the
+// tile is in flight.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -44,24 +44,6 @@ struct GdnParams {
   int* status;  // device status word: the caller's workspace or the per-device word
 };
 
-// Sequential L2 of one head held in shared memory: sum of squares left to
-// right, + eps, sqrt, 1/x (delta.rs:28-62).
-template <int N>
-HB_DEV float l2_inverse(const float* x, float eps) {
-  const float4* x4 = reinterpret_cast<const float4*>(x);
-  float sum = 0.f;
-#pragma unroll
-  for (int i = 0; i < N / 4; ++i) {
-    const float4 v = x4[i];
-    sum = __fadd_rn(sum, __fmul_rn(v.x, v.x));
-    sum = __fadd_rn(sum, __fmul_rn(v.y, v.y));
-    sum = __fadd_rn(sum, __fmul_rn(v.z, v.z));
-    sum = __fadd_rn(sum, __fmul_rn(v.w, v.w));
-  }
-  sum = __fadd_rn(sum, eps);
-  return __fdiv_rn(1.0f, __fsqrt_rn(sum));
-}
-
 template <int HKD>
 __global__ void __launch_bounds__(32)
     gdn_decode_kernel(const __grid_constant__ CUtensorMap tmS, const GdnParams p) {
@@ -79,14 +61,32 @@ __global__ void __launch_bounds__(32)
   if (lane == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
+    sm100::prefetch_tmap(&tmS);
   }
-  // Launched with programmatic stream serialization.  This kernel is the
-  // only one that lets a successor start early, and it never writes qkv,
-  // beta or decay, so the first position's inputs are read (and
-  // L2-normalised) at once -- overlapping the previous step's tail when
-  // that step is this kernel; the state is touched only after
-  // griddepcontrol.wait, i.e. after the previous kernel completed, and the
-  // next step is released only then (one step in flight ahead, not a chain).
+  // Launched with programmatic stream serialization: the CTAs are made
+  // resident while the previous kernel finishes, and until
+  // griddepcontrol.wait they only prefetch into L2 (the state tile and the
+  // first position's lines; a prefetch cannot change what a later load
+  // returns).  Every load follows the wait: the previous kernel may be the
+  // front end that writes qkv, beta and decay.
+  {
+    const float* row = p.qkv;
+    if (lane == 0) sm100::tma_prefetch_l2_2d(&tmS, col0, h * HKD);
+    if (lane < HKD / 32) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(row + int64_t(kh) * HKD + lane * 32));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(row + key + int64_t(kh) * HKD + lane * 32));
+    }
+    if (lane == 4) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + 2 * key + int64_t(h) * p.hvd + col0));
+    if (lane == 5) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.beta + h));
+    if (lane == 6) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.decay + h));
+  }
+  __syncwarp();
+  griddep_wait();
+  griddep_launch_dependents();
+  if (lane == 0) {  // the state tile, in flight while the first position's norms run
+    mbar_arrive_expect_tx(&bar, HKD * 32 * 4);
+    sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
+  }
   bool loaded = false;
   float s[HKD];
 
@@ -119,12 +119,6 @@ __global__ void __launch_bounds__(32)
     }
     __syncwarp();
     if (!loaded) {  // the state tile (first position only)
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      asm volatile("griddepcontrol.launch_dependents;" :::);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&bar, HKD * 32 * 4);
-        sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
-      }
       if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar, 0))) {
         // the call's outputs are not written; the status word tells the caller
         if (lane == 0) record_status(p.status, kStatusTimeout);
@@ -136,39 +130,14 @@ __global__ void __launch_bounds__(32)
       loaded = true;
     }
 
-    const float4* k4 = reinterpret_cast<const float4*>(kn);
-    const float4* q4 = reinterpret_cast<const float4*>(qn);
-    // pass 1: decay, then read kv = S^T k
-    float kv = 0.f;
-#pragma unroll
-    for (int k = 0; k < HKD / 4; ++k) {
-      const float4 kk = k4[k];
-      const float kw[4] = {kk.x, kk.y, kk.z, kk.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float r = __fmul_rn(s[4 * k + e], decay);
-        s[4 * k + e] = r;
-        kv = __fadd_rn(kv, __fmul_rn(r, kw[e]));
-      }
-    }
-    const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
-    // pass 2: write S += k delta, read out = S^T (q scale)
-    float o = 0.f;
-#pragma unroll
-    for (int k = 0; k < HKD / 4; ++k) {
-      const float4 kk = k4[k], qq = q4[k];
-      const float kw[4] = {kk.x, kk.y, kk.z, kk.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float r = __fadd_rn(s[4 * k + e], __fmul_rn(kw[e], delta));
-        s[4 * k + e] = r;
-        o = __fadd_rn(o, __fmul_rn(r, qw[e]));
-      }
-    }
+    const float o = gdn_step_column<HKD>(s, kn, qn, v, beta, decay);
     p.out[t * value + int64_t(h) * p.hvd + col] = o;
     __syncwarp();
   }
-  if (!loaded) return;  // no position (the host refuses empty calls): state untouched
+  if (!loaded) {  // no position (the host refuses empty calls): state untouched
+    mbar_wait(&bar, 0);  // the copy in flight lands before the CTA ends (bounded)
+    return;
+  }
 #pragma unroll
   for (int kd = 0; kd < HKD; ++kd) st[kd * 32 + lane] = s[kd];
   sm100::fence_proxy_async_smem();

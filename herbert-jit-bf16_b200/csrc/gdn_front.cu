@@ -207,16 +207,20 @@ struct __align__(128) FrontSmem {
   int abort;
 };
 
-// One gate task (delta.rs:290-389).
+// The gates of one (row, V head) from its a, b, dt_bias and a_log
+// (delta.rs:290-389).
+HB_DEV void gate_values(float a, float b, uint16_t dt_bias, float a_log, float& beta, float& decay) {
+  beta = __fdiv_rn(1.0f, __fadd_rn(expf_ref(neg(b)), 1.0f));
+  float dt = __fadd_rn(a, bf16_to_f32(dt_bias));
+  if (!(dt > 20.0f)) dt = logf_ref(__fadd_rn(expf_ref(dt), 1.0f));
+  decay = expf_ref(__fmul_rn(neg(expf_ref(a_log)), dt));
+}
+
+// One gate task: row task / nv, V head task % nv.
 __device__ void gate_task(const FrontParams& p, int task) {
   const int row = task / p.nv, h = task - row * p.nv;
   const float* r = p.ab + static_cast<size_t>(row) * 2 * p.nv;
-  const float e = __fadd_rn(expf_ref(neg(r[p.nv + h])), 1.0f);
-  p.beta[task] = __fdiv_rn(1.0f, e);
-  float dt = __fadd_rn(r[h], bf16_to_f32(p.dt_bias[h]));
-  if (!(dt > 20.0f)) dt = logf_ref(__fadd_rn(expf_ref(dt), 1.0f));
-  const float m = neg(expf_ref(p.a_log[h]));
-  p.decay[task] = expf_ref(__fmul_rn(m, dt));
+  gate_values(r[h], r[p.nv + h], p.dt_bias[h], p.a_log[h], p.beta[task], p.decay[task]);
 }
 
 __global__ void __launch_bounds__(kFrontThreads)
@@ -360,6 +364,36 @@ HB_DEV uint32_t bf16x2_cvtne_fast(float lo, float hi) {
   return bf16x2_cvtne(lo, hi);
 }
 
+// 1 / sqrt(sum x^2 / dim + eps) of one row in the vector kernel's order,
+// dim = 16 NB (NB <= 8), every lane of the warp taking part.  Lane (l, h) =
+// (lane % 16, lane / 16) enters with xv[k] = x[16 b + l], b = 2h + (k & 1) +
+// 4 (k >> 1) (0 where b >= NB): zmm lane l of blocks 2h, 2h + 1, 2h + 4,
+// 2h + 5, chains 2h and 2h + 1 of the sum of squares (block b feeds chain
+// b % 4; absent chains stay +0, which adds exactly).  Every lane returns the
+// same value.
+template <int NB>
+HB_DEV float norm_inverse_vec(const float (&xv)[4], float eps) {
+  const int h = (threadIdx.x & 31) >> 4;
+  float acc[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    const int b = 2 * h + (k & 1) + 4 * (k >> 1);
+    if (b < NB) acc[k & 1] = __fmaf_rn(xv[k], xv[k], acc[k & 1]);
+  }
+  // chains added in order: ((c0 + c1) + c2) + c3, on the lanes l < 16
+  const float c2 = __shfl_down_sync(0xFFFFFFFFu, acc[0], 16);
+  const float c3 = __shfl_down_sync(0xFFFFFFFFu, acc[1], 16);
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), c2), c3);
+  // hsum: (l, l+8), (l, l+4), then the two hadds
+  s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 8));
+  s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 4));
+  s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 1));
+  s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 2));
+  s = __shfl_sync(0xFFFFFFFFu, s, 0);
+  s = __fadd_rn(__fdiv_rn(s, static_cast<float>(16 * NB)), eps);
+  return __fdiv_rn(1.0f, __fsqrt_rn(s));
+}
+
 // The vector kernel's form at dim = 16 NB (NB <= 8).  A warp walks rows
 // (row, V head) with a stride of the grid's warps, the weights held in
 // registers.  Lane (l, h) = (lane % 16, lane / 16) holds zmm lane l of
@@ -382,26 +416,14 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_vec(const NormPar
     const size_t base = static_cast<size_t>(row) * dim;
     const float* x = p.x + base;
     const float* z = p.z + base;
-    float xv[4], zv[4], acc[2] = {0.0f, 0.0f};
+    float xv[4], zv[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
       const int b = 2 * h + (k & 1) + 4 * (k >> 1);
       xv[k] = b < NB ? x[16 * b + l] : 0.0f;
       zv[k] = b < NB ? z[16 * b + l] : 0.0f;
-      if (b < NB) acc[k & 1] = __fmaf_rn(xv[k], xv[k], acc[k & 1]);
     }
-    // chains added in order: ((c0 + c1) + c2) + c3, on the lanes l < 16
-    const float c2 = __shfl_down_sync(0xFFFFFFFFu, acc[0], 16);
-    const float c3 = __shfl_down_sync(0xFFFFFFFFu, acc[1], 16);
-    float s = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), c2), c3);
-    // hsum: (l, l+8), (l, l+4), then the two hadds
-    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 8));
-    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 4));
-    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 1));
-    s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, 2));
-    s = __shfl_sync(0xFFFFFFFFu, s, 0);
-    s = __fadd_rn(__fdiv_rn(s, static_cast<float>(dim)), p.eps);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(s));
+    const float inv = norm_inverse_vec<NB>(xv, p.eps);
     // elements k and k + 1 on paired lanes (absent blocks compute on zeros
     // and are not stored)
 #pragma unroll
@@ -449,6 +471,210 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
   }
 }
 
+// ------------------------------------------------ one-row DeltaNet layer
+//
+// A decode step of a whole DeltaNet layer in one launch: conv + SiLU of the
+// row, the gates, the L2 step, the recurrence and the gated norm, each in
+// the operation order of its own kernel above (and of the reference), so
+// the results are the three-launch path's bits.  CTA h = V head h, 128
+// threads: thread t owns q / k channel t of the head's key head, v channel
+// t and state column t.  The V heads of one key head read the same q / k
+// inputs and conv state, and the first of them writes them back in place:
+// they form one cluster, every thread arrives on the cluster barrier once
+// its reads are done and waits on it before any write.  Launched with
+// programmatic stream serialization: before griddepcontrol.wait only L2
+// prefetches (the state tile and the row's lines).
+
+constexpr int kRowThreads = 128;
+
+struct RowParams {
+  float* qkv;                   // [conv] conv + SiLU in place
+  float* conv_state;            // [conv][4]
+  const uint16_t* conv_weight;  // [conv][4] bf16
+  const float* ab;              // [2 nv]
+  const uint16_t* dt_bias;      // [nv] bf16
+  const float* a_log;           // [nv]
+  const float* z;               // [nv hvd]
+  const uint16_t* norm_weight;  // [hvd] bf16
+  uint16_t* out;                // [nv hvd] bf16
+  float* out_f32;               // [nv hvd] or nullptr
+  int nk, nv;
+  float l2_eps, scale, norm_eps;
+  int* status;
+};
+
+HB_DEV void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+HB_DEV void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// (s1 w0 + s2 w1) + (s3 w2 + x w3): the vector kernel's sum at ck = 4 for a
+// row whose taps are the state's last three inputs and x.
+HB_DEV float conv4_sum(const float4& st, uint2 w, float x) {
+  const float a = __fadd_rn(__fmul_rn(st.y, bf16lo(w.x)), __fmul_rn(st.z, bf16hi(w.x)));
+  const float b = __fadd_rn(__fmul_rn(st.w, bf16lo(w.y)), __fmul_rn(x, bf16hi(w.y)));
+  return __fadd_rn(a, b);
+}
+
+template <int HKD, int NB>
+__global__ void __launch_bounds__(kRowThreads, 1)
+    gdn_row_kernel(const __grid_constant__ CUtensorMap tmS, const RowParams p) {
+  constexpr int HVD = 16 * NB;
+  static_assert(HKD <= kRowThreads && HVD <= kRowThreads && HVD % 32 == 0, "one thread per column");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  float* st = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* qn = st + HKD * HVD;  // [HKD] q, then q inv_q scale
+  float* kn = qn + HKD;        // [HKD] k, then k inv_k
+  float* os = kn + HKD;        // [HVD] recurrence output
+  float* misc = os + HVD;      // inv_q, inv_k, beta, decay
+  uint64_t* bar = reinterpret_cast<uint64_t*>(misc + 4);
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int h = blockIdx.x, ratio = p.nv / p.nk, kh = h / ratio;
+  const bool writer = h % ratio == 0;  // writes the key head's q / k channels back
+  const int64_t key = int64_t(p.nk) * HKD;
+  const int64_t cq = int64_t(kh) * HKD + tid, ck = key + cq, cv = 2 * key + int64_t(h) * HVD + tid;
+  const bool has_qk = tid < HKD, has_v = tid < HVD;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    sm100::prefetch_tmap(&tmS);
+    sm100::tma_prefetch_l2_2d(&tmS, 0, h * HKD);
+  }
+  if (has_qk && lane % 8 == 0) {  // conv state: 8 channels per line; q, k, weights a line per warp
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cq * 4));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + ck * 4));
+    if (lane == 0) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + cq));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + ck));
+    }
+    if (lane % 16 == 0) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + cq * 4));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + ck * 4));
+    }
+  }
+  if (has_v && lane % 8 == 0) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cv * 4));
+    if (lane == 0) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + cv));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.z + int64_t(h) * HVD + tid));
+    }
+    if (lane % 16 == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + cv * 4));
+  }
+  __syncthreads();  // the barrier's initialisation is visible
+  griddep_wait();
+  griddep_launch_dependents();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, HKD * HVD * 4);
+    sm100::tma_load_2d(st, &tmS, bar, 0, h * HKD);
+  }
+
+  // every load of the row, then the cluster arrival: after it the writer
+  // may overwrite the shared inputs
+  float4 sq = make_float4(0.f, 0.f, 0.f, 0.f), sk = sq, sv = sq;
+  uint2 wq = make_uint2(0u, 0u), wk = wq, wv = wq;
+  float xq = 0.f, xk = 0.f, xv = 0.f, zz = 0.f, nw = 0.f;
+  if (has_qk) {
+    sq = *reinterpret_cast<const float4*>(p.conv_state + cq * 4);
+    sk = *reinterpret_cast<const float4*>(p.conv_state + ck * 4);
+    wq = *reinterpret_cast<const uint2*>(p.conv_weight + cq * 4);
+    wk = *reinterpret_cast<const uint2*>(p.conv_weight + ck * 4);
+    xq = p.qkv[cq];
+    xk = p.qkv[ck];
+  }
+  if (has_v) {
+    sv = *reinterpret_cast<const float4*>(p.conv_state + cv * 4);
+    wv = *reinterpret_cast<const uint2*>(p.conv_weight + cv * 4);
+    xv = p.qkv[cv];
+    zz = p.z[int64_t(h) * HVD + tid];
+    nw = bf16_to_f32(p.norm_weight[tid]);
+  }
+  float ga = 0.f, gb = 0.f, a_log = 0.f;
+  uint16_t dtb = 0;
+  if (tid == 64) {
+    ga = p.ab[h];
+    gb = p.ab[p.nv + h];
+    dtb = p.dt_bias[h];
+    a_log = p.a_log[h];
+  }
+  cluster_arrive_release();
+
+  float yq = 0.f, yk = 0.f, yv = 0.f;
+  if (has_qk) {
+    silu_poly2(conv4_sum(sq, wq, xq), conv4_sum(sk, wk, xk), yq, yk);
+    qn[tid] = yq;
+    kn[tid] = yk;
+  }
+  if (has_v) {
+    float unused;
+    const float g = conv4_sum(sv, wv, xv);
+    silu_poly2(g, g, yv, unused);
+  }
+  __syncthreads();
+  if (tid == 0 || tid == 32) misc[tid >> 5] = l2_inverse<HKD>(tid == 0 ? qn : kn, p.l2_eps);
+  if (tid == 64) gate_values(ga, gb, dtb, a_log, misc[2], misc[3]);
+  __syncthreads();
+  if (has_qk) {
+    qn[tid] = __fmul_rn(__fmul_rn(qn[tid], misc[0]), p.scale);
+    kn[tid] = __fmul_rn(kn[tid], misc[1]);
+  }
+  // every V head of the key head has read the inputs (they arrived before
+  // their norms, so this rarely waits): the conv's results go back in place
+  // now, and their registers are free for the state column
+  cluster_wait_acquire();
+  if (has_qk && writer) {
+    p.qkv[cq] = yq;
+    p.qkv[ck] = yk;
+    *reinterpret_cast<float4*>(p.conv_state + cq * 4) = make_float4(sq.y, sq.z, sq.w, xq);
+    *reinterpret_cast<float4*>(p.conv_state + ck * 4) = make_float4(sk.y, sk.z, sk.w, xk);
+  }
+  if (has_v) {
+    p.qkv[cv] = yv;
+    *reinterpret_cast<float4*>(p.conv_state + cv * 4) = make_float4(sv.y, sv.z, sv.w, xv);
+  }
+  const bool late = __syncthreads_or(!mbar_wait(bar, 0));  // the state tile
+
+  if (!late) {
+    if (has_v) {
+      float s[HKD];
+#pragma unroll
+      for (int kd = 0; kd < HKD; ++kd) s[kd] = st[kd * HVD + tid];
+      os[tid] = gdn_step_column<HKD>(s, kn, qn, yv, misc[2], misc[3]);
+#pragma unroll
+      for (int kd = 0; kd < HKD; ++kd) st[kd * HVD + tid] = s[kd];
+    }
+    sm100::fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      sm100::tma_store_2d(&tmS, st, 0, h * HKD);
+      sm100::tma_store_commit();
+    }
+    // the gated norm: every warp forms the row's inverse (the same bits)
+    // and finishes its own columns
+    float xs[4];
+    const int l = lane & 15, hh = lane >> 4;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int b = 2 * hh + (k & 1) + 4 * (k >> 1);
+      xs[k] = b < NB ? os[16 * b + l] : 0.0f;
+    }
+    const float inv = norm_inverse_vec<NB>(xs, p.norm_eps);
+    if (has_v) {
+      float s0, s1;
+      silu_poly2(zz, zz, s0, s1);
+      const float y = __fmul_rn(__fmul_rn(__fmul_rn(os[tid], inv), nw), s0);
+      const int64_t o = int64_t(h) * HVD + tid;
+      if (p.out_f32) p.out_f32[o] = y;
+      p.out[o] = static_cast<uint16_t>(bf16x2_cvtne_fast(y, y) & 0xFFFFu);
+    }
+  } else if (tid == 0) {
+    // the state and the outputs are not written (the conv results are, as
+    // the three-launch path's front end would have written them)
+    record_status(p.status, kStatusTimeout);
+    mbar_wait(bar, 0);  // a second bounded wait for the copy in flight
+  }
+  if (tid == 0 && !late) sm100::tma_store_wait_read();
+}
+
 }  // namespace
 
 bool gdn_front_serves(int64_t conv, int64_t ck) {
@@ -489,6 +715,84 @@ cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st) {
   }
   gdn_front_kernel<<<n_strips, kFrontThreads, smem, st>>>(tm, p);
   return cudaGetLastError();
+}
+
+bool gdn_row_serves(const hb_gdn_shape& s, int64_t ck) {
+  return ck == 4 && (s.hkd == 64 || s.hkd == 128) && s.hvd % 32 == 0 && s.hvd >= 32 &&
+         s.hvd <= kRowThreads && s.nk > 0 && s.nv % s.nk == 0 && s.nv / s.nk <= 8;
+}
+
+namespace {
+template <int HKD, int NB>
+cudaError_t launch_row(const CUtensorMap& tm, const RowParams& p, cudaLaunchConfig_t cfg) {
+  constexpr int HVD = 16 * NB;
+  const size_t smem = 1024 + size_t(HKD) * HVD * 4 + (2 * HKD + HVD + 4) * 4 + 8;
+  static bool attr = false;  // one flag per instantiation
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(gdn_row_kernel<HKD, NB>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  cfg.dynamicSmemBytes = smem;
+  return cudaLaunchKernelEx(&cfg, gdn_row_kernel<HKD, NB>, tm, p);
+}
+}  // namespace
+
+cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st) {
+  RowParams p;
+  p.qkv = L.qkv;
+  p.conv_state = L.conv_state;
+  p.conv_weight = L.conv_weight;
+  p.ab = L.ab;
+  p.dt_bias = L.dt_bias;
+  p.a_log = L.a_log;
+  p.z = L.z;
+  p.norm_weight = L.norm_weight;
+  p.out = L.out;
+  p.out_f32 = L.out_f32;
+  p.nk = int(L.shape.nk);
+  p.nv = int(L.shape.nv);
+  p.l2_eps = L.l2_eps;
+  p.scale = L.scale;
+  p.norm_eps = L.norm_eps;
+  p.status = L.status;
+  // the state as [nv*hkd rows][hvd columns] f32, one [hkd][hvd] tile per V head
+  CUtensorMap tm;
+  if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.state, uint64_t(L.shape.nv) * L.shape.hkd,
+                 uint64_t(L.shape.hvd), uint64_t(L.shape.hvd), uint32_t(L.shape.hkd),
+                 uint32_t(L.shape.hvd), CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(L.shape.nv));
+  cfg.blockDim = dim3(kRowThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;  // the V heads of one key head
+  attr[0].val.clusterDim.x = unsigned(L.shape.nv / L.shape.nk);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const int nb = int(L.shape.hvd / 16);
+  if (L.shape.hkd == 128) {
+    switch (nb) {
+      case 2: return launch_row<128, 2>(tm, p, cfg);
+      case 4: return launch_row<128, 4>(tm, p, cfg);
+      case 6: return launch_row<128, 6>(tm, p, cfg);
+      case 8: return launch_row<128, 8>(tm, p, cfg);
+    }
+  } else if (L.shape.hkd == 64) {
+    switch (nb) {
+      case 2: return launch_row<64, 2>(tm, p, cfg);
+      case 4: return launch_row<64, 4>(tm, p, cfg);
+      case 6: return launch_row<64, 6>(tm, p, cfg);
+      case 8: return launch_row<64, 8>(tm, p, cfg);
+    }
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_gdn_gated_norm(const GdnNormLaunch& L, cudaStream_t st) {

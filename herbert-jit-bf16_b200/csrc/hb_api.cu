@@ -624,8 +624,8 @@ static hb_status check_gdn_shape(const hb_gdn_shape* s) {
   return HB_OK;
 }
 
-hb_status hb_gdn_front(const hb_gdn_shape* s, const hb_gdn_front_call* c, void* ws, size_t ws_bytes,
-                       hb_stream_t stream) {
+static hb_status check_gdn_front(const hb_gdn_shape* s, const hb_gdn_front_call* c, void* ws,
+                                 size_t ws_bytes) {
   if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or front call is null");
   hb_status r = check_gdn_shape(s);
   if (r != HB_OK) return r;
@@ -639,7 +639,25 @@ hb_status hb_gdn_front(const hb_gdn_shape* s, const hb_gdn_front_call* c, void* 
       !c->beta || !c->decay)
     return fail(HB_ERR_ARG, "null DeltaNet front pointer");
   if (!aligned16(c->qkv)) return fail(HB_ERR_ARG, "qkv must be 16-byte aligned");
-  if ((r = check_ws(ws, ws_bytes, kWsHeader)) != HB_OK) return r;
+  return check_ws(ws, ws_bytes, kWsHeader);
+}
+
+static hb_status check_gdn_norm(const hb_gdn_shape* s, const hb_gdn_norm_call* c) {
+  if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or norm call is null");
+  hb_status r = check_gdn_shape(s);
+  if (r != HB_OK) return r;
+  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
+  if (c->rows >= (int64_t(1) << 40) / (s->nv * s->hvd)) return fail(HB_ERR_ARG, "DeltaNet block too long");
+  if (!c->x || !c->z || !c->weight || !c->out) return fail(HB_ERR_ARG, "null DeltaNet norm pointer");
+  if (!(c->eps >= 0.f) || c->eps == INFINITY) return fail(HB_ERR_ARG, "invalid gated-norm eps");
+  return HB_OK;
+}
+
+hb_status hb_gdn_front(const hb_gdn_shape* s, const hb_gdn_front_call* c, void* ws, size_t ws_bytes,
+                       hb_stream_t stream) {
+  hb_status r = check_gdn_front(s, c, ws, ws_bytes);
+  if (r != HB_OK) return r;
+  const int64_t conv = 2 * s->nk * s->hkd + s->nv * s->hvd;
   GdnFrontLaunch L;
   L.qkv = c->qkv;
   L.state = c->conv_state;
@@ -660,13 +678,8 @@ hb_status hb_gdn_front(const hb_gdn_shape* s, const hb_gdn_front_call* c, void* 
 }
 
 hb_status hb_gdn_gated_norm(const hb_gdn_shape* s, const hb_gdn_norm_call* c, hb_stream_t stream) {
-  if (!s || !c) return fail(HB_ERR_ARG, "DeltaNet shape or norm call is null");
-  hb_status r = check_gdn_shape(s);
+  hb_status r = check_gdn_norm(s, c);
   if (r != HB_OK) return r;
-  if (c->rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
-  if (c->rows >= (int64_t(1) << 40) / (s->nv * s->hvd)) return fail(HB_ERR_ARG, "DeltaNet block too long");
-  if (!c->x || !c->z || !c->weight || !c->out) return fail(HB_ERR_ARG, "null DeltaNet norm pointer");
-  if (!(c->eps >= 0.f) || c->eps == INFINITY) return fail(HB_ERR_ARG, "invalid gated-norm eps");
   GdnNormLaunch L;
   L.x = c->x;
   L.z = c->z;
@@ -713,3 +726,48 @@ hb_status hb_gdn_prefill(const hb_gdn_shape* s, const hb_gdn_call* c, void* ws, 
 }
 
 }  // extern "C"
+
+namespace hb {
+
+hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, const hb_gdn_call* gc,
+                        const hb_gdn_norm_call* nc, void* front_ws, size_t front_ws_bytes,
+                        int* status, hb_stream_t stream, bool* served) {
+  *served = false;
+  if (!s || !fc || !gc || !nc || fc->rows != 1 || gc->rows != 1 || nc->rows != 1 ||
+      !gdn_row_serves(*s, fc->ck) || gc->l2 != 1 || gc->qkv != fc->qkv || nc->x != gc->output)
+    return HB_OK;
+  // the three nodes' own checks, all before anything launches
+  hb_status r = check_gdn_front(s, fc, front_ws, front_ws_bytes);
+  if (r == HB_OK) r = check_gdn(s, gc);
+  if (r == HB_OK) r = check_gdn_norm(s, nc);
+  if (r != HB_OK) {
+    *served = true;
+    return r;
+  }
+  const uintptr_t mis16 = reinterpret_cast<uintptr_t>(fc->conv_state) | reinterpret_cast<uintptr_t>(gc->state);
+  if ((mis16 & 15) != 0 || (reinterpret_cast<uintptr_t>(fc->conv_weight) & 7) != 0) return HB_OK;
+  *served = true;
+  GdnRowLaunch L;
+  L.shape = *s;
+  L.qkv = fc->qkv;
+  L.conv_state = fc->conv_state;
+  L.conv_weight = fc->conv_weight;
+  L.ab = fc->ab;
+  L.dt_bias = fc->dt_bias;
+  L.a_log = fc->a_log;
+  L.state = gc->state;
+  L.z = nc->z;
+  L.norm_weight = nc->weight;
+  L.out = nc->out;
+  L.out_f32 = nc->out_f32;
+  L.l2_eps = gc->eps;
+  L.scale = 1.0f / std::sqrt(float(s->hkd));
+  L.norm_eps = nc->eps;
+  L.status = status;
+  cudaError_t e = launch_gdn_row(L, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "gdn_row launch");
+  return HB_OK;
+}
+
+}  // namespace hb
+

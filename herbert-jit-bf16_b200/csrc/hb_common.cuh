@@ -262,4 +262,62 @@ HB_DEV void record_status(int* status, int code) {
   if (status) atomicMax(status, code);
 }
 
+// Sequential L2 of one head held in shared memory: sum of squares left to
+// right, + eps, sqrt, 1/x (the L2 step of delta-l2-gates,
+// src/jit/target/x86/execution/delta.rs:28-62).
+template <int N>
+HB_DEV float l2_inverse(const float* x, float eps) {
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < N / 4; ++i) {
+    const float4 v = x4[i];
+    sum = __fadd_rn(sum, __fmul_rn(v.x, v.x));
+    sum = __fadd_rn(sum, __fmul_rn(v.y, v.y));
+    sum = __fadd_rn(sum, __fmul_rn(v.z, v.z));
+    sum = __fadd_rn(sum, __fmul_rn(v.w, v.w));
+  }
+  sum = __fadd_rn(sum, eps);
+  return __fdiv_rn(1.0f, __fsqrt_rn(sum));
+}
+
+// One position of the delta rule on the state column s[0..HKD) a thread
+// owns (delta-causal-recurrence, src/jit/target/x86/emit_recurrence.rs:108-217):
+// pass 1 decays the column and reads kv = S^T k, pass 2 adds k delta and
+// reads out = S^T q, each sum over kd in increasing order with separate
+// multiply and add.  kn and qn are the normalised k and the scaled q in
+// shared memory.
+template <int HKD>
+HB_DEV float gdn_step_column(float (&s)[HKD], const float* kn, const float* qn, float v, float beta,
+                             float decay) {
+  const float4* k4 = reinterpret_cast<const float4*>(kn);
+  const float4* q4 = reinterpret_cast<const float4*>(qn);
+  float kv = 0.f;
+#pragma unroll
+  for (int k = 0; k < HKD / 4; ++k) {
+    const float4 kk = k4[k];
+    const float kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float r = __fmul_rn(s[4 * k + e], decay);
+      s[4 * k + e] = r;
+      kv = __fadd_rn(kv, __fmul_rn(r, kw[e]));
+    }
+  }
+  const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
+  float o = 0.f;
+#pragma unroll
+  for (int k = 0; k < HKD / 4; ++k) {
+    const float4 kk = k4[k], qq = q4[k];
+    const float kw[4] = {kk.x, kk.y, kk.z, kk.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float r = __fadd_rn(s[4 * k + e], __fmul_rn(kw[e], delta));
+      s[4 * k + e] = r;
+      o = __fadd_rn(o, __fmul_rn(r, qw[e]));
+    }
+  }
+  return o;
+}
+
 }  // namespace hb

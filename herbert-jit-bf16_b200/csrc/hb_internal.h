@@ -136,6 +136,35 @@ struct GdnNormLaunch {
   float eps;
 };
 bool gdn_front_serves(int64_t conv, int64_t ck);
+// one decode row of a whole DeltaNet layer (conv + gates + L2 + recurrence
+// + gated norm) in one launch; beta, decay and the recurrence output are
+// not materialised
+struct GdnRowLaunch {
+  hb_gdn_shape shape;
+  float* qkv;                   // [conv] conv + SiLU in place
+  float* conv_state;            // [conv][4], 16-byte aligned
+  const uint16_t* conv_weight;  // [conv][4] bf16, 8-byte aligned
+  const float* ab;
+  const uint16_t* dt_bias;
+  const float* a_log;
+  float* state;                 // [nv][hkd][hvd], 16-byte aligned
+  const float* z;
+  const uint16_t* norm_weight;
+  uint16_t* out;
+  float* out_f32;
+  float l2_eps, scale, norm_eps;
+  int* status;
+};
+bool gdn_row_serves(const hb_gdn_shape& s, int64_t ck);
+cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st);
+// A one-row DeltaNet layer given as its three nodes' calls (front, L2 +
+// recurrence, gated norm): when the fused kernel serves it (*served), the
+// three calls' checks run first and then the one launch; otherwise nothing
+// happens and the caller runs the nodes.
+hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, const hb_gdn_call* gc,
+                        const hb_gdn_norm_call* nc, void* front_ws, size_t front_ws_bytes,
+                        int* status, hb_stream_t stream, bool* served);
+
 cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st);
 cudaError_t launch_gdn_gated_norm(const GdnNormLaunch& L, cudaStream_t st);
 

@@ -341,8 +341,6 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   fc.decay = m->decay;
   fc.rows = c->rows;
   fc.ck = m->desc.conv_kernel;
-  if ((r = hb_gdn_front(&shape, &fc, m->front_ws, kWsHeader, stream)) != HB_OK)
-    return after_entry(m, r, false);
   // the L2 of delta-l2-gates + delta-causal-recurrence (lowering.rs:935-986)
   hb_gdn_call gc{};
   gc.state = rt.recurrent_state;
@@ -353,8 +351,6 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   gc.rows = c->rows;
   gc.l2 = 1;
   gc.eps = kDeltaL2Eps;
-  if ((r = hb_gdn_prefill(&shape, &gc, m->gdn_ws, m->gdn_ws_bytes, stream)) != HB_OK)
-    return after_entry(m, r, true);
   // delta-gated-norm (lowering.rs:987-1010)
   hb_gdn_norm_call nc{};
   nc.x = m->rec_out;
@@ -364,5 +360,17 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
   nc.out_f32 = c->out_f32;
   nc.rows = c->rows;
   nc.eps = m->desc.norm_eps;
+  if (c->rows == 1) {
+    // a decode row: the three nodes in one launch where the shape allows
+    // (every node's checks first, so a refusal launches nothing)
+    bool served = false;
+    r = gdn_layer_row(&shape, &fc, &gc, &nc, m->front_ws, kWsHeader, static_cast<int*>(m->gdn_ws),
+                      stream, &served);
+    if (served) return after_entry(m, r, false);
+  }
+  if ((r = hb_gdn_front(&shape, &fc, m->front_ws, kWsHeader, stream)) != HB_OK)
+    return after_entry(m, r, false);
+  if ((r = hb_gdn_prefill(&shape, &gc, m->gdn_ws, m->gdn_ws_bytes, stream)) != HB_OK)
+    return after_entry(m, r, true);
   return after_entry(m, hb_gdn_gated_norm(&shape, &nc, stream), true);
 }
