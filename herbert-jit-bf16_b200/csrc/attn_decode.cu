@@ -726,6 +726,7 @@ size_t decode_partial_floats(int64_t gqa, int64_t head_dim) {
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st) {
   cudaError_t mma_err = cudaSuccess;
   if (launch_attn_decode_mma(L, st, &mma_err)) return mma_err;
+  if (launch_attn_decode_long(L, st, &mma_err)) return mma_err;
   DecodeParams p;
   p.seqs = L.seqs;
   p.one = L.one;

@@ -456,6 +456,448 @@ cudaError_t launch_mma(const DecodeLaunch& L, int nsplit, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, attn_decode_mma_kernel<G>, tk, tv, p);
 }
 
+// ----------------------------------------------- long sequences: split-KV
+//
+// One sequence beyond the cluster forms' reach: unit = (query row, KV head),
+// split = `chunk` positions (a multiple of 128) of the unit, grid = (splits,
+// KV heads, rows), about one CTA per SM.  A CTA loops over its 128-position
+// tiles:
+//   warp 4 (TMA)   K_t, V_t into a ring of three 64 KB slots (K_0 V_0 K_1 ...)
+//   warp 5 (MMA)   S_t^T = K_t Q^T into S buffer t % 2, then O_{t-1}^T =
+//                  V_{t-1}^T P_{t-1}^T into O buffer (t - 1) % 2: the scores of
+//                  the next tile are in flight while the softmax of this one runs
+//   warps 0-3      online softmax of tile t (one position per thread: the
+//                  running max M and sum L per head, P_t^T in bf16 into P
+//                  buffer t % 2), then O_{t-1} out of TMEM (one dim per
+//                  thread, dims d and d + 128) folded into f32 registers with
+//                  the correction 2^(M_acc - M_{t-1})
+// The CTA's (O, M, L) partial goes to the workspace in the layout of the
+// CUDA-core kernel's partials; the last CTA of the unit to arrive (atomic
+// counter, reset after use) merges them, divides, rounds to bf16 and
+// applies the gate with the reference's steps.  A unit with one split
+// finalises directly.
+
+constexpr int kThreadsL = 192;               // warps 0-3 softmax, 4 TMA, 5 MMA
+constexpr int L_SLOT = 65536;                // one K or V tile: 4 blocks [128][128 B]
+constexpr int L_OFF_Q = 3 * L_SLOT;          // Q^T: 4 blocks [16 rows][128 B]
+constexpr int L_OFF_P = L_OFF_Q + 8192;      // P^T: 2 buffers x 2 blocks [16][128 B]
+constexpr int L_OFF_RED = L_OFF_P + 8192;    // maxima [2][4 warps][16], then sums [2][4][16]
+constexpr int L_OFF_BAR = L_OFF_RED + 2 * 2 * 4 * 16 * 4;
+constexpr int L_SMEM = L_OFF_BAR + 256 + 1024;  // + alignment slack
+constexpr uint32_t L_TMEM_COLS = 128;        // S^T 2 x 16 columns, O^T 2 x 32
+enum LBar { L_FULL = 0, L_EMPTY = 3, L_S_FULL = 6, L_S_FREE = 8, L_P_READY = 10, L_O_FULL = 12,
+            L_O_FREE = 14, L_MERGE = 16, L_NBAR = 17 };
+
+struct DecodeLongParams {
+  const uint16_t* q;
+  uint16_t* out;
+  int64_t q_row, q_head, out_row;
+  int64_t gate_offset;  // < 0: no gate
+  int64_t past;         // row r sees past + r + 1 positions
+  int hkv, chunk, nsplit;
+  float scale_log2;
+  int* status;
+  unsigned* counters;   // one per unit
+  float* partials;      // [unit][split][G*HD + 2G rounded up to 4]
+};
+
+template <int G>
+__global__ void __launch_bounds__(kThreadsL, 1)
+    attn_decode_long_kernel(const __grid_constant__ CUtensorMap tmK,
+                            const __grid_constant__ CUtensorMap tmV, const DecodeLongParams p) {
+  constexpr int PSTRIDE = G * HDM + ((2 * G + 3) & ~3);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L_OFF_BAR);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + L_NBAR);
+  volatile int* flags = reinterpret_cast<volatile int*>(tslot + 1);  // [0] abort, [1] last
+  float* red = reinterpret_cast<float*>(smem + L_OFF_RED);
+
+  const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int64_t n = p.past + row + 1;  // positions this row sees
+  const int64_t p0 = int64_t(split) * p.chunk;
+  if (p0 >= n) return;  // beyond the row's last split: not counted
+  const int64_t p1 = min(n, p0 + p.chunk);
+  const int nt = int((p1 - p0 + BT - 1) / BT);
+  const int active = int((n + p.chunk - 1) / p.chunk);
+  const int unit = row * p.hkv + kh;
+  const int h0 = kh * G;
+  const uint16_t* qrow = p.q + int64_t(row) * p.q_row;
+
+  if (tid == 0) {
+    for (int i = 0; i < L_NBAR; ++i) {
+      // the S_FREE, P_READY and O_FREE barriers count the four softmax warps
+      const bool four = (i >= L_S_FREE && i < L_S_FREE + 2) || (i >= L_P_READY && i < L_P_READY + 2) ||
+                        (i >= L_O_FREE && i < L_O_FREE + 2);
+      mbar_init(&bar[i], four ? 4u : 1u);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc(tslot, L_TMEM_COLS);
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = *tslot;
+  griddep_launch_dependents();
+
+  auto wait = [&](int b, uint32_t parity) -> bool {
+    if (flags[0]) return false;
+    if (mbar_wait(&bar[b], parity)) return true;
+    record_status(p.status, kStatusTimeout);
+    flags[0] = 1;
+    return false;
+  };
+
+  if (warp == 4) {  // ------------------------------------------------- TMA
+    if (lane == 0) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      // the first tiles into L2 while the previous grid finishes
+      for (int t = 0; t < nt && t < 2; ++t)
+        for (int cb = 0; cb < 4; ++cb) {
+          tma_prefetch_l2_3d(&tmK, cb * 64, int(p0) + t * BT, kh);
+          tma_prefetch_l2_3d(&tmV, cb * 64, int(p0) + t * BT, kh);
+        }
+      griddep_wait();
+      int issued = 0;
+      for (int i = 0; i < 2 * nt; ++i) {
+        const int s = i % 3;
+        if (i >= 3 && !wait(L_EMPTY + s, ((i / 3) - 1) & 1)) break;
+        const int pos = int(p0) + (i >> 1) * BT;
+        const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
+        mbar_arrive_expect_tx(&bar[L_FULL + s], 4 * 16384);
+        for (int cb = 0; cb < 4; ++cb)
+          tma_load_3d(smem + s * L_SLOT + cb * 16384, tm, &bar[L_FULL + s], cb * 64, pos, kh);
+        issued = i + 1;
+      }
+      // every copy into this CTA's shared memory lands before it ends: the
+      // last three (earlier slots were consumed before their reuse)
+      for (int i = max(0, issued - 3); i < issued; ++i) mbar_wait(&bar[L_FULL + i % 3], (i / 3) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 5) {  // ------------------------------------------- MMA
+    nbar_sync(1, 128 + 32);  // Q^T written by warps 0-3
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16(BT, NQ, false, false);
+      constexpr uint32_t idPV = idesc_bf16(BT, NQ, true, false);
+      const uint64_t qd0 = sw128_desc(smem_u32(smem + L_OFF_Q), 16, 1024);
+      bool ok = true;
+      // iteration t: the scores of tile t (t < nt), then O of tile t - 1
+      for (int t = 0; t <= nt && ok; ++t) {
+        if (t < nt) {
+          const int s = (2 * t) % 3;
+          if (!(wait(L_FULL + s, ((2 * t) / 3) & 1) &&
+                (t < 2 || wait(L_S_FREE + (t & 1), ((t - 2) >> 1) & 1)))) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          const uint64_t kd0 = sw128_desc(smem_u32(smem + s * L_SLOT), 16, 1024);
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb)
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              mma_bf16_ss(tmem + (t & 1) * 16, desc_add(kd0, cb * 16384 + k4 * 32),
+                          desc_add(qd0, cb * 2048 + k4 * 32), idS, cb > 0 || k4 > 0);
+          mma_commit(&bar[L_S_FULL + (t & 1)]);
+          mma_commit(&bar[L_EMPTY + s]);
+        }
+        if (t >= 1) {
+          const int j = t - 1, s = (2 * j + 1) % 3;
+          if (!(wait(L_FULL + s, ((2 * j + 1) / 3) & 1) && wait(L_P_READY + (j & 1), (j >> 1) & 1) &&
+                (j < 2 || wait(L_O_FREE + (j & 1), ((j - 2) >> 1) & 1)))) {
+            ok = false;
+            break;
+          }
+          fence_after_sync();
+          // O^T = V^T P^T: M128 (dims) N16 K128, V MN-major (64-dim blocks
+          // 16 KB apart, 8-position groups 1 KB apart), dims 0-127 and 128-255
+          const uint64_t vd0 = sw128_desc(smem_u32(smem + s * L_SLOT), 16384, 1024),
+                         pd0 = sw128_desc(smem_u32(smem + L_OFF_P + (j & 1) * 4096), 16, 1024);
+          const uint32_t od = tmem + 32 + (j & 1) * 32;
+#pragma unroll
+          for (int mm = 0; mm < 2; ++mm)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_bf16_ss(od + NQ * mm, desc_add(vd0, 2 * mm * 16384 + kk * 2048),
+                          desc_add(pd0, (kk >> 2) * 2048 + (kk & 3) * 32), idPV, kk > 0);
+          mma_commit(&bar[L_O_FULL + (j & 1)]);
+          mma_commit(&bar[L_EMPTY + s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {  // ---------------------------------------------- warps 0-3
+    if (tid < G * 4) {
+      const int g = tid >> 2, ln = tid & 3;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(
+          reinterpret_cast<const char*>(qrow + int64_t(h0 + g) * p.q_head) + ln * 128));
+    }
+    griddep_wait();
+    {  // Q^T rows (zero for h >= G) and the zero rows G..15 of both P^T buffers
+      const int h = tid >> 3, dg = tid & 7;
+      uint4 v[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                    make_uint4(0, 0, 0, 0)};
+      if (h < G) {
+        const uint4* src = reinterpret_cast<const uint4*>(qrow + int64_t(h0 + h) * p.q_head + dg * 32);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[c] = src[c];
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(smem + L_OFF_Q + swz(h, dg * 32 + c * 8, 2048)) = v[c];
+      for (int i = tid; i < 4 * (NQ - G) * 8; i += 128) {
+        const int blk = i / ((NQ - G) * 8), rr = G + (i / 8) % (NQ - G), ch = i & 7;
+        *reinterpret_cast<uint4*>(smem + L_OFF_P + blk * 2048 + rr * 128 + (ch << 4)) =
+            make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_smem();
+    }
+    nbar_sync(1, 128 + 32);  // Q^T ready for the MMA warp
+
+    const int pl = warp * 32 + lane;  // position in the tile; dim pl (and pl + 128) of O
+    // Mt0 / Mt1: M after the last even / odd tile
+    float M[G], Lsum[G], Macc[G], Mt0[G], Mt1[G], o[2][G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      M[g] = -INFINITY;
+      Lsum[g] = 0.f;
+      Macc[g] = -INFINITY;
+      o[0][g] = 0.f;
+      o[1][g] = 0.f;
+      Mt0[g] = Mt1[g] = -INFINITY;
+    }
+    bool ok = true;
+    // iteration t: the softmax of tile t (t < nt), then O of tile t - 1
+    for (int t = 0; t <= nt; ++t) {
+      const int b = t & 1;
+      if (t < nt) {
+        float sc[G];
+        {
+          const bool got = __all_sync(0xFFFFFFFFu, wait(L_S_FULL + b, (t >> 1) & 1));
+          ok = ok && got;
+          fence_after_sync();
+          uint32_t raw[16];
+          tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + b * 16, raw);
+          tmem_wait_ld();
+          fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar[L_S_FREE + b]);
+          const bool valid = got && p0 + int64_t(t) * BT + pl < p1;
+#pragma unroll
+          for (int g = 0; g < G; ++g) sc[g] = valid ? __uint_as_float(raw[g]) * p.scale_log2 : -INFINITY;
+        }
+        float* rm = red + b * 64;        // [4 warps][16] maxima of tile parity b
+        float* rl = red + 128 + b * 64;  // and sums
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float mx = warp_max(sc[g]);
+          if (lane == 0) rm[warp * 16 + g] = mx;
+        }
+        nbar_sync(2, 128);
+        uint8_t* pbuf = smem + L_OFF_P + b * 4096;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float tm = fmaxf(fmaxf(rm[g], rm[16 + g]), fmaxf(rm[32 + g], rm[48 + g]));
+          const float mn = fmaxf(M[g], tm);
+          const float pr = mn == -INFINITY ? 0.f : fast_exp2(sc[g] - mn);
+          const float sm = warp_sum(pr);
+          if (lane == 0) rl[warp * 16 + g] = sm;
+          *reinterpret_cast<uint16_t*>(pbuf + swz(g, pl, 2048)) = uint16_t(pack_bf16x2(pr, 0.f) & 0xFFFFu);
+          const float corr = M[g] == -INFINITY ? 0.f : fast_exp2(M[g] - mn);
+          Lsum[g] *= corr;  // the tile's sum is added below
+          M[g] = mn;
+          if (b) Mt1[g] = mn; else Mt0[g] = mn;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[L_P_READY + b]);
+        nbar_sync(2, 128);
+#pragma unroll
+        for (int g = 0; g < G; ++g) Lsum[g] += ((rl[g] + rl[16 + g]) + rl[32 + g]) + rl[48 + g];
+      }
+      if (t >= 1) {  // O of tile j = t - 1 out of TMEM, folded into the registers
+        const int j = t - 1;
+        const bool got = __all_sync(0xFFFFFFFFu, wait(L_O_FULL + (j & 1), (j >> 1) & 1));
+        ok = ok && got;
+        fence_after_sync();
+        uint32_t r0[16], r1[16];
+        const uint32_t base = tmem + (uint32_t(warp * 32) << 16) + 32 + (j & 1) * 32;
+        tmem_ld16(base, r0);
+        tmem_ld16(base + NQ, r1);
+        tmem_wait_ld();
+        fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[L_O_FREE + (j & 1)]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float mj = (j & 1) ? Mt1[g] : Mt0[g];
+          const float c = Macc[g] == -INFINITY ? 0.f : fast_exp2(Macc[g] - mj);
+          o[0][g] = fmaf(o[0][g], c, got ? __uint_as_float(r0[g]) : 0.f);
+          o[1][g] = fmaf(o[1][g], c, got ? __uint_as_float(r1[g]) : 0.f);
+          Macc[g] = mj;
+        }
+      }
+    }
+    if (!ok && lane == 0) flags[0] = 1;
+
+    // ------------------------------------------------ partial or finalise
+    uint16_t* orow = p.out + int64_t(row) * p.out_row;
+    if (active == 1) {
+      if (!flags[0]) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float inv = Lsum[g] > 0.f ? 1.f / Lsum[g] : 0.f;
+#pragma unroll
+          for (int mm = 0; mm < 2; ++mm) {
+            const int dd = mm * 128 + pl;
+            uint16_t a = f32_to_bf16_cvtne(o[mm][g] * inv);
+            if (p.gate_offset >= 0) a = gate_bf16(a, qrow[p.gate_offset + int64_t(h0 + g) * HDM + dd]);
+            orow[int64_t(h0 + g) * HDM + dd] = a;
+          }
+        }
+      }
+    } else {
+      float* mine = p.partials + (int64_t(unit) * p.nsplit + split) * PSTRIDE;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        __stcg(mine + g * HDM + pl, o[0][g]);
+        __stcg(mine + g * HDM + 128 + pl, o[1][g]);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        if (tid == g) {
+          __stcg(mine + G * HDM + g, M[g]);
+          __stcg(mine + G * HDM + G + g, Lsum[g]);
+        }
+      nbar_sync(2, 128);  // every partial store of this CTA precedes thread 0's release
+      if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&p.counters[unit], 1u);
+        __threadfence();
+        flags[1] = prev == unsigned(active - 1);
+      }
+      nbar_sync(2, 128);
+      if (flags[1]) {
+        // The last CTA of the unit merges every split.  The splits' maxima
+        // and sums first (one warp per head, lanes across the splits: the
+        // weights 2^(m_s - M) and the merged sum), then the O partials come
+        // into the idle ring by bulk copies, as many splits at a time as it
+        // holds, all of a batch in flight on one barrier, and each thread
+        // sums its output quads from shared memory.
+        const float* up = p.partials + int64_t(unit) * p.nsplit * PSTRIDE;
+        float* sml = reinterpret_cast<float*>(smem + L_OFF_Q);  // [active][2G] m, l (Q^T, P^T are done)
+        float* smw = sml + active * 2 * G;                      // [active][G] weights
+        float* smL = reinterpret_cast<float*>(smem + L_OFF_RED);  // [G]
+        constexpr int ROW = G * HDM * 4;                        // bytes of one split's O
+        constexpr int BATCH = 3 * L_SLOT / ROW;
+        const bool staged = active * 3 * G * 4 <= 16384;        // m, l and weights fit Q^T + P^T
+        auto issue = [&](int b0) {  // warp 0: the O rows of splits b0 .. b0 + BATCH - 1
+          const int nb = min(BATCH, active - b0);
+          if (lane == 0) mbar_arrive_expect_tx(&bar[L_MERGE], uint32_t(nb) * ROW);
+          __syncwarp();
+          for (int i = lane; i < nb; i += 32) bulk_g2s(smem + i * ROW, up + (b0 + i) * PSTRIDE, ROW, &bar[L_MERGE]);
+        };
+        if (staged) {
+          if (warp == 0) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            issue(0);  // in flight while the weights are formed
+          }
+          for (int i = tid; i < active * 2 * G; i += 128)
+            sml[i] = __ldcg(up + (i / (2 * G)) * PSTRIDE + G * HDM + (i % (2 * G)));
+          nbar_sync(2, 128);
+          for (int g = warp; g < G; g += 4) {
+            float Mx = -INFINITY;
+            for (int sp = lane; sp < active; sp += 32) Mx = fmaxf(Mx, sml[sp * 2 * G + g]);
+            Mx = warp_max(Mx);
+            const float Mu = Mx == -INFINITY ? 0.f : Mx;
+            float Ls = 0.f;
+            for (int sp = lane; sp < active; sp += 32) {
+              const float w = fast_exp2(sml[sp * 2 * G + g] - Mu);
+              smw[sp * G + g] = w;
+              Ls = fmaf(sml[sp * 2 * G + G + g], w, Ls);
+            }
+            Ls = warp_sum(Ls);
+            if (lane == 0) smL[g] = Ls;
+          }
+        }
+        nbar_sync(2, 128);
+        constexpr int NQD = G * HDM / 4;  // output quads
+        constexpr int QPT = (NQD + 127) / 128;
+        float4 acc[QPT];
+#pragma unroll
+        for (int k = 0; k < QPT; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (staged) {
+          for (int b0 = 0, it = 0; b0 < active; b0 += BATCH, ++it) {
+            const int nb = min(BATCH, active - b0);
+            if (it > 0 && warp == 0) issue(b0);
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar[L_MERGE], it & 1))) {
+              if (tid == 0) {
+                record_status(p.status, kStatusTimeout);
+                mbar_wait(&bar[L_MERGE], it & 1);  // a second bounded wait for the copies in flight
+              }
+              flags[0] = 1;
+            }
+            if (!flags[0]) {
+#pragma unroll
+              for (int k = 0; k < QPT; ++k) {
+                const int qd = tid + k * 128;
+                if (qd < NQD) {
+                  const int g = qd * 4 / HDM;
+                  for (int i = 0; i < nb; ++i) {
+                    const float4 v = reinterpret_cast<const float4*>(smem + i * ROW)[qd];
+                    const float w = smw[(b0 + i) * G + g];
+                    acc[k].x = fmaf(w, v.x, acc[k].x);
+                    acc[k].y = fmaf(w, v.y, acc[k].y);
+                    acc[k].z = fmaf(w, v.z, acc[k].z);
+                    acc[k].w = fmaf(w, v.w, acc[k].w);
+                  }
+                }
+              }
+            }
+            nbar_sync(2, 128);  // the batch is summed: its buffers may take the next
+            if (flags[0]) break;
+          }
+        } else if (tid == 0) {
+          // more splits than the weight buffer holds: the launcher does not
+          // send such calls here
+          record_status(p.status, kStatusArg);
+        }
+#pragma unroll
+        for (int k = 0; k < QPT; ++k) {
+          const int qd = tid + k * 128;
+          if (qd >= NQD || flags[0] || !staged) continue;
+          const int e = qd * 4, g = e / HDM, dd = e % HDM, hq = h0 + g;
+          const float Ls = smL[g];
+          const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+          uint16_t a[4] = {f32_to_bf16_cvtne(acc[k].x * inv), f32_to_bf16_cvtne(acc[k].y * inv),
+                           f32_to_bf16_cvtne(acc[k].z * inv), f32_to_bf16_cvtne(acc[k].w * inv)};
+          if (p.gate_offset >= 0) {
+            const uint2 gw =
+                *reinterpret_cast<const uint2*>(qrow + p.gate_offset + int64_t(hq) * HDM + dd);
+            a[0] = gate_bf16(a[0], uint16_t(gw.x & 0xFFFFu));
+            a[1] = gate_bf16(a[1], uint16_t(gw.x >> 16));
+            a[2] = gate_bf16(a[2], uint16_t(gw.y & 0xFFFFu));
+            a[3] = gate_bf16(a[3], uint16_t(gw.y >> 16));
+          }
+          *reinterpret_cast<uint2*>(orow + int64_t(hq) * HDM + dd) =
+              make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
+        }
+        if (tid == 0) p.counters[unit] = 0u;  // leave the workspace reusable
+      }
+    }
+  }
+  fence_before_sync();
+  __syncthreads();  // every TMEM read and every MMA of this CTA is done
+  if (warp == 5) {
+    fence_after_sync();
+    tmem_dealloc(tmem, L_TMEM_COLS);
+  }
+}
+
 }  // namespace
 
 bool launch_attn_decode_mma(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err) {
@@ -475,6 +917,78 @@ bool launch_attn_decode_mma(const DecodeLaunch& L, cudaStream_t st, cudaError_t*
   }
   HB_MMA_CASE(1) HB_MMA_CASE(2) HB_MMA_CASE(4) HB_MMA_CASE(8)
 #undef HB_MMA_CASE
+  return false;
+}
+
+namespace {
+template <int G>
+cudaError_t launch_long(const DecodeLaunch& L, int chunk, int nsplit, cudaStream_t st) {
+  static DeviceFlags configured;
+  cudaError_t e = configured.once([] {
+    return cudaFuncSetAttribute(attn_decode_long_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                L_SMEM);
+  });
+  if (e != cudaSuccess) return e;
+  CUtensorMap tk, tv;
+  const int64_t kv_rows = L.one.past + L.rows;
+  const cuuint64_t kd[3] = {cuuint64_t(HDM), cuuint64_t(kv_rows), cuuint64_t(L.hkv)};
+  const cuuint64_t ks[2] = {cuuint64_t(HDM) * 2, cuuint64_t(L.one.kv_stride) * 2};
+  const cuuint32_t box[3] = {64, BT, 1};
+  if (!encode_tiled(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, L.one.keys, kd, ks, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tiled(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, L.one.values, kd, ks, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  DecodeLongParams p;
+  p.q = L.one.q;
+  p.out = L.one.output;
+  p.q_row = L.q_row;
+  p.q_head = L.q_head;
+  p.out_row = L.out_row;
+  p.gate_offset = L.gate_offset;
+  p.past = L.one.past;
+  p.hkv = int(L.hkv);
+  p.chunk = chunk;
+  p.nsplit = nsplit;
+  p.scale_log2 = L.scale * 1.4426950408889634f;
+  p.status = L.status;
+  p.counters = L.counters;
+  p.partials = L.partials;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(nsplit), unsigned(L.hkv), unsigned(L.rows));
+  cfg.blockDim = dim3(kThreadsL);
+  cfg.dynamicSmemBytes = L_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attn_decode_long_kernel<G>, tk, tv, p);
+}
+}  // namespace
+
+bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err) {
+  if (L.seqs != nullptr || L.nseq != 1 || L.head_dim != HDM) return false;
+  if ((reinterpret_cast<uintptr_t>(L.one.q) | reinterpret_cast<uintptr_t>(L.one.keys) |
+       reinterpret_cast<uintptr_t>(L.one.values) | reinterpret_cast<uintptr_t>(L.one.output)) & 15)
+    return false;
+  // beyond the reach of the cluster forms (16 splits of <= 256 positions);
+  // splits of whole tiles, no more of them than the plan's workspace holds
+  const int64_t max_n = L.one.past + L.rows;
+  if (max_n <= 16 * 256) return false;
+  const int64_t chunk = (int64_t(L.chunk) + BT - 1) / BT * BT;
+  const int64_t nsplit = (max_n + chunk - 1) / chunk;
+  if (chunk > (int64_t(1) << 30) || nsplit > L.nsplit || max_n + BT > (int64_t(1) << 31)) return false;
+  // the merge keeps the splits' maxima, sums and weights in 16 KB of shared memory
+  if (nsplit * L.gqa * 12 > 16384) return false;
+#define HB_LONG_CASE(G_)                                                       \
+  if (L.gqa == G_) {                                                           \
+    *err = launch_long<G_>(L, int(chunk), int(nsplit), st);                    \
+    return true;                                                               \
+  }
+  HB_LONG_CASE(1) HB_LONG_CASE(2) HB_LONG_CASE(4) HB_LONG_CASE(8)
+#undef HB_LONG_CASE
   return false;
 }
 

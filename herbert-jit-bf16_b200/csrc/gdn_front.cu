@@ -476,16 +476,22 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
 // A decode step of a whole DeltaNet layer in one launch: conv + SiLU of the
 // row, the gates, the L2 step, the recurrence and the gated norm, each in
 // the operation order of its own kernel above (and of the reference), so
-// the results are the three-launch path's bits.  CTA h = V head h, 128
-// threads: thread t owns q / k channel t of the head's key head, v channel
-// t and state column t.  The V heads of one key head read the same q / k
+// the results are the three-launch path's bits.  CTA h = V head h, 4 hvd
+// threads: thread t < hkd owns q / k channel t of the head's key head,
+// thread t < hvd v channel t.  The recurrence gives state column c to four
+// threads, one per quarter of the kd rows (thread q hvd + c holds rows
+// [q hkd/4, (q + 1) hkd/4) in registers): all four form their products at
+// once, then the sums over kd run quarter after quarter in increasing kd,
+// each continuing the previous quarter's value through shared memory -- the
+// reference's order, with 32-step code (not 128) to fetch and run.  The V heads of one key head read the same q / k
 // inputs and conv state, and the first of them writes them back in place:
 // they form one cluster, every thread arrives on the cluster barrier once
 // its reads are done and waits on it before any write.  Launched with
 // programmatic stream serialization: before griddepcontrol.wait only L2
 // prefetches (the state tile and the row's lines).
 
-constexpr int kRowThreads = 128;
+constexpr int kRowSubs = 4;       // threads per state column
+constexpr int kRowMaxHvd = 128;
 
 struct RowParams {
   float* qkv;                   // [conv] conv + SiLU in place
@@ -498,6 +504,7 @@ struct RowParams {
   const uint16_t* norm_weight;  // [hvd] bf16
   uint16_t* out;                // [nv hvd] bf16
   float* out_f32;               // [nv hvd] or nullptr
+  float* state;                 // [nv][hkd][hvd] (read by the tensor map, written by bulk copies)
   int nk, nv;
   float l2_eps, scale, norm_eps;
   int* status;
@@ -515,16 +522,21 @@ HB_DEV float conv4_sum(const float4& st, uint2 w, float x) {
 }
 
 template <int HKD, int NB>
-__global__ void __launch_bounds__(kRowThreads, 1)
+__global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
     gdn_row_kernel(const __grid_constant__ CUtensorMap tmS, const RowParams p) {
   constexpr int HVD = 16 * NB;
-  static_assert(HKD <= kRowThreads && HVD <= kRowThreads && HVD % 32 == 0, "one thread per column");
+  constexpr int KS = HKD / kRowSubs;  // kd rows per thread in the recurrence
+  static_assert(HKD <= kRowSubs * HVD && HVD <= kRowMaxHvd && HVD % 32 == 0 && KS % 4 == 0,
+                "thread roles");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   float* st = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* qn = st + HKD * HVD;  // [HKD] q, then q inv_q scale
   float* kn = qn + HKD;        // [HKD] k, then k inv_k
   float* os = kn + HKD;        // [HVD] recurrence output
-  float* misc = os + HVD;      // inv_q, inv_k, beta, decay
+  float* vb = os + HVD;        // [HVD] v after the conv
+  float* cb = vb + HVD;        // [HVD] a column's sum handed to the next quarter
+  float* db = cb + HVD;        // [HVD] delta
+  float* misc = db + HVD;      // inv_q, inv_k, beta, decay
   uint64_t* bar = reinterpret_cast<uint64_t*>(misc + 4);
 
   const int tid = threadIdx.x, lane = tid & 31;
@@ -608,6 +620,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     float unused;
     const float g = conv4_sum(sv, wv, xv);
     silu_poly2(g, g, yv, unused);
+    vb[tid] = yv;
   }
   __syncthreads();
   if (tid == 0 || tid == 32) misc[tid >> 5] = l2_inverse<HKD>(tid == 0 ? qn : kn, p.l2_eps);
@@ -634,19 +647,73 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   const bool late = __syncthreads_or(!mbar_wait(bar, 0));  // the state tile
 
   if (!late) {
-    if (has_v) {
-      float s[HKD];
+    const int sub = tid / HVD, col = tid % HVD;  // uniform per warp: HVD is a multiple of 32
+    float sr[KS], pr[KS];
+    const float4* k4 = reinterpret_cast<const float4*>(kn + sub * KS);
+    const float4* q4 = reinterpret_cast<const float4*>(qn + sub * KS);
+    const float decay = misc[3], beta = misc[2];
 #pragma unroll
-      for (int kd = 0; kd < HKD; ++kd) s[kd] = st[kd * HVD + tid];
-      os[tid] = gdn_step_column<HKD>(s, kn, qn, yv, misc[2], misc[3]);
+    for (int j = 0; j < KS; ++j) sr[j] = st[(sub * KS + j) * HVD + col];
+    // pass 1: decay the rows, the products r k
 #pragma unroll
-      for (int kd = 0; kd < HKD; ++kd) st[kd * HVD + tid] = s[kd];
+    for (int j4 = 0; j4 < KS / 4; ++j4) {
+      const float4 kk = k4[j4];
+      const float kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float r = __fmul_rn(sr[4 * j4 + e], decay);
+        sr[4 * j4 + e] = r;
+        pr[4 * j4 + e] = __fmul_rn(r, kw[e]);
+      }
     }
+    // kv = S^T k, kd in increasing order across the quarters; the last one
+    // forms delta
+#pragma unroll 1
+    for (int i = 0; i < kRowSubs; ++i) {
+      if (sub == i) {
+        float acc = i == 0 ? 0.f : cb[col];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) acc = __fadd_rn(acc, pr[j]);
+        if (i < kRowSubs - 1) cb[col] = acc;
+        else db[col] = __fmul_rn(__fsub_rn(vb[col], acc), beta);
+      }
+      __syncthreads();
+    }
+    // pass 2: S += k delta, the products r (q scale)
+    const float delta = db[col];
+#pragma unroll
+    for (int j4 = 0; j4 < KS / 4; ++j4) {
+      const float4 kk = k4[j4], qq = q4[j4];
+      const float kw[4] = {kk.x, kk.y, kk.z, kk.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float r = __fadd_rn(sr[4 * j4 + e], __fmul_rn(kw[e], delta));
+        sr[4 * j4 + e] = r;
+        pr[4 * j4 + e] = __fmul_rn(r, qw[e]);
+      }
+    }
+    // this quarter's new state rows back into the tile and out by one bulk
+    // copy (its KS rows are contiguous in both), in flight during the sums
+#pragma unroll
+    for (int j = 0; j < KS; ++j) st[(sub * KS + j) * HVD + col] = sr[j];
     sm100::fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      sm100::tma_store_2d(&tmS, st, 0, h * HKD);
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + sub), "r"(HVD) : "memory");  // the quarter's warps
+    if (col == 0) {
+      sm100::bulk_s2g(p.state + (int64_t(h) * HKD + sub * KS) * HVD, st + sub * KS * HVD,
+                      uint32_t(KS * HVD * 4));
       sm100::tma_store_commit();
+    }
+    // out = S^T (q scale), in the same order
+#pragma unroll 1
+    for (int i = 0; i < kRowSubs; ++i) {
+      if (sub == i) {
+        float acc = i == 0 ? 0.f : cb[col];
+#pragma unroll
+        for (int j = 0; j < KS; ++j) acc = __fadd_rn(acc, pr[j]);
+        if (i < kRowSubs - 1) cb[col] = acc;
+        else os[col] = acc;
+      }
+      __syncthreads();
     }
     // the gated norm: every warp forms the row's inverse (the same bits)
     // and finishes its own columns
@@ -666,13 +733,13 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       if (p.out_f32) p.out_f32[o] = y;
       p.out[o] = static_cast<uint16_t>(bf16x2_cvtne_fast(y, y) & 0xFFFFu);
     }
+    if (col == 0) sm100::tma_store_wait_read();  // the tile stays until the copy has read it
   } else if (tid == 0) {
     // the state and the outputs are not written (the conv results are, as
     // the three-launch path's front end would have written them)
     record_status(p.status, kStatusTimeout);
     mbar_wait(bar, 0);  // a second bounded wait for the copy in flight
   }
-  if (tid == 0 && !late) sm100::tma_store_wait_read();
 }
 
 }  // namespace
@@ -719,14 +786,14 @@ cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st) {
 
 bool gdn_row_serves(const hb_gdn_shape& s, int64_t ck) {
   return ck == 4 && (s.hkd == 64 || s.hkd == 128) && s.hvd % 32 == 0 && s.hvd >= 32 &&
-         s.hvd <= kRowThreads && s.nk > 0 && s.nv % s.nk == 0 && s.nv / s.nk <= 8;
+         s.hvd <= kRowMaxHvd && s.nk > 0 && s.nv % s.nk == 0 && s.nv / s.nk <= 8;
 }
 
 namespace {
 template <int HKD, int NB>
 cudaError_t launch_row(const CUtensorMap& tm, const RowParams& p, cudaLaunchConfig_t cfg) {
   constexpr int HVD = 16 * NB;
-  const size_t smem = 1024 + size_t(HKD) * HVD * 4 + (2 * HKD + HVD + 4) * 4 + 8;
+  const size_t smem = 1024 + size_t(HKD) * HVD * 4 + (2 * HKD + 4 * HVD + 4) * 4 + 8;
   static bool attr = false;  // one flag per instantiation
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(gdn_row_kernel<HKD, NB>,
@@ -734,6 +801,7 @@ cudaError_t launch_row(const CUtensorMap& tm, const RowParams& p, cudaLaunchConf
     if (e != cudaSuccess) return e;
     attr = true;
   }
+  cfg.blockDim = dim3(kRowSubs * HVD);
   cfg.dynamicSmemBytes = smem;
   return cudaLaunchKernelEx(&cfg, gdn_row_kernel<HKD, NB>, tm, p);
 }
@@ -751,6 +819,7 @@ cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st) {
   p.norm_weight = L.norm_weight;
   p.out = L.out;
   p.out_f32 = L.out_f32;
+  p.state = L.state;
   p.nk = int(L.shape.nk);
   p.nv = int(L.shape.nv);
   p.l2_eps = L.l2_eps;
@@ -765,7 +834,6 @@ cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st) {
     return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(L.shape.nv));
-  cfg.blockDim = dim3(kRowThreads);
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;  // the V heads of one key head

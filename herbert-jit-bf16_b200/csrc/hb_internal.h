@@ -62,6 +62,9 @@ cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
 // head_dim 256: returns false (nothing launched) when the call is not in
 // its domain, else launches and sets *err.
 bool launch_attn_decode_mma(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err);
+// one sequence longer than 16 x 256 positions: split-KV on the tensor cores
+// (false: not served, the CUDA-core kernel runs)
+bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err);
 
 // ---------------------------------------------------------- attn prefill
 struct PrefillLaunch {

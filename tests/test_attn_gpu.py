@@ -33,6 +33,13 @@ DECODE_CASES = [
     (1, 1000, 16, 2, 256, True),    # gqa 8
     (1, 600, 4, 4, 256, False),     # gqa 1, no gate
     (2, 1500, 16, 4, 256, True),
+    # one sequence beyond 16 x 256 positions at head_dim 256: split-KV on the
+    # tensor cores, 128-position tiles, partials merged by the last CTA
+    (1, 32767, 16, 4, 256, True),   # the mixers' attention layer, n = 32768
+    (1, 9000, 16, 2, 256, True),    # gqa 8, ragged last tile
+    (2, 6000, 8, 8, 256, False),    # gqa 1, rows > 1, no gate
+    (1, 20000, 8, 4, 256, True),    # gqa 2
+    (3, 4094, 16, 4, 256, True),    # rows 0-1 at the cluster forms' limit, row 2 beyond it
 ]
 
 
