@@ -483,12 +483,16 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
 // [q hkd/4, (q + 1) hkd/4) in registers): all four form their products at
 // once, then the sums over kd run quarter after quarter in increasing kd,
 // each continuing the previous quarter's value through shared memory -- the
-// reference's order, with 32-step code (not 128) to fetch and run.  The V heads of one key head read the same q / k
-// inputs and conv state, and the first of them writes them back in place:
-// they form one cluster, every thread arrives on the cluster barrier once
-// its reads are done and waits on it before any write.  Launched with
-// programmatic stream serialization: before griddepcontrol.wait only L2
-// prefetches (the state tile and the row's lines).
+// reference's order, with 32-step code (not 128) to fetch and run.
+//
+// The V heads of one key head read the same q / k inputs and conv state and
+// compute the same conv results; the last of them to finish reading writes
+// those back in place.  After its reads each CTA counts itself on the key
+// head's counter (an acquire-release atomic add): the CTA that sees the count
+// complete resets it and writes, when every other CTA of the key head is
+// past its reads -- no CTA waits for another.  Launched with programmatic
+// stream serialization: before griddepcontrol.wait only L2 prefetches (the
+// state tile and the row's lines).
 
 constexpr int kRowSubs = 4;       // threads per state column
 constexpr int kRowMaxHvd = 128;
@@ -505,13 +509,12 @@ struct RowParams {
   uint16_t* out;                // [nv hvd] bf16
   float* out_f32;               // [nv hvd] or nullptr
   float* state;                 // [nv][hkd][hvd] (read by the tensor map, written by bulk copies)
+  unsigned* counters;           // [nk] readers of each key head's inputs (zero between calls)
   int nk, nv;
   float l2_eps, scale, norm_eps;
   int* status;
 };
 
-HB_DEV void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
-HB_DEV void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // (s1 w0 + s2 w1) + (s3 w2 + x w3): the vector kernel's sum at ck = 4 for a
 // row whose taps are the state's last three inputs and x.
@@ -536,12 +539,13 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
   float* vb = os + HVD;        // [HVD] v after the conv
   float* cb = vb + HVD;        // [HVD] a column's sum handed to the next quarter
   float* db = cb + HVD;        // [HVD] delta
-  float* misc = db + HVD;      // inv_q, inv_k, beta, decay
-  uint64_t* bar = reinterpret_cast<uint64_t*>(misc + 4);
+  float* yb = db + HVD;        // [2 HKD] the conv results of q, k (written back by the last reader)
+  float4* sb = reinterpret_cast<float4*>(yb + 2 * HKD);  // [2 HKD] their new conv states
+  float* misc = reinterpret_cast<float*>(sb + 2 * HKD);  // inv_q, inv_k, beta, decay
+  uint64_t* bar = reinterpret_cast<uint64_t*>(misc + 8);  // misc[4]: the last-reader flag
 
   const int tid = threadIdx.x, lane = tid & 31;
   const int h = blockIdx.x, ratio = p.nv / p.nk, kh = h / ratio;
-  const bool writer = h % ratio == 0;  // writes the key head's q / k channels back
   const int64_t key = int64_t(p.nk) * HKD;
   const int64_t cq = int64_t(kh) * HKD + tid, ck = key + cq, cv = 2 * key + int64_t(h) * HVD + tid;
   const bool has_qk = tid < HKD, has_v = tid < HVD;
@@ -580,8 +584,7 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
     sm100::tma_load_2d(st, &tmS, bar, 0, h * HKD);
   }
 
-  // every load of the row, then the cluster arrival: after it the writer
-  // may overwrite the shared inputs
+  // every load of the row
   float4 sq = make_float4(0.f, 0.f, 0.f, 0.f), sk = sq, sv = sq;
   uint2 wq = make_uint2(0u, 0u), wk = wq, wv = wq;
   float xq = 0.f, xk = 0.f, xv = 0.f, zz = 0.f, nw = 0.f;
@@ -608,13 +611,16 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
     dtb = p.dt_bias[h];
     a_log = p.a_log[h];
   }
-  cluster_arrive_release();
 
   float yq = 0.f, yk = 0.f, yv = 0.f;
   if (has_qk) {
     silu_poly2(conv4_sum(sq, wq, xq), conv4_sum(sk, wk, xk), yq, yk);
     qn[tid] = yq;
     kn[tid] = yk;
+    yb[tid] = yq;
+    yb[HKD + tid] = yk;
+    sb[tid] = make_float4(sq.y, sq.z, sq.w, xq);
+    sb[HKD + tid] = make_float4(sk.y, sk.z, sk.w, xk);
   }
   if (has_v) {
     float unused;
@@ -622,7 +628,13 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
     silu_poly2(g, g, yv, unused);
     vb[tid] = yv;
   }
-  __syncthreads();
+  __syncthreads();  // every thread has consumed its loads
+  // this CTA is past its reads of the key head's inputs (the answer is
+  // used at the end, so nothing waits on the atomic here)
+  unsigned readers_before = 0;
+  if (tid == 96)  // release: the CTA's reads (ordered by the barrier) come before it
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(readers_before) : "l"(p.counters + kh) : "memory");
   if (tid == 0 || tid == 32) misc[tid >> 5] = l2_inverse<HKD>(tid == 0 ? qn : kn, p.l2_eps);
   if (tid == 64) gate_values(ga, gb, dtb, a_log, misc[2], misc[3]);
   __syncthreads();
@@ -630,17 +642,7 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
     qn[tid] = __fmul_rn(__fmul_rn(qn[tid], misc[0]), p.scale);
     kn[tid] = __fmul_rn(kn[tid], misc[1]);
   }
-  // every V head of the key head has read the inputs (they arrived before
-  // their norms, so this rarely waits): the conv's results go back in place
-  // now, and their registers are free for the state column
-  cluster_wait_acquire();
-  if (has_qk && writer) {
-    p.qkv[cq] = yq;
-    p.qkv[ck] = yk;
-    *reinterpret_cast<float4*>(p.conv_state + cq * 4) = make_float4(sq.y, sq.z, sq.w, xq);
-    *reinterpret_cast<float4*>(p.conv_state + ck * 4) = make_float4(sk.y, sk.z, sk.w, xk);
-  }
-  if (has_v) {
+  if (has_v) {  // this head's own v channel back in place
     p.qkv[cv] = yv;
     *reinterpret_cast<float4*>(p.conv_state + cv * 4) = make_float4(sv.y, sv.z, sv.w, xv);
   }
@@ -740,6 +742,21 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
     record_status(p.status, kStatusTimeout);
     mbar_wait(bar, 0);  // a second bounded wait for the copy in flight
   }
+  // the last reader of the key head's inputs writes the conv results back
+  // and leaves the counter at zero for the next call
+  int* last = reinterpret_cast<int*>(misc + 4);
+  if (tid == 96) {
+    const bool is_last = readers_before == unsigned(ratio - 1);
+    if (is_last) p.counters[kh] = 0u;
+    *last = is_last;
+  }
+  __syncthreads();
+  if (*last && has_qk) {
+    p.qkv[cq] = yb[tid];
+    p.qkv[ck] = yb[HKD + tid];
+    *reinterpret_cast<float4*>(p.conv_state + cq * 4) = sb[tid];
+    *reinterpret_cast<float4*>(p.conv_state + ck * 4) = sb[HKD + tid];
+  }
 }
 
 }  // namespace
@@ -786,14 +803,14 @@ cudaError_t launch_gdn_front(const GdnFrontLaunch& L, cudaStream_t st) {
 
 bool gdn_row_serves(const hb_gdn_shape& s, int64_t ck) {
   return ck == 4 && (s.hkd == 64 || s.hkd == 128) && s.hvd % 32 == 0 && s.hvd >= 32 &&
-         s.hvd <= kRowMaxHvd && s.nk > 0 && s.nv % s.nk == 0 && s.nv / s.nk <= 8;
+         s.hvd <= kRowMaxHvd && s.nk > 0 && s.nk <= kRowMaxKeyHeads && s.nv % s.nk == 0;
 }
 
 namespace {
 template <int HKD, int NB>
 cudaError_t launch_row(const CUtensorMap& tm, const RowParams& p, cudaLaunchConfig_t cfg) {
   constexpr int HVD = 16 * NB;
-  const size_t smem = 1024 + size_t(HKD) * HVD * 4 + (2 * HKD + 4 * HVD + 4) * 4 + 8;
+  const size_t smem = 1024 + size_t(HKD) * HVD * 4 + (2 * HKD + 4 * HVD + 2 * HKD + 8 * HKD + 8) * 4 + 8;
   static bool attr = false;  // one flag per instantiation
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(gdn_row_kernel<HKD, NB>,
@@ -820,6 +837,7 @@ cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st) {
   p.out = L.out;
   p.out_f32 = L.out_f32;
   p.state = L.state;
+  p.counters = L.counters;
   p.nk = int(L.shape.nk);
   p.nv = int(L.shape.nv);
   p.l2_eps = L.l2_eps;
@@ -835,15 +853,11 @@ cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(L.shape.nv));
   cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;  // the V heads of one key head
-  attr[0].val.clusterDim.x = unsigned(L.shape.nv / L.shape.nk);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   const int nb = int(L.shape.hvd / 16);
   if (L.shape.hkd == 128) {
     switch (nb) {

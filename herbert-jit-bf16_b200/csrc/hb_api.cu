@@ -734,7 +734,8 @@ hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, cons
                         int* status, hb_stream_t stream, bool* served) {
   *served = false;
   if (!s || !fc || !gc || !nc || fc->rows != 1 || gc->rows != 1 || nc->rows != 1 ||
-      !gdn_row_serves(*s, fc->ck) || gc->l2 != 1 || gc->qkv != fc->qkv || nc->x != gc->output)
+      !gdn_row_serves(*s, fc->ck) || gc->l2 != 1 || gc->qkv != fc->qkv || nc->x != gc->output ||
+      !front_ws || front_ws_bytes < kWsHeader + kRowCounterBytes)
     return HB_OK;
   // the three nodes' own checks, all before anything launches
   hb_status r = check_gdn_front(s, fc, front_ws, front_ws_bytes);
@@ -764,6 +765,7 @@ hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, cons
   L.scale = 1.0f / std::sqrt(float(s->hkd));
   L.norm_eps = nc->eps;
   L.status = status;
+  L.counters = reinterpret_cast<unsigned*>(static_cast<char*>(front_ws) + kWsHeader);
   cudaError_t e = launch_gdn_row(L, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "gdn_row launch");
   return HB_OK;

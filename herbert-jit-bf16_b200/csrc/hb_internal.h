@@ -157,13 +157,20 @@ struct GdnRowLaunch {
   float* out_f32;
   float l2_eps, scale, norm_eps;
   int* status;
+  unsigned* counters;           // [nk], zero between calls
 };
+// key heads whose write-back counters the one-row launch keeps (after the
+// 256-byte header of the caller's front-end workspace)
+constexpr int kRowMaxKeyHeads = 1024;
+constexpr size_t kRowCounterBytes = kRowMaxKeyHeads * sizeof(unsigned);
 bool gdn_row_serves(const hb_gdn_shape& s, int64_t ck);
 cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st);
 // A one-row DeltaNet layer given as its three nodes' calls (front, L2 +
 // recurrence, gated norm): when the fused kernel serves it (*served), the
 // three calls' checks run first and then the one launch; otherwise nothing
 // happens and the caller runs the nodes.
+// front_ws holds the header, then the key heads' counters (kRowCounterBytes,
+// zero between calls) when front_ws_bytes covers them.
 hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, const hb_gdn_call* gc,
                         const hb_gdn_norm_call* nc, void* front_ws, size_t front_ws_bytes,
                         int* status, hb_stream_t stream, bool* served);

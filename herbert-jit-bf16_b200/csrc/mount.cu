@@ -224,14 +224,14 @@ hb_status hb_mount_create(const hb_mount_desc* d, hb_mount** out) {
   if (e == cudaSuccess && any_delta) {
     const size_t nv = size_t(d->delta.nv), vd = nv * size_t(d->delta.hvd);
     e = cudaMalloc(&m->gdn_ws, m->gdn_ws_bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&m->front_ws, kWsHeader);
+    if (e == cudaSuccess) e = cudaMalloc(&m->front_ws, kWsHeader + kRowCounterBytes);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&m->beta), 4 * size_t(R) * nv);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&m->decay), 4 * size_t(R) * nv);
     if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&m->rec_out), 4 * size_t(R) * vd);
   }
   if (e == cudaSuccess && m->attn_ws) e = cudaMemset(m->attn_ws, 0, m->attn_ws_bytes);
   if (e == cudaSuccess && m->gdn_ws) e = cudaMemset(m->gdn_ws, 0, m->gdn_ws_bytes);
-  if (e == cudaSuccess && m->front_ws) e = cudaMemset(m->front_ws, 0, kWsHeader);
+  if (e == cudaSuccess && m->front_ws) e = cudaMemset(m->front_ws, 0, kWsHeader + kRowCounterBytes);
   if (e != cudaSuccess) {
     release(m);
     return cuda_fail(e, "hb_mount_create");
@@ -264,6 +264,10 @@ hb_status hb_mount_reset(hb_mount* m, hb_stream_t stream) {
   cudaError_t e = cudaSuccess;
   for (void* ws : {m->attn_ws, m->gdn_ws, m->front_ws})
     if (ws && e == cudaSuccess) e = cudaMemsetAsync(ws, 0, kWsHeader, st);
+  // the one-row DeltaNet launches' counters (a failed call may have left
+  // some counted)
+  if (m->front_ws && e == cudaSuccess)
+    e = cudaMemsetAsync(static_cast<char*>(m->front_ws) + kWsHeader, 0, kRowCounterBytes, st);
   if (e != cudaSuccess) return cuda_fail(e, "hb_mount_reset");
   m->poison = HB_OK;
   m->poison_msg[0] = 0;
@@ -364,8 +368,8 @@ hb_status hb_mount_delta(hb_mount* m, int64_t layer, const hb_mount_delta_call* 
     // a decode row: the three nodes in one launch where the shape allows
     // (every node's checks first, so a refusal launches nothing)
     bool served = false;
-    r = gdn_layer_row(&shape, &fc, &gc, &nc, m->front_ws, kWsHeader, static_cast<int*>(m->gdn_ws),
-                      stream, &served);
+    r = gdn_layer_row(&shape, &fc, &gc, &nc, m->front_ws, kWsHeader + kRowCounterBytes,
+                      static_cast<int*>(m->gdn_ws), stream, &served);
     if (served) return after_entry(m, r, false);
   }
   if ((r = hb_gdn_front(&shape, &fc, m->front_ws, kWsHeader, stream)) != HB_OK)
