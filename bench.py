@@ -840,8 +840,10 @@ class MixersWorkload(Workload):
         self.bytes_per_step = mixer_step_bytes()
         self.R = 1
         self.set_bytes = self.bytes_per_step
-        # attention: front end + decode; DeltaNet: one launch per one-row layer
-        self.launches_per_step = (SNAP_LAYERS // SNAP_EVERY) * 2 + n_delta
+        # one launch per layer: the one-row attention layer over SNAP_POS
+        # positions runs its front end inside the decode launch, the one-row
+        # DeltaNet layer is one fused launch
+        self.launches_per_step = SNAP_LAYERS
         self.h_in = [self.q.cpu().pin_memory(), self.qkv.cpu().pin_memory()]
         self.h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory()
                       for t in (self.attn_out, self.delta_out)]

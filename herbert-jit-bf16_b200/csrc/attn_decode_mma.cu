@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 
 #include "hb_common.cuh"
+#include "hb_front.cuh"
 #include "hb_internal.h"
 #include "hb_sm100.cuh"
 
@@ -476,17 +477,27 @@ cudaError_t launch_mma(const DecodeLaunch& L, int nsplit, cudaStream_t st) {
 // counter, reset after use) merges them, divides, rounds to bf16 and
 // applies the gate with the reference's steps.  A unit with one split
 // finalises directly.
+//
+// FRONT: a one-row call whose front end (head-norm-rope of q and k, the
+// kv-append of the row's position) runs here instead of in attn_front.cu,
+// with the same arithmetic (hb_front.cuh).  Warps 0-3 norm and rotate the
+// group's q heads straight into the Q^T operand; the CTA whose split holds
+// the row's position also norms and rotates the k head, writes k and v into
+// the cache row (and k in place) and signals the TMA warp, which loads that
+// tile only then; the CTA that finalises the unit (the last to arrive, when
+// every other CTA has read q) writes the normed q back in place.
 
 constexpr int kThreadsL = 192;               // warps 0-3 softmax, 4 TMA, 5 MMA
 constexpr int L_SLOT = 65536;                // one K or V tile: 4 blocks [128][128 B]
 constexpr int L_OFF_Q = 3 * L_SLOT;          // Q^T: 4 blocks [16 rows][128 B]
 constexpr int L_OFF_P = L_OFF_Q + 8192;      // P^T: 2 buffers x 2 blocks [16][128 B]
 constexpr int L_OFF_RED = L_OFF_P + 8192;    // maxima [2][4 warps][16], then sums [2][4][16]
-constexpr int L_OFF_BAR = L_OFF_RED + 2 * 2 * 4 * 16 * 4;
+constexpr int L_OFF_XS = L_OFF_RED + 2 * 2 * 4 * 16 * 4;  // FRONT: 4 warps x 512 B norm scratch
+constexpr int L_OFF_BAR = L_OFF_XS + 4 * 512;
 constexpr int L_SMEM = L_OFF_BAR + 256 + 1024;  // + alignment slack
 constexpr uint32_t L_TMEM_COLS = 128;        // S^T 2 x 16 columns, O^T 2 x 32
 enum LBar { L_FULL = 0, L_EMPTY = 3, L_S_FULL = 6, L_S_FREE = 8, L_P_READY = 10, L_O_FULL = 12,
-            L_O_FREE = 14, L_MERGE = 16, L_NBAR = 17 };
+            L_O_FREE = 14, L_MERGE = 16, L_KV = 17, L_NBAR = 18 };
 
 struct DecodeLongParams {
   const uint16_t* q;
@@ -499,9 +510,22 @@ struct DecodeLongParams {
   int* status;
   unsigned* counters;   // one per unit
   float* partials;      // [unit][split][G*HD + 2G rounded up to 4]
+  // FRONT (rows == 1): the row's k and v ([hkv][256] each; k normed and
+  // rotated in place), the norm weights, the RoPE table, the cache
+  uint16_t* kf;
+  const uint16_t* vf;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  const uint16_t* cos;
+  const uint16_t* sin;
+  uint16_t* kcache;  // KV head 0 of the layer's K cache, heads kv_stride apart
+  uint16_t* vcache;
+  int64_t kv_stride;
+  int rotary, gemma;
+  float eps, inv_dim;
 };
 
-template <int G>
+template <int G, bool FRONT>
 __global__ void __launch_bounds__(kThreadsL, 1)
     attn_decode_long_kernel(const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const DecodeLongParams p) {
@@ -524,6 +548,8 @@ __global__ void __launch_bounds__(kThreadsL, 1)
   const int unit = row * p.hkv + kh;
   const int h0 = kh * G;
   const uint16_t* qrow = p.q + int64_t(row) * p.q_row;
+  // FRONT: this CTA's split holds the row's own position (rows == 1)
+  const bool tail = FRONT && p.past >= p0 && p.past < p1;
 
   if (tid == 0) {
     for (int i = 0; i < L_NBAR; ++i) {
@@ -562,10 +588,13 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           tma_prefetch_l2_3d(&tmV, cb * 64, int(p0) + t * BT, kh);
         }
       griddep_wait();
+      const int t_tail = tail ? int((p.past - p0) / BT) : -1;
       int issued = 0;
       for (int i = 0; i < 2 * nt; ++i) {
         const int s = i % 3;
         if (i >= 3 && !wait(L_EMPTY + s, ((i / 3) - 1) & 1)) break;
+        // the tile of the row's position once its k and v are in the cache
+        if (i == 2 * t_tail && !wait(L_KV, 0)) break;
         const int pos = int(p0) + (i >> 1) * BT;
         const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
         mbar_arrive_expect_tx(&bar[L_FULL + s], 4 * 16384);
@@ -637,7 +666,52 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           reinterpret_cast<const char*>(qrow + int64_t(h0 + g) * p.q_head) + ln * 128));
     }
     griddep_wait();
-    {  // Q^T rows (zero for h >= G) and the zero rows G..15 of both P^T buffers
+    constexpr int QW = (G + 3) / 4;  // q heads per warp (FRONT)
+    uint32_t qy[QW][4];              // FRONT: this warp's normed q heads, for the write-back
+    if constexpr (FRONT) {
+      // head-norm-rope of the group's q heads (warp w: heads w, w + 4) into
+      // Q^T, and for the position's split the k head and the kv-append
+      const int64_t pos = p.past;
+      uint32_t* xs = reinterpret_cast<uint32_t*>(smem + L_OFF_XS) + warp * 128;
+      uint32_t cw[4] = {0u, 0u, 0u, 0u}, sw[4] = {0u, 0u, 0u, 0u}, ww[4];
+      const int half = p.rotary / 2;
+      if (lane * 8 < p.rotary) {
+        const int j0 = lane * 8 < half ? lane * 8 : lane * 8 - half;
+        front::load_words<4>(cw, p.cos + pos * half + j0);
+        front::load_words<4>(sw, p.sin + pos * half + j0);
+      }
+      front::load_words<4>(ww, p.q_norm + lane * 8);
+#pragma unroll
+      for (int i = 0; i < QW; ++i) {
+        const int hh = warp + 4 * i;
+        if (hh < G) {  // warp-uniform
+          uint32_t xw[4];
+          front::load_words<4>(xw, qrow + int64_t(h0 + hh) * p.q_head + lane * 8);
+          front::norm_rope<HDM>(xw, ww, cw, sw, p.rotary, p.eps, p.inv_dim, p.gemma != 0, xs, lane, qy[i]);
+          *reinterpret_cast<uint4*>(smem + L_OFF_Q + swz(hh, lane * 8, 2048)) =
+              make_uint4(qy[i][0], qy[i][1], qy[i][2], qy[i][3]);
+        }
+      }
+      for (int i = tid; i < (NQ - G) * 32; i += 128)
+        *reinterpret_cast<uint4*>(smem + L_OFF_Q + swz(G + i / 32, (i % 32) * 8, 2048)) =
+            make_uint4(0, 0, 0, 0);
+      if (tail && warp == 0) {
+        uint32_t kw[4], knw[4], vw[4], ky[4];
+        uint16_t* krow = p.kf + int64_t(kh) * HDM + lane * 8;
+        front::load_words<4>(kw, krow);
+        front::load_words<4>(knw, p.k_norm + lane * 8);
+        front::load_words<4>(vw, p.vf + int64_t(kh) * HDM + lane * 8);
+        front::norm_rope<HDM>(kw, knw, cw, sw, p.rotary, p.eps, p.inv_dim, p.gemma != 0, xs, lane, ky);
+        const int64_t dst = int64_t(kh) * p.kv_stride + pos * HDM + lane * 8;
+        front::store_words<4>(p.kcache + dst, ky);
+        front::store_words<4>(p.vcache + dst, vw);
+        front::store_words<4>(krow, ky);
+        // the cache row before the TMA warp's loads of its tile
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[L_KV]);
+      }
+    } else {  // Q^T rows (zero for h >= G)
       const int h = tid >> 3, dg = tid & 7;
       uint4 v[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
                     make_uint4(0, 0, 0, 0)};
@@ -649,6 +723,8 @@ __global__ void __launch_bounds__(kThreadsL, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         *reinterpret_cast<uint4*>(smem + L_OFF_Q + swz(h, dg * 32 + c * 8, 2048)) = v[c];
+    }
+    {  // the zero rows G..15 of both P^T buffers
       for (int i = tid; i < 4 * (NQ - G) * 8; i += 128) {
         const int blk = i / ((NQ - G) * 8), rr = G + (i / 8) % (NQ - G), ch = i & 7;
         *reinterpret_cast<uint4*>(smem + L_OFF_P + blk * 2048 + rr * 128 + (ch << 4)) =
@@ -759,6 +835,12 @@ __global__ void __launch_bounds__(kThreadsL, 1)
             orow[int64_t(h0 + g) * HDM + dd] = a;
           }
         }
+      }
+      if constexpr (FRONT) {  // the only CTA of the unit: the normed q back in place
+#pragma unroll
+        for (int i = 0; i < QW; ++i)
+          if (warp + 4 * i < G)
+            front::store_words<4>(const_cast<uint16_t*>(qrow) + int64_t(h0 + warp + 4 * i) * p.q_head + lane * 8, qy[i]);
       }
     } else {
       float* mine = p.partials + (int64_t(unit) * p.nsplit + split) * PSTRIDE;
@@ -886,6 +968,12 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           *reinterpret_cast<uint2*>(orow + int64_t(hq) * HDM + dd) =
               make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
         }
+        if constexpr (FRONT) {  // every other CTA of the unit has read q: the normed q in place
+#pragma unroll
+          for (int i = 0; i < QW; ++i)
+            if (warp + 4 * i < G)
+              front::store_words<4>(const_cast<uint16_t*>(qrow) + int64_t(h0 + warp + 4 * i) * p.q_head + lane * 8, qy[i]);
+        }
         if (tid == 0) p.counters[unit] = 0u;  // leave the workspace reusable
       }
     }
@@ -921,12 +1009,13 @@ bool launch_attn_decode_mma(const DecodeLaunch& L, cudaStream_t st, cudaError_t*
 }
 
 namespace {
-template <int G>
-cudaError_t launch_long(const DecodeLaunch& L, int chunk, int nsplit, cudaStream_t st) {
+template <int G, bool FRONT>
+cudaError_t launch_long(const DecodeLaunch& L, const DecodeFront* F, int chunk, int nsplit,
+                        cudaStream_t st) {
   static DeviceFlags configured;
   cudaError_t e = configured.once([] {
-    return cudaFuncSetAttribute(attn_decode_long_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                L_SMEM);
+    return cudaFuncSetAttribute(attn_decode_long_kernel<G, FRONT>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, L_SMEM);
   });
   if (e != cudaSuccess) return e;
   CUtensorMap tk, tv;
@@ -954,6 +1043,19 @@ cudaError_t launch_long(const DecodeLaunch& L, int chunk, int nsplit, cudaStream
   p.status = L.status;
   p.counters = L.counters;
   p.partials = L.partials;
+  p.kf = F ? F->k : nullptr;
+  p.vf = F ? F->v : nullptr;
+  p.q_norm = F ? F->q_norm : nullptr;
+  p.k_norm = F ? F->k_norm : nullptr;
+  p.cos = F ? F->cos : nullptr;
+  p.sin = F ? F->sin : nullptr;
+  p.kcache = const_cast<uint16_t*>(L.one.keys);
+  p.vcache = const_cast<uint16_t*>(L.one.values);
+  p.kv_stride = L.one.kv_stride;
+  p.rotary = F ? int(F->rotary) : 0;
+  p.gemma = F && F->gemma ? 1 : 0;
+  p.eps = F ? F->eps : 0.f;
+  p.inv_dim = 1.0f / float(HDM);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(nsplit), unsigned(L.hkv), unsigned(L.rows));
   cfg.blockDim = dim3(kThreadsL);
@@ -964,12 +1066,15 @@ cudaError_t launch_long(const DecodeLaunch& L, int chunk, int nsplit, cudaStream
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attn_decode_long_kernel<G>, tk, tv, p);
+  return cudaLaunchKernelEx(&cfg, attn_decode_long_kernel<G, FRONT>, tk, tv, p);
 }
 }  // namespace
 
-bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err) {
+bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err,
+                             const DecodeFront* front) {
   if (L.seqs != nullptr || L.nseq != 1 || L.head_dim != HDM) return false;
+  if (front && (L.rows != 1 || front->rotary < 0 || front->rotary % 32 != 0 || front->rotary > HDM))
+    return false;
   if ((reinterpret_cast<uintptr_t>(L.one.q) | reinterpret_cast<uintptr_t>(L.one.keys) |
        reinterpret_cast<uintptr_t>(L.one.values) | reinterpret_cast<uintptr_t>(L.one.output)) & 15)
     return false;
@@ -982,10 +1087,11 @@ bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t
   if (chunk > (int64_t(1) << 30) || nsplit > L.nsplit || max_n + BT > (int64_t(1) << 31)) return false;
   // the merge keeps the splits' maxima, sums and weights in 16 KB of shared memory
   if (nsplit * L.gqa * 12 > 16384) return false;
-#define HB_LONG_CASE(G_)                                                       \
-  if (L.gqa == G_) {                                                           \
-    *err = launch_long<G_>(L, int(chunk), int(nsplit), st);                    \
-    return true;                                                               \
+#define HB_LONG_CASE(G_)                                                                      \
+  if (L.gqa == G_) {                                                                          \
+    *err = front ? launch_long<G_, true>(L, front, int(chunk), int(nsplit), st)               \
+                 : launch_long<G_, false>(L, nullptr, int(chunk), int(nsplit), st);           \
+    return true;                                                                              \
   }
   HB_LONG_CASE(1) HB_LONG_CASE(2) HB_LONG_CASE(4) HB_LONG_CASE(8)
 #undef HB_LONG_CASE

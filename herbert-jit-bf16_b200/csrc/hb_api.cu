@@ -277,8 +277,8 @@ size_t hb_attn_decode_workspace_bytes(const hb_attn_spec* s, const hb_attn_call*
 
 // Launches the decode kernel of one sequence on a validated call with the
 // workspace `ws` laid out by plan `pl`.
-static hb_status decode_launch(const hb_attn_spec* s, const hb_attn_call* c, const DecodePlan& pl,
-                               void* ws, hb_stream_t stream, int* status = nullptr) {
+static DecodeLaunch decode_launch_of(const hb_attn_spec* s, const hb_attn_call* c, const DecodePlan& pl,
+                                     void* ws, int* status) {
   DecodeLaunch L;
   L.seqs = nullptr;
   L.one.q = c->q;
@@ -303,6 +303,12 @@ static hb_status decode_launch(const hb_attn_spec* s, const hb_attn_call* c, con
   L.status = status ? status : reinterpret_cast<int*>(base);
   L.counters = reinterpret_cast<unsigned*>(base + pl.counters_off);
   L.partials = reinterpret_cast<float*>(base + pl.partials_off);
+  return L;
+}
+
+static hb_status decode_launch(const hb_attn_spec* s, const hb_attn_call* c, const DecodePlan& pl,
+                               void* ws, hb_stream_t stream, int* status = nullptr) {
+  const DecodeLaunch L = decode_launch_of(s, c, pl, ws, status);
   cudaError_t e = launch_attn_decode(L, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attn_decode launch");
   return HB_OK;
@@ -503,8 +509,8 @@ hb_status hb_kv_append(const hb_kv_spec* s, const hb_kv_call* c, hb_stream_t str
   return HB_OK;
 }
 
-hb_status hb_attn_front(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
-                        const hb_front_call* c, hb_stream_t stream) {
+static hb_status check_front(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
+                             const hb_front_call* c) {
   hb_status r = check_spec(s);
   if (r != HB_OK) return r;
   if (!kv || !f || !c) return fail(HB_ERR_ARG, "kv spec, front spec or call is null");
@@ -539,6 +545,14 @@ hb_status hb_attn_front(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_fr
                   (long long)c->rows, (long long)c->past, (long long)kv->capacity,
                   (long long)kv->max_batch);
   }
+  return HB_OK;
+}
+
+hb_status hb_attn_front(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
+                        const hb_front_call* c, hb_stream_t stream) {
+  hb_status r = check_front(s, kv, f, c);
+  if (r != HB_OK) return r;
+  const int64_t hkv = s->heads / s->gqa;
   FrontLaunch L;
   L.q = c->q;
   L.k = c->k;
@@ -728,6 +742,38 @@ hb_status hb_gdn_prefill(const hb_gdn_shape* s, const hb_gdn_call* c, void* ws, 
 }  // extern "C"
 
 namespace hb {
+
+hb_status attn_layer_row(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
+                         const hb_front_call* fc, const hb_attn_call* ac, void* ws, size_t ws_bytes,
+                         hb_stream_t stream, bool* served) {
+  *served = false;
+  if (!s || !kv || !f || !fc || !ac || fc->rows != 1 || ac->rows != 1 || fc->past != ac->past ||
+      fc->q != ac->q || !fc->keys || fc->keys != ac->keys || fc->values != ac->values ||
+      kv->stride != ac->kv_stride)
+    return HB_OK;
+  // both nodes' checks; a call either refuses goes the two-launch way,
+  // which reports it as before
+  if (check_front(s, kv, f, fc) != HB_OK || check_spec(s) != HB_OK || check_call(s, ac) != HB_OK)
+    return HB_OK;
+  const DecodePlan pl = plan_decode(s, 1, ac->rows, ac->past + ac->rows, row_positions(ac->past, ac->rows));
+  if (check_ws(ws, ws_bytes, pl.bytes) != HB_OK) return HB_OK;
+  const DecodeLaunch L = decode_launch_of(s, ac, pl, ws, nullptr);
+  DecodeFront F;
+  F.k = fc->k;
+  F.v = fc->v;
+  F.q_norm = fc->q_norm;
+  F.k_norm = fc->k_norm;
+  F.cos = fc->cos;
+  F.sin = fc->sin;
+  F.rotary = f->rotary;
+  F.eps = f->eps;
+  F.gemma = f->gemma != 0;
+  cudaError_t e = cudaSuccess;
+  if (!launch_attn_decode_long(L, reinterpret_cast<cudaStream_t>(stream), &e, &F)) return HB_OK;
+  *served = true;
+  if (e != cudaSuccess) return cuda_fail(e, "attn_decode launch (with the front end)");
+  return HB_OK;
+}
 
 hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, const hb_gdn_call* gc,
                         const hb_gdn_norm_call* nc, void* front_ws, size_t front_ws_bytes,

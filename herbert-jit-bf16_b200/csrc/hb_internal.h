@@ -62,9 +62,25 @@ cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
 // head_dim 256: returns false (nothing launched) when the call is not in
 // its domain, else launches and sets *err.
 bool launch_attn_decode_mma(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err);
+// The front end of a one-row call (head-norm-rope of q and k, kv-append of
+// the row's position) for the long decode kernel to run itself.
+struct DecodeFront {
+  uint16_t* k;              // the row's k [hkv][head_dim]: normed and rotated in place
+  const uint16_t* v;        // the row's v
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  const uint16_t* cos;
+  const uint16_t* sin;
+  int64_t rotary;
+  float eps;
+  bool gemma;
+};
 // one sequence longer than 16 x 256 positions: split-KV on the tensor cores
-// (false: not served, the CUDA-core kernel runs)
-bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err);
+// (false: not served, the CUDA-core kernel runs); with `front`, a one-row
+// call that also runs its front end (q normed in place through L.one.q,
+// k and v into L.one.keys / values at position L.one.past)
+bool launch_attn_decode_long(const DecodeLaunch& L, cudaStream_t st, cudaError_t* err,
+                             const DecodeFront* front = nullptr);
 
 // ---------------------------------------------------------- attn prefill
 struct PrefillLaunch {
@@ -169,6 +185,13 @@ cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st);
 // recurrence, gated norm): when the fused kernel serves it (*served), the
 // three calls' checks run first and then the one launch; otherwise nothing
 // happens and the caller runs the nodes.
+// A one-row attention layer given as its two nodes' calls (front end,
+// decode): when both pass their checks and the long decode kernel serves
+// the call (*served), that kernel runs the front end too, in one launch;
+// otherwise nothing happens and the caller runs the nodes.
+hb_status attn_layer_row(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
+                         const hb_front_call* fc, const hb_attn_call* ac, void* ws, size_t ws_bytes,
+                         hb_stream_t stream, bool* served);
 // front_ws holds the header, then the key heads' counters (kRowCounterBytes,
 // zero between calls) when front_ws_bytes covers them.
 hb_status gdn_layer_row(const hb_gdn_shape* s, const hb_gdn_front_call* fc, const hb_gdn_call* gc,

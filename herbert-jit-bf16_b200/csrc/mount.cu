@@ -308,7 +308,6 @@ hb_status hb_mount_attention(hb_mount* m, int64_t layer, const hb_mount_attentio
   fc.values = rt.values;
   fc.rows = c->rows;
   fc.past = c->pos;
-  if ((r = hb_attn_front(&spec, &kv, &front, &fc, stream)) != HB_OK) return after_entry(m, r, false);
   // attention + output gate (lowering.rs:600-666), by regime
   hb_attn_call ac{};
   ac.q = c->q;
@@ -320,6 +319,14 @@ hb_status hb_mount_attention(hb_mount* m, int64_t layer, const hb_mount_attentio
   ac.kv_stride = rt.kv_stride;
   ac.capacity = res;
   ac.scale = m->desc.attn_scale;
+  if (c->rows == 1) {
+    // a decode row over a long cache: the decode kernel runs the front end
+    // too (both nodes checked first), in one launch
+    bool served = false;
+    r = attn_layer_row(&spec, &kv, &front, &fc, &ac, m->attn_ws, m->attn_ws_bytes, stream, &served);
+    if (served) return after_entry(m, r, false);
+  }
+  if ((r = hb_attn_front(&spec, &kv, &front, &fc, stream)) != HB_OK) return after_entry(m, r, false);
   if (c->rows == 1)
     return after_entry(m, hb_attn_decode(&spec, &ac, m->attn_ws, m->attn_ws_bytes, stream), true);
   return after_entry(m, hb_attn_prefill(&spec, &ac, m->attn_ws, m->attn_ws_bytes, stream), true);
