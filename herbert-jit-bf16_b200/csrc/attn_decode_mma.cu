@@ -56,7 +56,7 @@ constexpr int M_OFF_RBUF = M_OFF_RML + 16 * 16 * 4;     // received output quads
 constexpr int M_OFF_BAR = M_OFF_RBUF + 528 * 16;
 constexpr int M_SMEM = M_OFF_BAR + 64 + 1024;  // + alignment slack
 constexpr uint32_t M_TMEM_COLS = 64;  // S^T [0, 16), O^T [16, 48)
-enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3 };
+enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3, PEERS = 4, MERGE = 5, M_NBAR = 6 };
 
 struct DecodeMmaParams {
   const uint16_t* q;  // query rows (and gates)
@@ -86,21 +86,22 @@ HB_DEV uint32_t dsmem_addr_m(const void* local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
   return r;
 }
-HB_DEV void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+// Stores into a peer's shared memory that count their bytes on the peer's
+// mbarrier `bar` (complete_tx): the receiver waits on its own barrier.
+HB_DEV void st_async_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(addr),
+               "f"(v), "r"(bar)
+               : "memory");
 }
-HB_DEV void st_cluster_v4(uint32_t addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y),
-               "f"(v.z), "f"(v.w)
+HB_DEV void st_async_v4(uint32_t addr, float4 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
                : "memory");
 }
 // Split cluster barrier: arrive early (this CTA has started), wait later.
 HB_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 HB_DEV void cluster_wait_m() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
-HB_DEV void cluster_sync_m() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
-                   "memory");
-}
 // byte offset of element (row, col) in 128B-swizzled K-major blocks of
 // [rows][64 columns], `block_bytes` apart
 HB_DEV uint32_t swz(int row, int col, int block_bytes) {
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + M_OFF_BAR);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + M_NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
   float* cpart = reinterpret_cast<float*>(smem + M_OFF_PART);
   float* red_m = reinterpret_cast<float*>(smem + M_OFF_RED);  // [4][16]
@@ -131,9 +132,15 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   const int h0 = kh * G;
   const uint16_t* qrow = p.q + int64_t(row) * p.q_row;
 
+  constexpr int Q4 = G * HDM / 4;       // output quads of the unit
+  const int nqs = (Q4 + ns - 1) / ns;    // quads per slice (the last one may be short)
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
+    for (int i = 0; i < M_NBAR; ++i) mbar_init(&bar[i], 1);
     *abort_flag = 0;
+    // the bytes every CTA of the cluster will store here: its (m, l) and
+    // the quads of this CTA's output slice
+    const int nq = max(0, min(nqs, Q4 - split * nqs));
+    mbar_arrive_expect_tx(&bar[MERGE], uint32_t(ns) * uint32_t(2 * G * 4 + nq * 16));
     fence_mbar_init();
   }
   if (warp == 4) tmem_alloc(tslot, M_TMEM_COLS);
@@ -142,7 +149,7 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   fence_after_sync();
   const uint32_t tmem = *tslot;
   griddep_launch_dependents();
-  cluster_arrive_relaxed();  // waited for before the first store into a peer
+  cluster_arrive_relaxed();  // warp 4 waits for the whole cluster (PEERS) before any peer store
 
   auto wait = [&](int b, uint32_t parity) -> bool {
     if (*abort_flag) return false;
@@ -196,6 +203,11 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       }
     }
     __syncwarp();
+    // every CTA of the cluster has started and initialised its barriers:
+    // the wait runs here, beside the softmax, and releases the stores into
+    // the peers through PEERS
+    cluster_wait_m();
+    if (lane == 0) mbar_arrive(&bar[PEERS]);
     nbar_sync(3, kThreadsM);  // P^T written
     if (lane == 0 && has && !*abort_flag) {
       // O^T = V^T P^T: M128 (dims) N16 K128, V MN-major (64-dim blocks 16 KB
@@ -316,27 +328,32 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   // quads s merges (quads [s nqs, (s + 1) nqs)); after one cluster barrier
   // each CTA merges its slice from its own shared memory and nothing reads
   // a peer any more.
-  constexpr int Q4 = G * HDM / 4;
-  const int nqs = (Q4 + ns - 1) / ns;  // quads per slice (the last one may be short)
   float* rml = reinterpret_cast<float*>(smem + M_OFF_RML);      // [split][16]
   float4* rbuf = reinterpret_cast<float4*>(smem + M_OFF_RBUF);  // [split][nqs]
-  if (warp < 4) nbar_sync(2, 128);  // this CTA's partial is complete
-  __syncwarp();
-  cluster_wait_m();  // every CTA of the cluster has started
   if (warp < 4) {
-    for (int i = tid; i < ns * 2 * G; i += 128) {
-      const int sp = i / (2 * G), k = i % (2 * G);
-      st_cluster_f32(dsmem_addr_m(rml + split * 16 + k, uint32_t(sp)), cpart[G * HDM + k]);
+    nbar_sync(2, 128);  // this CTA's partial is complete
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar[PEERS], 0))) {
+      if (lane == 0) record_status(p.status, kStatusTimeout);
+      *abort_flag = 1;
+    } else {
+      for (int i = tid; i < ns * 2 * G; i += 128) {
+        const int sp = i / (2 * G), k = i % (2 * G);
+        st_async_f32(dsmem_addr_m(rml + split * 16 + k, uint32_t(sp)), cpart[G * HDM + k],
+                     dsmem_addr_m(&bar[MERGE], uint32_t(sp)));
+      }
+      for (int q = tid; q < Q4; q += 128) {
+        const int sp = q / nqs, qi = q - sp * nqs;
+        st_async_v4(dsmem_addr_m(rbuf + split * nqs + qi, uint32_t(sp)),
+                    *reinterpret_cast<const float4*>(cpart + q * 4),
+                    dsmem_addr_m(&bar[MERGE], uint32_t(sp)));
+      }
     }
-    for (int q = tid; q < Q4; q += 128) {
-      const int sp = q / nqs, qi = q - sp * nqs;
-      st_cluster_v4(dsmem_addr_m(rbuf + split * nqs + qi, uint32_t(sp)),
-                    *reinterpret_cast<const float4*>(cpart + q * 4));
+    // every CTA's stores into this one have landed (counted in bytes)
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar[MERGE], 0))) {
+      if (lane == 0) record_status(p.status, kStatusTimeout);
+      *abort_flag = 1;
     }
   }
-  fence_before_sync();
-  __syncwarp();
-  cluster_sync_m();  // every store into this CTA has landed
   if (warp < 4) {
     // the splits' weights 2^(m_r - M) and the merged sums, one warp per head
     float* wb = reinterpret_cast<float*>(smem + M_OFF_K);  // [split][16] (the K tile is done)
@@ -370,6 +387,8 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       }
     }
   }
+  fence_before_sync();
+  __syncthreads();  // every TMEM read of this CTA is done
   if (warp == 4) {
     fence_after_sync();
     tmem_dealloc(tmem, M_TMEM_COLS);
