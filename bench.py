@@ -59,7 +59,9 @@ sys.path[:0] = [os.path.join(ROOT, "herbert-jit-bf16_b200")]
 HQ, HKV, HD = 16, 4, 256
 NK, NV, HKD, HVD = 16, 32, 128, 128
 PREFILL_S = 4096
-DECODE_N = 2048
+# cached positions of the decode configuration (BASELINE configs[0] at
+# 2048); HB_DECODE_N measures the same step over a longer cache
+DECODE_N = int(os.environ.get("HB_DECODE_N", 2048))
 GDN_T, GDN_STEPS = 4096, 256
 CP_S = 131072
 FRONT_ROTARY = 64  # Qwen3.5: partial_rotary_factor 0.25 of head_dim 256
@@ -879,7 +881,7 @@ def config_of(cfg, world):
         d = dict(workload="causal prefill SDPA (BASELINE configs[1])", seq_len=PREFILL_S,
                  past=0, **attn, l2=rotated)
     elif cfg == "decode":
-        d = dict(workload="single decode step gated SDPA (BASELINE configs[0])",
+        d = dict(workload="single decode step gated SDPA" + (" (BASELINE configs[0])" if DECODE_N == 2048 else f" over {DECODE_N} cached positions"),
                  kv_len=DECODE_N, **attn, l2=rotated)
     elif cfg == "gdn":
         d = dict(workload="GatedDeltaNet prefill then decode (BASELINE configs[2])",
@@ -1117,7 +1119,8 @@ def run_ours(args):
                          "peak_source": pk["source"] + (
                              ("" if unit != "TFLOP/s" else
                               " sustained (timed region >= 0.5 s)" if sustained else " burst")),
-                         "traffic": None if cfg == "cp" and world > 1 else NCU_TRAFFIC.get(cfg)},
+                         "traffic": None if (cfg == "cp" and world > 1) or (cfg == "decode" and DECODE_N != 2048)
+                                    else NCU_TRAFFIC.get(cfg)},
             "e2e": {"value": round(value_of(total_work, t_e2e / args.steps, wl.units), 4),
                     "unit": wl.units, "h2d_bytes_per_step": int(wl.h2d),
                     "d2h_bytes_per_step": int(wl.d2h)},

@@ -568,7 +568,8 @@ HB_API hb_status hb_mount_status(hb_mount *mount, hb_stream_t stream);
  * (src/jit/execution/runtime.rs:144-151, 310-327; program.rs:289).  Refusals
  * before any launch (declines, bad arguments) do not poison.  Reset after the
  * caller has restored (hb_snapshot_restore) or cleared every state buffer the
- * failed call may have touched; it clears the workspaces' status words. */
+ * failed call may have touched; it clears the workspaces' status words and
+ * the one-row DeltaNet launches' write-back counters. */
 HB_API int hb_mount_needs_reset(const hb_mount *mount);
 HB_API hb_status hb_mount_reset(hb_mount *mount, hb_stream_t stream);
 
@@ -582,6 +583,12 @@ typedef struct hb_mount_attention_call {
     int64_t rows;              /* 1 .. max_rows                                                     */
     int64_t pos;               /* position of row 0 (pos + rows <= kv_reserve)                      */
 } hb_mount_attention_call;
+/* One attention layer's block: head-norm-rope of q and k, kv-append, then the
+ * attention and gate (decode for one row, prefill otherwise).  A one-row
+ * block over more than 4096 cached positions (head_dim 256) runs as one
+ * launch -- the split-KV decode does the front end itself -- with the same
+ * bits as the node-by-node path; a block either node refuses takes that path
+ * and is reported as before. */
 HB_API hb_status hb_mount_attention(hb_mount *mount, int64_t layer, const hb_mount_attention_call *call,
                                     hb_stream_t stream);
 
@@ -597,6 +604,11 @@ typedef struct hb_mount_delta_call {
     float *out_f32;               /* optional f32 copy of out (NULL: not written)                */
     int64_t rows;                 /* 1 .. max_rows                                               */
 } hb_mount_delta_call;
+/* One DeltaNet layer's block: conv + gates, L2 + recurrence, gated norm.  A
+ * one-row block (conv kernel 4, hkd 64 or 128, hvd a multiple of 32 up to
+ * 128) runs as one launch with the node-by-node path's bits; every node's
+ * checks run before it, so a refused one-row call launches nothing and does
+ * not poison the mount. */
 HB_API hb_status hb_mount_delta(hb_mount *mount, int64_t layer, const hb_mount_delta_call *call,
                                 hb_stream_t stream);
 
