@@ -11,15 +11,23 @@
 // column for the whole call, holds its hkd values in registers, and runs the
 // kd sums in increasing order with separate multiply and add (__fmul_rn /
 // __fadd_rn): the outputs and the state are the reference's bits.  Grid =
-// (value heads, hvd/32), one warp per CTA; the state crosses HBM once per
-// call however many positions the call carries.
+// (value heads, hvd/32); the state crosses HBM once per call however many
+// positions the call carries.
+//
+// CTA = one state warp and two producer warps.  The producers (even and odd
+// positions) stage each position's inputs in an 8-slot shared-memory ring
+// ahead of use: the key head's q and k, L2-normalised (sequential sums, as
+// the reference) with q scaled, the CTA's 32 v values, beta and decay.  The
+// state warp then only runs the recurrence, and runs two positions' sums at
+// once: for each kd, pass 2 of position t (S += k_t delta_t, out_t += S q_t)
+// and then pass 1 of position t + 1 (S *= decay_{t+1}, kv_{t+1} += S k_{t+1})
+// -- per element the same operations in the same order as one position
+// after the other, with the two dependent sums interleaved.
 //
 // The CTA's state slice [hkd rows][32 columns] f32 moves as one TMA tile
-// each way (shared memory in between): with one warp per SM, per-thread
-// loads of 128 strided rows left the step latency-bound on memory
-// parallelism (a loads-and-stores-only kernel took 9 us per step, the TMA
-// tile takes one request).  The first position's L2 norms run while the
-// tile is in flight.
+// each way (shared memory in between): per-thread loads of 128 strided rows
+// left a step latency-bound on memory parallelism, the TMA tile takes one
+// request.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -44,22 +52,74 @@ struct GdnParams {
   int* status;  // device status word: the caller's workspace or the per-device word
 };
 
+constexpr int kRing = 8;       // positions staged ahead of the state warp
+constexpr int kProducers = 2;  // warps 1 .. kProducers: positions w - 1, w - 1 + kProducers, ...
+
+// One staged position: normalised (and for q scaled) q and k of the key
+// head, the CTA's 32 v values, beta, decay.
 template <int HKD>
-__global__ void __launch_bounds__(32)
+struct __align__(16) Stage {
+  float q[HKD];
+  float k[HKD];
+  float v[32];
+  float beta, decay, pad[2];
+};
+
+// Pass 2 of position t fused with pass 1 of position t + 1 on the column s:
+// per kd, r = s + k_t delta_t; out += r q_t; r' = r decay_{t+1};
+// kv += r' k_{t+1}; s = r'.  NEXT false: pass 2 alone (the last position).
+template <int HKD, bool NEXT>
+HB_DEV void sweep(float (&s)[HKD], const float* kt, const float* qt, float delta, const float* kn,
+                  float decay_n, float& out, float& kv) {
+  const float4* k4 = reinterpret_cast<const float4*>(kt);
+  const float4* q4 = reinterpret_cast<const float4*>(qt);
+  const float4* n4 = reinterpret_cast<const float4*>(kn);
+  float o = 0.f, a = 0.f;
+#pragma unroll
+  for (int k = 0; k < HKD / 4; ++k) {
+    const float4 kk = k4[k], qq = q4[k];
+    const float kw[4] = {kk.x, kk.y, kk.z, kk.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
+    float nw[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (NEXT) {
+      const float4 nn = n4[k];
+      nw[0] = nn.x; nw[1] = nn.y; nw[2] = nn.z; nw[3] = nn.w;
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float r = __fadd_rn(s[4 * k + e], __fmul_rn(kw[e], delta));
+      o = __fadd_rn(o, __fmul_rn(r, qw[e]));
+      if constexpr (NEXT) {
+        r = __fmul_rn(r, decay_n);
+        a = __fadd_rn(a, __fmul_rn(r, nw[e]));
+      }
+      s[4 * k + e] = r;
+    }
+  }
+  out = o;
+  kv = a;
+}
+
+template <int HKD>
+__global__ void __launch_bounds__(32 * (1 + kProducers), 1)
     gdn_decode_kernel(const __grid_constant__ CUtensorMap tmS, const GdnParams p) {
   __shared__ __align__(128) float st[HKD * 32];  // state rows kd, columns col0..col0+31
-  __shared__ __align__(16) float qn[HKD];
-  __shared__ __align__(16) float kn[HKD];
-  __shared__ float inv[2];
-  __shared__ __align__(8) uint64_t bar;
-  const int h = blockIdx.x, lane = threadIdx.x;
+  __shared__ Stage<HKD> ring[kRing];
+  __shared__ float inv[kProducers][2];
+  __shared__ __align__(8) uint64_t bar, full[kRing], empty[kRing];
+  __shared__ int abort_flag;
+  const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col0 = blockIdx.y * 32, col = col0 + lane;
   const int kh = h / (p.nv / p.nk);
   const int64_t key = int64_t(p.nk) * HKD, value = int64_t(p.nv) * p.hvd;
   const int64_t conv = 2 * key + value;
 
-  if (lane == 0) {
+  if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    abort_flag = 0;
     fence_mbar_init();
     sm100::prefetch_tmap(&tmS);
   }
@@ -69,75 +129,116 @@ __global__ void __launch_bounds__(32)
   // first position's lines; a prefetch cannot change what a later load
   // returns).  Every load follows the wait: the previous kernel may be the
   // front end that writes qkv, beta and decay.
-  {
-    const float* row = p.qkv;
+  if (warp == 0) {
     if (lane == 0) sm100::tma_prefetch_l2_2d(&tmS, col0, h * HKD);
     if (lane < HKD / 32) {
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(row + int64_t(kh) * HKD + lane * 32));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(row + key + int64_t(kh) * HKD + lane * 32));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + int64_t(kh) * HKD + lane * 32));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + key + int64_t(kh) * HKD + lane * 32));
     }
-    if (lane == 4) asm volatile("prefetch.global.L2 [%0];" ::"l"(row + 2 * key + int64_t(h) * p.hvd + col0));
-    if (lane == 5) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.beta + h));
-    if (lane == 6) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.decay + h));
   }
-  __syncwarp();
+  __syncthreads();
   griddep_wait();
   griddep_launch_dependents();
-  if (lane == 0) {  // the state tile, in flight while the first position's norms run
+  auto wait = [&](uint64_t* b, uint32_t parity) -> bool {
+    if (*reinterpret_cast<volatile int*>(&abort_flag)) return false;
+    if (__all_sync(0xFFFFFFFFu, mbar_wait(b, parity))) return true;
+    if (lane == 0) record_status(p.status, kStatusTimeout);
+    *reinterpret_cast<volatile int*>(&abort_flag) = 1;
+    return false;
+  };
+
+  if (warp > 0) {  // ------------------------------------------- producers
+    const int w = warp - 1;
+    for (int64_t t = w; t < p.rows; t += kProducers) {
+      const int slot = int(t % kRing);
+      const int64_t use = t / kRing;
+      if (use > 0 && !wait(&empty[slot], uint32_t((use - 1) & 1))) break;
+      Stage<HKD>& S = ring[slot];
+      const float* row = p.qkv + t * conv;
+#pragma unroll
+      for (int i = lane; i < HKD; i += 32) {
+        S.q[i] = row[int64_t(kh) * HKD + i];
+        S.k[i] = row[key + int64_t(kh) * HKD + i];
+      }
+      S.v[lane] = row[2 * key + int64_t(h) * p.hvd + col];
+      if (lane == 0) {
+        S.beta = p.beta[t * p.nv + h];
+        S.decay = p.decay[t * p.nv + h];
+      }
+      __syncwarp();
+      // q <- q * inv_q * scale (the reference scales q inside pass 2, per
+      // element, after the L2 step: the same two roundings), k <- k * inv_k
+      float iq = 1.f, ik = 1.f;
+      if (p.l2) {
+        if (lane < 2) inv[w][lane] = l2_inverse<HKD>(lane == 0 ? S.q : S.k, p.eps);
+        __syncwarp();
+        iq = inv[w][0];
+        ik = inv[w][1];
+      }
+#pragma unroll
+      for (int i = lane; i < HKD; i += 32) {
+        const float qv = p.l2 ? __fmul_rn(S.q[i], iq) : S.q[i];
+        S.q[i] = __fmul_rn(qv, p.scale);
+        if (p.l2) S.k[i] = __fmul_rn(S.k[i], ik);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[slot]);
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------- state warp
+  if (lane == 0) {
     mbar_arrive_expect_tx(&bar, HKD * 32 * 4);
     sm100::tma_load_2d(st, &tmS, &bar, col0, h * HKD);
   }
-  bool loaded = false;
   float s[HKD];
-
-  for (int64_t t = 0; t < p.rows; ++t) {
-    const float* row = p.qkv + t * conv;
-    // every load of the position first, so their latencies overlap
-    const float beta = p.beta[t * p.nv + h];
-    const float decay = p.decay[t * p.nv + h];
-    const float v = row[2 * key + int64_t(h) * p.hvd + col];
-#pragma unroll
-    for (int i = lane; i < HKD; i += 32) {
-      qn[i] = row[int64_t(kh) * HKD + i];
-      kn[i] = row[key + int64_t(kh) * HKD + i];
-    }
-    __syncwarp();
-    // qn <- q * inv_q * scale (the reference scales q inside pass 2, per
-    // element, after the L2 step: the same two roundings), kn <- k * inv_k
-    float iq = 1.f, ik = 1.f;
-    if (p.l2) {
-      if (lane < 2) inv[lane] = l2_inverse<HKD>(lane == 0 ? qn : kn, p.eps);
-      __syncwarp();
-      iq = inv[0];
-      ik = inv[1];
-    }
-#pragma unroll
-    for (int i = lane; i < HKD; i += 32) {
-      const float qv = p.l2 ? __fmul_rn(qn[i], iq) : qn[i];
-      qn[i] = __fmul_rn(qv, p.scale);
-      if (p.l2) kn[i] = __fmul_rn(kn[i], ik);
-    }
-    __syncwarp();
-    if (!loaded) {  // the state tile (first position only)
-      if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar, 0))) {
-        // the call's outputs are not written; the status word tells the caller
-        if (lane == 0) record_status(p.status, kStatusTimeout);
-        mbar_wait(&bar, 0);  // a second bounded wait for the copy in flight
-        return;
-      }
-#pragma unroll
-      for (int kd = 0; kd < HKD; ++kd) s[kd] = st[kd * 32 + lane];
-      loaded = true;
-    }
-
-    const float o = gdn_step_column<HKD>(s, kn, qn, v, beta, decay);
-    p.out[t * value + int64_t(h) * p.hvd + col] = o;
-    __syncwarp();
-  }
-  if (!loaded) {  // no position (the host refuses empty calls): state untouched
-    mbar_wait(&bar, 0);  // the copy in flight lands before the CTA ends (bounded)
+  const bool have = wait(&bar, 0);
+  if (!have) {
+    mbar_wait(&bar, 0);  // a second bounded wait for the copy in flight
     return;
   }
+#pragma unroll
+  for (int kd = 0; kd < HKD; ++kd) s[kd] = st[kd * 32 + lane];
+  bool ok = p.rows > 0 && wait(&full[0], 0);
+  float delta = 0.f;
+  if (ok) {  // pass 1 of position 0: decay, then kv = S^T k
+    const Stage<HKD>& A = ring[0];
+    const float4* k4 = reinterpret_cast<const float4*>(A.k);
+    float kv = 0.f;
+#pragma unroll
+    for (int k = 0; k < HKD / 4; ++k) {
+      const float4 kk = k4[k];
+      const float kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float r = __fmul_rn(s[4 * k + e], A.decay);
+        s[4 * k + e] = r;
+        kv = __fadd_rn(kv, __fmul_rn(r, kw[e]));
+      }
+    }
+    delta = __fmul_rn(__fsub_rn(A.v[lane], kv), A.beta);
+  }
+  for (int64_t t = 0; ok && t < p.rows; ++t) {
+    const int slot = int(t % kRing), nslot = int((t + 1) % kRing);
+    const Stage<HKD>& A = ring[slot];
+    const bool next = t + 1 < p.rows;
+    if (next && !wait(&full[nslot], uint32_t(((t + 1) / kRing) & 1))) {
+      ok = false;
+      break;
+    }
+    const Stage<HKD>& B = ring[nslot];
+    float o, kv;
+    if (next)
+      sweep<HKD, true>(s, A.k, A.q, delta, B.k, B.decay, o, kv);
+    else
+      sweep<HKD, false>(s, A.k, A.q, delta, nullptr, 0.f, o, kv);
+    p.out[t * value + int64_t(h) * p.hvd + col] = o;
+    if (next) delta = __fmul_rn(__fsub_rn(B.v[lane], kv), B.beta);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);  // slot t is read
+  }
+  if (!ok) return;  // the status word tells the caller; the state is not written
 #pragma unroll
   for (int kd = 0; kd < HKD; ++kd) st[kd * 32 + lane] = s[kd];
   sm100::fence_proxy_async_smem();
@@ -182,7 +283,7 @@ cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st) {
   // kernel orders every memory access after it)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(L.shape.nv), unsigned(L.shape.hvd / 32));
-  cfg.blockDim = dim3(32);
+  cfg.blockDim = dim3(32 * (1 + kProducers));
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
