@@ -54,9 +54,12 @@ constexpr int M_OFF_RED = M_OFF_PART + M_PART_MAX;  // [2][4 warps][16] maxima, 
 constexpr int M_OFF_RML = M_OFF_RED + 2 * 4 * 16 * 4;  // [16 splits][16]: m[G], l[G] received
 constexpr int M_OFF_RBUF = M_OFF_RML + 16 * 16 * 4;     // received output quads (<= 528 float4)
 constexpr int M_OFF_BAR = M_OFF_RBUF + 528 * 16;
-constexpr int M_SMEM = M_OFF_BAR + 64 + 1024;  // + alignment slack
+constexpr int M_SMEM = M_OFF_BAR + 128 + 1024;  // + alignment slack
 constexpr uint32_t M_TMEM_COLS = 64;  // S^T [0, 16), O^T [16, 48)
-enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3, PEERS = 4, MERGE = 5, M_NBAR = 6 };
+// K_FULL and KB1..KB3: the K tile's four 64-dim column blocks, each on its
+// own barrier so that the S products start as the first block lands
+enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3, PEERS = 4, MERGE = 5, KB1 = 6, M_NBAR = 9 };
+HB_DEV constexpr int kblock_bar(int cb) { return cb == 0 ? int(K_FULL) : int(KB1) + cb - 1; }
 
 struct DecodeMmaParams {
   const uint16_t* q;  // query rows (and gates)
@@ -176,9 +179,10 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       }
       griddep_wait();
       if (has) {
-        mbar_arrive_expect_tx(&bar[K_FULL], 4 * 16384);
-        for (int cb = 0; cb < 4; ++cb)
-          tma_load_3d(smem + M_OFF_K + cb * 16384, &tmK, &bar[K_FULL], cb * 64, int(p0), kh);
+        for (int cb = 0; cb < 4; ++cb) {
+          mbar_arrive_expect_tx(&bar[kblock_bar(cb)], 16384);
+          tma_load_3d(smem + M_OFF_K + cb * 16384, &tmK, &bar[kblock_bar(cb)], cb * 64, int(p0), kh);
+        }
         mbar_arrive_expect_tx(&bar[V_FULL], 4 * 16384);
         for (int cb = 0; cb < 4; ++cb)
           tma_load_3d(smem + M_OFF_V + cb * 16384, &tmV, &bar[V_FULL], cb * 64, int(p0), kh);
@@ -191,16 +195,20 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       constexpr uint32_t idS = idesc_bf16(BT, NQ, false, false);
       const uint64_t kd0 = sw128_desc(smem_u32(smem + M_OFF_K), 16, 1024),
                      qd0 = sw128_desc(smem_u32(smem + M_OFF_Q), 16, 1024);
-      if (wait(K_FULL, 0)) {
+      bool kok = true;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {  // each column block's 4 products as soon as it lands
+        if (!wait(kblock_bar(cb), 0)) {
+          kok = false;
+          break;
+        }
         fence_after_sync();
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb)
-#pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4)
-            mma_bf16_ss(tmem, desc_add(kd0, cb * 16384 + k4 * 32), desc_add(qd0, cb * 2048 + k4 * 32),
-                        idS, cb > 0 || k4 > 0);
-        mma_commit(&bar[S_DONE]);
+        for (int k4 = 0; k4 < 4; ++k4)
+          mma_bf16_ss(tmem, desc_add(kd0, cb * 16384 + k4 * 32), desc_add(qd0, cb * 2048 + k4 * 32),
+                      idS, cb > 0 || k4 > 0);
       }
+      if (kok) mma_commit(&bar[S_DONE]);
     }
     __syncwarp();
     // every CTA of the cluster has started and initialised its barriers:
@@ -297,13 +305,13 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       *reinterpret_cast<uint16_t*>(smem + M_OFF_P + swz(g, pl, 2048)) = b;
     }
     fence_proxy_async_smem();
-    nbar_sync(2, 128);
-    if (tid < G) {  // the tile's partial (m, l) of head tid
-      cpart[G * HDM + tid] = m[tid];
-      cpart[G * HDM + G + tid] =
-          ((red_l[tid] + red_l[16 + tid]) + red_l[32 + tid]) + red_l[48 + tid];
-    }
-    nbar_sync(3, kThreadsM);  // P^T ready for the MMA
+    nbar_sync(3, kThreadsM);  // P^T ready for the MMA; every warp's sums written
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      if (tid == g) {  // the tile's partial (m, l) of head g
+        cpart[G * HDM + g] = m[g];
+        cpart[G * HDM + G + g] = ((red_l[g] + red_l[16 + g]) + red_l[32 + g]) + red_l[48 + g];
+      }
 
     // O^T out of TMEM: thread = dim 32 warp + lane (+ 128), columns = heads
     if (has) {
