@@ -162,6 +162,10 @@ __global__ void __launch_bounds__(kThreadsM, 1)
     return false;
   };
 
+  // warps 0-3: the gate divisor 1 + exp(-g) of the thread's first output in
+  // this CTA's merge slice, by the reference's steps, formed early so that
+  // the merge only divides
+  float gdiv0 = 1.f;
   if (warp == 4) {  // ------------------------------------------ TMA + MMA
     if (lane == 0) {
       prefetch_tmap(&tmK);
@@ -246,6 +250,13 @@ __global__ void __launch_bounds__(kThreadsM, 1)
             reinterpret_cast<const char*>(qrow + p.gate_offset + int64_t(h0 + g) * HDM) + ln * 128));
     }
     griddep_wait();
+    {
+      const int q0 = split * nqs, nq0 = max(0, min(nqs, Q4 - q0));
+      if (p.gate_offset >= 0 && tid < 4 * nq0) {
+        const int e = q0 * 4 + tid;
+        gdiv0 = gate_divisor(qrow[p.gate_offset + int64_t(h0 + e / HDM) * HDM + e % HDM]);
+      }
+    }
     // Q^T: row h = tid / 8 (zero for h >= G), dims 32 (tid % 8) ..; and the
     // padding rows G..15 of P^T
     {
@@ -363,34 +374,31 @@ __global__ void __launch_bounds__(kThreadsM, 1)
     }
   }
   if (warp < 4) {
-    // the splits' weights 2^(m_r - M) and the merged sums, one warp per head
-    float* wb = reinterpret_cast<float*>(smem + M_OFF_K);  // [split][16] (the K tile is done)
-    float* Lb = wb + 16 * 16;                              // [G]
-    for (int g = warp; g < G; g += 4) {
-      const float mv = lane < ns ? rml[lane * 16 + g] : -INFINITY;
-      const float lv = lane < ns ? rml[lane * 16 + G + g] : 0.f;
-      const float M = warp_max(mv);
-      const float Mu = M == -INFINITY ? 0.f : M;
-      const float w = lane < ns ? fast_exp2(mv - Mu) : 0.f;
-      const float L = warp_sum(lv * w);
-      if (lane < ns) wb[lane * 16 + g] = w;
-      if (lane == 0) Lb[g] = L;
-    }
-    nbar_sync(2, 128);
-    // one output element per thread: the splits' weighted sum, / l, bf16,
-    // the gate with the reference's steps
+    // one output element per thread: its head's maximum over the splits, the
+    // weights 2^(m_r - M) and the merged sum formed by the thread itself (no
+    // block barrier), the weighted sum of the splits, / l, bf16, and the gate
+    // with the reference's steps (its divisor formed at the start)
     const int q0 = split * nqs, nq = max(0, min(nqs, Q4 - q0));
     uint16_t* orow = p.out + int64_t(row) * p.out_row;
     if (!*abort_flag) {
       const float* rf = reinterpret_cast<const float*>(rbuf);
       for (int t = tid; t < 4 * nq; t += 128) {
         const int e = q0 * 4 + t, g = e / HDM, dd = e % HDM;
-        float acc = 0.f;
-        for (int r = 0; r < ns; ++r) acc = fmaf(wb[r * 16 + g], rf[r * nqs * 4 + t], acc);
-        const float Ls = Lb[g];
+        float M = -INFINITY;
+        for (int r = 0; r < ns; ++r) M = fmaxf(M, rml[r * 16 + g]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float acc = 0.f, Ls = 0.f;
+        for (int r = 0; r < ns; ++r) {
+          const float w = fast_exp2(rml[r * 16 + g] - Mu);
+          Ls = fmaf(rml[r * 16 + G + g], w, Ls);
+          acc = fmaf(w, rf[r * nqs * 4 + t], acc);
+        }
         const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
         uint16_t a = f32_to_bf16_cvtne(acc * inv);
-        if (p.gate_offset >= 0) a = gate_bf16(a, qrow[p.gate_offset + int64_t(h0 + g) * HDM + dd]);
+        if (p.gate_offset >= 0) {  // gate_bf16's steps, the divisor formed early
+          const float d = t == tid ? gdiv0 : gate_divisor(qrow[p.gate_offset + int64_t(h0 + g) * HDM + dd]);
+          a = f32_to_bf16_cvtne(__fdiv_rn(bf16_to_f32(a), d));
+        }
         orow[int64_t(h0 + g) * HDM + dd] = a;
       }
     }
