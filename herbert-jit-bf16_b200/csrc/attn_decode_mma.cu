@@ -58,7 +58,9 @@ constexpr int M_SMEM = M_OFF_BAR + 128 + 1024;  // + alignment slack
 constexpr uint32_t M_TMEM_COLS = 64;  // S^T [0, 16), O^T [16, 48)
 // K_FULL and KB1..KB3: the K tile's four 64-dim column blocks, each on its
 // own barrier so that the S products start as the first block lands
-enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3, PEERS = 4, MERGE = 5, KB1 = 6, M_NBAR = 9 };
+// O_DONE / O_DONE2: the two 128-dim halves of O^T
+enum MBar { K_FULL = 0, V_FULL = 1, S_DONE = 2, O_DONE = 3, PEERS = 4, MERGE = 5, KB1 = 6, O_DONE2 = 9,
+            M_NBAR = 10 };
 HB_DEV constexpr int kblock_bar(int cb) { return cb == 0 ? int(K_FULL) : int(KB1) + cb - 1; }
 
 struct DecodeMmaParams {
@@ -230,12 +232,13 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       if (wait(V_FULL, 0)) {
         fence_after_sync();
 #pragma unroll
-        for (int mm = 0; mm < 2; ++mm)
+        for (int mm = 0; mm < 2; ++mm) {  // each half committed on its own: its read-out starts early
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_bf16_ss(tmem + NQ + NQ * mm, desc_add(vd0, 2 * mm * 16384 + kk * 2048),
                         desc_add(pd0, (kk >> 2) * 2048 + (kk & 3) * 32), idPV, kk > 0);
-        mma_commit(&bar[O_DONE]);
+          mma_commit(&bar[mm == 0 ? O_DONE : O_DONE2]);
+        }
       }
     }
     __syncwarp();
@@ -309,27 +312,27 @@ __global__ void __launch_bounds__(kThreadsM, 1)
     for (int g = 0; g < G; ++g) {
       m[g] = fmaxf(fmaxf(red_m[g], red_m[16 + g]), fmaxf(red_m[32 + g], red_m[48 + g]));
       pr[g] = m[g] == -INFINITY ? 0.f : fast_exp2(s[g] - m[g]);  // masked: 2^-inf = 0
-      const float sm = warp_sum(pr[g]);
-      if (lane == 0) red_l[warp * 16 + g] = sm;
       // P^T element (head g, position pl), bf16
       const uint16_t b = uint16_t(pack_bf16x2(pr[g], 0.f) & 0xFFFFu);
       *reinterpret_cast<uint16_t*>(smem + M_OFF_P + swz(g, pl, 2048)) = b;
     }
     fence_proxy_async_smem();
-    nbar_sync(3, kThreadsM);  // P^T ready for the MMA; every warp's sums written
+    nbar_sync(3, kThreadsM);  // P^T ready for the MMA
+    // the tile's maxima, and each warp's part of the sums (added by the
+    // senders below, after the block barrier that completes the partial)
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-      if (tid == g) {  // the tile's partial (m, l) of head g
-        cpart[G * HDM + g] = m[g];
-        cpart[G * HDM + G + g] = ((red_l[g] + red_l[16 + g]) + red_l[32 + g]) + red_l[48 + g];
-      }
+    for (int g = 0; g < G; ++g) {
+      const float sm = warp_sum(pr[g]);
+      if (lane == 0) red_l[warp * 16 + g] = sm;
+      if (tid == g) cpart[G * HDM + g] = m[g];
+    }
 
     // O^T out of TMEM: thread = dim 32 warp + lane (+ 128), columns = heads
     if (has) {
-      ok = __all_sync(0xFFFFFFFFu, wait(O_DONE, 0)) && ok;
-      fence_after_sync();
 #pragma unroll
       for (int mm = 0; mm < 2; ++mm) {
+        ok = __all_sync(0xFFFFFFFFu, wait(mm == 0 ? O_DONE : O_DONE2, 0)) && ok;
+        fence_after_sync();
         uint32_t o[16];
         tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + NQ + NQ * mm, o);
         tmem_wait_ld();
@@ -357,7 +360,10 @@ __global__ void __launch_bounds__(kThreadsM, 1)
     } else {
       for (int i = tid; i < ns * 2 * G; i += 128) {
         const int sp = i / (2 * G), k = i % (2 * G);
-        st_async_f32(dsmem_addr_m(rml + split * 16 + k, uint32_t(sp)), cpart[G * HDM + k],
+        const int g = k - G;  // k >= G: the sum of head g over the four warps
+        const float v = k < G ? cpart[G * HDM + k]
+                              : ((red_l[g] + red_l[16 + g]) + red_l[32 + g]) + red_l[48 + g];
+        st_async_f32(dsmem_addr_m(rml + split * 16 + k, uint32_t(sp)), v,
                      dsmem_addr_m(&bar[MERGE], uint32_t(sp)));
       }
       for (int q = tid; q < Q4; q += 128) {
