@@ -76,10 +76,12 @@ struct DecodeMmaParams {
 HB_DEV void nbar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// The warp's maximum in one instruction (sm_100a; NaN inputs are ignored
+// unless all are NaN, as fmaxf does).
 HB_DEV float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-  return v;
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
 }
 HB_DEV float warp_sum(float v) {
 #pragma unroll
