@@ -100,12 +100,6 @@ HB_DEV void st_async_f32(uint32_t addr, float v, uint32_t bar) {
                "f"(v), "r"(bar)
                : "memory");
 }
-HB_DEV void st_async_v4(uint32_t addr, float4 v, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
-                   addr),
-               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
-               : "memory");
-}
 // Split cluster barrier: arrive early (this CTA has started), wait later.
 HB_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 HB_DEV void cluster_wait_m() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
@@ -170,6 +164,7 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   // this CTA's merge slice, by the reference's steps, formed early so that
   // the merge only divides
   float gdiv0 = 1.f;
+  bool peers = false;  // warps 0-3: every CTA of the cluster has started (stores into peers allowed)
   if (warp == 4) {  // ------------------------------------------ TMA + MMA
     if (lane == 0) {
       prefetch_tmap(&tmK);
@@ -329,21 +324,35 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       if (tid == g) cpart[G * HDM + g] = m[g];
     }
 
-    // O^T out of TMEM: thread = dim 32 warp + lane (+ 128), columns = heads
-    if (has) {
+    // O^T out of TMEM (thread = dim 32 warp + lane, + 128 in the second
+    // half; columns = heads), each element stored straight into the CTA of
+    // the cluster that merges it (quads [s nqs, (s + 1) nqs) go to CTA s)
+    peers = __all_sync(0xFFFFFFFFu, mbar_wait(&bar[PEERS], 0));
+    if (!peers) {
+      if (lane == 0) record_status(p.status, kStatusTimeout);
+      *abort_flag = 1;
+    }
+    float* rbf = reinterpret_cast<float*>(smem + M_OFF_RBUF);  // receivers: [split][nqs quads]
 #pragma unroll
-      for (int mm = 0; mm < 2; ++mm) {
+    for (int mm = 0; mm < 2; ++mm) {
+      uint32_t o[16];
+      bool got = false;
+      if (has) {
         ok = __all_sync(0xFFFFFFFFu, wait(mm == 0 ? O_DONE : O_DONE2, 0)) && ok;
         fence_after_sync();
-        uint32_t o[16];
         tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + NQ + NQ * mm, o);
         tmem_wait_ld();
+        got = ok;
+      }
+      if (peers) {
         const int dim = mm * 128 + pl;
 #pragma unroll
-        for (int g = 0; g < G; ++g) cpart[g * HDM + dim] = ok ? __uint_as_float(o[g]) : 0.f;
+        for (int g = 0; g < G; ++g) {
+          const int e = g * HDM + dim, r = (e >> 2) / nqs;
+          st_async_f32(dsmem_addr_m(rbf + (split * nqs - r * nqs) * 4 + e, uint32_t(r)),
+                       got ? __uint_as_float(o[g]) : 0.f, dsmem_addr_m(&bar[MERGE], uint32_t(r)));
+        }
       }
-    } else {
-      for (int e = tid; e < G * HDM; e += 128) cpart[e] = 0.f;
     }
   }
 
@@ -355,11 +364,8 @@ __global__ void __launch_bounds__(kThreadsM, 1)
   float* rml = reinterpret_cast<float*>(smem + M_OFF_RML);      // [split][16]
   float4* rbuf = reinterpret_cast<float4*>(smem + M_OFF_RBUF);  // [split][nqs]
   if (warp < 4) {
-    nbar_sync(2, 128);  // this CTA's partial is complete
-    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&bar[PEERS], 0))) {
-      if (lane == 0) record_status(p.status, kStatusTimeout);
-      *abort_flag = 1;
-    } else {
+    nbar_sync(2, 128);  // the tile's maxima and every warp's part of the sums are written
+    if (peers) {
       for (int i = tid; i < ns * 2 * G; i += 128) {
         const int sp = i / (2 * G), k = i % (2 * G);
         const int g = k - G;  // k >= G: the sum of head g over the four warps
@@ -367,12 +373,6 @@ __global__ void __launch_bounds__(kThreadsM, 1)
                               : ((red_l[g] + red_l[16 + g]) + red_l[32 + g]) + red_l[48 + g];
         st_async_f32(dsmem_addr_m(rml + split * 16 + k, uint32_t(sp)), v,
                      dsmem_addr_m(&bar[MERGE], uint32_t(sp)));
-      }
-      for (int q = tid; q < Q4; q += 128) {
-        const int sp = q / nqs, qi = q - sp * nqs;
-        st_async_v4(dsmem_addr_m(rbuf + split * nqs + qi, uint32_t(sp)),
-                    *reinterpret_cast<const float4*>(cpart + q * 4),
-                    dsmem_addr_m(&bar[MERGE], uint32_t(sp)));
       }
     }
     // every CTA's stores into this one have landed (counted in bytes)
