@@ -14,8 +14,9 @@
 //
 // CTA = 1 producer warp + 8 consumer warps.  The producer streams 32-position
 // tiles of K and V with 1-D bulk copies (a tile of one head is contiguous in
-// the reference layout) into a 128 KB shared-memory ring (4 stages at
-// head_dim 256), completion tracked by mbarriers.  Consumer warp w owns positions 4w..4w+3 of every tile and
+// the reference layout) into a shared-memory ring, completion tracked by
+// mbarriers: 96 KB (3 stages at head_dim 256) and two CTAs per SM for groups
+// of up to 4 query heads, 128 KB and one CTA for 8.  Consumer warp w owns positions 4w..4w+3 of every tile and
 // keeps its own online-softmax state (max, sum, G x head_dim accumulator, in
 // the log2 domain).  A lane holds head_dim/32 consecutive dimensions: each K
 // or V row is one 16-byte (head_dim 256) shared-memory load per lane.  The
@@ -67,7 +68,13 @@ cudaError_t noalloc_scratch(void** ptr) {
 namespace {
 
 constexpr int kTile = 32;           // positions per pipeline tile
-constexpr int kRingBytes = 131072;  // K+V tiles in flight per CTA (one CTA per SM)
+// K+V tiles in flight per CTA: groups of up to 4 query heads run two CTAs
+// per SM (96 KB rings: twice the warps to hide each tile's latency chain),
+// larger groups one (128 KB, the registers of 8 heads' accumulators)
+template <int G>
+struct RingBytes { static constexpr int value = G <= 4 ? 98304 : 131072; };
+template <int G>
+struct CtasPerSm { static constexpr int value = G <= 4 ? 2 : 1; };
 constexpr int kConsumerWarps = 8;   // 4 positions per warp per tile
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr uint32_t kFull = 0xFFFFFFFFu;
@@ -161,12 +168,12 @@ HB_DEV float transpose_reduce(float (&v)[NV], int lane) {
 
 HB_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory"); }
 
-template <int HD>
-struct Ring { static constexpr int stages = kRingBytes / (2 * kTile * HD * 2); };
+template <int HD, int G>
+struct Ring { static constexpr int stages = RingBytes<G>::value / (2 * kTile * HD * 2); };
 
 template <int HD, int G, bool CL>
-__global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodeParams p) {
-  constexpr int kStages = Ring<HD>::stages;
+__global__ void __launch_bounds__(kThreads, CtasPerSm<G>::value) attn_decode_kernel(const DecodeParams p) {
+  constexpr int kStages = Ring<HD, G>::stages;
   constexpr int DPL = HD / 32;             // dims per lane
   constexpr int NV = 4 * G;                // partial sums per lane per tile
   constexpr int SH = 5 - Log2<NV>::value;  // lane >> SH = value index
@@ -603,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_decode_kernel(const DecodePa
 
 template <int HD, int G>
 size_t smem_bytes() {
-  constexpr int kStages = Ring<HD>::stages;
+  constexpr int kStages = Ring<HD, G>::stages;
   const size_t ring = size_t(2) * kStages * kTile * HD * sizeof(uint16_t);
   const size_t merge = size_t(kConsumerWarps) * (G * HD + 2 * G) * sizeof(float);
   const size_t body = ((ring > merge ? ring : merge) + 15) / 16 * 16;
