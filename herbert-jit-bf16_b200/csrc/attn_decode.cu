@@ -718,7 +718,7 @@ int decode_chunk(int64_t total_positions, int64_t units, int64_t max_n, int num_
   c = (c + kTile - 1) / kTile * kTile;
   if (c < 2 * kTile) c = 2 * kTile;
   if (c > 8192) c = 8192;
-  // the last CTA stages 3G floats per split in the 128 KB ring: at most
+  // the last CTA stages 3G floats per split in the ring (96 or 128 KB): at most
   // 1024 splits per unit
   const int64_t min_chunk = (max_n + kMaxSplits - 1) / kMaxSplits;
   if (c < min_chunk) c = (min_chunk + kTile - 1) / kTile * kTile;
