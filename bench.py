@@ -76,7 +76,7 @@ L2_BYTES = 126 << 20
 # single-GPU prefill of the whole sequence (the ring's hops are other
 # launches), and None marks a configuration whose launch was not captured.
 NCU_TRAFFIC = {"prefill": 93_118_464, "decode": 8_439_296, "gdn": 504_317_696,
-               "batch": 4_638_916_864, "cp": 39_260_000_000, "cp_hops": None, "front": 56_784_128,
+               "batch": 4_633_303_808, "cp": 39_260_000_000, "cp_hops": None, "front": 56_784_128,
                "gdn_front": 213_700_000, "gdn_norm": 153_000_000, "snapshot": None,
                "mixers": None}
 

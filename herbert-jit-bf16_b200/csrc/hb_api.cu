@@ -108,7 +108,7 @@ namespace {
 
 struct DecodePlan {
   int64_t units;
-  int chunk, nsplit;
+  int chunk, nsplit, ranges;
   size_t counters_off, partials_off, bytes;
 };
 
@@ -119,10 +119,15 @@ DecodePlan plan_decode(const hb_attn_spec* s, int64_t nseq, int64_t rows, int64_
   p.units = mul_sat(mul_sat(nseq, rows), hkv);
   p.chunk = decode_chunk(mul_sat(total_positions, hkv), p.units, max_n, device_sms());
   p.nsplit = int((max_n + p.chunk - 1) / p.chunk);
+  p.ranges = decode_ranges(mul_sat(total_positions, hkv), s->gqa, device_sms());
   p.counters_off = kWsHeader;
   p.partials_off = p.counters_off + align256(size_t(mul_sat(p.units, sizeof(unsigned))));
+  // partial slots: [unit][split] for the split forms, [range + unit] for
+  // the balanced ranges
+  const int64_t split_slots = mul_sat(p.units, p.nsplit);
+  const int64_t range_slots = p.units + p.ranges;
   const int64_t partial_bytes =
-      mul_sat(mul_sat(p.units, p.nsplit),
+      mul_sat(split_slots > range_slots ? split_slots : range_slots,
               mul_sat(int64_t(decode_partial_floats(s->gqa, s->head_dim)), sizeof(float)));
   p.bytes = p.partials_off + align256(size_t(partial_bytes));
   return p;
@@ -299,6 +304,7 @@ static DecodeLaunch decode_launch_of(const hb_attn_spec* s, const hb_attn_call* 
   L.scale = c->scale;
   L.chunk = pl.chunk;
   L.nsplit = pl.nsplit;
+  L.ranges = pl.ranges;
   char* base = static_cast<char*>(ws);
   L.status = status ? status : reinterpret_cast<int*>(base);
   L.counters = reinterpret_cast<unsigned*>(base + pl.counters_off);
@@ -400,6 +406,7 @@ hb_status hb_attn_decode_batch(const hb_attn_spec* s, const hb_decode_seq* seqs,
   L.scale = 1.0f / std::sqrt(float(s->head_dim));
   L.chunk = pl.chunk;
   L.nsplit = pl.nsplit;
+  L.ranges = pl.ranges;
   char* base = static_cast<char*>(ws);
   L.status = reinterpret_cast<int*>(base);
   L.counters = reinterpret_cast<unsigned*>(base + pl.counters_off);

@@ -44,7 +44,8 @@ struct DecodeLaunch {
   int64_t nseq, rows, hkv, gqa, head_dim;
   int64_t q_row, q_head, out_row, gate_offset;
   float scale;
-  int chunk, nsplit;
+  int chunk, nsplit;  // splits of the cluster and tensor-core forms
+  int ranges;         // CTAs of the balanced-range form
   int* status;
   unsigned* counters;
   float* partials;
@@ -56,6 +57,9 @@ cudaError_t noalloc_scratch(void** ptr);
 // Positions per split of the decode kernel: `total_positions` summed over
 // the `units` (row, KV head) pairs, each at most max_n long.
 int decode_chunk(int64_t total_positions, int64_t units, int64_t max_n, int num_sms);
+// CTAs of the balanced-range decode: `unit_positions` summed over the
+// (row, KV head) units.
+int decode_ranges(int64_t unit_positions, int64_t gqa, int num_sms);
 size_t decode_partial_floats(int64_t gqa, int64_t head_dim);
 cudaError_t launch_attn_decode(const DecodeLaunch& L, cudaStream_t st);
 // The tensor-core form for one sequence of at most 16 x 128 positions at

@@ -117,6 +117,43 @@ def test_batched_decode_ragged(cuda_device):
         assert_sdpa_close(bits_of(out), ref, f"batch n={n}")
 
 
+@pytest.mark.parametrize("case", ["300 short", "upper-bound sum", "reuse"])
+def test_batched_decode_balanced_ranges(cuda_device, case):
+    # The batch kernel lays the tiles of all (sequence, KV head) units end to
+    # end and cuts them into one range per CTA: many short sequences (a
+    # range crossing many units, more sequences than threads in the CTA's
+    # scan), a plan from the upper-bound total (sum_past 0: more ranges than
+    # tiles), and two calls through one workspace (counters left at zero).
+    import numpy as np
+    import torch
+    import herbert_b200 as hb
+    if case == "300 short":
+        lens = [int(x) for x in np.random.default_rng(7).integers(1, 100, 300)]
+    else:
+        lens = [1, 3, 40, 64, 65, 700]
+    spec = hb.attention_spec()
+    seqs, keep, refs = [], [], []
+    for i, n in enumerate(lens):
+        inp = AttentionInputs(1, n - 1, capacity=n, seed=5000 + 7 * i)
+        q, k, v = to_dev_bf16(inp.q), to_dev_bf16(inp.keys), to_dev_bf16(inp.values)
+        out = torch.zeros((1, inp.out_row), dtype=torch.int16, device="cuda")
+        keep.append((q, k, v, out))
+        seqs.append(hb.DecodeSeq(q=q.data_ptr(), keys=k.data_ptr(), values=v.data_ptr(),
+                                 output=out.data_ptr(), past=n - 1, kv_stride=inp.kv_stride))
+        refs.append(oracle_attention(inp))
+    table = hb.seq_table(seqs)
+    sum_past = 0 if case == "upper-bound sum" else sum(lens) - len(lens)
+    ws = None
+    for _ in range(2 if case == "reuse" else 1):
+        for _, _, _, out in keep:
+            out.zero_()
+        ws = hb.decode_batch(spec, table, len(lens), max(lens) - 1, sum_past, workspace=ws)
+        torch.cuda.synchronize()
+        ws.status()
+        for (q, k, v, out), ref, n in zip(keep, refs, lens):
+            assert_sdpa_close(bits_of(out), ref, f"{case} n={n}")
+
+
 def test_workspace_too_small_is_refused(cuda_device):
     import ctypes
     import torch
