@@ -237,6 +237,14 @@ class _AttnWorkload(Workload):
 
     def e2e_step(self, i=0):
         q, k, v, out = self.sets[0]
+        n = self.past + self.rows
+        if self.regime == "prefill":
+            # hb_attn_prefill_host: the copies of each block of rows overlap
+            # the computation of the others
+            self.ws = self.hb.prefill_host(self.spec, *self.h_in, self.h_out, q, k, v, out,
+                                           rows=self.rows, past=self.past, kv_stride=n * HD,
+                                           capacity=n, workspace=self.ws)
+            return
         for d, h in zip((q, k, v), self.h_in):
             d.copy_(h, non_blocking=True)
         self.step(0)
@@ -425,6 +433,15 @@ class CpWorkload(Workload):
                                      comm=self.comm, workspace=self.ws, comm_stream=self.side)
 
     def e2e_step(self, i=0):
+        if self.world == 1:
+            # hb_attn_prefill_host: the copies of each block of rows overlap
+            # the computation of the others
+            c = self.chunk
+            self.ws = self.hb.prefill_host(self.spec, self.h_in[0], self.h_in[1][0], self.h_in[1][1],
+                                           self.h_out, self.q, self.kv[0], self.kv[1], self.out,
+                                           rows=2 * c, past=0, kv_stride=2 * c * HD,
+                                           capacity=2 * c, workspace=self.ws)
+            return
         self.q.copy_(self.h_in[0], non_blocking=True)
         self.kv.copy_(self.h_in[1], non_blocking=True)
         self.step()

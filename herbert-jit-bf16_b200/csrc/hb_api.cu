@@ -454,7 +454,6 @@ hb_status hb_decode_shard_plan(const int64_t* cost, int64_t nseq, int32_t parts,
 // Rows from which the tensor-core kernel takes a prefill block; shorter
 // blocks go to the decode kernel, as the reference serves the rows a block
 // kernel does not cover with its decode kernel.
-static constexpr int64_t kPrefillMinRows = 64;
 
 static bool prefill_on_tensor_cores(const hb_attn_spec* s, const hb_attn_call* c) {
   return prefill_serves(s->head_dim) && c->rows >= kPrefillMinRows &&

@@ -269,5 +269,13 @@ bool aligned16(const void* p);
 hb_status check_spec(const hb_attn_spec* s);
 hb_status check_call(const hb_attn_spec* s, const hb_attn_call* c);
 hb_status check_ws(void* ws, size_t have, size_t need);
+// Fewest rows hb_attn_prefill takes to the tensor-core kernel (fewer go to
+// the decode kernel).
+constexpr int64_t kPrefillMinRows = 64;
+// hb_attn_prefill_host's blocks: rows per block (block_rows, or the
+// library's choice when 0) and the number of blocks, the last one taking
+// the rest.
+int64_t prefill_host_block(int64_t rows, int64_t block_rows);
+int64_t prefill_host_blocks(int64_t rows, int64_t block);
 
 }  // namespace hb

@@ -61,6 +61,11 @@ class AttentionCall(ctypes.Structure):
                 ("sink", c_float)]
 
 
+class AttentionHostCall(ctypes.Structure):
+    _fields_ = [("dev", AttentionCall), ("q_host", c_void_p), ("keys_host", c_void_p),
+                ("values_host", c_void_p), ("out_host", c_void_p), ("block_rows", c_int64)]
+
+
 class DecodeSeq(ctypes.Structure):
     _fields_ = [("q", c_void_p), ("keys", c_void_p), ("values", c_void_p),
                 ("output", c_void_p), ("past", c_int64), ("kv_stride", c_int64)]
@@ -182,6 +187,9 @@ _SIGNATURES = {
     "hb_attn_prefill_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionCall)]),
     "hb_attn_prefill": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionCall), c_void_p, c_size_t,
                                        c_void_p]),
+    "hb_attn_prefill_host_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionHostCall)]),
+    "hb_attn_prefill_host": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionHostCall), c_void_p,
+                                            c_size_t, c_void_p]),
     "hb_kv_append": (ctypes.c_int, [_P(KvSpec), _P(KvCall), c_void_p]),
     "hb_attn_front": (ctypes.c_int, [_P(AttentionSpec), _P(KvSpec), _P(FrontSpec), _P(FrontCall),
                                      c_void_p]),
@@ -363,6 +371,34 @@ def attention(spec: AttentionSpec, q, keys, values, out, *, rows: int, past: int
         workspace.ensure(nbytes, stream)
     check(run(ctypes.byref(spec), ctypes.byref(call), c_void_p(workspace.ptr), workspace.nbytes,
               _stream(stream)))
+    return workspace
+
+
+def prefill_host(spec: AttentionSpec, q_host, keys_host, values_host, out_host, q, keys, values,
+                 out, *, rows: int, past: int, kv_stride: int, capacity: int = 0,
+                 scale: float | None = None, block_rows: int = 0,
+                 workspace: Workspace | None = None, stream=None) -> Workspace:
+    """hb_attn_prefill_host: prefill whose q rows, new K/V positions and output
+    are host tensors (pin them for asynchronous copies) mirroring the device
+    tensors q, keys, values, out; copies and computation overlap block by
+    block.  Returns the workspace used."""
+    dev = AttentionCall(q=_ptr(q), keys=_ptr(keys), values=_ptr(values), output=_ptr(out),
+                        rows=rows, past=past, kv_stride=kv_stride, capacity=capacity,
+                        scale=(1.0 / spec.head_dim ** 0.5) if scale is None else scale, sink=0.0)
+    call = AttentionHostCall(dev=dev, q_host=q_host.data_ptr(), keys_host=keys_host.data_ptr(),
+                             values_host=values_host.data_ptr(), out_host=out_host.data_ptr(),
+                             block_rows=block_rows)
+    L = lib()
+    nbytes = L.hb_attn_prefill_host_workspace_bytes(ctypes.byref(spec), ctypes.byref(call))
+    if nbytes == 0:
+        check(L.hb_attn_prefill_host(ctypes.byref(spec), ctypes.byref(call), None, 0,
+                                     _stream(stream)))
+    if workspace is None:
+        workspace = Workspace(nbytes, q.device, stream)
+    else:
+        workspace.ensure(nbytes, stream)
+    check(L.hb_attn_prefill_host(ctypes.byref(spec), ctypes.byref(call), c_void_p(workspace.ptr),
+                                 workspace.nbytes, _stream(stream)))
     return workspace
 
 

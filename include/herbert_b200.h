@@ -6,8 +6,9 @@
  * decode over an f32 per-head state, chunked prefill).
  *
  * Conventions
- *  - Every pointer in a *_call record is DEVICE memory; records themselves
- *    are read on the host during the call (they may live on the stack).
+ *  - Every pointer in a *_call record is DEVICE memory (except the *_host
+ *    fields of hb_attn_host_call); records themselves are read on the host
+ *    during the call (they may live on the stack).
  *  - Strides are in ELEMENTS (bf16 for attention, f32 for DeltaNet), as in
  *    the reference's call records.
  *  - Layouts are the reference's:
@@ -202,6 +203,40 @@ HB_API hb_status hb_decode_shard_plan(const int64_t *cost, int64_t nseq, int32_t
 HB_API size_t hb_attn_prefill_workspace_bytes(const hb_attn_spec *spec, const hb_attn_call *call);
 HB_API hb_status hb_attn_prefill(const hb_attn_spec *spec, const hb_attn_call *call,
                           void *workspace, size_t workspace_bytes, hb_stream_t stream);
+
+/*
+ * Prefill from host memory: hb_attn_prefill for rows whose q rows, new K/V
+ * positions and output live in host memory (the reference hands its prefill
+ * node host buffers owned by the Runner, src/jit/model.rs:570-611), with the
+ * transfers overlapped with the computation.  `dev` is the device call
+ * (device buffers with the same row strides and KV layout, rows, past,
+ * kv_stride, capacity, scale); positions [0, past) must already be in the
+ * device cache.  The host buffers mirror the device layouts: q_host
+ * [rows][q_row], keys_host/values_host [kv_head][kv_stride] of which
+ * positions past .. past+rows-1 are copied, out_host [rows][out_row].  The
+ * rows are cut into blocks of `block_rows` (a multiple of 128; 0 = about
+ * sixteen blocks of at least 512 rows; a remainder under 64 rows joins the
+ * last block): block j's inputs are copied on the
+ * library's copy stream, its prefill runs on `stream` once they have
+ * landed, and its output is copied back on another copy stream, so that
+ * copies and computation overlap.
+ * Every row is computed exactly as by hb_attn_prefill over all the rows.
+ * On return the work, copies included, is ordered on `stream`; pinned host
+ * memory lets the copies run asynchronously.  The calls on one device queue
+ * their work one at a time (a lock), and may be captured in a graph.
+ */
+typedef struct hb_attn_host_call {
+    hb_attn_call dev;           /* device buffers and the call                 */
+    const uint16_t *q_host;     /* [rows][q_row] bf16                          */
+    const uint16_t *keys_host;  /* [kv_head][kv_stride] bf16                   */
+    const uint16_t *values_host;
+    uint16_t *out_host;         /* [rows][out_row] bf16                        */
+    int64_t block_rows;         /* rows per block, a multiple of 128; 0: auto */
+} hb_attn_host_call;
+HB_API size_t hb_attn_prefill_host_workspace_bytes(const hb_attn_spec *spec,
+                                                   const hb_attn_host_call *call);
+HB_API hb_status hb_attn_prefill_host(const hb_attn_spec *spec, const hb_attn_host_call *call,
+                                      void *workspace, size_t workspace_bytes, hb_stream_t stream);
 
 /*
  * Context-parallel causal prefill over a ring of P GPUs.  No counterpart in
