@@ -215,7 +215,7 @@ HB_API hb_status hb_attn_prefill(const hb_attn_spec *spec, const hb_attn_call *c
  * [rows][q_row], keys_host/values_host [kv_head][kv_stride] of which
  * positions past .. past+rows-1 are copied, out_host [rows][out_row].  The
  * rows are cut into blocks of `block_rows` (a multiple of 128; 0 = about
- * sixteen blocks of at least 512 rows; a remainder under 64 rows joins the
+ * sixteen blocks of at least 1024 rows; a remainder under 64 rows joins the
  * last block): block j's inputs are copied on the
  * library's copy stream, its prefill runs on `stream` once they have
  * landed, and its output is copied back on another copy stream, so that
