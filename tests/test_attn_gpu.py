@@ -154,6 +154,46 @@ def test_batched_decode_balanced_ranges(cuda_device, case):
             assert_sdpa_close(bits_of(out), ref, f"{case} n={n}")
 
 
+def test_batched_decode_misaligned_entry_is_skipped(cuda_device):
+    # One table entry whose K pointer is 2 bytes off: the kernel checks each
+    # entry before its bulk copies, issues no load and writes no output for
+    # it, and reports HB_ERR_ARG through the workspace; the other sequences
+    # match the oracle, and the workspace serves the next (good) call.  The entry
+    # spans several ranges, so its partials and counter still run.
+    import torch
+    import herbert_b200 as hb
+    lens = [300, 5000, 700]
+    spec = hb.attention_spec()
+    keep, refs = [], []
+    for i, n in enumerate(lens):
+        inp = AttentionInputs(1, n - 1, capacity=n + 8, seed=7000 + 3 * i)
+        q, k, v = to_dev_bf16(inp.q), to_dev_bf16(inp.keys), to_dev_bf16(inp.values)
+        out = torch.zeros((1, inp.out_row), dtype=torch.int16, device="cuda")
+        keep.append((q, k, v, out, inp))
+        refs.append(oracle_attention(inp))
+
+    def table(bad):
+        return hb.seq_table([hb.DecodeSeq(q=q.data_ptr(), keys=k.data_ptr() + (2 if bad and i == 1 else 0),
+                                          values=v.data_ptr(), output=out.data_ptr(), past=n - 1,
+                                          kv_stride=inp.kv_stride)
+                             for i, ((q, k, v, out, inp), n) in enumerate(zip(keep, lens))])
+
+    t_bad, t_good = table(True), table(False)
+    ws = hb.decode_batch(spec, t_bad, len(lens), max(lens) - 1, sum(lens) - len(lens))
+    torch.cuda.synchronize()
+    with pytest.raises(hb.HBError) as err:
+        ws.status()
+    assert err.value.status == hb.HB_ERR_ARG
+    assert not bits_of(keep[1][3]).any(), "no output for the skipped entry"
+    for j in (0, 2):
+        assert_sdpa_close(bits_of(keep[j][3]), refs[j], f"batch n={lens[j]} beside a bad entry")
+    hb.decode_batch(spec, t_good, len(lens), max(lens) - 1, sum(lens) - len(lens), workspace=ws)
+    torch.cuda.synchronize()
+    ws.status()
+    for (q, k, v, out, inp), ref, n in zip(keep, refs, lens):
+        assert_sdpa_close(bits_of(out), ref, f"batch n={n} after the bad call")
+
+
 def test_workspace_too_small_is_refused(cuda_device):
     import ctypes
     import torch
