@@ -223,7 +223,10 @@ HB_API hb_status hb_attn_prefill(const hb_attn_spec *spec, const hb_attn_call *c
  * Every row is computed exactly as by hb_attn_prefill over all the rows.
  * On return the work, copies included, is ordered on `stream`; pinned host
  * memory lets the copies run asynchronously.  The calls on one device queue
- * their work one at a time (a lock), and may be captured in a graph.
+ * their work one at a time (a lock) on the library's two copy streams of
+ * that device, and may be captured in a graph; a captured call keeps those
+ * streams in its capture until the capture ends, so no other call on the
+ * device may run meanwhile (it would fail with HB_ERR_CUDA).
  */
 typedef struct hb_attn_host_call {
     hb_attn_call dev;           /* device buffers and the call                 */
