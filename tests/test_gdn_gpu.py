@@ -12,6 +12,9 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("rows,nk,nv,hkd,hvd,l2,warm", [
     (1, 16, 32, 128, 128, True, False),    # one decode step at Qwen3.5 geometry
+    (1, 16, 32, 128, 128, True, True),     # the one-row form, warm state
+    (1, 4, 8, 64, 128, False, True),       # the one-row form at hkd 64, no L2 step
+    (1, 2, 4, 128, 96, True, True),        # one row at hvd 96: the pipelined form
     (7, 16, 32, 128, 128, True, True),
     (4, 2, 4, 128, 64, False, True),
     (3, 4, 4, 64, 96, True, False),
