@@ -323,13 +323,17 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) nxt[j] = x4[4 * (b + 1) + j];
           }
+          // the block's squares first (independent), then the ordered sum
+          float sq[16];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            sum = __fadd_rn(sum, __fmul_rn(cur[j].x, cur[j].x));
-            sum = __fadd_rn(sum, __fmul_rn(cur[j].y, cur[j].y));
-            sum = __fadd_rn(sum, __fmul_rn(cur[j].z, cur[j].z));
-            sum = __fadd_rn(sum, __fmul_rn(cur[j].w, cur[j].w));
+            sq[4 * j] = __fmul_rn(cur[j].x, cur[j].x);
+            sq[4 * j + 1] = __fmul_rn(cur[j].y, cur[j].y);
+            sq[4 * j + 2] = __fmul_rn(cur[j].z, cur[j].z);
+            sq[4 * j + 3] = __fmul_rn(cur[j].w, cur[j].w);
           }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sum = __fadd_rn(sum, sq[e]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
         }
@@ -361,7 +365,7 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
   asm volatile("bar.sync 1, 64;" ::: "memory");  // kn, qn ready
   const float4* k4 = reinterpret_cast<const float4*>(kn_s);
   const float4* q4 = reinterpret_cast<const float4*>(qn_s);
-  constexpr int B = 4;  // operands read one block of B ahead of the sums
+  constexpr int B = 8;  // operands read one block of B ahead of the sums
   // pass 1: decay, then kv = S^T k (kd ascending)
   float kv = 0.f;
   {
@@ -374,6 +378,8 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
 #pragma unroll
         for (int j = 0; j < B / 4; ++j) nxt[j] = k4[(B / 4) * (b + 1) + j];
       }
+      // the block's decayed rows and products first, then the ordered sum
+      float pr[B];
 #pragma unroll
       for (int j = 0; j < B / 4; ++j) {
         const float kw[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
@@ -382,9 +388,11 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
           const int kd = B * b + 4 * j + e;
           const float r = __fmul_rn(s[kd], decay);
           s[kd] = r;
-          kv = __fadd_rn(kv, __fmul_rn(r, kw[e]));
+          pr[4 * j + e] = __fmul_rn(r, kw[e]);
         }
       }
+#pragma unroll
+      for (int e = 0; e < B; ++e) kv = __fadd_rn(kv, pr[e]);
 #pragma unroll
       for (int j = 0; j < B / 4; ++j) cur[j] = nxt[j];
     }
@@ -409,6 +417,8 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
           qx[j] = q4[(B / 4) * (b + 1) + j];
         }
       }
+      // the block's new rows and products first, then the ordered sum
+      float pr[B];
 #pragma unroll
       for (int j = 0; j < B / 4; ++j) {
         const float kw[4] = {kc[j].x, kc[j].y, kc[j].z, kc[j].w};
@@ -417,10 +427,12 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
         for (int e = 0; e < 4; ++e) {
           const int kd = B * b + 4 * j + e;
           const float r = __fadd_rn(s[kd], __fmul_rn(kw[e], delta));
-          o = __fadd_rn(o, __fmul_rn(r, qw[e]));
+          pr[4 * j + e] = __fmul_rn(r, qw[e]);
           srow[kd * HVD] = r;
         }
       }
+#pragma unroll
+      for (int e = 0; e < B; ++e) o = __fadd_rn(o, pr[e]);
 #pragma unroll
       for (int j = 0; j < B / 4; ++j) {
         kc[j] = kx[j];
