@@ -476,25 +476,39 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
 // A decode step of a whole DeltaNet layer in one launch: conv + SiLU of the
 // row, the gates, the L2 step, the recurrence and the gated norm, each in
 // the operation order of its own kernel above (and of the reference), so
-// the results are the three-launch path's bits.  CTA h = V head h, 4 hvd
-// threads: thread t < hkd owns q / k channel t of the head's key head,
-// thread t < hvd v channel t.  The recurrence gives state column c to four
-// threads, one per quarter of the kd rows (thread q hvd + c holds rows
-// [q hkd/4, (q + 1) hkd/4) in registers): all four form their products at
-// once, then the sums over kd run quarter after quarter in increasing kd,
-// each continuing the previous quarter's value through shared memory -- the
-// reference's order, with 32-step code (not 128) to fetch and run.
+// the results are the three-launch path's bits.
 //
-// The V heads of one key head read the same q / k inputs and conv state and
+// A step is a chain of latencies: the row's inputs, the two L2 sums, pass 1
+// (kv) and pass 2 (out) of the recurrence, each a sequential sum of hkd
+// terms, then the gated norm over the head's hvd outputs.  So each V head is
+// a cluster of hvd / 32 CTAs, CTA c owning the state columns [32 c, 32 c +
+// 32), and every CTA runs the head's front end itself:
+//   warp 0        the v channels of its columns (conv + SiLU), then the
+//                 recurrence of its columns: the state column loaded straight
+//                 into each lane's registers right after griddepcontrol.wait
+//                 (landing while the front end runs), each pass forming a
+//                 block's products before its ordered sum with the block's
+//                 k / q read from shared memory one block ahead, every state
+//                 row stored as pass 2 finishes it;
+//   warps 1..     q / k channel t - 32 of the key head (conv + SiLU); warp 1's
+//                 lanes 0 / 1 then run the q / k L2 sums and the warp scales
+//                 q and k;
+//   the last warp the gates, then the key head's reader count.
+// The gated norm needs the head's whole output row: each CTA stores its 32
+// outputs into every CTA of the cluster with st.async, counted on the
+// receiver's mbarrier (no cluster barrier on the path), and every CTA forms
+// the same norm and finishes its own columns.
+//
+// The CTAs of one key head read the same q / k inputs and conv state and
 // compute the same conv results; the last of them to finish reading writes
-// those back in place.  After its reads each CTA counts itself on the key
-// head's counter (an acquire-release atomic add): the CTA that sees the count
-// complete resets it and writes, when every other CTA of the key head is
-// past its reads -- no CTA waits for another.  Launched with programmatic
-// stream serialization: before griddepcontrol.wait only L2 prefetches (the
-// state tile and the row's lines).
+// those back in place.  The last warp counts the CTA on the key head's
+// counter once the q / k warps are past their reads (an acquire-release
+// atomic add, off the recurrence's path); the CTA that sees the count
+// complete resets it, and its q / k warps write, when every other CTA of the
+// key head is past its reads -- no CTA waits for another.  Launched with
+// programmatic stream serialization: before griddepcontrol.wait only L2
+// prefetches.
 
-constexpr int kRowSubs = 4;       // threads per state column
 constexpr int kRowMaxHvd = 128;
 
 struct RowParams {
@@ -508,13 +522,12 @@ struct RowParams {
   const uint16_t* norm_weight;  // [hvd] bf16
   uint16_t* out;                // [nv hvd] bf16
   float* out_f32;               // [nv hvd] or nullptr
-  float* state;                 // [nv][hkd][hvd] (read by the tensor map, written by bulk copies)
+  float* state;                 // [nv][hkd][hvd]
   unsigned* counters;           // [nk] readers of each key head's inputs (zero between calls)
   int nk, nv;
   float l2_eps, scale, norm_eps;
   int* status;
 };
-
 
 // (s1 w0 + s2 w1) + (s3 w2 + x w3): the vector kernel's sum at ck = 4 for a
 // row whose taps are the state's last three inputs and x.
@@ -524,39 +537,229 @@ HB_DEV float conv4_sum(const float4& st, uint2 w, float x) {
   return __fadd_rn(a, b);
 }
 
-template <int HKD, int NB>
-__global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
-    gdn_row_kernel(const __grid_constant__ CUtensorMap tmS, const RowParams p) {
-  constexpr int HVD = 16 * NB;
-  constexpr int KS = HKD / kRowSubs;  // kd rows per thread in the recurrence
-  static_assert(HKD <= kRowSubs * HVD && HVD <= kRowMaxHvd && HVD % 32 == 0 && KS % 4 == 0,
-                "thread roles");
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  float* st = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* qn = st + HKD * HVD;  // [HKD] q, then q inv_q scale
-  float* kn = qn + HKD;        // [HKD] k, then k inv_k
-  float* os = kn + HKD;        // [HVD] recurrence output
-  float* vb = os + HVD;        // [HVD] v after the conv
-  float* cb = vb + HVD;        // [HVD] a column's sum handed to the next quarter
-  float* db = cb + HVD;        // [HVD] delta
-  float* yb = db + HVD;        // [2 HKD] the conv results of q, k (written back by the last reader)
-  float4* sb = reinterpret_cast<float4*>(yb + 2 * HKD);  // [2 HKD] their new conv states
-  float* misc = reinterpret_cast<float*>(sb + 2 * HKD);  // inv_q, inv_k, beta, decay
-  uint64_t* bar = reinterpret_cast<uint64_t*>(misc + 8);  // misc[4]: the last-reader flag
+// Named barriers of the row kernel (0 is __syncthreads):
+//   kRowReady  kn, qn scaled and the gates in misc (warps 1 and last arrive, warp 0 waits)
+//   kRowRead   the q / k warps are past their reads (they arrive, the last warp waits)
+//   kRowLast   the count's answer is in `last` (the last warp arrives, the q / k warps wait)
+//   kRowFront  kn, qn written (q / k warps 2.. arrive, warp 1 waits)
+constexpr int kRowReady = 1, kRowRead = 2, kRowLast = 3, kRowFront = 4;
+HB_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+HB_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// The address of `local`'s counterpart in cluster CTA `rank`.
+HB_DEV uint32_t peer_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+// A store into a cluster CTA's shared memory whose 4 bytes count on that
+// CTA's mbarrier (complete_tx).
+HB_DEV void st_peer_f32(uint32_t addr, float v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(addr),
+               "f"(v), "r"(bar)
+               : "memory");
+}
 
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int h = blockIdx.x, ratio = p.nv / p.nk, kh = h / ratio;
+template <int HKD, int NB>
+__global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p) {
+  constexpr int HVD = 16 * NB;
+  constexpr int QC = HVD / 32;           // CTAs of a V head's cluster
+  constexpr int LAST = HKD / 32 + 1;     // the gates / counting warp
+  constexpr int QK = HKD + 32;           // q / k warps plus the last warp
+  static_assert(HVD <= kRowMaxHvd && HVD % 32 == 0 && HKD % 32 == 0 && HKD >= 64, "thread roles");
+  __shared__ __align__(16) float qn[HKD];  // q, then q inv_q scale
+  __shared__ __align__(16) float kn[HKD];  // k, then k inv_k
+  __shared__ float os[HVD];                // the head's recurrence outputs (every CTA's columns)
+  __shared__ float misc[4];                // inv_q, inv_k, beta, decay
+  __shared__ __align__(8) uint64_t os_bar; // the cluster's outputs have landed in os
+  __shared__ int last;                     // this CTA is the key head's last reader
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint32_t crank;
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  const int h = blockIdx.x / QC, col = int(crank) * 32 + lane;
+  const int ratio = p.nv / p.nk, kh = h / ratio;
   const int64_t key = int64_t(p.nk) * HKD;
-  const int64_t cq = int64_t(kh) * HKD + tid, ck = key + cq, cv = 2 * key + int64_t(h) * HVD + tid;
-  const bool has_qk = tid < HKD, has_v = tid < HVD;
+  const int ch = tid - 32;  // q / k channel of warps 1 .. HKD / 32
+  const int64_t cq = int64_t(kh) * HKD + ch, ck = key + cq, cv = 2 * key + int64_t(h) * HVD + col;
+  float* scol = p.state + int64_t(h) * HKD * HVD + col;  // state column col: row kd at kd * HVD
 
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(&os_bar, 1);
+    mbar_arrive_expect_tx(&os_bar, (QC - 1) * 32 * 4);  // the other CTAs' outputs
     fence_mbar_init();
-    sm100::prefetch_tmap(&tmS);
-    sm100::tma_prefetch_l2_2d(&tmS, 0, h * HKD);
   }
-  if (has_qk && lane % 8 == 0) {  // conv state: 8 channels per line; q, k, weights a line per warp
+  __syncthreads();
+  // this CTA's barrier is set: warp 0 waits for the whole cluster before its
+  // first store into a peer
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+
+  if (warp == 0) {  // ---------------------------------------- v, recurrence
+#pragma unroll
+    for (int i = 0; i < HKD / 32; ++i)  // the warp's 32 columns share each state row's line
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(scol - lane + (lane + 32 * i) * HVD));
+    if (lane % 8 == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cv * 4));
+    if (lane % 16 == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + cv * 4));
+    if (lane == 0) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + cv));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.z + int64_t(h) * HVD + col));
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    const float4 sv = *reinterpret_cast<const float4*>(p.conv_state + cv * 4);
+    const uint2 wv = *reinterpret_cast<const uint2*>(p.conv_weight + cv * 4);
+    const float xv = p.qkv[cv];
+    const float zz = p.z[int64_t(h) * HVD + col];
+    const float nw = bf16_to_f32(p.norm_weight[col]);
+    float s[HKD];
+#pragma unroll
+    for (int kd = 0; kd < HKD; ++kd) s[kd] = scol[kd * HVD];
+    float v, sz;
+    {
+      const float g = conv4_sum(sv, wv, xv);
+      silu_poly2(g, zz, v, sz);  // the v channel; SiLU(z) of the norm's gate
+    }
+    // this CTA's own v channel back in place
+    p.qkv[cv] = v;
+    *reinterpret_cast<float4*>(p.conv_state + cv * 4) = make_float4(sv.y, sv.z, sv.w, xv);
+    named_sync(kRowReady, 96);  // kn, qn, beta, decay
+    const float beta = misc[2], decay = misc[3];
+    const float4* k4 = reinterpret_cast<const float4*>(kn);
+    const float4* q4 = reinterpret_cast<const float4*>(qn);
+    constexpr int B = 8;  // operands read one block of B ahead of the sums
+    // pass 1: decay, then kv = S^T k (kd ascending)
+    float kv = 0.f;
+    {
+      float4 cur[B / 4], nxt[B / 4];
+#pragma unroll
+      for (int j = 0; j < B / 4; ++j) cur[j] = k4[j];
+#pragma unroll
+      for (int b = 0; b < HKD / B; ++b) {
+        if (b + 1 < HKD / B) {
+#pragma unroll
+          for (int j = 0; j < B / 4; ++j) nxt[j] = k4[(B / 4) * (b + 1) + j];
+        }
+        // the block's decayed rows and products first, then the ordered sum
+        float pr[B];
+#pragma unroll
+        for (int j = 0; j < B / 4; ++j) {
+          const float kw[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kd = B * b + 4 * j + e;
+            const float r = __fmul_rn(s[kd], decay);
+            s[kd] = r;
+            pr[4 * j + e] = __fmul_rn(r, kw[e]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < B; ++e) kv = __fadd_rn(kv, pr[e]);
+#pragma unroll
+        for (int j = 0; j < B / 4; ++j) cur[j] = nxt[j];
+      }
+    }
+    const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
+    // pass 2: S += k delta, out = S^T (q scale) (kd ascending); each state
+    // row stored as soon as it is final
+    float o = 0.f;
+    {
+      float4 kc[B / 4], qc[B / 4], kx[B / 4], qx[B / 4];
+#pragma unroll
+      for (int j = 0; j < B / 4; ++j) {
+        kc[j] = k4[j];
+        qc[j] = q4[j];
+      }
+#pragma unroll
+      for (int b = 0; b < HKD / B; ++b) {
+        if (b + 1 < HKD / B) {
+#pragma unroll
+          for (int j = 0; j < B / 4; ++j) {
+            kx[j] = k4[(B / 4) * (b + 1) + j];
+            qx[j] = q4[(B / 4) * (b + 1) + j];
+          }
+        }
+        float pr[B];
+#pragma unroll
+        for (int j = 0; j < B / 4; ++j) {
+          const float kw[4] = {kc[j].x, kc[j].y, kc[j].z, kc[j].w};
+          const float qw[4] = {qc[j].x, qc[j].y, qc[j].z, qc[j].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kd = B * b + 4 * j + e;
+            const float r = __fadd_rn(s[kd], __fmul_rn(kw[e], delta));
+            pr[4 * j + e] = __fmul_rn(r, qw[e]);
+            scol[kd * HVD] = r;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < B; ++e) o = __fadd_rn(o, pr[e]);
+#pragma unroll
+        for (int j = 0; j < B / 4; ++j) {
+          kc[j] = kx[j];
+          qc[j] = qx[j];
+        }
+      }
+    }
+    // the 32 outputs into os of this CTA and of every other CTA of the cluster
+    os[col] = o;
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+#pragma unroll
+    for (int r = 0; r < QC; ++r)
+      if (r != int(crank))
+        st_peer_f32(peer_addr(&os[col], uint32_t(r)), o, peer_addr(&os_bar, uint32_t(r)));
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait(&os_bar, 0))) {  // the outputs are not written
+      if (lane == 0) record_status(p.status, kStatusTimeout);
+      return;
+    }
+    __syncwarp();  // the warp's own os entries
+    // the gated norm: the row's inverse (every CTA forms the same bits),
+    // then this CTA's columns
+    float xs[4];
+    const int l = lane & 15, hh = lane >> 4;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const int b = 2 * hh + (k & 1) + 4 * (k >> 1);
+      xs[k] = b < NB ? os[16 * b + l] : 0.0f;
+    }
+    const float inv = norm_inverse_vec<NB>(xs, p.norm_eps);
+    const float y = __fmul_rn(__fmul_rn(__fmul_rn(o, inv), nw), sz);
+    const int64_t oi = int64_t(h) * HVD + col;
+    if (p.out_f32) p.out_f32[oi] = y;
+    p.out[oi] = static_cast<uint16_t>(bf16x2_cvtne_fast(y, y) & 0xFFFFu);
+    return;
+  }
+
+  if (warp == LAST) {  // ------------------------------ gates, reader count
+    float ga = 0.f, gb = 0.f, a_log = 0.f;
+    uint16_t dtb = 0;
+    if (lane == 0) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.ab + h));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.ab + p.nv + h));
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    if (lane == 0) {
+      ga = p.ab[h];
+      gb = p.ab[p.nv + h];
+      dtb = p.dt_bias[h];
+      a_log = p.a_log[h];
+      gate_values(ga, gb, dtb, a_log, misc[2], misc[3]);
+    }
+    named_arrive(kRowReady, 96);
+    named_sync(kRowRead, QK);  // the q / k warps are past their reads
+    if (lane == 0) {
+      unsigned before;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                   : "=r"(before) : "l"(p.counters + kh) : "memory");
+      const bool is_last = before == unsigned(ratio * QC - 1);
+      if (is_last) p.counters[kh] = 0u;  // zero for the next call
+      last = is_last;
+    }
+    named_arrive(kRowLast, QK);
+    return;
+  }
+
+  // ---------------------------------------------------------- q / k warps
+  if (lane % 8 == 0) {  // conv state: 8 channels per line; q, k, weights a line per warp
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cq * 4));
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + ck * 4));
     if (lane == 0) {
@@ -568,194 +771,72 @@ __global__ void __launch_bounds__(kRowSubs * 16 * NB, 1)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + ck * 4));
     }
   }
-  if (has_v && lane % 8 == 0) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cv * 4));
-    if (lane == 0) {
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.qkv + cv));
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(p.z + int64_t(h) * HVD + tid));
-    }
-    if (lane % 16 == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + cv * 4));
-  }
-  __syncthreads();  // the barrier's initialisation is visible
   griddep_wait();
   griddep_launch_dependents();
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar, HKD * HVD * 4);
-    sm100::tma_load_2d(st, &tmS, bar, 0, h * HKD);
-  }
-
-  // every load of the row
-  float4 sq = make_float4(0.f, 0.f, 0.f, 0.f), sk = sq, sv = sq;
-  uint2 wq = make_uint2(0u, 0u), wk = wq, wv = wq;
-  float xq = 0.f, xk = 0.f, xv = 0.f, zz = 0.f, nw = 0.f;
-  if (has_qk) {
-    sq = *reinterpret_cast<const float4*>(p.conv_state + cq * 4);
-    sk = *reinterpret_cast<const float4*>(p.conv_state + ck * 4);
-    wq = *reinterpret_cast<const uint2*>(p.conv_weight + cq * 4);
-    wk = *reinterpret_cast<const uint2*>(p.conv_weight + ck * 4);
-    xq = p.qkv[cq];
-    xk = p.qkv[ck];
-  }
-  if (has_v) {
-    sv = *reinterpret_cast<const float4*>(p.conv_state + cv * 4);
-    wv = *reinterpret_cast<const uint2*>(p.conv_weight + cv * 4);
-    xv = p.qkv[cv];
-    zz = p.z[int64_t(h) * HVD + tid];
-    nw = bf16_to_f32(p.norm_weight[tid]);
-  }
-  float ga = 0.f, gb = 0.f, a_log = 0.f;
-  uint16_t dtb = 0;
-  if (tid == 64) {
-    ga = p.ab[h];
-    gb = p.ab[p.nv + h];
-    dtb = p.dt_bias[h];
-    a_log = p.a_log[h];
-  }
-
-  float yq = 0.f, yk = 0.f, yv = 0.f;
-  if (has_qk) {
-    silu_poly2(conv4_sum(sq, wq, xq), conv4_sum(sk, wk, xk), yq, yk);
-    qn[tid] = yq;
-    kn[tid] = yk;
-    yb[tid] = yq;
-    yb[HKD + tid] = yk;
-    sb[tid] = make_float4(sq.y, sq.z, sq.w, xq);
-    sb[HKD + tid] = make_float4(sk.y, sk.z, sk.w, xk);
-  }
-  if (has_v) {
-    float unused;
-    const float g = conv4_sum(sv, wv, xv);
-    silu_poly2(g, g, yv, unused);
-    vb[tid] = yv;
-  }
-  __syncthreads();  // every thread has consumed its loads
-  // this CTA is past its reads of the key head's inputs (the answer is
-  // used at the end, so nothing waits on the atomic here)
-  unsigned readers_before = 0;
-  if (tid == 96)  // release: the CTA's reads (ordered by the barrier) come before it
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                 : "=r"(readers_before) : "l"(p.counters + kh) : "memory");
-  if (tid == 0 || tid == 32) misc[tid >> 5] = l2_inverse<HKD>(tid == 0 ? qn : kn, p.l2_eps);
-  if (tid == 64) gate_values(ga, gb, dtb, a_log, misc[2], misc[3]);
-  __syncthreads();
-  if (has_qk) {
-    qn[tid] = __fmul_rn(__fmul_rn(qn[tid], misc[0]), p.scale);
-    kn[tid] = __fmul_rn(kn[tid], misc[1]);
-  }
-  if (has_v) {  // this head's own v channel back in place
-    p.qkv[cv] = yv;
-    *reinterpret_cast<float4*>(p.conv_state + cv * 4) = make_float4(sv.y, sv.z, sv.w, xv);
-  }
-  const bool late = __syncthreads_or(!mbar_wait(bar, 0));  // the state tile
-
-  if (!late) {
-    const int sub = tid / HVD, col = tid % HVD;  // uniform per warp: HVD is a multiple of 32
-    float sr[KS], pr[KS];
-    const float4* k4 = reinterpret_cast<const float4*>(kn + sub * KS);
-    const float4* q4 = reinterpret_cast<const float4*>(qn + sub * KS);
-    const float decay = misc[3], beta = misc[2];
+  const float4 sq = *reinterpret_cast<const float4*>(p.conv_state + cq * 4);
+  const float4 sk = *reinterpret_cast<const float4*>(p.conv_state + ck * 4);
+  const uint2 wq = *reinterpret_cast<const uint2*>(p.conv_weight + cq * 4);
+  const uint2 wk = *reinterpret_cast<const uint2*>(p.conv_weight + ck * 4);
+  const float xq = p.qkv[cq], xk = p.qkv[ck];
+  float yq, yk;
+  silu_poly2(conv4_sum(sq, wq, xq), conv4_sum(sk, wk, xk), yq, yk);
+  qn[ch] = yq;
+  kn[ch] = yk;
+  named_arrive(kRowRead, QK);  // past the reads of the key head's inputs
+  if (warp == 1) {
+    named_sync(kRowFront, HKD);  // every channel of q and k
+    if (lane < 2) {  // lanes 0 / 1: sum of squares of q / k in order, a block of 16 ahead
+      const float4* x4 = reinterpret_cast<const float4*>(lane == 0 ? qn : kn);
+      float4 cur[4], nxt[4];
 #pragma unroll
-    for (int j = 0; j < KS; ++j) sr[j] = st[(sub * KS + j) * HVD + col];
-    // pass 1: decay the rows, the products r k
+      for (int j = 0; j < 4; ++j) cur[j] = x4[j];
+      float sum = 0.f;
 #pragma unroll
-    for (int j4 = 0; j4 < KS / 4; ++j4) {
-      const float4 kk = k4[j4];
-      const float kw[4] = {kk.x, kk.y, kk.z, kk.w};
+      for (int b = 0; b < HKD / 16; ++b) {
+        if (b + 1 < HKD / 16) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float r = __fmul_rn(sr[4 * j4 + e], decay);
-        sr[4 * j4 + e] = r;
-        pr[4 * j4 + e] = __fmul_rn(r, kw[e]);
+          for (int j = 0; j < 4; ++j) nxt[j] = x4[4 * (b + 1) + j];
+        }
+        // the block's squares first (independent), then the ordered sum
+        float sqr[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sqr[4 * j] = __fmul_rn(cur[j].x, cur[j].x);
+          sqr[4 * j + 1] = __fmul_rn(cur[j].y, cur[j].y);
+          sqr[4 * j + 2] = __fmul_rn(cur[j].z, cur[j].z);
+          sqr[4 * j + 3] = __fmul_rn(cur[j].w, cur[j].w);
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) sum = __fadd_rn(sum, sqr[e]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
       }
+      sum = __fadd_rn(sum, p.l2_eps);
+      misc[lane] = __fdiv_rn(1.0f, __fsqrt_rn(sum));
     }
-    // kv = S^T k, kd in increasing order across the quarters; the last one
-    // forms delta
-#pragma unroll 1
-    for (int i = 0; i < kRowSubs; ++i) {
-      if (sub == i) {
-        float acc = i == 0 ? 0.f : cb[col];
+    __syncwarp();
+    // q <- q inv_q scale (two roundings), k <- k inv_k: lane i the elements
+    // [i PER, (i + 1) PER)
+    constexpr int PER = HKD / 32;
+    const float iq = misc[0], ik = misc[1];
 #pragma unroll
-        for (int j = 0; j < KS; ++j) acc = __fadd_rn(acc, pr[j]);
-        if (i < kRowSubs - 1) cb[col] = acc;
-        else db[col] = __fmul_rn(__fsub_rn(vb[col], acc), beta);
-      }
-      __syncthreads();
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane * PER + i;
+      const float qq = qn[e], kk = kn[e];
+      qn[e] = __fmul_rn(__fmul_rn(qq, iq), p.scale);
+      kn[e] = __fmul_rn(kk, ik);
     }
-    // pass 2: S += k delta, the products r (q scale)
-    const float delta = db[col];
-#pragma unroll
-    for (int j4 = 0; j4 < KS / 4; ++j4) {
-      const float4 kk = k4[j4], qq = q4[j4];
-      const float kw[4] = {kk.x, kk.y, kk.z, kk.w}, qw[4] = {qq.x, qq.y, qq.z, qq.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float r = __fadd_rn(sr[4 * j4 + e], __fmul_rn(kw[e], delta));
-        sr[4 * j4 + e] = r;
-        pr[4 * j4 + e] = __fmul_rn(r, qw[e]);
-      }
-    }
-    // this quarter's new state rows back into the tile and out by one bulk
-    // copy (its KS rows are contiguous in both), in flight during the sums
-#pragma unroll
-    for (int j = 0; j < KS; ++j) st[(sub * KS + j) * HVD + col] = sr[j];
-    sm100::fence_proxy_async_smem();
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + sub), "r"(HVD) : "memory");  // the quarter's warps
-    if (col == 0) {
-      sm100::bulk_s2g(p.state + (int64_t(h) * HKD + sub * KS) * HVD, st + sub * KS * HVD,
-                      uint32_t(KS * HVD * 4));
-      sm100::tma_store_commit();
-    }
-    // out = S^T (q scale), in the same order
-#pragma unroll 1
-    for (int i = 0; i < kRowSubs; ++i) {
-      if (sub == i) {
-        float acc = i == 0 ? 0.f : cb[col];
-#pragma unroll
-        for (int j = 0; j < KS; ++j) acc = __fadd_rn(acc, pr[j]);
-        if (i < kRowSubs - 1) cb[col] = acc;
-        else os[col] = acc;
-      }
-      __syncthreads();
-    }
-    // the gated norm: every warp forms the row's inverse (the same bits)
-    // and finishes its own columns
-    float xs[4];
-    const int l = lane & 15, hh = lane >> 4;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const int b = 2 * hh + (k & 1) + 4 * (k >> 1);
-      xs[k] = b < NB ? os[16 * b + l] : 0.0f;
-    }
-    const float inv = norm_inverse_vec<NB>(xs, p.norm_eps);
-    if (has_v) {
-      float s0, s1;
-      silu_poly2(zz, zz, s0, s1);
-      const float y = __fmul_rn(__fmul_rn(__fmul_rn(os[tid], inv), nw), s0);
-      const int64_t o = int64_t(h) * HVD + tid;
-      if (p.out_f32) p.out_f32[o] = y;
-      p.out[o] = static_cast<uint16_t>(bf16x2_cvtne_fast(y, y) & 0xFFFFu);
-    }
-    if (col == 0) sm100::tma_store_wait_read();  // the tile stays until the copy has read it
-  } else if (tid == 0) {
-    // the state and the outputs are not written (the conv results are, as
-    // the three-launch path's front end would have written them)
-    record_status(p.status, kStatusTimeout);
-    mbar_wait(bar, 0);  // a second bounded wait for the copy in flight
+    named_arrive(kRowReady, 96);  // kn, qn scaled
+  } else {
+    named_arrive(kRowFront, HKD);
   }
   // the last reader of the key head's inputs writes the conv results back
-  // and leaves the counter at zero for the next call
-  int* last = reinterpret_cast<int*>(misc + 4);
-  if (tid == 96) {
-    const bool is_last = readers_before == unsigned(ratio - 1);
-    if (is_last) p.counters[kh] = 0u;
-    *last = is_last;
-  }
-  __syncthreads();
-  if (*last && has_qk) {
-    p.qkv[cq] = yb[tid];
-    p.qkv[ck] = yb[HKD + tid];
-    *reinterpret_cast<float4*>(p.conv_state + cq * 4) = sb[tid];
-    *reinterpret_cast<float4*>(p.conv_state + ck * 4) = sb[HKD + tid];
+  named_sync(kRowLast, QK);
+  if (last) {
+    p.qkv[cq] = yq;
+    p.qkv[ck] = yk;
+    *reinterpret_cast<float4*>(p.conv_state + cq * 4) = make_float4(sq.y, sq.z, sq.w, xq);
+    *reinterpret_cast<float4*>(p.conv_state + ck * 4) = make_float4(sk.y, sk.z, sk.w, xk);
   }
 }
 
@@ -808,19 +889,21 @@ bool gdn_row_serves(const hb_gdn_shape& s, int64_t ck) {
 
 namespace {
 template <int HKD, int NB>
-cudaError_t launch_row(const CUtensorMap& tm, const RowParams& p, cudaLaunchConfig_t cfg) {
-  constexpr int HVD = 16 * NB;
-  const size_t smem = 1024 + size_t(HKD) * HVD * 4 + (2 * HKD + 4 * HVD + 2 * HKD + 8 * HKD + 8) * 4 + 8;
-  static bool attr = false;  // one flag per instantiation
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_row_kernel<HKD, NB>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  cfg.blockDim = dim3(kRowSubs * HVD);
-  cfg.dynamicSmemBytes = smem;
-  return cudaLaunchKernelEx(&cfg, gdn_row_kernel<HKD, NB>, tm, p);
+cudaError_t launch_row(const RowParams& p, cudaLaunchConfig_t cfg) {
+  constexpr int QC = NB / 2;  // hvd / 32 CTAs per V head
+  cfg.gridDim = dim3(unsigned(p.nv * QC));
+  cfg.blockDim = dim3(HKD + 64);
+  cfg.dynamicSmemBytes = 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = QC;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gdn_row_kernel<HKD, NB>, p);
 }
 }  // namespace
 
@@ -844,34 +927,22 @@ cudaError_t launch_gdn_row(const GdnRowLaunch& L, cudaStream_t st) {
   p.scale = L.scale;
   p.norm_eps = L.norm_eps;
   p.status = L.status;
-  // the state as [nv*hkd rows][hvd columns] f32, one [hkd][hvd] tile per V head
-  CUtensorMap tm;
-  if (!encode_2d(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.state, uint64_t(L.shape.nv) * L.shape.hkd,
-                 uint64_t(L.shape.hvd), uint64_t(L.shape.hvd), uint32_t(L.shape.hkd),
-                 uint32_t(L.shape.hvd), CU_TENSOR_MAP_SWIZZLE_NONE))
-    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(L.shape.nv));
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const int nb = int(L.shape.hvd / 16);
   if (L.shape.hkd == 128) {
     switch (nb) {
-      case 2: return launch_row<128, 2>(tm, p, cfg);
-      case 4: return launch_row<128, 4>(tm, p, cfg);
-      case 6: return launch_row<128, 6>(tm, p, cfg);
-      case 8: return launch_row<128, 8>(tm, p, cfg);
+      case 2: return launch_row<128, 2>(p, cfg);
+      case 4: return launch_row<128, 4>(p, cfg);
+      case 6: return launch_row<128, 6>(p, cfg);
+      case 8: return launch_row<128, 8>(p, cfg);
     }
   } else if (L.shape.hkd == 64) {
     switch (nb) {
-      case 2: return launch_row<64, 2>(tm, p, cfg);
-      case 4: return launch_row<64, 4>(tm, p, cfg);
-      case 6: return launch_row<64, 6>(tm, p, cfg);
-      case 8: return launch_row<64, 8>(tm, p, cfg);
+      case 2: return launch_row<64, 2>(p, cfg);
+      case 4: return launch_row<64, 4>(p, cfg);
+      case 6: return launch_row<64, 6>(p, cfg);
+      case 8: return launch_row<64, 8>(p, cfg);
     }
   }
   return cudaErrorInvalidValue;
