@@ -624,11 +624,15 @@ __global__ void __launch_bounds__(kThreadsL, 1)
     if (lane == 0) {
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
+      // K and V are read once per step: their lines are the first L2 evicts,
+      // so a sweep of the cache leaves other layers' data (a DeltaNet
+      // layer's state, the next step's inputs) in L2
+      const uint64_t once = l2_evict_first_policy();
       // the first tiles into L2 while the previous grid finishes
       for (int t = 0; t < nt && t < 2; ++t)
         for (int cb = 0; cb < 4; ++cb) {
-          tma_prefetch_l2_3d(&tmK, cb * 64, int(p0) + t * BT, kh);
-          tma_prefetch_l2_3d(&tmV, cb * 64, int(p0) + t * BT, kh);
+          tma_prefetch_l2_3d_hint(&tmK, cb * 64, int(p0) + t * BT, kh, once);
+          tma_prefetch_l2_3d_hint(&tmV, cb * 64, int(p0) + t * BT, kh, once);
         }
       griddep_wait();
       const int t_tail = tail ? int((p.past - p0) / BT) : -1;
@@ -642,7 +646,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
         const CUtensorMap* tm = (i & 1) ? &tmV : &tmK;
         mbar_arrive_expect_tx(&bar[L_FULL + s], 4 * 16384);
         for (int cb = 0; cb < 4; ++cb)
-          tma_load_3d(smem + s * L_SLOT + cb * 16384, tm, &bar[L_FULL + s], cb * 64, pos, kh);
+          tma_load_3d_hint(smem + s * L_SLOT + cb * 16384, tm, &bar[L_FULL + s], cb * 64, pos, kh, once);
         issued = i + 1;
       }
       // every copy into this CTA's shared memory lands before it ends: the

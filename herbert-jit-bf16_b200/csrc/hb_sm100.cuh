@@ -59,6 +59,31 @@ HB_DEV void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, 
       : "memory");
 }
 
+// An L2 policy that marks the lines an access brings in as the first to
+// evict: for a stream read once (a KV cache swept by a decode step), so that
+// it does not push out data that later launches read again.
+HB_DEV uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load_3d and tma_prefetch_l2_3d under an L2 policy.
+HB_DEV void tma_load_3d_hint(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2,
+                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+HB_DEV void tma_prefetch_l2_3d_hint(const CUtensorMap* m, int c0, int c1, int c2, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile.L2::cache_hint [%0, {%1, %2, %3}], %4;" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+               : "memory");
+}
+
 // Tiled store shared -> global (bulk group); rows/columns outside the
 // tensor are not written.  Coordinates must be >= 0.
 HB_DEV void tma_store_2d(const CUtensorMap* m, const void* src, int c0, int c1) {
