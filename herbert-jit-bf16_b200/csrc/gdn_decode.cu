@@ -254,6 +254,9 @@ __global__ void __launch_bounds__(32 * (1 + kProducers), 1)
   __syncwarp();
 }
 
+HB_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+HB_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
 // ------------------------------------------------------------- one row
 // A call of one position (every decode step) is a chain of latencies: the
 // inputs, the two L2 sums, pass 1 (kv) and pass 2 (out), each a sequential
@@ -443,6 +446,183 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
   p.out[int64_t(h) * HVD + col] = o;
 }
 
+// ------------------------------------------------- one row, split passes
+// The same position as gdn_step_kernel with the recurrence's products taken
+// off the summing warp.  A pass over kd is a sequential sum of HKD terms,
+// and one warp that also forms the terms (two or three multiplies each, a
+// store in pass 2) issues about ten cycles per term; a warp that only adds
+// issues about six.  So warp 0 only sums: the q / k L2 sums (lanes 0 / 1),
+// then kv and out for its 32 columns, each term read from shared memory.
+// The HKD / 32 row warps hold the state rows, 8-row blocks dealt round-robin
+// (warp w: rows 8 (NR g + w) .. + 8 for g = 0, 1, ...), and form each pass's
+// terms for a group of rows at a time: group g, rows [8 NR g, 8 NR (g + 1)),
+// is one block from every row warp, published by named barrier 1 + g.  Pass
+// 2's row warps also store the new state rows.  Terms are laid out
+// [kd / 4][column][4] so that a row warp writes four rows of its column with
+// one 16-byte store and warp 0 reads four terms with one.  Same operations,
+// same order, same bits as gdn_step_column.
+template <int HKD, int HVD>
+__global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnParams p) {
+  constexpr int NR = HKD / 32;      // row warps
+  constexpr int NG = 4;             // groups of rows (barriers 1 .. 4)
+  constexpr int GR = HKD / NG;      // rows per group = 8 NR
+  static_assert(GR == 8 * NR, "one 8-row block per row warp and group");
+  constexpr int kFront = 5, kInv = 6, kDelta = 7;  // named barriers, HKD + 32 threads each
+  __shared__ __align__(16) float qraw[HKD];
+  __shared__ __align__(16) float kraw[HKD];
+  __shared__ __align__(16) float4 terms[HKD / 4][32];
+  __shared__ float misc[4];  // inv_q, inv_k, decay
+  __shared__ float ds[32];   // delta per column
+  const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int col = blockIdx.y * 32 + lane;
+  const int kh = h / (p.nv / p.nk);
+  const int64_t key = int64_t(p.nk) * HKD;
+  const float* qrow = p.qkv + int64_t(kh) * HKD;
+  const float* krow = p.qkv + key + int64_t(kh) * HKD;
+  float* srow = p.state + int64_t(h) * HKD * HVD + col;  // column col, row kd at kd * HVD
+  constexpr int NT = HKD + 32;
+
+  if (warp > 0) {  // ------------------------------------------------ row warps
+    const int w = warp - 1, t = threadIdx.x - 32;
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(srow - lane + (8 * (NR * g + w) + (lane & 7)) * HVD));
+    if (lane == 0) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(qrow + 32 * w));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(krow + 32 * w));
+    }
+    griddep_wait();
+    griddep_launch_dependents();
+    qraw[t] = qrow[t];
+    kraw[t] = krow[t];
+    float s[NG * 8];
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[8 * g + e] = srow[(8 * (NR * g + w) + e) * HVD];
+    named_arrive(kFront, NT);
+    named_sync(kInv, NT);  // the inverses and the decay
+    const float ik = misc[1], decay = misc[2];
+    float kn[NG * 8], qn[NG * 8];  // this warp's rows of k inv_k and q inv_q scale
+    // pass 1: the decayed rows and their terms r k
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const int kd0 = 8 * (NR * g + w);
+      float tm[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kn[8 * g + e] = p.l2 ? __fmul_rn(kraw[kd0 + e], ik) : kraw[kd0 + e];
+        const float r = __fmul_rn(s[8 * g + e], decay);
+        s[8 * g + e] = r;
+        tm[e] = __fmul_rn(r, kn[8 * g + e]);
+      }
+      terms[kd0 / 4][lane] = make_float4(tm[0], tm[1], tm[2], tm[3]);
+      terms[kd0 / 4 + 1][lane] = make_float4(tm[4], tm[5], tm[6], tm[7]);
+      named_arrive(1 + g, NT);
+    }
+    {  // q inv_q scale (two roundings) while warp 0 sums
+      const float iq = misc[0];
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float qq = qraw[8 * (NR * g + w) + e];
+          qn[8 * g + e] = __fmul_rn(p.l2 ? __fmul_rn(qq, iq) : qq, p.scale);
+        }
+    }
+    named_sync(kDelta, NT);  // warp 0 has summed pass 1's terms
+    const float delta = ds[lane];
+    // pass 2: the new rows S + k delta, stored, and their terms r (q scale)
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const int kd0 = 8 * (NR * g + w);
+      float tm[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float r = __fadd_rn(s[8 * g + e], __fmul_rn(kn[8 * g + e], delta));
+        tm[e] = __fmul_rn(r, qn[8 * g + e]);
+        srow[(kd0 + e) * HVD] = r;
+      }
+      terms[kd0 / 4][lane] = make_float4(tm[0], tm[1], tm[2], tm[3]);
+      terms[kd0 / 4 + 1][lane] = make_float4(tm[4], tm[5], tm[6], tm[7]);
+      named_arrive(1 + g, NT);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------- warp 0
+  griddep_wait();
+  griddep_launch_dependents();
+  const float v = p.qkv[2 * key + int64_t(h) * HVD + col];
+  const float beta = p.beta[h], decay = p.decay[h];
+  named_sync(kFront, NT);  // q, k in shared memory
+  if (p.l2 && lane < 2) {  // lanes 0 / 1: sum of squares of q / k in order, a block of 16 ahead
+    const float4* x4 = reinterpret_cast<const float4*>(lane == 0 ? qraw : kraw);
+    float4 cur[4], nxt[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cur[j] = x4[j];
+    float sum = 0.f;
+#pragma unroll
+    for (int b = 0; b < HKD / 16; ++b) {
+      if (b + 1 < HKD / 16) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) nxt[j] = x4[4 * (b + 1) + j];
+      }
+      float sq[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sq[4 * j] = __fmul_rn(cur[j].x, cur[j].x);
+        sq[4 * j + 1] = __fmul_rn(cur[j].y, cur[j].y);
+        sq[4 * j + 2] = __fmul_rn(cur[j].z, cur[j].z);
+        sq[4 * j + 3] = __fmul_rn(cur[j].w, cur[j].w);
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sum = __fadd_rn(sum, sq[e]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+    }
+    sum = __fadd_rn(sum, p.eps);
+    misc[lane] = __fdiv_rn(1.0f, __fsqrt_rn(sum));
+  }
+  if (lane == 2) misc[2] = decay;
+  __syncwarp();
+  named_arrive(kInv, NT);
+  // kv = S^T k, then out = S^T (q scale): kd ascending, a group at a time
+  float kv = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    named_sync(1 + g, NT);
+    float4 tq[GR / 4];
+#pragma unroll
+    for (int j = 0; j < GR / 4; ++j) tq[j] = terms[g * (GR / 4) + j][lane];
+#pragma unroll
+    for (int j = 0; j < GR / 4; ++j) {
+      kv = __fadd_rn(kv, tq[j].x);
+      kv = __fadd_rn(kv, tq[j].y);
+      kv = __fadd_rn(kv, tq[j].z);
+      kv = __fadd_rn(kv, tq[j].w);
+    }
+  }
+  ds[lane] = __fmul_rn(__fsub_rn(v, kv), beta);
+  named_arrive(kDelta, NT);
+  float o = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    named_sync(1 + g, NT);
+    float4 tq[GR / 4];
+#pragma unroll
+    for (int j = 0; j < GR / 4; ++j) tq[j] = terms[g * (GR / 4) + j][lane];
+#pragma unroll
+    for (int j = 0; j < GR / 4; ++j) {
+      o = __fadd_rn(o, tq[j].x);
+      o = __fadd_rn(o, tq[j].y);
+      o = __fadd_rn(o, tq[j].z);
+      o = __fadd_rn(o, tq[j].w);
+    }
+  }
+  p.out[int64_t(h) * HVD + col] = o;
+}
+
 }  // namespace
 
 bool gdn_decode_serves(const hb_gdn_shape& s) {
@@ -484,9 +664,9 @@ cudaError_t launch_gdn_decode(const GdnLaunch& L, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (L.call.rows == 1 && L.shape.hvd == 128) {  // one position: the latency-first form
-    cfg.blockDim = dim3(64);
-    if (L.shape.hkd == 128) return cudaLaunchKernelEx(&cfg, gdn_step_kernel<128, 128>, p);
-    if (L.shape.hkd == 64) return cudaLaunchKernelEx(&cfg, gdn_step_kernel<64, 128>, p);
+    cfg.blockDim = dim3(unsigned(L.shape.hkd + 32));
+    if (L.shape.hkd == 128) return cudaLaunchKernelEx(&cfg, gdn_step_split_kernel<128, 128>, p);
+    if (L.shape.hkd == 64) return cudaLaunchKernelEx(&cfg, gdn_step_split_kernel<64, 128>, p);
     return cudaErrorInvalidValue;
   }
   if (L.shape.hkd == 128) return cudaLaunchKernelEx(&cfg, gdn_decode_kernel<128>, tm, p);
