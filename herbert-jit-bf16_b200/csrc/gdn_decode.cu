@@ -254,9 +254,6 @@ __global__ void __launch_bounds__(32 * (1 + kProducers), 1)
   __syncwarp();
 }
 
-HB_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-HB_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-
 // ------------------------------------------------------------- one row
 // A call of one position (every decode step) is a chain of latencies: the
 // inputs, the two L2 sums, pass 1 (kv) and pass 2 (out), each a sequential
@@ -447,6 +444,7 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
 }
 
 // ------------------------------------------------- one row, split passes
+
 // The same position as gdn_step_kernel with the recurrence's products taken
 // off the summing warp.  A pass over kd is a sequential sum of HKD terms,
 // and one warp that also forms the terms (two or three multiplies each, a
@@ -471,6 +469,7 @@ __global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnPa
   __shared__ __align__(16) float qraw[HKD];
   __shared__ __align__(16) float kraw[HKD];
   __shared__ __align__(16) float4 terms[HKD / 4][32];
+  __shared__ __align__(16) float sqs[2][HKD];  // the squares of q and of k
   __shared__ float misc[4];  // inv_q, inv_k, decay
   __shared__ float ds[32];   // delta per column
   const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -493,8 +492,11 @@ __global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnPa
     }
     griddep_wait();
     griddep_launch_dependents();
-    qraw[t] = qrow[t];
-    kraw[t] = krow[t];
+    const float qv = qrow[t], kv = krow[t];
+    qraw[t] = qv;
+    kraw[t] = kv;
+    sqs[0][t] = __fmul_rn(qv, qv);
+    sqs[1][t] = __fmul_rn(kv, kv);
     float s[NG * 8];
 #pragma unroll
     for (int g = 0; g < NG; ++g)
@@ -537,15 +539,17 @@ __global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnPa
     for (int g = 0; g < NG; ++g) {
       const int kd0 = 8 * (NR * g + w);
       float tm[8];
+      float rn[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float r = __fadd_rn(s[8 * g + e], __fmul_rn(kn[8 * g + e], delta));
-        tm[e] = __fmul_rn(r, qn[8 * g + e]);
-        srow[(kd0 + e) * HVD] = r;
+        rn[e] = __fadd_rn(s[8 * g + e], __fmul_rn(kn[8 * g + e], delta));
+        tm[e] = __fmul_rn(rn[e], qn[8 * g + e]);
       }
       terms[kd0 / 4][lane] = make_float4(tm[0], tm[1], tm[2], tm[3]);
       terms[kd0 / 4 + 1][lane] = make_float4(tm[4], tm[5], tm[6], tm[7]);
       named_arrive(1 + g, NT);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) srow[(kd0 + e) * HVD] = rn[e];
     }
     return;
   }
@@ -556,30 +560,21 @@ __global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnPa
   const float v = p.qkv[2 * key + int64_t(h) * HVD + col];
   const float beta = p.beta[h], decay = p.decay[h];
   named_sync(kFront, NT);  // q, k in shared memory
-  if (p.l2 && lane < 2) {  // lanes 0 / 1: sum of squares of q / k in order, a block of 16 ahead
-    const float4* x4 = reinterpret_cast<const float4*>(lane == 0 ? qraw : kraw);
-    float4 cur[4], nxt[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) cur[j] = x4[j];
+  if (p.l2 && lane < 2) {  // lanes 0 / 1: the squares of q / k summed in order, 32 at a time
+    const float4* x4 = reinterpret_cast<const float4*>(sqs[lane]);
     float sum = 0.f;
 #pragma unroll
-    for (int b = 0; b < HKD / 16; ++b) {
-      if (b + 1 < HKD / 16) {
+    for (int b = 0; b < HKD / 32; ++b) {
+      float4 r[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) nxt[j] = x4[4 * (b + 1) + j];
+      for (int j = 0; j < 8; ++j) r[j] = x4[8 * b + j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sum = __fadd_rn(sum, r[j].x);
+        sum = __fadd_rn(sum, r[j].y);
+        sum = __fadd_rn(sum, r[j].z);
+        sum = __fadd_rn(sum, r[j].w);
       }
-      float sq[16];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        sq[4 * j] = __fmul_rn(cur[j].x, cur[j].x);
-        sq[4 * j + 1] = __fmul_rn(cur[j].y, cur[j].y);
-        sq[4 * j + 2] = __fmul_rn(cur[j].z, cur[j].z);
-        sq[4 * j + 3] = __fmul_rn(cur[j].w, cur[j].w);
-      }
-#pragma unroll
-      for (int e = 0; e < 16; ++e) sum = __fadd_rn(sum, sq[e]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
     }
     sum = __fadd_rn(sum, p.eps);
     misc[lane] = __fdiv_rn(1.0f, __fsqrt_rn(sum));
@@ -588,39 +583,10 @@ __global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnPa
   __syncwarp();
   named_arrive(kInv, NT);
   // kv = S^T k, then out = S^T (q scale): kd ascending, a group at a time
-  float kv = 0.f;
-#pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    named_sync(1 + g, NT);
-    float4 tq[GR / 4];
-#pragma unroll
-    for (int j = 0; j < GR / 4; ++j) tq[j] = terms[g * (GR / 4) + j][lane];
-#pragma unroll
-    for (int j = 0; j < GR / 4; ++j) {
-      kv = __fadd_rn(kv, tq[j].x);
-      kv = __fadd_rn(kv, tq[j].y);
-      kv = __fadd_rn(kv, tq[j].z);
-      kv = __fadd_rn(kv, tq[j].w);
-    }
-  }
+  const float kv = sum_terms<NG, GR>(terms, lane, NT);
   ds[lane] = __fmul_rn(__fsub_rn(v, kv), beta);
   named_arrive(kDelta, NT);
-  float o = 0.f;
-#pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    named_sync(1 + g, NT);
-    float4 tq[GR / 4];
-#pragma unroll
-    for (int j = 0; j < GR / 4; ++j) tq[j] = terms[g * (GR / 4) + j][lane];
-#pragma unroll
-    for (int j = 0; j < GR / 4; ++j) {
-      o = __fadd_rn(o, tq[j].x);
-      o = __fadd_rn(o, tq[j].y);
-      o = __fadd_rn(o, tq[j].z);
-      o = __fadd_rn(o, tq[j].w);
-    }
-  }
-  p.out[int64_t(h) * HVD + col] = o;
+  p.out[int64_t(h) * HVD + col] = sum_terms<NG, GR>(terms, lane, NT);
 }
 
 }  // namespace

@@ -482,17 +482,20 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
 // (kv) and pass 2 (out) of the recurrence, each a sequential sum of hkd
 // terms, then the gated norm over the head's hvd outputs.  So each V head is
 // a cluster of hvd / 32 CTAs, CTA c owning the state columns [32 c, 32 c +
-// 32), and every CTA runs the head's front end itself:
-//   warp 0        the v channels of its columns (conv + SiLU), then the
-//                 recurrence of its columns: the state column loaded straight
-//                 into each lane's registers right after griddepcontrol.wait
-//                 (landing while the front end runs), each pass forming a
-//                 block's products before its ordered sum with the block's
-//                 k / q read from shared memory one block ahead, every state
-//                 row stored as pass 2 finishes it;
-//   warps 1..     q / k channel t - 32 of the key head (conv + SiLU); warp 1's
-//                 lanes 0 / 1 then run the q / k L2 sums and the warp scales
-//                 q and k;
+// 32), and every CTA runs the head's front end itself.  A pass over kd is a
+// sequential sum of hkd terms: a warp that only adds issues about four
+// cycles per term, one that also forms the terms (two or three multiplies, a
+// store in pass 2) about ten, so the terms are formed by other warps:
+//   warp 0        the v channels of its columns (conv + SiLU), then only
+//                 sums: the q / k L2 sums (lanes 0 / 1, over the squares the
+//                 row warps wrote), kv and out of its 32 columns, reading
+//                 each group of terms while the previous group is summed;
+//   row warps     warp 1 + w: q / k channel 32 w + lane of the key head (conv
+//                 + SiLU, the squares), and the state rows 8 (NR g + w) ..
+//                 + 8 (g = 0 .. 3) of the CTA's 32 columns, loaded straight
+//                 into registers; for each pass and group g, the terms of
+//                 those 8 rows (pass 2: also the new rows, stored once the
+//                 terms are out), published by named barrier 1 + g;
 //   the last warp the gates, then the key head's reader count.
 // The gated norm needs the head's whole output row: each CTA stores its 32
 // outputs into every CTA of the cluster with st.async, counted on the
@@ -538,13 +541,14 @@ HB_DEV float conv4_sum(const float4& st, uint2 w, float x) {
 }
 
 // Named barriers of the row kernel (0 is __syncthreads):
-//   kRowReady  kn, qn scaled and the gates in misc (warps 1 and last arrive, warp 0 waits)
-//   kRowRead   the q / k warps are past their reads (they arrive, the last warp waits)
-//   kRowLast   the count's answer is in `last` (the last warp arrives, the q / k warps wait)
-//   kRowFront  kn, qn written (q / k warps 2.. arrive, warp 1 waits)
-constexpr int kRowReady = 1, kRowRead = 2, kRowLast = 3, kRowFront = 4;
-HB_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-HB_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+//   1 .. 4     a group of rows' terms published (row warps arrive, warp 0 waits)
+//   kRowFront  q, k and their squares written (row warps arrive, warp 0 waits)
+//   kRowInv    the L2 inverses (warp 0) and the gates (the last warp) in misc
+//              (they arrive, the row warps wait)
+//   kRowDelta  delta in ds (warp 0 arrives, the row warps wait)
+//   kRowRead   the row warps are past their reads (they arrive, the last warp waits)
+//   kRowLast   the count's answer is in `last` (the last warp arrives, the row warps wait)
+constexpr int kRowFront = 5, kRowInv = 6, kRowDelta = 7, kRowRead = 8, kRowLast = 9;
 // The address of `local`'s counterpart in cluster CTA `rank`.
 HB_DEV uint32_t peer_addr(const void* local, uint32_t rank) {
   uint32_t r;
@@ -562,16 +566,23 @@ HB_DEV void st_peer_f32(uint32_t addr, float v, uint32_t bar) {
 template <int HKD, int NB>
 __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p) {
   constexpr int HVD = 16 * NB;
-  constexpr int QC = HVD / 32;           // CTAs of a V head's cluster
-  constexpr int LAST = HKD / 32 + 1;     // the gates / counting warp
-  constexpr int QK = HKD + 32;           // q / k warps plus the last warp
-  static_assert(HVD <= kRowMaxHvd && HVD % 32 == 0 && HKD % 32 == 0 && HKD >= 64, "thread roles");
-  __shared__ __align__(16) float qn[HKD];  // q, then q inv_q scale
-  __shared__ __align__(16) float kn[HKD];  // k, then k inv_k
-  __shared__ float os[HVD];                // the head's recurrence outputs (every CTA's columns)
-  __shared__ float misc[4];                // inv_q, inv_k, beta, decay
-  __shared__ __align__(8) uint64_t os_bar; // the cluster's outputs have landed in os
-  __shared__ int last;                     // this CTA is the key head's last reader
+  constexpr int QC = HVD / 32;        // CTAs of a V head's cluster
+  constexpr int NR = HKD / 32;        // q / k warps, which also hold the state rows
+  constexpr int LAST = NR + 1;        // the gates / counting warp
+  constexpr int NG = 4;               // groups of rows (named barriers 1 .. 4)
+  constexpr int GR = HKD / NG;        // rows per group: an 8-row block of every row warp
+  constexpr int NT = HKD + 32;        // row warps and warp 0 (or the last warp)
+  static_assert(HVD <= kRowMaxHvd && HVD % 32 == 0 && HKD % 32 == 0 && HKD >= 64 && GR == 8 * NR,
+                "thread roles");
+  __shared__ __align__(16) float qraw[HKD];       // q, k after the conv
+  __shared__ __align__(16) float kraw[HKD];
+  __shared__ __align__(16) float sqs[2][HKD];     // their squares
+  __shared__ __align__(16) float4 terms[HKD / 4][32];
+  __shared__ float os[HVD];                       // the head's recurrence outputs (every CTA's columns)
+  __shared__ float misc[4];                       // inv_q, inv_k, decay, beta
+  __shared__ float ds[32];                        // delta per column
+  __shared__ __align__(8) uint64_t os_bar;        // the cluster's outputs have landed in os
+  __shared__ int last;                            // this CTA is the key head's last reader
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t crank;
@@ -579,7 +590,7 @@ __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p)
   const int h = blockIdx.x / QC, col = int(crank) * 32 + lane;
   const int ratio = p.nv / p.nk, kh = h / ratio;
   const int64_t key = int64_t(p.nk) * HKD;
-  const int ch = tid - 32;  // q / k channel of warps 1 .. HKD / 32
+  const int ch = tid - 32;  // q / k channel of the row warps
   const int64_t cq = int64_t(kh) * HKD + ch, ck = key + cq, cv = 2 * key + int64_t(h) * HVD + col;
   float* scol = p.state + int64_t(h) * HKD * HVD + col;  // state column col: row kd at kd * HVD
 
@@ -593,10 +604,7 @@ __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p)
   // first store into a peer
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
-  if (warp == 0) {  // ---------------------------------------- v, recurrence
-#pragma unroll
-    for (int i = 0; i < HKD / 32; ++i)  // the warp's 32 columns share each state row's line
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(scol - lane + (lane + 32 * i) * HVD));
+  if (warp == 0) {  // ---------------------------------- v channels, the sums
     if (lane % 8 == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cv * 4));
     if (lane % 16 == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_weight + cv * 4));
     if (lane == 0) {
@@ -610,95 +618,39 @@ __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p)
     const float xv = p.qkv[cv];
     const float zz = p.z[int64_t(h) * HVD + col];
     const float nw = bf16_to_f32(p.norm_weight[col]);
-    float s[HKD];
-#pragma unroll
-    for (int kd = 0; kd < HKD; ++kd) s[kd] = scol[kd * HVD];
     float v, sz;
-    {
-      const float g = conv4_sum(sv, wv, xv);
-      silu_poly2(g, zz, v, sz);  // the v channel; SiLU(z) of the norm's gate
-    }
+    silu_poly2(conv4_sum(sv, wv, xv), zz, v, sz);  // the v channel; SiLU(z) of the norm's gate
     // this CTA's own v channel back in place
     p.qkv[cv] = v;
     *reinterpret_cast<float4*>(p.conv_state + cv * 4) = make_float4(sv.y, sv.z, sv.w, xv);
-    named_sync(kRowReady, 96);  // kn, qn, beta, decay
-    const float beta = misc[2], decay = misc[3];
-    const float4* k4 = reinterpret_cast<const float4*>(kn);
-    const float4* q4 = reinterpret_cast<const float4*>(qn);
-    constexpr int B = 8;  // operands read one block of B ahead of the sums
-    // pass 1: decay, then kv = S^T k (kd ascending)
-    float kv = 0.f;
-    {
-      float4 cur[B / 4], nxt[B / 4];
+    named_sync(kRowFront, NT);  // q, k and their squares in shared memory
+    if (lane < 2) {  // lanes 0 / 1: the squares of q / k summed in order, 32 at a time
+      const float4* x4 = reinterpret_cast<const float4*>(sqs[lane]);
+      float sum = 0.f;
 #pragma unroll
-      for (int j = 0; j < B / 4; ++j) cur[j] = k4[j];
+      for (int b = 0; b < HKD / 32; ++b) {
+        float4 r[8];
 #pragma unroll
-      for (int b = 0; b < HKD / B; ++b) {
-        if (b + 1 < HKD / B) {
+        for (int j = 0; j < 8; ++j) r[j] = x4[8 * b + j];
 #pragma unroll
-          for (int j = 0; j < B / 4; ++j) nxt[j] = k4[(B / 4) * (b + 1) + j];
+        for (int j = 0; j < 8; ++j) {
+          sum = __fadd_rn(sum, r[j].x);
+          sum = __fadd_rn(sum, r[j].y);
+          sum = __fadd_rn(sum, r[j].z);
+          sum = __fadd_rn(sum, r[j].w);
         }
-        // the block's decayed rows and products first, then the ordered sum
-        float pr[B];
-#pragma unroll
-        for (int j = 0; j < B / 4; ++j) {
-          const float kw[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int kd = B * b + 4 * j + e;
-            const float r = __fmul_rn(s[kd], decay);
-            s[kd] = r;
-            pr[4 * j + e] = __fmul_rn(r, kw[e]);
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < B; ++e) kv = __fadd_rn(kv, pr[e]);
-#pragma unroll
-        for (int j = 0; j < B / 4; ++j) cur[j] = nxt[j];
       }
+      sum = __fadd_rn(sum, p.l2_eps);
+      misc[lane] = __fdiv_rn(1.0f, __fsqrt_rn(sum));
     }
-    const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
-    // pass 2: S += k delta, out = S^T (q scale) (kd ascending); each state
-    // row stored as soon as it is final
-    float o = 0.f;
-    {
-      float4 kc[B / 4], qc[B / 4], kx[B / 4], qx[B / 4];
-#pragma unroll
-      for (int j = 0; j < B / 4; ++j) {
-        kc[j] = k4[j];
-        qc[j] = q4[j];
-      }
-#pragma unroll
-      for (int b = 0; b < HKD / B; ++b) {
-        if (b + 1 < HKD / B) {
-#pragma unroll
-          for (int j = 0; j < B / 4; ++j) {
-            kx[j] = k4[(B / 4) * (b + 1) + j];
-            qx[j] = q4[(B / 4) * (b + 1) + j];
-          }
-        }
-        float pr[B];
-#pragma unroll
-        for (int j = 0; j < B / 4; ++j) {
-          const float kw[4] = {kc[j].x, kc[j].y, kc[j].z, kc[j].w};
-          const float qw[4] = {qc[j].x, qc[j].y, qc[j].z, qc[j].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int kd = B * b + 4 * j + e;
-            const float r = __fadd_rn(s[kd], __fmul_rn(kw[e], delta));
-            pr[4 * j + e] = __fmul_rn(r, qw[e]);
-            scol[kd * HVD] = r;
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < B; ++e) o = __fadd_rn(o, pr[e]);
-#pragma unroll
-        for (int j = 0; j < B / 4; ++j) {
-          kc[j] = kx[j];
-          qc[j] = qx[j];
-        }
-      }
-    }
+    __syncwarp();
+    named_arrive(kRowInv, NT + 32);
+    // kv = S^T k; delta; out = S^T (q scale): kd ascending, the row warps'
+    // terms a group at a time
+    const float kv = sum_terms<NG, GR>(terms, lane, NT);
+    ds[lane] = __fmul_rn(__fsub_rn(v, kv), misc[3]);
+    named_arrive(kRowDelta, NT);
+    const float o = sum_terms<NG, GR>(terms, lane, NT);
     // the 32 outputs into os of this CTA and of every other CTA of the cluster
     os[col] = o;
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
@@ -729,23 +681,16 @@ __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p)
   }
 
   if (warp == LAST) {  // ------------------------------ gates, reader count
-    float ga = 0.f, gb = 0.f, a_log = 0.f;
-    uint16_t dtb = 0;
     if (lane == 0) {
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p.ab + h));
       asm volatile("prefetch.global.L2 [%0];" ::"l"(p.ab + p.nv + h));
     }
     griddep_wait();
     griddep_launch_dependents();
-    if (lane == 0) {
-      ga = p.ab[h];
-      gb = p.ab[p.nv + h];
-      dtb = p.dt_bias[h];
-      a_log = p.a_log[h];
-      gate_values(ga, gb, dtb, a_log, misc[2], misc[3]);
-    }
-    named_arrive(kRowReady, 96);
-    named_sync(kRowRead, QK);  // the q / k warps are past their reads
+    if (lane == 0) gate_values(p.ab[h], p.ab[p.nv + h], p.dt_bias[h], p.a_log[h], misc[3], misc[2]);
+    __syncwarp();
+    named_arrive(kRowInv, NT + 32);
+    named_sync(kRowRead, NT);  // the row warps are past their reads of the key head's inputs
     if (lane == 0) {
       unsigned before;
       asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
@@ -754,11 +699,15 @@ __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p)
       if (is_last) p.counters[kh] = 0u;  // zero for the next call
       last = is_last;
     }
-    named_arrive(kRowLast, QK);
+    named_arrive(kRowLast, NT);
     return;
   }
 
-  // ---------------------------------------------------------- q / k warps
+  // ----------------------------------------------------------- row warps
+  const int w = warp - 1;
+#pragma unroll
+  for (int g = 0; g < NG; ++g)  // the state rows' lines (lanes 0..7: the 8 rows of block g)
+    if (lane < 8) asm volatile("prefetch.global.L2 [%0];" ::"l"(scol - lane + (8 * (NR * g + w) + lane) * HVD));
   if (lane % 8 == 0) {  // conv state: 8 channels per line; q, k, weights a line per warp
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + cq * 4));
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p.conv_state + ck * 4));
@@ -778,60 +727,64 @@ __global__ void __launch_bounds__(HKD + 64, 1) gdn_row_kernel(const RowParams p)
   const uint2 wq = *reinterpret_cast<const uint2*>(p.conv_weight + cq * 4);
   const uint2 wk = *reinterpret_cast<const uint2*>(p.conv_weight + ck * 4);
   const float xq = p.qkv[cq], xk = p.qkv[ck];
+  float s[NG * 8];  // state rows 8 (NR g + w) + e of column col
+#pragma unroll
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[8 * g + e] = scol[(8 * (NR * g + w) + e) * HVD];
   float yq, yk;
   silu_poly2(conv4_sum(sq, wq, xq), conv4_sum(sk, wk, xk), yq, yk);
-  qn[ch] = yq;
-  kn[ch] = yk;
-  named_arrive(kRowRead, QK);  // past the reads of the key head's inputs
-  if (warp == 1) {
-    named_sync(kRowFront, HKD);  // every channel of q and k
-    if (lane < 2) {  // lanes 0 / 1: sum of squares of q / k in order, a block of 16 ahead
-      const float4* x4 = reinterpret_cast<const float4*>(lane == 0 ? qn : kn);
-      float4 cur[4], nxt[4];
+  qraw[ch] = yq;
+  kraw[ch] = yk;
+  sqs[0][ch] = __fmul_rn(yq, yq);
+  sqs[1][ch] = __fmul_rn(yk, yk);
+  named_arrive(kRowRead, NT);   // past the reads of the key head's inputs
+  named_arrive(kRowFront, NT);  // q, k, squares written
+  named_sync(kRowInv, NT + 32); // the inverses (warp 0) and the gates (the last warp)
+  const float iq = misc[0], ik = misc[1], decay = misc[2];
+  float kn[NG * 8], qn[NG * 8];  // this warp's rows of k inv_k and q inv_q scale
+  // pass 1: the decayed rows and their terms r k
 #pragma unroll
-      for (int j = 0; j < 4; ++j) cur[j] = x4[j];
-      float sum = 0.f;
+  for (int g = 0; g < NG; ++g) {
+    const int kd0 = 8 * (NR * g + w);
+    float tm[8];
 #pragma unroll
-      for (int b = 0; b < HKD / 16; ++b) {
-        if (b + 1 < HKD / 16) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) nxt[j] = x4[4 * (b + 1) + j];
-        }
-        // the block's squares first (independent), then the ordered sum
-        float sqr[16];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sqr[4 * j] = __fmul_rn(cur[j].x, cur[j].x);
-          sqr[4 * j + 1] = __fmul_rn(cur[j].y, cur[j].y);
-          sqr[4 * j + 2] = __fmul_rn(cur[j].z, cur[j].z);
-          sqr[4 * j + 3] = __fmul_rn(cur[j].w, cur[j].w);
-        }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) sum = __fadd_rn(sum, sqr[e]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
-      }
-      sum = __fadd_rn(sum, p.l2_eps);
-      misc[lane] = __fdiv_rn(1.0f, __fsqrt_rn(sum));
+    for (int e = 0; e < 8; ++e) {
+      kn[8 * g + e] = __fmul_rn(kraw[kd0 + e], ik);
+      const float r = __fmul_rn(s[8 * g + e], decay);
+      s[8 * g + e] = r;
+      tm[e] = __fmul_rn(r, kn[8 * g + e]);
     }
-    __syncwarp();
-    // q <- q inv_q scale (two roundings), k <- k inv_k: lane i the elements
-    // [i PER, (i + 1) PER)
-    constexpr int PER = HKD / 32;
-    const float iq = misc[0], ik = misc[1];
+    terms[kd0 / 4][lane] = make_float4(tm[0], tm[1], tm[2], tm[3]);
+    terms[kd0 / 4 + 1][lane] = make_float4(tm[4], tm[5], tm[6], tm[7]);
+    named_arrive(1 + g, NT);
+  }
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = lane * PER + i;
-      const float qq = qn[e], kk = kn[e];
-      qn[e] = __fmul_rn(__fmul_rn(qq, iq), p.scale);
-      kn[e] = __fmul_rn(kk, ik);
+  for (int g = 0; g < NG; ++g)  // q inv_q scale (two roundings) while warp 0 sums
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      qn[8 * g + e] = __fmul_rn(__fmul_rn(qraw[8 * (NR * g + w) + e], iq), p.scale);
+  named_sync(kRowDelta, NT);  // warp 0 has summed pass 1's terms
+  const float delta = ds[lane];
+  // pass 2: the new rows S + k delta and their terms r (q scale); the
+  // group's rows stored once its terms are out
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int kd0 = 8 * (NR * g + w);
+    float tm[8], rn[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      rn[e] = __fadd_rn(s[8 * g + e], __fmul_rn(kn[8 * g + e], delta));
+      tm[e] = __fmul_rn(rn[e], qn[8 * g + e]);
     }
-    named_arrive(kRowReady, 96);  // kn, qn scaled
-  } else {
-    named_arrive(kRowFront, HKD);
+    terms[kd0 / 4][lane] = make_float4(tm[0], tm[1], tm[2], tm[3]);
+    terms[kd0 / 4 + 1][lane] = make_float4(tm[4], tm[5], tm[6], tm[7]);
+    named_arrive(1 + g, NT);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) scol[(kd0 + e) * HVD] = rn[e];
   }
   // the last reader of the key head's inputs writes the conv results back
-  named_sync(kRowLast, QK);
+  named_sync(kRowLast, NT);
   if (last) {
     p.qkv[cq] = yq;
     p.qkv[ck] = yk;

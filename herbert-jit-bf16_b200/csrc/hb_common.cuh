@@ -262,6 +262,41 @@ HB_DEV void record_status(int* status, int code) {
   if (status) atomicMax(status, code);
 }
 
+// Named barriers: bar.sync waits for `n` threads to arrive (itself
+// included), bar.arrive counts the calling warp without waiting.
+HB_DEV void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+HB_DEV void named_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+// Warp 0's ordered sum of one pass's terms for column `lane`, kd ascending:
+// group g (rows [GR g, GR (g + 1)), published by named barrier 1 + g of
+// `nt` threads) read from shared memory while group g - 1 is summed.
+template <int NG, int GR>
+HB_DEV float sum_terms(const float4 (*terms)[32], int lane, int nt) {
+  float acc = 0.f;
+  float4 cur[GR / 4], nxt[GR / 4];
+  named_sync(1, nt);
+#pragma unroll
+  for (int j = 0; j < GR / 4; ++j) cur[j] = terms[j][lane];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    if (g + 1 < NG) {
+      named_sync(2 + g, nt);
+#pragma unroll
+      for (int j = 0; j < GR / 4; ++j) nxt[j] = terms[(g + 1) * (GR / 4) + j][lane];
+    }
+#pragma unroll
+    for (int j = 0; j < GR / 4; ++j) {
+      acc = __fadd_rn(acc, cur[j].x);
+      acc = __fadd_rn(acc, cur[j].y);
+      acc = __fadd_rn(acc, cur[j].z);
+      acc = __fadd_rn(acc, cur[j].w);
+    }
+#pragma unroll
+    for (int j = 0; j < GR / 4; ++j) cur[j] = nxt[j];
+  }
+  return acc;
+}
+
 // Sequential L2 of one head held in shared memory: sum of squares left to
 // right, + eps, sqrt, 1/x (the L2 step of delta-l2-gates,
 // src/jit/target/x86/execution/delta.rs:28-62).
