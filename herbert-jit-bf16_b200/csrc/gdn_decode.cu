@@ -30,7 +30,7 @@
 // request.
 //
 // A call of one position (every decode step of a model) takes a second
-// form, gdn_step_kernel, built for latency: see its comment.
+// form, gdn_step_split_kernel, built for latency: see its comment.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -257,200 +257,11 @@ __global__ void __launch_bounds__(32 * (1 + kProducers), 1)
 // ------------------------------------------------------------- one row
 // A call of one position (every decode step) is a chain of latencies: the
 // inputs, the two L2 sums, pass 1 (kv) and pass 2 (out), each a sequential
-// sum of HKD terms.  This form keeps every operand of those sums where the
-// sum can take it without a memory round trip: warp 1's lanes 0 and 1 hold
-// all of q and of k in registers for the norms' sums; warp 0 loads its state
-// columns straight into registers, reads kn and qn from shared memory a
-// block of 16 ahead of the sums, and stores each state row as pass 2
-// finishes it (no shared-memory staging of the state).  Same operations in
-// the same order as gdn_step_column.  HVD (the state's row length) is a
-// constant, so that the state rows are one base address and immediate
-// offsets.
-template <int HKD, int HVD>
-__global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
-  __shared__ __align__(16) float kn_s[HKD];
-  __shared__ __align__(16) float qn_s[HKD];
-  __shared__ float inv_s[2];
-  const int h = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int col = blockIdx.y * 32 + lane;
-  const int kh = h / (p.nv / p.nk);
-  const int64_t key = int64_t(p.nk) * HKD;
-  const float* qrow = p.qkv + int64_t(kh) * HKD;
-  const float* krow = p.qkv + key + int64_t(kh) * HKD;
-  float* srow = p.state + int64_t(h) * HKD * HVD + col;  // column col, row kd at kd * HVD
-  // resident while the previous grid finishes: only L2 prefetches before the
-  // wait (the state column lines, q and k); every load that returns data,
-  // and every store, follows it
-  if (warp == 0) {
-#pragma unroll
-    for (int i = 0; i < HKD / 32; ++i)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(srow + (lane + 32 * i) * HVD));
-  } else if (lane < HKD / 32) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(qrow + lane * 32));
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(krow + lane * 32));
-  }
-  griddep_wait();
-  griddep_launch_dependents();
-
-  if (warp == 1) {  // ------------------------------------------ q, k norms
-    // every lane's share of q and k (HKD / 32 elements each)
-    constexpr int PER = HKD / 32;
-    float qv[PER], kv_[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      qv[i] = qrow[lane * PER + i];
-      kv_[i] = krow[lane * PER + i];
-    }
-    float iq = 1.f, ik = 1.f;
-    if (p.l2) {
-      // q, k into shared memory (each lane its share), then lanes 0 / 1 sum
-      // the squares of q / k in order, reading a block of 16 ahead
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        qn_s[lane * PER + i] = qv[i];
-        kn_s[lane * PER + i] = kv_[i];
-      }
-      __syncwarp();
-      if (lane < 2) {
-        const float4* x4 = reinterpret_cast<const float4*>(lane == 0 ? qn_s : kn_s);
-        float4 cur[4], nxt[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) cur[j] = x4[j];
-        float sum = 0.f;
-#pragma unroll
-        for (int b = 0; b < HKD / 16; ++b) {
-          if (b + 1 < HKD / 16) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) nxt[j] = x4[4 * (b + 1) + j];
-          }
-          // the block's squares first (independent), then the ordered sum
-          float sq[16];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            sq[4 * j] = __fmul_rn(cur[j].x, cur[j].x);
-            sq[4 * j + 1] = __fmul_rn(cur[j].y, cur[j].y);
-            sq[4 * j + 2] = __fmul_rn(cur[j].z, cur[j].z);
-            sq[4 * j + 3] = __fmul_rn(cur[j].w, cur[j].w);
-          }
-#pragma unroll
-          for (int e = 0; e < 16; ++e) sum = __fadd_rn(sum, sq[e]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
-        }
-        sum = __fadd_rn(sum, p.eps);
-        inv_s[lane] = __fdiv_rn(1.0f, __fsqrt_rn(sum));
-      }
-      __syncwarp();
-      iq = inv_s[0];
-      ik = inv_s[1];
-    }
-    // q <- q * inv_q * scale (the two roundings of the reference's pass 2),
-    // k <- k * inv_k
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const float qq = p.l2 ? __fmul_rn(qv[i], iq) : qv[i];
-      qn_s[lane * PER + i] = __fmul_rn(qq, p.scale);
-      kn_s[lane * PER + i] = p.l2 ? __fmul_rn(kv_[i], ik) : kv_[i];
-    }
-    asm volatile("bar.arrive 1, 64;" ::: "memory");  // kn, qn written
-    return;
-  }
-
-  // ------------------------------------------------------------ state warp
-  float s[HKD];
-#pragma unroll
-  for (int kd = 0; kd < HKD; ++kd) s[kd] = srow[kd * HVD];
-  const float v = p.qkv[2 * key + int64_t(h) * HVD + col];
-  const float beta = p.beta[h], decay = p.decay[h];
-  asm volatile("bar.sync 1, 64;" ::: "memory");  // kn, qn ready
-  const float4* k4 = reinterpret_cast<const float4*>(kn_s);
-  const float4* q4 = reinterpret_cast<const float4*>(qn_s);
-  constexpr int B = 8;  // operands read one block of B ahead of the sums
-  // pass 1: decay, then kv = S^T k (kd ascending)
-  float kv = 0.f;
-  {
-    float4 cur[B / 4], nxt[B / 4];
-#pragma unroll
-    for (int j = 0; j < B / 4; ++j) cur[j] = k4[j];
-#pragma unroll
-    for (int b = 0; b < HKD / B; ++b) {
-      if (b + 1 < HKD / B) {
-#pragma unroll
-        for (int j = 0; j < B / 4; ++j) nxt[j] = k4[(B / 4) * (b + 1) + j];
-      }
-      // the block's decayed rows and products first, then the ordered sum
-      float pr[B];
-#pragma unroll
-      for (int j = 0; j < B / 4; ++j) {
-        const float kw[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int kd = B * b + 4 * j + e;
-          const float r = __fmul_rn(s[kd], decay);
-          s[kd] = r;
-          pr[4 * j + e] = __fmul_rn(r, kw[e]);
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < B; ++e) kv = __fadd_rn(kv, pr[e]);
-#pragma unroll
-      for (int j = 0; j < B / 4; ++j) cur[j] = nxt[j];
-    }
-  }
-  const float delta = __fmul_rn(__fsub_rn(v, kv), beta);
-  // pass 2: S += k delta, out = S^T q (kd ascending); each state row stored
-  // as soon as it is final
-  float o = 0.f;
-  {
-    float4 kc[B / 4], qc[B / 4], kx[B / 4], qx[B / 4];
-#pragma unroll
-    for (int j = 0; j < B / 4; ++j) {
-      kc[j] = k4[j];
-      qc[j] = q4[j];
-    }
-#pragma unroll
-    for (int b = 0; b < HKD / B; ++b) {
-      if (b + 1 < HKD / B) {
-#pragma unroll
-        for (int j = 0; j < B / 4; ++j) {
-          kx[j] = k4[(B / 4) * (b + 1) + j];
-          qx[j] = q4[(B / 4) * (b + 1) + j];
-        }
-      }
-      // the block's new rows and products first, then the ordered sum
-      float pr[B];
-#pragma unroll
-      for (int j = 0; j < B / 4; ++j) {
-        const float kw[4] = {kc[j].x, kc[j].y, kc[j].z, kc[j].w};
-        const float qw[4] = {qc[j].x, qc[j].y, qc[j].z, qc[j].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int kd = B * b + 4 * j + e;
-          const float r = __fadd_rn(s[kd], __fmul_rn(kw[e], delta));
-          pr[4 * j + e] = __fmul_rn(r, qw[e]);
-          srow[kd * HVD] = r;
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < B; ++e) o = __fadd_rn(o, pr[e]);
-#pragma unroll
-      for (int j = 0; j < B / 4; ++j) {
-        kc[j] = kx[j];
-        qc[j] = qx[j];
-      }
-    }
-  }
-  p.out[int64_t(h) * HVD + col] = o;
-}
-
-// ------------------------------------------------- one row, split passes
-
-// The same position as gdn_step_kernel with the recurrence's products taken
-// off the summing warp.  A pass over kd is a sequential sum of HKD terms,
-// and one warp that also forms the terms (two or three multiplies each, a
-// store in pass 2) issues about ten cycles per term; a warp that only adds
-// issues about six.  So warp 0 only sums: the q / k L2 sums (lanes 0 / 1),
-// then kv and out for its 32 columns, each term read from shared memory.
+// sum of HKD terms.  A warp that only adds issues about four cycles per
+// term; one that also forms the terms (two or three multiplies each, a
+// store in pass 2) about ten.  So warp 0 only sums: the q / k L2 sums (lanes
+// 0 / 1, over the squares the row warps wrote), then kv and out for its 32
+// columns, each term read from shared memory.
 // The HKD / 32 row warps hold the state rows, 8-row blocks dealt round-robin
 // (warp w: rows 8 (NR g + w) .. + 8 for g = 0, 1, ...), and form each pass's
 // terms for a group of rows at a time: group g, rows [8 NR g, 8 NR (g + 1)),
@@ -458,7 +269,9 @@ __global__ void __launch_bounds__(64, 1) gdn_step_kernel(const GdnParams p) {
 // 2's row warps also store the new state rows.  Terms are laid out
 // [kd / 4][column][4] so that a row warp writes four rows of its column with
 // one 16-byte store and warp 0 reads four terms with one.  Same operations,
-// same order, same bits as gdn_step_column.
+// same order, same bits as gdn_step_column.  HVD (the state's row length) is
+// a constant, so that the state rows are one base address and immediate
+// offsets.
 template <int HKD, int HVD>
 __global__ void __launch_bounds__(HKD + 32, 1) gdn_step_split_kernel(const GdnParams p) {
   constexpr int NR = HKD / 32;      // row warps
