@@ -552,6 +552,7 @@ struct DecodeLongParams {
   float scale_log2;
   int* status;
   unsigned* counters;   // one per unit
+  int spread;           // every CTA of the grid resident at once: the last G CTAs of a unit merge it
   float* partials;      // [unit][split][G*HD + 2G rounded up to 4]
   // FRONT (rows == 1): the row's k and v ([hkv][256] each; k normed and
   // rotated in place), the norm weights, the RoPE table, the cache
@@ -903,34 +904,58 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           __stcg(mine + G * HDM + G + g, Lsum[g]);
         }
       nbar_sync(2, 128);  // every partial store of this CTA precedes thread 0's release
+      // The last K CTAs of the unit to count themselves merge it, one slice
+      // of K of its G heads each (K = G when the launch spreads the merge:
+      // every CTA of the grid resident at once; else K = 1, the last CTA
+      // merges every head).  A merger that is not the last waits until
+      // every split has counted itself, then adds itself once more; the one
+      // that brings the count to active + K resets it for the next call.
+      const int K = (p.spread && active >= G) ? G : 1;
       if (tid == 0) {
         __threadfence();
         const unsigned prev = atomicAdd(&p.counters[unit], 1u);
         __threadfence();
-        flags[1] = prev == unsigned(active - 1);
+        const int mi = int(prev) - (active - K);
+        flags[1] = mi >= 0 ? mi : -1;
+        if (mi >= 0 && mi < K - 1) {  // wait for the splits after this one
+          const long long t0 = clock64();
+          unsigned c;
+          for (;;) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(p.counters + unit) : "memory");
+            if (c >= unsigned(active)) break;
+            if (clock64() - t0 > kSpinCycles) {
+              record_status(p.status, kStatusTimeout);
+              flags[0] = 1;
+              break;
+            }
+          }
+        }
       }
       nbar_sync(2, 128);
-      if (flags[1]) {
-        // The last CTA of the unit merges every split.  The splits' maxima
-        // and sums first (one warp per head, lanes across the splits: the
-        // weights 2^(m_s - M) and the merged sum), then the O partials come
+      const int mi = flags[1];
+      if (mi >= 0) {
+        // This CTA's heads [g0, g0 + GM).  Their splits' maxima and sums
+        // first (one warp per head, lanes across the splits: the weights
+        // 2^(m_s - M) and the merged sum), then the heads' O partials come
         // into the idle ring by bulk copies, as many splits at a time as it
         // holds, all of a batch in flight on one barrier, and each thread
         // sums its output quads from shared memory.
+        const int GM = G / K, g0 = mi * GM;
         const float* up = p.partials + int64_t(unit) * p.nsplit * PSTRIDE;
         float* sml = reinterpret_cast<float*>(smem + L_OFF_Q);  // [active][2G] m, l (Q^T, P^T are done)
         float* smw = sml + active * 2 * G;                      // [active][G] weights
         float* smL = reinterpret_cast<float*>(smem + L_OFF_RED);  // [G]
-        constexpr int ROW = G * HDM * 4;                        // bytes of one split's O
-        constexpr int BATCH = 3 * L_SLOT / ROW;
+        const int ROW = GM * HDM * 4;                           // bytes of the heads' O in one split
+        const int BATCH = 3 * L_SLOT / ROW;
         const bool staged = active * 3 * G * 4 <= 16384;        // m, l and weights fit Q^T + P^T
-        auto issue = [&](int b0) {  // warp 0: the O rows of splits b0 .. b0 + BATCH - 1
+        auto issue = [&](int b0) {  // warp 0: the heads' O rows of splits b0 .. b0 + BATCH - 1
           const int nb = min(BATCH, active - b0);
           if (lane == 0) mbar_arrive_expect_tx(&bar[L_MERGE], uint32_t(nb) * ROW);
           __syncwarp();
-          for (int i = lane; i < nb; i += 32) bulk_g2s(smem + i * ROW, up + (b0 + i) * PSTRIDE, ROW, &bar[L_MERGE]);
+          for (int i = lane; i < nb; i += 32)
+            bulk_g2s(smem + i * ROW, up + (b0 + i) * PSTRIDE + g0 * HDM, ROW, &bar[L_MERGE]);
         };
-        if (staged) {
+        if (staged && !flags[0]) {
           if (warp == 0) {
             asm volatile("fence.proxy.async.global;" ::: "memory");
             issue(0);  // in flight while the weights are formed
@@ -938,7 +963,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           for (int i = tid; i < active * 2 * G; i += 128)
             sml[i] = __ldcg(up + (i / (2 * G)) * PSTRIDE + G * HDM + (i % (2 * G)));
           nbar_sync(2, 128);
-          for (int g = warp; g < G; g += 4) {
+          for (int g = g0 + warp; g < g0 + GM; g += 4) {
             float Mx = -INFINITY;
             for (int sp = lane; sp < active; sp += 32) Mx = fmaxf(Mx, sml[sp * 2 * G + g]);
             Mx = warp_max(Mx);
@@ -954,12 +979,12 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           }
         }
         nbar_sync(2, 128);
-        constexpr int NQD = G * HDM / 4;  // output quads
-        constexpr int QPT = (NQD + 127) / 128;
+        constexpr int QPT = (G * HDM / 4 + 127) / 128;
+        const int NQD = GM * HDM / 4;  // output quads of this CTA's heads
         float4 acc[QPT];
 #pragma unroll
         for (int k = 0; k < QPT; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (staged) {
+        if (staged && !flags[0]) {
           for (int b0 = 0, it = 0; b0 < active; b0 += BATCH, ++it) {
             const int nb = min(BATCH, active - b0);
             if (it > 0 && warp == 0) issue(b0);
@@ -975,7 +1000,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
               for (int k = 0; k < QPT; ++k) {
                 const int qd = tid + k * 128;
                 if (qd < NQD) {
-                  const int g = qd * 4 / HDM;
+                  const int g = g0 + qd * 4 / HDM;
                   for (int i = 0; i < nb; ++i) {
                     const float4 v = reinterpret_cast<const float4*>(smem + i * ROW)[qd];
                     const float w = smw[(b0 + i) * G + g];
@@ -990,7 +1015,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
             nbar_sync(2, 128);  // the batch is summed: its buffers may take the next
             if (flags[0]) break;
           }
-        } else if (tid == 0) {
+        } else if (tid == 0 && !staged) {
           // more splits than the weight buffer holds: the launcher does not
           // send such calls here
           record_status(p.status, kStatusArg);
@@ -999,7 +1024,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
         for (int k = 0; k < QPT; ++k) {
           const int qd = tid + k * 128;
           if (qd >= NQD || flags[0] || !staged) continue;
-          const int e = qd * 4, g = e / HDM, dd = e % HDM, hq = h0 + g;
+          const int e = g0 * HDM + qd * 4, g = e / HDM, dd = e % HDM, hq = h0 + g;
           const float Ls = smL[g];
           const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
           uint16_t a[4] = {f32_to_bf16_cvtne(acc[k].x * inv), f32_to_bf16_cvtne(acc[k].y * inv),
@@ -1016,12 +1041,20 @@ __global__ void __launch_bounds__(kThreadsL, 1)
               make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
         }
         if constexpr (FRONT) {  // every other CTA of the unit has read q: the normed q in place
+          if (mi == 0) {
 #pragma unroll
-          for (int i = 0; i < QW; ++i)
-            if (warp + 4 * i < G)
-              front::store_words<4>(const_cast<uint16_t*>(qrow) + int64_t(h0 + warp + 4 * i) * p.q_head + lane * 8, qy[i]);
+            for (int i = 0; i < QW; ++i)
+              if (warp + 4 * i < G)
+                front::store_words<4>(const_cast<uint16_t*>(qrow) + int64_t(h0 + warp + 4 * i) * p.q_head + lane * 8, qy[i]);
+          }
         }
-        if (tid == 0) p.counters[unit] = 0u;  // leave the workspace reusable
+        // leave the workspace reusable: the merger that completes the
+        // second count (every merger is past its wait) resets it
+        if (tid == 0) {
+          __threadfence();
+          const unsigned prev = atomicAdd(&p.counters[unit], 1u);
+          if (prev == unsigned(active + K - 1)) p.counters[unit] = 0u;
+        }
       }
     }
   }
@@ -1106,6 +1139,16 @@ cudaError_t launch_long(const DecodeLaunch& L, const DecodeFront* F, int chunk, 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(nsplit), unsigned(L.hkv), unsigned(L.rows));
   cfg.blockDim = dim3(kThreadsL);
+  // one CTA per SM (its shared memory): the merge waits on other CTAs only
+  // when every CTA of the grid can be resident at once
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 0;
+  }
+  p.spread = int64_t(nsplit) * L.hkv * L.rows <= sms ? 1 : 0;
   cfg.dynamicSmemBytes = L_SMEM;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
