@@ -34,12 +34,14 @@ DECODE_CASES = [
     (1, 600, 4, 4, 256, False),     # gqa 1, no gate
     (2, 1500, 16, 4, 256, True),
     # one sequence beyond 16 x 256 positions at head_dim 256: split-KV on the
-    # tensor cores, 128-position tiles, partials merged by the last CTA
+    # tensor cores, 128-position tiles, partials merged by the last G CTAs of
+    # a unit (one q head each) when the whole grid is resident at once
     (1, 32767, 16, 4, 256, True),   # the mixers' attention layer, n = 32768
     (1, 9000, 16, 2, 256, True),    # gqa 8, ragged last tile
     (2, 6000, 8, 8, 256, False),    # gqa 1, rows > 1, no gate
     (1, 20000, 8, 4, 256, True),    # gqa 2
     (3, 4094, 16, 4, 256, True),    # rows 0-1 at the cluster forms' limit, row 2 beyond it
+    (2, 32000, 16, 4, 256, True),   # more CTAs than SMs: the last CTA of a unit merges every head
 ]
 
 
