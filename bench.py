@@ -315,11 +315,29 @@ class GdnWorkload(Workload):
                                 rows=1, regime="decode")
 
     def e2e_step(self, i=0):
+        """The step from host buffers: the prefill rows through
+        hb_gdn_prefill_host (each block's copies overlapped with the blocks
+        before it), the decode rows' inputs copied on a side stream meanwhile,
+        then the one-row steps and their outputs back."""
+        import torch
+        hb, T = self.hb, self.T
         qkv, beta, decay, out = self.sets[0]
-        for d, h in zip((qkv, beta, decay), self.h_in):
-            d.copy_(h, non_blocking=True)
-        self.step(0)
-        self.h_out.copy_(out, non_blocking=True)
+        h_qkv, h_beta, h_decay = self.h_in
+        cur = torch.cuda.current_stream()
+        if not hasattr(self, "side"):
+            self.side = torch.cuda.Stream()
+        self.side.wait_stream(cur)
+        with torch.cuda.stream(self.side):
+            for d, h in zip((qkv, beta, decay), self.h_in):
+                d[T:].copy_(h[T:], non_blocking=True)
+        self.state.zero_()
+        self.ws = hb.delta_prefill_host(self.shape, self.state, out, qkv, beta, decay, h_qkv,
+                                        h_beta, h_decay, self.h_out, rows=T, workspace=self.ws)
+        cur.wait_stream(self.side)
+        for t in range(T, T + self.steps):
+            hb.delta_recurrence(self.shape, self.state, out[t], qkv[t], beta[t], decay[t],
+                                rows=1, regime="decode")
+        self.h_out[T:].copy_(out[T:], non_blocking=True)
 
     def kernel_probe(self, reps=5):
         """(FLOPs, seconds) of one chunked prefill (prep + scan kernels), by

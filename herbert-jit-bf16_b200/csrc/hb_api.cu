@@ -749,6 +749,8 @@ hb_status hb_gdn_prefill(const hb_gdn_shape* s, const hb_gdn_call* c, void* ws, 
 
 namespace hb {
 
+hb_status hb_gdn_check(const hb_gdn_shape* s, const hb_gdn_call* c) { return check_gdn(s, c); }
+
 hb_status attn_layer_row(const hb_attn_spec* s, const hb_kv_spec* kv, const hb_front_spec* f,
                          const hb_front_call* fc, const hb_attn_call* ac, void* ws, size_t ws_bytes,
                          hb_stream_t stream, bool* served) {

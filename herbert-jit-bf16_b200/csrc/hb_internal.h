@@ -269,6 +269,8 @@ bool aligned16(const void* p);
 hb_status check_spec(const hb_attn_spec* s);
 hb_status check_call(const hb_attn_spec* s, const hb_attn_call* c);
 hb_status check_ws(void* ws, size_t have, size_t need);
+// hb_gdn_decode / hb_gdn_prefill's checks of a call (hb_api.cu).
+hb_status hb_gdn_check(const hb_gdn_shape* s, const hb_gdn_call* c);
 // Fewest rows hb_attn_prefill takes to the tensor-core kernel (fewer go to
 // the decode kernel).
 constexpr int64_t kPrefillMinRows = 64;

@@ -1,6 +1,6 @@
-// prefill_host.cu -- hb_attn_prefill_host: the prefill of rows whose q, new
-// K/V positions and output are in host memory, with the host <-> device
-// copies overlapped with the computation.
+// prefill_host.cu -- hb_attn_prefill_host and hb_gdn_prefill_host: the
+// prefill of rows whose inputs and output are in host memory, with the
+// host <-> device copies overlapped with the computation.
 //
 // An engine that keeps its buffers on the host -- the reference's own
 // arrangement, Runner-owned buffers handed to the prefill node
@@ -22,6 +22,18 @@
 // Block boundaries are query-tile boundaries, so every row is computed by
 // the same products in the same order as in one hb_attn_prefill call over
 // all the rows: the result is bit-identical.
+//
+// hb_gdn_prefill_host does the same for the chunked DeltaNet prefill: block
+// j's qkv, beta and decay rows in, hb_gdn_prefill over the block (the state
+// carried in place from block to block), its output rows out.  The chunked
+// kernels carry the state between chunks only through its bf16 rounding
+// (each chunk's products read the bf16 state; the f32 state is formed by
+// them), and a call starts by rounding the f32 state it reads, so blocks
+// that start on chunk boundaries and all take the chunked kernels (128 rows
+// or more each) give one call's bits.  DeltaNet rows are copy-bound (32 KB
+// of f32 inputs per row at Qwen3.5 geometry against ≈ 50 ns of computation),
+// so the blocks are small enough that the first block's copy, the only one
+// not hidden, stays short.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -116,6 +128,42 @@ hb_attn_call block_call(const hb_attn_spec* s, const hb_attn_call& c, int64_t r0
   return b;
 }
 
+int64_t gdn_host_block(int64_t rows, int64_t block_rows) {
+  if (block_rows > 0) return block_rows;
+  // about sixteen blocks, at least 256 rows each
+  const int64_t b = ((rows + 15) / 16 + 63) / 64 * 64;
+  return std::max<int64_t>(256, b);
+}
+
+int64_t gdn_host_blocks(int64_t rows, int64_t block) {
+  int64_t n = (rows + block - 1) / block;
+  // a remainder below the chunked kernels' minimum joins the block before it
+  if (n > 1 && rows - (n - 1) * block < 128) --n;
+  return n;
+}
+
+hb_status check_gdn_host_call(const hb_gdn_shape* s, const hb_gdn_host_call* h) {
+  if (!s || !h) return fail(HB_ERR_ARG, "DeltaNet shape or host call is null");
+  if (!h->qkv_host || !h->beta_host || !h->decay_host || !h->output_host)
+    return fail(HB_ERR_ARG, "host qkv/beta/decay/output pointers must not be null");
+  if (h->block_rows < 0 || h->block_rows % 64)
+    return fail(HB_ERR_ARG, "block_rows %lld must be 0 or a positive multiple of 64",
+                (long long)h->block_rows);
+  if (h->dev.rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
+  return HB_OK;
+}
+
+hb_gdn_call gdn_block_call(const hb_gdn_shape* s, const hb_gdn_call& c, int64_t r0, int64_t nb) {
+  const int64_t conv = 2 * s->nk * s->hkd + s->nv * s->hvd;
+  hb_gdn_call b = c;
+  b.qkv = c.qkv + r0 * conv;
+  b.beta = c.beta + r0 * s->nv;
+  b.decay = c.decay + r0 * s->nv;
+  b.output = c.output + r0 * s->nv * s->hvd;
+  b.rows = nb;
+  return b;
+}
+
 }  // namespace
 }  // namespace hb
 
@@ -192,5 +240,70 @@ hb_status hb_attn_prefill_host(const hb_attn_spec* s, const hb_attn_host_call* h
   if ((e = cudaEventRecord(join, hs->out)) != cudaSuccess ||
       (e = cudaStreamWaitEvent(main, join, 0)) != cudaSuccess)
     return cuda_fail(e, "hb_attn_prefill_host join");
+  return HB_OK;
+}
+
+size_t hb_gdn_prefill_host_workspace_bytes(const hb_gdn_shape* s, const hb_gdn_host_call* h) {
+  if (check_gdn_host_call(s, h) != HB_OK) return 0;
+  const int64_t rows = h->dev.rows, block = gdn_host_block(rows, h->block_rows);
+  const int64_t nblocks = gdn_host_blocks(rows, block);
+  size_t need = 0;
+  for (int64_t j = 0; j < nblocks; ++j) {
+    const int64_t nb = j + 1 < nblocks ? block : rows - j * block;
+    need = std::max(need, hb_gdn_prefill_workspace_bytes(s, nb));
+  }
+  return need;
+}
+
+hb_status hb_gdn_prefill_host(const hb_gdn_shape* s, const hb_gdn_host_call* h, void* ws,
+                              size_t ws_bytes, hb_stream_t stream) {
+  hb_status r = check_gdn_host_call(s, h);
+  if (r != HB_OK) return r;
+  const hb_gdn_call& c = h->dev;
+  const int64_t rows = c.rows, block = gdn_host_block(rows, h->block_rows);
+  const int64_t nblocks = gdn_host_blocks(rows, block);
+  // the blocks' own checks before any copy is queued
+  if ((r = check_ws(ws, ws_bytes, hb_gdn_prefill_host_workspace_bytes(s, h))) != HB_OK) return r;
+  const hb_gdn_call first = gdn_block_call(s, c, 0, std::min(rows, block));
+  if ((r = hb_gdn_check(s, &first)) != HB_OK) return r;
+  HostStreams* hs = nullptr;
+  cudaError_t e = host_streams(&hs);
+  if (e != cudaSuccess) return cuda_fail(e, "hb_gdn_prefill_host streams");
+  const cudaStream_t main = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t conv = 2 * s->nk * s->hkd + s->nv * s->hvd, value = s->nv * s->hvd;
+  std::lock_guard<std::mutex> lock(hs->mu);
+  if ((e = pool_events(hs, size_t(2 * nblocks + 2))) != cudaSuccess)
+    return cuda_fail(e, "hb_gdn_prefill_host events");
+  cudaEvent_t* ev = hs->events.data();
+  if ((e = cudaEventRecord(ev[0], main)) != cudaSuccess ||
+      (e = cudaStreamWaitEvent(hs->in, ev[0], 0)) != cudaSuccess ||
+      (e = cudaStreamWaitEvent(hs->out, ev[0], 0)) != cudaSuccess)
+    return cuda_fail(e, "hb_gdn_prefill_host fork");
+  for (int64_t j = 0; j < nblocks; ++j) {
+    const int64_t r0 = j * block, nb = j + 1 < nblocks ? block : rows - r0;
+    const hb_gdn_call b = gdn_block_call(s, c, r0, nb);
+    e = cudaMemcpyAsync(const_cast<float*>(b.qkv), h->qkv_host + r0 * conv, size_t(nb * conv) * 4,
+                        cudaMemcpyHostToDevice, hs->in);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(const_cast<float*>(b.beta), h->beta_host + r0 * s->nv,
+                          size_t(nb * s->nv) * 4, cudaMemcpyHostToDevice, hs->in);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(const_cast<float*>(b.decay), h->decay_host + r0 * s->nv,
+                          size_t(nb * s->nv) * 4, cudaMemcpyHostToDevice, hs->in);
+    cudaEvent_t landed = ev[1 + 2 * j], done = ev[2 + 2 * j];
+    if (e == cudaSuccess) e = cudaEventRecord(landed, hs->in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, landed, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "hb_gdn_prefill_host copy-in");
+    if ((r = hb_gdn_prefill(s, &b, ws, ws_bytes, stream)) != HB_OK) return r;
+    if ((e = cudaEventRecord(done, main)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(hs->out, done, 0)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(h->output_host + r0 * value, b.output, size_t(nb * value) * 4,
+                             cudaMemcpyDeviceToHost, hs->out)) != cudaSuccess)
+      return cuda_fail(e, "hb_gdn_prefill_host copy-out");
+  }
+  cudaEvent_t join = ev[1 + 2 * nblocks];
+  if ((e = cudaEventRecord(join, hs->out)) != cudaSuccess ||
+      (e = cudaStreamWaitEvent(main, join, 0)) != cudaSuccess)
+    return cuda_fail(e, "hb_gdn_prefill_host join");
   return HB_OK;
 }

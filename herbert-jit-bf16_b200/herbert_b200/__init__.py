@@ -102,6 +102,11 @@ class RecurrenceCall(ctypes.Structure):
                 ("l2", c_int32), ("eps", c_float)]
 
 
+class RecurrenceHostCall(ctypes.Structure):
+    _fields_ = [("dev", RecurrenceCall), ("qkv_host", c_void_p), ("beta_host", c_void_p),
+                ("decay_host", c_void_p), ("output_host", c_void_p), ("block_rows", c_int64)]
+
+
 class GdnFrontCall(ctypes.Structure):
     """hb_gdn_front_call: conv + SiLU in place over qkv, then the beta/decay gates."""
     _fields_ = [("qkv", c_void_p), ("conv_state", c_void_p), ("conv_weight", c_void_p),
@@ -190,6 +195,9 @@ _SIGNATURES = {
     "hb_attn_prefill_host_workspace_bytes": (c_size_t, [_P(AttentionSpec), _P(AttentionHostCall)]),
     "hb_attn_prefill_host": (ctypes.c_int, [_P(AttentionSpec), _P(AttentionHostCall), c_void_p,
                                             c_size_t, c_void_p]),
+    "hb_gdn_prefill_host_workspace_bytes": (c_size_t, [_P(DeltaShape), _P(RecurrenceHostCall)]),
+    "hb_gdn_prefill_host": (ctypes.c_int, [_P(DeltaShape), _P(RecurrenceHostCall), c_void_p,
+                                           c_size_t, c_void_p]),
     "hb_kv_append": (ctypes.c_int, [_P(KvSpec), _P(KvCall), c_void_p]),
     "hb_attn_front": (ctypes.c_int, [_P(AttentionSpec), _P(KvSpec), _P(FrontSpec), _P(FrontCall),
                                      c_void_p]),
@@ -483,6 +491,33 @@ def delta_recurrence(shape: DeltaShape, state, out, qkv, beta, decay, *, rows: i
         workspace.ensure(nbytes, stream)
     check(L.hb_gdn_prefill(ctypes.byref(shape), ctypes.byref(call), c_void_p(workspace.ptr),
                            workspace.nbytes, _stream(stream)))
+    return workspace
+
+
+def delta_prefill_host(shape: DeltaShape, state, out, qkv, beta, decay, qkv_host, beta_host,
+                       decay_host, out_host, *, rows: int, l2: bool = True, eps: float = 1e-6,
+                       block_rows: int = 0, workspace: Workspace | None = None,
+                       stream=None) -> Workspace:
+    """hb_gdn_prefill_host: the chunked prefill of rows whose qkv, beta,
+    decay and output are host tensors (pin them for asynchronous copies)
+    mirroring the device tensors; copies and computation overlap block by
+    block, the state carried in place.  Returns the workspace used."""
+    dev = RecurrenceCall(state=_ptr(state), output=_ptr(out), qkv=_ptr(qkv), beta=_ptr(beta),
+                         decay=_ptr(decay), rows=rows, l2=int(l2), eps=eps)
+    call = RecurrenceHostCall(dev=dev, qkv_host=qkv_host.data_ptr(), beta_host=beta_host.data_ptr(),
+                              decay_host=decay_host.data_ptr(), output_host=out_host.data_ptr(),
+                              block_rows=block_rows)
+    L = lib()
+    nbytes = L.hb_gdn_prefill_host_workspace_bytes(ctypes.byref(shape), ctypes.byref(call))
+    if nbytes == 0:
+        check(L.hb_gdn_prefill_host(ctypes.byref(shape), ctypes.byref(call), None, 0,
+                                    _stream(stream)))
+    if workspace is None:
+        workspace = Workspace(nbytes, state.device, stream)
+    else:
+        workspace.ensure(nbytes, stream)
+    check(L.hb_gdn_prefill_host(ctypes.byref(shape), ctypes.byref(call), c_void_p(workspace.ptr),
+                                workspace.nbytes, _stream(stream)))
     return workspace
 
 

@@ -418,6 +418,35 @@ HB_API hb_status hb_gdn_prefill(const hb_gdn_shape *shape, const hb_gdn_call *ca
                          size_t workspace_bytes, hb_stream_t stream);
 
 /*
+ * hb_gdn_prefill for rows whose inputs (qkv, beta, decay) and output live in
+ * host memory, with the copies overlapped with the computation.  `dev`
+ * names the device buffers the rows go through (state, output, qkv, beta,
+ * decay; rows, l2, eps as in hb_gdn_prefill); the *_host arrays hold the
+ * same rows in the same layouts.  The rows run in blocks of `block_rows`
+ * (0: the library's choice; else a positive multiple of 64): block j's
+ * inputs go in on a copy stream, hb_gdn_prefill runs the block on `stream`
+ * (the state carried from block to block), its output rows come back on a
+ * second copy stream.  Blocks start on chunk boundaries and every block
+ * takes the same kernels one call over all the rows would (a remainder of
+ * fewer than 128 rows joins the block before it), so the output and the
+ * final state are that call's bits.  Pin the host arrays: pageable memory
+ * makes the copies synchronous.  Not for stream capture on a device's first
+ * call (the copy streams and events are created then).
+ */
+typedef struct hb_gdn_host_call {
+    hb_gdn_call dev;
+    const float *qkv_host;     /* [rows][2*nk*hkd + nv*hvd] */
+    const float *beta_host;    /* [rows][nv]                */
+    const float *decay_host;   /* [rows][nv]                */
+    float *output_host;        /* [rows][nv*hvd]            */
+    int64_t block_rows;
+} hb_gdn_host_call;
+HB_API size_t hb_gdn_prefill_host_workspace_bytes(const hb_gdn_shape *shape,
+                                                  const hb_gdn_host_call *call);
+HB_API hb_status hb_gdn_prefill_host(const hb_gdn_shape *shape, const hb_gdn_host_call *call,
+                                     void *workspace, size_t workspace_bytes, hb_stream_t stream);
+
+/*
  * DeltaNet front end of one layer, in one launch: the delta-causal-convolution
  * node (src/jit/target/x86/execution/delta.rs:609-705) and the gate part of
  * delta-l2-gates (delta.rs:290-389; its L2 part is hb_gdn_call.l2).  Per

@@ -39,7 +39,8 @@ def test_record_layouts_match_the_header(tmp_path):
             "hb_cp_spec": hb.CpSpec, "hb_front_spec": hb.FrontSpec,
             "hb_front_call": hb.FrontCall, "hb_gdn_front_call": hb.GdnFrontCall,
             "hb_gdn_norm_call": hb.GdnNormCall, "hb_state_geometry": hb.StateGeometry,
-            "hb_state_buffers": hb.StateBuffers}
+            "hb_state_buffers": hb.StateBuffers, "hb_attn_host_call": hb.AttentionHostCall,
+            "hb_gdn_host_call": hb.RecurrenceHostCall}
     body = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{hb.HEADER_PATH}"',
             "int main(void){"]
     for c, py in recs.items():
@@ -123,6 +124,33 @@ def test_kv_and_delta_refusals():
     sh.hkd = 128
     rc.rows = 0
     assert L.hb_gdn_decode(ctypes.byref(sh), ctypes.byref(rc), None) == hb.HB_DECLINE_EMPTY
+
+
+def test_host_call_refusals():
+    # the host-buffer prefills check their calls before any CUDA call
+    L = hb.lib()
+    sh = hb.DeltaShape(nk=2, nv=4, hkd=128, hvd=128)
+    dev = hb.RecurrenceCall(state=16, output=16, qkv=16, beta=16, decay=16, rows=256, l2=1, eps=1e-6)
+    call = hb.RecurrenceHostCall(dev=dev, qkv_host=16, beta_host=16, decay_host=16, output_host=16,
+                                 block_rows=100)
+    assert L.hb_gdn_prefill_host_workspace_bytes(ctypes.byref(sh), ctypes.byref(call)) == 0
+    assert L.hb_gdn_prefill_host(ctypes.byref(sh), ctypes.byref(call), None, 0, None) == hb.HB_ERR_ARG
+    assert "block_rows" in hb.last_error()
+    call.block_rows = 128
+    assert L.hb_gdn_prefill_host_workspace_bytes(ctypes.byref(sh), ctypes.byref(call)) > 0
+    assert (L.hb_gdn_prefill_host(ctypes.byref(sh), ctypes.byref(call), None, 0, None)
+            == hb.HB_ERR_WORKSPACE)
+    call.decay_host = None
+    assert L.hb_gdn_prefill_host(ctypes.byref(sh), ctypes.byref(call), None, 0, None) == hb.HB_ERR_ARG
+    call.decay_host, call.dev.rows = 16, 0
+    assert (L.hb_gdn_prefill_host(ctypes.byref(sh), ctypes.byref(call), None, 0, None)
+            == hb.HB_DECLINE_EMPTY)
+    spec = hb.attention_spec()
+    acall = hb.AttentionHostCall(dev=_call(spec, rows=256, past=0, kv_stride=256 * 256),
+                                 q_host=16, keys_host=16, values_host=16, out_host=16,
+                                 block_rows=64)
+    assert L.hb_attn_prefill_host(ctypes.byref(spec), ctypes.byref(acall), None, 0, None) == hb.HB_ERR_ARG
+    assert "block_rows" in hb.last_error()
 
 
 def test_status_names():
