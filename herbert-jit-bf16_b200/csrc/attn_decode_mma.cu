@@ -392,15 +392,30 @@ __global__ void __launch_bounds__(kThreadsM, 1)
       const float* rf = reinterpret_cast<const float*>(rbuf);
       for (int t = tid; t < 4 * nq; t += 128) {
         const int e = q0 * 4 + t, g = e / HDM, dd = e % HDM;
-        float M = -INFINITY;
-        for (int r = 0; r < ns; ++r) M = fmaxf(M, rml[r * 16 + g]);
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float acc = 0.f, Ls = 0.f;
-        for (int r = 0; r < ns; ++r) {
-          const float w = fast_exp2(rml[r * 16 + g] - Mu);
-          Ls = fmaf(rml[r * 16 + G + g], w, Ls);
-          acc = fmaf(w, rf[r * nqs * 4 + t], acc);
+        // every split's (m, l, value) read at once (ns <= 16 splits: the
+        // cluster), the weights formed in parallel, then the sums in split
+        // order
+        float mr[16], lr[16], vr[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          mr[r] = r < ns ? rml[r * 16 + g] : -INFINITY;
+          lr[r] = r < ns ? rml[r * 16 + G + g] : 0.f;
+          vr[r] = r < ns ? rf[r * nqs * 4 + t] : 0.f;
         }
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) M = fmaxf(M, mr[r]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float w[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) w[r] = fast_exp2(mr[r] - Mu);
+        float acc = 0.f, Ls = 0.f;
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+          if (r < ns) {
+            Ls = fmaf(lr[r], w[r], Ls);
+            acc = fmaf(w[r], vr[r], acc);
+          }
         const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
         uint16_t a = f32_to_bf16_cvtne(acc * inv);
         if (p.gate_offset >= 0) {  // gate_bf16's steps, the divisor formed early
