@@ -470,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<G>::value)
 
   if (warp == kConsumerWarps) {  // ---------------------------- producer
     if (lane == 0) {
+      const uint64_t once = l2_evict_first();  // K and V are read once per step
       // this split's K and V into L2 while the previous grid finishes;
       // every load that returns data waits for it
       if (p1 > p0) {
@@ -488,8 +489,8 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<G>::value)
         const int64_t pos = p0 + int64_t(t) * kTile;
         const uint32_t bytes = uint32_t(min(int64_t(kTile), p1 - pos)) * HD * 2u;
         mbar_arrive_expect_tx(&full[s], 2u * bytes);
-        bulk_g2s(ks + s * TILE_ELEMS, kbase + pos * HD, bytes, &full[s]);
-        bulk_g2s(vs + s * TILE_ELEMS, vbase + pos * HD, bytes, &full[s]);
+        bulk_g2s_hint(ks + s * TILE_ELEMS, kbase + pos * HD, bytes, &full[s], once);
+        bulk_g2s_hint(vs + s * TILE_ELEMS, vbase + pos * HD, bytes, &full[s], once);
       }
     }
     // the producer warp takes part in both cluster barriers
@@ -759,6 +760,7 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<G>::value)
     const int64_t u = int64_t(z) * hkv + y;
     if (warp == kConsumerWarps) {  // -------------------------- producer
       if (lane == 0) {
+        const uint64_t once = l2_evict_first();  // K and V are read once per step
         const uint16_t* kbase = d.keys + int64_t(y) * d.kv_stride;
         const uint16_t* vbase = d.values + int64_t(y) * d.kv_stride;
         for (int t = 0; t < nt; ++t) {
@@ -773,8 +775,8 @@ __global__ void __launch_bounds__(kThreads, CtasPerSm<G>::value)
           const int64_t pos = p0 + int64_t(t) * kTile;
           const uint32_t bytes = uint32_t(min(int64_t(kTile), p1 - pos)) * HD * 2u;
           mbar_arrive_expect_tx(&full[s], 2u * bytes);
-          bulk_g2s(ks + s * TILE_ELEMS, kbase + pos * HD, bytes, &full[s]);
-          bulk_g2s(vs + s * TILE_ELEMS, vbase + pos * HD, bytes, &full[s]);
+          bulk_g2s_hint(ks + s * TILE_ELEMS, kbase + pos * HD, bytes, &full[s], once);
+          bulk_g2s_hint(vs + s * TILE_ELEMS, vbase + pos * HD, bytes, &full[s], once);
           issued = i + 1;
         }
       }

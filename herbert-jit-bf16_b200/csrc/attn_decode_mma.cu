@@ -643,7 +643,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
       // K and V are read once per step: their lines are the first L2 evicts,
       // so a sweep of the cache leaves other layers' data (a DeltaNet
       // layer's state, the next step's inputs) in L2
-      const uint64_t once = l2_evict_first_policy();
+      const uint64_t once = l2_evict_first();
       // the first tiles into L2 while the previous grid finishes
       for (int t = 0; t < nt && t < 2; ++t)
         for (int cb = 0; cb < 4; ++cb) {

@@ -244,6 +244,24 @@ HB_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
       : "memory");
 }
 
+// bulk_g2s under an L2 policy (l2_evict_first below).
+HB_DEV void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// An L2 policy that marks the lines an access brings in as the first to
+// evict: for a stream read once (a KV cache swept by a decode step), so that
+// it does not push out data that later launches read again.
+HB_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // Hint: bring `bytes` (a multiple of 16) from 16-byte-aligned global memory
 // into L2.  A prefetch has no effect on the values any load returns (L2 is
 // the point of coherence), so it may run before griddep_wait().

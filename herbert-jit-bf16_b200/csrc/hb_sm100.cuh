@@ -59,16 +59,7 @@ HB_DEV void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, 
       : "memory");
 }
 
-// An L2 policy that marks the lines an access brings in as the first to
-// evict: for a stream read once (a KV cache swept by a decode step), so that
-// it does not push out data that later launches read again.
-HB_DEV uint64_t l2_evict_first_policy() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-// tma_load_3d and tma_prefetch_l2_3d under an L2 policy.
+// tma_load_3d and tma_prefetch_l2_3d under an L2 policy (l2_evict_first).
 HB_DEV void tma_load_3d_hint(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2,
                              uint64_t policy) {
   asm volatile(
