@@ -130,6 +130,11 @@ typedef struct hb_decode_seq {
  * SdpaHeadFn (src/jit/emit_sdpa.rs:131-140) driven by the tile selector
  * (src/jit/target/x86/execution/attention.rs:56-224), followed by the
  * output-gate node ElemOp::SigmoidMul (src/jit/target/x86/emit_elem.rs:333-420).
+ * Beyond 4096 positions the splits' merge is spread over the last CTAs of
+ * each KV head, which wait (a bounded wait, about a second) for the others
+ * to finish; that needs every CTA of the launch resident at once (one per
+ * SM), so a kernel on another stream that holds SMs for that long makes the
+ * call report HB_ERR_TIMEOUT through hb_workspace_status.
  */
 HB_API size_t hb_attn_decode_workspace_bytes(const hb_attn_spec *spec, const hb_attn_call *call);
 HB_API hb_status hb_attn_decode(const hb_attn_spec *spec, const hb_attn_call *call,
