@@ -482,10 +482,10 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
 // (kv) and pass 2 (out) of the recurrence, each a sequential sum of hkd
 // terms, then the gated norm over the head's hvd outputs.  So each V head is
 // a cluster of hvd / 32 CTAs, CTA c owning the state columns [32 c, 32 c +
-// 32), and every CTA runs the head's front end itself.  A pass over kd is a
-// sequential sum of hkd terms: a warp that only adds issues about four
-// cycles per term, one that also forms the terms (two or three multiplies, a
-// store in pass 2) about ten, so the terms are formed by other warps:
+// 32), and every CTA runs the head's front end itself.  A warp that only
+// adds issues about four cycles per term of such a sum, one that also forms
+// the terms (two or three multiplies, a store in pass 2) about ten, so the
+// terms are formed by other warps:
 //   warp 0        the v channels of its columns (conv + SiLU), then only
 //                 sums: the q / k L2 sums (lanes 0 / 1, over the squares the
 //                 row warps wrote), kv and out of its 32 columns, reading
@@ -505,10 +505,10 @@ __global__ void __launch_bounds__(kNormThreads) gdn_gated_norm_scalar(const Norm
 // The CTAs of one key head read the same q / k inputs and conv state and
 // compute the same conv results; the last of them to finish reading writes
 // those back in place.  The last warp counts the CTA on the key head's
-// counter once the q / k warps are past their reads (an acquire-release
-// atomic add, off the recurrence's path); the CTA that sees the count
-// complete resets it, and its q / k warps write, when every other CTA of the
-// key head is past its reads -- no CTA waits for another.  Launched with
+// counter once the row warps are past their reads (an acquire-release atomic
+// add, off the recurrence's path); the CTA that sees the count complete
+// resets it, and its row warps write, when every other CTA of the key head
+// is past its reads -- no CTA waits for another.  Launched with
 // programmatic stream serialization: before griddepcontrol.wait only L2
 // prefetches.
 
