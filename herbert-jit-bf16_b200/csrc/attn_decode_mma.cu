@@ -956,6 +956,24 @@ __global__ void __launch_bounds__(kThreadsL, 1)
         // holds, all of a batch in flight on one barrier, and each thread
         // sums its output quads from shared memory.
         const int GM = G / K, g0 = mi * GM;
+        constexpr int QPT = (G * HDM / 4 + 127) / 128;
+        const int NQD = GM * HDM / 4;  // output quads of this CTA's heads
+        // the gate divisors 1 + exp(-g) of this thread's output quads, formed
+        // while the partials come in: the gate's read is off the merge's tail
+        float gd[QPT][4];
+#pragma unroll
+        for (int k = 0; k < QPT; ++k) {
+          const int qd = tid + k * 128;
+          gd[k][0] = gd[k][1] = gd[k][2] = gd[k][3] = 1.f;
+          if (qd < NQD && p.gate_offset >= 0) {
+            const int e = g0 * HDM + qd * 4, hq = h0 + e / HDM, dd = e % HDM;
+            const uint2 gw = *reinterpret_cast<const uint2*>(qrow + p.gate_offset + int64_t(hq) * HDM + dd);
+            gd[k][0] = gate_divisor(uint16_t(gw.x & 0xFFFFu));
+            gd[k][1] = gate_divisor(uint16_t(gw.x >> 16));
+            gd[k][2] = gate_divisor(uint16_t(gw.y & 0xFFFFu));
+            gd[k][3] = gate_divisor(uint16_t(gw.y >> 16));
+          }
+        }
         const float* up = p.partials + int64_t(unit) * p.nsplit * PSTRIDE;
         float* sml = reinterpret_cast<float*>(smem + L_OFF_Q);  // [active][2G] m, l (Q^T, P^T are done)
         float* smw = sml + active * 2 * G;                      // [active][G] weights
@@ -994,8 +1012,6 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           }
         }
         nbar_sync(2, 128);
-        constexpr int QPT = (G * HDM / 4 + 127) / 128;
-        const int NQD = GM * HDM / 4;  // output quads of this CTA's heads
         float4 acc[QPT];
 #pragma unroll
         for (int k = 0; k < QPT; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1044,13 +1060,9 @@ __global__ void __launch_bounds__(kThreadsL, 1)
           const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
           uint16_t a[4] = {f32_to_bf16_cvtne(acc[k].x * inv), f32_to_bf16_cvtne(acc[k].y * inv),
                            f32_to_bf16_cvtne(acc[k].z * inv), f32_to_bf16_cvtne(acc[k].w * inv)};
-          if (p.gate_offset >= 0) {
-            const uint2 gw =
-                *reinterpret_cast<const uint2*>(qrow + p.gate_offset + int64_t(hq) * HDM + dd);
-            a[0] = gate_bf16(a[0], uint16_t(gw.x & 0xFFFFu));
-            a[1] = gate_bf16(a[1], uint16_t(gw.x >> 16));
-            a[2] = gate_bf16(a[2], uint16_t(gw.y & 0xFFFFu));
-            a[3] = gate_bf16(a[3], uint16_t(gw.y >> 16));
+          if (p.gate_offset >= 0) {  // gate_bf16's steps, the divisors formed early
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = f32_to_bf16_cvtne(__fdiv_rn(bf16_to_f32(a[i]), gd[k][i]));
           }
           *reinterpret_cast<uint2*>(orow + int64_t(hq) * HDM + dd) =
               make_uint2(uint32_t(a[0]) | (uint32_t(a[1]) << 16), uint32_t(a[2]) | (uint32_t(a[3]) << 16));
