@@ -15,7 +15,8 @@ pytestmark = pytest.mark.gpu
     (1, 16, 32, 128, 128, True, True),     # the one-row form, warm state
     (1, 4, 8, 64, 128, False, True),       # the one-row form at hkd 64, no L2 step
     (1, 2, 4, 128, 96, True, True),        # one row at hvd 96: the pipelined form
-    (7, 16, 32, 128, 128, True, True),
+    (7, 16, 32, 128, 128, True, True),     # a short block: the split form
+    (40, 16, 32, 128, 128, True, True),    # a longer block: the pipelined form
     (4, 2, 4, 128, 64, False, True),
     (3, 4, 4, 64, 96, True, False),
 ])
