@@ -1168,14 +1168,7 @@ cudaError_t launch_long(const DecodeLaunch& L, const DecodeFront* F, int chunk, 
   cfg.blockDim = dim3(kThreadsL);
   // one CTA per SM (its shared memory): the merge waits on other CTAs only
   // when every CTA of the grid can be resident at once
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      sms = 0;
-  }
-  p.spread = int64_t(nsplit) * L.hkv * L.rows <= sms ? 1 : 0;
+  p.spread = int64_t(nsplit) * L.hkv * L.rows <= device_sms() ? 1 : 0;
   cfg.dynamicSmemBytes = L_SMEM;
   cfg.stream = st;
   cudaLaunchAttribute at[1];

@@ -915,14 +915,7 @@ cudaError_t launch_gdn_gated_norm(const GdnNormLaunch& L, cudaStream_t st) {
   long long ctas = (p.n_rows + warps - 1) / warps;
   if (p.dim % 16 == 0 && p.dim <= 128) {
     // a resident grid (eight CTAs per SM) whose warps stride over the rows
-    static int sms = 0;
-    if (!sms) {
-      int dev = 0;
-      cudaGetDevice(&dev);
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      if (sms <= 0) sms = 148;
-    }
-    ctas = std::min<long long>(ctas, 8LL * sms);
+    ctas = std::min<long long>(ctas, 8LL * device_sms());
     switch (p.dim / 16) {
       case 1: gdn_gated_norm_vec<1><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;
       case 2: gdn_gated_norm_vec<2><<<unsigned(ctas), kNormThreads, 0, st>>>(p); break;

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -201,17 +202,17 @@ cudaError_t device_status_word(int** out) {
 }
 
 int device_sms() {
-  static int cache[64] = {0};
+  static std::atomic<int> cache[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  int& v = cache[dev & 63];
-  if (v == 0) {
-    int n = 0;
+  std::atomic<int>& v = cache[dev & 63];
+  int n = v.load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
       n = 148;
-    v = n;
+    v.store(n, std::memory_order_relaxed);
   }
-  return v;
+  return n;
 }
 
 }  // namespace hb
