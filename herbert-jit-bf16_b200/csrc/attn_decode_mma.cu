@@ -927,9 +927,12 @@ __global__ void __launch_bounds__(kThreadsL, 1)
       // that brings the count to active + K resets it for the next call.
       const int K = (p.spread && active >= G) ? G : 1;
       if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&p.counters[unit], 1u);
-        __threadfence();
+        // acquire-release at gpu scope: the CTA's partial (ordered before
+        // this thread by the block barrier) is visible to whoever reads the
+        // count after it, and this CTA sees every partial counted before
+        unsigned prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(prev) : "l"(p.counters + unit) : "memory");
         const int mi = int(prev) - (active - K);
         flags[1] = mi >= 0 ? mi : -1;
         if (mi >= 0 && mi < K - 1) {  // wait for the splits after this one
