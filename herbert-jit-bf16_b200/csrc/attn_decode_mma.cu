@@ -588,7 +588,6 @@ template <int G, bool FRONT>
 __global__ void __launch_bounds__(kThreadsL, 1)
     attn_decode_long_kernel(const __grid_constant__ CUtensorMap tmK,
                             const __grid_constant__ CUtensorMap tmV, const DecodeLongParams p) {
-  constexpr int PSTRIDE = G * HDM + ((2 * G + 3) & ~3);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L_OFF_BAR);
@@ -906,17 +905,22 @@ __global__ void __launch_bounds__(kThreadsL, 1)
             front::store_words<4>(const_cast<uint16_t*>(qrow) + int64_t(h0 + warp + 4 * i) * p.q_head + lane * 8, qy[i]);
       }
     } else {
-      float* mine = p.partials + (int64_t(unit) * p.nsplit + split) * PSTRIDE;
+      // the partial, head-major: O rows at [unit][head][split][HD] (a head's
+      // rows of every split contiguous, one bulk copy for a merger), the
+      // maxima and sums at [unit][split][2G] after all the O rows
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        __stcg(mine + g * HDM + pl, o[0][g]);
-        __stcg(mine + g * HDM + 128 + pl, o[1][g]);
+        float* orow_p = p.partials + ((int64_t(unit) * G + g) * p.nsplit + split) * HDM;
+        __stcg(orow_p + pl, o[0][g]);
+        __stcg(orow_p + 128 + pl, o[1][g]);
       }
+      float* ml = p.partials + int64_t(gridDim.y) * gridDim.z * G * p.nsplit * HDM +
+                  (int64_t(unit) * p.nsplit + split) * 2 * G;
 #pragma unroll
       for (int g = 0; g < G; ++g)
         if (tid == g) {
-          __stcg(mine + G * HDM + g, M[g]);
-          __stcg(mine + G * HDM + G + g, Lsum[g]);
+          __stcg(ml + g, M[g]);
+          __stcg(ml + G + g, Lsum[g]);
         }
       nbar_sync(2, 128);  // every partial store of this CTA precedes thread 0's release
       // The last K CTAs of the unit to count themselves merge it, one slice
@@ -977,19 +981,22 @@ __global__ void __launch_bounds__(kThreadsL, 1)
             gd[k][3] = gate_divisor(uint16_t(gw.y >> 16));
           }
         }
-        const float* up = p.partials + int64_t(unit) * p.nsplit * PSTRIDE;
+        const float* uo = p.partials + int64_t(unit) * G * p.nsplit * HDM;  // [head][split][HD]
+        const float* uml = p.partials + int64_t(gridDim.y) * gridDim.z * G * p.nsplit * HDM +
+                           int64_t(unit) * p.nsplit * 2 * G;  // [split][2G]
         float* sml = reinterpret_cast<float*>(smem + L_OFF_Q);  // [active][2G] m, l (Q^T, P^T are done)
         float* smw = sml + active * 2 * G;                      // [active][G] weights
         float* smL = reinterpret_cast<float*>(smem + L_OFF_RED);  // [G]
         const int ROW = GM * HDM * 4;                           // bytes of the heads' O in one split
-        const int BATCH = 3 * L_SLOT / ROW;
+        const int BATCH = 3 * L_SLOT / ROW;  // splits per batch; in shared memory [head][split][HD]
         const bool staged = active * 3 * G * 4 <= 16384;        // m, l and weights fit Q^T + P^T
         auto issue = [&](int b0) {  // warp 0: the heads' O rows of splits b0 .. b0 + BATCH - 1
           const int nb = min(BATCH, active - b0);
           if (lane == 0) mbar_arrive_expect_tx(&bar[L_MERGE], uint32_t(nb) * ROW);
           __syncwarp();
-          for (int i = lane; i < nb; i += 32)
-            bulk_g2s(smem + i * ROW, up + (b0 + i) * PSTRIDE + g0 * HDM, ROW, &bar[L_MERGE]);
+          if (lane < GM)  // one copy per head: its nb rows are contiguous
+            bulk_g2s(smem + lane * nb * HDM * 4, uo + (int64_t(g0 + lane) * p.nsplit + b0) * HDM,
+                     uint32_t(nb) * HDM * 4, &bar[L_MERGE]);
         };
         if (staged && !flags[0]) {
           if (warp == 0) {
@@ -997,7 +1004,7 @@ __global__ void __launch_bounds__(kThreadsL, 1)
             issue(0);  // in flight while the weights are formed
           }
           for (int i = tid; i < active * 2 * G; i += 128)
-            sml[i] = __ldcg(up + (i / (2 * G)) * PSTRIDE + G * HDM + (i % (2 * G)));
+            sml[i] = __ldcg(uml + i);
           nbar_sync(2, 128);
           for (int g = g0 + warp; g < g0 + GM; g += 4) {
             float Mx = -INFINITY;
@@ -1034,9 +1041,10 @@ __global__ void __launch_bounds__(kThreadsL, 1)
               for (int k = 0; k < QPT; ++k) {
                 const int qd = tid + k * 128;
                 if (qd < NQD) {
-                  const int g = g0 + qd * 4 / HDM;
+                  const int gh = qd * 4 / HDM, g = g0 + gh, dq = (qd * 4) % HDM;
+                  const float4* hv = reinterpret_cast<const float4*>(smem + gh * nb * HDM * 4) + dq / 4;
                   for (int i = 0; i < nb; ++i) {
-                    const float4 v = reinterpret_cast<const float4*>(smem + i * ROW)[qd];
+                    const float4 v = hv[i * (HDM / 4)];
                     const float w = smw[(b0 + i) * G + g];
                     acc[k].x = fmaf(w, v.x, acc[k].x);
                     acc[k].y = fmaf(w, v.y, acc[k].y);
