@@ -150,6 +150,8 @@ hb_status check_gdn_host_call(const hb_gdn_shape* s, const hb_gdn_host_call* h) 
     return fail(HB_ERR_ARG, "block_rows %lld must be 0 or a positive multiple of 64",
                 (long long)h->block_rows);
   if (h->dev.rows <= 0) return fail(HB_DECLINE_EMPTY, "empty DeltaNet block");
+  if (h->dev.rows >= (int64_t(1) << 31))
+    return fail(HB_ERR_ARG, "rows %lld beyond the host prefill's range", (long long)h->dev.rows);
   return HB_OK;
 }
 
@@ -173,8 +175,10 @@ size_t hb_attn_prefill_host_workspace_bytes(const hb_attn_spec* s, const hb_attn
   if (check_host_call(s, h) != HB_OK) return 0;
   const int64_t rows = h->dev.rows, block = prefill_host_block(rows, h->block_rows);
   const int64_t nblocks = prefill_host_blocks(rows, block);
+  // a block's need grows with its rows and its first position: the first
+  // block, the last full one and the last one cover every block
   size_t need = 0;
-  for (int64_t j = 0; j < nblocks; ++j) {
+  for (const int64_t j : {int64_t(0), std::max<int64_t>(0, nblocks - 2), nblocks - 1}) {
     const int64_t r0 = j * block, nb = j + 1 < nblocks ? block : rows - r0;
     const hb_attn_call b = block_call(s, h->dev, r0, nb);
     need = std::max(need, hb_attn_prefill_workspace_bytes(s, &b));
@@ -247,12 +251,10 @@ size_t hb_gdn_prefill_host_workspace_bytes(const hb_gdn_shape* s, const hb_gdn_h
   if (check_gdn_host_call(s, h) != HB_OK) return 0;
   const int64_t rows = h->dev.rows, block = gdn_host_block(rows, h->block_rows);
   const int64_t nblocks = gdn_host_blocks(rows, block);
-  size_t need = 0;
-  for (int64_t j = 0; j < nblocks; ++j) {
-    const int64_t nb = j + 1 < nblocks ? block : rows - j * block;
-    need = std::max(need, hb_gdn_prefill_workspace_bytes(s, nb));
-  }
-  return need;
+  // every block but the last has `block` rows
+  const int64_t last = rows - (nblocks - 1) * block;
+  return std::max(hb_gdn_prefill_workspace_bytes(s, std::min(rows, block)),
+                  hb_gdn_prefill_workspace_bytes(s, last));
 }
 
 hb_status hb_gdn_prefill_host(const hb_gdn_shape* s, const hb_gdn_host_call* h, void* ws,

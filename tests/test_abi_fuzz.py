@@ -75,6 +75,11 @@ def test_attention_entry_points():
         nbytes = _pick(rng, [0, 255, 256, 1 << 20, 1 << 40])
         _ok(L.hb_attn_decode(s, c, ws, nbytes, None))
         _ok(L.hb_attn_prefill(s, c, ws, nbytes, None))
+        hc = hb.AttentionHostCall(dev=call, q_host=_pick(rng, PTRS), keys_host=_pick(rng, PTRS),
+                                  values_host=_pick(rng, PTRS), out_host=_pick(rng, PTRS),
+                                  block_rows=_pick(rng, I64 + [0, 128, 1024]))
+        L.hb_attn_prefill_host_workspace_bytes(s, ctypes.byref(hc))
+        _ok(L.hb_attn_prefill_host(s, ctypes.byref(hc), ws, nbytes, None))
         _ok(L.hb_attn_decode_batch(s, ctypes.c_void_p(_pick(rng, PTRS)), _pick(rng, I64),
                                    _pick(rng, I64), _pick(rng, I64), ws, nbytes, None))
         kv = _fill(rng, hb.KvSpec, dict(heads=4, head_dim=256, stride=256 * 256, capacity=256,
@@ -111,6 +116,11 @@ def test_deltanet_entry_points():
         L.hb_gdn_prefill_workspace_bytes(sh, _pick(rng, I64))
         _ok(L.hb_gdn_decode(sh, ctypes.byref(call), None))
         _ok(L.hb_gdn_prefill(sh, ctypes.byref(call), ws, _pick(rng, [0, 256, 1 << 30]), None))
+        hc = hb.RecurrenceHostCall(dev=call, qkv_host=_pick(rng, PTRS), beta_host=_pick(rng, PTRS),
+                                   decay_host=_pick(rng, PTRS), output_host=_pick(rng, PTRS),
+                                   block_rows=_pick(rng, I64 + [0, 64, 128, 256]))
+        L.hb_gdn_prefill_host_workspace_bytes(sh, ctypes.byref(hc))
+        _ok(L.hb_gdn_prefill_host(sh, ctypes.byref(hc), ws, _pick(rng, [0, 256, 1 << 30]), None))
         fc = _fill(rng, hb.GdnFrontCall, dict(qkv=256, conv_state=256, conv_weight=256, ab=256,
                                               dt_bias=256, a_log=256, beta=256, decay=256,
                                               rows=3, ck=4))
